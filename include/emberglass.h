@@ -1,0 +1,236 @@
+/*
+ * emberglass.h -- C ABI of libemberglass_cuda.so, the B200 (sm_100a)
+ * replacement for the Emberglass WebGPU decode path
+ * (maceip/vibethinker-webgpu-lora, src/qwgpu/runtime.js `QwenWGPU`).
+ *
+ * Conventions
+ *  - Every function returns an eg_status (0 = EG_OK).  On failure
+ *    eg_last_error() returns a thread-local message; the reference throws a
+ *    JS Error with the same text at the cited line.
+ *  - Plain pointers and sizes only.  Runtime entry points (eg_token, ...)
+ *    take HOST buffers and do their own host<->device copies; single-op
+ *    entry points (eg_op_*) take DEVICE pointers and a cudaStream_t passed as
+ *    void* (NULL = legacy default stream) and are asynchronous.
+ *  - All calls on one eg_rt are serialised on that runtime's stream; the
+ *    library starts no threads of its own for device work.  Concurrent
+ *    readback calls on one handle fail with EG_ERR_BUSY, as the reference's
+ *    busy flags do (runtime.js:1603-1605, :1649-1650, :1686-1687).
+ *  - Weight layouts are the reference's: int4 = 8 two's-complement nibbles
+ *    per u32, low nibble = lowest k, f32 scale per (row, 128-group)
+ *    (quantize.js:81-111); int8 = 4 per u32 little-endian with one f32 scale
+ *    per row (quantize.js:28-57).
+ */
+#ifndef EMBERGLASS_H
+#define EMBERGLASS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EG_API __attribute__((visibility("default")))
+
+typedef enum {
+  EG_OK = 0,
+  EG_ERR_ARG = 1,      /* bad argument / shape (reference: throw new Error) */
+  EG_ERR_CUDA = 2,     /* a CUDA call failed */
+  EG_ERR_STATE = 3,    /* call not valid in the current state */
+  EG_ERR_OOM = 4,      /* device or host allocation failed */
+  EG_ERR_BUSY = 5,     /* concurrent readback on one handle */
+  EG_ERR_DEVICE = 6    /* a kernel reported a failed bounded wait */
+} eg_status;
+
+typedef struct eg_rt eg_rt;
+typedef struct eg_lora eg_lora;
+
+/* QWEN25_3B in src/config.js:27-48. */
+typedef struct {
+  int hidden_size;        /* 2048 */
+  int num_layers;         /* 36 */
+  int num_heads;          /* 16 */
+  int num_kv_heads;       /* 2 */
+  int head_dim;           /* 128 (the only value the kernels support) */
+  int intermediate_size;  /* 11008 */
+  int vocab_size;         /* 151936 */
+  float rms_norm_eps;     /* 1e-6 */
+  double rope_theta;      /* 1e6 */
+  int tie_word_embeddings;/* must be 1 (model_schema.js:43-45) */
+  int attention_bias;     /* q/k/v bias (config.js:46) */
+} eg_config;
+
+/* QwenWGPU constructor opts (runtime.js:85-128, :541-570) plus B200 knobs. */
+typedef struct {
+  int device;              /* CUDA ordinal */
+  int max_ctx;             /* KV cache length, default 8192 */
+  int max_prefill_t;       /* prefill cap, default = max_ctx */
+  int kv_f16;              /* 1: f16 KV cache with the reference's f16 staging
+                              numerics (setUseF16, runtime.js:146-151, the
+                              default on shader-f16 devices); 0: f32 path */
+  int decode_batch_capacity; /* tokens per eg_decode_greedy call, default 32 */
+  int sampling_top_k;      /* default 40 */
+  int max_sampling_top_k;  /* default 64 (max 64) */
+  int attn_chunk;          /* keys per attention split; 0 = adaptive */
+  int use_graphs;          /* capture the decode step in a CUDA graph (default 1) */
+  int use_pdl;             /* programmatic dependent launch (default 1) */
+} eg_options;
+
+EG_API const char* eg_last_error(void);
+EG_API const char* eg_version(void);
+EG_API void eg_default_config(eg_config* c);   /* QWEN25_3B */
+EG_API void eg_default_options(eg_options* o);
+
+/* new QwenWGPU(device, cfg, opts), runtime.js:87-101.  Allocates nothing
+ * large until weights arrive. */
+EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** out);
+EG_API eg_status eg_destroy(eg_rt* rt);
+
+/* ---------------- quantisers (host, bit-exact with quantize.js) ---------- */
+/* quantizeInt4Group, quantize.js:81-111.  packed: N*K/8 u32, scale: N*K/group f32. */
+EG_API eg_status eg_quantize_int4_group(const float* W, int N, int K, int group,
+                                        uint32_t* packed, float* scale);
+/* quantizeInt8RowMajor, quantize.js:28-57.  packed: N*K/4 u32, scale: N f32. */
+EG_API eg_status eg_quantize_int8_rows(const float* W, int N, int K, uint32_t* packed,
+                                       float* scale);
+
+/* ---------------- weights (build(source), runtime.js:326-539) ------------- */
+/* ModelUploader.visit (model_uploader.js:39-63): one HF-named f32 tensor,
+ * quantised per the schema (model_schema.js:53-126): int4 g128 for the seven
+ * projections, int8 rows for model.embed_tokens.weight, f32 for norms and
+ * q/k/v biases.  q/k/v and gate/up are packed as _buildPackedProjectionBuffers
+ * does (runtime.js:607-659).  Shape errors: "shape mismatch for <name>: ...". */
+EG_API eg_status eg_upload_tensor(eg_rt* rt, const char* name, const float* data,
+                                  const int64_t* shape, int ndim);
+/* Same, for a tensor the caller already quantised in the reference layout.
+ * kind: 4 = int4 (packed N*K/8 u32 + N*K/128 scales), 8 = int8 rows. */
+EG_API eg_status eg_upload_quantized(eg_rt* rt, const char* name, int kind,
+                                     const uint32_t* packed, const float* scale,
+                                     const int64_t* shape, int ndim);
+/* build('mock') equivalent with seeded weights instead of zeros: every
+ * matrix and q/k/v bias ~ N(0, std) from the SplitMix64/Box-Muller stream
+ * of tensor id t (seed_t = stream(seed)[t]; embed t=0, layer i projection p
+ * (q,k,v,o,gate,up,down) t=16i+1+p, bias b t=16i+8+b), norms = 1. */
+EG_API eg_status eg_build_synthetic(eg_rt* rt, uint64_t seed, double std_w);
+/* uploader.finalize + schema.assertComplete (model_schema.js:117-124):
+ * "missing N required tensor(s): ..." ; then RoPE tables and KV cache. */
+EG_API eg_status eg_finalize(eg_rt* rt);
+
+/* ---------------- decode (runtime.js:1466-1793) --------------------------- */
+/* token(id, pos), runtime.js:1735-1741: embed id, one decode step at pos,
+ * logits left on the device. */
+EG_API eg_status eg_token(eg_rt* rt, uint32_t id, int pos);
+/* decodeBatch(startPos, K), runtime.js:1776-1793: K = min(K, capacity,
+ * max_ctx - start_pos) chained greedy tokens starting from the token held in
+ * s.amax; ids copied to out_ids (K entries), *n_out = K. */
+EG_API eg_status eg_decode_greedy(eg_rt* rt, int start_pos, int K, uint32_t* out_ids,
+                                  int* n_out);
+/* decodeBatch without the readback: enqueue K chained greedy steps on the
+ * runtime's stream and return at once (ids stay on the device until
+ * eg_read_ids).  K is clamped as in eg_decode_greedy; *n_out = K. */
+EG_API eg_status eg_decode_greedy_async(eg_rt* rt, int start_pos, int K, int* n_out);
+/* Copy the first n ids produced by the last decode call to host memory. */
+EG_API eg_status eg_read_ids(eg_rt* rt, uint32_t* out_ids, int n);
+/* The runtime's cudaStream_t (as void*), for callers that order their own
+ * work (or CUDA events) after the runtime's. */
+EG_API void* eg_stream(eg_rt* rt);
+/* Wait for all work queued on the runtime; reports asynchronous errors. */
+EG_API eg_status eg_sync(eg_rt* rt);
+/* prefillBatch(ids), runtime.js:1936-1945: positions 0..T-1; throws
+ * "prompt T > maxPrefillT M" / "prompt T > maxCtx M".  Logits of the last
+ * position are left on the device. */
+EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T);
+/* argmaxLogits(), runtime.js:1602-1629: writes s.amax and returns it. */
+EG_API eg_status eg_argmax(eg_rt* rt, uint32_t* out_id);
+/* topKLogits(k), runtime.js:1648-1678: k clamped to [1, max_sampling_top_k,
+ * vocab]; *k_out = k.  Order: value desc, ties to the lower id. */
+EG_API eg_status eg_topk(eg_rt* rt, int k, uint32_t* ids, float* vals, int* k_out);
+/* sampleToken(temp, r), runtime.js:1685-1732 (r clamped to [0,1]). */
+EG_API eg_status eg_sample(eg_rt* rt, float temp, float r, uint32_t* out_id);
+/* readLogits(), runtime.js:1633-1646: vocab floats. */
+EG_API eg_status eg_read_logits(eg_rt* rt, float* out);
+/* Final hidden state (s.hidden) after the last step: hidden_size floats. */
+EG_API eg_status eg_read_hidden(eg_rt* rt, float* out);
+/* generate(ids, n, {sample, temp}), runtime.js:2481-2516.  r_seq supplies
+ * the uniforms sampleToken would draw (n entries; ignored when !sample). */
+EG_API eg_status eg_generate(eg_rt* rt, const uint32_t* prompt, int n_prompt, int max_new,
+                             int sample, float temp, const float* r_seq, uint32_t* out_ids);
+
+/* ---------------- LoRA (lora_gpu.js:65-113, runtime.js:717-734) ----------- */
+typedef struct {
+  const char* key;        /* "layers.I.self_attn.q_proj" (moduleKeyFromTensorName) */
+  const float* A;         /* lora_A as stored: [r][in] or [in][r] */
+  int64_t a_rows, a_cols;
+  const float* B;         /* lora_B as stored: [out][r] or [r][out] */
+  int64_t b_rows, b_cols;
+  float scale;            /* MLX scale | alpha/r | 2.0 (lora_gpu.js:73-80,108) */
+} eg_lora_module;
+
+/* loadLoraAdapterGPU: rank = smallest dim, A -> [r][in], B -> [r][out]
+ * (lora_gpu.js:100-107); device copies owned by the adapter. */
+EG_API eg_status eg_lora_create(eg_rt* rt, int n, const eg_lora_module* mods, eg_lora** out);
+EG_API eg_status eg_lora_destroy(eg_rt* rt, eg_lora* lora);
+/* Replace one module's A/B contents in place (same shapes). */
+EG_API eg_status eg_lora_update(eg_rt* rt, eg_lora* lora, const char* key, const float* A,
+                                const float* B);
+EG_API eg_status eg_set_lora(eg_rt* rt, eg_lora* lora);      /* setLora */
+EG_API eg_status eg_clear_lora(eg_rt* rt);                    /* clearLora */
+EG_API eg_status eg_invalidate_lora(eg_rt* rt);               /* invalidateLora */
+
+/* ---------------- observability ------------------------------------------ */
+/* enableProf/profToken (runtime.js:775-806): one token at (id, pos) with a
+ * CUDA event around each kernel; us[] per category in this order:
+ * embed+qkv, attn, o, gate_up, down, lm_head.  n_cat receives 6. */
+EG_API eg_status eg_profile_token(eg_rt* rt, uint32_t id, int pos, double* us, int* n_cat);
+/* memoryFootprintBytes (runtime.js:661-681). */
+EG_API eg_status eg_memory_footprint(eg_rt* rt, int64_t* kv_bytes, int64_t* weight_bytes,
+                                     int64_t* scratch_bytes);
+/* Kernel launches one decode step issues (lastDispatchCount, runtime.js:743). */
+EG_API int eg_launches_per_step(eg_rt* rt);
+
+/* ---------------- single ops (kernels.js WGSL entry points) --------------- */
+/* GEMV4 / GEMV4_ADD, kernels.js:884-971: y = W4 x (+bias) ; accumulate=1
+ * gives y += W4 x.  group must be 128, K % 128 == 0, any N >= 1. */
+EG_API eg_status eg_op_gemv_q4(const float* x, const uint32_t* w, const float* scale,
+                               const float* bias, int N, int K, int group, float* y,
+                               int accumulate, void* stream);
+/* GATE_UP_SILU_GEMV4, kernels.js:1021-1072: w/scale hold 2N rows [gate;up]. */
+EG_API eg_status eg_op_gate_up_silu(const float* x, const uint32_t* w, const float* scale,
+                                    int N, int K, float* y, void* stream);
+/* GEMV (int8 rows), kernels.js:20-59: y = (W8 x) * scale[n]. */
+EG_API eg_status eg_op_gemv_q8(const float* x, const uint32_t* w, const float* scale, int N,
+                               int K, float* y, void* stream);
+/* RMSNORM / RMSNORM_F16, kernels.js:128-166. */
+EG_API eg_status eg_op_rmsnorm(const float* x, const float* g, int K, float eps, int f16,
+                               float* y, void* stream);
+/* ROPE_QK / ROPE_QK_F16, kernels.js:205-257 (in place, head_dim 128). */
+EG_API eg_status eg_op_rope_qk(float* q, float* k, int nq, int nkv, int pos, const float* cos_t,
+                               const float* sin_t, int f16, void* stream);
+/* ROPE_QK + KV append (runtime.js:1509-1514) + ATTN_PARTIAL/ATTN_COMBINE
+ * (kernels.js:258-388; _F16 variants when kv_f16): qkv = raw [q | k | v],
+ * caches [max_ctx][nkv][128] (f16 when kv_f16 else f32); attends over
+ * positions 0..pos.  chunk = keys per split, 0 = adaptive.  Uses library
+ * scratch memory for the split partials. */
+EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cache,
+                                   const float* cos_t, const float* sin_t, int nh, int nkv,
+                                   int pos, int max_ctx, int kv_f16, int chunk, float* out,
+                                   void* stream);
+/* EMBED_BUF, kernels.js:537-550: id read from device memory. */
+EG_API eg_status eg_op_embed(const uint32_t* w, const float* scale, const uint32_t* id, int H,
+                             float* out, void* stream);
+/* LORA_A, kernels.js:60-78: d[r] = A[r] . x. */
+EG_API eg_status eg_op_lora_a(const float* x, const float* A, int K, int rank, float* d,
+                              void* stream);
+/* ARGMAX, kernels.js:771-784 (ties -> lowest index; uses library scratch). */
+EG_API eg_status eg_op_argmax(const float* logits, int n, uint32_t* out, void* stream);
+/* TOPK_SELECT x k, kernels.js:785-813 (1 <= k <= 64; uses library scratch). */
+EG_API eg_status eg_op_topk(const float* logits, int n, int k, uint32_t* ids, float* vals,
+                            void* stream);
+/* SAMPLE_TOPK, kernels.js:814-883 (k <= 64). */
+EG_API eg_status eg_op_sample_topk(const uint32_t* ids, const float* vals, int k, float temp,
+                                   float r, uint32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EMBERGLASS_H */

@@ -1,0 +1,211 @@
+"""End-to-end decode parity of the CUDA runtime (through the C ABI) against
+the CPU oracle stepping the same seeded synthetic model.
+
+Bars (north_star): logits/hidden max-abs <= 1e-2 and mean-rel <= 1e-3 vs the
+reference path; greedy token streams identical."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+import vibethinker_webgpu_lora_b200 as E
+from vibethinker_webgpu_lora_b200.config import small_config
+
+pytestmark = pytest.mark.gpu
+SEED = 0xE6B00000
+
+
+def close(got, ref, max_abs=1e-2, mean_rel=1e-3):
+    d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    assert d.max() <= max_abs, f"max abs {d.max()}"
+    rel = d.mean() / max(np.abs(ref).mean(), 1e-12)  # mean relative error
+    assert rel <= mean_rel, f"mean rel {rel}"
+
+
+# Greedy streams must be identical wherever the oracle's top-1/top-2 logit
+# margin exceeds the numerical noise of two f32 summation orders (plus f16
+# staging roundings); at a genuine near-tie below this bound the streams may
+# legitimately part, and comparison stops there.
+TIE_BOUND = 2e-3
+
+
+def assert_stream(got, ref, margins, bound=TIE_BOUND):
+    for i, (a, b) in enumerate(zip(list(got), list(ref))):
+        if a != b:
+            assert margins[i] < bound, f"token {i}: {a} != {b} with oracle margin {margins[i]:.3g}"
+            return i
+    assert len(got) == len(ref)
+    return len(ref)
+
+
+def make(cfg, f16, max_ctx=256, **opts):
+    rt = E.QwenB200(cfg, dict(maxCtx=max_ctx, useF16=f16, **opts)).build("synthetic", seed=SEED)
+    orc = O.OracleModel(cfg, max_ctx, f16, SEED)
+    return rt, orc
+
+
+@pytest.mark.parametrize("f16", [True, False])
+@pytest.mark.parametrize("graphs", [True, False])
+def test_small_model_logits_and_greedy(cuda, f16, graphs):
+    cfg = small_config(layers=3, vocab=5000, inter=1024)
+    rt, orc = make(cfg, f16, useGraphs=graphs)
+    prompt = O.token_ids(12, 0xE6B00010, cfg["vocabSize"])
+    for t, tok in enumerate(prompt):
+        rt.token(int(tok), t)
+        ref = orc.step(int(tok), t)
+        close(rt.readLogits(), ref)
+    close(rt.readHidden(), orc.hidden())
+    first = rt.argmaxLogits()
+    assert first == O.argmax(ref)
+    ids = rt.decodeBatch(len(prompt), 24)
+    ref_ids, margins = orc.generate(prompt, 25)
+    assert_stream([first] + ids, ref_ids, margins)
+
+
+def test_prefill_matches_token_loop(cuda):
+    cfg = small_config(layers=2, vocab=3000)
+    rt = E.QwenB200(cfg, dict(maxCtx=128)).build("synthetic", seed=SEED)
+    prompt = O.token_ids(20, 5, cfg["vocabSize"])
+    rt.prefillBatch(prompt)
+    a = rt.readLogits()
+    for t, tok in enumerate(prompt):
+        rt.token(int(tok), t)
+    assert np.array_equal(a, rt.readLogits())  # deterministic, bitwise
+
+
+def test_generate_greedy_and_sampled(cuda):
+    cfg = small_config(layers=2, vocab=3000)
+    rt, orc = make(cfg, True)
+    prompt = O.token_ids(10, 6, cfg["vocabSize"])
+    g = rt.generate(prompt, 20)
+    ref, margins = orc.generate(prompt, 20)
+    assert_stream(g, ref, margins)
+    # sampled generate: oracle = step + topk(40) + SAMPLE_TOPK with the same r
+    r = O.uniform(20, 0xE6B00200)
+    s = rt.generate(prompt, 20, {"sample": True, "temp": 0.7, "rSeq": r})
+    orc2 = O.OracleModel(cfg, 256, True, SEED)
+    for t, tok in enumerate(prompt):
+        logits = orc2.step(int(tok), t)
+    pos = len(prompt)
+    for i in range(20):
+        ids, vals = O.topk(logits, 40)
+        nxt = O.sample_topk(ids, vals, 40, 0.7, float(r[i]))
+        if s[i] != nxt:
+            # only a near-boundary draw or a near-tied top-k may part the streams
+            p = np.exp(vals.astype(np.float64) / 0.7)
+            cdf = np.cumsum(p / p.sum())
+            assert np.abs(cdf - r[i]).min() < 1e-3 or np.diff(vals).max() > -TIE_BOUND, i
+            break
+        logits = orc2.step(nxt, pos)
+        pos += 1
+
+
+def test_topk_sample_api(cuda):
+    cfg = small_config(layers=2, vocab=3000)
+    rt, orc = make(cfg, True)
+    prompt = O.token_ids(8, 7, cfg["vocabSize"])
+    rt.prefillBatch(prompt)
+    for t, tok in enumerate(prompt):
+        ref = orc.step(int(tok), t)
+    top = rt.topKLogits(40)
+    rid, rv = O.topk(ref, 40)
+    ids = [d["id"] for d in top]
+    assert len(set(ids)) == 40 and ids[0] == rt.argmaxLogits()
+    assert all(np.isfinite(d["logit"]) for d in top)
+    assert all(top[i]["logit"] >= top[i + 1]["logit"] for i in range(39))
+    assert ids[:10] == rid[:10].tolist()
+    assert len(rt.topKLogits(500)) == 64      # clamped to maxSamplingTopK
+    t = rt.sampleToken(0.7, 0.3)
+    assert t == O.sample_topk(rid, rv, 40, 0.7, 0.3)
+
+
+def test_lora_apply_swap_clear(cuda):
+    cfg = small_config(layers=2, vocab=3000)
+    rt, orc = make(cfg, True)
+    prompt = O.token_ids(6, 8, cfg["vocabSize"])
+    rt.prefillBatch(prompt)
+    base = rt.readLogits()
+    a1 = E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16)
+    a2 = E.synthetic_adapter(rt, 0xA2, rank=8, alpha=16)
+    rt.setLora(a1)
+    rt.prefillBatch(prompt)
+    l1 = rt.readLogits()
+    orc.lora_synth(0xA1, 8, 2.0)
+    for t, tok in enumerate(prompt):
+        ref1 = orc.step(int(tok), t)
+    close(l1, ref1)
+    assert np.abs(l1 - base).max() > 1e-3
+    rt.setLora(a2)  # hot swap
+    rt.prefillBatch(prompt)
+    l2 = rt.readLogits()
+    assert np.abs(l2 - l1).max() > 1e-3
+    rt.clearLora()
+    rt.prefillBatch(prompt)
+    assert np.array_equal(rt.readLogits(), base)  # clearLora restores base bit-exact
+    # in-place update + invalidate (the trainer path)
+    rt.setLora(a1)
+    key = "layers.0.self_attn.q_proj"
+    a1.update(key, B=np.zeros((8, 2048), np.float32))
+    rt.invalidateLora()
+    rt.prefillBatch(prompt)
+    assert not np.array_equal(rt.readLogits(), l1)
+    a1.destroy()
+    a2.destroy()
+
+
+def test_errors_and_limits(cuda):
+    cfg = small_config(layers=1, vocab=1000)
+    rt = E.QwenB200(cfg, dict(maxCtx=64, maxPrefillT=32))
+    with pytest.raises(E.EmberglassError, match="not built"):
+        rt.token(0, 0)
+    with pytest.raises(E.EmberglassError, match="missing .* required tensor"):
+        rt.finalize()
+    with pytest.raises(E.EmberglassError, match="shape mismatch"):
+        rt.uploadTensor("model.norm.weight", np.ones(7, np.float32))
+    rt = E.QwenB200(cfg, dict(maxCtx=64, maxPrefillT=32)).build("synthetic")
+    with pytest.raises(E.EmberglassError, match="maxPrefillT"):
+        rt.prefillBatch(np.zeros(40, np.uint32))
+    with pytest.raises(E.EmberglassError):
+        rt.token(5000, 0)
+    rt.prefillBatch(np.zeros(4, np.uint32))
+    rt.argmaxLogits()
+    assert len(rt.decodeBatch(60, 32)) == 4   # clamped to maxCtx - startPos
+    assert rt.decodeBatch(64, 8) == []
+
+
+def test_upload_named_tensors_equals_synthetic(cuda):
+    """build(tensors) through ModelUploader semantics == the synthetic build."""
+    cfg = small_config(layers=1, vocab=1000)
+    from vibethinker_webgpu_lora_b200.quantize import synth_normal
+    from vibethinker_webgpu_lora_b200 import _lib as L
+    lib = L.lib()
+    H, I = cfg["hiddenSize"], cfg["intermediateSize"]
+    dims = [(2048, H), (256, H), (256, H), (H, 2048), (I, H), (I, H), (H, I)]
+    names = ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+             "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"]
+    t = {"model.embed_tokens.weight": synth_normal(1000 * H, lib.eg_synth_stream_at(SEED, 0), 0.02).reshape(1000, H),
+         "model.norm.weight": np.ones(H, np.float32),
+         "model.layers.0.input_layernorm.weight": np.ones(H, np.float32),
+         "model.layers.0.post_attention_layernorm.weight": np.ones(H, np.float32)}
+    for p, (n, k) in enumerate(dims):
+        t[f"model.layers.0.{names[p]}.weight"] = synth_normal(n * k, lib.eg_synth_stream_at(SEED, 1 + p), 0.02).reshape(n, k)
+        if p < 3:
+            t[f"model.layers.0.{names[p]}.bias"] = synth_normal(n, lib.eg_synth_stream_at(SEED, 8 + p), 0.02)
+    a = E.QwenB200(cfg, dict(maxCtx=32)).build(t)
+    b = E.QwenB200(cfg, dict(maxCtx=32)).build("synthetic", seed=SEED)
+    a.prefillBatch([1, 2, 3])
+    b.prefillBatch([1, 2, 3])
+    assert np.array_equal(a.readLogits(), b.readLogits())
+
+
+@pytest.mark.slow
+def test_full_model_greedy_128(cuda):
+    """Qwen2.5-3B shape, 32-token prompt, 128 greedy tokens."""
+    cfg = E.QWEN25_3B
+    rt, orc = make(cfg, True, max_ctx=256)
+    prompt = O.token_ids(32, 0xE6B00010, cfg["vocabSize"])
+    ids = rt.generate(prompt, 128)
+    ref, margins = orc.generate(prompt, 128)
+    n = assert_stream(ids, ref, margins)
+    print(f"full model: {n}/128 greedy tokens identical; min oracle margin {margins.min():.3g}")
+    if n == 128:
+        close(rt.readLogits(), orc.logits())

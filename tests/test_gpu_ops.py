@@ -1,0 +1,200 @@
+"""Single-op parity: every CUDA kernel entry point against the CPU oracle on
+the same seeded inputs.  Tolerances: logits/activations max-abs <= 1e-2 and
+mean-rel <= 1e-3 (the reference f32 path bar), much tighter where the op is
+short; index outputs (argmax, top-k ids, sampled id) bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from vibethinker_webgpu_lora_b200 import kernels as K
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def close(got, ref, max_abs, mean_rel=1e-3):
+    d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    assert d.max() <= max_abs, f"max abs {d.max()}"
+    rel = d.mean() / max(np.abs(ref).mean(), 1e-12)  # mean relative error
+    assert rel <= mean_rel, f"mean rel {rel}"
+
+
+@pytest.mark.parametrize("N,Kd,seed", [(2048, 2048, 1), (517, 2048, 2), (2560, 2048, 3),
+                                       (2048, 11008, 4), (16, 128, 5), (1, 256, 6)])
+def test_gemv_q4(cuda, N, Kd, seed):
+    W = O.normal(N * Kd, 0xE6B00001 + seed, 0.02).reshape(N, Kd)
+    x = O.normal(Kd, 0xE6B00002 + seed, 1.0)
+    bias = O.normal(N, 0xE6B00003 + seed, 0.02)
+    p, s = O.quantize_int4_group(W)
+    ref = O.gemv_q4(x, p, s, N, Kd, bias=bias)
+    y = torch.zeros(N, device=cuda)
+    K.gemv_q4(dev(x), dev(p), dev(s), N, Kd, y, bias=dev(bias))
+    close(host(y), ref, 2e-4, 1e-4)
+    # accumulate (GEMV4_ADD): y += W x
+    y0 = O.normal(N, 9, 1.0)
+    yt = dev(y0)
+    K.gemv_q4(dev(x), dev(p), dev(s), N, Kd, yt, accumulate=True)
+    ref2 = O.gemv_q4(x, p, s, N, Kd, y=y0.copy(), add=True)
+    close(host(yt), ref2, 2e-4, 1e-4)
+
+
+def test_gemv_q4_large_activations(cuda):
+    """|x| beyond the f16 range goes through the power-of-two prescale."""
+    N, Kd = 64, 2048
+    W = O.normal(N * Kd, 41, 0.02).reshape(N, Kd)
+    x = O.normal(Kd, 42, 1.0) * 3e5
+    p, s = O.quantize_int4_group(W)
+    ref = O.gemv_q4(x, p, s, N, Kd)
+    y = torch.zeros(N, device=cuda)
+    K.gemv_q4(dev(x), dev(p), dev(s), N, Kd, y)
+    got = host(y)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_gate_up_silu(cuda):
+    N, Kd = 11008, 2048
+    W = O.normal(2 * N * Kd, 51, 0.02).reshape(2 * N, Kd)
+    x = O.normal(Kd, 52, 1.0)
+    p, s = O.quantize_int4_group(W)
+    ref = O.gate_up_silu(x, p, s, N, Kd)
+    y = torch.zeros(N, device=cuda)
+    K.gate_up_silu(dev(x), dev(p), dev(s), N, Kd, y)
+    close(host(y), ref, 1e-4, 1e-3)
+
+
+@pytest.mark.parametrize("N", [151936, 1000, 17])
+def test_gemv_q8(cuda, N):
+    Kd = 2048
+    W = O.normal(N * Kd, 61, 0.02).reshape(N, Kd)
+    x = O.normal(Kd, 62, 1.0)
+    p, s = O.quantize_int8_rows(W)
+    ref = O.gemv_q8(x, p, s, N, Kd)
+    y = torch.zeros(N, device=cuda)
+    K.gemv_q8(dev(x), dev(p), dev(s), N, Kd, y)
+    close(host(y), ref, 1e-4, 1e-4)
+
+
+@pytest.mark.parametrize("f16", [0, 1])
+def test_rmsnorm(cuda, f16):
+    x = O.normal(2048, 71, 2.0)
+    g = O.normal(2048, 72, 0.1) + 1
+    ref = O.rmsnorm(x, g, 1e-6, bool(f16))
+    y = torch.zeros(2048, device=cuda)
+    K.rmsnorm(dev(x), dev(g), 2048, 1e-6, f16, y)
+    got = host(y)
+    # rsqrt differs from a correctly rounded 1/sqrt by <= 2 ulp
+    tol = 2e-3 if f16 else 1e-5
+    assert np.abs(got - ref).max() <= tol * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("f16", [0, 1])
+def test_rope_qk(cuda, f16):
+    c, s = O.rope_tables(512, 128, 1e6)
+    q = O.normal(2048, 81, 1.0)
+    k = O.normal(256, 82, 1.0)
+    for pos in (0, 1, 77, 511):
+        rq, rk = O.rope_qk(q, k, 16, 2, 128, pos, c, s, bool(f16))
+        tq, tk = dev(q), dev(k)
+        K.rope_qk(tq, tk, 16, 2, pos, dev(c), dev(s), f16)
+        assert np.array_equal(host(tq), rq) and np.array_equal(host(tk), rk)
+
+
+@pytest.mark.parametrize("f16", [0, 1])
+@pytest.mark.parametrize("pos,chunk", [(0, 0), (16, 0), (127, 0), (300, 0), (1000, 16), (4095, 0), (4095, 64)])
+def test_attn_decode(cuda, f16, pos, chunk):
+    nh, nkv, hd, max_ctx = 16, 2, 128, 4096
+    c, s = O.rope_tables(max_ctx, hd, 1e6)
+    ctx = pos + 1
+    kc = O.normal(max_ctx * nkv * hd, 91, 1.0)
+    vc = O.normal(max_ctx * nkv * hd, 92, 1.0)
+    if f16:  # an f16 cache holds f16-representable values
+        kc = kc.astype(np.float16).astype(np.float32)
+        vc = vc.astype(np.float16).astype(np.float32)
+    qkv = O.normal(nh * hd + 2 * nkv * hd, 93 + pos, 1.0)
+    q, k = O.rope_qk(qkv[: nh * hd], qkv[nh * hd: nh * hd + nkv * hd], nh, nkv, hd, pos, c, s, bool(f16))
+    v = qkv[nh * hd + nkv * hd:]
+    kref = kc.copy().reshape(max_ctx, nkv * hd)
+    vref = vc.copy().reshape(max_ctx, nkv * hd)
+    kref[pos] = k
+    vref[pos] = v
+    ref = O.attention(q, kref[:ctx].ravel(), vref[:ctx].ravel(), nh, nkv, ctx, hd, 128, bool(f16))
+    dt = torch.float16 if f16 else torch.float32
+    tk = torch.from_numpy(kc).to(dt).cuda()
+    tv = torch.from_numpy(vc).to(dt).cuda()
+    out = torch.zeros(nh * hd, device=cuda)
+    K.attn_decode(dev(qkv), tk, tv, dev(c), dev(s), nh, nkv, pos, max_ctx, f16, out, chunk=chunk)
+    close(host(out), ref, 2e-5 if not f16 else 2e-3, 1e-4 if not f16 else 1e-3)
+    # the new k/v row landed in the cache (f16-rounded in the f16 cache)
+    krow = host(tk.float()).reshape(max_ctx, nkv * hd)[pos]
+    vrow = host(tv.float()).reshape(max_ctx, nkv * hd)[pos]
+    assert np.array_equal(krow, k.astype(np.float16).astype(np.float32) if f16 else k)
+    assert np.array_equal(vrow, v.astype(np.float16).astype(np.float32) if f16 else v)
+
+
+def test_argmax_topk_ties_reference_case(cuda):
+    logits = np.full(300, -5, np.float32)
+    logits[1] = 7
+    logits[256] = 7
+    logits[129] = 6
+    out = torch.zeros(1, dtype=torch.int32, device=cuda)
+    K.argmax(dev(logits), 300, out)
+    assert int(host(out)[0]) == 1
+    ids = torch.zeros(3, dtype=torch.int32, device=cuda)
+    vals = torch.zeros(3, device=cuda)
+    K.topk(dev(logits), 300, 3, ids, vals)
+    assert host(ids).tolist() == [1, 256, 129]
+    sid = torch.tensor([10, 20, 30, 40], dtype=torch.int32, device=cuda)
+    sv = torch.tensor([4.0, 3.0, 2.0, 1.0], device=cuda)
+    K.sample_topk(sid, sv, 4, 1.0, 0.9, out)
+    assert int(host(out)[0]) == 30
+
+
+@pytest.mark.parametrize("n,k,seed", [(151936, 40, 1), (151936, 64, 2), (151936, 1, 3), (1000, 64, 4),
+                                      (70, 64, 5)])
+def test_topk_vs_oracle(cuda, n, k, seed):
+    logits = O.normal(n, 100 + seed, 1.0)
+    logits[::97] = logits[5]  # many exact ties
+    rid, rv = O.topk(logits, k)
+    ids = torch.zeros(k, dtype=torch.int32, device=cuda)
+    vals = torch.zeros(k, device=cuda)
+    K.topk(dev(logits), n, k, ids, vals)
+    assert host(ids).astype(np.uint32).tolist() == rid.tolist()
+    assert np.array_equal(host(vals), rv)
+    out = torch.zeros(1, dtype=torch.int32, device=cuda)
+    K.argmax(dev(logits), n, out)
+    assert int(host(out)[0]) == O.argmax(logits)
+
+
+def test_sample_vs_oracle(cuda):
+    for seed in range(20):
+        vals = np.sort(O.normal(40, 200 + seed, 2.0))[::-1].copy()
+        ids = np.arange(1000, 1040, dtype=np.uint32)
+        r = float(O.uniform(1, 300 + seed)[0])
+        ref = O.sample_topk(ids, vals, 40, 0.7, r)
+        out = torch.zeros(1, dtype=torch.int32, device=cuda)
+        K.sample_topk(dev(ids.astype(np.int32)), dev(vals), 40, 0.7, r, out)
+        assert int(host(out)[0]) == ref
+
+
+def test_embed_and_lora_a(cuda):
+    V, H = 1000, 2048
+    W = O.normal(V * H, 301, 0.02).reshape(V, H)
+    p, s = O.quantize_int8_rows(W)
+    idt = torch.tensor([777], dtype=torch.int32, device=cuda)
+    out = torch.zeros(H, device=cuda)
+    K.embed(dev(p), dev(s), idt, H, out)
+    assert np.array_equal(host(out), O.embed(p, s, 777, H))
+    A = O.normal(8 * H, 302, 0.02)
+    x = O.normal(H, 303, 1.0)
+    d = torch.zeros(8, device=cuda)
+    K.lora_a(dev(x), dev(A), H, 8, d)
+    close(host(d), O.lora_a(x, A, H, 8), 1e-5, 1e-4)

@@ -1,0 +1,115 @@
+// eg_kernels.h -- internal launch API of the Emberglass B200 kernels.
+// Everything here takes device pointers and a stream; the C ABI in
+// eg_runtime.cu is built on top of it.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eg {
+
+// One LoRA module in device memory (src/lora_gpu.js:96-109 layout):
+// A [rank][in] f32, B [rank][out] f32, y += scale * (A x) . B.
+struct LoraMod {
+  const float* A;
+  const float* B;
+  int rank;
+  float scale;
+};
+
+enum XMode { X_PLAIN = 0, X_RMS = 1, X_EMBED_RMS = 2 };
+
+// Where a GEMV's input vector comes from (its prologue).
+struct XSrc {
+  int mode;
+  const float* x;       // X_PLAIN: the vector; X_RMS: hidden state to normalise
+  const float* norm_g;  // RMSNorm weight
+  float eps;
+  int f16;              // RMSNORM_F16 arithmetic (kernels.js:145-166)
+  // X_EMBED_RMS: hidden = embed(ids[*pos]) (EMBED_BUF, kernels.js:537-550),
+  // written to hidden_out by block 0, then normalised.
+  const uint32_t* emb_w;
+  const float* emb_s;
+  const int* pos;
+  const uint32_t* ids;
+  float* hidden_out;
+};
+
+enum EpiMode { EPI_STORE = 0, EPI_ADD = 1, EPI_SILU = 2 };
+
+struct Epi {
+  int mode;
+  float* y;
+  const float* bias;  // EPI_STORE only, may be null
+  int N;              // output rows (EPI_SILU: rows of one half)
+  // LoRA: up to 3 modules split by output row (q/k/v), or gate/up for SILU.
+  const LoraMod* mods;  // null => no LoRA
+  const float* lora_d;  // [3][kMaxRank] d = A x
+  int split1, split2;   // row boundaries between module 0/1 and 1/2
+};
+
+constexpr int kMaxRank = 256;
+constexpr int kCandMax = 148;  // candidate blocks of the argmax/top-k stage 1
+
+// Final step of a greedy/advance decode step, run by the LM head's last block.
+struct StepTail {
+  int* pos;            // device position counter, incremented by one
+  uint32_t* ids;       // token id per position: ids[pos+1] = argmax (greedy)
+  uint32_t* amax;      // s.amax equivalent
+  uint32_t* out_ids;   // out_ids[*out_idx] = argmax (greedy)
+  int* out_idx;
+  int greedy;          // 0: only advance pos
+  float* cand_v;       // [grid] per-block best value
+  uint32_t* cand_i;    // [grid] per-block best index
+  unsigned* counter;   // last-block-done counter (self-resetting)
+};
+
+int sm_count();
+
+// y = W4 x  (reference layout: packed u32 [N][K/8], scale f32 [N][K/128]).
+// dual: EPI_SILU over rows n and N+n of a packed [gate;up] matrix.
+void gemv_q4(const uint32_t* w, const float* s, int N, int K, const XSrc& x, const Epi& e,
+             cudaStream_t st, bool pdl);
+// y = W8 x * scale[n] (int8 rows).  tail != null fuses argmax/advance.
+void gemv_q8(const uint32_t* w, const float* s, int N, int K, const XSrc& x, float* y,
+             const StepTail* tail, cudaStream_t st, bool pdl);
+
+struct AttnArgs {
+  const float* qkv;  // raw q [nh*128] | k [nkv*128] | v [nkv*128] from the QKV GEMV
+  void* kc;          // [max_ctx][nkv][128] f16 or f32
+  void* vc;
+  const float* cosT;
+  const float* sinT;
+  const int* pos;    // device: current position (ctx = pos + 1)
+  int fixed_pos;     // used when pos == null
+  int nh, nkv, max_splits;
+  int kv_f16;        // 1: f16 cache + ATTN_*_F16 / ROPE_QK_F16 numerics
+  int chunk;         // 0: adaptive; >0 fixed keys per split
+  float *pm, *pz, *po;  // partials [nh][max_splits], po [nh][max_splits][128]
+  float* out;        // attention output [nh*128]
+  unsigned* counters;  // [nkv] split-arrival counters, zero between launches
+};
+int attn_max_splits(int max_ctx);
+void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
+
+// y[r] += A[r] . x for up to 3 modules (LORA_A, kernels.js:60-78); x from src.
+void lora_a(const XSrc& x, int K, const LoraMod* mods, int nmods, int max_rank, float* d,
+            cudaStream_t st, bool pdl);
+
+void rmsnorm(const float* x, const float* g, int K, float eps, int f16, float* y, cudaStream_t st);
+void rope_qk(float* q, float* k, int nq, int nkv, int pos, const float* cosT, const float* sinT,
+             int f16, cudaStream_t st);
+void embed_rows(const uint32_t* w, const float* s, const uint32_t* id_dev, int H, float* out,
+                cudaStream_t st);
+
+// Sampling (kernels.js:771-883).
+void argmax(const float* logits, int n, uint32_t* out, float* cand_v, uint32_t* cand_i,
+            cudaStream_t st);
+int topk_cand_blocks(int n);
+void topk(const float* logits, int n, int k, uint32_t* ids, float* vals, float* cand_v,
+          uint32_t* cand_i, cudaStream_t st);
+void sample_topk(const uint32_t* ids, const float* vals, int k, float temp, float r,
+                 uint32_t* out, uint32_t* out2, cudaStream_t st);
+
+void copy_u32(const uint32_t* src, uint32_t* dst, cudaStream_t st);
+
+}  // namespace eg

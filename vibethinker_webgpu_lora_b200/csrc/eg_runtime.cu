@@ -1,0 +1,1319 @@
+// eg_runtime.cu -- the QwenWGPU-equivalent runtime behind the C ABI.
+//
+// One runtime = one CUDA device + one stream.  Weights live in HBM in the
+// reference's packed layouts; q/k/v and gate/up are concatenated at upload as
+// _buildPackedProjectionBuffers does (runtime.js:607-659).  The decode step
+// (runtime.js:1466-1571) is a fixed sequence of kernels whose only changing
+// inputs (position, token id) live in device memory, so the whole step is
+// captured once in a CUDA graph and replayed per token; the LM head's last
+// block runs argmax and advances the position, so decodeBatch's chain of K
+// greedy tokens (runtime.js:1776-1793) needs no host round trip.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "eg_host.h"
+#include "eg_kernels.h"
+#include "emberglass.h"
+
+namespace eg {
+
+static thread_local char g_err[1024] = "";
+
+eg_status fail(eg_status st, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return st;
+}
+
+#define CK(x)                                                                              \
+  do {                                                                                     \
+    cudaError_t e_ = (x);                                                                  \
+    if (e_ != cudaSuccess) return eg::fail(EG_ERR_CUDA, "%s: %s", #x, cudaGetErrorString(e_)); \
+  } while (0)
+
+struct Layer {
+  uint32_t *qkv_w = nullptr, *o_w = nullptr, *gu_w = nullptr, *d_w = nullptr;
+  float *qkv_s = nullptr, *o_s = nullptr, *gu_s = nullptr, *d_s = nullptr, *qkv_b = nullptr;
+  float *in_norm = nullptr, *post_norm = nullptr;
+  void *kc = nullptr, *vc = nullptr;
+};
+
+struct DevState {
+  int pos;
+  int out_idx;
+};
+
+}  // namespace eg
+
+struct eg_lora {
+  std::vector<eg::LoraMod> table;  // [layers*7], rank 0 where absent
+  std::vector<void*> allocs;
+  std::vector<int64_t> shapes;     // per slot: rank, in, out
+  int max_rank = 0;
+};
+
+struct eg_rt {
+  eg_config c{};
+  eg_options o{};
+  cudaStream_t st = nullptr;
+  std::vector<eg::Layer> L;
+  uint32_t* emb_w = nullptr;
+  float* emb_s = nullptr;
+  float* final_norm = nullptr;
+  float *cosT = nullptr, *sinT = nullptr;
+  float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *tmp = nullptr, *logits = nullptr;
+  float *pm = nullptr, *pz = nullptr, *po = nullptr, *lora_d = nullptr;
+  eg::DevState* state = nullptr;
+  uint32_t *ids = nullptr, *amax = nullptr, *out_ids = nullptr, *sampled = nullptr;
+  float* cand_v = nullptr;
+  uint32_t* cand_i = nullptr;
+  unsigned* counter = nullptr;
+  unsigned* attn_counters = nullptr;
+  uint32_t* sample_ids = nullptr;
+  float* sample_vals = nullptr;
+  eg::LoraMod* lora_table = nullptr;  // device [layers*7]
+  uint32_t* h_small = nullptr;        // pinned readback staging
+  int max_splits = 0;
+  std::vector<void*> allocs;
+  std::set<std::string> seen;
+  bool finalized = false;
+  eg_lora* active = nullptr;
+  cudaGraphExec_t graph[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [greedy][lora]
+  int graph_rank[2] = {0, 0};
+  int launches_per_step = 0;
+  std::atomic<bool> busy{false};
+  int64_t weight_bytes = 0, kv_bytes = 0, scratch_bytes = 0;
+};
+
+namespace eg {
+
+static eg_status dalloc(eg_rt* rt, void** p, size_t bytes, int64_t* counter) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) return fail(EG_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  rt->allocs.push_back(*p);
+  if (counter) *counter += (int64_t)bytes;
+  return EG_OK;
+}
+#define DALLOC(ptr, bytes, ctr)                                                          \
+  do {                                                                                   \
+    void* p_ = nullptr;                                                                  \
+    eg_status s_ = eg::dalloc(rt, &p_, (bytes), (ctr));                                  \
+    if (s_) return s_;                                                                   \
+    (ptr) = reinterpret_cast<decltype(ptr)>(p_);                                         \
+  } while (0)
+
+struct Busy {
+  eg_rt* rt;
+  bool ok;
+  explicit Busy(eg_rt* r) : rt(r) { ok = !rt->busy.exchange(true); }
+  ~Busy() {
+    if (ok) rt->busy.store(false);
+  }
+};
+
+static void drop_graphs(eg_rt* rt) {
+  for (auto& g : rt->graph)
+    for (auto& x : g)
+      if (x) {
+        cudaGraphExecDestroy(x);
+        x = nullptr;
+      }
+}
+
+// ------------------------------------------------------------------ schema
+// Tensor names and shapes of model_schema.js:53-113.
+enum Role { R_EMBED, R_FINAL_NORM, R_IN_NORM, R_POST_NORM, R_PROJ, R_BIAS, R_UNKNOWN };
+struct Desc {
+  Role role = R_UNKNOWN;
+  int layer = -1, proj = -1;  // proj 0..6 = q,k,v,o,gate,up,down ; bias 0..2
+  int64_t rows = 0, cols = 0;  // expected shape (cols 0 => 1-D)
+};
+
+static const char* kProj[7] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                               "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj",
+                               "mlp.down_proj"};
+
+static void proj_shape(const eg_config& c, int p, int64_t* N, int64_t* K) {
+  const int64_t H = c.hidden_size, QD = (int64_t)c.num_heads * c.head_dim,
+                KVD = (int64_t)c.num_kv_heads * c.head_dim, I = c.intermediate_size;
+  const int64_t t[7][2] = {{QD, H}, {KVD, H}, {KVD, H}, {H, QD}, {I, H}, {I, H}, {H, I}};
+  *N = t[p][0];
+  *K = t[p][1];
+}
+
+static Desc describe(const eg_config& c, const char* name) {
+  Desc d;
+  if (!strcmp(name, "model.embed_tokens.weight")) {
+    d.role = R_EMBED;
+    d.rows = c.vocab_size;
+    d.cols = c.hidden_size;
+    return d;
+  }
+  if (!strcmp(name, "model.norm.weight")) {
+    d.role = R_FINAL_NORM;
+    d.rows = c.hidden_size;
+    return d;
+  }
+  int layer = -1, off = 0;
+  if (sscanf(name, "model.layers.%d.%n", &layer, &off) != 1 || off == 0 || layer < 0 ||
+      layer >= c.num_layers)
+    return d;
+  const char* rest = name + off;
+  d.layer = layer;
+  if (!strcmp(rest, "input_layernorm.weight")) {
+    d.role = R_IN_NORM;
+    d.rows = c.hidden_size;
+    return d;
+  }
+  if (!strcmp(rest, "post_attention_layernorm.weight")) {
+    d.role = R_POST_NORM;
+    d.rows = c.hidden_size;
+    return d;
+  }
+  for (int p = 0; p < 7; p++) {
+    const size_t n = strlen(kProj[p]);
+    if (strncmp(rest, kProj[p], n)) continue;
+    if (!strcmp(rest + n, ".weight")) {
+      d.role = R_PROJ;
+      d.proj = p;
+      proj_shape(c, p, &d.rows, &d.cols);
+      return d;
+    }
+    if (p < 3 && c.attention_bias && !strcmp(rest + n, ".bias")) {
+      d.role = R_BIAS;
+      d.proj = p;
+      int64_t K;
+      proj_shape(c, p, &d.rows, &K);
+      return d;
+    }
+  }
+  return d;
+}
+
+static std::vector<std::string> expected_names(const eg_config& c) {
+  std::vector<std::string> v = {"model.embed_tokens.weight", "model.norm.weight"};
+  char buf[128];
+  for (int i = 0; i < c.num_layers; i++) {
+    snprintf(buf, sizeof buf, "model.layers.%d.input_layernorm.weight", i);
+    v.push_back(buf);
+    snprintf(buf, sizeof buf, "model.layers.%d.post_attention_layernorm.weight", i);
+    v.push_back(buf);
+    for (int p = 0; p < 7; p++) {
+      snprintf(buf, sizeof buf, "model.layers.%d.%s.weight", i, kProj[p]);
+      v.push_back(buf);
+      if (p < 3 && c.attention_bias) {
+        snprintf(buf, sizeof buf, "model.layers.%d.%s.bias", i, kProj[p]);
+        v.push_back(buf);
+      }
+    }
+  }
+  return v;
+}
+
+static eg_status check_shape(const char* name, const Desc& d, const int64_t* shape, int ndim) {
+  const int want = d.cols ? 2 : 1;
+  bool ok = ndim == want && shape && shape[0] == d.rows && (want == 1 || shape[1] == d.cols);
+  if (ok) return EG_OK;
+  char got[64] = "", exp[64];
+  for (int i = 0; i < ndim && shape; i++)
+    snprintf(got + strlen(got), sizeof got - strlen(got), i ? ",%lld" : "%lld", (long long)shape[i]);
+  if (want == 2)
+    snprintf(exp, sizeof exp, "%lld,%lld", (long long)d.rows, (long long)d.cols);
+  else
+    snprintf(exp, sizeof exp, "%lld", (long long)d.rows);
+  return fail(EG_ERR_ARG, "shape mismatch for %s: got [%s], expected [%s]", name, got, exp);
+}
+
+// Allocate every weight buffer (once, on the first upload).
+static eg_status alloc_weights(eg_rt* rt) {
+  if (!rt->L.empty()) return EG_OK;
+  const eg_config& c = rt->c;
+  const int64_t H = c.hidden_size, QD = (int64_t)c.num_heads * c.head_dim,
+                KVD = (int64_t)c.num_kv_heads * c.head_dim, I = c.intermediate_size;
+  const int64_t NQKV = QD + 2 * KVD;
+  int64_t* wb = &rt->weight_bytes;
+  rt->L.resize(c.num_layers);
+  for (auto& l : rt->L) {
+    DALLOC(l.qkv_w, NQKV * H / 2, wb);
+    DALLOC(l.qkv_s, NQKV * (H / 128) * 4, wb);
+    DALLOC(l.qkv_b, NQKV * 4, wb);
+    DALLOC(l.o_w, H * QD / 2, wb);
+    DALLOC(l.o_s, H * (QD / 128) * 4, wb);
+    DALLOC(l.gu_w, 2 * I * H / 2, wb);
+    DALLOC(l.gu_s, 2 * I * (H / 128) * 4, wb);
+    DALLOC(l.d_w, H * I / 2, wb);
+    DALLOC(l.d_s, H * (I / 128) * 4, wb);
+    DALLOC(l.in_norm, H * 4, wb);
+    DALLOC(l.post_norm, H * 4, wb);
+    CK(cudaMemsetAsync(l.qkv_b, 0, NQKV * 4, rt->st));  // enc.clearBuffer(bias), runtime.js:625
+  }
+  DALLOC(rt->emb_w, (int64_t)c.vocab_size * H, wb);
+  DALLOC(rt->emb_s, (int64_t)c.vocab_size * 4, wb);
+  DALLOC(rt->final_norm, H * 4, wb);
+  return EG_OK;
+}
+
+// Destination of a projection/bias inside the packed buffers.
+static void proj_dest(eg_rt* rt, const Desc& d, uint32_t** w, float** s, int64_t* row0) {
+  const eg_config& c = rt->c;
+  const int64_t QD = (int64_t)c.num_heads * c.head_dim, KVD = (int64_t)c.num_kv_heads * c.head_dim;
+  eg::Layer& l = rt->L[d.layer];
+  switch (d.proj) {
+    case 0: *w = l.qkv_w; *s = l.qkv_s; *row0 = 0; break;
+    case 1: *w = l.qkv_w; *s = l.qkv_s; *row0 = QD; break;
+    case 2: *w = l.qkv_w; *s = l.qkv_s; *row0 = QD + KVD; break;
+    case 3: *w = l.o_w; *s = l.o_s; *row0 = 0; break;
+    case 4: *w = l.gu_w; *s = l.gu_s; *row0 = 0; break;
+    case 5: *w = l.gu_w; *s = l.gu_s; *row0 = c.intermediate_size; break;
+    default: *w = l.d_w; *s = l.d_s; *row0 = 0; break;
+  }
+}
+
+static eg_status put_quantized(eg_rt* rt, const char* name, const Desc& d, int kind,
+                               const uint32_t* packed, const float* scale) {
+  if (d.role == R_EMBED) {
+    if (kind != 8) return fail(EG_ERR_ARG, "%s must be int8 rows", name);
+    CK(cudaMemcpyAsync(rt->emb_w, packed, d.rows * d.cols, cudaMemcpyHostToDevice, rt->st));
+    CK(cudaMemcpyAsync(rt->emb_s, scale, d.rows * 4, cudaMemcpyHostToDevice, rt->st));
+  } else {
+    if (kind != 4) return fail(EG_ERR_ARG, "%s must be int4 group-128", name);
+    uint32_t* w;
+    float* s;
+    int64_t row0;
+    proj_dest(rt, d, &w, &s, &row0);
+    const int64_t gpr = d.cols / 128;
+    CK(cudaMemcpyAsync(w + row0 * d.cols / 8, packed, d.rows * d.cols / 2, cudaMemcpyHostToDevice,
+                       rt->st));
+    CK(cudaMemcpyAsync(s + row0 * gpr, scale, d.rows * gpr * 4, cudaMemcpyHostToDevice, rt->st));
+  }
+  CK(cudaStreamSynchronize(rt->st));
+  rt->seen.insert(name);
+  return EG_OK;
+}
+
+static eg_status put_f32(eg_rt* rt, const char* name, const Desc& d, const float* data) {
+  float* dst = nullptr;
+  switch (d.role) {
+    case R_FINAL_NORM: dst = rt->final_norm; break;
+    case R_IN_NORM: dst = rt->L[d.layer].in_norm; break;
+    case R_POST_NORM: dst = rt->L[d.layer].post_norm; break;
+    case R_BIAS: {
+      const eg_config& c = rt->c;
+      const int64_t QD = (int64_t)c.num_heads * c.head_dim,
+                    KVD = (int64_t)c.num_kv_heads * c.head_dim;
+      dst = rt->L[d.layer].qkv_b + (d.proj == 0 ? 0 : d.proj == 1 ? QD : QD + KVD);
+      break;
+    }
+    default: return fail(EG_ERR_ARG, "%s is not an f32 tensor", name);
+  }
+  CK(cudaMemcpyAsync(dst, data, d.rows * 4, cudaMemcpyHostToDevice, rt->st));
+  CK(cudaStreamSynchronize(rt->st));
+  rt->seen.insert(name);
+  return EG_OK;
+}
+
+static eg_status upload_f32_tensor(eg_rt* rt, const char* name, const Desc& d, const float* data) {
+  if (d.role == R_EMBED) {
+    std::vector<uint32_t> pk((size_t)d.rows * d.cols / 4);
+    std::vector<float> sc((size_t)d.rows);
+    eg_status s = eg_quantize_int8_rows(data, (int)d.rows, (int)d.cols, pk.data(), sc.data());
+    if (s) return s;
+    return put_quantized(rt, name, d, 8, pk.data(), sc.data());
+  }
+  if (d.role == R_PROJ) {
+    std::vector<uint32_t> pk((size_t)d.rows * d.cols / 8);
+    std::vector<float> sc((size_t)d.rows * d.cols / 128);
+    eg_status s = eg_quantize_int4_group(data, (int)d.rows, (int)d.cols, 128, pk.data(), sc.data());
+    if (s) return s;
+    return put_quantized(rt, name, d, 4, pk.data(), sc.data());
+  }
+  return put_f32(rt, name, d, data);
+}
+
+// ------------------------------------------------------------------ the step
+struct StepOpts {
+  bool greedy, lora, pdl;
+  int lora_rank;
+  std::vector<cudaEvent_t>* marks;  // profiling: event after each category
+};
+
+static void mark(eg_rt* rt, const StepOpts& so, int cat, std::vector<int>* cats) {
+  if (!so.marks) return;
+  cudaEvent_t e;
+  cudaEventCreate(&e);
+  cudaEventRecord(e, rt->st);
+  so.marks->push_back(e);
+  cats->push_back(cat);
+}
+
+// One decode step at the device-resident position: runtime.js:1466-1571
+// with default flags, plus EMBED_BUF in front and (greedy) ARGMAX behind.
+static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
+  const eg_config& c = rt->c;
+  const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
+  const int I = c.intermediate_size, NQKV = QD + 2 * KVD;
+  cudaStream_t st = rt->st;
+  const bool pdl = so.pdl;
+  int launches = 0;
+  const LoraMod* lt = rt->lora_table;
+  for (int i = 0; i < c.num_layers; i++) {
+    const Layer& l = rt->L[i];
+    XSrc xa = {};
+    xa.mode = i == 0 ? X_EMBED_RMS : X_RMS;
+    xa.x = rt->hidden;
+    xa.norm_g = l.in_norm;
+    xa.eps = c.rms_norm_eps;
+    xa.f16 = rt->o.kv_f16;
+    xa.emb_w = rt->emb_w;
+    xa.emb_s = rt->emb_s;
+    xa.pos = &rt->state->pos;
+    xa.ids = rt->ids;
+    xa.hidden_out = rt->hidden;
+    if (so.lora) {
+      XSrc xl = xa;
+      xl.hidden_out = nullptr;
+      lora_a(xl, H, lt + i * 7 + 0, 3, so.lora_rank, rt->lora_d, st, pdl);
+      launches++;
+    }
+    Epi e = {};
+    e.mode = EPI_STORE;
+    e.y = rt->qkv;
+    e.bias = c.attention_bias ? l.qkv_b : nullptr;
+    e.N = NQKV;
+    e.mods = so.lora ? lt + i * 7 + 0 : nullptr;
+    e.lora_d = rt->lora_d;
+    e.split1 = QD;
+    e.split2 = QD + KVD;
+    gemv_q4(l.qkv_w, l.qkv_s, NQKV, H, xa, e, st, pdl);
+    launches++;
+    mark(rt, so, 0, cats);
+
+    AttnArgs a = {};
+    a.qkv = rt->qkv;
+    a.kc = l.kc;
+    a.vc = l.vc;
+    a.cosT = rt->cosT;
+    a.sinT = rt->sinT;
+    a.pos = &rt->state->pos;
+    a.nh = c.num_heads;
+    a.nkv = c.num_kv_heads;
+    a.max_splits = rt->max_splits;
+    a.kv_f16 = rt->o.kv_f16;
+    a.chunk = rt->o.attn_chunk;
+    a.pm = rt->pm;
+    a.pz = rt->pz;
+    a.po = rt->po;
+    a.out = rt->attn;
+    a.counters = rt->attn_counters;
+    attn_decode(a, st, pdl);
+    launches += 1;
+    mark(rt, so, 1, cats);
+
+    XSrc xo = {};
+    xo.mode = X_PLAIN;
+    xo.x = rt->attn;
+    if (so.lora) {
+      lora_a(xo, QD, lt + i * 7 + 3, 1, so.lora_rank, rt->lora_d, st, pdl);
+      launches++;
+    }
+    Epi eo = {};
+    eo.mode = EPI_ADD;  // GEMV4_ADD: hidden += Wo attn (runtime.js:1531)
+    eo.y = rt->hidden;
+    eo.N = H;
+    eo.mods = so.lora ? lt + i * 7 + 3 : nullptr;
+    eo.lora_d = rt->lora_d;
+    eo.split1 = eo.split2 = H;
+    gemv_q4(l.o_w, l.o_s, H, QD, xo, eo, st, pdl);
+    launches++;
+    mark(rt, so, 2, cats);
+
+    XSrc xb = {};
+    xb.mode = X_RMS;
+    xb.x = rt->hidden;
+    xb.norm_g = l.post_norm;
+    xb.eps = c.rms_norm_eps;
+    xb.f16 = rt->o.kv_f16;
+    if (so.lora) {
+      lora_a(xb, H, lt + i * 7 + 4, 2, so.lora_rank, rt->lora_d, st, pdl);
+      launches++;
+    }
+    Epi eg = {};
+    eg.mode = EPI_SILU;
+    eg.y = rt->tmp;
+    eg.N = I;
+    eg.mods = so.lora ? lt + i * 7 + 4 : nullptr;
+    eg.lora_d = rt->lora_d;
+    gemv_q4(l.gu_w, l.gu_s, I, H, xb, eg, st, pdl);
+    launches++;
+    mark(rt, so, 3, cats);
+
+    XSrc xd = {};
+    xd.mode = X_PLAIN;
+    xd.x = rt->tmp;
+    if (so.lora) {
+      lora_a(xd, I, lt + i * 7 + 6, 1, so.lora_rank, rt->lora_d, st, pdl);
+      launches++;
+    }
+    Epi ed = {};
+    ed.mode = EPI_ADD;
+    ed.y = rt->hidden;
+    ed.N = H;
+    ed.mods = so.lora ? lt + i * 7 + 6 : nullptr;
+    ed.lora_d = rt->lora_d;
+    ed.split1 = ed.split2 = H;
+    gemv_q4(l.d_w, l.d_s, H, I, xd, ed, st, pdl);
+    launches++;
+    mark(rt, so, 4, cats);
+  }
+  XSrc xf = {};
+  xf.mode = X_RMS;
+  xf.x = rt->hidden;
+  xf.norm_g = rt->final_norm;
+  xf.eps = c.rms_norm_eps;
+  xf.f16 = rt->o.kv_f16;
+  StepTail tail = {};
+  tail.pos = &rt->state->pos;
+  tail.ids = rt->ids;
+  tail.amax = rt->amax;
+  tail.out_ids = rt->out_ids;
+  tail.out_idx = &rt->state->out_idx;
+  tail.greedy = so.greedy ? 1 : 0;
+  tail.cand_v = rt->cand_v;
+  tail.cand_i = rt->cand_i;
+  tail.counter = rt->counter;
+  gemv_q8(rt->emb_w, rt->emb_s, c.vocab_size, H, xf, rt->logits, &tail, st, pdl);
+  launches++;
+  mark(rt, so, 5, cats);
+  return launches;
+}
+
+static eg_status run_step(eg_rt* rt, bool greedy) {
+  const bool lora = rt->active != nullptr;
+  const int rank = lora ? rt->active->max_rank : 0;
+  StepOpts so{greedy, lora, rt->o.use_pdl != 0, rank, nullptr};
+  if (!rt->o.use_graphs) {
+    rt->launches_per_step = enqueue_step(rt, so, nullptr);
+    CK(cudaGetLastError());
+    return EG_OK;
+  }
+  cudaGraphExec_t& ge = rt->graph[greedy][lora];
+  if (ge && lora && rt->graph_rank[greedy] < rank) {
+    cudaGraphExecDestroy(ge);
+    ge = nullptr;
+  }
+  if (!ge) {
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(rt->st, cudaStreamCaptureModeThreadLocal));
+    rt->launches_per_step = enqueue_step(rt, so, nullptr);
+    cudaError_t e1 = cudaGetLastError();
+    cudaError_t e2 = cudaStreamEndCapture(rt->st, &g);
+    if (e1 != cudaSuccess) return fail(EG_ERR_CUDA, "step capture: %s", cudaGetErrorString(e1));
+    if (e2 != cudaSuccess) return fail(EG_ERR_CUDA, "end capture: %s", cudaGetErrorString(e2));
+    cudaError_t e3 = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e3 != cudaSuccess) return fail(EG_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e3));
+    if (lora) rt->graph_rank[greedy] = rank;
+  }
+  CK(cudaGraphLaunch(ge, rt->st));
+  return EG_OK;
+}
+
+__global__ void set_state_kernel(DevState* s, uint32_t* ids, int pos, int out_idx, int set_id,
+                                 uint32_t id, const uint32_t* id_from) {
+  s->pos = pos;
+  s->out_idx = out_idx;
+  if (set_id) ids[pos] = id_from ? *id_from : id;
+}
+
+static eg_status set_state(eg_rt* rt, int pos, int set_id, uint32_t id, const uint32_t* id_from) {
+  set_state_kernel<<<1, 1, 0, rt->st>>>(rt->state, rt->ids, pos, 0, set_id, id, id_from);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+static eg_status need_ready(eg_rt* rt) {
+  if (!rt) return fail(EG_ERR_ARG, "null runtime");
+  if (!rt->finalized) return fail(EG_ERR_STATE, "runtime not built: call eg_finalize first");
+  return EG_OK;
+}
+
+static eg_status sync(eg_rt* rt) {
+  CK(cudaStreamSynchronize(rt->st));
+  return EG_OK;
+}
+
+static bool parse_key(const char* key, int layers, int* layer, int* proj) {
+  int i = -1, off = 0;
+  char sub[64] = "";
+  if (!key || sscanf(key, "layers.%d.%n", &i, &off) != 1 || off == 0) return false;
+  if (i < 0 || i >= layers) return false;
+  snprintf(sub, sizeof sub, "%s", key + off);
+  for (int p = 0; p < 7; p++)
+    if (!strcmp(sub, kProj[p])) {
+      *layer = i;
+      *proj = p;
+      return true;
+    }
+  return false;
+}
+
+// Per-device scratch for single-op entry points.
+struct OpScratch {
+  std::mutex mu;
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+static OpScratch g_scratch[64];
+static eg_status op_scratch(size_t bytes, void** out) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  OpScratch& s = g_scratch[dev & 63];
+  std::lock_guard<std::mutex> lk(s.mu);
+  if (s.bytes < bytes) {
+    if (s.p) {
+      CK(cudaDeviceSynchronize());
+      cudaFree(s.p);
+      s.p = nullptr;
+      s.bytes = 0;
+    }
+    CK(cudaMalloc(&s.p, bytes));
+    s.bytes = bytes;
+  }
+  *out = s.p;
+  return EG_OK;
+}
+
+}  // namespace eg
+
+using namespace eg;
+
+extern "C" {
+
+EG_API const char* eg_last_error(void) { return g_err; }
+EG_API const char* eg_version(void) { return "emberglass-b200 0.1 (sm_100a)"; }
+
+EG_API void eg_default_config(eg_config* c) {
+  if (!c) return;
+  *c = eg_config{2048, 36, 16, 2, 128, 11008, 151936, 1e-6f, 1000000.0, 1, 1};
+}
+EG_API void eg_default_options(eg_options* o) {
+  if (!o) return;
+  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1};
+}
+
+EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** out) {
+  if (!cfg || !out) return fail(EG_ERR_ARG, "eg_create: null argument");
+  *out = nullptr;
+  const eg_config& c = *cfg;
+  if (!c.tie_word_embeddings)
+    return fail(EG_ERR_ARG, "QwenWGPU currently requires tied input/output embeddings");
+  if (c.head_dim != 128) return fail(EG_ERR_ARG, "head_dim must be 128");
+  if (c.num_heads <= 0 || c.num_kv_heads <= 0 || c.num_heads % c.num_kv_heads ||
+      c.num_heads / c.num_kv_heads > 8)
+    return fail(EG_ERR_ARG, "num_heads must be a multiple of num_kv_heads (group <= 8)");
+  if (c.hidden_size % 128 || c.intermediate_size % 128 || (c.num_heads * c.head_dim) % 128 ||
+      c.hidden_size > 12288 || c.intermediate_size > 12288)
+    return fail(EG_ERR_ARG, "hidden/intermediate sizes must be multiples of 128, at most 12288");
+  if (c.vocab_size <= 0 || c.vocab_size > 148 * 2048 || c.num_layers <= 0)
+    return fail(EG_ERR_ARG, "vocab_size must be in [1, 303104]");
+  eg_options o;
+  eg_default_options(&o);
+  if (opt) o = *opt;
+  if (o.max_ctx <= 0) o.max_ctx = 8192;
+  if (o.max_prefill_t <= 0 || o.max_prefill_t > o.max_ctx) o.max_prefill_t = o.max_ctx;
+  if (o.decode_batch_capacity <= 0) o.decode_batch_capacity = 32;
+  if (o.max_sampling_top_k <= 0 || o.max_sampling_top_k > 64) o.max_sampling_top_k = 64;
+  if (o.sampling_top_k <= 0) o.sampling_top_k = 40;
+  o.max_sampling_top_k = std::max(o.max_sampling_top_k, std::min(o.sampling_top_k, 64));
+  if (o.attn_chunk < 0 || o.attn_chunk > 64 || o.attn_chunk % 16)
+    return fail(EG_ERR_ARG, "attn_chunk must be 0 or a multiple of 16 up to 64");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || o.device < 0 || o.device >= ndev)
+    return fail(EG_ERR_CUDA, "no CUDA device %d", o.device);
+  CK(cudaSetDevice(o.device));
+  eg_rt* rt = new eg_rt();
+  rt->c = c;
+  rt->o = o;
+  if (cudaStreamCreateWithFlags(&rt->st, cudaStreamNonBlocking) != cudaSuccess) {
+    delete rt;
+    return fail(EG_ERR_CUDA, "stream create failed");
+  }
+  *out = rt;
+  return EG_OK;
+}
+
+EG_API eg_status eg_destroy(eg_rt* rt) {
+  if (!rt) return EG_OK;
+  cudaSetDevice(rt->o.device);
+  cudaStreamSynchronize(rt->st);
+  drop_graphs(rt);
+  for (void* p : rt->allocs) cudaFree(p);
+  if (rt->h_small) cudaFreeHost(rt->h_small);
+  cudaStreamDestroy(rt->st);
+  delete rt;
+  return EG_OK;
+}
+
+EG_API eg_status eg_upload_tensor(eg_rt* rt, const char* name, const float* data,
+                                  const int64_t* shape, int ndim) {
+  if (!rt || !name || !data) return fail(EG_ERR_ARG, "eg_upload_tensor: null argument");
+  if (rt->finalized) return fail(EG_ERR_STATE, "weights are already finalized");
+  CK(cudaSetDevice(rt->o.device));
+  Desc d = describe(rt->c, name);
+  if (d.role == R_UNKNOWN) return EG_OK;  // schema.validateTensor: unknown names are skipped
+  eg_status s = check_shape(name, d, shape, ndim);
+  if (s) return s;
+  if ((s = alloc_weights(rt))) return s;
+  return upload_f32_tensor(rt, name, d, data);
+}
+
+EG_API eg_status eg_upload_quantized(eg_rt* rt, const char* name, int kind, const uint32_t* packed,
+                                     const float* scale, const int64_t* shape, int ndim) {
+  if (!rt || !name || !packed || !scale) return fail(EG_ERR_ARG, "eg_upload_quantized: null argument");
+  if (rt->finalized) return fail(EG_ERR_STATE, "weights are already finalized");
+  CK(cudaSetDevice(rt->o.device));
+  Desc d = describe(rt->c, name);
+  if (d.role != R_PROJ && d.role != R_EMBED)
+    return fail(EG_ERR_ARG, "%s is not a quantised tensor", name);
+  eg_status s = check_shape(name, d, shape, ndim);
+  if (s) return s;
+  if ((s = alloc_weights(rt))) return s;
+  return put_quantized(rt, name, d, kind, packed, scale);
+}
+
+EG_API eg_status eg_build_synthetic(eg_rt* rt, uint64_t seed, double std_w) {
+  if (!rt) return fail(EG_ERR_ARG, "null runtime");
+  if (rt->finalized) return fail(EG_ERR_STATE, "weights are already finalized");
+  CK(cudaSetDevice(rt->o.device));
+  eg_status s = alloc_weights(rt);
+  if (s) return s;
+  const eg_config& c = rt->c;
+  const int H = c.hidden_size;
+  {  // embedding in row chunks (int8 rows quantise independently)
+    const int rows = 8192;
+    std::vector<float> f((size_t)rows * H);
+    std::vector<uint32_t> pk((size_t)rows * H / 4);
+    std::vector<float> sc(rows);
+    const uint64_t sd = stream_at(seed, 0);
+    for (int r0 = 0; r0 < c.vocab_size; r0 += rows) {
+      const int nr = std::min(rows, c.vocab_size - r0);
+      fill_normal(f.data(), (int64_t)nr * H, sd, std_w, (int64_t)r0 * H);
+      if ((s = eg_quantize_int8_rows(f.data(), nr, H, pk.data(), sc.data()))) return s;
+      CK(cudaMemcpy(rt->emb_w + (size_t)r0 * H / 4, pk.data(), (size_t)nr * H, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(rt->emb_s + r0, sc.data(), (size_t)nr * 4, cudaMemcpyHostToDevice));
+    }
+    rt->seen.insert("model.embed_tokens.weight");
+  }
+  std::vector<float> ones(std::max(H, 1), 1.0f);
+  int64_t shp[2] = {H, 0};
+  if ((s = eg_upload_tensor(rt, "model.norm.weight", ones.data(), shp, 1))) return s;
+  std::vector<float> f;
+  char name[160];
+  for (int i = 0; i < c.num_layers; i++) {
+    snprintf(name, sizeof name, "model.layers.%d.input_layernorm.weight", i);
+    if ((s = eg_upload_tensor(rt, name, ones.data(), shp, 1))) return s;
+    snprintf(name, sizeof name, "model.layers.%d.post_attention_layernorm.weight", i);
+    if ((s = eg_upload_tensor(rt, name, ones.data(), shp, 1))) return s;
+    for (int p = 0; p < 7; p++) {
+      int64_t sh[2];
+      proj_shape(c, p, &sh[0], &sh[1]);
+      f.resize((size_t)sh[0] * sh[1]);
+      fill_normal(f.data(), sh[0] * sh[1], stream_at(seed, 16 * i + 1 + p), std_w, 0);
+      snprintf(name, sizeof name, "model.layers.%d.%s.weight", i, kProj[p]);
+      if ((s = eg_upload_tensor(rt, name, f.data(), sh, 2))) return s;
+      if (p < 3 && c.attention_bias) {
+        f.resize(sh[0]);
+        fill_normal(f.data(), sh[0], stream_at(seed, 16 * i + 8 + p), std_w, 0);
+        snprintf(name, sizeof name, "model.layers.%d.%s.bias", i, kProj[p]);
+        if ((s = eg_upload_tensor(rt, name, f.data(), sh, 1))) return s;
+      }
+    }
+  }
+  return EG_OK;
+}
+
+EG_API eg_status eg_finalize(eg_rt* rt) {
+  if (!rt) return fail(EG_ERR_ARG, "null runtime");
+  if (rt->finalized) return EG_OK;
+  CK(cudaSetDevice(rt->o.device));
+  std::vector<std::string> missing;
+  for (auto& n : expected_names(rt->c))
+    if (!rt->seen.count(n)) missing.push_back(n);
+  if (!missing.empty()) {
+    std::string sample;
+    for (size_t i = 0; i < missing.size() && i < 12; i++) sample += (i ? ", " : "") + missing[i];
+    return fail(EG_ERR_STATE, "missing %zu required tensor(s): %s%s", missing.size(),
+                sample.c_str(), missing.size() > 12 ? ", ..." : "");
+  }
+  const eg_config& c = rt->c;
+  const int hd = c.head_dim, H = c.hidden_size, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
+  const int mc = rt->o.max_ctx;
+  std::vector<float> cs((size_t)mc * hd), sn((size_t)mc * hd);
+  rope_tables(mc, hd, c.rope_theta, cs.data(), sn.data());
+  int64_t* sb = &rt->scratch_bytes;
+  DALLOC(rt->cosT, cs.size() * 4, sb);
+  DALLOC(rt->sinT, sn.size() * 4, sb);
+  CK(cudaMemcpy(rt->cosT, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(rt->sinT, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  const size_t kvel = (size_t)mc * KVD * (rt->o.kv_f16 ? 2 : 4);
+  for (auto& l : rt->L) {
+    DALLOC(l.kc, kvel, &rt->kv_bytes);
+    DALLOC(l.vc, kvel, &rt->kv_bytes);
+    CK(cudaMemset(l.kc, 0, kvel));
+    CK(cudaMemset(l.vc, 0, kvel));
+  }
+  rt->max_splits = attn_max_splits(mc);
+  DALLOC(rt->hidden, H * 4, sb);
+  DALLOC(rt->qkv, (QD + 2 * KVD) * 4, sb);
+  DALLOC(rt->attn, QD * 4, sb);
+  DALLOC(rt->tmp, (size_t)c.intermediate_size * 4, sb);
+  DALLOC(rt->logits, (size_t)c.vocab_size * 4, sb);
+  DALLOC(rt->pm, (size_t)c.num_heads * rt->max_splits * 4, sb);
+  DALLOC(rt->pz, (size_t)c.num_heads * rt->max_splits * 4, sb);
+  DALLOC(rt->po, (size_t)c.num_heads * rt->max_splits * hd * 4, sb);
+  DALLOC(rt->lora_d, 3 * kMaxRank * 4, sb);
+  DALLOC(rt->state, sizeof(DevState), sb);
+  DALLOC(rt->ids, ((size_t)mc + 1) * 4, sb);
+  DALLOC(rt->amax, 4, sb);
+  DALLOC(rt->sampled, 4, sb);
+  DALLOC(rt->out_ids, (size_t)std::max(rt->o.decode_batch_capacity, mc) * 4, sb);
+  const int ncand = std::max(sm_count() * 4, 148 * 64);
+  DALLOC(rt->cand_v, (size_t)ncand * 4, sb);
+  DALLOC(rt->cand_i, (size_t)ncand * 4, sb);
+  DALLOC(rt->counter, 4, sb);
+  DALLOC(rt->attn_counters, 64 * 4, sb);
+  CK(cudaMemset(rt->attn_counters, 0, 64 * 4));
+  DALLOC(rt->sample_ids, 64 * 4, sb);
+  DALLOC(rt->sample_vals, 64 * 4, sb);
+  DALLOC(rt->lora_table, (size_t)c.num_layers * 7 * sizeof(LoraMod), sb);
+  CK(cudaMemset(rt->counter, 0, 4));
+  CK(cudaMemset(rt->hidden, 0, H * 4));
+  CK(cudaMemset(rt->logits, 0, (size_t)c.vocab_size * 4));
+  CK(cudaMemset(rt->ids, 0, ((size_t)mc + 1) * 4));
+  CK(cudaMemset(rt->amax, 0, 4));
+  CK(cudaMemset(rt->state, 0, sizeof(DevState)));
+  CK(cudaMemset(rt->lora_table, 0, (size_t)c.num_layers * 7 * sizeof(LoraMod)));
+  CK(cudaMallocHost(&rt->h_small, (size_t)std::max(mc, rt->o.decode_batch_capacity) * 4 + 64));
+  CK(cudaDeviceSynchronize());
+  rt->finalized = true;
+  return EG_OK;
+}
+
+EG_API eg_status eg_token(eg_rt* rt, uint32_t id, int pos) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (pos < 0 || pos >= rt->o.max_ctx) return fail(EG_ERR_ARG, "pos %d outside [0, %d)", pos, rt->o.max_ctx);
+  if (id >= (uint32_t)rt->c.vocab_size) return fail(EG_ERR_ARG, "token id %u >= vocab", id);
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = set_state(rt, pos, 1, id, nullptr))) return s;
+  return run_step(rt, false);
+}
+
+EG_API eg_status eg_decode_greedy(eg_rt* rt, int start_pos, int K, uint32_t* out_ids, int* n_out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (n_out) *n_out = 0;
+  K = std::min(K, std::min(rt->o.decode_batch_capacity, rt->o.max_ctx - start_pos));
+  if (K <= 0) return EG_OK;
+  if (start_pos < 0) return fail(EG_ERR_ARG, "start_pos %d < 0", start_pos);
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "decodeBatch() is already in flight");
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = set_state(rt, start_pos, 1, 0, rt->amax))) return s;  // embed s.amax at start_pos
+  for (int k = 0; k < K; k++)
+    if ((s = run_step(rt, true))) return s;
+  CK(cudaMemcpyAsync(rt->h_small, rt->out_ids, (size_t)K * 4, cudaMemcpyDeviceToHost, rt->st));
+  if ((s = sync(rt))) return s;
+  if (out_ids) memcpy(out_ids, rt->h_small, (size_t)K * 4);
+  if (n_out) *n_out = K;
+  return EG_OK;
+}
+
+EG_API eg_status eg_decode_greedy_async(eg_rt* rt, int start_pos, int K, int* n_out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (n_out) *n_out = 0;
+  if (start_pos < 0) return fail(EG_ERR_ARG, "start_pos %d < 0", start_pos);
+  K = std::min(K, std::min(rt->o.decode_batch_capacity, rt->o.max_ctx - start_pos));
+  if (K <= 0) return EG_OK;
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = set_state(rt, start_pos, 1, 0, rt->amax))) return s;
+  for (int k = 0; k < K; k++)
+    if ((s = run_step(rt, true))) return s;
+  if (n_out) *n_out = K;
+  return EG_OK;
+}
+
+EG_API eg_status eg_read_ids(eg_rt* rt, uint32_t* out_ids, int n) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (n < 0 || n > std::max(rt->o.decode_batch_capacity, rt->o.max_ctx) || (n && !out_ids))
+    return fail(EG_ERR_ARG, "read_ids: bad count");
+  CK(cudaSetDevice(rt->o.device));
+  CK(cudaMemcpyAsync(rt->h_small, rt->out_ids, (size_t)n * 4, cudaMemcpyDeviceToHost, rt->st));
+  if ((s = sync(rt))) return s;
+  memcpy(out_ids, rt->h_small, (size_t)n * 4);
+  return EG_OK;
+}
+
+EG_API void* eg_stream(eg_rt* rt) { return rt ? (void*)rt->st : nullptr; }
+
+EG_API eg_status eg_sync(eg_rt* rt) {
+  if (!rt) return fail(EG_ERR_ARG, "null runtime");
+  CK(cudaSetDevice(rt->o.device));
+  return sync(rt);
+}
+
+EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (!ids || T <= 0) return fail(EG_ERR_ARG, "prefill: empty prompt");
+  if (T > rt->o.max_prefill_t) return fail(EG_ERR_ARG, "prompt %d > maxPrefillT %d", T, rt->o.max_prefill_t);
+  if (T > rt->o.max_ctx) return fail(EG_ERR_ARG, "prompt %d > maxCtx %d", T, rt->o.max_ctx);
+  for (int t = 0; t < T; t++)
+    if (ids[t] >= (uint32_t)rt->c.vocab_size) return fail(EG_ERR_ARG, "token id %u >= vocab", ids[t]);
+  CK(cudaSetDevice(rt->o.device));
+  CK(cudaMemcpyAsync(rt->ids, ids, (size_t)T * 4, cudaMemcpyHostToDevice, rt->st));
+  if ((s = set_state(rt, 0, 0, 0, nullptr))) return s;
+  for (int t = 0; t < T; t++)
+    if ((s = run_step(rt, false))) return s;
+  return EG_OK;
+}
+
+EG_API eg_status eg_argmax(eg_rt* rt, uint32_t* out_id) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "argmaxLogits() is already in flight; concurrent generation is not supported");
+  CK(cudaSetDevice(rt->o.device));
+  argmax(rt->logits, rt->c.vocab_size, rt->amax, rt->cand_v, rt->cand_i, rt->st);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(rt->h_small, rt->amax, 4, cudaMemcpyDeviceToHost, rt->st));
+  if ((s = sync(rt))) return s;
+  if (out_id) *out_id = rt->h_small[0];
+  return EG_OK;
+}
+
+EG_API eg_status eg_topk(eg_rt* rt, int k, uint32_t* ids, float* vals, int* k_out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "topKLogits() is already in flight; concurrent sampling is not supported");
+  k = std::min(std::max(1, k), std::min(rt->o.max_sampling_top_k, rt->c.vocab_size));
+  CK(cudaSetDevice(rt->o.device));
+  topk(rt->logits, rt->c.vocab_size, k, rt->sample_ids, rt->sample_vals, rt->cand_v, rt->cand_i, rt->st);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(rt->h_small, rt->sample_ids, (size_t)k * 4, cudaMemcpyDeviceToHost, rt->st));
+  CK(cudaMemcpyAsync(rt->h_small + 64, rt->sample_vals, (size_t)k * 4, cudaMemcpyDeviceToHost, rt->st));
+  if ((s = sync(rt))) return s;
+  if (ids) memcpy(ids, rt->h_small, (size_t)k * 4);
+  if (vals) memcpy(vals, rt->h_small + 64, (size_t)k * 4);
+  if (k_out) *k_out = k;
+  return EG_OK;
+}
+
+static eg_status sample_dev(eg_rt* rt, float temp, float r, uint32_t* also) {
+  const int k = std::min(std::min(rt->o.sampling_top_k, rt->o.max_sampling_top_k), rt->c.vocab_size);
+  topk(rt->logits, rt->c.vocab_size, k, rt->sample_ids, rt->sample_vals, rt->cand_v, rt->cand_i, rt->st);
+  r = std::max(0.f, std::min(1.f, r));
+  sample_topk(rt->sample_ids, rt->sample_vals, k, temp > 0 ? temp : 1.0f, r, rt->sampled, also, rt->st);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_sample(eg_rt* rt, float temp, float r, uint32_t* out_id) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "sampleToken: top-k selection already in flight");
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = sample_dev(rt, temp, r, nullptr))) return s;
+  CK(cudaMemcpyAsync(rt->h_small, rt->sampled, 4, cudaMemcpyDeviceToHost, rt->st));
+  if ((s = sync(rt))) return s;
+  if (out_id) *out_id = rt->h_small[0];
+  return EG_OK;
+}
+
+EG_API eg_status eg_read_logits(eg_rt* rt, float* out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (!out) return fail(EG_ERR_ARG, "null output");
+  CK(cudaSetDevice(rt->o.device));
+  CK(cudaMemcpyAsync(out, rt->logits, (size_t)rt->c.vocab_size * 4, cudaMemcpyDeviceToHost, rt->st));
+  return sync(rt);
+}
+
+EG_API eg_status eg_read_hidden(eg_rt* rt, float* out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (!out) return fail(EG_ERR_ARG, "null output");
+  CK(cudaSetDevice(rt->o.device));
+  CK(cudaMemcpyAsync(out, rt->hidden, (size_t)rt->c.hidden_size * 4, cudaMemcpyDeviceToHost, rt->st));
+  return sync(rt);
+}
+
+EG_API eg_status eg_generate(eg_rt* rt, const uint32_t* prompt, int n_prompt, int max_new,
+                             int sample, float temp, const float* r_seq, uint32_t* out_ids) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (max_new <= 0) return EG_OK;
+  if (!out_ids || (sample && !r_seq)) return fail(EG_ERR_ARG, "generate: null output / r_seq");
+  if (n_prompt + max_new - 1 > rt->o.max_ctx)
+    return fail(EG_ERR_ARG, "prompt %d + %d new tokens exceed maxCtx %d", n_prompt, max_new, rt->o.max_ctx);
+  if ((s = eg_prefill(rt, prompt, n_prompt))) return s;
+  if (!sample) {
+    uint32_t first;
+    if ((s = eg_argmax(rt, &first))) return s;
+    out_ids[0] = first;
+    int done = 1, pos = n_prompt;
+    while (done < max_new) {
+      int n = 0;
+      if ((s = eg_decode_greedy(rt, pos, max_new - done, out_ids + done, &n))) return s;
+      if (n <= 0) return fail(EG_ERR_STATE, "generate: context exhausted");
+      done += n;
+      pos += n;
+    }
+    return EG_OK;
+  }
+  CK(cudaSetDevice(rt->o.device));
+  // sampled: GPU-resident loop, the sampled id is written straight into
+  // s.amax (generate's writeBuffer, runtime.js:2494) and the id buffer.
+  const float t = temp > 0 ? temp : 1.0f;
+  int pos = n_prompt;
+  for (int g = 0; g < max_new; g++) {
+    if ((s = sample_dev(rt, t, r_seq[g], rt->amax))) return s;
+    copy_u32(rt->amax, rt->out_ids + g, rt->st);
+    if (g + 1 == max_new) break;
+    if ((s = set_state(rt, pos, 1, 0, rt->amax))) return s;
+    if ((s = run_step(rt, false))) return s;
+    pos++;
+  }
+  CK(cudaMemcpyAsync(rt->h_small, rt->out_ids, (size_t)max_new * 4, cudaMemcpyDeviceToHost, rt->st));
+  if ((s = sync(rt))) return s;
+  memcpy(out_ids, rt->h_small, (size_t)max_new * 4);
+  return EG_OK;
+}
+
+// ---------------------------------------------------------------- LoRA
+EG_API eg_status eg_lora_create(eg_rt* rt, int n, const eg_lora_module* mods, eg_lora** out) {
+  if (!rt || !out || (n > 0 && !mods)) return fail(EG_ERR_ARG, "eg_lora_create: null argument");
+  *out = nullptr;
+  CK(cudaSetDevice(rt->o.device));
+  const eg_config& c = rt->c;
+  eg_lora* lo = new eg_lora();
+  lo->table.assign((size_t)c.num_layers * 7, LoraMod{nullptr, nullptr, 0, 0.f});
+  lo->shapes.assign((size_t)c.num_layers * 7 * 3, 0);
+  auto bail = [&](eg_status st) {
+    for (void* p : lo->allocs) cudaFree(p);
+    delete lo;
+    return st;
+  };
+  int matched = 0;
+  for (int m = 0; m < n; m++) {
+    const eg_lora_module& md = mods[m];
+    int layer, p;
+    if (!parse_key(md.key, c.num_layers, &layer, &p)) continue;
+    if (!md.A || !md.B) continue;
+    int64_t N, K;
+    proj_shape(c, p, &N, &K);
+    const int64_t r = std::min(std::min(md.a_rows, md.a_cols), std::min(md.b_rows, md.b_cols));
+    if (r <= 0 || r > kMaxRank)
+      return bail(fail(EG_ERR_ARG, "%s: rank %lld outside [1, %d]", md.key, (long long)r, kMaxRank));
+    // A -> [r][in], B -> [r][out] (lora_gpu.js:100-107)
+    const bool a_t = md.a_rows != r, b_t = md.b_rows != r;
+    const int64_t a_in = a_t ? md.a_rows : md.a_cols, b_out = b_t ? md.b_rows : md.b_cols;
+    if (a_in != K || b_out != N)
+      return bail(fail(EG_ERR_ARG, "%s: A/B shapes do not match the %lldx%lld projection", md.key,
+                       (long long)N, (long long)K));
+    std::vector<float> A((size_t)r * K), B((size_t)r * N);
+    for (int64_t i = 0; i < r; i++)
+      for (int64_t k = 0; k < K; k++) A[i * K + k] = a_t ? md.A[k * r + i] : md.A[i * K + k];
+    for (int64_t i = 0; i < r; i++)
+      for (int64_t j = 0; j < N; j++) B[i * N + j] = b_t ? md.B[j * r + i] : md.B[i * N + j];
+    float *dA = nullptr, *dB = nullptr;
+    if (cudaMalloc(&dA, A.size() * 4) != cudaSuccess || cudaMalloc(&dB, B.size() * 4) != cudaSuccess) {
+      if (dA) cudaFree(dA);
+      return bail(fail(EG_ERR_OOM, "LoRA allocation failed"));
+    }
+    lo->allocs.push_back(dA);
+    lo->allocs.push_back(dB);
+    if (cudaMemcpy(dA, A.data(), A.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dB, B.data(), B.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return bail(fail(EG_ERR_CUDA, "LoRA upload failed"));
+    const size_t slot = (size_t)layer * 7 + p;
+    lo->table[slot] = LoraMod{dA, dB, (int)r, md.scale};
+    lo->shapes[slot * 3 + 0] = r;
+    lo->shapes[slot * 3 + 1] = K;
+    lo->shapes[slot * 3 + 2] = N;
+    lo->max_rank = std::max(lo->max_rank, (int)r);
+    matched++;
+  }
+  if (!matched) return bail(fail(EG_ERR_ARG, "no LoRA modules matched layers.*.{self_attn,mlp}.*_proj"));
+  *out = lo;
+  return EG_OK;
+}
+
+EG_API eg_status eg_lora_destroy(eg_rt* rt, eg_lora* lora) {
+  if (!lora) return EG_OK;
+  if (rt && rt->active == lora) eg_clear_lora(rt);
+  if (rt) cudaStreamSynchronize(rt->st);
+  for (void* p : lora->allocs) cudaFree(p);
+  delete lora;
+  return EG_OK;
+}
+
+EG_API eg_status eg_lora_update(eg_rt* rt, eg_lora* lora, const char* key, const float* A, const float* B) {
+  if (!rt || !lora) return fail(EG_ERR_ARG, "null argument");
+  int layer, p;
+  if (!parse_key(key, rt->c.num_layers, &layer, &p)) return fail(EG_ERR_ARG, "bad module key %s", key ? key : "");
+  const size_t slot = (size_t)layer * 7 + p;
+  const LoraMod& m = lora->table[slot];
+  if (m.rank <= 0) return fail(EG_ERR_ARG, "module %s not in adapter", key);
+  CK(cudaSetDevice(rt->o.device));
+  const int64_t r = lora->shapes[slot * 3], K = lora->shapes[slot * 3 + 1], N = lora->shapes[slot * 3 + 2];
+  if (A) CK(cudaMemcpyAsync((void*)m.A, A, (size_t)r * K * 4, cudaMemcpyHostToDevice, rt->st));
+  if (B) CK(cudaMemcpyAsync((void*)m.B, B, (size_t)r * N * 4, cudaMemcpyHostToDevice, rt->st));
+  return sync(rt);
+}
+
+static eg_status push_table(eg_rt* rt) {
+  const size_t n = (size_t)rt->c.num_layers * 7;
+  if (!rt->active) return EG_OK;
+  CK(cudaMemcpyAsync(rt->lora_table, rt->active->table.data(), n * sizeof(LoraMod),
+                     cudaMemcpyHostToDevice, rt->st));
+  return sync(rt);
+}
+
+EG_API eg_status eg_set_lora(eg_rt* rt, eg_lora* lora) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  CK(cudaSetDevice(rt->o.device));
+  rt->active = lora;
+  return push_table(rt);
+}
+EG_API eg_status eg_clear_lora(eg_rt* rt) {
+  if (!rt) return fail(EG_ERR_ARG, "null runtime");
+  rt->active = nullptr;
+  return EG_OK;
+}
+EG_API eg_status eg_invalidate_lora(eg_rt* rt) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  CK(cudaSetDevice(rt->o.device));
+  return push_table(rt);
+}
+
+// ---------------------------------------------------------------- observability
+EG_API eg_status eg_profile_token(eg_rt* rt, uint32_t id, int pos, double* us, int* n_cat) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (pos < 0 || pos >= rt->o.max_ctx || id >= (uint32_t)rt->c.vocab_size)
+    return fail(EG_ERR_ARG, "profile_token: bad id/pos");
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = set_state(rt, pos, 1, id, nullptr))) return s;
+  std::vector<cudaEvent_t> marks;
+  std::vector<int> cats;
+  cudaEvent_t start;
+  CK(cudaEventCreate(&start));
+  CK(cudaEventRecord(start, rt->st));
+  StepOpts so{false, rt->active != nullptr, false, rt->active ? rt->active->max_rank : 0, &marks};
+  enqueue_step(rt, so, &cats);
+  CK(cudaGetLastError());
+  if ((s = sync(rt))) return s;
+  double acc[6] = {0, 0, 0, 0, 0, 0};
+  cudaEvent_t prev = start;
+  for (size_t i = 0; i < marks.size(); i++) {
+    float ms = 0;
+    cudaEventElapsedTime(&ms, prev, marks[i]);
+    acc[cats[i]] += ms * 1000.0;
+    prev = marks[i];
+  }
+  for (auto e : marks) cudaEventDestroy(e);
+  cudaEventDestroy(start);
+  if (us)
+    for (int i = 0; i < 6; i++) us[i] = acc[i];
+  if (n_cat) *n_cat = 6;
+  return EG_OK;
+}
+
+EG_API eg_status eg_memory_footprint(eg_rt* rt, int64_t* kv, int64_t* w, int64_t* scratch) {
+  if (!rt) return fail(EG_ERR_ARG, "null runtime");
+  if (kv) *kv = rt->kv_bytes;
+  if (w) *w = rt->weight_bytes;
+  if (scratch) *scratch = rt->scratch_bytes;
+  return EG_OK;
+}
+
+EG_API int eg_launches_per_step(eg_rt* rt) { return rt ? rt->launches_per_step : 0; }
+
+// ---------------------------------------------------------------- single ops
+#define OPSTREAM reinterpret_cast<cudaStream_t>(stream)
+
+EG_API eg_status eg_op_gemv_q4(const float* x, const uint32_t* w, const float* scale, const float* bias,
+                               int N, int K, int group, float* y, int accumulate, void* stream) {
+  if (!x || !w || !scale || !y || N <= 0 || K <= 0) return fail(EG_ERR_ARG, "gemv_q4: bad argument");
+  if (group != 128 || K % 128 || K > 12288)
+    return fail(EG_ERR_ARG, "gemv_q4: group must be 128, K %% 128 == 0, K <= 12288");
+  XSrc xs = {};
+  xs.mode = X_PLAIN;
+  xs.x = x;
+  Epi e = {};
+  e.mode = accumulate ? EPI_ADD : EPI_STORE;
+  e.y = y;
+  e.bias = accumulate ? nullptr : bias;
+  e.N = N;
+  e.split1 = e.split2 = N;
+  if (accumulate && bias) return fail(EG_ERR_ARG, "gemv_q4: bias with accumulate is not supported");
+  gemv_q4(w, scale, N, K, xs, e, OPSTREAM, false);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_gate_up_silu(const float* x, const uint32_t* w, const float* scale, int N, int K,
+                                    float* y, void* stream) {
+  if (!x || !w || !scale || !y || N <= 0 || K <= 0 || K % 128 || K > 12288)
+    return fail(EG_ERR_ARG, "gate_up_silu: need K %% 128 == 0, K <= 12288");
+  XSrc xs = {};
+  xs.mode = X_PLAIN;
+  xs.x = x;
+  Epi e = {};
+  e.mode = EPI_SILU;
+  e.y = y;
+  e.N = N;
+  gemv_q4(w, scale, N, K, xs, e, OPSTREAM, false);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_gemv_q8(const float* x, const uint32_t* w, const float* scale, int N, int K, float* y,
+                               void* stream) {
+  if (!x || !w || !scale || !y || N <= 0 || K <= 0 || K % 64 || K > 12288)
+    return fail(EG_ERR_ARG, "gemv_q8: K must be a multiple of 64, <= 12288");
+  XSrc xs = {};
+  xs.mode = X_PLAIN;
+  xs.x = x;
+  gemv_q8(w, scale, N, K, xs, y, nullptr, OPSTREAM, false);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_rmsnorm(const float* x, const float* g, int K, float eps, int f16, float* y, void* stream) {
+  if (!x || !g || !y || K <= 0) return fail(EG_ERR_ARG, "rmsnorm: bad argument");
+  rmsnorm(x, g, K, eps, f16, y, OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_rope_qk(float* q, float* k, int nq, int nkv, int pos, const float* cos_t,
+                               const float* sin_t, int f16, void* stream) {
+  if (!q || !k || !cos_t || !sin_t || nq < 0 || nkv < 0 || pos < 0) return fail(EG_ERR_ARG, "rope_qk: bad argument");
+  rope_qk(q, k, nq, nkv, pos, cos_t, sin_t, f16, OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cache, const float* cos_t,
+                                   const float* sin_t, int nh, int nkv, int pos, int max_ctx, int kv_f16,
+                                   int chunk, float* out, void* stream) {
+  if (!qkv || !k_cache || !v_cache || !cos_t || !sin_t || !out) return fail(EG_ERR_ARG, "attn_decode: null argument");
+  if (nh <= 0 || nkv <= 0 || nh % nkv || nh / nkv > 8 || pos < 0 || pos >= max_ctx)
+    return fail(EG_ERR_ARG, "attn_decode: bad heads/pos");
+  if (chunk < 0 || chunk > 64 || chunk % 16) return fail(EG_ERR_ARG, "attn_decode: chunk must be 0 or 16/32/48/64");
+  const int ms = attn_max_splits(max_ctx);
+  void* scr = nullptr;
+  const size_t part = (size_t)nh * ms * (128 + 2) * 4;
+  eg_status s = op_scratch(part + 64 * 4, &scr);
+  if (s) return s;
+  unsigned* counters = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(scr) + part);
+  CK(cudaMemsetAsync(counters, 0, nkv * 4, OPSTREAM));
+  AttnArgs a = {};
+  a.qkv = qkv;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.cosT = cos_t;
+  a.sinT = sin_t;
+  a.pos = nullptr;
+  a.fixed_pos = pos;
+  a.nh = nh;
+  a.nkv = nkv;
+  a.max_splits = ms;
+  a.kv_f16 = kv_f16;
+  a.chunk = chunk;
+  a.pm = reinterpret_cast<float*>(scr);
+  a.pz = a.pm + (size_t)nh * ms;
+  a.po = a.pz + (size_t)nh * ms;
+  a.out = out;
+  a.counters = counters;
+  attn_decode(a, OPSTREAM, false);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_embed(const uint32_t* w, const float* scale, const uint32_t* id, int H, float* out,
+                             void* stream) {
+  if (!w || !scale || !id || !out || H <= 0 || H % 4) return fail(EG_ERR_ARG, "embed: bad argument");
+  embed_rows(w, scale, id, H, out, OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_lora_a(const float* x, const float* A, int K, int rank, float* d, void* stream) {
+  if (!x || !A || !d || K <= 0 || rank <= 0 || rank > kMaxRank) return fail(EG_ERR_ARG, "lora_a: bad argument");
+  void* scr = nullptr;
+  eg_status s = op_scratch(sizeof(LoraMod) + kMaxRank * 4, &scr);
+  if (s) return s;
+  LoraMod m{A, nullptr, rank, 1.f};
+  CK(cudaMemcpyAsync(scr, &m, sizeof m, cudaMemcpyHostToDevice, OPSTREAM));
+  float* dd = reinterpret_cast<float*>(reinterpret_cast<char*>(scr) + 256);
+  XSrc xs = {};
+  xs.mode = X_PLAIN;
+  xs.x = x;
+  lora_a(xs, K, reinterpret_cast<const LoraMod*>(scr), 1, rank, dd, OPSTREAM, false);
+  CK(cudaMemcpyAsync(d, dd, (size_t)rank * 4, cudaMemcpyDeviceToDevice, OPSTREAM));
+  CK(cudaStreamSynchronize(OPSTREAM));
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_argmax(const float* logits, int n, uint32_t* out, void* stream) {
+  if (!logits || !out || n <= 0) return fail(EG_ERR_ARG, "argmax: bad argument");
+  void* scr = nullptr;
+  eg_status s = op_scratch((size_t)kCandMax * 8, &scr);
+  if (s) return s;
+  argmax(logits, n, out, reinterpret_cast<float*>(scr),
+         reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(scr) + kCandMax * 4), OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_topk(const float* logits, int n, int k, uint32_t* ids, float* vals, void* stream) {
+  if (!logits || !ids || !vals || n <= 0 || k < 1 || k > 64) return fail(EG_ERR_ARG, "topk: need 1 <= k <= 64");
+  if (n > 148 * 2048) return fail(EG_ERR_ARG, "topk: n too large");
+  void* scr = nullptr;
+  const size_t nc = (size_t)kCandMax * 64;
+  eg_status s = op_scratch(nc * 8, &scr);
+  if (s) return s;
+  topk(logits, n, k, ids, vals, reinterpret_cast<float*>(scr),
+       reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(scr) + nc * 4), OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_sample_topk(const uint32_t* ids, const float* vals, int k, float temp, float r,
+                                   uint32_t* out, void* stream) {
+  if (!ids || !vals || !out || k < 0 || k > 64) return fail(EG_ERR_ARG, "sample_topk: need 0 <= k <= 64");
+  sample_topk(ids, vals, k, temp, r, out, nullptr, OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,227 @@
+"""QwenB200: the host-side runtime with the reference's `QwenWGPU` surface
+(src/qwgpu/runtime.js:84-2571), driving libemberglass_cuda through its C ABI.
+
+Method names, argument meaning and error behaviour follow the reference
+(camelCase kept so reference-style harnesses read the same); all device work
+happens in the CUDA library.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib as L
+from .config import QWEN25_3B
+
+PROFILE_CATEGORIES = ("embed+qkv", "attn", "o", "gate_up", "down", "lm_head")
+
+
+def _cfg_struct(cfg: dict) -> L.EgConfig:
+    return L.EgConfig(cfg["hiddenSize"], cfg["numLayers"], cfg["numHeads"], cfg["numKVHeads"],
+                      cfg["headDim"], cfg["intermediateSize"], cfg["vocabSize"], cfg["rmsNormEps"],
+                      cfg["ropeTheta"], int(cfg.get("tieWordEmbeddings", True)),
+                      int(cfg.get("attentionBias", True)))
+
+
+class QwenB200:
+    """new QwenWGPU(device, cfg, opts) (runtime.js:87).
+
+    opts: maxCtx, maxPrefillT, decodeBatchSize (capacity of one decodeBatch
+    call), samplingTopK, maxSamplingTopK, useF16 (f16 KV cache + the
+    reference's f16 staging numerics, default True), attnChunk, useGraphs,
+    usePdl, device.
+    """
+
+    def __init__(self, cfg: dict | None = None, opts: dict | None = None):
+        self.cfg = dict(cfg or QWEN25_3B)
+        opts = dict(opts or {})
+        o = L.EgOptions()
+        L.lib().eg_default_options(C.byref(o))
+        o.device = int(opts.get("device", 0))
+        o.max_ctx = int(opts.get("maxCtx", 8192))
+        o.max_prefill_t = int(opts.get("maxPrefillT", 0))
+        o.kv_f16 = int(bool(opts.get("useF16", True)))
+        o.decode_batch_capacity = int(opts.get("decodeBatchSize", 32))
+        o.sampling_top_k = int(opts.get("samplingTopK", 40))
+        o.max_sampling_top_k = int(opts.get("maxSamplingTopK", 64))
+        o.attn_chunk = int(opts.get("attnChunk", 0))
+        o.use_graphs = int(bool(opts.get("useGraphs", True)))
+        o.use_pdl = int(bool(opts.get("usePdl", True)))
+        self.opts = o
+        h = C.c_void_p()
+        L.check(L.lib().eg_create(C.byref(_cfg_struct(self.cfg)), C.byref(o), C.byref(h)))
+        self._h = h
+        self.lora = None
+        self.maxCtx = o.max_ctx
+
+    # ------------------------------------------------------------ lifecycle
+    def close(self):
+        if getattr(self, "_h", None):
+            L.lib().eg_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def usingF16(self) -> bool:
+        return bool(self.opts.kv_f16)
+
+    # ------------------------------------------------------------ weights
+    def build(self, source="synthetic", seed: int = 0xE6B00000, std: float = 0.02):
+        """build(source) (runtime.js:326): 'synthetic' = seeded N(0, std)
+        weights, or a mapping / iterable of (HF name, f32 array)."""
+        lib = L.lib()
+        if source == "synthetic":
+            L.check(lib.eg_build_synthetic(self._h, seed, std))
+        else:
+            items = source.items() if hasattr(source, "items") else source
+            for name, arr in items:
+                self.uploadTensor(name, arr)
+        L.check(lib.eg_finalize(self._h))
+        return self
+
+    def uploadTensor(self, name: str, arr: np.ndarray):
+        a = np.ascontiguousarray(arr, np.float32)
+        shape = (C.c_int64 * a.ndim)(*a.shape)
+        L.check(L.lib().eg_upload_tensor(self._h, name.encode(), a.ctypes.data, shape, a.ndim))
+
+    def uploadQuantized(self, name: str, kind: int, packed: np.ndarray, scale: np.ndarray, shape):
+        p = np.ascontiguousarray(packed, np.uint32)
+        s = np.ascontiguousarray(scale, np.float32)
+        sh = (C.c_int64 * len(shape))(*shape)
+        L.check(L.lib().eg_upload_quantized(self._h, name.encode(), kind, p.ctypes.data,
+                                            s.ctypes.data, sh, len(shape)))
+
+    def finalize(self):
+        L.check(L.lib().eg_finalize(self._h))
+
+    # ------------------------------------------------------------ decode
+    def token(self, id: int, pos: int):
+        """token(id, pos) (runtime.js:1735-1741)."""
+        L.check(L.lib().eg_token(self._h, int(id), int(pos)))
+
+    step = token
+
+    def decodeBatch(self, startPos: int, K: int) -> list[int]:
+        """decodeBatch(startPos, K) (runtime.js:1776-1793)."""
+        out = np.zeros(max(int(K), 1), np.uint32)
+        n = C.c_int(0)
+        L.check(L.lib().eg_decode_greedy(self._h, int(startPos), int(K), out.ctypes.data, C.byref(n)))
+        return out[: n.value].tolist()
+
+    decodeGreedyBatch = decodeBatch
+
+    def decodeBatchAsync(self, startPos: int, K: int) -> int:
+        """Enqueue K chained greedy tokens without reading them back."""
+        n = C.c_int(0)
+        L.check(L.lib().eg_decode_greedy_async(self._h, int(startPos), int(K), C.byref(n)))
+        return n.value
+
+    def readIds(self, n: int) -> list[int]:
+        out = np.zeros(max(int(n), 1), np.uint32)
+        L.check(L.lib().eg_read_ids(self._h, out.ctypes.data, int(n)))
+        return out[: int(n)].tolist()
+
+    def sync(self):
+        L.check(L.lib().eg_sync(self._h))
+
+    @property
+    def stream(self) -> int:
+        return L.lib().eg_stream(self._h)
+
+    def prefillBatch(self, ids):
+        """prefillBatch(ids) (runtime.js:1936-1945)."""
+        a = np.ascontiguousarray(ids, np.uint32)
+        L.check(L.lib().eg_prefill(self._h, a.ctypes.data, int(a.size)))
+
+    def argmaxLogits(self) -> int:
+        v = C.c_uint32(0)
+        L.check(L.lib().eg_argmax(self._h, C.byref(v)))
+        return int(v.value)
+
+    def topKLogits(self, k: int | None = None):
+        k = self.opts.sampling_top_k if k is None else int(k)
+        ids = np.zeros(64, np.uint32)
+        vals = np.zeros(64, np.float32)
+        kk = C.c_int(0)
+        L.check(L.lib().eg_topk(self._h, k, ids.ctypes.data, vals.ctypes.data, C.byref(kk)))
+        return [{"id": int(ids[i]), "logit": float(vals[i])} for i in range(kk.value)]
+
+    def sampleToken(self, temp: float = 1.0, r: float | None = None) -> int:
+        if r is None:
+            r = float(np.random.random())
+        v = C.c_uint32(0)
+        L.check(L.lib().eg_sample(self._h, float(temp), float(r), C.byref(v)))
+        return int(v.value)
+
+    def readLogits(self) -> np.ndarray:
+        out = np.empty(self.cfg["vocabSize"], np.float32)
+        L.check(L.lib().eg_read_logits(self._h, out.ctypes.data))
+        return out
+
+    def readHidden(self) -> np.ndarray:
+        out = np.empty(self.cfg["hiddenSize"], np.float32)
+        L.check(L.lib().eg_read_hidden(self._h, out.ctypes.data))
+        return out
+
+    def generate(self, promptIds, maxNewTokens: int = 32, opts: dict | None = None) -> list[int]:
+        """generate(ids, n, {sample, temp, rSeq}) (runtime.js:2481-2516)."""
+        opts = opts or {}
+        p = np.ascontiguousarray(promptIds, np.uint32)
+        n = int(maxNewTokens)
+        out = np.zeros(max(n, 1), np.uint32)
+        sample = bool(opts.get("sample", False))
+        r = None
+        if sample:
+            r = np.ascontiguousarray(opts.get("rSeq", np.random.random(n)), np.float32)
+        L.check(L.lib().eg_generate(self._h, p.ctypes.data, int(p.size), n, int(sample),
+                                    float(opts.get("temp", 1.0)),
+                                    None if r is None else r.ctypes.data, out.ctypes.data))
+        ids = out[:n].tolist()
+        cb = opts.get("onToken")
+        if cb:
+            for t in ids:
+                cb(t)
+        return ids
+
+    # ------------------------------------------------------------ LoRA
+    def setLora(self, adapter):
+        """setLora(adapter) (runtime.js:717-721)."""
+        L.check(L.lib().eg_set_lora(self._h, adapter.handle))
+        self.lora = adapter
+
+    def clearLora(self):
+        L.check(L.lib().eg_clear_lora(self._h))
+        self.lora = None
+
+    def invalidateLora(self):
+        L.check(L.lib().eg_invalidate_lora(self._h))
+
+    # ------------------------------------------------------------ observability
+    def profToken(self, id: int, pos: int) -> dict:
+        us = (C.c_double * 6)()
+        n = C.c_int(0)
+        L.check(L.lib().eg_profile_token(self._h, int(id), int(pos), us, C.byref(n)))
+        return {PROFILE_CATEGORIES[i]: us[i] for i in range(n.value)}
+
+    def memoryFootprintBytes(self) -> dict:
+        kv, w, s = C.c_int64(), C.c_int64(), C.c_int64()
+        L.check(L.lib().eg_memory_footprint(self._h, C.byref(kv), C.byref(w), C.byref(s)))
+        return {"kvBytes": kv.value, "packedBytes": w.value, "decodeScratchBytes": s.value}
+
+    def estimateKvCacheBytes(self) -> int:
+        c = self.cfg
+        return c["numLayers"] * 2 * c["numKVHeads"] * self.maxCtx * c["headDim"] * (
+            2 if self.usingF16() else 4)
+
+    @property
+    def lastDispatchCount(self) -> int:
+        return L.lib().eg_launches_per_step(self._h)
