@@ -312,6 +312,19 @@ def run_reference(args, ws, rank):
             "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def ncu_probe(ctx):
+    """Smallest run that contains full decode steps, for ncu launch lists and
+    single-kernel captures (the weights are 1.8 GB; nothing else is held)."""
+    import vibethinker_webgpu_lora_b200 as E
+    from oracle import oracle as O
+    rt = E.QwenB200(E.QWEN25_3B, {"maxCtx": ctx + 40}).build("synthetic", seed=SEED)
+    rt.prefillBatch(O.token_ids(ctx, PROMPT_SEED, E.QWEN25_3B["vocabSize"]))
+    rt.argmaxLogits()
+    rt.decodeBatchAsync(ctx, 2)
+    rt.sync()
+    print(json.dumps({"ncu_probe": ctx, "launches_per_step": rt.lastDispatchCount}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -321,7 +334,13 @@ def main():
     ap.add_argument("--ctx", type=int, default=128, choices=[128, 4096, 7800])
     ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-probe", type=int, default=0, metavar="CTX",
+                    help="profiling target: build, prefill CTX tokens, decode 2 tokens, exit "
+                         "(CTX * launches/step launches precede the 2 profiled steps)")
     args = ap.parse_args()
+    if args.ncu_probe:
+        ncu_probe(args.ncu_probe)
+        return
     assert args.warmup >= 3, "at least 3 warm-up steps"
     ws, rank, local = dist_setup() if args.impl == "ours" else (
         int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
