@@ -215,6 +215,20 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
                                    const float* cos_t, const float* sin_t, int nh, int nkv,
                                    int pos, int max_ctx, int kv_f16, int chunk, float* out,
                                    void* stream);
+/* No counterpart in the reference.  eg_op_attn_decode for callers that must
+ * not allocate device memory at call time (a framework whose caching
+ * allocator already holds the device memory, or a latency-critical loop that
+ * cannot take cudaMalloc's implicit synchronisation): same arguments and
+ * results, with the split partials in a 2 MB static device array loaded with
+ * the library instead of library-allocated scratch.  Rejects calls needing
+ * nh * ceil((pos+1) / max(chunk, 16)) > 4096 slots (EG_ERR_ARG).  All calls
+ * share the array: calls that overlap on the GPU race.  The first call on a
+ * device looks up the array's device address; make it before any stream
+ * capture. */
+EG_API eg_status eg_op_attn_decode_noalloc(const float* qkv, void* k_cache, void* v_cache,
+                                           const float* cos_t, const float* sin_t, int nh,
+                                           int nkv, int pos, int max_ctx, int kv_f16, int chunk,
+                                           float* out, void* stream);
 /* EMBED_BUF, kernels.js:537-550: id read from device memory. */
 EG_API eg_status eg_op_embed(const uint32_t* w, const float* scale, const uint32_t* id, int H,
                              float* out, void* stream);

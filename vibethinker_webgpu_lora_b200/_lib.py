@@ -89,6 +89,7 @@ _SIGS = {
     "eg_op_rmsnorm": (i32, [vp, vp, i32, f32, i32, vp, vp]),
     "eg_op_rope_qk": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),
     "eg_op_attn_decode": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
+    "eg_op_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
     "eg_op_embed": (i32, [vp, vp, vp, i32, vp, vp]),
     "eg_op_lora_a": (i32, [vp, vp, i32, i32, vp, vp]),
     "eg_op_argmax": (i32, [vp, i32, vp, vp]),
