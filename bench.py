@@ -158,8 +158,10 @@ def run_ours(args, ws, rank, local):
     period = 64 if long else 128
     max_ctx = n_prompt + period + 8
     cap = 32
-    rt = E.QwenB200(cfg, {"maxCtx": max_ctx, "useF16": True, "device": local,
-                          "decodeBatchSize": cap}).build("synthetic", seed=SEED)
+    opts = {"maxCtx": max_ctx, "useF16": True, "device": local, "decodeBatchSize": cap}
+    if args.path != "auto":
+        opts["useFused"] = args.path == "fused"
+    rt = E.QwenB200(cfg, opts).build("synthetic", seed=SEED)
     prompt = O.token_ids(n_prompt, PROMPT_SEED ^ rank, cfg["vocabSize"])
     rt.prefillBatch(prompt)
     rt.argmaxLogits()
@@ -334,6 +336,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=128, choices=[128, 4096, 7800])
     ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", default="auto", choices=["auto", "fused", "graph"],
+                    help="decode path: persistent fused kernel or per-op CUDA graph")
     ap.add_argument("--ncu-probe", type=int, default=0, metavar="CTX",
                     help="profiling target: build, prefill CTX tokens, decode 2 tokens, exit "
                          "(CTX * launches/step launches precede the 2 profiled steps)")

@@ -74,6 +74,9 @@ typedef struct {
   int attn_chunk;          /* keys per attention split; 0 = adaptive */
   int use_graphs;          /* capture the decode step in a CUDA graph (default 1) */
   int use_pdl;             /* programmatic dependent launch (default 1) */
+  int use_fused;           /* 1: persistent fused decode kernel (one cooperative
+                              launch per token batch) when no LoRA is active;
+                              0 (default): per-op kernels in a CUDA graph */
 } eg_options;
 
 EG_API const char* eg_last_error(void);
@@ -182,6 +185,13 @@ EG_API eg_status eg_invalidate_lora(eg_rt* rt);               /* invalidateLora 
  * CUDA event around each kernel; us[] per category in this order:
  * embed+qkv, attn, o, gate_up, down, lm_head.  n_cat receives 6. */
 EG_API eg_status eg_profile_token(eg_rt* rt, uint32_t id, int pos, double* us, int* n_cat);
+/* The fused path's counterpart of profToken: one greedy step at start_pos
+ * (input token = s.amax) with globaltimer stamps; out_ns[2p] = start of phase
+ * p on the first CTA, out_ns[2p+1] = latest end of phase p's work over all
+ * CTAs.  Phases: 5 per layer (qkv, attn, o, gate_up, down) then the LM head;
+ * *n_out = 2 * (5 * num_layers + 1). */
+EG_API eg_status eg_profile_fused(eg_rt* rt, int start_pos, uint64_t* out_ns, int n_max,
+                                  int* n_out);
 /* memoryFootprintBytes (runtime.js:661-681). */
 EG_API eg_status eg_memory_footprint(eg_rt* rt, int64_t* kv_bytes, int64_t* weight_bytes,
                                      int64_t* scratch_bytes);

@@ -44,10 +44,10 @@ def make(cfg, f16, max_ctx=256, **opts):
 
 
 @pytest.mark.parametrize("f16", [True, False])
-@pytest.mark.parametrize("graphs", [True, False])
-def test_small_model_logits_and_greedy(cuda, f16, graphs):
+@pytest.mark.parametrize("path", ["fused", "graph", "eager"])
+def test_small_model_logits_and_greedy(cuda, f16, path):
     cfg = small_config(layers=3, vocab=5000, inter=1024)
-    rt, orc = make(cfg, f16, useGraphs=graphs)
+    rt, orc = make(cfg, f16, useFused=path == "fused", useGraphs=path == "graph")
     prompt = O.token_ids(12, 0xE6B00010, cfg["vocabSize"])
     for t, tok in enumerate(prompt):
         rt.token(int(tok), t)
@@ -61,15 +61,33 @@ def test_small_model_logits_and_greedy(cuda, f16, graphs):
     assert_stream([first] + ids, ref_ids, margins)
 
 
-def test_prefill_matches_token_loop(cuda):
+@pytest.mark.parametrize("fused", [True, False])
+def test_prefill_matches_token_loop(cuda, fused):
     cfg = small_config(layers=2, vocab=3000)
-    rt = E.QwenB200(cfg, dict(maxCtx=128)).build("synthetic", seed=SEED)
+    rt = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused)).build("synthetic", seed=SEED)
     prompt = O.token_ids(20, 5, cfg["vocabSize"])
     rt.prefillBatch(prompt)
     a = rt.readLogits()
     for t, tok in enumerate(prompt):
         rt.token(int(tok), t)
     assert np.array_equal(a, rt.readLogits())  # deterministic, bitwise
+
+
+def test_fused_equals_graph_path(cuda):
+    """The persistent fused kernel and the per-op graph run the same math
+    (summation orders differ: both are held to the oracle bars)."""
+    cfg = small_config(layers=3, vocab=4000)
+    prompt = O.token_ids(16, 9, cfg["vocabSize"])
+    orc = O.OracleModel(cfg, 128, True, SEED)
+    ref, margins = orc.generate(prompt, 33)
+    for fused in (True, False):
+        rt = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused)).build("synthetic", seed=SEED)
+        rt.prefillBatch(prompt)
+        first = rt.argmaxLogits()
+        ids = rt.decodeBatch(len(prompt), 32)
+        n = assert_stream([first] + ids, ref, margins)
+        if n == 33:
+            close(rt.readLogits(), orc.logits())
 
 
 def test_generate_greedy_and_sampled(cuda):

@@ -35,7 +35,7 @@ class EgOptions(C.Structure):
         ("device", C.c_int), ("max_ctx", C.c_int), ("max_prefill_t", C.c_int), ("kv_f16", C.c_int),
         ("decode_batch_capacity", C.c_int), ("sampling_top_k", C.c_int),
         ("max_sampling_top_k", C.c_int), ("attn_chunk", C.c_int), ("use_graphs", C.c_int),
-        ("use_pdl", C.c_int),
+        ("use_pdl", C.c_int), ("use_fused", C.c_int),
     ]
 
 
@@ -81,6 +81,7 @@ _SIGS = {
     "eg_clear_lora": (i32, [vp]),
     "eg_invalidate_lora": (i32, [vp]),
     "eg_profile_token": (i32, [vp, u32, i32, vp, C.POINTER(i32)]),
+    "eg_profile_fused": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
     "eg_memory_footprint": (i32, [vp, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
     "eg_launches_per_step": (i32, [vp]),
     "eg_op_gemv_q4": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, i32, vp]),

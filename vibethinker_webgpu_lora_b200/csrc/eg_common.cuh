@@ -68,12 +68,20 @@ EG_DEV uint32_t pack_h2(float lo, float hi) {
 // Split f32 values into (hi, lo) f16 pairs with v ~= hi + lo (22 significant
 // bits), so a tensor-core dot of exact integer weights with hi and lo columns
 // reproduces an f32 dot to within f32 rounding.
+// (Paired f32->f16 conversions: the single-value conversion runs on the
+// narrow XU pipe, the paired one at ~4x its rate.)
 EG_DEV void split_h2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  __half ha = __float2half_rn(a), hb = __float2half_rn(b);
-  __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
-  __half2 h = __halves2half2(ha, hb), l = __halves2half2(la, lb);
-  hi = *reinterpret_cast<uint32_t*>(&h);
-  lo = *reinterpret_cast<uint32_t*>(&l);
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+// Round two f32 values to f16 and back (each rounded once, RNE).
+EG_DEV void round_h2(float& a, float& b) {
+  const float2 r = __half22float2(__floats2half2_rn(a, b));
+  a = r.x;
+  b = r.y;
 }
 
 EG_DEV float round_h(float v) { return __half2float(__float2half_rn(v)); }
@@ -97,6 +105,12 @@ EG_DEV float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+
+// The building blocks in eg_device.cuh run on a 256-thread group: the whole
+// CTA of a per-op kernel, or the 8 consumer warps of the fused kernel (whose
+// producer warp never joins).  Named barrier 1 over those 256 threads.
+constexpr int kCtaThreads = 256;
+EG_DEV void cta_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // Programmatic dependent launch: wait for the producing kernel's writes /
 // allow the next kernel in the stream to start its independent prologue.

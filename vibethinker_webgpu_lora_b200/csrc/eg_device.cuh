@@ -1,0 +1,591 @@
+// eg_device.cuh -- device building blocks shared by the per-op kernels
+// (eg_kernels.cu) and the persistent fused decode kernel (eg_fused.cu):
+// block reductions, the activation prologue that builds MMA B fragments,
+// GEMV epilogues, weight batch loaders, and one attention work item.
+#pragma once
+#include <float.h>
+#include <math.h>
+
+#include "eg_common.cuh"
+#include "eg_kernels.h"
+
+namespace eg {
+
+// Intra-phase timeline (profiling only): the fused kernel points g_marks at
+// a buffer and sets s_mark_base for one CTA and phase; mark(k) stores the
+// globaltimer there.  Null everywhere else.
+static __device__ unsigned long long* g_marks = nullptr;
+static __shared__ int s_mark_base;
+__device__ __forceinline__ void mark(int k) {
+  if (g_marks && threadIdx.x == 0 && s_mark_base >= 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_marks[s_mark_base + k] = t;
+    g_marks[80 + s_mark_base + k] = (unsigned long long)clock64();
+  }
+}
+
+// ======================================================================
+// Block reductions
+// ======================================================================
+__device__ __forceinline__ float block_sum(float v, float* sbuf) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kCtaThreads >> 5;
+  v = warp_sum(v);
+  cta_sync();
+  if (lane == 0) sbuf[warp] = v;
+  cta_sync();
+  float r = 0.f;
+  for (int i = 0; i < nw; i++) r += sbuf[i];  // fixed order: deterministic
+  return r;
+}
+__device__ __forceinline__ float block_max(float v, float* sbuf) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kCtaThreads >> 5;
+  v = warp_max(v);
+  cta_sync();
+  if (lane == 0) sbuf[warp] = v;
+  cta_sync();
+  float r = sbuf[0];
+  for (int i = 1; i < nw; i++) r = fmaxf(r, sbuf[i]);
+  return r;
+}
+
+// ======================================================================
+// GEMV prologue: resolve the input vector (plain / RMSNorm / embed+RMSNorm)
+// ======================================================================
+struct XCtx {
+  int mode, f16;
+  const float* x;
+  const float* g;
+  const int8_t* erow;
+  float escale, inv;
+  __half inv16;
+};
+
+__device__ __forceinline__ float raw_at(const XCtx& c, int k) {
+  return c.mode == X_EMBED_RMS ? (float)c.erow[k] * c.escale : c.x[k];
+}
+// RMSNORM: y = x*inv*g (kernels.js:143); RMSNORM_F16: f16(f16(x)*inv)*f16(g)
+// (kernels.js:165) with inv rounded to f16.
+__device__ __forceinline__ float xval(const XCtx& c, int k) {
+  const float r = raw_at(c, k);
+  if (c.mode == X_PLAIN) return r;
+  if (!c.f16) return __fmul_rn(__fmul_rn(r, c.inv), c.g[k]);
+  __half t = __hmul_rn(__float2half_rn(r), c.inv16);
+  t = __hmul_rn(t, __float2half_rn(c.g[k]));
+  return __half2float(t);
+}
+
+__device__ __forceinline__ void setup_x(const XSrc& s, int K, XCtx& c, float* sred) {
+  c.mode = s.mode;
+  c.f16 = s.f16;
+  c.x = s.x;
+  c.g = s.norm_g;
+  c.erow = nullptr;
+  c.escale = 0.f;
+  c.inv = 1.f;
+  c.inv16 = __float2half_rn(1.f);
+  if (s.mode == X_EMBED_RMS) {
+    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
+    c.erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
+    c.escale = s.emb_s[id];
+    if (blockIdx.x == 0 && s.hidden_out)
+      for (int k = threadIdx.x; k < K; k += kCtaThreads) s.hidden_out[k] = raw_at(c, k);
+  }
+  if (s.mode != X_PLAIN) {
+    float ss = 0.f;
+    for (int k = threadIdx.x; k < K; k += kCtaThreads) {
+      const float v = raw_at(c, k);
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+    ss = block_sum(ss, sred);
+    c.inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
+    c.inv16 = __float2half_rn(c.inv);
+  }
+}
+
+// Power-of-two shift keeping |x| * 2^-e inside the f16 range.
+__device__ __forceinline__ int shift_for(float amax) {
+  if (!(amax > 16384.f)) return 0;
+  int e;
+  frexpf(amax / 16384.f, &e);
+  return e;
+}
+
+// Register-staged prologue.  Thread i owns the 8-element units
+// u = i, i + blockDim, ... (k = 8u..8u+7); every global load of the input
+// (and of the norm weight) is issued before any is consumed, so the whole
+// prologue costs one memory latency.  The values are then transformed
+// (RMSNorm), range-checked and written once as MMA B fragments:
+//   fmt 4: int4 layout (see write_int4_word), fmt 8: int8 layout.
+// NORM = false compiles the plain-vector case only (fewer live registers).
+template <int MAXU, bool NORM = true>
+__device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred) {
+  const int K8 = K / 8;
+  float v[MAXU][8];
+  float gw[NORM ? MAXU : 1][8];
+  const int8_t* erow = nullptr;
+  float escale = 0.f;
+  if ((NORM && s.mode == X_EMBED_RMS)) {
+    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
+    erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
+    escale = s.emb_s[id];
+  }
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * kCtaThreads;
+    const bool ok = u < K8;
+    if ((NORM && s.mode == X_EMBED_RMS)) {
+      const uint2 b = ok ? *reinterpret_cast<const uint2*>(erow + 8 * u) : make_uint2(0, 0);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int8_t q = (int8_t)(((j < 4 ? b.x : b.y) >> (8 * (j & 3))) & 0xFF);
+        v[i][j] = __fmul_rn((float)q, escale);  // EMBED_BUF: f32(q8) * scale[id]
+      }
+    } else {
+      const float4 a = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u)) : make_float4(0, 0, 0, 0);
+      const float4 b = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u + 4)) : make_float4(0, 0, 0, 0);
+      v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+      v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+    }
+    if ((NORM && s.mode != X_PLAIN)) {
+      const float4 a = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u)) : make_float4(0, 0, 0, 0);
+      const float4 b = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u + 4)) : make_float4(0, 0, 0, 0);
+      gw[NORM ? i : 0][0] = a.x; gw[NORM ? i : 0][1] = a.y; gw[NORM ? i : 0][2] = a.z; gw[NORM ? i : 0][3] = a.w;
+      gw[NORM ? i : 0][4] = b.x; gw[NORM ? i : 0][5] = b.y; gw[NORM ? i : 0][6] = b.z; gw[NORM ? i : 0][7] = b.w;
+    }
+  }
+  if ((NORM && s.mode == X_EMBED_RMS) && blockIdx.x == 0 && s.hidden_out) {
+#pragma unroll
+    for (int i = 0; i < MAXU; i++) {
+      const int u = threadIdx.x + i * kCtaThreads;
+      if (u < K8) {
+        *reinterpret_cast<float4*>(s.hidden_out + 8 * u) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        *reinterpret_cast<float4*>(s.hidden_out + 8 * u + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+      }
+    }
+  }
+  mark(6);
+  if ((NORM && s.mode != X_PLAIN)) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
+    ss = block_sum(ss, sred);
+    // RMSNORM: inverseSqrt(sum/K + eps) (kernels.js:142), IEEE sqrt + divide
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
+    const __half inv16 = __float2half_rn(inv);
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        if (!s.f16) {
+          v[i][j] = __fmul_rn(__fmul_rn(v[i][j], inv), gw[NORM ? i : 0][j]);
+          v[i][j + 1] = __fmul_rn(__fmul_rn(v[i][j + 1], inv), gw[NORM ? i : 0][j + 1]);
+        } else {  // RMSNORM_F16: f16(f16(x) * inv) * f16(g), two lanes at a time
+          __half2 t = __hmul2_rn(__floats2half2_rn(v[i][j], v[i][j + 1]), __half2half2(inv16));
+          t = __hmul2_rn(t, __floats2half2_rn(gw[NORM ? i : 0][j], gw[NORM ? i : 0][j + 1]));
+          const float2 r = __half22float2(t);
+          v[i][j] = r.x;
+          v[i][j + 1] = r.y;
+        }
+      }
+  }
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXU; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
+  mark(7);
+  const int e = shift_for(block_max(am, sred));
+  mark(8);
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * kCtaThreads;
+    if (u >= K8) continue;
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) x[j] = e ? ldexpf(v[i][j], -e) : v[i][j];
+    if (fmt == 4) {
+      uint4* xs = reinterpret_cast<uint4*>(smem);
+      uint4* lo = xs + K8 + 4;
+      uint4 h, l;
+      split_h2(x[0], x[4], h.x, l.x);
+      split_h2(x[1] * 0.0625f, x[5] * 0.0625f, h.y, l.y);
+      split_h2(x[2], x[6], h.z, l.z);
+      split_h2(x[3] * 0.0625f, x[7] * 0.0625f, h.w, l.w);
+      const int slot = (u & ~15) + 4 * (u & 3) + ((u >> 2) & 3);
+      xs[slot] = h;
+      lo[slot] = l;
+    } else {
+      uint2* xs2 = reinterpret_cast<uint2*>(smem);
+      uint2* lo = xs2 + K / 4 + 2;
+      uint2 h, l;
+      split_h2(x[0], x[2], h.x, l.x);
+      split_h2(x[1], x[3], h.y, l.y);
+      xs2[2 * u] = h;
+      lo[2 * u] = l;
+      split_h2(x[4], x[6], h.x, l.x);
+      split_h2(x[5], x[7], h.y, l.y);
+      xs2[2 * u + 1] = h;
+      lo[2 * u + 1] = l;
+    }
+  }
+  cta_sync();
+  return e;
+}
+
+// ======================================================================
+// Epilogues (GEMV4 / GEMV4_ADD / GATE_UP_SILU_GEMV4, kernels.js:884-1072)
+// ======================================================================
+__device__ __forceinline__ float lora_dot(const Epi& e, int m, int nm, int Nm) {
+  const LoraMod md = e.mods[m];
+  if (md.rank <= 0 || !md.B) return 0.f;
+  const float* d = e.lora_d + m * kMaxRank;
+  float dl = 0.f;
+  for (int r = 0; r < md.rank; r++) dl = __fadd_rn(dl, __fmul_rn(d[r], md.B[(size_t)r * Nm + nm]));
+  return __fmul_rn(md.scale, dl);
+}
+
+__device__ __forceinline__ void epilogue_row(const Epi& e, int n, float v, float v2) {
+  if (n >= e.N) return;
+  if (e.mode == EPI_SILU) {
+    float g = v, u = v2;
+    if (e.mods) {
+      g = __fadd_rn(g, lora_dot(e, 0, n, e.N));
+      u = __fadd_rn(u, lora_dot(e, 1, n, e.N));
+    }
+    e.y[n] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+    return;
+  }
+  float o = v;
+  if (e.bias) o = __fadd_rn(o, e.bias[n]);
+  if (e.mods) {
+    int m = 0, nm = n, Nm = e.split1;
+    if (n >= e.split2) {
+      m = 2;
+      nm = n - e.split2;
+      Nm = e.N - e.split2;
+    } else if (n >= e.split1) {
+      m = 1;
+      nm = n - e.split1;
+      Nm = e.split2 - e.split1;
+    }
+    o = __fadd_rn(o, lora_dot(e, m, nm, Nm));
+  }
+  e.y[n] = e.mode == EPI_ADD ? __fadd_rn(__ldcg(e.y + n), o) : o;
+}
+
+// The global value an epilogue row reads (residual y[n] or bias[n]), loaded
+// ahead of time so the epilogue itself does no memory round trip.
+__device__ __forceinline__ float epi_pre(const Epi& e, int n) {
+  if (n >= e.N) return 0.f;
+  if (e.mode == EPI_ADD) return __ldcg(e.y + n);
+  if (e.mode == EPI_STORE && e.bias) return __ldg(e.bias + n);
+  return 0.f;
+}
+// epilogue_row with the epi_pre value supplied (no LoRA: fused path).
+__device__ __forceinline__ void epilogue_row_pre(const Epi& e, int n, float v, float v2, float pre) {
+  if (n >= e.N) return;
+  if (e.mode == EPI_SILU) {
+    e.y[n] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.f, expf(-v))), v2);
+    return;
+  }
+  if (e.mode == EPI_ADD) {
+    e.y[n] = __fadd_rn(pre, v);
+    return;
+  }
+  e.y[n] = e.bias ? __fadd_rn(v, pre) : v;
+}
+
+// ======================================================================
+// int4 GEMV
+// ======================================================================
+// R = row tiles per block (2 for the gate/up pair), U = groups in flight per
+// warp, W = warps (split-K over the 128-wide groups).  The first U groups of
+// weights are requested before the activation prologue (they do not depend on
+// the previous kernel), so their HBM latency overlaps the wait and the
+// x-staging; later groups are fetched one batch ahead of the math.
+template <int R, int U>
+struct WBatch {
+  uint4 a[U][R], b[U][R];
+};
+
+template <int R, int U, int W>
+__device__ __forceinline__ void load_batch(WBatch<R, U>& wb, const uint32_t* __restrict__ w, int K8,
+                                           int gpr, int G0, const int (&row_a)[R],
+                                           const int (&row_b)[R], const bool (&va)[R],
+                                           const bool (&vb)[R], int t) {
+#pragma unroll
+  for (int u = 0; u < U; u++) {
+    const int G = G0 + u * W;
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      const bool ok = G < gpr;
+      wb.a[u][r] = (ok && va[r]) ? ldg_stream(w + (size_t)row_a[r] * K8 + 16 * G + 4 * t)
+                                 : make_uint4(0, 0, 0, 0);
+      wb.b[u][r] = (ok && vb[r]) ? ldg_stream(w + (size_t)row_b[r] * K8 + 16 * G + 4 * t)
+                                 : make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+template <int U>
+struct W8Batch {
+  uint4 a[U], b[U];
+};
+template <int U, int W>
+__device__ __forceinline__ void load8(W8Batch<U>& wb, const uint32_t* __restrict__ w, int K4, int nch,
+                                      int N, int tile, int C0, int gq, int t) {
+  const int ra = tile * 16 + gq, rb = ra + 8;
+#pragma unroll
+  for (int u = 0; u < U; u++) {
+    const int Ch = C0 + u * W;
+    wb.a[u] = (Ch < nch && ra < N) ? ldg_stream(w + (size_t)ra * K4 + 16 * Ch + 4 * t) : make_uint4(0, 0, 0, 0);
+    wb.b[u] = (Ch < nch && rb < N) ? ldg_stream(w + (size_t)rb * K4 + 16 * Ch + 4 * t) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// RoPE pair (kernels.js:224-227 / 251-254): two separately rounded products
+// then one add; the f16 variant rounds inputs, products and sum to f16.
+__device__ __forceinline__ void rope_pair(float& lo, float& hi, float c, float s, int f16) {
+  if (!f16) {
+    const float a = __fmul_rn(lo, c), b = __fmul_rn(-hi, s);
+    const float d = __fmul_rn(hi, c), e = __fmul_rn(lo, s);
+    lo = __fadd_rn(a, b);
+    hi = __fadd_rn(d, e);
+  } else {
+    // (xl*c + -(xh*s), xh*c + xl*s), each product and sum rounded to f16
+    const __half2 cs = __floats2half2_rn(c, s);
+    const __half2 x = __floats2half2_rn(lo, hi);                     // (xl, xh)
+    const __half2 p = __hmul2_rn(x, __low2half2(cs));                 // (xl*c, xh*c)
+    const __half2 q = __hmul2_rn(__lowhigh2highlow(x), __high2half2(cs));  // (xh*s, xl*s)
+    const __half2 r = __hadd2_rn(p, __halves2half2(__hneg(__low2half(q)), __high2half(q)));
+    const float2 f = __half22float2(r);
+    lo = f.x;
+    hi = f.y;
+  }
+}
+
+__host__ __device__ __forceinline__ int attn_chunk(int ctx, int fixed) {
+  if (fixed > 0) return fixed;
+  int c = (ctx + 63) / 64;          // aim for ~64 splits per KV head
+  c = (c + 15) & ~15;
+  return c < 16 ? 16 : (c > 64 ? 64 : c);
+}
+
+constexpr int kAttnMaxChunk = 64;
+constexpr int kAttnMaxGroup = 8;
+
+template <typename KVT>
+__device__ __forceinline__ float kv_load(const KVT* p);
+template <>
+__device__ __forceinline__ float kv_load<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float kv_load<__half>(const __half* p) { return __half2float(*p); }
+template <typename KVT>
+__device__ __forceinline__ KVT kv_cvt(float v);
+template <>
+__device__ __forceinline__ float kv_cvt<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half kv_cvt<__half>(float v) { return __float2half_rn(v); }
+
+template <typename KVT>
+__device__ __forceinline__ void kv_row4(const KVT* p, float* dst);  // 4 consecutive values
+template <>
+__device__ __forceinline__ void kv_row4<float>(const float* p, float* dst) {
+  *reinterpret_cast<float4*>(dst) = __ldcg(reinterpret_cast<const float4*>(p));
+}
+template <>
+__device__ __forceinline__ void kv_row4<__half>(const __half* p, float* dst) {
+  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  *reinterpret_cast<float4*>(dst) = make_float4(a.x, a.y, b.x, b.y);
+}
+
+constexpr int kKsStride = kHeadDim + 4;  // padded K rows (keeps float4 alignment)
+
+__device__ __forceinline__ void block_best(float& v, uint32_t& id, float* sv, uint32_t* si) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kCtaThreads >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, id, o);
+    if (beats(ov, oi, v, id)) {
+      v = ov;
+      id = oi;
+    }
+  }
+  cta_sync();
+  if (lane == 0) {
+    sv[warp] = v;
+    si[warp] = id;
+  }
+  cta_sync();
+  v = sv[0];
+  id = si[0];
+  for (int i = 1; i < nw; i++)
+    if (beats(sv[i], si[i], v, id)) {
+      v = sv[i];
+      id = si[i];
+    }
+}
+
+// One block per (split, kv head): RoPE on the group's q heads, RoPE + append
+// of the new k/v row when this split holds position pos, split-K partials for
+// the group's q heads (one warp per head), then the last block of the KV head
+// to finish merges all splits (ATTN_COMBINE) and writes the output.
+template <typename KVT>
+__device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_smem, int pdl) {
+  __shared__ __align__(16) float qs[kAttnMaxGroup][kHeadDim];
+  __shared__ float sc[kAttnMaxGroup][kAttnMaxChunk];
+  __shared__ __align__(16) float knew[kHeadDim];
+  __shared__ __align__(16) float vnew[kHeadDim];
+  __shared__ bool last;
+  float* ks = attn_smem;                              // [chunk][kKsStride]
+  float* vs = attn_smem + kAttnMaxChunk * kKsStride;  // [chunk][128]
+  if (pdl) pdl_wait();
+  const int pos = a.pos ? *a.pos : a.fixed_pos;
+  const int ctx = pos + 1;
+  const int chunk = attn_chunk(ctx, a.chunk);
+  const int nsplit = (ctx + chunk - 1) / chunk;
+  if (split >= nsplit) return;
+  if (pdl) pdl_launch_dependents();
+  const int G = a.nh / a.nkv, hd = kHeadDim, half = hd / 2;
+  const int kvd = a.nkv * hd;
+  const int f16 = a.kv_f16;
+  const float* cs = a.cosT + (size_t)pos * hd;
+  const float* sn = a.sinT + (size_t)pos * hd;
+  for (int idx = threadIdx.x; idx < G * half; idx += kCtaThreads) {
+    const int hh = idx / half, j = idx % half;
+    const float* q = a.qkv + (kvh * G + hh) * hd;
+    float lo = __ldcg(q + j), hi = __ldcg(q + j + half);
+    rope_pair(lo, hi, cs[j], sn[j], f16);
+    if (f16) round_h2(lo, hi);  // ATTN_PARTIAL_F16 reads q through f16
+    qs[hh][j] = lo;
+    qs[hh][j + half] = hi;
+  }
+  mark(1);
+  const int t0 = split * chunk;
+  const int t1 = min(t0 + chunk, ctx);
+  const int len = t1 - t0;
+  KVT* kc = reinterpret_cast<KVT*>(a.kc);
+  KVT* vc = reinterpret_cast<KVT*>(a.vc);
+  const bool has_new = pos >= t0 && pos < t1;
+  if (has_new) {  // ROPE_QK on k, then the KV append (runtime.js:1509-1514)
+    const float* k = a.qkv + a.nh * hd + kvh * hd;
+    const float* v = a.qkv + a.nh * hd + kvd + kvh * hd;
+    for (int j = threadIdx.x; j < half; j += kCtaThreads) {
+      float lo = __ldcg(k + j), hi = __ldcg(k + j + half);
+      rope_pair(lo, hi, cs[j], sn[j], f16);
+      float rl = lo, rh = hi;
+      if (f16) round_h2(rl, rh);
+      knew[j] = rl;
+      knew[j + half] = rh;
+      kc[(size_t)pos * kvd + kvh * hd + j] = kv_cvt<KVT>(lo);
+      kc[(size_t)pos * kvd + kvh * hd + j + half] = kv_cvt<KVT>(hi);
+    }
+    for (int j = threadIdx.x; j < hd; j += kCtaThreads) {
+      const float vj = __ldcg(v + j);
+      vnew[j] = f16 ? round_h(vj) : vj;
+      vc[(size_t)pos * kvd + kvh * hd + j] = kv_cvt<KVT>(vj);
+    }
+  }
+  cta_sync();
+  for (int idx = threadIdx.x; idx < len * (hd / 4); idx += kCtaThreads) {
+    const int tt = idx / (hd / 4), d = 4 * (idx % (hd / 4)), t = t0 + tt;
+    if (t == pos) {
+      *reinterpret_cast<float4*>(ks + tt * kKsStride + d) = *reinterpret_cast<const float4*>(knew + d);
+      *reinterpret_cast<float4*>(vs + tt * hd + d) = *reinterpret_cast<const float4*>(vnew + d);
+    } else {
+      kv_row4<KVT>(kc + (size_t)t * kvd + kvh * hd + d, ks + tt * kKsStride + d);
+      kv_row4<KVT>(vc + (size_t)t * kvd + kvh * hd + d, vs + tt * hd + d);
+    }
+  }
+  cta_sync();
+  mark(3);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float scale = 1.0f / sqrtf((float)hd);
+  for (int hh = warp; hh < G; hh += kCtaThreads / 32) {
+    const float4 q4 = *reinterpret_cast<const float4*>(&qs[hh][4 * lane]);
+    float m = -1e30f;
+    for (int tt = 0; tt < len; tt++) {
+      const float4 k4 = *reinterpret_cast<const float4*>(ks + tt * kKsStride + 4 * lane);
+      float p = __fmul_rn(q4.x, k4.x);
+      p = __fadd_rn(p, __fmul_rn(q4.y, k4.y));
+      p = __fadd_rn(p, __fmul_rn(q4.z, k4.z));
+      p = __fadd_rn(p, __fmul_rn(q4.w, k4.w));
+      const float sv = __fmul_rn(warp_sum(p), scale);
+      if (lane == 0) sc[hh][tt] = sv;
+      m = fmaxf(m, sv);
+    }
+    __syncwarp();
+    float z = 0.f;
+    for (int tt = lane; tt < len; tt += 32) {
+      const float ev = expf(sc[hh][tt] - m);
+      sc[hh][tt] = ev;
+      z += ev;
+    }
+    z = warp_sum(z);
+    __syncwarp();
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int tt = 0; tt < len; tt++) {
+      const float ev = sc[hh][tt];
+      const float4 v4 = *reinterpret_cast<const float4*>(vs + tt * hd + 4 * lane);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(ev, v4.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(ev, v4.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(ev, v4.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(ev, v4.w));
+    }
+    const int h = kvh * G + hh;
+    *reinterpret_cast<float4*>(a.po + ((size_t)h * a.max_splits + split) * hd + 4 * lane) = acc;
+    if (lane == 0) {
+      a.pm[h * a.max_splits + split] = m;
+      a.pz[h * a.max_splits + split] = z;
+    }
+  }
+  mark(4);
+  // ---- last block of this KV head merges the splits (ATTN_COMBINE[_F16],
+  // kernels.js:346-388)
+  __threadfence();
+  cta_sync();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(a.counters + kvh, 1u);
+    last = prev == (unsigned)nsplit - 1;
+  }
+  cta_sync();
+  mark(5);
+  if (!last) return;
+  __threadfence();
+  for (int hh = warp; hh < G; hh += kCtaThreads / 32) {
+    const int h = kvh * G + hh;
+    const float* pm = a.pm + h * a.max_splits;
+    const float* pz = a.pz + h * a.max_splits;
+    float M = -1e30f;
+    for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(pm + s2));
+    float Z = 0.f;
+    for (int s2 = 0; s2 < nsplit; s2++) Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), expf(__ldcg(pm + s2) - M)));
+    const float invZ = 1.0f / Z;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s2 = 0; s2 < nsplit; s2++) {
+      const float wgt = expf(__ldcg(pm + s2) - M);
+      float4 p = __ldcg(reinterpret_cast<const float4*>(a.po + ((size_t)h * a.max_splits + s2) * hd + 4 * lane));
+      if (f16) {
+        round_h2(p.x, p.y);
+        round_h2(p.z, p.w);
+      }
+      acc.x = __fadd_rn(acc.x, __fmul_rn(wgt, p.x));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(wgt, p.y));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(wgt, p.z));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(wgt, p.w));
+    }
+    *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
+        make_float4(__fmul_rn(acc.x, invZ), __fmul_rn(acc.y, invZ), __fmul_rn(acc.z, invZ),
+                    __fmul_rn(acc.w, invZ));
+  }
+  if (threadIdx.x == 0) a.counters[kvh] = 0u;  // ready for the next launch
+  cta_sync();
+}
+
+}  // namespace eg

@@ -29,9 +29,10 @@ struct XSrc {
   // written to hidden_out by block 0, then normalised.
   const uint32_t* emb_w;
   const float* emb_s;
-  const int* pos;
+  const int* pos;       // device position, or null to use fixed_pos
   const uint32_t* ids;
   float* hidden_out;
+  int fixed_pos;
 };
 
 enum EpiMode { EPI_STORE = 0, EPI_ADD = 1, EPI_SILU = 2 };

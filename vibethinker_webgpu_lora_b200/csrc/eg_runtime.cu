@@ -9,6 +9,7 @@
 // block runs argmax and advances the position, so decodeBatch's chain of K
 // greedy tokens (runtime.js:1776-1793) needs no host round trip.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -19,6 +20,7 @@
 #include <string>
 #include <vector>
 
+#include "eg_fused.h"
 #include "eg_host.h"
 #include "eg_kernels.h"
 #include "emberglass.h"
@@ -79,6 +81,9 @@ struct eg_rt {
   uint32_t* cand_i = nullptr;
   unsigned* counter = nullptr;
   unsigned* attn_counters = nullptr;
+  unsigned* lm_counter = nullptr;
+  unsigned* fused_sync = nullptr;     // [0] barrier counter, [1] error word
+  eg::FusedLayer* d_layers = nullptr;  // device copy of the per-layer pointers
   uint32_t* sample_ids = nullptr;
   float* sample_vals = nullptr;
   eg::LoraMod* lora_table = nullptr;  // device [layers*7]
@@ -91,6 +96,8 @@ struct eg_rt {
   cudaGraphExec_t graph[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [greedy][lora]
   int graph_rank[2] = {0, 0};
   int launches_per_step = 0;
+  int diag = 0;
+  int l2_ahead = 16;  // fused path: units of L2 prefetch ahead of the smem ring
   std::atomic<bool> busy{false};
   int64_t weight_bytes = 0, kv_bytes = 0, scratch_bytes = 0;
 };
@@ -549,6 +556,82 @@ static eg_status need_ready(eg_rt* rt) {
 
 static eg_status sync(eg_rt* rt) {
   CK(cudaStreamSynchronize(rt->st));
+  if (rt->fused_sync) {
+    unsigned err = 0;
+    CK(cudaMemcpy(&err, rt->fused_sync + 1, 4, cudaMemcpyDeviceToHost));
+    if (err) return fail(EG_ERR_DEVICE, "fused decode: a grid barrier wait timed out");
+  }
+  return EG_OK;
+}
+
+static bool fused_ok(eg_rt* rt) {
+  const eg_config& c = rt->c;
+  return rt->o.use_fused && !rt->active && c.hidden_size <= 2048 &&
+         c.num_heads * c.head_dim <= 2048 && c.intermediate_size <= 12288;
+}
+
+// n decode steps from start_pos in one cooperative launch (ids[start_pos..]
+// already hold the input tokens; greedy chains argmax into the next id).
+static eg_status run_fused(eg_rt* rt, int start_pos, int n, bool greedy, bool lm_every,
+                           unsigned long long* prof = nullptr) {
+  const eg_config& c = rt->c;
+  CK(cudaMemsetAsync(rt->fused_sync, 0, 2 * sizeof(unsigned), rt->st));
+  FusedArgs a = {};
+  a.layers = rt->d_layers;
+  a.layers_n = c.num_layers;
+  a.H = c.hidden_size;
+  a.QD = c.num_heads * c.head_dim;
+  a.KVD = c.num_kv_heads * c.head_dim;
+  a.I = c.intermediate_size;
+  a.V = c.vocab_size;
+  a.nh = c.num_heads;
+  a.nkv = c.num_kv_heads;
+  a.eps = c.rms_norm_eps;
+  a.f16 = rt->o.kv_f16;
+  a.emb_w = rt->emb_w;
+  a.emb_s = rt->emb_s;
+  a.final_norm = rt->final_norm;
+  a.cosT = rt->cosT;
+  a.sinT = rt->sinT;
+  a.hidden = rt->hidden;
+  a.qkv = rt->qkv;
+  a.attn = rt->attn;
+  a.tmp = rt->tmp;
+  a.logits = rt->logits;
+  a.pm = rt->pm;
+  a.pz = rt->pz;
+  a.po = rt->po;
+  a.attn_counters = rt->attn_counters;
+  a.max_splits = rt->max_splits;
+  a.attn_chunk = rt->o.attn_chunk;
+  a.ids = rt->ids;
+  a.amax = rt->amax;
+  a.out_ids = rt->out_ids;
+  a.state_pos = &rt->state->pos;
+  a.cand_v = rt->cand_v;
+  a.cand_i = rt->cand_i;
+  a.lm_counter = rt->lm_counter;
+  a.bar = rt->fused_sync;
+  a.err = reinterpret_cast<int*>(rt->fused_sync + 1);
+  a.start_pos = start_pos;
+  a.n_tokens = n;
+  a.greedy = greedy ? 1 : 0;
+  a.lm_every = lm_every ? 1 : 0;
+  a.prof = prof;
+  a.l2_ahead = rt->l2_ahead;
+  a.diag = rt->diag;
+  CK(fused_decode(a, rt->st));
+  rt->launches_per_step = 1;
+  return EG_OK;
+}
+
+// n decode steps from start_pos: fused when possible, else the graph step.
+static eg_status run_tokens(eg_rt* rt, int start_pos, int n, bool greedy, bool lm_every) {
+  if (fused_ok(rt)) return run_fused(rt, start_pos, n, greedy, lm_every);
+  for (int k = 0; k < n; k++) {
+    eg_status s = run_step(rt, greedy);
+    if (s) return s;
+  }
   return EG_OK;
 }
 
@@ -608,7 +691,7 @@ EG_API void eg_default_config(eg_config* c) {
 }
 EG_API void eg_default_options(eg_options* o) {
   if (!o) return;
-  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1};
+  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0};
 }
 
 EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** out) {
@@ -644,6 +727,8 @@ EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** 
   eg_rt* rt = new eg_rt();
   rt->c = c;
   rt->o = o;
+  if (const char* v = getenv("EG_L2_AHEAD")) rt->l2_ahead = atoi(v);
+  if (const char* v = getenv("EG_FUSED_DIAG")) rt->diag = atoi(v);
   if (cudaStreamCreateWithFlags(&rt->st, cudaStreamNonBlocking) != cudaSuccess) {
     delete rt;
     return fail(EG_ERR_CUDA, "stream create failed");
@@ -792,6 +877,10 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
   DALLOC(rt->cand_i, (size_t)ncand * 4, sb);
   DALLOC(rt->counter, 4, sb);
   DALLOC(rt->attn_counters, 64 * 4, sb);
+  DALLOC(rt->lm_counter, 4, sb);
+  DALLOC(rt->fused_sync, 2 * 4, sb);
+  CK(cudaMemset(rt->lm_counter, 0, 4));
+  CK(cudaMemset(rt->fused_sync, 0, 8));
   CK(cudaMemset(rt->attn_counters, 0, 64 * 4));
   DALLOC(rt->sample_ids, 64 * 4, sb);
   DALLOC(rt->sample_vals, 64 * 4, sb);
@@ -803,6 +892,16 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
   CK(cudaMemset(rt->amax, 0, 4));
   CK(cudaMemset(rt->state, 0, sizeof(DevState)));
   CK(cudaMemset(rt->lora_table, 0, (size_t)c.num_layers * 7 * sizeof(LoraMod)));
+  {
+    std::vector<FusedLayer> fl(c.num_layers);
+    for (int i = 0; i < c.num_layers; i++) {
+      const Layer& l = rt->L[i];
+      fl[i] = FusedLayer{l.qkv_w, l.o_w, l.gu_w, l.d_w, l.qkv_s, l.o_s, l.gu_s, l.d_s,
+                         c.attention_bias ? l.qkv_b : nullptr, l.in_norm, l.post_norm, l.kc, l.vc};
+    }
+    DALLOC(rt->d_layers, fl.size() * sizeof(FusedLayer), sb);
+    CK(cudaMemcpy(rt->d_layers, fl.data(), fl.size() * sizeof(FusedLayer), cudaMemcpyHostToDevice));
+  }
   CK(cudaMallocHost(&rt->h_small, (size_t)std::max(mc, rt->o.decode_batch_capacity) * 4 + 64));
   CK(cudaDeviceSynchronize());
   rt->finalized = true;
@@ -816,7 +915,7 @@ EG_API eg_status eg_token(eg_rt* rt, uint32_t id, int pos) {
   if (id >= (uint32_t)rt->c.vocab_size) return fail(EG_ERR_ARG, "token id %u >= vocab", id);
   CK(cudaSetDevice(rt->o.device));
   if ((s = set_state(rt, pos, 1, id, nullptr))) return s;
-  return run_step(rt, false);
+  return run_tokens(rt, pos, 1, false, true);
 }
 
 EG_API eg_status eg_decode_greedy(eg_rt* rt, int start_pos, int K, uint32_t* out_ids, int* n_out) {
@@ -830,8 +929,7 @@ EG_API eg_status eg_decode_greedy(eg_rt* rt, int start_pos, int K, uint32_t* out
   if (!b.ok) return fail(EG_ERR_BUSY, "decodeBatch() is already in flight");
   CK(cudaSetDevice(rt->o.device));
   if ((s = set_state(rt, start_pos, 1, 0, rt->amax))) return s;  // embed s.amax at start_pos
-  for (int k = 0; k < K; k++)
-    if ((s = run_step(rt, true))) return s;
+  if ((s = run_tokens(rt, start_pos, K, true, true))) return s;
   CK(cudaMemcpyAsync(rt->h_small, rt->out_ids, (size_t)K * 4, cudaMemcpyDeviceToHost, rt->st));
   if ((s = sync(rt))) return s;
   if (out_ids) memcpy(out_ids, rt->h_small, (size_t)K * 4);
@@ -848,8 +946,7 @@ EG_API eg_status eg_decode_greedy_async(eg_rt* rt, int start_pos, int K, int* n_
   if (K <= 0) return EG_OK;
   CK(cudaSetDevice(rt->o.device));
   if ((s = set_state(rt, start_pos, 1, 0, rt->amax))) return s;
-  for (int k = 0; k < K; k++)
-    if ((s = run_step(rt, true))) return s;
+  if ((s = run_tokens(rt, start_pos, K, true, true))) return s;
   if (n_out) *n_out = K;
   return EG_OK;
 }
@@ -885,8 +982,7 @@ EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T) {
   CK(cudaSetDevice(rt->o.device));
   CK(cudaMemcpyAsync(rt->ids, ids, (size_t)T * 4, cudaMemcpyHostToDevice, rt->st));
   if ((s = set_state(rt, 0, 0, 0, nullptr))) return s;
-  for (int t = 0; t < T; t++)
-    if ((s = run_step(rt, false))) return s;
+  if ((s = run_tokens(rt, 0, T, false, false))) return s;  // logits of the last position only
   return EG_OK;
 }
 
@@ -995,7 +1091,7 @@ EG_API eg_status eg_generate(eg_rt* rt, const uint32_t* prompt, int n_prompt, in
     copy_u32(rt->amax, rt->out_ids + g, rt->st);
     if (g + 1 == max_new) break;
     if ((s = set_state(rt, pos, 1, 0, rt->amax))) return s;
-    if ((s = run_step(rt, false))) return s;
+    if ((s = run_tokens(rt, pos, 1, false, true))) return s;
     pos++;
   }
   CK(cudaMemcpyAsync(rt->h_small, rt->out_ids, (size_t)max_new * 4, cudaMemcpyDeviceToHost, rt->st));
@@ -1144,6 +1240,30 @@ EG_API eg_status eg_profile_token(eg_rt* rt, uint32_t id, int pos, double* us, i
     for (int i = 0; i < 6; i++) us[i] = acc[i];
   if (n_cat) *n_cat = 6;
   return EG_OK;
+}
+
+EG_API eg_status eg_profile_fused(eg_rt* rt, int start_pos, uint64_t* out_ns, int n_max, int* n_out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (!fused_ok(rt)) return fail(EG_ERR_STATE, "fused decode not available (LoRA active or disabled)");
+  if (start_pos < 0 || start_pos >= rt->o.max_ctx) return fail(EG_ERR_ARG, "bad start_pos");
+  const int nph = 2 * (rt->c.num_layers * 5 + 1);
+  if (!out_ns || n_max < nph) return fail(EG_ERR_ARG, "need room for %d timestamps", nph);
+  const bool marks = n_max >= nph + 160;
+  CK(cudaSetDevice(rt->o.device));
+  unsigned long long* d = nullptr;
+  CK(cudaMalloc(&d, (nph + 160) * 8));
+  CK(cudaMemsetAsync(d, 0, (nph + 160) * 8, rt->st));
+  if (marks) CK(fused_set_marks(d + nph));
+  if ((s = set_state(rt, start_pos, 1, 0, rt->amax))) { cudaFree(d); return s; }
+  s = run_fused(rt, start_pos, 1, true, true, d);
+  if (!s) s = sync(rt);
+  if (!s && cudaMemcpy(out_ns, d, (marks ? nph + 160 : nph) * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+    s = fail(EG_ERR_CUDA, "profile readback failed");
+  if (marks) fused_set_marks(nullptr);
+  cudaFree(d);
+  if (n_out) *n_out = marks ? nph + 160 : nph;
+  return s;
 }
 
 EG_API eg_status eg_memory_footprint(eg_rt* rt, int64_t* kv, int64_t* w, int64_t* scratch) {

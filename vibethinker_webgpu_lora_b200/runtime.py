@@ -30,7 +30,7 @@ class QwenB200:
     opts: maxCtx, maxPrefillT, decodeBatchSize (capacity of one decodeBatch
     call), samplingTopK, maxSamplingTopK, useF16 (f16 KV cache + the
     reference's f16 staging numerics, default True), attnChunk, useGraphs,
-    usePdl, device.
+    usePdl, useFused (persistent fused decode), device.
     """
 
     def __init__(self, cfg: dict | None = None, opts: dict | None = None):
@@ -48,6 +48,7 @@ class QwenB200:
         o.attn_chunk = int(opts.get("attnChunk", 0))
         o.use_graphs = int(bool(opts.get("useGraphs", True)))
         o.use_pdl = int(bool(opts.get("usePdl", True)))
+        o.use_fused = int(bool(opts.get("useFused", False)))
         self.opts = o
         h = C.c_void_p()
         L.check(L.lib().eg_create(C.byref(_cfg_struct(self.cfg)), C.byref(o), C.byref(h)))
@@ -211,6 +212,26 @@ class QwenB200:
         n = C.c_int(0)
         L.check(L.lib().eg_profile_token(self._h, int(id), int(pos), us, C.byref(n)))
         return {PROFILE_CATEGORIES[i]: us[i] for i in range(n.value)}
+
+    def profFused(self, startPos: int) -> dict:
+        """Per-phase microseconds of one fused greedy step: 'work' = phase
+        start to the last CTA's end of work, 'wait' = from there to the next
+        phase's start (barrier + skew), summed by phase kind."""
+        n = 2 * (5 * self.cfg["numLayers"] + 1)
+        buf = np.zeros(n, np.uint64)
+        nn = C.c_int(0)
+        L.check(L.lib().eg_profile_fused(self._h, int(startPos), buf.ctypes.data, n, C.byref(nn)))
+        t = buf.astype(np.int64)
+        kinds = ["qkv", "attn", "o", "gate_up", "down"]
+        out = {f"{k}_{w}": 0.0 for k in kinds + ["lm_head"] for w in ("work", "wait")}
+        nph = n // 2
+        for p in range(nph):
+            k = "lm_head" if p == nph - 1 else kinds[p % 5]
+            out[f"{k}_work"] += (t[2 * p + 1] - t[2 * p]) / 1000
+            if p + 1 < nph:
+                out[f"{k}_wait"] += (t[2 * p + 2] - t[2 * p + 1]) / 1000
+        out["total"] = (t[-1] - t[0]) / 1000
+        return out
 
     def memoryFootprintBytes(self) -> dict:
         kv, w, s = C.c_int64(), C.c_int64(), C.c_int64()
