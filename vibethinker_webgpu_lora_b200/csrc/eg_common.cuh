@@ -61,6 +61,25 @@ EG_DEV void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A(16x32 u8, row) * B(32x8 s8, col) + C, s32 accumulate (exact).
+EG_DEV void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                      uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Nibbles 0,2,4,6 (lo) or 1,3,5,7 (hi) of a packed int4 word as four bytes
+// q + 8 in [0, 15] (offset binary), one LOP3 (+ one shift).
+EG_DEV uint32_t nib_lo_u8(uint32_t w) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(w), "r"(0x0F0F0F0Fu), "r"(0x08080808u));
+  return d;
+}
+EG_DEV uint32_t nib_hi_u8(uint32_t w) { return nib_lo_u8(w >> 4); }
+
 EG_DEV uint32_t pack_h2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);

@@ -26,6 +26,76 @@ __device__ __forceinline__ void mark(int k) {
 }
 
 // ======================================================================
+// mbarriers and bulk copies (shared-memory rings fed by cp.async.bulk)
+// ======================================================================
+constexpr long long kSpinLimit = 1LL << 24;  // polls before a wait gives up
+
+__device__ __forceinline__ bool err_set(const int* err) { return *(volatile const int*)err != 0; }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// One try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about kWaitSliceNs pass, instead of re-polling (polling warps
+// take issue slots from the warps doing the math).
+constexpr uint32_t kWaitSliceNs = 20000;
+constexpr long long kWaitSlices = 1LL << 17;  // ~2.6 s at most
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(a), "r"(parity), "r"(kWaitSliceNs)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded mbarrier phase wait; false = gave up (error recorded or seen).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t a = smem_addr(bar);
+  for (long long i = 0;; i++) {
+    if (mbar_try(a, parity)) return true;
+    // the error word is a global load (an L2 round trip): only on long waits
+    if ((i & 15) == 15 && err_set(err)) return false;
+    if (i > kWaitSlices) {
+      atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+
+// Bounded wait that ignores the error word (draining copies in flight).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_addr(bar);
+  for (long long i = 0; i <= kWaitSlices; i++)
+    if (mbar_try(a, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// global -> shared bulk copy completing on bar (16-byte aligned, size % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// ======================================================================
 // Block reductions
 // ======================================================================
 __device__ __forceinline__ float block_sum(float v, float* sbuf) {
@@ -118,9 +188,13 @@ __device__ __forceinline__ int shift_for(float amax) {
 // (RMSNorm), range-checked and written once as MMA B fragments:
 //   fmt 4: int4 layout (see write_int4_word), fmt 8: int8 layout.
 // NORM = false compiles the plain-vector case only (fewer live registers).
+// [u0, u1): the 8-wide units staged (default all); only a plain input may be
+// staged partially (RMSNorm needs the whole vector).
 template <int MAXU, bool NORM = true>
-__device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred) {
+__device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred, int u0 = 0,
+                       int u1 = -1) {
   const int K8 = K / 8;
+  if (u1 < 0) u1 = K8;
   float v[MAXU][8];
   float gw[NORM ? MAXU : 1][8];
   const int8_t* erow = nullptr;
@@ -132,8 +206,8 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred) {
   }
 #pragma unroll
   for (int i = 0; i < MAXU; i++) {
-    const int u = threadIdx.x + i * kCtaThreads;
-    const bool ok = u < K8;
+    const int u = u0 + threadIdx.x + i * kCtaThreads;
+    const bool ok = u < u1;
     if ((NORM && s.mode == X_EMBED_RMS)) {
       const uint2 b = ok ? *reinterpret_cast<const uint2*>(erow + 8 * u) : make_uint2(0, 0);
 #pragma unroll
@@ -157,8 +231,8 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred) {
   if ((NORM && s.mode == X_EMBED_RMS) && blockIdx.x == 0 && s.hidden_out) {
 #pragma unroll
     for (int i = 0; i < MAXU; i++) {
-      const int u = threadIdx.x + i * kCtaThreads;
-      if (u < K8) {
+      const int u = u0 + threadIdx.x + i * kCtaThreads;
+      if (u < u1) {
         *reinterpret_cast<float4*>(s.hidden_out + 8 * u) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
         *reinterpret_cast<float4*>(s.hidden_out + 8 * u + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
       }
@@ -201,8 +275,8 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred) {
   mark(8);
 #pragma unroll
   for (int i = 0; i < MAXU; i++) {
-    const int u = threadIdx.x + i * kCtaThreads;
-    if (u >= K8) continue;
+    const int u = u0 + threadIdx.x + i * kCtaThreads;
+    if (u >= u1) continue;
     float x[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) x[j] = e ? ldexpf(v[i][j], -e) : v[i][j];
@@ -233,6 +307,257 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred) {
   }
   cta_sync();
   return e;
+}
+
+// Prologue of the streaming int4 GEMV: the same loads and RMSNorm as
+// stage_x (fmt 4 layout), but the f16 range shift is chosen per 128-wide
+// group -- xsc[G] = 2^e_G, 1 unless some |x| in the group exceeds 16384 --
+// from a 16-lane shuffle, so a plain input needs no block-wide reduction.
+// pdl: the norm weights are read first, then griddepcontrol.wait, then the
+// input (which the previous kernel writes).
+template <int MAXU, bool NORM>
+__device__ void stage_xg(const XSrc& s, int K, uint4* xs, float* xsc, float* sred, int pdl) {
+  const int K8 = K / 8;
+  float v[MAXU][8];
+  float gw[NORM ? MAXU : 1][8];
+  if (NORM && s.mode != X_PLAIN) {
+#pragma unroll
+    for (int i = 0; i < MAXU; i++) {
+      const int u = threadIdx.x + i * kCtaThreads;
+      const bool ok = u < K8;
+      const float4 a = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u)) : make_float4(0, 0, 0, 0);
+      const float4 b = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u + 4)) : make_float4(0, 0, 0, 0);
+      gw[NORM ? i : 0][0] = a.x; gw[NORM ? i : 0][1] = a.y; gw[NORM ? i : 0][2] = a.z; gw[NORM ? i : 0][3] = a.w;
+      gw[NORM ? i : 0][4] = b.x; gw[NORM ? i : 0][5] = b.y; gw[NORM ? i : 0][6] = b.z; gw[NORM ? i : 0][7] = b.w;
+    }
+  }
+  if (pdl) pdl_wait();
+  const int8_t* erow = nullptr;
+  float escale = 0.f;
+  if (NORM && s.mode == X_EMBED_RMS) {
+    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
+    erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
+    escale = s.emb_s[id];
+  }
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * kCtaThreads;
+    const bool ok = u < K8;
+    if (NORM && s.mode == X_EMBED_RMS) {
+      const uint2 b = ok ? *reinterpret_cast<const uint2*>(erow + 8 * u) : make_uint2(0, 0);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int8_t q = (int8_t)(((j < 4 ? b.x : b.y) >> (8 * (j & 3))) & 0xFF);
+        v[i][j] = __fmul_rn((float)q, escale);  // EMBED_BUF: f32(q8) * scale[id]
+      }
+    } else {
+      const float4 a = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u)) : make_float4(0, 0, 0, 0);
+      const float4 b = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u + 4)) : make_float4(0, 0, 0, 0);
+      v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+      v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+    }
+  }
+  if (NORM && s.mode == X_EMBED_RMS && blockIdx.x == 0 && s.hidden_out) {
+#pragma unroll
+    for (int i = 0; i < MAXU; i++) {
+      const int u = threadIdx.x + i * kCtaThreads;
+      if (u < K8) {
+        *reinterpret_cast<float4*>(s.hidden_out + 8 * u) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        *reinterpret_cast<float4*>(s.hidden_out + 8 * u + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+      }
+    }
+  }
+  if (NORM && s.mode != X_PLAIN) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
+    ss = block_sum(ss, sred);
+    // RMSNORM: inverseSqrt(sum/K + eps) (kernels.js:142), IEEE sqrt + divide
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
+    const __half inv16 = __float2half_rn(inv);
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        if (!s.f16) {
+          v[i][j] = __fmul_rn(__fmul_rn(v[i][j], inv), gw[NORM ? i : 0][j]);
+          v[i][j + 1] = __fmul_rn(__fmul_rn(v[i][j + 1], inv), gw[NORM ? i : 0][j + 1]);
+        } else {  // RMSNORM_F16: f16(f16(x) * inv) * f16(g), two lanes at a time
+          __half2 t = __hmul2_rn(__floats2half2_rn(v[i][j], v[i][j + 1]), __half2half2(inv16));
+          t = __hmul2_rn(t, __floats2half2_rn(gw[NORM ? i : 0][j], gw[NORM ? i : 0][j + 1]));
+          const float2 r = __half22float2(t);
+          v[i][j] = r.x;
+          v[i][j + 1] = r.y;
+        }
+      }
+  }
+  uint4* lo = xs + K8 + 4;
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * kCtaThreads;
+    float am = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
+    // the 16 units of a group sit in 16 consecutive lanes (K8 % 16 == 0)
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const int e = shift_for(am);
+    if (u >= K8) continue;
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) x[j] = e ? ldexpf(v[i][j], -e) : v[i][j];
+    uint4 h, l;
+    split_h2(x[0], x[4], h.x, l.x);
+    split_h2(x[1] * 0.0625f, x[5] * 0.0625f, h.y, l.y);
+    split_h2(x[2], x[6], h.z, l.z);
+    split_h2(x[3] * 0.0625f, x[7] * 0.0625f, h.w, l.w);
+    const int slot = (u & ~15) + 4 * (u & 3) + ((u >> 2) & 3);
+    xs[slot] = h;
+    lo[slot] = l;
+    if ((u & 15) == 0) xsc[u >> 4] = e ? ldexpf(1.f, e) : 1.f;
+  }
+  cta_sync();
+}
+
+// Activation prologue of the integer-MMA int4 GEMV.  Each 128-wide group G
+// is put in fixed point, X = round(x * 2^f_G) with |X| < 2^30, and X is
+// written as four balanced base-256 digits d_p in [-128, 127]
+// (X = sum_p d_p 256^p; bytes of (X + 0x80808080) ^ 0x80808080), one s8
+// plane per MMA column.  Per group it stores
+//   xb:   the m16n8k32 B fragments, uint2 [G][p][t][m] (lane (p, t) of MMA m
+//         holds plane p of elements 8(4m+t) + {0,2,4,6} and + {1,3,5,7}),
+//   xcor: 8 (S_{2i} + 256 S_{2i+1}), S_p = sum of plane p over the group
+//         (removes the +8 offset of the u8 weights), i = 0, 1,
+//   xmul: 2^-f_G * 65536^i (weight of the column pair (2i, 2i+1)).
+// pdl: the norm weights are read first, then griddepcontrol.wait, then the
+// input (which the previous kernel writes).
+template <int MAXU, bool NORM>
+__device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul, float* sred,
+                         int pdl) {
+  const int K8 = K / 8;
+  float v[MAXU][8];
+  float gw[NORM ? MAXU : 1][8];
+  if (NORM && s.mode != X_PLAIN) {
+#pragma unroll
+    for (int i = 0; i < MAXU; i++) {
+      const int u = threadIdx.x + i * kCtaThreads;
+      const bool ok = u < K8;
+      const float4 a = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u)) : make_float4(0, 0, 0, 0);
+      const float4 b = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u + 4)) : make_float4(0, 0, 0, 0);
+      gw[NORM ? i : 0][0] = a.x; gw[NORM ? i : 0][1] = a.y; gw[NORM ? i : 0][2] = a.z; gw[NORM ? i : 0][3] = a.w;
+      gw[NORM ? i : 0][4] = b.x; gw[NORM ? i : 0][5] = b.y; gw[NORM ? i : 0][6] = b.z; gw[NORM ? i : 0][7] = b.w;
+    }
+  }
+  if (pdl) pdl_wait();
+  const int8_t* erow = nullptr;
+  float escale = 0.f;
+  if (NORM && s.mode == X_EMBED_RMS) {
+    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
+    erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
+    escale = s.emb_s[id];
+  }
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * kCtaThreads;
+    const bool ok = u < K8;
+    if (NORM && s.mode == X_EMBED_RMS) {
+      const uint2 b = ok ? *reinterpret_cast<const uint2*>(erow + 8 * u) : make_uint2(0, 0);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int8_t q = (int8_t)(((j < 4 ? b.x : b.y) >> (8 * (j & 3))) & 0xFF);
+        v[i][j] = __fmul_rn((float)q, escale);  // EMBED_BUF: f32(q8) * scale[id]
+      }
+    } else {
+      const float4 a = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u)) : make_float4(0, 0, 0, 0);
+      const float4 b = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u + 4)) : make_float4(0, 0, 0, 0);
+      v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+      v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+    }
+  }
+  if (NORM && s.mode == X_EMBED_RMS && blockIdx.x == 0 && s.hidden_out) {
+#pragma unroll
+    for (int i = 0; i < MAXU; i++) {
+      const int u = threadIdx.x + i * kCtaThreads;
+      if (u < K8) {
+        *reinterpret_cast<float4*>(s.hidden_out + 8 * u) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        *reinterpret_cast<float4*>(s.hidden_out + 8 * u + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+      }
+    }
+  }
+  if (NORM && s.mode != X_PLAIN) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
+    ss = block_sum(ss, sred);
+    // RMSNORM: inverseSqrt(sum/K + eps) (kernels.js:142), IEEE sqrt + divide
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
+    const __half inv16 = __float2half_rn(inv);
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        if (!s.f16) {
+          v[i][j] = __fmul_rn(__fmul_rn(v[i][j], inv), gw[NORM ? i : 0][j]);
+          v[i][j + 1] = __fmul_rn(__fmul_rn(v[i][j + 1], inv), gw[NORM ? i : 0][j + 1]);
+        } else {  // RMSNORM_F16: f16(f16(x) * inv) * f16(g), two lanes at a time
+          __half2 t = __hmul2_rn(__floats2half2_rn(v[i][j], v[i][j + 1]), __half2half2(inv16));
+          t = __hmul2_rn(t, __floats2half2_rn(gw[NORM ? i : 0][j], gw[NORM ? i : 0][j + 1]));
+          const float2 r = __half22float2(t);
+          v[i][j] = r.x;
+          v[i][j + 1] = r.y;
+        }
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * kCtaThreads;
+    float am = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
+    // the 16 units of a group sit in 16 consecutive lanes (K8 % 16 == 0)
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    // am < 2^ex, ex from the exponent field (0 and subnormals: f = 126)
+    const int ex = ((__float_as_int(am) >> 23) & 0xFF) - 126;
+    const int f = min(30 - ex, 126);
+    const float sf = __int_as_float((127 + f) << 23);  // 2^f
+    uint32_t D[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int X = __float2int_rn(v[i][j] * sf);  // exact scaling, |X| < 2^30
+      D[j] = ((uint32_t)X + 0x80808080u) ^ 0x80808080u;   // balanced base-256 digits
+    }
+    int S[4];
+    uint2 pl[4];
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      const uint32_t sel = (uint32_t)(p | ((p + 4) << 4));
+      const uint32_t e0 = __byte_perm(D[0], D[2], sel), e1 = __byte_perm(D[4], D[6], sel);
+      const uint32_t o0 = __byte_perm(D[1], D[3], sel), o1 = __byte_perm(D[5], D[7], sel);
+      pl[p].x = __byte_perm(e0, e1, 0x5410);
+      pl[p].y = __byte_perm(o0, o1, 0x5410);
+      S[p] = __dp4a((int)pl[p].x, 0x01010101, __dp4a((int)pl[p].y, 0x01010101, 0));
+    }
+#pragma unroll
+    for (int p = 0; p < 4; p++)
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) S[p] += __shfl_xor_sync(0xffffffffu, S[p], o);
+    if (u >= K8) continue;
+    const int G = u >> 4, q = u & 15, m = q >> 2, t = q & 3;
+#pragma unroll
+    for (int p = 0; p < 4; p++) xb[((G * 4 + p) * 4 + t) * 4 + m] = pl[p];
+    if (q == 0) {
+      xcor[2 * G] = 8 * (S[0] + 256 * S[1]);
+      xcor[2 * G + 1] = 8 * (S[2] + 256 * S[3]);
+      xmul[2 * G] = __int_as_float((127 - f) << 23);      // 2^-f
+      xmul[2 * G + 1] = __int_as_float((143 - f) << 23);  // 2^(16-f)
+    }
+  }
+  cta_sync();
 }
 
 // ======================================================================
@@ -440,8 +765,6 @@ template <typename KVT>
 __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_smem, int pdl) {
   __shared__ __align__(16) float qs[kAttnMaxGroup][kHeadDim];
   __shared__ float sc[kAttnMaxGroup][kAttnMaxChunk];
-  __shared__ __align__(16) float knew[kHeadDim];
-  __shared__ __align__(16) float vnew[kHeadDim];
   __shared__ bool last;
   float* ks = attn_smem;                              // [chunk][kKsStride]
   float* vs = attn_smem + kAttnMaxChunk * kKsStride;  // [chunk][128]
@@ -457,6 +780,18 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
   const int f16 = a.kv_f16;
   const float* cs = a.cosT + (size_t)pos * hd;
   const float* sn = a.sinT + (size_t)pos * hd;
+  const int t0 = split * chunk;
+  const int t1 = min(t0 + chunk, ctx);
+  const int len = t1 - t0;
+  KVT* kc = reinterpret_cast<KVT*>(a.kc);
+  KVT* vc = reinterpret_cast<KVT*>(a.vc);
+  // the cached K/V rows first: they do not depend on this step's q/k/v
+  for (int idx = threadIdx.x; idx < len * (hd / 4); idx += kCtaThreads) {
+    const int tt = idx / (hd / 4), d = 4 * (idx % (hd / 4)), t = t0 + tt;
+    if (t == pos) continue;
+    kv_row4<KVT>(kc + (size_t)t * kvd + kvh * hd + d, ks + tt * kKsStride + d);
+    kv_row4<KVT>(vc + (size_t)t * kvd + kvh * hd + d, vs + tt * hd + d);
+  }
   for (int idx = threadIdx.x; idx < G * half; idx += kCtaThreads) {
     const int hh = idx / half, j = idx % half;
     const float* q = a.qkv + (kvh * G + hh) * hd;
@@ -467,13 +802,8 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
     qs[hh][j + half] = hi;
   }
   mark(1);
-  const int t0 = split * chunk;
-  const int t1 = min(t0 + chunk, ctx);
-  const int len = t1 - t0;
-  KVT* kc = reinterpret_cast<KVT*>(a.kc);
-  KVT* vc = reinterpret_cast<KVT*>(a.vc);
-  const bool has_new = pos >= t0 && pos < t1;
-  if (has_new) {  // ROPE_QK on k, then the KV append (runtime.js:1509-1514)
+  if (pos >= t0 && pos < t1) {  // ROPE_QK on k, then the KV append (runtime.js:1509-1514)
+    const int tn = pos - t0;
     const float* k = a.qkv + a.nh * hd + kvh * hd;
     const float* v = a.qkv + a.nh * hd + kvd + kvh * hd;
     for (int j = threadIdx.x; j < half; j += kCtaThreads) {
@@ -481,26 +811,15 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
       rope_pair(lo, hi, cs[j], sn[j], f16);
       float rl = lo, rh = hi;
       if (f16) round_h2(rl, rh);
-      knew[j] = rl;
-      knew[j + half] = rh;
+      ks[tn * kKsStride + j] = rl;
+      ks[tn * kKsStride + j + half] = rh;
       kc[(size_t)pos * kvd + kvh * hd + j] = kv_cvt<KVT>(lo);
       kc[(size_t)pos * kvd + kvh * hd + j + half] = kv_cvt<KVT>(hi);
     }
     for (int j = threadIdx.x; j < hd; j += kCtaThreads) {
       const float vj = __ldcg(v + j);
-      vnew[j] = f16 ? round_h(vj) : vj;
+      vs[tn * hd + j] = f16 ? round_h(vj) : vj;
       vc[(size_t)pos * kvd + kvh * hd + j] = kv_cvt<KVT>(vj);
-    }
-  }
-  cta_sync();
-  for (int idx = threadIdx.x; idx < len * (hd / 4); idx += kCtaThreads) {
-    const int tt = idx / (hd / 4), d = 4 * (idx % (hd / 4)), t = t0 + tt;
-    if (t == pos) {
-      *reinterpret_cast<float4*>(ks + tt * kKsStride + d) = *reinterpret_cast<const float4*>(knew + d);
-      *reinterpret_cast<float4*>(vs + tt * hd + d) = *reinterpret_cast<const float4*>(vnew + d);
-    } else {
-      kv_row4<KVT>(kc + (size_t)t * kvd + kvh * hd + d, ks + tt * kKsStride + d);
-      kv_row4<KVT>(vc + (size_t)t * kvd + kvh * hd + d, vs + tt * hd + d);
     }
   }
   cta_sync();
@@ -539,6 +858,18 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
       acc.w = __fadd_rn(acc.w, __fmul_rn(ev, v4.w));
     }
     const int h = kvh * G + hh;
+    if (nsplit == 1) {  // one split: the combine is a plain 1/Z scaling (ATTN_COMBINE with nsplit 1)
+      float4 p = acc;
+      if (f16) {
+        round_h2(p.x, p.y);
+        round_h2(p.z, p.w);
+      }
+      // M = m, Z = z * e^0, o = (e^0 * po) / Z
+      const float invZ = 1.0f / z;
+      *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
+          make_float4(__fmul_rn(p.x, invZ), __fmul_rn(p.y, invZ), __fmul_rn(p.z, invZ), __fmul_rn(p.w, invZ));
+      continue;
+    }
     *reinterpret_cast<float4*>(a.po + ((size_t)h * a.max_splits + split) * hd + 4 * lane) = acc;
     if (lane == 0) {
       a.pm[h * a.max_splits + split] = m;
@@ -546,6 +877,10 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
     }
   }
   mark(4);
+  if (nsplit == 1) {
+    cta_sync();
+    return;
+  }
   // ---- last block of this KV head merges the splits (ATTN_COMBINE[_F16],
   // kernels.js:346-388)
   __threadfence();

@@ -36,11 +36,8 @@ constexpr int kSegs = 32;
 constexpr int kScaleSeg = 96;                   // per-segment room for its row's group scales
 constexpr int kStageBytes = kSegs * (kSegBytes + kScaleSeg);  // 32 KB weights + 3 KB scales
 constexpr int kChunkK = 2048;                   // int4 k-values per 1 KB row segment
-constexpr long long kSpinLimit = 1LL << 24;     // polls before a wait gives up
 
 // ---------------------------------------------------------------- waits
-__device__ __forceinline__ bool err_set(const int* err) { return *(volatile const int*)err != 0; }
-
 // Monotonic arrival counter over the consumer groups of all CTAs: the k-th
 // barrier completes when the counter reaches k * gridDim.x.  Returns false
 // (uniformly for the consumer group) when the launch is being abandoned.
@@ -71,34 +68,6 @@ __device__ __forceinline__ bool grid_barrier(unsigned* bar, int* err, unsigned& 
   }
   cta_sync();
   return s_ok != 0;
-}
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-// Bounded mbarrier phase wait; false = gave up (error recorded or seen).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  const uint32_t a = smem_addr(bar);
-  for (long long i = 0;; i++) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 63) == 0 && err_set(err)) return false;
-    if (i > kSpinLimit) {
-      atomicExch(err, 1);
-      return false;
-    }
-  }
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tile_range(int tiles, int& t0, int& t1) {

@@ -15,6 +15,8 @@
 #include <float.h>
 #include <math.h>
 
+#include <stdlib.h>
+
 #include <algorithm>
 
 #include "eg_common.cuh"
@@ -50,133 +52,378 @@ static void launch(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, 
   cudaLaunchKernelEx(&cfg, k, args...);
 }
 
-template <int R, int U, int W, int MAXU>
-__global__ void __launch_bounds__(W * 32) gemv_q4_kernel(const uint32_t* __restrict__ w,
-                                                         const float* __restrict__ s, int N,
-                                                         int K, XSrc xsrc, Epi epi, int pdl) {
-  extern __shared__ uint4 smem[];
+// ----------------------------------------------------------------------
+// Streaming int4 GEMV over the "stream" layout (q4_to_stream): the matrix
+// as blocks (tile, group) -- 16 rows x 128 k of packed nibbles (for
+// [gate;up] a tile is the gate tile plus its up tile), stored in MMA
+// fragment order and followed by the block's 16 (32) group scales -- laid
+// out tile-major, group-minor.  The tiles are split into gridDim.x
+// contiguous ranges, one per CTA, and any contiguous run of blocks is one
+// contiguous byte range: warp 8 moves each ring stage (<= 16 KB of nibbles)
+// with a single cp.async.bulk.  The weights do not depend on the previous
+// kernel, so those copies start before griddepcontrol.wait.  Warps 0-7 build
+// the activation fragments (stage_xg), then turn each stage into m16n8k16
+// MMAs; each warp's 16-byte fragment loads cover 512 contiguous bytes (no
+// bank conflicts).  Every tile is finished inside one CTA, so the epilogue
+// needs no cross-CTA combine (a memory fence under a saturated memory
+// system costs microseconds).
+struct G4Args {
+  const unsigned char* ws;  // stream layout
+  int N, K;
+  XSrc x;
+  Epi e;
+  int* err;
+  int stages, stage_bytes, xs_off, ring_off;
+  int pdl;
+};
+
+// Block of the stream layout: R * (1024 bytes of nibbles + 64 bytes of scales).
+__host__ __device__ constexpr int q4_block_bytes(int R) { return R * 1088; }
+
+constexpr int kG4Threads = kCtaThreads + 32;
+
+#ifdef EG_G4_TRACE  // timeline probe (clock64 per CTA), never in library builds
+__device__ long long g4_trace[512][64];
+__device__ int g4_diag;  // 1: consumers skip the math, 2: skip stage_xg too
+#define G4T(slot)                                                     \
+  do {                                                                \
+    if (lane == 0 && (slot) < 64) g4_trace[blockIdx.x][(slot)] = clock64(); \
+  } while (0)
+#else
+#define G4T(slot) \
+  do {            \
+  } while (0)
+#endif
+
+template <int R, int MAXU, bool NORM>
+__global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
+  extern __shared__ __align__(128) unsigned char g4_smem[];
   __shared__ float sred[32];
-  __shared__ float red[W][R][16];
-  const int K8 = K / 8, gpr = K / kGroup;
+  __shared__ float red[2][8][R][16];  // double buffered: one barrier per tile
+  uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
+  uint64_t* empty = full + p.stages;
+  const int gpr = p.K / kGroup;
+  uint2* xb = reinterpret_cast<uint2*>(g4_smem + p.xs_off);  // [gpr][4][4][4]
+  int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);  // [gpr][2]
+  float* xmul = reinterpret_cast<float*>(xcor + 2 * gpr);     // [gpr][2]
+  unsigned char* ring = g4_smem + p.ring_off;
+  const int ngcap = 16 / R;
+  const int tiles = (p.N + 15) / 16;
+  const int P = gridDim.x, c = blockIdx.x;
+  const int t_lo = (int)((long long)tiles * c / P), t_hi = (int)((long long)tiles * (c + 1) / P);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int gq = lane >> 2, t = lane & 3;
-  const int tile = blockIdx.x;
 
-  int row_a[R], row_b[R];
-  bool va[R], vb[R];
-#pragma unroll
-  for (int r = 0; r < R; r++) {
-    const int base = tile * 16 + (r ? N : 0);  // r = 1: the "up" half of [gate;up]
-    row_a[r] = base + gq;
-    row_b[r] = base + gq + 8;
-    va[r] = (tile * 16 + gq) < N;
-    vb[r] = (tile * 16 + gq + 8) < N;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.stages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 8);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  WBatch<R, U> cur;
-  load_batch<R, U, W>(cur, w, K8, gpr, warp, row_a, row_b, va, vb, t);
+  __syncthreads();
+  if (p.pdl) pdl_launch_dependents();
+  if (warp == 0) G4T(0);
 
-  if (pdl) pdl_wait();
-  const int e = stage_x<MAXU>(xsrc, K, 4, smem, sred);
-  if (pdl) pdl_launch_dependents();
+  const int blk = q4_block_bytes(R);
+  if (warp == 8) {  // ---------------------------------------------- producer
+#ifdef EG_G4_TRACE
+    if (g4_diag == 3) return;
+#endif
+    // chunks: tiles t_lo..t_hi-1, groups [g0, g0 + ng) of each; ring slot st
+    // in phase ph (incremental: no divisions in the loop)
+    uint32_t n = 0;
+    int st = 0, ph = 0;
+    bool stop = false;
+    for (int tile = t_lo; tile < t_hi && !stop; tile++)
+      for (int g0 = 0; g0 < gpr; n++) {
+        const int ng = min(ngcap, gpr - g0);
+        if (!mbar_wait(&empty[st], ph ^ 1, p.err)) {
+          stop = true;
+          break;
+        }
+        G4T(24 + (int)n);
+        if (lane == 0) {
+          mbar_expect_tx(&full[st], (uint32_t)(ng * blk));
+          bulk_g2s(ring + (size_t)st * p.stage_bytes, p.ws + ((size_t)tile * gpr + g0) * blk,
+                   (uint32_t)(ng * blk), &full[st]);
+        }
+        __syncwarp();
+        g0 += ng;
+        if (++st == p.stages) {
+          st = 0;
+          ph ^= 1;
+        }
+      }
+    // every issued copy has landed before the CTA may exit (bounded even
+    // after an error elsewhere)
+    for (uint32_t k = n > (uint32_t)p.stages ? n - p.stages : 0; k < n; k++)
+      if (!mbar_wait_bounded(&full[k % p.stages], (k / p.stages) & 1)) break;
+    return;
+  }
 
-  const uint4* xs = gq == 0 ? smem : smem + K8 + 4;
-  const bool bl = gq < 2;
+  // ------------------------------------------------------------- consumers
+#ifdef EG_G4_TRACE
+  if (g4_diag != 2)
+#endif
+  stage_xd<MAXU, NORM>(p.x, p.K, xb, xcor, xmul, sred, p.pdl);
+  // the epilogue's residual / bias of the first tile, read ahead
+  const bool lora = p.e.mods != nullptr;
+  float pre = 0.f;
+  if (warp == 0 && lane < 16 && !lora) pre = epi_pre(p.e, t_lo * 16 + lane);
+  if (warp == 0) G4T(1);
+  const int gq = lane >> 2, t = lane & 3;
+  const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
   float acc[R][2];
 #pragma unroll
   for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
-
-  for (int G0 = warp; G0 < gpr; G0 += W * U) {
-    WBatch<R, U> nxt;
-    const bool more = G0 + W * U < gpr;
-    if (more) load_batch<R, U, W>(nxt, w, K8, gpr, G0 + W * U, row_a, row_b, va, vb, t);
+  uint32_t n = 0;
+  int buf = 0, st = 0, ph = 0;
+  bool dead = false;
+  int tile = t_lo, g0 = 0;
+  for (; tile < t_hi; n++) {
+    const int ng = min(ngcap, gpr - g0);
+    // after a failed wait the CTA runs on without waiting (meeting every
+    // named barrier) and its results are void; the host sees the error word
+#ifdef EG_G4_TRACE
+    if (g4_diag == 3) dead = true;  // probe: no waits, no copies (garbage data)
+#endif
+    if (!dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
+    if (warp == 0) G4T(2 + (int)n);
+    const unsigned char* stage = ring + (size_t)st * p.stage_bytes;
+    // this warp's groups of the stage (warp, warp + 8): all shared-memory
+    // loads first, then the MMA chains interleaved, then the scaling
+    constexpr int NK = 16 / (8 * R);
+    uint4 X0[NK], X1[NK], A[NK][R], B[NK][R];
+    bool ok[NK];
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      const int G = G0 + u * W;
-      if (G >= gpr) break;
-      float c[R][4];
+    for (int k = 0; k < NK; k++) {
+      const int gi = warp + 8 * k;
+      ok[k] = gi < ng;
+#ifdef EG_G4_TRACE
+      if (g4_diag == 1 || g4_diag == 2) ok[k] = false;
+#endif
+      const int gl = ok[k] ? gi : 0;
+      // B: digit plane gq of this group's 4 k32 blocks (zero for gq >= 4)
+      X0[k] = X1[k] = make_uint4(0, 0, 0, 0);
+      if (bl) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xb + (((g0 + gl) * 4 + gq) * 4 + t) * 4);
+        X0[k] = xp[0];
+        X1[k] = xp[1];
+      }
+      const unsigned char* bp = stage + gl * blk;
 #pragma unroll
-      for (int r = 0; r < R; r++) c[r][0] = c[r][1] = c[r][2] = c[r][3] = 0.f;
+      for (int r = 0; r < R; r++) {
+        // words t, 4+t, 8+t, 12+t of rows gq (A) and gq+8 (B)
+        A[k][r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + lane * 16);
+        B[k][r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + 512 + lane * 16);
+      }
+    }
+    int c[NK][R][4];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const uint4 xb = bl ? xs[16 * G + 4 * j + t] : make_uint4(0, 0, 0, 0);
+    for (int k = 0; k < NK; k++)
+#pragma unroll
+      for (int r = 0; r < R; r++) c[k][r][0] = c[k][r][1] = c[k][r][2] = c[k][r][3] = 0;
+#pragma unroll
+    for (int m = 0; m < 4; m++)
+#pragma unroll
+      for (int k = 0; k < NK; k++)
 #pragma unroll
         for (int r = 0; r < R; r++) {
-          const uint4& A = cur.a[u][r];
-          const uint4& B = cur.b[u][r];
-          const uint32_t wa = j == 0 ? A.x : j == 1 ? A.y : j == 2 ? A.z : A.w;
-          const uint32_t wbw = j == 0 ? B.x : j == 1 ? B.y : j == 2 ? B.z : B.w;
-          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-          deq_int4(wa, a0, a1, a2, a3);
-          deq_int4(wbw, b0, b1, b2, b3);
-          mma16816(c[r], a0, b0, a1, b1, xb.x, xb.y);
-          mma16816(c[r], a2, b2, a3, b3, xb.z, xb.w);
+          const uint32_t wa = m == 0 ? A[k][r].x : m == 1 ? A[k][r].y : m == 2 ? A[k][r].z : A[k][r].w;
+          const uint32_t wb = m == 0 ? B[k][r].x : m == 1 ? B[k][r].y : m == 2 ? B[k][r].z : B[k][r].w;
+          const uint32_t b0 = m == 0 ? X0[k].x : m == 1 ? X0[k].z : m == 2 ? X1[k].x : X1[k].z;
+          const uint32_t b1 = m == 0 ? X0[k].y : m == 1 ? X0[k].w : m == 2 ? X1[k].y : X1[k].w;
+          imma16832(c[k][r], nib_lo_u8(wa), nib_lo_u8(wb), nib_hi_u8(wa), nib_hi_u8(wb), b0, b1);
         }
-      }
-      if (t == 0) {
+    if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
+#pragma unroll
+      for (int k = 0; k < NK; k++) {
+        if (!ok[k]) continue;
+        const int G = g0 + warp + 8 * k;
+        const int cor = xcor[2 * G + t];
+        const float mul = xmul[2 * G + t];
+        const float* sc = reinterpret_cast<const float*>(stage + (warp + 8 * k) * blk + R * 1024);
 #pragma unroll
         for (int r = 0; r < R; r++) {
-          const float sa = va[r] ? __ldg(s + (size_t)row_a[r] * gpr + G) : 0.f;
-          const float sb = vb[r] ? __ldg(s + (size_t)row_b[r] * gpr + G) : 0.f;
-          acc[r][0] = fmaf(sa, c[r][0] + c[r][1], acc[r][0]);
-          acc[r][1] = fmaf(sb, c[r][2] + c[r][3], acc[r][1]);
+          const float sa = sc[16 * r + gq] * mul, sb = sc[16 * r + gq + 8] * mul;
+          acc[r][0] = fmaf(sa, (float)(c[k][r][0] + 256 * c[k][r][1] - cor), acc[r][0]);
+          acc[r][1] = fmaf(sb, (float)(c[k][r][2] + 256 * c[k][r][3] - cor), acc[r][1]);
         }
       }
     }
-    if (more) cur = nxt;
-  }
-  if (t == 0) {
+    __syncwarp();
+    if (warp == 0) G4T(36 + (int)min(n, 11u));
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (++st == p.stages) {
+      st = 0;
+      ph ^= 1;
+    }
+    g0 += ng;
+    if (g0 < gpr) continue;
+    // ---- tile complete: reduce over the lanes t = 0, 1 and the warps,
+    // epilogue by warp 0
 #pragma unroll
     for (int r = 0; r < R; r++) {
-      red[warp][r][gq] = acc[r][0];
-      red[warp][r][gq + 8] = acc[r][1];
+      acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], 1);
+      acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], 1);
     }
-  }
-  __syncthreads();
-  if (threadIdx.x < 16) {
-    const int i = threadIdx.x;
-    float v[R];
+    if (t == 0) {
 #pragma unroll
-    for (int r = 0; r < R; r++) {
-      float a = 0.f;
-      for (int ww = 0; ww < W; ww++) a += red[ww][r][i];
-      v[r] = e ? ldexpf(a, e) : a;
+      for (int r = 0; r < R; r++) {
+        red[buf][warp][r][gq] = acc[r][0];
+        red[buf][warp][r][gq + 8] = acc[r][1];
+      }
     }
-    epilogue_row(epi, tile * 16 + i, v[0], R == 2 ? v[R - 1] : 0.f);
+#pragma unroll
+    for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
+    cta_sync();
+    if (warp == 0) {
+      float v = 0.f;
+      if (lane < 16 * R)
+        for (int ww = 0; ww < 8; ww++) v += red[buf][ww][lane >> 4][lane & 15];
+      const float up = __shfl_down_sync(0xffffffffu, v, 16);
+      if (lane < 16) {
+        const int row = tile * 16 + lane;
+        if (lora)
+          epilogue_row(p.e, row, v, R == 2 ? up : 0.f);
+        else
+          epilogue_row_pre(p.e, row, v, R == 2 ? up : 0.f, pre);
+        if (!lora && tile + 1 < t_hi) pre = epi_pre(p.e, row + 16);
+      }
+    }
+    if (warp == 0) G4T(48 + (int)min(n, 14u));
+    buf ^= 1;
+    g0 = 0;
+    tile++;
   }
+  if (warp == 0) G4T(63);
+#ifdef EG_G4_TRACE
+  if (threadIdx.x == 0) {
+    unsigned sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    g4_trace[blockIdx.x][62] = sm;
+  }
+#endif
 }
 
-// Units of 8 activations per thread (256 threads) the prologue holds.
+// Units of 8 activations per thread (256 threads) a register-staged
+// prologue holds.
 static int maxu_for(int K) {
   const int u = (K / 8 + 255) / 256;
   return u <= 1 ? 1 : u <= 2 ? 2 : 6;  // K <= 12288
 }
 
-template <int R, int U, int MAXU>
-static void gemv_q4_go(const uint32_t* w, const float* s, int N, int K, const XSrc& x, const Epi& e,
-                       cudaStream_t st, bool pdl) {
-  const int tiles = (N + 15) / 16;
-  const size_t smem = (size_t)(2 * (K / 8) + 8) * sizeof(uint4);
-  auto k = gemv_q4_kernel<R, U, 8, MAXU>;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch(k, dim3(tiles), dim3(256), smem, st, pdl, w, s, N, K, x, e, (int)pdl);
+// Shared-memory plan of one launch (bytes): barriers, x fragments + group
+// multipliers, then the ring.
+struct G4Plan {
+  int stages, stage_bytes, xs_off, ring_off, smem;
+};
+static G4Plan g4_plan(int R, int K) {
+  G4Plan q;
+  const int gpr = K / kGroup;
+  q.stage_bytes = (16 / R) * q4_block_bytes(R);  // 17 KB
+  q.xs_off = 128;
+  const int xbytes = gpr * (512 + 16);
+  q.ring_off = (q.xs_off + xbytes + 127) & ~127;
+  // two CTAs per SM (this kernel and the next one under PDL): ~110 KB each
+  const int budget = 110 * 1024;
+  q.stages = std::max(2, std::min(8, (budget - q.ring_off) / q.stage_bytes));
+  q.smem = q.ring_off + q.stages * q.stage_bytes;
+  return q;
 }
 
-template <int R, int U>
-static void gemv_q4_k(const uint32_t* w, const float* s, int N, int K, const XSrc& x, const Epi& e,
-                      cudaStream_t st, bool pdl) {
-  switch (maxu_for(K)) {
-    case 1: gemv_q4_go<R, U, 1>(w, s, N, K, x, e, st, pdl); break;
-    case 2: gemv_q4_go<R, U, 2>(w, s, N, K, x, e, st, pdl); break;
-    default: gemv_q4_go<R, U, 6>(w, s, N, K, x, e, st, pdl); break;
+int gemv_q4_ctas() { return getenv("EG_G4_CPS") ? atoi(getenv("EG_G4_CPS")) * sm_count() : 2 * sm_count(); }
+
+template <int R, int MAXU, bool NORM>
+static void gemv_q4_go(const G4Args& a0, const G4Plan& q, cudaStream_t st, bool pdl) {
+  G4Args a = a0;
+  a.stages = q.stages;
+  a.stage_bytes = q.stage_bytes;
+  a.xs_off = q.xs_off;
+  a.ring_off = q.ring_off;
+  a.pdl = pdl ? 1 : 0;
+  const int P = std::min(gemv_q4_ctas(), (a.N + 15) / 16);
+  auto k = gemv_q4_kernel<R, MAXU, NORM>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q.smem);
+  launch(k, dim3(P), dim3(kG4Threads), (size_t)q.smem, st, pdl, a);
+}
+
+template <int R>
+static void gemv_q4_r(const G4Args& a, cudaStream_t st, bool pdl) {
+  const G4Plan q = g4_plan(R, a.K);
+  const int u = (a.K / 8 + kCtaThreads - 1) / kCtaThreads;
+  if (a.x.mode != X_PLAIN) {  // RMSNorm holds the whole vector in registers
+    if (u <= 1) gemv_q4_go<R, 1, true>(a, q, st, pdl);
+    else if (u <= 2) gemv_q4_go<R, 2, true>(a, q, st, pdl);
+    else gemv_q4_go<R, 6, true>(a, q, st, pdl);  // K > 4096: spills, still exact
+  } else if (u <= 1) {
+    gemv_q4_go<R, 1, false>(a, q, st, pdl);
+  } else if (u <= 2) {
+    gemv_q4_go<R, 2, false>(a, q, st, pdl);
+  } else {
+    gemv_q4_go<R, 6, false>(a, q, st, pdl);
   }
 }
 
-void gemv_q4(const uint32_t* w, const float* s, int N, int K, const XSrc& x, const Epi& e,
-             cudaStream_t st, bool pdl) {
+void gemv_q4(const unsigned char* ws, int N, int K, const XSrc& x, const Epi& e, cudaStream_t st,
+             bool pdl, const GemvWork& wk) {
+  G4Args a = {};
+  a.ws = ws;
+  a.N = N;
+  a.K = K;
+  a.x = x;
+  a.e = e;
+  a.err = wk.err;
   if (e.mode == EPI_SILU)
-    gemv_q4_k<2, 2>(w, s, N, K, x, e, st, pdl);
+    gemv_q4_r<2>(a, st, pdl);
   else
-    gemv_q4_k<1, 4>(w, s, N, K, x, e, st, pdl);
+    gemv_q4_r<1>(a, st, pdl);
+}
+
+size_t q4_stream_bytes(int N, int K, int R) {
+  return (size_t)((N + 15) / 16) * (K / kGroup) * q4_block_bytes(R);
+}
+
+// One thread per 16-byte fragment word of the stream layout; rows past N
+// are zero.  Threads with u >= the fragment count copy the scales instead.
+__global__ void q4_to_stream_kernel(const uint32_t* __restrict__ w, const float* __restrict__ s,
+                                    int N, int K, int R, unsigned char* __restrict__ out) {
+  const int gpr = K / kGroup, tiles = (N + 15) / 16;
+  const long long nfrag = (long long)tiles * gpr * R * 64;  // 16-byte words
+  const long long nsc = (long long)tiles * gpr * R * 16;
+  const long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (u < nfrag) {
+    const int lane = (int)(u & 31), h = (int)((u >> 5) & 1);
+    const long long q = u >> 6;  // (block, r)
+    const int r = (int)(q % R);
+    const long long b = q / R;
+    const int G = (int)(b % gpr), tile = (int)(b / gpr);
+    const int rt = tile * 16 + 8 * h + (lane >> 2);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (rt < N) {
+      const size_t row = (size_t)rt + (size_t)r * N;
+      // words t, 4+t, 8+t, 12+t of the group (the integer-MMA k order)
+      const uint32_t* src = w + row * (K / 8) + 16 * G + (lane & 3);
+      v = make_uint4(src[0], src[4], src[8], src[12]);
+    }
+    *reinterpret_cast<uint4*>(out + b * q4_block_bytes(R) + r * 1024 + h * 512 + lane * 16) = v;
+  } else if (u < nfrag + nsc) {
+    const long long v = u - nfrag;
+    const int i = (int)(v & 15);
+    const long long q = v >> 4;
+    const int r = (int)(q % R);
+    const long long b = q / R;
+    const int G = (int)(b % gpr), tile = (int)(b / gpr);
+    const int rt = tile * 16 + i;
+    const float sv = rt < N ? s[((size_t)rt + (size_t)r * N) * gpr + G] : 0.f;
+    reinterpret_cast<float*>(out + b * q4_block_bytes(R) + R * 1024)[r * 16 + i] = sv;
+  }
+}
+
+void q4_to_stream(const uint32_t* w, const float* s, int N, int K, int R, unsigned char* out,
+                  cudaStream_t st) {
+  const long long n = (long long)((N + 15) / 16) * (K / kGroup) * R * 80;
+  q4_to_stream_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, s, N, K, R, out);
 }
 
 // ======================================================================

@@ -66,10 +66,25 @@ struct StepTail {
 
 int sm_count();
 
-// y = W4 x  (reference layout: packed u32 [N][K/8], scale f32 [N][K/128]).
-// dual: EPI_SILU over rows n and N+n of a packed [gate;up] matrix.
-void gemv_q4(const uint32_t* w, const float* s, int N, int K, const XSrc& x, const Epi& e,
-             cudaStream_t st, bool pdl);
+// Error word of the streaming int4 GEMV, set when a bounded wait gives up.
+struct GemvWork {
+  int* err;
+};
+int gemv_q4_ctas();
+
+// int4 matrices are kept on the device in the "stream" layout: blocks of
+// 16 rows x 128 k (R = 2: the gate tile and its up tile) in MMA fragment
+// order, each followed by its 16R group scales, tile-major.  q4_to_stream
+// builds it from the reference layout (packed u32 [R*N][K/8], scale f32
+// [R*N][K/128], quantize.js:81-111).
+size_t q4_stream_bytes(int N, int K, int R);
+void q4_to_stream(const uint32_t* w, const float* s, int N, int K, int R, unsigned char* out,
+                  cudaStream_t st);
+
+// y = W4 x over a stream-layout matrix (R = 2 for EPI_SILU: rows n and N+n
+// of a packed [gate;up] matrix).  Requires K % 128 == 0, K <= 12288.
+void gemv_q4(const unsigned char* ws, int N, int K, const XSrc& x, const Epi& e, cudaStream_t st,
+             bool pdl, const GemvWork& wk);
 // y = W8 x * scale[n] (int8 rows).  tail != null fuses argmax/advance.
 void gemv_q8(const uint32_t* w, const float* s, int N, int K, const XSrc& x, float* y,
              const StepTail* tail, cudaStream_t st, bool pdl);

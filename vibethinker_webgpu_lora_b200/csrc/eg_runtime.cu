@@ -48,6 +48,8 @@ struct Layer {
   float *qkv_s = nullptr, *o_s = nullptr, *gu_s = nullptr, *d_s = nullptr, *qkv_b = nullptr;
   float *in_norm = nullptr, *post_norm = nullptr;
   void *kc = nullptr, *vc = nullptr;
+  // stream-layout copies of the int4 matrices (q4_to_stream), built at finalize
+  unsigned char *qkv_t = nullptr, *o_t = nullptr, *gu_t = nullptr, *d_t = nullptr;
 };
 
 struct DevState {
@@ -110,6 +112,14 @@ static eg_status dalloc(eg_rt* rt, void** p, size_t bytes, int64_t* counter) {
   rt->allocs.push_back(*p);
   if (counter) *counter += (int64_t)bytes;
   return EG_OK;
+}
+static void dfree(eg_rt* rt, void** p, int64_t bytes, int64_t* counter) {
+  if (!*p) return;
+  for (auto& a : rt->allocs)
+    if (a == *p) a = nullptr;
+  cudaFree(*p);
+  *p = nullptr;
+  if (counter) *counter -= bytes;
 }
 #define DALLOC(ptr, bytes, ctr)                                                          \
   do {                                                                                   \
@@ -373,6 +383,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
   const bool pdl = so.pdl;
   int launches = 0;
   const LoraMod* lt = rt->lora_table;
+  const GemvWork wk{reinterpret_cast<int*>(rt->fused_sync + 1)};
   for (int i = 0; i < c.num_layers; i++) {
     const Layer& l = rt->L[i];
     XSrc xa = {};
@@ -401,7 +412,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     e.lora_d = rt->lora_d;
     e.split1 = QD;
     e.split2 = QD + KVD;
-    gemv_q4(l.qkv_w, l.qkv_s, NQKV, H, xa, e, st, pdl);
+    gemv_q4(l.qkv_t, NQKV, H, xa, e, st, pdl, wk);
     launches++;
     mark(rt, so, 0, cats);
 
@@ -440,7 +451,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     eo.mods = so.lora ? lt + i * 7 + 3 : nullptr;
     eo.lora_d = rt->lora_d;
     eo.split1 = eo.split2 = H;
-    gemv_q4(l.o_w, l.o_s, H, QD, xo, eo, st, pdl);
+    gemv_q4(l.o_t, H, QD, xo, eo, st, pdl, wk);
     launches++;
     mark(rt, so, 2, cats);
 
@@ -460,7 +471,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     eg.N = I;
     eg.mods = so.lora ? lt + i * 7 + 4 : nullptr;
     eg.lora_d = rt->lora_d;
-    gemv_q4(l.gu_w, l.gu_s, I, H, xb, eg, st, pdl);
+    gemv_q4(l.gu_t, I, H, xb, eg, st, pdl, wk);
     launches++;
     mark(rt, so, 3, cats);
 
@@ -478,7 +489,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     ed.mods = so.lora ? lt + i * 7 + 6 : nullptr;
     ed.lora_d = rt->lora_d;
     ed.split1 = ed.split2 = H;
-    gemv_q4(l.d_w, l.d_s, H, I, xd, ed, st, pdl);
+    gemv_q4(l.d_t, H, I, xd, ed, st, pdl, wk);
     launches++;
     mark(rt, so, 4, cats);
   }
@@ -559,7 +570,7 @@ static eg_status sync(eg_rt* rt) {
   if (rt->fused_sync) {
     unsigned err = 0;
     CK(cudaMemcpy(&err, rt->fused_sync + 1, 4, cudaMemcpyDeviceToHost));
-    if (err) return fail(EG_ERR_DEVICE, "fused decode: a grid barrier wait timed out");
+    if (err) return fail(EG_ERR_DEVICE, "a bounded device-side wait timed out");
   }
   return EG_OK;
 }
@@ -673,6 +684,25 @@ static eg_status op_scratch(size_t bytes, void** out) {
     s.bytes = bytes;
   }
   *out = s.p;
+  return EG_OK;
+}
+
+
+// Scratch of one single-op streaming GEMV: the error word and the matrix
+// converted to the stream layout (the single-op entry points take the
+// reference layout; the conversion is one extra pass over the weights).
+static eg_status op_gemv_work(int N, int K, int R, const uint32_t* w, const float* scale,
+                              const unsigned char** ws, GemvWork* wk, cudaStream_t st) {
+  void* scr = nullptr;
+  eg_status s = op_scratch(256 + q4_stream_bytes(N, K, R), &scr);
+  if (s) return s;
+  char* b = static_cast<char*>(scr);
+  wk->err = reinterpret_cast<int*>(b);
+  CK(cudaMemsetAsync(b, 0, 4, st));
+  unsigned char* t = reinterpret_cast<unsigned char*>(b + 256);
+  q4_to_stream(w, scale, N, K, R, t, st);
+  CK(cudaGetLastError());
+  *ws = t;
   return EG_OK;
 }
 
@@ -850,6 +880,35 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
   DALLOC(rt->sinT, sn.size() * 4, sb);
   CK(cudaMemcpy(rt->cosT, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(rt->sinT, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  {  // stream layouts of the int4 matrices; the reference-layout copies stay
+     // only for the fused kernel, which reads them directly
+    const int I = c.intermediate_size, NQKV = QD + 2 * KVD;
+    int64_t* wb = &rt->weight_bytes;
+    for (auto& l : rt->L) {
+      DALLOC(l.qkv_t, q4_stream_bytes(NQKV, H, 1), wb);
+      DALLOC(l.o_t, q4_stream_bytes(H, QD, 1), wb);
+      DALLOC(l.gu_t, q4_stream_bytes(I, H, 2), wb);
+      DALLOC(l.d_t, q4_stream_bytes(H, I, 1), wb);
+      q4_to_stream(l.qkv_w, l.qkv_s, NQKV, H, 1, l.qkv_t, rt->st);
+      q4_to_stream(l.o_w, l.o_s, H, QD, 1, l.o_t, rt->st);
+      q4_to_stream(l.gu_w, l.gu_s, I, H, 2, l.gu_t, rt->st);
+      q4_to_stream(l.d_w, l.d_s, H, I, 1, l.d_t, rt->st);
+      CK(cudaGetLastError());
+    }
+    if (!rt->o.use_fused) {
+      CK(cudaStreamSynchronize(rt->st));
+      for (auto& l : rt->L) {
+        dfree(rt, (void**)&l.qkv_w, (int64_t)NQKV * H / 2, wb);
+        dfree(rt, (void**)&l.qkv_s, (int64_t)NQKV * (H / 128) * 4, wb);
+        dfree(rt, (void**)&l.o_w, (int64_t)H * QD / 2, wb);
+        dfree(rt, (void**)&l.o_s, (int64_t)H * (QD / 128) * 4, wb);
+        dfree(rt, (void**)&l.gu_w, (int64_t)2 * I * H / 2, wb);
+        dfree(rt, (void**)&l.gu_s, (int64_t)2 * I * (H / 128) * 4, wb);
+        dfree(rt, (void**)&l.d_w, (int64_t)H * I / 2, wb);
+        dfree(rt, (void**)&l.d_s, (int64_t)H * (I / 128) * 4, wb);
+      }
+    }
+  }
   const size_t kvel = (size_t)mc * KVD * (rt->o.kv_f16 ? 2 : 4);
   for (auto& l : rt->L) {
     DALLOC(l.kc, kvel, &rt->kv_bytes);
@@ -1282,6 +1341,7 @@ EG_API int eg_launches_per_step(eg_rt* rt) { return rt ? rt->launches_per_step :
 EG_API eg_status eg_op_gemv_q4(const float* x, const uint32_t* w, const float* scale, const float* bias,
                                int N, int K, int group, float* y, int accumulate, void* stream) {
   if (!x || !w || !scale || !y || N <= 0 || K <= 0) return fail(EG_ERR_ARG, "gemv_q4: bad argument");
+  if (reinterpret_cast<uintptr_t>(w) & 15) return fail(EG_ERR_ARG, "gemv_q4: w must be 16-byte aligned");
   if (group != 128 || K % 128 || K > 12288)
     return fail(EG_ERR_ARG, "gemv_q4: group must be 128, K %% 128 == 0, K <= 12288");
   XSrc xs = {};
@@ -1294,7 +1354,11 @@ EG_API eg_status eg_op_gemv_q4(const float* x, const uint32_t* w, const float* s
   e.N = N;
   e.split1 = e.split2 = N;
   if (accumulate && bias) return fail(EG_ERR_ARG, "gemv_q4: bias with accumulate is not supported");
-  gemv_q4(w, scale, N, K, xs, e, OPSTREAM, false);
+  GemvWork wk;
+  const unsigned char* ws = nullptr;
+  eg_status s = op_gemv_work(N, K, 1, w, scale, &ws, &wk, OPSTREAM);
+  if (s) return s;
+  gemv_q4(ws, N, K, xs, e, OPSTREAM, false, wk);
   CK(cudaGetLastError());
   return EG_OK;
 }
@@ -1303,6 +1367,7 @@ EG_API eg_status eg_op_gate_up_silu(const float* x, const uint32_t* w, const flo
                                     float* y, void* stream) {
   if (!x || !w || !scale || !y || N <= 0 || K <= 0 || K % 128 || K > 12288)
     return fail(EG_ERR_ARG, "gate_up_silu: need K %% 128 == 0, K <= 12288");
+  if (reinterpret_cast<uintptr_t>(w) & 15) return fail(EG_ERR_ARG, "gate_up_silu: w must be 16-byte aligned");
   XSrc xs = {};
   xs.mode = X_PLAIN;
   xs.x = x;
@@ -1310,7 +1375,11 @@ EG_API eg_status eg_op_gate_up_silu(const float* x, const uint32_t* w, const flo
   e.mode = EPI_SILU;
   e.y = y;
   e.N = N;
-  gemv_q4(w, scale, N, K, xs, e, OPSTREAM, false);
+  GemvWork wk;
+  const unsigned char* ws = nullptr;
+  eg_status s = op_gemv_work(N, K, 2, w, scale, &ws, &wk, OPSTREAM);
+  if (s) return s;
+  gemv_q4(ws, N, K, xs, e, OPSTREAM, false, wk);
   CK(cudaGetLastError());
   return EG_OK;
 }
