@@ -108,6 +108,22 @@ __device__ __forceinline__ float block_sum(float v, float* sbuf) {
   for (int i = 0; i < nw; i++) r += sbuf[i];  // fixed order: deterministic
   return r;
 }
+// block_sum over the NT threads of named barrier 1 (NT a multiple of 32).
+template <int NT>
+__device__ __forceinline__ void bar_sync_n() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
+template <int NT>
+__device__ __forceinline__ float block_sum_n(float v, float* sbuf) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  bar_sync_n<NT>();
+  if (lane == 0) sbuf[warp] = v;
+  bar_sync_n<NT>();
+  float r = 0.f;
+  for (int i = 0; i < NT / 32; i++) r += sbuf[i];  // fixed order: deterministic
+  return r;
+}
 __device__ __forceinline__ float block_max(float v, float* sbuf) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kCtaThreads >> 5;
   v = warp_max(v);
@@ -433,7 +449,7 @@ __device__ void stage_xg(const XSrc& s, int K, uint4* xs, float* xsc, float* sre
 //   xmul: 2^-f_G * 65536^i (weight of the column pair (2i, 2i+1)).
 // pdl: the norm weights are read first, then griddepcontrol.wait, then the
 // input (which the previous kernel writes).
-template <int MAXU, bool NORM>
+template <int MAXU, bool NORM, int NT = kCtaThreads>
 __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul, float* sred,
                          int pdl) {
   const int K8 = K / 8;
@@ -442,7 +458,7 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
   if (NORM && s.mode != X_PLAIN) {
 #pragma unroll
     for (int i = 0; i < MAXU; i++) {
-      const int u = threadIdx.x + i * kCtaThreads;
+      const int u = threadIdx.x + i * NT;
       const bool ok = u < K8;
       const float4 a = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u)) : make_float4(0, 0, 0, 0);
       const float4 b = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u + 4)) : make_float4(0, 0, 0, 0);
@@ -460,7 +476,7 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
   }
 #pragma unroll
   for (int i = 0; i < MAXU; i++) {
-    const int u = threadIdx.x + i * kCtaThreads;
+    const int u = threadIdx.x + i * NT;
     const bool ok = u < K8;
     if (NORM && s.mode == X_EMBED_RMS) {
       const uint2 b = ok ? *reinterpret_cast<const uint2*>(erow + 8 * u) : make_uint2(0, 0);
@@ -479,7 +495,7 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
   if (NORM && s.mode == X_EMBED_RMS && blockIdx.x == 0 && s.hidden_out) {
 #pragma unroll
     for (int i = 0; i < MAXU; i++) {
-      const int u = threadIdx.x + i * kCtaThreads;
+      const int u = threadIdx.x + i * NT;
       if (u < K8) {
         *reinterpret_cast<float4*>(s.hidden_out + 8 * u) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
         *reinterpret_cast<float4*>(s.hidden_out + 8 * u + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
@@ -492,7 +508,7 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
     for (int i = 0; i < MAXU; i++)
 #pragma unroll
       for (int j = 0; j < 8; j++) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
-    ss = block_sum(ss, sred);
+    ss = block_sum_n<NT>(ss, sred);
     // RMSNORM: inverseSqrt(sum/K + eps) (kernels.js:142), IEEE sqrt + divide
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
     const __half inv16 = __float2half_rn(inv);
@@ -514,7 +530,7 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
   }
 #pragma unroll
   for (int i = 0; i < MAXU; i++) {
-    const int u = threadIdx.x + i * kCtaThreads;
+    const int u = threadIdx.x + i * NT;
     float am = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
@@ -557,7 +573,7 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
       xmul[2 * G + 1] = __int_as_float((143 - f) << 23);  // 2^(16-f)
     }
   }
-  cta_sync();
+  bar_sync_n<NT>();
 }
 
 // ======================================================================

@@ -80,7 +80,6 @@ struct G4Args {
 // Block of the stream layout: R * (1024 bytes of nibbles + 64 bytes of scales).
 __host__ __device__ constexpr int q4_block_bytes(int R) { return R * 1088; }
 
-constexpr int kG4Threads = kCtaThreads + 32;
 
 #ifdef EG_G4_TRACE  // timeline probe (clock64 per CTA), never in library builds
 __device__ long long g4_trace[512][64];
@@ -95,13 +94,26 @@ __device__ int g4_diag;  // 1: consumers skip the math, 2: skip stage_xg too
   } while (0)
 #endif
 
-template <int R, int MAXU, bool NORM>
-__global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
+// CW consumer warps (8 or 16), one producer warp (CW) and one epilogue warp
+// (CW + 1).  A stage holds 16 / R groups x R row sets = 16 (group, row set)
+// items; with CW = 16 each warp takes one item, with CW = 8 two.  At the end
+// of a tile the consumers leave their partial row sums in red[buf] and
+// arrive on tile_full[buf]; the epilogue warp sums them, releases the buffer
+// (tile_free[buf]) and runs the epilogue while the consumers go on.
+template <int R, int MAXU, bool NORM, int CW>
+__global__ void __launch_bounds__(CW * 32 + 64, 1) gemv_q4_kernel(G4Args p) {
+  constexpr int NT = CW * 32;
+  // items of this warp: groups gbase + GSTEP * k (k < NK), row sets r0 .. r0 + RW - 1
+  constexpr int RW = CW == 16 ? 1 : R;
+  constexpr int NK = CW == 16 ? 1 : 16 / (8 * R);
+  constexpr int GSTEP = 8;
   extern __shared__ __align__(128) unsigned char g4_smem[];
   __shared__ float sred[32];
-  __shared__ float red[2][8][R][16];  // double buffered: one barrier per tile
+  __shared__ float red[2][CW][R][16];  // double buffered: one barrier per tile
   uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
   uint64_t* empty = full + p.stages;
+  uint64_t* tile_full = empty + p.stages;  // [2]
+  uint64_t* tile_free = tile_full + 2;     // [2]
   const int gpr = p.K / kGroup;
   uint2* xb = reinterpret_cast<uint2*>(g4_smem + p.xs_off);  // [gpr][4][4][4]
   int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);  // [gpr][2]
@@ -116,7 +128,11 @@ __global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; i++) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 8);
+      mbar_init(&empty[i], CW);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&tile_full[i], CW);
+      mbar_init(&tile_free[i], 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -125,7 +141,7 @@ __global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
   if (warp == 0) G4T(0);
 
   const int blk = q4_block_bytes(R);
-  if (warp == 8) {  // ---------------------------------------------- producer
+  if (warp == CW) {  // --------------------------------------------- producer
 #ifdef EG_G4_TRACE
     if (g4_diag == 3) return;
 #endif
@@ -161,21 +177,45 @@ __global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
     return;
   }
 
+  if (warp == CW + 1) {  // ------------------------------------------- epilogue
+    if (p.pdl) pdl_wait();  // residuals are written by earlier kernels
+    const bool lora = p.e.mods != nullptr;
+    float pre = 0.f;
+    if (lane < 16 && !lora) pre = epi_pre(p.e, t_lo * 16 + lane);
+    for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
+      const int b = j & 1;
+      if (!mbar_wait(&tile_full[b], (j >> 1) & 1, p.err)) break;
+      float v = 0.f;
+      if (lane < 16 * R)
+        for (int ww = 0; ww < CW; ww++) v += red[b][ww][lane >> 4][lane & 15];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tile_free[b]);
+      const float up = __shfl_down_sync(0xffffffffu, v, 16);
+      if (lane < 16) {
+        const int row = tile * 16 + lane;
+        if (lora)
+          epilogue_row(p.e, row, v, R == 2 ? up : 0.f);
+        else
+          epilogue_row_pre(p.e, row, v, R == 2 ? up : 0.f, pre);
+        if (!lora && tile + 1 < t_hi) pre = epi_pre(p.e, row + 16);
+      }
+    }
+    return;
+  }
+
   // ------------------------------------------------------------- consumers
 #ifdef EG_G4_TRACE
   if (g4_diag != 2)
 #endif
-  stage_xd<MAXU, NORM>(p.x, p.K, xb, xcor, xmul, sred, p.pdl);
-  // the epilogue's residual / bias of the first tile, read ahead
-  const bool lora = p.e.mods != nullptr;
-  float pre = 0.f;
-  if (warp == 0 && lane < 16 && !lora) pre = epi_pre(p.e, t_lo * 16 + lane);
+  stage_xd<MAXU, NORM, NT>(p.x, p.K, xb, xcor, xmul, sred, p.pdl);
   if (warp == 0) G4T(1);
   const int gq = lane >> 2, t = lane & 3;
   const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
-  float acc[R][2];
+  const int gbase = CW == 16 && R == 2 ? (warp & 7) : warp;
+  const int r0 = CW == 16 && R == 2 ? (warp >> 3) : 0;
+  float acc[RW][2];
 #pragma unroll
-  for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
+  for (int r = 0; r < RW; r++) acc[r][0] = acc[r][1] = 0.f;
   uint32_t n = 0;
   int buf = 0, st = 0, ph = 0;
   bool dead = false;
@@ -190,14 +230,13 @@ __global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
     if (!dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
     if (warp == 0) G4T(2 + (int)n);
     const unsigned char* stage = ring + (size_t)st * p.stage_bytes;
-    // this warp's groups of the stage (warp, warp + 8): all shared-memory
-    // loads first, then the MMA chains interleaved, then the scaling
-    constexpr int NK = 16 / (8 * R);
-    uint4 X0[NK], X1[NK], A[NK][R], B[NK][R];
+    // this warp's items of the stage: all shared-memory loads first, then
+    // the MMA chains interleaved, then the scaling
+    uint4 X0[NK], X1[NK], A[NK][RW], B[NK][RW];
     bool ok[NK];
 #pragma unroll
     for (int k = 0; k < NK; k++) {
-      const int gi = warp + 8 * k;
+      const int gi = gbase + GSTEP * k;
       ok[k] = gi < ng;
 #ifdef EG_G4_TRACE
       if (g4_diag == 1 || g4_diag == 2) ok[k] = false;
@@ -212,23 +251,23 @@ __global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
       }
       const unsigned char* bp = stage + gl * blk;
 #pragma unroll
-      for (int r = 0; r < R; r++) {
+      for (int r = 0; r < RW; r++) {
         // words t, 4+t, 8+t, 12+t of rows gq (A) and gq+8 (B)
-        A[k][r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + lane * 16);
-        B[k][r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + 512 + lane * 16);
+        A[k][r] = *reinterpret_cast<const uint4*>(bp + (r0 + r) * 1024 + lane * 16);
+        B[k][r] = *reinterpret_cast<const uint4*>(bp + (r0 + r) * 1024 + 512 + lane * 16);
       }
     }
-    int c[NK][R][4];
+    int c[NK][RW][4];
 #pragma unroll
     for (int k = 0; k < NK; k++)
 #pragma unroll
-      for (int r = 0; r < R; r++) c[k][r][0] = c[k][r][1] = c[k][r][2] = c[k][r][3] = 0;
+      for (int r = 0; r < RW; r++) c[k][r][0] = c[k][r][1] = c[k][r][2] = c[k][r][3] = 0;
 #pragma unroll
     for (int m = 0; m < 4; m++)
 #pragma unroll
       for (int k = 0; k < NK; k++)
 #pragma unroll
-        for (int r = 0; r < R; r++) {
+        for (int r = 0; r < RW; r++) {
           const uint32_t wa = m == 0 ? A[k][r].x : m == 1 ? A[k][r].y : m == 2 ? A[k][r].z : A[k][r].w;
           const uint32_t wb = m == 0 ? B[k][r].x : m == 1 ? B[k][r].y : m == 2 ? B[k][r].z : B[k][r].w;
           const uint32_t b0 = m == 0 ? X0[k].x : m == 1 ? X0[k].z : m == 2 ? X1[k].x : X1[k].z;
@@ -239,13 +278,13 @@ __global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
 #pragma unroll
       for (int k = 0; k < NK; k++) {
         if (!ok[k]) continue;
-        const int G = g0 + warp + 8 * k;
+        const int gi = gbase + GSTEP * k, G = g0 + gi;
         const int cor = xcor[2 * G + t];
         const float mul = xmul[2 * G + t];
-        const float* sc = reinterpret_cast<const float*>(stage + (warp + 8 * k) * blk + R * 1024);
+        const float* sc = reinterpret_cast<const float*>(stage + gi * blk + R * 1024);
 #pragma unroll
-        for (int r = 0; r < R; r++) {
-          const float sa = sc[16 * r + gq] * mul, sb = sc[16 * r + gq + 8] * mul;
+        for (int r = 0; r < RW; r++) {
+          const float sa = sc[16 * (r0 + r) + gq] * mul, sb = sc[16 * (r0 + r) + gq + 8] * mul;
           acc[r][0] = fmaf(sa, (float)(c[k][r][0] + 256 * c[k][r][1] - cor), acc[r][0]);
           acc[r][1] = fmaf(sb, (float)(c[k][r][2] + 256 * c[k][r][3] - cor), acc[r][1]);
         }
@@ -260,37 +299,27 @@ __global__ void __launch_bounds__(kG4Threads, 2) gemv_q4_kernel(G4Args p) {
     }
     g0 += ng;
     if (g0 < gpr) continue;
-    // ---- tile complete: reduce over the lanes t = 0, 1 and the warps,
-    // epilogue by warp 0
+    // ---- tile complete: reduce over the lanes t = 0, 1; hand the warp's
+    // partial rows to the epilogue warp
 #pragma unroll
-    for (int r = 0; r < R; r++) {
+    for (int r = 0; r < RW; r++) {
       acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], 1);
       acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], 1);
     }
+    const int j = tile - t_lo;
+    if (!dead && !mbar_wait(&tile_free[buf], ((j >> 1) & 1) ^ 1, p.err)) dead = true;
     if (t == 0) {
 #pragma unroll
-      for (int r = 0; r < R; r++) {
-        red[buf][warp][r][gq] = acc[r][0];
-        red[buf][warp][r][gq + 8] = acc[r][1];
+      for (int r = 0; r < R; r++) {  // row sets this warp does not hold: 0
+        const bool mine = r >= r0 && r < r0 + RW;
+        red[buf][warp][r][gq] = mine ? acc[mine ? r - r0 : 0][0] : 0.f;
+        red[buf][warp][r][gq + 8] = mine ? acc[mine ? r - r0 : 0][1] : 0.f;
       }
     }
 #pragma unroll
-    for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
-    cta_sync();
-    if (warp == 0) {
-      float v = 0.f;
-      if (lane < 16 * R)
-        for (int ww = 0; ww < 8; ww++) v += red[buf][ww][lane >> 4][lane & 15];
-      const float up = __shfl_down_sync(0xffffffffu, v, 16);
-      if (lane < 16) {
-        const int row = tile * 16 + lane;
-        if (lora)
-          epilogue_row(p.e, row, v, R == 2 ? up : 0.f);
-        else
-          epilogue_row_pre(p.e, row, v, R == 2 ? up : 0.f, pre);
-        if (!lora && tile + 1 < t_hi) pre = epi_pre(p.e, row + 16);
-      }
-    }
+    for (int r = 0; r < RW; r++) acc[r][0] = acc[r][1] = 0.f;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tile_full[buf]);
     if (warp == 0) G4T(48 + (int)min(n, 14u));
     buf ^= 1;
     g0 = 0;
@@ -322,17 +351,19 @@ static G4Plan g4_plan(int R, int K) {
   G4Plan q;
   const int gpr = K / kGroup;
   q.stage_bytes = (16 / R) * q4_block_bytes(R);  // 17 KB
-  q.xs_off = 128;
+  q.xs_off = 256;  // barriers: 2 * stages + 4 mbarriers (stages <= 8)
   const int xbytes = gpr * (512 + 16);
   q.ring_off = (q.xs_off + xbytes + 127) & ~127;
-  // two CTAs per SM (this kernel and the next one under PDL): ~110 KB each
-  const int budget = 110 * 1024;
+  // one CTA per SM
+  const int budget = getenv("EG_G4_SMEM") ? atoi(getenv("EG_G4_SMEM")) * 1024 : 200 * 1024;
   q.stages = std::max(2, std::min(8, (budget - q.ring_off) / q.stage_bytes));
   q.smem = q.ring_off + q.stages * q.stage_bytes;
   return q;
 }
 
-int gemv_q4_ctas() { return getenv("EG_G4_CPS") ? atoi(getenv("EG_G4_CPS")) * sm_count() : 2 * sm_count(); }
+int gemv_q4_ctas() { return sm_count(); }
+
+constexpr int kG4Warps = 16;  // consumer warps per CTA (one CTA per SM)
 
 template <int R, int MAXU, bool NORM>
 static void gemv_q4_go(const G4Args& a0, const G4Plan& q, cudaStream_t st, bool pdl) {
@@ -343,25 +374,22 @@ static void gemv_q4_go(const G4Args& a0, const G4Plan& q, cudaStream_t st, bool 
   a.ring_off = q.ring_off;
   a.pdl = pdl ? 1 : 0;
   const int P = std::min(gemv_q4_ctas(), (a.N + 15) / 16);
-  auto k = gemv_q4_kernel<R, MAXU, NORM>;
+  auto k = gemv_q4_kernel<R, MAXU, NORM, kG4Warps>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q.smem);
-  launch(k, dim3(P), dim3(kG4Threads), (size_t)q.smem, st, pdl, a);
+  launch(k, dim3(P), dim3(kG4Warps * 32 + 64), (size_t)q.smem, st, pdl, a);
 }
 
 template <int R>
 static void gemv_q4_r(const G4Args& a, cudaStream_t st, bool pdl) {
   const G4Plan q = g4_plan(R, a.K);
-  const int u = (a.K / 8 + kCtaThreads - 1) / kCtaThreads;
+  const int u = (a.K / 8 + kG4Warps * 32 - 1) / (kG4Warps * 32);  // units per thread
   if (a.x.mode != X_PLAIN) {  // RMSNorm holds the whole vector in registers
     if (u <= 1) gemv_q4_go<R, 1, true>(a, q, st, pdl);
-    else if (u <= 2) gemv_q4_go<R, 2, true>(a, q, st, pdl);
-    else gemv_q4_go<R, 6, true>(a, q, st, pdl);  // K > 4096: spills, still exact
+    else gemv_q4_go<R, 3, true>(a, q, st, pdl);
   } else if (u <= 1) {
     gemv_q4_go<R, 1, false>(a, q, st, pdl);
-  } else if (u <= 2) {
-    gemv_q4_go<R, 2, false>(a, q, st, pdl);
   } else {
-    gemv_q4_go<R, 6, false>(a, q, st, pdl);
+    gemv_q4_go<R, 3, false>(a, q, st, pdl);  // K <= 12288
   }
 }
 
