@@ -784,13 +784,15 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
   __shared__ bool last;
   float* ks = attn_smem;                              // [chunk][kKsStride]
   float* vs = attn_smem + kAttnMaxChunk * kKsStride;  // [chunk][128]
-  if (pdl) pdl_wait();
-  const int pos = a.pos ? *a.pos : a.fixed_pos;
+  // The position and the cached K/V rows (t != pos) were written before the
+  // producing GEMV started (it triggers this launch only after its own
+  // griddepcontrol.wait), so they are read before this kernel's wait; only
+  // this step's q/k/v rows need it.
+  const int pos = a.pos ? __ldcg(a.pos) : a.fixed_pos;
   const int ctx = pos + 1;
   const int chunk = attn_chunk(ctx, a.chunk);
   const int nsplit = (ctx + chunk - 1) / chunk;
   if (split >= nsplit) return;
-  if (pdl) pdl_launch_dependents();
   const int G = a.nh / a.nkv, hd = kHeadDim, half = hd / 2;
   const int kvd = a.nkv * hd;
   const int f16 = a.kv_f16;
@@ -807,6 +809,10 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
     if (t == pos) continue;
     kv_row4<KVT>(kc + (size_t)t * kvd + kvh * hd + d, ks + tt * kKsStride + d);
     kv_row4<KVT>(vc + (size_t)t * kvd + kvh * hd + d, vs + tt * hd + d);
+  }
+  if (pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
   }
   for (int idx = threadIdx.x; idx < G * half; idx += kCtaThreads) {
     const int hh = idx / half, j = idx % half;

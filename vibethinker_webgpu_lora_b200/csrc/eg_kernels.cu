@@ -73,7 +73,7 @@ struct G4Args {
   XSrc x;
   Epi e;
   int* err;
-  int stages, stage_bytes, xs_off, ring_off;
+  int stages, stage_bytes, cap, xs_off, ring_off;
   int pdl;
 };
 
@@ -83,7 +83,6 @@ __host__ __device__ constexpr int q4_block_bytes(int R) { return R * 1088; }
 
 #ifdef EG_G4_TRACE  // timeline probe (clock64 per CTA), never in library builds
 __device__ long long g4_trace[512][64];
-__device__ int g4_diag;  // 1: consumers skip the math, 2: skip stage_xg too
 #define G4T(slot)                                                     \
   do {                                                                \
     if (lane == 0 && (slot) < 64) g4_trace[blockIdx.x][(slot)] = clock64(); \
@@ -94,22 +93,24 @@ __device__ int g4_diag;  // 1: consumers skip the math, 2: skip stage_xg too
   } while (0)
 #endif
 
-// CW consumer warps (8 or 16), one producer warp (CW) and one epilogue warp
-// (CW + 1).  A stage holds 16 / R groups x R row sets = 16 (group, row set)
-// items; with CW = 16 each warp takes one item, with CW = 8 two.  At the end
-// of a tile the consumers leave their partial row sums in red[buf] and
-// arrive on tile_full[buf]; the epilogue warp sums them, releases the buffer
-// (tile_free[buf]) and runs the epilogue while the consumers go on.
-template <int R, int MAXU, bool NORM, int CW>
-__global__ void __launch_bounds__(CW * 32 + 64, 1) gemv_q4_kernel(G4Args p) {
-  constexpr int NT = CW * 32;
-  // items of this warp: groups gbase + GSTEP * k (k < NK), row sets r0 .. r0 + RW - 1
-  constexpr int RW = CW == 16 ? 1 : R;
-  constexpr int NK = CW == 16 ? 1 : 16 / (8 * R);
-  constexpr int GSTEP = 8;
+constexpr int kG4Warps = 16;                   // consumer warps per CTA (one CTA per SM)
+constexpr int kG4Threads = kG4Warps * 32 + 64;  // + producer warp + epilogue warp
+
+// One CTA per SM.  Warps 0-15 consume, warp 16 produces, warp 17 runs the
+// epilogues.  The CTA's tiles form a contiguous run of blocks (items) in the
+// stream layout; the producer copies it in stages of p.cap items (one
+// cp.async.bulk each) into a ring.  Consumer warp w takes items w, w + 16,
+// w + 32, ... (so for K = 2048 every warp holds one group of every tile),
+// keeps one running sum per row pair across stages, and at the end of each
+// tile leaves its partial row sums in red[buf] for the epilogue warp.  Every
+// consumer waits on every stage and releases it, items or not, so the ring
+// protocol needs no per-warp bookkeeping.
+template <int R, int MAXU, bool NORM>
+__global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
+  constexpr int CW = kG4Warps, NT = CW * 32;
   extern __shared__ __align__(128) unsigned char g4_smem[];
   __shared__ float sred[32];
-  __shared__ float red[2][CW][R][16];  // double buffered: one barrier per tile
+  __shared__ float red[2][CW][R][16];  // double buffered tile hand-off
   uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
   uint64_t* empty = full + p.stages;
   uint64_t* tile_full = empty + p.stages;  // [2]
@@ -119,10 +120,14 @@ __global__ void __launch_bounds__(CW * 32 + 64, 1) gemv_q4_kernel(G4Args p) {
   int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);  // [gpr][2]
   float* xmul = reinterpret_cast<float*>(xcor + 2 * gpr);     // [gpr][2]
   unsigned char* ring = g4_smem + p.ring_off;
-  const int ngcap = 16 / R;
   const int tiles = (p.N + 15) / 16;
   const int P = gridDim.x, c = blockIdx.x;
   const int t_lo = (int)((long long)tiles * c / P), t_hi = (int)((long long)tiles * (c + 1) / P);
+  const int nitems = (t_hi - t_lo) * gpr;
+  const int cap = p.cap;
+  const int nchunks = (nitems + cap - 1) / cap;
+  const int blk = q4_block_bytes(R);
+  const unsigned char* src0 = p.ws + (size_t)t_lo * gpr * blk;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   if (threadIdx.x == 0) {
@@ -137,42 +142,26 @@ __global__ void __launch_bounds__(CW * 32 + 64, 1) gemv_q4_kernel(G4Args p) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (p.pdl) pdl_launch_dependents();
   if (warp == 0) G4T(0);
 
-  const int blk = q4_block_bytes(R);
   if (warp == CW) {  // --------------------------------------------- producer
-#ifdef EG_G4_TRACE
-    if (g4_diag == 3) return;
-#endif
-    // chunks: tiles t_lo..t_hi-1, groups [g0, g0 + ng) of each; ring slot st
-    // in phase ph (incremental: no divisions in the loop)
-    uint32_t n = 0;
-    int st = 0, ph = 0;
-    bool stop = false;
-    for (int tile = t_lo; tile < t_hi && !stop; tile++)
-      for (int g0 = 0; g0 < gpr; n++) {
-        const int ng = min(ngcap, gpr - g0);
-        if (!mbar_wait(&empty[st], ph ^ 1, p.err)) {
-          stop = true;
-          break;
-        }
-        G4T(24 + (int)n);
-        if (lane == 0) {
-          mbar_expect_tx(&full[st], (uint32_t)(ng * blk));
-          bulk_g2s(ring + (size_t)st * p.stage_bytes, p.ws + ((size_t)tile * gpr + g0) * blk,
-                   (uint32_t)(ng * blk), &full[st]);
-        }
-        __syncwarp();
-        g0 += ng;
-        if (++st == p.stages) {
-          st = 0;
-          ph ^= 1;
-        }
+    int st = 0, ph = 0, n = 0;
+    for (; n < nchunks; n++) {
+      if (!mbar_wait(&empty[st], ph ^ 1, p.err)) break;
+      if (lane == 0) {
+        const uint32_t bytes = (uint32_t)(min(cap, nitems - n * cap) * blk);
+        mbar_expect_tx(&full[st], bytes);
+        bulk_g2s(ring + (size_t)st * p.stage_bytes, src0 + (size_t)n * cap * blk, bytes, &full[st]);
       }
+      __syncwarp();
+      if (++st == p.stages) {
+        st = 0;
+        ph ^= 1;
+      }
+    }
     // every issued copy has landed before the CTA may exit (bounded even
     // after an error elsewhere)
-    for (uint32_t k = n > (uint32_t)p.stages ? n - p.stages : 0; k < n; k++)
+    for (int k = n > p.stages ? n - p.stages : 0; k < n; k++)
       if (!mbar_wait_bounded(&full[k % p.stages], (k / p.stages) & 1)) break;
     return;
   }
@@ -204,135 +193,109 @@ __global__ void __launch_bounds__(CW * 32 + 64, 1) gemv_q4_kernel(G4Args p) {
   }
 
   // ------------------------------------------------------------- consumers
-#ifdef EG_G4_TRACE
-  if (g4_diag != 2)
-#endif
   stage_xd<MAXU, NORM, NT>(p.x, p.K, xb, xcor, xmul, sred, p.pdl);
+  // the next kernel may start once this one's predecessors are complete
+  // (the attention kernel relies on that to read the position early)
+  if (p.pdl) pdl_launch_dependents();
   if (warp == 0) G4T(1);
   const int gq = lane >> 2, t = lane & 3;
   const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
-  const int gbase = CW == 16 && R == 2 ? (warp & 7) : warp;
-  const int r0 = CW == 16 && R == 2 ? (warp >> 3) : 0;
-  float acc[RW][2];
+  float acc[R][2];
 #pragma unroll
-  for (int r = 0; r < RW; r++) acc[r][0] = acc[r][1] = 0.f;
-  uint32_t n = 0;
-  int buf = 0, st = 0, ph = 0;
+  for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
+  // after a failed wait the CTA runs on without waiting and its results are
+  // void; the host sees the error word
   bool dead = false;
-  int tile = t_lo, g0 = 0;
-  for (; tile < t_hi; n++) {
-    const int ng = min(ngcap, gpr - g0);
-    // after a failed wait the CTA runs on without waiting (meeting every
-    // named barrier) and its results are void; the host sees the error word
-#ifdef EG_G4_TRACE
-    if (g4_diag == 3) dead = true;  // probe: no waits, no copies (garbage data)
-#endif
-    if (!dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
-    if (warp == 0) G4T(2 + (int)n);
-    const unsigned char* stage = ring + (size_t)st * p.stage_bytes;
-    // this warp's items of the stage: all shared-memory loads first, then
-    // the MMA chains interleaved, then the scaling
-    uint4 X0[NK], X1[NK], A[NK][RW], B[NK][RW];
-    bool ok[NK];
-#pragma unroll
-    for (int k = 0; k < NK; k++) {
-      const int gi = gbase + GSTEP * k;
-      ok[k] = gi < ng;
-#ifdef EG_G4_TRACE
-      if (g4_diag == 1 || g4_diag == 2) ok[k] = false;
-#endif
-      const int gl = ok[k] ? gi : 0;
+  int st = 0, ph = 0, chunk = 0, chunk_lo = 0;
+  if (nchunks > 0 && !mbar_wait(&full[0], 0, p.err)) dead = true;
+  const unsigned char* stage = ring;
+  int i = warp;  // item index within the CTA's run
+  for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
+    const int tile_end = (j + 1) * gpr;
+    for (; i < tile_end; i += 16) {
+      while (i >= chunk_lo + cap) {  // next stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (++st == p.stages) {
+          st = 0;
+          ph ^= 1;
+        }
+        chunk++;
+        chunk_lo += cap;
+        stage = ring + (size_t)st * p.stage_bytes;
+        if (!dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
+        if (warp == 0) G4T(2 + chunk);
+      }
+      const int g = i - j * gpr;
+      const unsigned char* bp = stage + (size_t)(i - chunk_lo) * blk;
       // B: digit plane gq of this group's 4 k32 blocks (zero for gq >= 4)
-      X0[k] = X1[k] = make_uint4(0, 0, 0, 0);
+      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
       if (bl) {
-        const uint4* xp = reinterpret_cast<const uint4*>(xb + (((g0 + gl) * 4 + gq) * 4 + t) * 4);
-        X0[k] = xp[0];
-        X1[k] = xp[1];
+        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 4);
+        X0 = xp[0];
+        X1 = xp[1];
       }
-      const unsigned char* bp = stage + gl * blk;
+      uint4 A[R], B[R];
 #pragma unroll
-      for (int r = 0; r < RW; r++) {
+      for (int r = 0; r < R; r++) {
         // words t, 4+t, 8+t, 12+t of rows gq (A) and gq+8 (B)
-        A[k][r] = *reinterpret_cast<const uint4*>(bp + (r0 + r) * 1024 + lane * 16);
-        B[k][r] = *reinterpret_cast<const uint4*>(bp + (r0 + r) * 1024 + 512 + lane * 16);
+        A[r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + lane * 16);
+        B[r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + 512 + lane * 16);
       }
-    }
-    int c[NK][RW][4];
+      int cc[R][4];
 #pragma unroll
-    for (int k = 0; k < NK; k++)
+      for (int r = 0; r < R; r++) {
+        cc[r][0] = cc[r][1] = cc[r][2] = cc[r][3] = 0;
+        imma16832(cc[r], nib_lo_u8(A[r].x), nib_lo_u8(B[r].x), nib_hi_u8(A[r].x), nib_hi_u8(B[r].x), X0.x, X0.y);
+        imma16832(cc[r], nib_lo_u8(A[r].y), nib_lo_u8(B[r].y), nib_hi_u8(A[r].y), nib_hi_u8(B[r].y), X0.z, X0.w);
+        imma16832(cc[r], nib_lo_u8(A[r].z), nib_lo_u8(B[r].z), nib_hi_u8(A[r].z), nib_hi_u8(B[r].z), X1.x, X1.y);
+        imma16832(cc[r], nib_lo_u8(A[r].w), nib_lo_u8(B[r].w), nib_hi_u8(A[r].w), nib_hi_u8(B[r].w), X1.z, X1.w);
+      }
+      if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
+        const int cor = xcor[2 * g + t];
+        const float mul = xmul[2 * g + t];
+        const float* sc = reinterpret_cast<const float*>(bp + R * 1024);
 #pragma unroll
-      for (int r = 0; r < RW; r++) c[k][r][0] = c[k][r][1] = c[k][r][2] = c[k][r][3] = 0;
-#pragma unroll
-    for (int m = 0; m < 4; m++)
-#pragma unroll
-      for (int k = 0; k < NK; k++)
-#pragma unroll
-        for (int r = 0; r < RW; r++) {
-          const uint32_t wa = m == 0 ? A[k][r].x : m == 1 ? A[k][r].y : m == 2 ? A[k][r].z : A[k][r].w;
-          const uint32_t wb = m == 0 ? B[k][r].x : m == 1 ? B[k][r].y : m == 2 ? B[k][r].z : B[k][r].w;
-          const uint32_t b0 = m == 0 ? X0[k].x : m == 1 ? X0[k].z : m == 2 ? X1[k].x : X1[k].z;
-          const uint32_t b1 = m == 0 ? X0[k].y : m == 1 ? X0[k].w : m == 2 ? X1[k].y : X1[k].w;
-          imma16832(c[k][r], nib_lo_u8(wa), nib_lo_u8(wb), nib_hi_u8(wa), nib_hi_u8(wb), b0, b1);
-        }
-    if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
-#pragma unroll
-      for (int k = 0; k < NK; k++) {
-        if (!ok[k]) continue;
-        const int gi = gbase + GSTEP * k, G = g0 + gi;
-        const int cor = xcor[2 * G + t];
-        const float mul = xmul[2 * G + t];
-        const float* sc = reinterpret_cast<const float*>(stage + gi * blk + R * 1024);
-#pragma unroll
-        for (int r = 0; r < RW; r++) {
-          const float sa = sc[16 * (r0 + r) + gq] * mul, sb = sc[16 * (r0 + r) + gq + 8] * mul;
-          acc[r][0] = fmaf(sa, (float)(c[k][r][0] + 256 * c[k][r][1] - cor), acc[r][0]);
-          acc[r][1] = fmaf(sb, (float)(c[k][r][2] + 256 * c[k][r][3] - cor), acc[r][1]);
+        for (int r = 0; r < R; r++) {
+          const float sa = sc[16 * r + gq] * mul, sb = sc[16 * r + gq + 8] * mul;
+          acc[r][0] = fmaf(sa, (float)(cc[r][0] + 256 * cc[r][1] - cor), acc[r][0]);
+          acc[r][1] = fmaf(sb, (float)(cc[r][2] + 256 * cc[r][3] - cor), acc[r][1]);
         }
       }
     }
+    // ---- tile complete for this warp: hand its partial rows to the epilogue
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], 1);
+      acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], 1);
+    }
+    const int b = j & 1;
+    if (!dead && !mbar_wait(&tile_free[b], ((j >> 1) & 1) ^ 1, p.err)) dead = true;
+    if (t == 0) {
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        red[b][warp][r][gq] = acc[r][0];
+        red[b][warp][r][gq + 8] = acc[r][1];
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
     __syncwarp();
-    if (warp == 0) G4T(36 + (int)min(n, 11u));
+    if (lane == 0) mbar_arrive(&tile_full[b]);
+    if (warp == 0) G4T(48 + min(j, 13));
+  }
+  // release the current stage and wait/release any later ones this warp had
+  // no items in, so every stage sees all CW arrivals
+  for (; chunk < nchunks; chunk++) {
+    __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (++st == p.stages) {
       st = 0;
       ph ^= 1;
     }
-    g0 += ng;
-    if (g0 < gpr) continue;
-    // ---- tile complete: reduce over the lanes t = 0, 1; hand the warp's
-    // partial rows to the epilogue warp
-#pragma unroll
-    for (int r = 0; r < RW; r++) {
-      acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], 1);
-      acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], 1);
-    }
-    const int j = tile - t_lo;
-    if (!dead && !mbar_wait(&tile_free[buf], ((j >> 1) & 1) ^ 1, p.err)) dead = true;
-    if (t == 0) {
-#pragma unroll
-      for (int r = 0; r < R; r++) {  // row sets this warp does not hold: 0
-        const bool mine = r >= r0 && r < r0 + RW;
-        red[buf][warp][r][gq] = mine ? acc[mine ? r - r0 : 0][0] : 0.f;
-        red[buf][warp][r][gq + 8] = mine ? acc[mine ? r - r0 : 0][1] : 0.f;
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < RW; r++) acc[r][0] = acc[r][1] = 0.f;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&tile_full[buf]);
-    if (warp == 0) G4T(48 + (int)min(n, 14u));
-    buf ^= 1;
-    g0 = 0;
-    tile++;
+    if (chunk + 1 < nchunks && !dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
   }
   if (warp == 0) G4T(63);
-#ifdef EG_G4_TRACE
-  if (threadIdx.x == 0) {
-    unsigned sm;
-    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
-    g4_trace[blockIdx.x][62] = sm;
-  }
-#endif
 }
 
 // Units of 8 activations per thread (256 threads) a register-staged
@@ -343,19 +306,20 @@ static int maxu_for(int K) {
 }
 
 // Shared-memory plan of one launch (bytes): barriers, x fragments + group
-// multipliers, then the ring.
+// multipliers, then the ring of stages of `cap` items.
 struct G4Plan {
-  int stages, stage_bytes, xs_off, ring_off, smem;
+  int stages, stage_bytes, cap, xs_off, ring_off, smem;
 };
 static G4Plan g4_plan(int R, int K) {
   G4Plan q;
   const int gpr = K / kGroup;
-  q.stage_bytes = (16 / R) * q4_block_bytes(R);  // 17 KB
+  q.cap = (getenv("EG_G4_CAP") ? atoi(getenv("EG_G4_CAP")) : 32) / R;  // items per stage: 35 KB
+  q.stage_bytes = q.cap * q4_block_bytes(R);
   q.xs_off = 256;  // barriers: 2 * stages + 4 mbarriers (stages <= 8)
   const int xbytes = gpr * (512 + 16);
   q.ring_off = (q.xs_off + xbytes + 127) & ~127;
-  // one CTA per SM
-  const int budget = getenv("EG_G4_SMEM") ? atoi(getenv("EG_G4_SMEM")) * 1024 : 200 * 1024;
+  // leave room for the attention kernel's CTA (67 KB) beside this one under PDL
+  const int budget = (getenv("EG_G4_SMEM") ? atoi(getenv("EG_G4_SMEM")) : 150) * 1024;
   q.stages = std::max(2, std::min(8, (budget - q.ring_off) / q.stage_bytes));
   q.smem = q.ring_off + q.stages * q.stage_bytes;
   return q;
@@ -363,20 +327,19 @@ static G4Plan g4_plan(int R, int K) {
 
 int gemv_q4_ctas() { return sm_count(); }
 
-constexpr int kG4Warps = 16;  // consumer warps per CTA (one CTA per SM)
-
 template <int R, int MAXU, bool NORM>
 static void gemv_q4_go(const G4Args& a0, const G4Plan& q, cudaStream_t st, bool pdl) {
   G4Args a = a0;
   a.stages = q.stages;
   a.stage_bytes = q.stage_bytes;
+  a.cap = q.cap;
   a.xs_off = q.xs_off;
   a.ring_off = q.ring_off;
   a.pdl = pdl ? 1 : 0;
   const int P = std::min(gemv_q4_ctas(), (a.N + 15) / 16);
-  auto k = gemv_q4_kernel<R, MAXU, NORM, kG4Warps>;
+  auto k = gemv_q4_kernel<R, MAXU, NORM>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q.smem);
-  launch(k, dim3(P), dim3(kG4Warps * 32 + 64), (size_t)q.smem, st, pdl, a);
+  launch(k, dim3(P), dim3(kG4Threads), (size_t)q.smem, st, pdl, a);
 }
 
 template <int R>
