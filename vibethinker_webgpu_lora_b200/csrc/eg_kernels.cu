@@ -627,22 +627,260 @@ void lora_a(const XSrc& x, int K, const LoraMod* mods, int nmods, int max_rank, 
 // ======================================================================
 int attn_max_splits(int max_ctx) { return std::max(64, (max_ctx + 15) / 16); }
 
+// ----------------------------------------------------------------------
+// Decode attention, one CTA per (query head, split of <= kAttnKeys keys).
+// Each of the 16 warps takes keys t0 + w, t0 + w + 16, ...; a lane holds 4
+// of the 128 dims.  All K and V rows of the warp are requested before
+// griddepcontrol.wait (the cache rows t != pos were written by earlier
+// steps), so the kernel pays one memory latency for them.  Each warp forms a
+// partial (m, z, sum e^(s-m) v) over its keys (ATTN_PARTIAL, kernels.js:
+// 258-345), the 16 warp partials are merged in shared memory with the
+// ATTN_COMBINE formula (kernels.js:346-388, f16 rounding of the partial
+// outputs in the f16 variant), and for contexts longer than one split the
+// CTA partials are merged once more by the last CTA of the head.  The new
+// k (RoPE) / v row of position pos is formed in registers; the first query
+// head of each KV group appends it to the cache (runtime.js:1509-1514).
+constexpr int kAttnWarps = 16;
+constexpr int kAttnKeys = 256;                   // keys per split (16 per warp)
+constexpr int kAttnKpw = kAttnKeys / kAttnWarps;
+
+// A value as the cache stores it (rounded to the cache type).
 template <typename KVT>
-__global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a, int pdl) {
-  extern __shared__ __align__(16) float attn_smem[];
-  attn_item<KVT>(a, blockIdx.x, blockIdx.y, attn_smem, pdl);
+__device__ __forceinline__ float kv_round(float v);
+template <>
+__device__ __forceinline__ float kv_round<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float kv_round<__half>(float v) { return round_h(v); }
+
+template <typename KVT>
+struct KvRow;  // 4 consecutive cache values of one lane
+template <>
+struct KvRow<__half> {
+  uint2 u;
+  __device__ __forceinline__ void load(const __half* p) { u = __ldcg(reinterpret_cast<const uint2*>(p)); }
+  __device__ __forceinline__ float4 get() const {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  __device__ __forceinline__ void set(float4 v) {  // values already f16-exact
+    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+  }
+};
+template <>
+struct KvRow<float> {
+  float4 f;
+  __device__ __forceinline__ void load(const float* p) { f = __ldcg(reinterpret_cast<const float4*>(p)); }
+  __device__ __forceinline__ float4 get() const { return f; }
+  __device__ __forceinline__ void set(float4 v) { f = v; }
+};
+
+template <typename KVT>
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_head_kernel(AttnArgs a, int pdl) {
+  __shared__ float wm[kAttnWarps], wz[kAttnWarps];
+  __shared__ __align__(16) float wo[kAttnWarps][kHeadDim];
+  __shared__ bool last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, split = blockIdx.x;
+  const int G = a.nh / a.nkv, kvh = h / G, hd = kHeadDim, half = hd / 2;
+  const int kvd = a.nkv * hd;
+  const int f16 = a.kv_f16;
+  // The position and the cached rows t != pos were written before the
+  // producing GEMV started (it triggers this launch only after its own
+  // griddepcontrol.wait).
+  const int pos = a.pos ? __ldcg(a.pos) : a.fixed_pos;
+  const int ctx = pos + 1;
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  const int nsplit = (ctx + keys - 1) / keys;
+  if (split >= nsplit) return;
+  const int t0 = split * keys, t1 = min(t0 + keys, ctx);
+  const KVT* kc = reinterpret_cast<const KVT*>(a.kc) + kvh * hd + 4 * lane;
+  const KVT* vc = reinterpret_cast<const KVT*>(a.vc) + kvh * hd + 4 * lane;
+  KvRow<KVT> K[kAttnKpw], V[kAttnKpw];
+#pragma unroll
+  for (int i = 0; i < kAttnKpw; i++) {
+    const int t = t0 + warp + kAttnWarps * i;
+    if (t < t1 && t != pos) {
+      K[i].load(kc + (size_t)t * kvd);
+      V[i].load(vc + (size_t)t * kvd);
+    }
+  }
+  if (pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+  // q (ROPE_QK, f16 round in the f16 variant): lane holds dims 4l..4l+3; the
+  // RoPE partner of dim j < 64 is j + 64, held by lane l ^ 16
+  const float* cs = a.cosT + (size_t)pos * hd;
+  const float* sn = a.sinT + (size_t)pos * hd;
+  auto rope4 = [&](float4 x) {
+    float4 o = x;
+    float* e = reinterpret_cast<float*>(&o);
+    const float* xi = reinterpret_cast<const float*>(&x);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const float other = __shfl_xor_sync(0xffffffffu, xi[c], 16);
+      const int d = 4 * lane + c, j = d & (half - 1);
+      float lo = lane < 16 ? xi[c] : other, hi = lane < 16 ? other : xi[c];
+      rope_pair(lo, hi, cs[j], sn[j], f16);
+      if (f16) round_h2(lo, hi);
+      e[c] = lane < 16 ? lo : hi;
+    }
+    return o;
+  };
+  const float4 q4 = rope4(__ldcg(reinterpret_cast<const float4*>(a.qkv + h * hd + 4 * lane)));
+  if (pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v (f16-rounded in the f16 cache)
+    const float* kn = a.qkv + a.nh * hd + kvh * hd;
+    const float* vn = a.qkv + a.nh * hd + kvd + kvh * hd;
+    float4 kr = __ldcg(reinterpret_cast<const float4*>(kn + 4 * lane));
+    float4 vr = __ldcg(reinterpret_cast<const float4*>(vn + 4 * lane));
+    // the cache keeps RoPE(k) rounded once to its type; scores use that value
+    float4 kx;
+    {
+      float* e = reinterpret_cast<float*>(&kx);
+      const float* xi = reinterpret_cast<const float*>(&kr);
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const float other = __shfl_xor_sync(0xffffffffu, xi[c], 16);
+        const int d = 4 * lane + c, j = d & (half - 1);
+        float lo = lane < 16 ? xi[c] : other, hi = lane < 16 ? other : xi[c];
+        rope_pair(lo, hi, cs[j], sn[j], f16);
+        e[c] = lane < 16 ? lo : hi;
+      }
+    }
+    KvRow<KVT> kn4, vn4;
+    kn4.set(make_float4(kv_round<KVT>(kx.x), kv_round<KVT>(kx.y), kv_round<KVT>(kx.z), kv_round<KVT>(kx.w)));
+    vn4.set(make_float4(kv_round<KVT>(vr.x), kv_round<KVT>(vr.y), kv_round<KVT>(vr.z), kv_round<KVT>(vr.w)));
+    const int i = (pos - t0) / kAttnWarps, w = (pos - t0) % kAttnWarps;
+    if (warp == w) {
+#pragma unroll
+      for (int ii = 0; ii < kAttnKpw; ii++)
+        if (ii == i) {
+          K[ii] = kn4;
+          V[ii] = vn4;
+        }
+    }
+    if (h % G == 0 && warp == 0) {  // one query head per KV group appends
+      KVT* kw = reinterpret_cast<KVT*>(a.kc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
+      KVT* vw = reinterpret_cast<KVT*>(a.vc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
+      kw[0] = kv_cvt<KVT>(kx.x); kw[1] = kv_cvt<KVT>(kx.y); kw[2] = kv_cvt<KVT>(kx.z); kw[3] = kv_cvt<KVT>(kx.w);
+      vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
+    }
+  }
+  // scores of this warp's keys: key i's score ends up in lane i
+  const float scale = 1.0f / sqrtf((float)hd);
+  float s_mine = -1e30f;
+  float m = -1e30f;
+#pragma unroll
+  for (int i = 0; i < kAttnKpw; i++) {
+    const int t = t0 + warp + kAttnWarps * i;
+    if (t >= t1) break;
+    const float4 k4 = K[i].get();
+    float p = __fmul_rn(q4.x, k4.x);
+    p = __fadd_rn(p, __fmul_rn(q4.y, k4.y));
+    p = __fadd_rn(p, __fmul_rn(q4.z, k4.z));
+    p = __fadd_rn(p, __fmul_rn(q4.w, k4.w));
+    const float sv = __fmul_rn(warp_sum(p), scale);
+    if (lane == i) s_mine = sv;
+    m = fmaxf(m, sv);
+  }
+  const int nk = t1 - t0 > warp ? (t1 - t0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
+  const float ev_mine = lane < nk ? expf(s_mine - m) : 0.f;
+  const float z = warp_sum(ev_mine);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kAttnKpw; i++) {
+    if (i >= nk) break;
+    const float ev = __shfl_sync(0xffffffffu, ev_mine, i);
+    const float4 v4 = V[i].get();
+    acc.x = __fadd_rn(acc.x, __fmul_rn(ev, v4.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(ev, v4.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(ev, v4.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(ev, v4.w));
+  }
+  if (f16) {  // ATTN_COMBINE_F16 reads the partial outputs through f16
+    round_h2(acc.x, acc.y);
+    round_h2(acc.z, acc.w);
+  }
+  if (lane == 0) {
+    wm[warp] = nk ? m : -1e30f;
+    wz[warp] = z;
+  }
+  *reinterpret_cast<float4*>(&wo[warp][4 * lane]) = acc;
+  __syncthreads();
+  // ---- merge the warp partials: warp 0, lane l holds dims 4l..4l+3
+  if (warp == 0) {
+    float M = -1e30f;
+    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wm[w]);
+    float Z = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int w = 0; w < kAttnWarps; w++) {
+      if (wz[w] == 0.f) continue;
+      const float wgt = expf(wm[w] - M);
+      Z = __fadd_rn(Z, __fmul_rn(wz[w], wgt));
+      const float4 p = *reinterpret_cast<const float4*>(&wo[w][4 * lane]);
+      o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
+      o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
+      o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
+      o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
+    }
+    if (nsplit == 1) {
+      const float invZ = 1.0f / Z;
+      *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
+          make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ), __fmul_rn(o.w, invZ));
+    } else {
+      if (f16) {
+        round_h2(o.x, o.y);
+        round_h2(o.z, o.w);
+      }
+      *reinterpret_cast<float4*>(a.po + ((size_t)h * a.max_splits + split) * hd + 4 * lane) = o;
+      if (lane == 0) {
+        a.pm[h * a.max_splits + split] = M;
+        a.pz[h * a.max_splits + split] = Z;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+  // ---- several splits: the last CTA of the head merges them
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(a.counters + h, 1u) == (unsigned)nsplit - 1;
+  __syncthreads();
+  if (!last || warp != 0) return;
+  __threadfence();
+  const float* pm = a.pm + h * a.max_splits;
+  const float* pz = a.pz + h * a.max_splits;
+  float M = -1e30f;
+  for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(pm + s2));
+  float Z = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s2 = 0; s2 < nsplit; s2++) {
+    const float wgt = expf(__ldcg(pm + s2) - M);
+    Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), wgt));
+    const float4 p = __ldcg(reinterpret_cast<const float4*>(a.po + ((size_t)h * a.max_splits + s2) * hd + 4 * lane));
+    o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
+    o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
+    o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
+    o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
+  }
+  const float invZ = 1.0f / Z;
+  *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
+      make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ), __fmul_rn(o.w, invZ));
+  if (lane == 0) a.counters[h] = 0u;  // ready for the next launch
 }
 
+
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  dim3 grid(a.max_splits, a.nkv);
-  const int smem = kAttnMaxChunk * (kKsStride + kHeadDim) * (int)sizeof(float);
-  if (a.kv_f16) {
-    cudaFuncSetAttribute(attn_partial_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    launch(attn_partial_kernel<__half>, grid, dim3(256), smem, st, pdl, a, (int)pdl);
-  } else {
-    cudaFuncSetAttribute(attn_partial_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    launch(attn_partial_kernel<float>, grid, dim3(256), smem, st, pdl, a, (int)pdl);
-  }
+  // splits of kAttnKeys keys (a fixed chunk, when given, for tests of the
+  // multi-split merge); the partial slots (max_splits per head) cover them
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  dim3 grid(std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys), a.nh);
+  if (a.kv_f16)
+    launch(attn_head_kernel<__half>, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, (int)pdl);
+  else
+    launch(attn_head_kernel<float>, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, (int)pdl);
 }
 
 // ======================================================================

@@ -98,6 +98,7 @@ struct AttnArgs {
   const int* pos;    // device: current position (ctx = pos + 1)
   int fixed_pos;     // used when pos == null
   int nh, nkv, max_splits;
+  int ctx_bound;     // upper bound of pos + 1 for this launch (sizes the grid)
   int kv_f16;        // 1: f16 cache + ATTN_*_F16 / ROPE_QK_F16 numerics
   int chunk;         // 0: adaptive; >0 fixed keys per split
   float *pm, *pz, *po;  // partials [nh][max_splits], po [nh][max_splits][128]

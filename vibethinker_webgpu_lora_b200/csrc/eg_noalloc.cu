@@ -19,7 +19,7 @@
 namespace {
 
 // Scratch capacity: 4096 (head, split) slots of 130 floats (split max, split
-// sum, 128-wide partial output) plus 64 per-KV-head arrival counters:
+// sum, 128-wide partial output) plus 64 per-head arrival counters:
 // 2,130,176 bytes, held by every GPU that loads the library until exit.
 constexpr int kSlots = 4096;
 constexpr size_t kPartialBytes = (size_t)kSlots * (128 + 2) * sizeof(float);
@@ -57,7 +57,7 @@ extern "C" {
 
 // Same inputs, outputs and results as eg_op_attn_decode; scratch comes from
 // the static array above.  Limits: nh * ceil((pos+1) / max(chunk, 16)) must
-// not exceed 4096 (the adaptive chunk is never below 16 keys), nkv <= 64.
+// not exceed 4096 (the adaptive chunk is never below 16 keys), nh <= 64.
 // Every call shares the one array: calls that overlap on the GPU (concurrent
 // streams, or several host threads on one device) race on it.  The first
 // call on a device resolves the array's device address; make that first call
@@ -68,7 +68,7 @@ EG_API eg_status eg_op_attn_decode_noalloc(const float* qkv, void* k_cache, void
                                            float* out, void* stream) {
   if (!qkv || !k_cache || !v_cache || !cos_t || !sin_t || !out)
     return eg::fail(EG_ERR_ARG, "attn_decode_noalloc: null argument");
-  if (nh <= 0 || nkv <= 0 || nkv > 64 || nh % nkv || nh / nkv > 8 || pos < 0 || pos >= max_ctx)
+  if (nh <= 0 || nh > 64 || nkv <= 0 || nh % nkv || nh / nkv > 8 || pos < 0 || pos >= max_ctx)
     return eg::fail(EG_ERR_ARG, "attn_decode_noalloc: bad heads/pos");
   if (chunk < 0 || chunk > 64 || chunk % 16)
     return eg::fail(EG_ERR_ARG, "attn_decode_noalloc: chunk must be 0 or 16/32/48/64");
@@ -87,7 +87,7 @@ EG_API eg_status eg_op_attn_decode_noalloc(const float* qkv, void* k_cache, void
   float* f = reinterpret_cast<float*>(base);
   unsigned* counters = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(base) + kPartialBytes);
   // the arrival counters must start at zero; the array keeps the last call's contents
-  cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)nkv * sizeof(unsigned), st);
+  cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)nh * sizeof(unsigned), st);
   if (e != cudaSuccess) return eg::fail(EG_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   eg::AttnArgs a = {};
   a.qkv = qkv;
@@ -100,6 +100,7 @@ EG_API eg_status eg_op_attn_decode_noalloc(const float* qkv, void* k_cache, void
   a.nh = nh;
   a.nkv = nkv;
   a.max_splits = splits;
+  a.ctx_bound = ctx;
   a.kv_f16 = kv_f16;
   a.chunk = chunk;
   a.pm = f;

@@ -426,6 +426,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     a.nh = c.num_heads;
     a.nkv = c.num_kv_heads;
     a.max_splits = rt->max_splits;
+    a.ctx_bound = rt->o.max_ctx;
     a.kv_f16 = rt->o.kv_f16;
     a.chunk = rt->o.attn_chunk;
     a.pm = rt->pm;
@@ -731,9 +732,10 @@ EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** 
   if (!c.tie_word_embeddings)
     return fail(EG_ERR_ARG, "QwenWGPU currently requires tied input/output embeddings");
   if (c.head_dim != 128) return fail(EG_ERR_ARG, "head_dim must be 128");
-  if (c.num_heads <= 0 || c.num_kv_heads <= 0 || c.num_heads % c.num_kv_heads ||
-      c.num_heads / c.num_kv_heads > 8)
-    return fail(EG_ERR_ARG, "num_heads must be a multiple of num_kv_heads (group <= 8)");
+  if (c.num_heads <= 0 || c.num_heads > 64 || c.num_kv_heads <= 0 ||
+      c.num_heads % c.num_kv_heads || c.num_heads / c.num_kv_heads > 8)
+    return fail(EG_ERR_ARG,
+                "num_heads must be a multiple of num_kv_heads (group <= 8), at most 64 heads");
   if (c.hidden_size % 128 || c.intermediate_size % 128 || (c.num_heads * c.head_dim) % 128 ||
       c.hidden_size > 12288 || c.intermediate_size > 12288)
     return fail(EG_ERR_ARG, "hidden/intermediate sizes must be multiples of 128, at most 12288");
@@ -1415,7 +1417,7 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
                                    const float* sin_t, int nh, int nkv, int pos, int max_ctx, int kv_f16,
                                    int chunk, float* out, void* stream) {
   if (!qkv || !k_cache || !v_cache || !cos_t || !sin_t || !out) return fail(EG_ERR_ARG, "attn_decode: null argument");
-  if (nh <= 0 || nkv <= 0 || nh % nkv || nh / nkv > 8 || pos < 0 || pos >= max_ctx)
+  if (nh <= 0 || nh > 64 || nkv <= 0 || nh % nkv || nh / nkv > 8 || pos < 0 || pos >= max_ctx)
     return fail(EG_ERR_ARG, "attn_decode: bad heads/pos");
   if (chunk < 0 || chunk > 64 || chunk % 16) return fail(EG_ERR_ARG, "attn_decode: chunk must be 0 or 16/32/48/64");
   const int ms = attn_max_splits(max_ctx);
@@ -1424,7 +1426,7 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
   eg_status s = op_scratch(part + 64 * 4, &scr);
   if (s) return s;
   unsigned* counters = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(scr) + part);
-  CK(cudaMemsetAsync(counters, 0, nkv * 4, OPSTREAM));
+  CK(cudaMemsetAsync(counters, 0, nh * 4, OPSTREAM));
   AttnArgs a = {};
   a.qkv = qkv;
   a.kc = k_cache;
@@ -1436,6 +1438,7 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
   a.nh = nh;
   a.nkv = nkv;
   a.max_splits = ms;
+  a.ctx_bound = pos + 1;
   a.kv_f16 = kv_f16;
   a.chunk = chunk;
   a.pm = reinterpret_cast<float*>(scr);
