@@ -236,14 +236,16 @@ def run_ours(args, ws, rank, local):
         "data": "synthetic",
         "config": {"workload": f"configs[{2 if long else 1}]: Qwen2.5-3B-shape int4 greedy decode, "
                                f"batch 1, prompt {n_prompt}, decode ctx {n_prompt}..{n_prompt + period}",
-                   "kv": "f16", "scales": "f32 (reference layout)", "lm_head": "int8 rows",
+                   "kv": "f16", "scales": "f32 (stream layout: 16x128 blocks, interleaved f32 scales)", "lm_head": "int8 rows",
                    "l2": "inputs larger than L2 (1.79 GB of weights streamed per step)",
                    "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "kernel": "gate_up+SiLU int4 GEMV (22016x2048)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                      "bytes_per_launch": GATE_UP_BYTES, "launch_us": round(gu_us, 3),
-                     "traffic": None},
+                     # dram__bytes_read + dram__bytes_write of one gate_up launch, ncu
+                     # --set full of `python bench.py --ncu-probe 4` (same kernel and shape)
+                     "traffic": 24012544, "traffic_source": "ncu, bench.py --ncu-probe 4"},
         "step_roofline": {"bytes_per_step": int(step_bytes),
                           "achieved_gbs": round(step_bytes * value / ws / 1e9, 1),
                           "frac": round(step_bytes * value / ws / 1e9 / hbm, 4),

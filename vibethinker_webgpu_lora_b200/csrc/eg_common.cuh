@@ -71,6 +71,16 @@ EG_DEV void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A(16x32 s8, row) * B(32x8 s8, col) + C, s32 accumulate (exact).
+EG_DEV void imma16832_ss(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Nibbles 0,2,4,6 (lo) or 1,3,5,7 (hi) of a packed int4 word as four bytes
 // q + 8 in [0, 15] (offset binary), one LOP3 (+ one shift).
 EG_DEV uint32_t nib_lo_u8(uint32_t w) {

@@ -1,7 +1,9 @@
 // eg_device.cuh -- device building blocks shared by the per-op kernels
 // (eg_kernels.cu) and the persistent fused decode kernel (eg_fused.cu):
-// block reductions, the activation prologue that builds MMA B fragments,
-// GEMV epilogues, weight batch loaders, and one attention work item.
+// mbarrier / bulk-copy helpers, block reductions, the activation prologues
+// that build MMA B fragments (f16 hi/lo split for the fused kernel, digit
+// planes for the integer-MMA GEMVs), GEMV epilogues and one attention work
+// item of the fused kernel.
 #pragma once
 #include <float.h>
 #include <math.h>
@@ -325,118 +327,6 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred, i
   return e;
 }
 
-// Prologue of the streaming int4 GEMV: the same loads and RMSNorm as
-// stage_x (fmt 4 layout), but the f16 range shift is chosen per 128-wide
-// group -- xsc[G] = 2^e_G, 1 unless some |x| in the group exceeds 16384 --
-// from a 16-lane shuffle, so a plain input needs no block-wide reduction.
-// pdl: the norm weights are read first, then griddepcontrol.wait, then the
-// input (which the previous kernel writes).
-template <int MAXU, bool NORM>
-__device__ void stage_xg(const XSrc& s, int K, uint4* xs, float* xsc, float* sred, int pdl) {
-  const int K8 = K / 8;
-  float v[MAXU][8];
-  float gw[NORM ? MAXU : 1][8];
-  if (NORM && s.mode != X_PLAIN) {
-#pragma unroll
-    for (int i = 0; i < MAXU; i++) {
-      const int u = threadIdx.x + i * kCtaThreads;
-      const bool ok = u < K8;
-      const float4 a = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u)) : make_float4(0, 0, 0, 0);
-      const float4 b = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u + 4)) : make_float4(0, 0, 0, 0);
-      gw[NORM ? i : 0][0] = a.x; gw[NORM ? i : 0][1] = a.y; gw[NORM ? i : 0][2] = a.z; gw[NORM ? i : 0][3] = a.w;
-      gw[NORM ? i : 0][4] = b.x; gw[NORM ? i : 0][5] = b.y; gw[NORM ? i : 0][6] = b.z; gw[NORM ? i : 0][7] = b.w;
-    }
-  }
-  if (pdl) pdl_wait();
-  const int8_t* erow = nullptr;
-  float escale = 0.f;
-  if (NORM && s.mode == X_EMBED_RMS) {
-    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
-    erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
-    escale = s.emb_s[id];
-  }
-#pragma unroll
-  for (int i = 0; i < MAXU; i++) {
-    const int u = threadIdx.x + i * kCtaThreads;
-    const bool ok = u < K8;
-    if (NORM && s.mode == X_EMBED_RMS) {
-      const uint2 b = ok ? *reinterpret_cast<const uint2*>(erow + 8 * u) : make_uint2(0, 0);
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const int8_t q = (int8_t)(((j < 4 ? b.x : b.y) >> (8 * (j & 3))) & 0xFF);
-        v[i][j] = __fmul_rn((float)q, escale);  // EMBED_BUF: f32(q8) * scale[id]
-      }
-    } else {
-      const float4 a = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u)) : make_float4(0, 0, 0, 0);
-      const float4 b = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u + 4)) : make_float4(0, 0, 0, 0);
-      v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
-      v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
-    }
-  }
-  if (NORM && s.mode == X_EMBED_RMS && blockIdx.x == 0 && s.hidden_out) {
-#pragma unroll
-    for (int i = 0; i < MAXU; i++) {
-      const int u = threadIdx.x + i * kCtaThreads;
-      if (u < K8) {
-        *reinterpret_cast<float4*>(s.hidden_out + 8 * u) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
-        *reinterpret_cast<float4*>(s.hidden_out + 8 * u + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
-      }
-    }
-  }
-  if (NORM && s.mode != X_PLAIN) {
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < MAXU; i++)
-#pragma unroll
-      for (int j = 0; j < 8; j++) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
-    ss = block_sum(ss, sred);
-    // RMSNORM: inverseSqrt(sum/K + eps) (kernels.js:142), IEEE sqrt + divide
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
-    const __half inv16 = __float2half_rn(inv);
-#pragma unroll
-    for (int i = 0; i < MAXU; i++)
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        if (!s.f16) {
-          v[i][j] = __fmul_rn(__fmul_rn(v[i][j], inv), gw[NORM ? i : 0][j]);
-          v[i][j + 1] = __fmul_rn(__fmul_rn(v[i][j + 1], inv), gw[NORM ? i : 0][j + 1]);
-        } else {  // RMSNORM_F16: f16(f16(x) * inv) * f16(g), two lanes at a time
-          __half2 t = __hmul2_rn(__floats2half2_rn(v[i][j], v[i][j + 1]), __half2half2(inv16));
-          t = __hmul2_rn(t, __floats2half2_rn(gw[NORM ? i : 0][j], gw[NORM ? i : 0][j + 1]));
-          const float2 r = __half22float2(t);
-          v[i][j] = r.x;
-          v[i][j + 1] = r.y;
-        }
-      }
-  }
-  uint4* lo = xs + K8 + 4;
-#pragma unroll
-  for (int i = 0; i < MAXU; i++) {
-    const int u = threadIdx.x + i * kCtaThreads;
-    float am = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
-    // the 16 units of a group sit in 16 consecutive lanes (K8 % 16 == 0)
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const int e = shift_for(am);
-    if (u >= K8) continue;
-    float x[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) x[j] = e ? ldexpf(v[i][j], -e) : v[i][j];
-    uint4 h, l;
-    split_h2(x[0], x[4], h.x, l.x);
-    split_h2(x[1] * 0.0625f, x[5] * 0.0625f, h.y, l.y);
-    split_h2(x[2], x[6], h.z, l.z);
-    split_h2(x[3] * 0.0625f, x[7] * 0.0625f, h.w, l.w);
-    const int slot = (u & ~15) + 4 * (u & 3) + ((u >> 2) & 3);
-    xs[slot] = h;
-    lo[slot] = l;
-    if ((u & 15) == 0) xsc[u >> 4] = e ? ldexpf(1.f, e) : 1.f;
-  }
-  cta_sync();
-}
-
 // Activation prologue of the integer-MMA int4 GEMV.  Each 128-wide group G
 // is put in fixed point, X = round(x * 2^f_G) with |X| < 2^30, and X is
 // written as four balanced base-256 digits d_p in [-128, 127]
@@ -576,6 +466,87 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
   bar_sync_n<NT>();
 }
 
+// The same fixed-point digit planes for the int8 (m16n8k32 s8.s8) GEMV:
+// units of 4 consecutive elements, 32 units per 128-wide group (one warp).
+// Lane (p, t) of MMA m holds plane p of elements 32m + 4t + {0..3} (b0) and
+// 32m + 16 + 4t + {0..3} (b1): xb as uint32 [G][p][t][m][2].  The weights
+// are signed, so no offset correction is needed; xmul as in stage_xd.
+// K: the input length; Kp: K rounded up to 128 (the zero tail is staged too).
+template <int MAXU, bool NORM, int NT>
+__device__ void stage_xd8(const XSrc& s, int K, int Kp, uint32_t* xb, float* xmul, float* sred,
+                          int pdl) {
+  const int K4 = K / 4, Kp4 = Kp / 4;
+  float v[MAXU][4];
+  float gw[NORM ? MAXU : 1][4];
+  if (NORM && s.mode != X_PLAIN) {
+#pragma unroll
+    for (int i = 0; i < MAXU; i++) {
+      const int u = threadIdx.x + i * NT;
+      const float4 a = u < K4 ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 4 * u)) : make_float4(0, 0, 0, 0);
+      gw[NORM ? i : 0][0] = a.x; gw[NORM ? i : 0][1] = a.y; gw[NORM ? i : 0][2] = a.z; gw[NORM ? i : 0][3] = a.w;
+    }
+  }
+  if (pdl) pdl_wait();
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * NT;
+    const float4 a = u < K4 ? __ldcg(reinterpret_cast<const float4*>(s.x + 4 * u)) : make_float4(0, 0, 0, 0);
+    v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+  }
+  if (NORM && s.mode != X_PLAIN) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
+    ss = block_sum_n<NT>(ss, sred);
+    // RMSNORM: inverseSqrt(sum/K + eps) (kernels.js:142), IEEE sqrt + divide
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
+    const __half inv16 = __float2half_rn(inv);
+#pragma unroll
+    for (int i = 0; i < MAXU; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j += 2) {
+        if (!s.f16) {
+          v[i][j] = __fmul_rn(__fmul_rn(v[i][j], inv), gw[NORM ? i : 0][j]);
+          v[i][j + 1] = __fmul_rn(__fmul_rn(v[i][j + 1], inv), gw[NORM ? i : 0][j + 1]);
+        } else {  // RMSNORM_F16: f16(f16(x) * inv) * f16(g)
+          __half2 t = __hmul2_rn(__floats2half2_rn(v[i][j], v[i][j + 1]), __half2half2(inv16));
+          t = __hmul2_rn(t, __floats2half2_rn(gw[NORM ? i : 0][j], gw[NORM ? i : 0][j + 1]));
+          const float2 r = __half22float2(t);
+          v[i][j] = r.x;
+          v[i][j + 1] = r.y;
+        }
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int u = threadIdx.x + i * NT;
+    float am = fmaxf(fmaxf(fabsf(v[i][0]), fabsf(v[i][1])), fmaxf(fabsf(v[i][2]), fabsf(v[i][3])));
+    am = warp_max(am);  // the 32 units of a group are one warp (Kp4 % 32 == 0)
+    const int ex = ((__float_as_int(am) >> 23) & 0xFF) - 126;
+    const int f = min(30 - ex, 126);
+    const float sf = __int_as_float((127 + f) << 23);  // 2^f
+    uint32_t D[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      D[j] = ((uint32_t)__float2int_rn(v[i][j] * sf) + 0x80808080u) ^ 0x80808080u;
+    if (u >= Kp4) continue;
+    const int G = u >> 5, q = u & 31, m = q >> 3, t = q & 3, hf = (q >> 2) & 1;
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      const uint32_t sel = (uint32_t)(p | ((p + 4) << 4));
+      const uint32_t w = __byte_perm(__byte_perm(D[0], D[1], sel), __byte_perm(D[2], D[3], sel), 0x5410);
+      xb[((((G * 4 + p) * 4 + t) * 4 + m) << 1) + hf] = w;
+    }
+    if (q == 0) {
+      xmul[2 * G] = __int_as_float((127 - f) << 23);      // 2^-f
+      xmul[2 * G + 1] = __int_as_float((143 - f) << 23);  // 2^(16-f)
+    }
+  }
+  bar_sync_n<NT>();
+}
+
 // ======================================================================
 // Epilogues (GEMV4 / GEMV4_ADD / GATE_UP_SILU_GEMV4, kernels.js:884-1072)
 // ======================================================================
@@ -637,54 +608,6 @@ __device__ __forceinline__ void epilogue_row_pre(const Epi& e, int n, float v, f
     return;
   }
   e.y[n] = e.bias ? __fadd_rn(v, pre) : v;
-}
-
-// ======================================================================
-// int4 GEMV
-// ======================================================================
-// R = row tiles per block (2 for the gate/up pair), U = groups in flight per
-// warp, W = warps (split-K over the 128-wide groups).  The first U groups of
-// weights are requested before the activation prologue (they do not depend on
-// the previous kernel), so their HBM latency overlaps the wait and the
-// x-staging; later groups are fetched one batch ahead of the math.
-template <int R, int U>
-struct WBatch {
-  uint4 a[U][R], b[U][R];
-};
-
-template <int R, int U, int W>
-__device__ __forceinline__ void load_batch(WBatch<R, U>& wb, const uint32_t* __restrict__ w, int K8,
-                                           int gpr, int G0, const int (&row_a)[R],
-                                           const int (&row_b)[R], const bool (&va)[R],
-                                           const bool (&vb)[R], int t) {
-#pragma unroll
-  for (int u = 0; u < U; u++) {
-    const int G = G0 + u * W;
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      const bool ok = G < gpr;
-      wb.a[u][r] = (ok && va[r]) ? ldg_stream(w + (size_t)row_a[r] * K8 + 16 * G + 4 * t)
-                                 : make_uint4(0, 0, 0, 0);
-      wb.b[u][r] = (ok && vb[r]) ? ldg_stream(w + (size_t)row_b[r] * K8 + 16 * G + 4 * t)
-                                 : make_uint4(0, 0, 0, 0);
-    }
-  }
-}
-
-template <int U>
-struct W8Batch {
-  uint4 a[U], b[U];
-};
-template <int U, int W>
-__device__ __forceinline__ void load8(W8Batch<U>& wb, const uint32_t* __restrict__ w, int K4, int nch,
-                                      int N, int tile, int C0, int gq, int t) {
-  const int ra = tile * 16 + gq, rb = ra + 8;
-#pragma unroll
-  for (int u = 0; u < U; u++) {
-    const int Ch = C0 + u * W;
-    wb.a[u] = (Ch < nch && ra < N) ? ldg_stream(w + (size_t)ra * K4 + 16 * Ch + 4 * t) : make_uint4(0, 0, 0, 0);
-    wb.b[u] = (Ch < nch && rb < N) ? ldg_stream(w + (size_t)rb * K4 + 16 * Ch + 4 * t) : make_uint4(0, 0, 0, 0);
-  }
 }
 
 // RoPE pair (kernels.js:224-227 / 251-254): two separately rounded products

@@ -1,17 +1,21 @@
 // eg_kernels.cu -- sm_100a kernels for the Emberglass batch-1 decode path.
 //
-// GEMVs: the weights stay in the reference's packed layouts (int4 group-128,
-// f32 group scales, quantize.js:81-111; int8 rows, quantize.js:28-57).  Each
-// warp streams 16-row tiles with 128-bit loads, turns nibbles/bytes into
-// exact f16 integers with one LOP3 + one HSUB2 per pair, and uses the
-// m16n8k16 tensor-core op as a dot-product engine: the activation vector is
-// split into f16 (hi, lo) columns so the result keeps ~f32 accuracy.  The
-// per-group scale is applied to each 128-wide group sum (the reference
-// applies it per 8-wide word: same value up to f32 rounding).
+// GEMVs (int4 layers and the int8 LM head): the weights are repacked once,
+// at finalize, from the reference's packed rows (quantize.js:28-111) into a
+// "stream" layout of 16-row x 128-k blocks stored as tensor-core A
+// fragments, tile-major, so that any contiguous run of blocks is one
+// contiguous byte range.  One persistent-style CTA per SM streams its run of
+// blocks through a shared-memory ring with one cp.async.bulk per stage (a
+// producer warp), 16 consumer warps multiply them with the integer tensor
+// path (m16n8k32 u8.s8 for int4, s8.s8 for int8) against the activation held
+// as four base-256 digit planes of a per-group fixed-point value (exact
+// integer dots per 128-wide group, scaled in f32), and an epilogue warp
+// applies the scale / residual / bias / SiLU / LoRA / argmax epilogue.
 //
-// Attention: split-K decode over the KV cache (ATTN_PARTIAL/ATTN_COMBINE,
-// kernels.js:258-388) with RoPE (ROPE_QK, kernels.js:205-257) and the KV
-// append (runtime.js:1509-1514) fused into the partial kernel.
+// Attention: one CTA per (query head, split of <= 256 keys) with the K/V rows
+// in registers (ATTN_PARTIAL/ATTN_COMBINE, kernels.js:258-388), RoPE
+// (ROPE_QK, kernels.js:205-257) and the KV append (runtime.js:1509-1514)
+// fused in.
 #include <float.h>
 #include <math.h>
 
@@ -96,6 +100,34 @@ __device__ long long g4_trace[512][64];
 constexpr int kG4Warps = 16;                   // consumer warps per CTA (one CTA per SM)
 constexpr int kG4Threads = kG4Warps * 32 + 64;  // + producer warp + epilogue warp
 
+// Producer warp of a streaming GEMV: copy `nitems` blocks of `blk` bytes
+// from src0 into the ring, `cap` blocks (one cp.async.bulk) per stage, each
+// stage reused once all consumer warps released it.
+__device__ __forceinline__ void ring_produce(unsigned char* ring, uint64_t* full, uint64_t* empty,
+                                             int stages, int stage_bytes,
+                                             const unsigned char* src0, int nitems, int cap,
+                                             int blk, int* err, int lane) {
+  const int nchunks = (nitems + cap - 1) / cap;
+  int st = 0, ph = 0, n = 0;
+  for (; n < nchunks; n++) {
+    if (!mbar_wait(&empty[st], ph ^ 1, err)) break;
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)(min(cap, nitems - n * cap) * blk);
+      mbar_expect_tx(&full[st], bytes);
+      bulk_g2s(ring + (size_t)st * stage_bytes, src0 + (size_t)n * cap * blk, bytes, &full[st]);
+    }
+    __syncwarp();
+    if (++st == stages) {
+      st = 0;
+      ph ^= 1;
+    }
+  }
+  // every issued copy has landed before the CTA may exit (bounded even after
+  // an error elsewhere)
+  for (int k = n > stages ? n - stages : 0; k < n; k++)
+    if (!mbar_wait_bounded(&full[k % stages], (k / stages) & 1)) break;
+}
+
 // One CTA per SM.  Warps 0-15 consume, warp 16 produces, warp 17 runs the
 // epilogues.  The CTA's tiles form a contiguous run of blocks (items) in the
 // stream layout; the producer copies it in stages of p.cap items (one
@@ -145,24 +177,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
   if (warp == 0) G4T(0);
 
   if (warp == CW) {  // --------------------------------------------- producer
-    int st = 0, ph = 0, n = 0;
-    for (; n < nchunks; n++) {
-      if (!mbar_wait(&empty[st], ph ^ 1, p.err)) break;
-      if (lane == 0) {
-        const uint32_t bytes = (uint32_t)(min(cap, nitems - n * cap) * blk);
-        mbar_expect_tx(&full[st], bytes);
-        bulk_g2s(ring + (size_t)st * p.stage_bytes, src0 + (size_t)n * cap * blk, bytes, &full[st]);
-      }
-      __syncwarp();
-      if (++st == p.stages) {
-        st = 0;
-        ph ^= 1;
-      }
-    }
-    // every issued copy has landed before the CTA may exit (bounded even
-    // after an error elsewhere)
-    for (int k = n > p.stages ? n - p.stages : 0; k < n; k++)
-      if (!mbar_wait_bounded(&full[k % p.stages], (k / p.stages) & 1)) break;
+    ring_produce(ring, full, empty, p.stages, p.stage_bytes, src0, nitems, cap, blk, p.err, lane);
     return;
   }
 
@@ -298,12 +313,6 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
   if (warp == 0) G4T(63);
 }
 
-// Units of 8 activations per thread (256 threads) a register-staged
-// prologue holds.
-static int maxu_for(int K) {
-  const int u = (K / 8 + 255) / 256;
-  return u <= 1 ? 1 : u <= 2 ? 2 : 6;  // K <= 12288
-}
 
 // Shared-memory plan of one launch (bytes): barriers, x fragments + group
 // multipliers, then the ring of stages of `cap` items.
@@ -420,181 +429,293 @@ void q4_to_stream(const uint32_t* w, const float* s, int N, int K, int R, unsign
 // ======================================================================
 // int8 GEMV (tied LM head, GEMV kernels.js:20-59) + fused argmax tail
 // ======================================================================
-// Grid-stride over 16-row tiles; the activation prologue runs once per block
-// and the next tile's first batch of weights is in flight while the current
-// tile is reduced.
-template <int U, int W, int MAXU>
-__global__ void __launch_bounds__(W * 32) gemv_q8_kernel(const uint32_t* __restrict__ w,
-                                                         const float* __restrict__ s, int N,
-                                                         int K, XSrc xsrc, float* __restrict__ y,
-                                                         StepTail tail, int has_tail, int pdl) {
-  extern __shared__ uint4 smem4[];
-  uint2* smem = reinterpret_cast<uint2*>(smem4);
-  __shared__ float sred[32];
-  __shared__ float red[W][16];
-  __shared__ float best_v[16];
-  __shared__ uint32_t best_i[16];
-  __shared__ bool last;
-  const int K4 = K / 4, nch = K / 64;  // 64-wide chunks
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int gq = lane >> 2, t = lane & 3;
-  const int tiles = (N + 15) / 16;
+// Stream layout of an int8 matrix (q8_to_stream): blocks of 16 rows x 128 k
+// (2 KB), tile-major, group-minor; inside a block [row half h][k half k2]
+// [lane (gq, t)][16 bytes] = row 8h + gq, words 16 k2 + t + {0, 4, 8, 12} of
+// the group, i.e. the m16n8k32 s8 A fragments of MMAs 2 k2 and 2 k2 + 1 with
+// no unpacking.  The row scales stay a plain f32 array (applied after the
+// row sum, as the reference does).
+constexpr int kQ8Block = 2048;
 
-  W8Batch<U> cur;
-  if (blockIdx.x < tiles) load8<U, W>(cur, w, K4, nch, N, blockIdx.x, warp, gq, t);
-  if (pdl) pdl_wait();
-  const int e = stage_x<MAXU>(xsrc, K, 8, smem4, sred);
-  if (pdl) pdl_launch_dependents();
-  const uint2* xs = gq == 0 ? smem : smem + K4 + 2;
-  const bool bl = gq < 2;
-  float bv = -1e30f;
-  uint32_t bi = 0xffffffffu;
+size_t q8_stream_bytes(int N, int K) {
+  return (size_t)((N + 15) / 16) * ((K + kGroup - 1) / kGroup) * kQ8Block;
+}
 
-  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int C0 = warp; C0 < nch; C0 += W * U) {
-      W8Batch<U> nxt;
-      const bool tail_batch = C0 + W * U >= nch;
-      const int ntile = tile + gridDim.x;
-      if (!tail_batch)
-        load8<U, W>(nxt, w, K4, nch, N, tile, C0 + W * U, gq, t);
-      else if (ntile < tiles)
-        load8<U, W>(nxt, w, K4, nch, N, ntile, warp, gq, t);
+__global__ void q8_to_stream_kernel(const uint32_t* __restrict__ w, int N, int K,
+                                    unsigned char* __restrict__ out) {
+  const int gpr = (K + kGroup - 1) / kGroup, K4 = K / 4, tiles = (N + 15) / 16;
+  const long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // 16-byte word
+  if (u >= (long long)tiles * gpr * (kQ8Block / 16)) return;
+  const int lane = (int)(u & 31), k2 = (int)((u >> 5) & 1), h = (int)((u >> 6) & 1);
+  const long long b = u >> 7;
+  const int G = (int)(b % gpr), tile = (int)(b / gpr);
+  const int row = tile * 16 + 8 * h + (lane >> 2);
+  uint32_t v[4] = {0u, 0u, 0u, 0u};
+  if (row < N)
 #pragma unroll
-      for (int u = 0; u < U; u++) {
-        const int Ch = C0 + u * W;
-        if (Ch >= nch) break;
-        const uint4* xp = reinterpret_cast<const uint4*>(xs + 16 * Ch + 4 * t);
-        const uint4 x01 = bl ? xp[0] : make_uint4(0, 0, 0, 0);
-        const uint4 x23 = bl ? xp[1] : make_uint4(0, 0, 0, 0);
-        uint32_t a0, a1, b0, b1;
-        deq_int8(cur.a[u].x, a0, a1);
-        deq_int8(cur.b[u].x, b0, b1);
-        mma16816(c, a0, b0, a1, b1, x01.x, x01.y);
-        deq_int8(cur.a[u].y, a0, a1);
-        deq_int8(cur.b[u].y, b0, b1);
-        mma16816(c, a0, b0, a1, b1, x01.z, x01.w);
-        deq_int8(cur.a[u].z, a0, a1);
-        deq_int8(cur.b[u].z, b0, b1);
-        mma16816(c, a0, b0, a1, b1, x23.x, x23.y);
-        deq_int8(cur.a[u].w, a0, a1);
-        deq_int8(cur.b[u].w, b0, b1);
-        mma16816(c, a0, b0, a1, b1, x23.z, x23.w);
-      }
-      cur = nxt;
+    for (int j = 0; j < 4; j++) {
+      const int word = G * 32 + 16 * k2 + (lane & 3) + 4 * j;
+      if (word < K4) v[j] = w[(size_t)row * K4 + word];
     }
-    if (t == 0) {
-      red[warp][gq] = c[0] + c[1];
-      red[warp][gq + 8] = c[2] + c[3];
+  *reinterpret_cast<uint4*>(out + b * kQ8Block + h * 1024 + k2 * 512 + lane * 16) =
+      make_uint4(v[0], v[1], v[2], v[3]);
+}
+
+void q8_to_stream(const uint32_t* w, int N, int K, unsigned char* out, cudaStream_t st) {
+  const long long n = (long long)((N + 15) / 16) * ((K + kGroup - 1) / kGroup) * (kQ8Block / 16);
+  q8_to_stream_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, N, K, out);
+}
+
+struct Q8Args {
+  const unsigned char* ws;  // stream layout
+  const float* s;           // row scales
+  int N, K;
+  XSrc x;
+  float* y;
+  StepTail tail;
+  int has_tail;
+  int* err;
+  int stages, stage_bytes, cap, xs_off, ring_off;
+  int pdl;
+};
+
+// Same warp roles as gemv_q4_kernel.  The epilogue warp writes
+// y[n] = (row sum) * s[n] and keeps the best (value, index); with a tail, the
+// CTAs' candidates are merged by the last CTA to finish, which also advances
+// the decode position (ARGMAX kernels.js:771-784, then decodeBatch's copy of
+// s.amax into the id buffer, runtime.js:1783-1785).
+template <int MAXU, bool NORM>
+__global__ void __launch_bounds__(kG4Threads, 1) gemv_q8_kernel(Q8Args p) {
+  constexpr int CW = kG4Warps, NT = CW * 32;
+  extern __shared__ __align__(128) unsigned char g4_smem[];
+  __shared__ float sred[32];
+  __shared__ float red[2][CW][16];
+  uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
+  uint64_t* empty = full + p.stages;
+  uint64_t* tile_full = empty + p.stages;  // [2]
+  uint64_t* tile_free = tile_full + 2;     // [2]
+  const int gpr = (p.K + kGroup - 1) / kGroup;
+  uint32_t* xb = reinterpret_cast<uint32_t*>(g4_smem + p.xs_off);  // [gpr][4][4][4][2]
+  float* xmul = reinterpret_cast<float*>(xb + (size_t)gpr * 128);  // [gpr][2]
+  unsigned char* ring = g4_smem + p.ring_off;
+  const int tiles = (p.N + 15) / 16;
+  const int P = gridDim.x, c = blockIdx.x;
+  const int t_lo = (int)((long long)tiles * c / P), t_hi = (int)((long long)tiles * (c + 1) / P);
+  const int nitems = (t_hi - t_lo) * gpr;
+  const int cap = p.cap;
+  const int nchunks = (nitems + cap - 1) / cap;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.stages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], CW);
     }
-    __syncthreads();
-    if (threadIdx.x < 16) {
-      const int n = tile * 16 + threadIdx.x;
-      float a = 0.f;
-      for (int ww = 0; ww < W; ww++) a += red[ww][threadIdx.x];
-      if (n < N) {
-        const float o = __fmul_rn(e ? ldexpf(a, e) : a, __ldg(s + n));  // sum first, scale last
-        y[n] = o;
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&tile_full[i], CW);
+      mbar_init(&tile_free[i], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == CW) {  // --------------------------------------------- producer
+    ring_produce(ring, full, empty, p.stages, p.stage_bytes, p.ws + (size_t)t_lo * gpr * kQ8Block,
+                 nitems, cap, kQ8Block, p.err, lane);
+    return;
+  }
+
+  if (warp == CW + 1) {  // ------------------------------------------- epilogue
+    float sc = lane < 16 && t_lo * 16 + lane < p.N ? __ldg(p.s + t_lo * 16 + lane) : 0.f;
+    float bv = -1e30f;
+    uint32_t bi = 0xffffffffu;
+    for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
+      const int b = j & 1;
+      if (!mbar_wait(&tile_full[b], (j >> 1) & 1, p.err)) break;
+      float v = 0.f;
+      if (lane < 16)
+        for (int ww = 0; ww < CW; ww++) v += red[b][ww][lane];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tile_free[b]);
+      const int n = tile * 16 + lane;
+      if (lane < 16 && n < p.N) {
+        const float o = __fmul_rn(v, sc);  // sum first, scale last
+        p.y[n] = o;
         if (beats(o, (uint32_t)n, bv, bi)) {
           bv = o;
           bi = (uint32_t)n;
         }
+        sc = n + 16 < p.N && tile + 1 < t_hi ? __ldg(p.s + n + 16) : 0.f;
       }
     }
-    __syncthreads();
-  }
-  if (!has_tail) return;
-  // ---- fused argmax + position advance (ARGMAX kernels.js:771-784, then
-  // decodeBatch's copy of s.amax into the id buffer, runtime.js:1783-1785)
-  if (threadIdx.x < 16) {
-    best_v[threadIdx.x] = bv;
-    best_i[threadIdx.x] = bi;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
+    if (!p.has_tail) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (beats(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    const StepTail& tl = p.tail;
+    unsigned prev = 0;
+    if (lane == 0) {
+      tl.cand_v[c] = bv;
+      tl.cand_i[c] = bi;
+      __threadfence();
+      prev = atomicAdd(tl.counter, 1u);
+    }
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != (unsigned)P - 1) return;
+    __threadfence();
     float v = -1e30f;
     uint32_t id = 0xffffffffu;
-    for (int i = 0; i < 16; i++)
-      if (beats(best_v[i], best_i[i], v, id)) {
-        v = best_v[i];
-        id = best_i[i];
+    for (int b = lane; b < P; b += 32) {
+      const float cv = __ldcg(tl.cand_v + b);
+      const uint32_t ci = __ldcg(tl.cand_i + b);
+      if (beats(cv, ci, v, id)) {
+        v = cv;
+        id = ci;
       }
-    tail.cand_v[blockIdx.x] = v;
-    tail.cand_i[blockIdx.x] = id;
-    __threadfence();
-    const unsigned prev = atomicAdd(tail.counter, 1u);
-    last = prev == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  float v = -1e30f;
-  uint32_t id = 0xffffffffu;
-  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
-    const float cv = __ldcg(tail.cand_v + b);
-    const uint32_t ci = __ldcg(tail.cand_i + b);
-    if (beats(cv, ci, v, id)) {
-      v = cv;
-      id = ci;
     }
-  }
-  // warp + block argmax reduction, ties to the lower index
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-    const uint32_t oi = __shfl_xor_sync(0xffffffffu, id, o);
-    if (beats(ov, oi, v, id)) {
-      v = ov;
-      id = oi;
-    }
-  }
-  if (lane == 0) {
-    best_v[warp] = v;
-    best_i[warp] = id;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    v = best_v[0];
-    id = best_i[0];
-    for (int i = 1; i < W; i++)
-      if (beats(best_v[i], best_i[i], v, id)) {
-        v = best_v[i];
-        id = best_i[i];
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, id, o);
+      if (beats(ov, oi, v, id)) {
+        v = ov;
+        id = oi;
       }
-    const int p = *tail.pos;
-    if (tail.greedy) {
-      *tail.amax = id;
-      tail.ids[p + 1] = id;
-      const int k = *tail.out_idx;
-      tail.out_ids[k] = id;
-      *tail.out_idx = k + 1;
     }
-    *tail.pos = p + 1;
-    *tail.counter = 0u;
+    if (lane == 0) {
+      const int ps = *tl.pos;
+      if (tl.greedy) {
+        *tl.amax = id;
+        tl.ids[ps + 1] = id;
+        const int k = *tl.out_idx;
+        tl.out_ids[k] = id;
+        *tl.out_idx = k + 1;
+      }
+      *tl.pos = ps + 1;
+      *tl.counter = 0u;
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------- consumers
+  stage_xd8<MAXU, NORM, NT>(p.x, p.K, gpr * kGroup, xb, xmul, sred, p.pdl);
+  if (p.pdl) pdl_launch_dependents();
+  const int gq = lane >> 2, t = lane & 3;
+  const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
+  float acc0 = 0.f, acc1 = 0.f;
+  bool dead = false;
+  int st = 0, ph = 0, chunk = 0, chunk_lo = 0;
+  if (nchunks > 0 && !mbar_wait(&full[0], 0, p.err)) dead = true;
+  const unsigned char* stage = ring;
+  int i = warp;
+  for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
+    const int tile_end = (j + 1) * gpr;
+    for (; i < tile_end; i += 16) {
+      while (i >= chunk_lo + cap) {  // next stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (++st == p.stages) {
+          st = 0;
+          ph ^= 1;
+        }
+        chunk++;
+        chunk_lo += cap;
+        stage = ring + (size_t)st * p.stage_bytes;
+        if (!dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
+      }
+      const int g = i - j * gpr;
+      const unsigned char* bp = stage + (size_t)(i - chunk_lo) * kQ8Block;
+      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
+      if (bl) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 8);
+        X0 = xp[0];
+        X1 = xp[1];
+      }
+      const uint4 A0 = *reinterpret_cast<const uint4*>(bp + lane * 16);
+      const uint4 A1 = *reinterpret_cast<const uint4*>(bp + 512 + lane * 16);
+      const uint4 B0 = *reinterpret_cast<const uint4*>(bp + 1024 + lane * 16);
+      const uint4 B1 = *reinterpret_cast<const uint4*>(bp + 1536 + lane * 16);
+      int cc[4] = {0, 0, 0, 0};
+      imma16832_ss(cc, A0.x, B0.x, A0.y, B0.y, X0.x, X0.y);
+      imma16832_ss(cc, A0.z, B0.z, A0.w, B0.w, X0.z, X0.w);
+      imma16832_ss(cc, A1.x, B1.x, A1.y, B1.y, X1.x, X1.y);
+      imma16832_ss(cc, A1.z, B1.z, A1.w, B1.w, X1.z, X1.w);
+      if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
+        const float mul = xmul[2 * g + t];
+        acc0 = fmaf(mul, (float)(cc[0] + 256 * cc[1]), acc0);
+        acc1 = fmaf(mul, (float)(cc[2] + 256 * cc[3]), acc1);
+      }
+    }
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    const int b = j & 1;
+    if (!dead && !mbar_wait(&tile_free[b], ((j >> 1) & 1) ^ 1, p.err)) dead = true;
+    if (t == 0) {
+      red[b][warp][gq] = acc0;
+      red[b][warp][gq + 8] = acc1;
+    }
+    acc0 = acc1 = 0.f;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tile_full[b]);
+  }
+  // release the current stage and wait/release the later ones (see gemv_q4_kernel)
+  for (; chunk < nchunks; chunk++) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (++st == p.stages) {
+      st = 0;
+      ph ^= 1;
+    }
+    if (chunk + 1 < nchunks && !dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
   }
 }
 
-template <int MAXU>
-static void gemv_q8_go(const uint32_t* w, const float* s, int N, int K, const XSrc& x, float* y,
-                       const StepTail* tail, cudaStream_t st, bool pdl) {
-  const int tiles = (N + 15) / 16;
-  const int grid = std::min(tiles, sm_count() * 4);
-  const size_t smem = (size_t)(2 * (K / 4) + 4) * sizeof(uint2);
-  auto k = gemv_q8_kernel<4, 8, MAXU>;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  StepTail tl = {};
-  if (tail) tl = *tail;
-  launch(k, dim3(grid), dim3(256), smem, st, pdl, w, s, N, K, x, y, tl, tail ? 1 : 0, (int)pdl);
+template <int MAXU, bool NORM>
+static void gemv_q8_go(const Q8Args& a0, cudaStream_t st, bool pdl) {
+  Q8Args a = a0;
+  const int gpr = (a.K + kGroup - 1) / kGroup;
+  a.cap = 16;  // 32 KB stages
+  a.stage_bytes = a.cap * kQ8Block;
+  a.xs_off = 256;
+  a.ring_off = (a.xs_off + gpr * (512 + 8) + 127) & ~127;
+  const int budget = 150 * 1024;
+  a.stages = std::max(2, std::min(8, (budget - a.ring_off) / a.stage_bytes));
+  const int smem = a.ring_off + a.stages * a.stage_bytes;
+  a.pdl = pdl ? 1 : 0;
+  const int P = std::min(sm_count(), (a.N + 15) / 16);
+  auto k = gemv_q8_kernel<MAXU, NORM>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  launch(k, dim3(P), dim3(kG4Threads), (size_t)smem, st, pdl, a);
 }
 
-void gemv_q8(const uint32_t* w, const float* s, int N, int K, const XSrc& x, float* y,
-             const StepTail* tail, cudaStream_t st, bool pdl) {
-  switch (maxu_for(K)) {
-    case 1: gemv_q8_go<1>(w, s, N, K, x, y, tail, st, pdl); break;
-    case 2: gemv_q8_go<2>(w, s, N, K, x, y, tail, st, pdl); break;
-    default: gemv_q8_go<6>(w, s, N, K, x, y, tail, st, pdl); break;
+void gemv_q8(const unsigned char* ws, const float* s, int N, int K, const XSrc& x, float* y,
+             const StepTail* tail, cudaStream_t st, bool pdl, const GemvWork& wk) {
+  Q8Args a = {};
+  a.ws = ws;
+  a.s = s;
+  a.N = N;
+  a.K = K;
+  a.x = x;
+  a.y = y;
+  if (tail) a.tail = *tail;
+  a.has_tail = tail ? 1 : 0;
+  a.err = wk.err;
+  const int u = (K / 4 + kG4Warps * 32 - 1) / (kG4Warps * 32);  // units of 4 per thread
+  if (x.mode != X_PLAIN) {
+    if (u <= 1) gemv_q8_go<1, true>(a, st, pdl);
+    else gemv_q8_go<6, true>(a, st, pdl);
+  } else {
+    if (u <= 1) gemv_q8_go<1, false>(a, st, pdl);
+    else gemv_q8_go<6, false>(a, st, pdl);
   }
 }
+
 
 // ======================================================================
 // LoRA A: d[m][r] = A_m[r] . x  (LORA_A, kernels.js:60-78)

@@ -85,10 +85,15 @@ void q4_to_stream(const uint32_t* w, const float* s, int N, int K, int R, unsign
 // of a packed [gate;up] matrix).  Requires K % 128 == 0, K <= 12288.
 void gemv_q4(const unsigned char* ws, int N, int K, const XSrc& x, const Epi& e, cudaStream_t st,
              bool pdl, const GemvWork& wk);
-// y = W8 x * scale[n] (int8 rows).  tail != null fuses argmax/advance.
-void gemv_q8(const uint32_t* w, const float* s, int N, int K, const XSrc& x, float* y,
-             const StepTail* tail, cudaStream_t st, bool pdl);
-
+// int8 row matrices in the "stream" layout: 16 x 128 blocks of m16n8k32 A
+// fragments, tile-major; q8_to_stream builds it from int8 rows (4 per u32,
+// quantize.js:28-57), zero-padding K to a multiple of 128.
+size_t q8_stream_bytes(int N, int K);
+void q8_to_stream(const uint32_t* w, int N, int K, unsigned char* out, cudaStream_t st);
+// y = (W8 x) * scale[n] over a stream-layout matrix.  tail != null fuses
+// argmax/advance.  Requires K % 4 == 0, K <= 12288.
+void gemv_q8(const unsigned char* ws, const float* s, int N, int K, const XSrc& x, float* y,
+             const StepTail* tail, cudaStream_t st, bool pdl, const GemvWork& wk);
 struct AttnArgs {
   const float* qkv;  // raw q [nh*128] | k [nkv*128] | v [nkv*128] from the QKV GEMV
   void* kc;          // [max_ctx][nkv][128] f16 or f32

@@ -73,6 +73,7 @@ struct eg_rt {
   std::vector<eg::Layer> L;
   uint32_t* emb_w = nullptr;
   float* emb_s = nullptr;
+  unsigned char* emb_t = nullptr;  // LM head in the int8 stream layout (emb_w stays for EMBED)
   float* final_norm = nullptr;
   float *cosT = nullptr, *sinT = nullptr;
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *tmp = nullptr, *logits = nullptr;
@@ -510,7 +511,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
   tail.cand_v = rt->cand_v;
   tail.cand_i = rt->cand_i;
   tail.counter = rt->counter;
-  gemv_q8(rt->emb_w, rt->emb_s, c.vocab_size, H, xf, rt->logits, &tail, st, pdl);
+  gemv_q8(rt->emb_t, rt->emb_s, c.vocab_size, H, xf, rt->logits, &tail, st, pdl, wk);
   launches++;
   mark(rt, so, 5, cats);
   return launches;
@@ -897,6 +898,9 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
       q4_to_stream(l.d_w, l.d_s, H, I, 1, l.d_t, rt->st);
       CK(cudaGetLastError());
     }
+    DALLOC(rt->emb_t, q8_stream_bytes(c.vocab_size, H), wb);
+    q8_to_stream(rt->emb_w, c.vocab_size, H, rt->emb_t, rt->st);
+    CK(cudaGetLastError());
     if (!rt->o.use_fused) {
       CK(cudaStreamSynchronize(rt->st));
       for (auto& l : rt->L) {
@@ -1393,7 +1397,15 @@ EG_API eg_status eg_op_gemv_q8(const float* x, const uint32_t* w, const float* s
   XSrc xs = {};
   xs.mode = X_PLAIN;
   xs.x = x;
-  gemv_q8(w, scale, N, K, xs, y, nullptr, OPSTREAM, false);
+  // the single-op entry takes int8 rows; convert them to the stream layout
+  void* scr = nullptr;
+  eg_status s = op_scratch(256 + q8_stream_bytes(N, K), &scr);
+  if (s) return s;
+  char* b = static_cast<char*>(scr);
+  CK(cudaMemsetAsync(b, 0, 4, OPSTREAM));
+  unsigned char* t = reinterpret_cast<unsigned char*>(b + 256);
+  q8_to_stream(w, N, K, t, OPSTREAM);
+  gemv_q8(t, scale, N, K, xs, y, nullptr, OPSTREAM, false, GemvWork{reinterpret_cast<int*>(b)});
   CK(cudaGetLastError());
   return EG_OK;
 }
