@@ -29,7 +29,8 @@ CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-fopenmp", "-ffp-contract=off", "-mar
 
 CU = ["eg_kernels.cu", "eg_fused.cu", "eg_runtime.cu", "eg_noalloc.cu"]
 CPP = ["eg_host.cpp"]
-HEADERS = ["eg_common.cuh", "eg_device.cuh", "eg_kernels.h", "eg_fused.h", "eg_host.h"]
+HEADERS = ["eg_common.cuh", "eg_device.cuh", "eg_stream.cuh", "eg_kernels.h", "eg_fused.h",
+           "eg_host.h"]
 
 
 def _stale(target: str, deps: list[str]) -> bool:

@@ -13,19 +13,6 @@
 
 namespace eg {
 
-// Intra-phase timeline (profiling only): the fused kernel points g_marks at
-// a buffer and sets s_mark_base for one CTA and phase; mark(k) stores the
-// globaltimer there.  Null everywhere else.
-static __device__ unsigned long long* g_marks = nullptr;
-static __shared__ int s_mark_base;
-__device__ __forceinline__ void mark(int k) {
-  if (g_marks && threadIdx.x == 0 && s_mark_base >= 0) {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g_marks[s_mark_base + k] = t;
-    g_marks[80 + s_mark_base + k] = (unsigned long long)clock64();
-  }
-}
 
 // ======================================================================
 // mbarriers and bulk copies (shared-memory rings fed by cp.async.bulk)
@@ -173,7 +160,8 @@ __device__ __forceinline__ void setup_x(const XSrc& s, int K, XCtx& c, float* sr
   c.inv = 1.f;
   c.inv16 = __float2half_rn(1.f);
   if (s.mode == X_EMBED_RMS) {
-    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
+    const uint32_t id =
+        s.use_fixed_id ? s.fixed_id : __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
     c.erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
     c.escale = s.emb_s[id];
     if (blockIdx.x == 0 && s.hidden_out)
@@ -218,7 +206,8 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred, i
   const int8_t* erow = nullptr;
   float escale = 0.f;
   if ((NORM && s.mode == X_EMBED_RMS)) {
-    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
+    const uint32_t id =
+        s.use_fixed_id ? s.fixed_id : __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
     erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
     escale = s.emb_s[id];
   }
@@ -256,7 +245,6 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred, i
       }
     }
   }
-  mark(6);
   if ((NORM && s.mode != X_PLAIN)) {
     float ss = 0.f;
 #pragma unroll
@@ -288,9 +276,7 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred, i
   for (int i = 0; i < MAXU; i++)
 #pragma unroll
     for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
-  mark(7);
   const int e = shift_for(block_max(am, sred));
-  mark(8);
 #pragma unroll
   for (int i = 0; i < MAXU; i++) {
     const int u = u0 + threadIdx.x + i * kCtaThreads;
@@ -360,7 +346,8 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
   const int8_t* erow = nullptr;
   float escale = 0.f;
   if (NORM && s.mode == X_EMBED_RMS) {
-    const uint32_t id = __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
+    const uint32_t id =
+        s.use_fixed_id ? s.fixed_id : __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
     erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
     escale = s.emb_s[id];
   }
@@ -746,7 +733,6 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
     qs[hh][j] = lo;
     qs[hh][j + half] = hi;
   }
-  mark(1);
   if (pos >= t0 && pos < t1) {  // ROPE_QK on k, then the KV append (runtime.js:1509-1514)
     const int tn = pos - t0;
     const float* k = a.qkv + a.nh * hd + kvh * hd;
@@ -768,7 +754,6 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
     }
   }
   cta_sync();
-  mark(3);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float scale = 1.0f / sqrtf((float)hd);
   for (int hh = warp; hh < G; hh += kCtaThreads / 32) {
@@ -821,7 +806,6 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
       a.pz[h * a.max_splits + split] = z;
     }
   }
-  mark(4);
   if (nsplit == 1) {
     cta_sync();
     return;
@@ -835,7 +819,6 @@ __device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_sme
     last = prev == (unsigned)nsplit - 1;
   }
   cta_sync();
-  mark(5);
   if (!last) return;
   __threadfence();
   for (int hh = warp; hh < G; hh += kCtaThreads / 32) {

@@ -1,683 +1,298 @@
-// eg_fused.cu -- persistent fused decode: K tokens of runtime.js:1466-1571
-// (plus EMBED_BUF in front and ARGMAX behind) in ONE cooperative launch.
+// eg_fused.cu -- persistent decode: n tokens of runtime.js:1466-1571 (plus
+// EMBED_BUF in front and ARGMAX behind) in ONE cooperative launch.
 //
-// Grid = one CTA per SM.  A token is a fixed sequence of phases -- per layer
-// QKV, ATTN, O, GATE_UP, DOWN, then the LM head -- each split statically over
-// the CTAs (16-row tiles of each matrix, (split, kv-head) attention items) and
-// separated by a grid barrier.
+// Grid = one CTA per SM, the warp roles of the streaming GEMVs
+// (eg_stream.cuh): warps 0-15 consume, warp 16 produces, warp 17 runs the
+// epilogues.  A token is a fixed sequence of phases -- per layer QKV, ATTN,
+// O, GATE_UP, DOWN, then the LM head -- separated by grid barriers; every
+// GEMV phase gives each CTA a contiguous range of the matrix's 16-row tiles.
 //
-// Inside a CTA, warp 8 is a producer: it walks the CTA's weight slices of the
-// whole launch (every layer, every token) in consumption order and streams
-// them with cp.async.bulk into a 4-stage shared-memory ring (32 KB per stage
-// = 32 row segments of <= 1 KB), signalling an mbarrier per stage.  The
-// weights do not depend on activations, so the producer never waits for a
-// grid barrier: HBM keeps streaming the next phase's weights while the 8
-// consumer warps wait, compute attention, or run epilogues.  Consumers turn
-// the nibbles/bytes of each stage into m16n8k16 fragments (eg_common.cuh) and
-// release the stage.
-//
-// Cross-CTA data (hidden, q/k/v, attention output, SiLU output, KV rows, token
-// ids) is written before a grid barrier and read after it with ld.global.cg,
-// so no stale L1 line is observed inside the launch.  Every wait (grid
-// barrier, mbarrier) is bounded: on timeout the waiter records an error word,
-// the other waits see it and give up, and the host reports EG_ERR_DEVICE.
+// The producer walks the CTA's weight runs of the whole launch (every phase
+// of every token) in order and streams them through one shared-memory ring,
+// one cp.async.bulk per stage.  The weights do not depend on activations, so
+// it never waits for a grid barrier: HBM keeps streaming the next phases'
+// weights while the consumers wait at a barrier, stage activations or run
+// attention.  At the end of a GEMV phase the epilogue warp, once its last
+// tile's outputs are written and fenced, bumps a shared-memory phase count;
+// consumer thread 0 waits for it, then arrives at the grid barrier
+// (red.release.gpu) and polls it (ld.acquire.gpu).  Activations written before a barrier are read after it
+// with ld.global.cg, so no stale L1 line is seen inside the launch.  After
+// the LM head every CTA reduces the CTAs' argmax candidates itself, so the
+// next token's embedding needs no further barrier.  Every wait is bounded:
+// on timeout the waiter records an error word, the others see it and leave,
+// and the host reports EG_ERR_DEVICE.
+#include <stdio.h>
+#include <stdlib.h>
+
 #include <algorithm>
 
-#include "eg_device.cuh"
 #include "eg_fused.h"
+#include "eg_stream.cuh"
 
 namespace eg {
 
-constexpr int kConsumerWarps = 8;                // == kCtaThreads / 32
-constexpr int kFusedThreads = kCtaThreads + 32;  // + producer warp
-constexpr int kStages = 4;
-constexpr int kSegBytes = 1024;
-constexpr int kSegs = 32;
-constexpr int kScaleSeg = 96;                   // per-segment room for its row's group scales
-constexpr int kStageBytes = kSegs * (kSegBytes + kScaleSeg);  // 32 KB weights + 3 KB scales
-constexpr int kChunkK = 2048;                   // int4 k-values per 1 KB row segment
+constexpr int kFStageBytes = 34816;  // 32 int4 blocks, 16 gate/up blocks, 17 int8 blocks
+constexpr int kFMaxStages = 6;
+constexpr int kFBarBytes = 256;      // ring + tile mbarriers
+constexpr unsigned long long kBarrierTimeoutNs = 2000000000ull;  // 2 s
 
-// ---------------------------------------------------------------- waits
-// Monotonic arrival counter over the consumer groups of all CTAs: the k-th
-// barrier completes when the counter reaches k * gridDim.x.  Returns false
-// (uniformly for the consumer group) when the launch is being abandoned.
-__device__ __forceinline__ bool grid_barrier(unsigned* bar, int* err, unsigned& epoch) {
-  __shared__ int s_ok;
-  cta_sync();
-  if (threadIdx.x == 0) {
-    epoch += 1;
-    const unsigned target = epoch * gridDim.x;
-    __threadfence();
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
-    int ok = 1;
-    for (long long spins = 0;; spins++) {
-      unsigned v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-      if (v >= target) break;
-      if ((spins & 255) == 0 && err_set(err)) {
-        ok = 0;
-        break;
-      }
-      if (spins > kSpinLimit) {
-        atomicExch(err, 1);
-        ok = 0;
-        break;
-      }
-    }
-    s_ok = ok && !err_set(err);
-  }
-  cta_sync();
-  return s_ok != 0;
-}
+enum { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4 };
 
-__device__ __forceinline__ void tile_range(int tiles, int& t0, int& t1) {
-  t0 = (int)((long long)tiles * blockIdx.x / gridDim.x);
-  t1 = (int)((long long)tiles * (blockIdx.x + 1) / gridDim.x);
-}
-
-// ---------------------------------------------------------------- units
-// A "unit" fills one ring stage.  int4 phases: two 16-row slots (tiles a and
-// a+1; gate/up: the gate tile and its up tile) x one 2048-wide k chunk;
-// segment 16*slot + r holds row r's bytes of that chunk.  LM head (int8): one
-// 16-row tile, segment 2r + h = row r's bytes [1024h, 1024h + 1024).
-enum { P_QKV = 0, P_O = 1, P_GU = 2, P_DOWN = 3, P_LM = 4 };
-
-struct Geo {
-  const uint32_t* w;
-  const float* s;
-  int N, K;    // rows of one matrix half (gate/up: I), reduction length
-  int t0, t1;  // this CTA's tiles
-  int pair;    // 1: slots are tiles a, a+1; 0: gate/up halves (or LM)
-  int nk;      // k chunks per slot pair
-};
-
-__device__ __forceinline__ Geo geo(const FusedArgs& a, const FusedLayer& l, int kind) {
-  Geo g = {};
-  switch (kind) {
-    case P_QKV: g.w = l.qkv_w; g.s = l.qkv_s; g.N = a.QD + 2 * a.KVD; g.K = a.H; g.pair = 1; break;
-    case P_O: g.w = l.o_w; g.s = l.o_s; g.N = a.H; g.K = a.QD; g.pair = 1; break;
-    case P_GU: g.w = l.gu_w; g.s = l.gu_s; g.N = a.I; g.K = a.H; g.pair = 0; break;
-    case P_DOWN: g.w = l.d_w; g.s = l.d_s; g.N = a.H; g.K = a.I; g.pair = 1; break;
-    default: g.w = a.emb_w; g.s = a.emb_s; g.N = a.V; g.K = a.H; g.pair = 0; break;
-  }
-  tile_range((g.N + 15) / 16, g.t0, g.t1);
-  g.nk = kind == P_LM ? 1 : (g.K + kChunkK - 1) / kChunkK;
-  return g;
-}
-
-__device__ __forceinline__ int units_of(const Geo& g, int kind) {
-  const int tiles = g.t1 - g.t0;
-  if (kind == P_LM) return tiles;
-  return (g.pair ? (tiles + 1) / 2 : tiles) * g.nk;
-}
-
-// Source and length of segment `seg` of unit u (bytes = 0: no segment).
-__device__ __forceinline__ const char* seg_src(const Geo& g, int kind, int u, int seg,
-                                               uint32_t& bytes) {
-  bytes = 0;
-  if (kind == P_LM) {
-    const int row = (g.t0 + u) * 16 + (seg >> 1);
-    if (row >= g.N) return nullptr;
-    bytes = kSegBytes;
-    return reinterpret_cast<const char*>(g.w) + (size_t)row * g.K + (seg & 1) * kSegBytes;
-  }
-  const int slot = seg >> 4, r = seg & 15;
-  const int p = u / g.nk, k = u % g.nk;
-  int row;
-  if (g.pair) {
-    const int tile = g.t0 + 2 * p + slot;
-    if (tile >= g.t1) return nullptr;
-    row = tile * 16 + r;
-    if (row >= g.N) return nullptr;
-  } else {
-    row = (g.t0 + p) * 16 + r + (slot ? g.N : 0);
-  }
-  const int kb = k * kChunkK, ke = min(g.K, kb + kChunkK);
-  bytes = (uint32_t)((ke - kb) / 2);
-  return reinterpret_cast<const char*>(g.w) + (size_t)row * (g.K / 2) + kb / 2;
-}
-
-// Group scales of segment `seg`: an aligned span holding floats [G0, G0+ng)
-// of the row's scale row starts `off` bytes into the copy (16-byte rules of
-// cp.async.bulk).  LM head: segment 0 carries the tile's 16 row scales.
-__device__ __forceinline__ const char* scale_src(const Geo& g, int kind, int u, int seg,
-                                                 uint32_t& bytes, uint32_t& off) {
-  bytes = 0;
-  off = 0;
-  if (kind == P_LM) {
-    const int row0 = (g.t0 + u) * 16;
-    if (seg != 0) return nullptr;
-    const int rows = min(16, g.N - row0);
-    bytes = (uint32_t)((rows * 4 + 15) & ~15);
-    return reinterpret_cast<const char*>(g.s + row0);
-  }
-  const int slot = seg >> 4, r = seg & 15;
-  const int p = u / g.nk, k = u % g.nk;
-  int row;
-  if (g.pair) {
-    const int tile = g.t0 + 2 * p + slot;
-    if (tile >= g.t1) return nullptr;
-    row = tile * 16 + r;
-    if (row >= g.N) return nullptr;
-  } else {
-    row = (g.t0 + p) * 16 + r + (slot ? g.N : 0);
-  }
-  const int gpr = g.K / kGroup;
-  const int ng = min(16, gpr - k * 16);
-  const size_t start = ((size_t)row * gpr + k * 16) * 4;
-  const size_t a0 = start & ~size_t(15);
-  off = (uint32_t)(start - a0);
-  bytes = (uint32_t)((off + ng * 4 + 15) & ~15u);
-  return reinterpret_cast<const char*>(g.s) + a0;
-}
-
-// Slots whose 16 rows are one contiguous span (K = 2048 int4, and every int8
-// LM tile) move as one weight copy + one scale copy each: few large bulk
-// copies instead of 32 row copies.
-__device__ __forceinline__ bool contiguous(const Geo& g, int kind) {
-  return kind == P_LM || (g.nk == 1 && g.K == kChunkK);
-}
-__device__ __forceinline__ int scale_stride(const Geo& g, int kind) {
-  return contiguous(g, kind) ? 64 : kScaleSeg;
-}
-
-// Copy `c` (0..3) of a contiguous unit: c = slot (weights) or 2 + slot (scales).
-__device__ __forceinline__ const char* contig_copy(const Geo& g, int kind, int u, int c,
-                                                   uint32_t& bytes, uint32_t& dst) {
-  bytes = 0;
-  dst = 0;
-  const int slot = c & 1;
-  int row0, rows;
-  if (kind == P_LM) {
-    if (slot) return nullptr;
-    row0 = (g.t0 + u) * 16;
-    rows = min(16, g.N - row0);
-    if (c < 2) {
-      bytes = (uint32_t)rows * g.K;
-      return reinterpret_cast<const char*>(g.w) + (size_t)row0 * g.K;
-    }
-    bytes = (uint32_t)((rows * 4 + 15) & ~15);
-    dst = kSegs * kSegBytes;
-    return reinterpret_cast<const char*>(g.s + row0);
-  }
-  if (g.pair) {
-    const int tile = g.t0 + 2 * u + slot;
-    if (tile >= g.t1) return nullptr;
-    row0 = tile * 16;
-    rows = min(16, g.N - row0);
-  } else {
-    row0 = (g.t0 + u) * 16 + (slot ? g.N : 0);
-    rows = 16;
-  }
-  if (c < 2) {
-    bytes = (uint32_t)rows * kSegBytes;
-    dst = slot * 16 * kSegBytes;
-    return reinterpret_cast<const char*>(g.w) + (size_t)row0 * kSegBytes;
-  }
-  bytes = (uint32_t)rows * 64;
-  dst = kSegs * kSegBytes + slot * 16 * 64;
-  return reinterpret_cast<const char*>(g.s + (size_t)row0 * 16);
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 __device__ __forceinline__ bool lm_runs(const FusedArgs& a, int tok) {
   return a.lm_every || tok == a.n_tokens - 1;
 }
 
-// ---------------------------------------------------------------- producer
-// The CTA's unit sequence of the launch: per token, per layer QKV, O,
-// GATE_UP, DOWN units, then the LM head's units when it runs.
-struct UnitIter {
-  int tok, li, kind, u, nu;
-  Geo g;
-  bool done;
+__device__ __forceinline__ void tile_range(int tiles, int& t_lo, int& t_hi) {
+  t_lo = (int)((long long)tiles * blockIdx.x / gridDim.x);
+  t_hi = (int)((long long)tiles * (blockIdx.x + 1) / gridDim.x);
+}
+
+// One GEMV phase of this CTA: the matrix, its tile range and ring geometry.
+struct Run {
+  const unsigned char* src;  // first block of the CTA's range
+  int t_lo, t_hi, gpr, blk, cap;
 };
 
-__device__ __forceinline__ void iter_load(const FusedArgs& a, UnitIter& it) {
-  for (;;) {
-    if (it.tok >= a.n_tokens) {
-      it.done = true;
-      return;
-    }
-    const bool lm = it.li == a.layers_n;
-    if (lm && !lm_runs(a, it.tok)) {  // no LM head for this token
-      it.tok++;
-      it.li = 0;
-      it.kind = P_QKV;
-      continue;
-    }
-    it.g = geo(a, a.layers[lm ? 0 : it.li], it.kind);
-    it.nu = units_of(it.g, it.kind);
-    if (it.nu > 0) return;
-    // empty phase: step to the next one
-    if (lm) {
-      it.tok++;
-      it.li = 0;
-      it.kind = P_QKV;
-    } else if (it.kind == P_DOWN) {
-      it.li++;
-      it.kind = it.li == a.layers_n ? P_LM : P_QKV;
-    } else {
-      it.kind++;
-    }
+__device__ __forceinline__ Run run_of(const FusedArgs& a, const FusedLayer& l, int ph) {
+  Run r;
+  int N, K, R = 1;
+  const unsigned char* w;
+  switch (ph) {
+    case PH_QKV: w = l.qkv; N = a.QD + 2 * a.KVD; K = a.H; break;
+    case PH_O: w = l.o; N = a.H; K = a.QD; break;
+    case PH_GU: w = l.gu; N = a.I; K = a.H; R = 2; break;
+    default: w = l.d; N = a.H; K = a.I; break;
   }
+  tile_range((N + 15) / 16, r.t_lo, r.t_hi);
+  r.gpr = K / kGroup;
+  r.blk = q4_block_bytes(R);
+  r.cap = kFStageBytes / r.blk;
+  r.src = w + (size_t)r.t_lo * r.gpr * r.blk;
+  return r;
 }
 
-__device__ __forceinline__ void iter_begin(const FusedArgs& a, UnitIter& it) {
-  it.tok = 0;
-  it.li = 0;
-  it.kind = P_QKV;
-  it.u = 0;
-  it.done = false;
-  iter_load(a, it);
+__device__ __forceinline__ Run run_lm(const FusedArgs& a) {
+  Run r;
+  tile_range((a.V + 15) / 16, r.t_lo, r.t_hi);
+  r.gpr = (a.H + kGroup - 1) / kGroup;
+  r.blk = kQ8Block;
+  r.cap = kFStageBytes / kQ8Block;
+  r.src = a.lm + (size_t)r.t_lo * r.gpr * kQ8Block;
+  return r;
 }
 
-__device__ __forceinline__ void iter_next(const FusedArgs& a, UnitIter& it) {
-  if (++it.u < it.nu) return;
-  it.u = 0;
-  if (it.kind == P_LM) {
-    it.tok++;
-    it.li = 0;
-    it.kind = P_QKV;
-  } else if (it.kind == P_DOWN) {
-    it.li++;
-    it.kind = it.li == a.layers_n ? P_LM : P_QKV;
-  } else {
-    it.kind++;
-  }
-  iter_load(a, it);
-}
-
-__device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
-  if (!bytes) return;
-  const uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
-  const uint32_t n = (uint32_t)((reinterpret_cast<uintptr_t>(p) + bytes - a + 15) & ~uintptr_t(15));
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(n) : "memory");
-}
-
-// Copy list of a unit: lane `lane` handles weight copy (src, bytes -> dst)
-// and, for row-wise units, its row's scale span.
-__device__ __forceinline__ void unit_copy(const UnitIter& it, int lane, const char*& src,
-                                          uint32_t& bytes, uint32_t& dst, const char*& ssrc,
-                                          uint32_t& sbytes) {
-  uint32_t soff;
-  ssrc = nullptr;
-  sbytes = 0;
-  dst = lane * kSegBytes;
-  if (contiguous(it.g, it.kind)) {
-    src = lane < 4 ? contig_copy(it.g, it.kind, it.u, lane, bytes, dst) : nullptr;
-    if (lane >= 4) bytes = 0;
-  } else {
-    src = seg_src(it.g, it.kind, it.u, lane, bytes);
-    ssrc = scale_src(it.g, it.kind, it.u, lane, sbytes, soff);
-  }
-}
-
-__device__ void producer(const FusedArgs& a, unsigned char* ring, uint64_t* full, uint64_t* empty) {
-  const int lane = threadIdx.x & 31;
-  UnitIter it, ahead;
-  iter_begin(a, it);
-  iter_begin(a, ahead);
-  // the L2 prefetch cursor runs l2_ahead units in front of the ring
-  for (int i = 0; i < a.l2_ahead && !ahead.done; i++) {
-    const char *src, *ssrc;
-    uint32_t bytes, dst, sbytes;
-    unit_copy(ahead, lane, src, bytes, dst, ssrc, sbytes);
-    if (bytes) l2_prefetch(src, bytes);
-    if (sbytes) l2_prefetch(ssrc, sbytes);
-    iter_next(a, ahead);
-  }
-  for (uint32_t n = 0; !it.done; n++, iter_next(a, it)) {
-    if (!ahead.done) {
-      const char *src, *ssrc;
-      uint32_t bytes, dst, sbytes;
-      unit_copy(ahead, lane, src, bytes, dst, ssrc, sbytes);
-      if (bytes) l2_prefetch(src, bytes);
-      if (sbytes) l2_prefetch(ssrc, sbytes);
-      iter_next(a, ahead);
-    }
-    const int st = n % kStages;
-    const uint32_t round = n / kStages;
-    if (!mbar_wait(&empty[st], (round & 1) ^ 1, a.err)) return;
-    const char *src, *ssrc;
-    uint32_t bytes, dst, sbytes;
-    unit_copy(it, lane, src, bytes, dst, ssrc, sbytes);
-    if (a.diag == 1) bytes = sbytes = 0;
-    uint32_t total = bytes + sbytes;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-    if (lane == 0)
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
-                       smem_addr(&full[st])),
-                   "r"(total)
-                   : "memory");
-    __syncwarp();
-    unsigned char* stage = ring + (size_t)st * kStageBytes;
-    if (bytes)
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
-          "[%3];" ::"r"(smem_addr(stage + dst)),
-          "l"(src), "r"(bytes), "r"(smem_addr(&full[st]))
-          : "memory");
-    if (sbytes)
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
-          "[%3];" ::"r"(smem_addr(stage + kSegs * kSegBytes + lane * kScaleSeg)),
-          "l"(ssrc), "r"(sbytes), "r"(smem_addr(&full[st]))
-          : "memory");
-  }
-}
-
-// ---------------------------------------------------------------- consumers
-// Ring position of the consumer group (same unit sequence as the producer).
-struct Cursor {
-  uint32_t n;
-};
-
-// An int4 GEMV phase: all of this CTA's units, epilogue per completed slot pair.
-__device__ __forceinline__ void slot_rows(const Geo& g, int p, int slot, int& rbase, bool& valid) {
-  if (g.pair) {
-    const int tile = g.t0 + 2 * p + slot;
-    valid = tile < g.t1;
-    rbase = tile * 16;
-  } else {
-    valid = true;
-    rbase = (g.t0 + p) * 16 + (slot ? g.N : 0);
-  }
-}
-
-template <int MAXU, bool NORM>
-__device__ __forceinline__ void gemv4_phase(const FusedArgs& a, const Geo g, int kind, Cursor& cur,
-                                            const unsigned char* ring, uint64_t* full,
-                                            uint64_t* empty, const XSrc& xsrc, uint4* xs_base,
-                                            float* sred, float (*red)[kConsumerWarps][2][16],
-                                            const Epi& epi) {
-  const int nu = units_of(g, kind);
-  // epilogue thread (slot, i): row of the first unit, its residual/bias read now
-  const int eslot = threadIdx.x >> 4, ei = threadIdx.x & 15;
-  float pre = 0.f;
-  if (threadIdx.x < 32 && nu) {
-    int rb;
-    bool ok;
-    slot_rows(g, 0, eslot, rb, ok);
-    if (ok && (g.pair || eslot == 0)) pre = epi_pre(epi, rb + ei);
-  }
-  const int e = stage_x<MAXU, NORM>(xsrc, g.K, 4, xs_base, sred);
-  mark(1);
-  if (!nu) return;
-  const int K8 = g.K / 8, gpr = g.K / kGroup;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int gq = lane >> 2, t = lane & 3;
-  const uint4* xs = gq == 0 ? xs_base : xs_base + K8 + 4;
-  const bool bl = gq < 2;
-  const int sstr = scale_stride(g, kind);
-  float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-  int pairs_done = 0;
-  for (int u = 0; u < nu; u++, cur.n++) {
-    const int p = u / g.nk, k = u % g.nk;
-    const int ng = min(16, (g.K - k * kChunkK) / kGroup);
-    int rbase[2];
-    bool sv[2];
-    slot_rows(g, p, 0, rbase[0], sv[0]);
-    slot_rows(g, p, 1, rbase[1], sv[1]);
-    bool gv[2];
-#pragma unroll
-    for (int i = 0; i < 2; i++) gv[i] = warp + 8 * i < ng && a.diag != 2;
-    const int st = cur.n % kStages;
-    if (a.diag != 3) mbar_wait(&full[st], (cur.n / kStages) & 1, a.err);
-    if (u == 0) mark(2);
-    const unsigned char* stage = ring + (size_t)st * kStageBytes;
-    const unsigned char* sstage = stage + kSegs * kSegBytes;
-    // this warp's two groups in turn, 4 independent accumulator chains each
-    float sa[2][2], sb[2][2];
-    if (t == 0) {
-#pragma unroll
-      for (int i = 0; i < 2; i++)
-#pragma unroll
-        for (int slot = 0; slot < 2; slot++) {
-          const int Gl = warp + 8 * i;
-          const int ra = rbase[slot] + gq, rb = ra + 8;
-          const int oa = sstr == kScaleSeg ? (int)((((size_t)ra * gpr + k * 16) * 4) & 15) : 0;
-          const int ob = sstr == kScaleSeg ? (int)((((size_t)rb * gpr + k * 16) * 4) & 15) : 0;
-          const bool ok = gv[i] && sv[slot];
-          sa[i][slot] = ok ? *reinterpret_cast<const float*>(sstage + (16 * slot + gq) * sstr + oa + 4 * Gl) : 0.f;
-          sb[i][slot] = ok ? *reinterpret_cast<const float*>(sstage + (16 * slot + gq + 8) * sstr + ob + 4 * Gl) : 0.f;
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      if (!gv[i]) continue;
-      const int Gl = warp + 8 * i;
-      uint4 X[4];
-#pragma unroll
-      for (int j = 0; j < 4; j++) X[j] = bl ? xs[16 * (k * 16 + Gl) + 4 * j + t] : make_uint4(0, 0, 0, 0);
-      uint4 A[2], B[2];
-#pragma unroll
-      for (int slot = 0; slot < 2; slot++) {
-        const unsigned char* ra = stage + (16 * slot + gq) * kSegBytes + Gl * 64 + t * 16;
-        A[slot] = sv[slot] ? *reinterpret_cast<const uint4*>(ra) : make_uint4(0, 0, 0, 0);
-        B[slot] = sv[slot] ? *reinterpret_cast<const uint4*>(ra + 8 * kSegBytes) : make_uint4(0, 0, 0, 0);
-      }
-      float c[2][2][4];
-#pragma unroll
-      for (int slot = 0; slot < 2; slot++)
-#pragma unroll
-        for (int h = 0; h < 2; h++) c[slot][h][0] = c[slot][h][1] = c[slot][h][2] = c[slot][h][3] = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; j++)
-#pragma unroll
-        for (int slot = 0; slot < 2; slot++) {
-          const uint32_t wa = j == 0 ? A[slot].x : j == 1 ? A[slot].y : j == 2 ? A[slot].z : A[slot].w;
-          const uint32_t wb = j == 0 ? B[slot].x : j == 1 ? B[slot].y : j == 2 ? B[slot].z : B[slot].w;
-          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-          deq_int4(wa, a0, a1, a2, a3);
-          deq_int4(wb, b0, b1, b2, b3);
-          mma16816(c[slot][j & 1], a0, b0, a1, b1, X[j].x, X[j].y);
-          mma16816(c[slot][j & 1], a2, b2, a3, b3, X[j].z, X[j].w);
-        }
-      if (t == 0) {
-#pragma unroll
-        for (int slot = 0; slot < 2; slot++) {
-          const float* c0 = c[slot][0];
-          const float* c1 = c[slot][1];
-          acc[slot][0] = fmaf(sa[i][slot], (c0[0] + c1[0]) + (c0[1] + c1[1]), acc[slot][0]);
-          acc[slot][1] = fmaf(sb[i][slot], (c0[2] + c1[2]) + (c0[3] + c1[3]), acc[slot][1]);
+// ---------------------------------------------------------------- barrier
+// Monotonic arrival counter: the k-th barrier completes when the counter
+// reaches k * gridDim.x.  Called by all consumer threads; thread 0 first
+// waits until the epilogue warp has finished this phase (`epi`: its
+// monotonic count of finished phases reaches pdone + 1; a count, not an
+// mbarrier phase, because a CTA without tiles in a phase lets the epilogue
+// warp finish two phases back to back), then arrives and polls.  Returns
+// false, uniformly, when the launch is being abandoned.
+__device__ bool phase_barrier(const FusedArgs& a, unsigned& epoch, const int* epi_done,
+                              int& pdone, bool epi, int* s_ok, int prof_ph) {
+  constexpr int NT = kG4Warps * 32;
+  bar_sync_n<NT>();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    if (epi) {
+      pdone++;
+      const unsigned long long t0 = gtime();
+      for (long long spins = 0; *(volatile const int*)epi_done < pdone; spins++) {
+        if ((spins & 255) == 255 && (err_set(a.err) || gtime() - t0 > kBarrierTimeoutNs)) {
+          atomicExch(a.err, 1);
+          ok = 0;
+          break;
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
-    if (u == nu - 1) mark(3);
-    if (k == g.nk - 1) {  // slot pair complete: reduce over warps, epilogue
-      float (*rb)[2][16] = red[pairs_done & 1];  // double buffered: one barrier per pair
-      if (t == 0) {
-#pragma unroll
-        for (int slot = 0; slot < 2; slot++) {
-          rb[warp][slot][gq] = acc[slot][0];
-          rb[warp][slot][gq + 8] = acc[slot][1];
-        }
-      }
-      acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
-      cta_sync();
-      if (threadIdx.x < 32) {
-        int rbs;
-        bool ok;
-        slot_rows(g, p, eslot, rbs, ok);
-        float v0 = 0.f, v1 = 0.f;
-        for (int ww = 0; ww < kConsumerWarps; ww++) {
-          v0 += rb[ww][0][ei];
-          v1 += rb[ww][1][ei];
-        }
-        if (e) {
-          v0 = ldexpf(v0, e);
-          v1 = ldexpf(v1, e);
-        }
-        if (pairs_done > 0 && ok && (g.pair || eslot == 0)) pre = epi_pre(epi, rbs + ei);
-        if (g.pair) {
-          if (ok) epilogue_row_pre(epi, rbs + ei, eslot ? v1 : v0, 0.f, pre);
-        } else if (eslot == 0) {
-          epilogue_row_pre(epi, rbs + ei, v0, v1, pre);  // gate, up
-        }
-      }
-      pairs_done++;
-    }
-  }
-  cta_sync();
-}
-
-// int8 LM head phase + this CTA's argmax candidate.
-__device__ __forceinline__ void lm_phase(const FusedArgs& a, const Geo g, Cursor& cur, const unsigned char* ring,
-                         uint64_t* full, uint64_t* empty, uint2* xs2_base, float* sred,
-                         float (*red)[2][16], float& bv, uint32_t& bi) {
-  XSrc xf = {};
-  xf.mode = X_RMS;
-  xf.x = a.hidden;
-  xf.norm_g = a.final_norm;
-  xf.eps = a.eps;
-  xf.f16 = a.f16;
-  const int e = stage_x<1>(xf, a.H, 8, xs2_base, sred);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int gq = lane >> 2, t = lane & 3;
-  const uint2* xs = gq == 0 ? xs2_base : xs2_base + a.H / 4 + 2;
-  const bool bl = gq < 2;
-  const int nch = a.H / 64;
-  const int nu = units_of(g, P_LM);
-  for (int u = 0; u < nu; u++, cur.n++) {
-    const int tile = g.t0 + u;
-    const int n = tile * 16 + threadIdx.x;
-    const int st = cur.n % kStages;
-    if (a.diag != 3) mbar_wait(&full[st], (cur.n / kStages) & 1, a.err);
-    const unsigned char* stage = ring + (size_t)st * kStageBytes;
-    const float srow = threadIdx.x < 16 && n < a.V
-                           ? *reinterpret_cast<const float*>(stage + kSegs * kSegBytes + 4 * threadIdx.x)
-                           : 0.f;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int Ch = warp; Ch < (a.diag == 2 ? 0 : nch); Ch += kConsumerWarps) {
-      const int off = (Ch & 15) * 64 + t * 16, h = Ch >> 4;
-      const uint4 A = *reinterpret_cast<const uint4*>(stage + (2 * gq + h) * kSegBytes + off);
-      const uint4 B = *reinterpret_cast<const uint4*>(stage + (2 * (gq + 8) + h) * kSegBytes + off);
-      const uint4* xp = reinterpret_cast<const uint4*>(xs + 16 * Ch + 4 * t);
-      const uint4 x01 = bl ? xp[0] : make_uint4(0, 0, 0, 0);
-      const uint4 x23 = bl ? xp[1] : make_uint4(0, 0, 0, 0);
-      uint32_t a0, a1, b0, b1;
-      deq_int8(A.x, a0, a1);
-      deq_int8(B.x, b0, b1);
-      mma16816(c, a0, b0, a1, b1, x01.x, x01.y);
-      deq_int8(A.y, a0, a1);
-      deq_int8(B.y, b0, b1);
-      mma16816(c, a0, b0, a1, b1, x01.z, x01.w);
-      deq_int8(A.z, a0, a1);
-      deq_int8(B.z, b0, b1);
-      mma16816(c, a0, b0, a1, b1, x23.x, x23.y);
-      deq_int8(A.w, a0, a1);
-      deq_int8(B.w, b0, b1);
-      mma16816(c, a0, b0, a1, b1, x23.z, x23.w);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (t == 0) {
-      red[warp][0][gq] = c[0] + c[1];
-      red[warp][0][gq + 8] = c[2] + c[3];
-    }
-    cta_sync();
-    if (threadIdx.x < 16) {
-      float aa = 0.f;
-      for (int ww = 0; ww < kConsumerWarps; ww++) aa += red[ww][0][threadIdx.x];
-      if (n < a.V) {
-        const float o = __fmul_rn(e ? ldexpf(aa, e) : aa, srow);  // sum first, scale last
-        a.logits[n] = o;
-        if (beats(o, (uint32_t)n, bv, bi)) {
-          bv = o;
-          bi = (uint32_t)n;
+    if (a.prof && prof_ph >= 0) atomicMax(a.prof + 2 * prof_ph + 1, gtime());
+    epoch += 1;
+    const unsigned target = epoch * gridDim.x;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+    const unsigned long long t0 = gtime();
+    for (long long spins = 0; ok; spins++) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+      if (v >= target) break;
+      if ((spins & 255) == 255) {
+        if (err_set(a.err)) {
+          ok = 0;
+        } else if (gtime() - t0 > kBarrierTimeoutNs) {
+          atomicExch(a.err, 1);
+          ok = 0;
         }
       }
     }
-    cta_sync();
+    if (err_set(a.err)) ok = 0;
+    *s_ok = ok;
   }
-}
-
-__device__ __forceinline__ unsigned long long gtime() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-// Phase profile hooks (token 0 only; no-ops unless a.prof is set).
-__device__ __forceinline__ void prof_start(const FusedArgs& a, int tok, int ph) {
-  if (a.prof && tok == 0 && blockIdx.x == 0 && threadIdx.x == 0) a.prof[2 * ph] = gtime();
-  // intra-phase marks: layer 2 of token 0, on CTA 1 (holds a tile of every matrix)
-  if (threadIdx.x == 0) s_mark_base = (tok == 0 && ph / 5 == 2 && blockIdx.x == 1) ? (ph % 5) * 16 : -1;
-  mark(0);
-}
-__device__ __forceinline__ void prof_end(const FusedArgs& a, int tok, int ph) {
-  mark(15);
-  if (a.prof && tok == 0) {
-    cta_sync();
-    if (threadIdx.x == 0) atomicMax(a.prof + 2 * ph + 1, gtime());
-  }
+  bar_sync_n<NT>();
+  return *s_ok != 0;
 }
 
 // ---------------------------------------------------------------- the kernel
+// 18 warps: the register file is allocated to them in 4-warp units (20
+// warps' worth), so a thread gets at most 96 registers.
 template <typename KVT>
-__global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(FusedArgs a) {
-  extern __shared__ __align__(1024) unsigned char dsm[];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
+__global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int kFStages) {
+  constexpr int NT = kG4Warps * 32;
+  extern __shared__ __align__(128) unsigned char dsm[];
   __shared__ float sred[32];
-  __shared__ float red[2][kConsumerWarps][2][16];
-  __shared__ float best_v[kConsumerWarps];
-  __shared__ uint32_t best_i[kConsumerWarps];
-  __shared__ int last_cta;
-  unsigned char* ring = dsm;
-  unsigned char* scratch = dsm + kStages * kStageBytes;
+  __shared__ TileRed<1> red1;
+  __shared__ TileRed<2> red2;
+  __shared__ AttnSmem asm_;
+  __shared__ int epi_done;  // phases the epilogue warp has finished
+  __shared__ int s_ok;
+  __shared__ uint32_t s_id;
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm);
+  uint64_t* empty = full + kFStages;
+  uint64_t* tile_full = empty + kFStages;
+  uint64_t* tile_free = tile_full + 2;
+  unsigned char* xreg = dsm + kFBarBytes;  // activation digit planes
+  unsigned char* ring = xreg + xbytes;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int L = a.layers_n;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; i++) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[i])) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(&empty[i])),
-                   "r"(kConsumerWarps)
-                   : "memory");
+    for (int i = 0; i < kFStages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kG4Warps);
     }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&tile_full[i], kG4Warps);
+      mbar_init(&tile_free[i], 1);
+    }
+    epi_done = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (threadIdx.x >= kCtaThreads) {  // producer warp
-    if (a.diag != 3) producer(a, ring, full, empty);
+  RingPos rp = {0, 0};
+  int tj = 0;
+  const int phs[4] = {PH_QKV, PH_O, PH_GU, PH_DOWN};
+
+  if (warp == kG4Warps) {  // ---------------------------------------- producer
+    int issued = 0;
+    bool ok = true;
+    for (int tok = 0; tok < a.n_tokens && ok; tok++) {
+      for (int li = 0; li < L && ok; li++)
+        for (int k = 0; k < 4 && ok; k++) {
+          const Run r = run_of(a, a.layers[li], phs[k]);
+          ok = ring_produce(ring, full, empty, kFStages, kFStageBytes, r.src,
+                            (r.t_hi - r.t_lo) * r.gpr, r.cap, r.blk, rp, issued, a.err, lane);
+        }
+      if (ok && lm_runs(a, tok)) {
+        const Run r = run_lm(a);
+        ok = ring_produce(ring, full, empty, kFStages, kFStageBytes, r.src,
+                          (r.t_hi - r.t_lo) * r.gpr, r.cap, r.blk, rp, issued, a.err, lane);
+      }
+    }
+    ring_drain(full, kFStages, rp, issued);
     return;
   }
 
+  if (warp == kG4Warps + 1) {  // ------------------------------------ epilogue
+    for (int tok = 0; tok < a.n_tokens; tok++) {
+      for (int li = 0; li < L; li++) {
+        const FusedLayer& l = a.layers[li];
+        for (int k = 0; k < 4; k++) {
+          const int ph = phs[k];
+          const Run r = run_of(a, l, ph);
+          Epi e = {};
+          bool ok;
+          if (ph == PH_GU) {
+            e.mode = EPI_SILU;
+            e.y = a.tmp;
+            e.N = a.I;
+            ok = epilogue_q4_run<2>(e, r.t_lo, r.t_hi, red2, tile_full, tile_free, tj, false, a.err);
+          } else {
+            if (ph == PH_QKV) {  // q/k/v rows + bias
+              e.mode = EPI_STORE;
+              e.y = a.qkv;
+              e.bias = l.qkv_b;
+              e.N = a.QD + 2 * a.KVD;
+            } else {  // GEMV4_ADD: hidden += W x (runtime.js:1531, :1566)
+              e.mode = EPI_ADD;
+              e.y = a.hidden;
+              e.N = a.H;
+            }
+            e.split1 = e.split2 = e.N;
+            ok = epilogue_q4_run<1>(e, r.t_lo, r.t_hi, red1, tile_full, tile_free, tj, false, a.err);
+          }
+          if (!ok) return;
+          __threadfence();  // the phase's outputs are visible GPU-wide ...
+          __syncwarp();
+          if (lane == 0) atomicAdd(&epi_done, 1);  // ... before the count moves
+        }
+      }
+      if (lm_runs(a, tok)) {
+        const Run r = run_lm(a);
+        float bv = -1e30f;
+        uint32_t bi = 0xffffffffu;
+        if (!epilogue_q8_run(a.emb_s, a.logits, a.V, r.t_lo, r.t_hi, red1, tile_full, tile_free, tj,
+                             bv, bi, a.err))
+          return;
+        if (lane == 0) {
+          a.cand_v[blockIdx.x] = bv;
+          a.cand_i[blockIdx.x] = bi;
+        }
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(&epi_done, 1);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
   unsigned epoch = 0;
-  Cursor cur{0};
-  const int L = a.layers_n, H = a.H, QD = a.QD, KVD = a.KVD, I = a.I;
-  const int NQKV = QD + 2 * KVD;
-  uint4* xs = reinterpret_cast<uint4*>(scratch);
+  int pdone = 0;
+  bool dead = false;
+  uint2* xb = reinterpret_cast<uint2*>(xreg);
+  // the first input token is ids[start_pos]; later ones come from the
+  // previous LM head (greedy) or from ids[] (prefill)
+  bool have_id = false;
+  uint32_t next_id = 0;
   for (int tok = 0; tok < a.n_tokens; tok++) {
     const int pos = a.start_pos + tok;
     for (int li = 0; li < L; li++) {
       const FusedLayer& l = a.layers[li];
-      const int ph = li * 5;
+      const int pb = tok == 0 ? li * 5 : -1000;  // profile index base (token 0)
+      const bool prof0 = a.prof && tok == 0 && blockIdx.x == 0 && threadIdx.x == 0;
       // ---- QKV: (embed +) RMSNorm prologue, q/k/v rows + bias
-      prof_start(a, tok, ph);
+      if (prof0) a.prof[2 * pb] = gtime();
       {
-        XSrc xa = {};
-        xa.mode = li == 0 ? X_EMBED_RMS : X_RMS;
-        xa.x = a.hidden;
-        xa.norm_g = l.in_norm;
-        xa.eps = a.eps;
-        xa.f16 = a.f16;
-        xa.emb_w = a.emb_w;
-        xa.emb_s = a.emb_s;
-        xa.ids = a.ids;
-        xa.fixed_pos = pos;
-        xa.hidden_out = a.hidden;
-        Epi ep = {};
-        ep.mode = EPI_STORE;
-        ep.y = a.qkv;
-        ep.bias = l.qkv_b;
-        ep.N = NQKV;
-        ep.split1 = ep.split2 = NQKV;
-        gemv4_phase<1, true>(a, geo(a, l, P_QKV), P_QKV, cur, ring, full, empty, xa, xs, sred, red, ep);
+        const Run r = run_of(a, l, PH_QKV);
+        const int gpr = a.H / kGroup;
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        float* xmul = reinterpret_cast<float*>(xcor + 2 * gpr);
+        XSrc x = {};
+        x.mode = li == 0 ? X_EMBED_RMS : X_RMS;
+        x.x = a.hidden;
+        x.norm_g = l.in_norm;
+        x.eps = a.eps;
+        x.f16 = a.f16;
+        x.emb_w = a.emb_w;
+        x.emb_s = a.emb_s;
+        x.ids = a.ids;
+        x.fixed_pos = pos;
+        x.use_fixed_id = have_id ? 1 : 0;
+        x.fixed_id = next_id;
+        x.hidden_out = a.hidden;
+        if (r.t_lo < r.t_hi) {
+          stage_xd<1, true, NT>(x, a.H, xb, xcor, xmul, sred, 0);
+          consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+                            xb, xcor, xmul, red1, tile_full, tile_free, rp, tj, dead, a.err);
+        }
       }
-      prof_end(a, tok, ph);
-      if (!grid_barrier(a.bar, a.err, epoch)) return;
-      // ---- attention: RoPE, KV append, split-K, last-item combine
-      prof_start(a, tok, ph + 1);
+      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb : -1)) return;
+      // ---- attention: RoPE, KV append, split partials, merge
+      if (prof0) a.prof[2 * (pb + 1)] = gtime();
       {
         AttnArgs at = {};
         at.qkv = a.qkv;
@@ -690,6 +305,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(FusedArg
         at.nh = a.nh;
         at.nkv = a.nkv;
         at.max_splits = a.max_splits;
+        at.ctx_bound = pos + 1;
         at.kv_f16 = a.f16;
         at.chunk = a.attn_chunk;
         at.pm = a.pm;
@@ -697,83 +313,98 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(FusedArg
         at.po = a.po;
         at.out = a.attn;
         at.counters = a.attn_counters;
-        const int chunk = attn_chunk(pos + 1, a.attn_chunk);
-        const int ns = (pos + chunk) / chunk;
-        for (int it = blockIdx.x; it < ns * a.nkv; it += gridDim.x)
-          attn_item<KVT>(at, it % ns, it / ns, reinterpret_cast<float*>(scratch), 0);
+        const int keys = a.attn_chunk > 0 ? a.attn_chunk : kAttnKeys;
+        const int items = (pos + keys) / keys * a.nh;
+        for (int it = blockIdx.x; it < items; it += gridDim.x)
+          attn_head_item<KVT>(at, it % a.nh, it / a.nh, 0, asm_);
       }
-      prof_end(a, tok, ph + 1);
-      if (!grid_barrier(a.bar, a.err, epoch)) return;
+      if (!phase_barrier(a, epoch, &epi_done, pdone, false, &s_ok, tok == 0 ? pb + 1 : -1)) return;
       // ---- O projection + residual
-      prof_start(a, tok, ph + 2);
+      if (prof0) a.prof[2 * (pb + 2)] = gtime();
       {
-        XSrc xo = {};
-        xo.mode = X_PLAIN;
-        xo.x = a.attn;
-        Epi ep = {};
-        ep.mode = EPI_ADD;
-        ep.y = a.hidden;
-        ep.N = H;
-        ep.split1 = ep.split2 = H;
-        gemv4_phase<1, false>(a, geo(a, l, P_O), P_O, cur, ring, full, empty, xo, xs, sred, red, ep);
+        const Run r = run_of(a, l, PH_O);
+        const int gpr = a.QD / kGroup;
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        float* xmul = reinterpret_cast<float*>(xcor + 2 * gpr);
+        XSrc x = {};
+        x.mode = X_PLAIN;
+        x.x = a.attn;
+        if (r.t_lo < r.t_hi) {
+          stage_xd<1, false, NT>(x, a.QD, xb, xcor, xmul, sred, 0);
+          consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+                            xb, xcor, xmul, red1, tile_full, tile_free, rp, tj, dead, a.err);
+        }
       }
-      prof_end(a, tok, ph + 2);
-      if (!grid_barrier(a.bar, a.err, epoch)) return;
+      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 2 : -1)) return;
       // ---- gate/up + SiLU
-      prof_start(a, tok, ph + 3);
+      if (prof0) a.prof[2 * (pb + 3)] = gtime();
       {
-        XSrc xb = {};
-        xb.mode = X_RMS;
-        xb.x = a.hidden;
-        xb.norm_g = l.post_norm;
-        xb.eps = a.eps;
-        xb.f16 = a.f16;
-        Epi ep = {};
-        ep.mode = EPI_SILU;
-        ep.y = a.tmp;
-        ep.N = I;
-        gemv4_phase<1, true>(a, geo(a, l, P_GU), P_GU, cur, ring, full, empty, xb, xs, sred, red, ep);
+        const Run r = run_of(a, l, PH_GU);
+        const int gpr = a.H / kGroup;
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        float* xmul = reinterpret_cast<float*>(xcor + 2 * gpr);
+        XSrc x = {};
+        x.mode = X_RMS;
+        x.x = a.hidden;
+        x.norm_g = l.post_norm;
+        x.eps = a.eps;
+        x.f16 = a.f16;
+        if (r.t_lo < r.t_hi) {
+          stage_xd<1, true, NT>(x, a.H, xb, xcor, xmul, sred, 0);
+          consume_q4_run<2>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+                            xb, xcor, xmul, red2, tile_full, tile_free, rp, tj, dead, a.err);
+        }
       }
-      prof_end(a, tok, ph + 3);
-      if (!grid_barrier(a.bar, a.err, epoch)) return;
+      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 3 : -1)) return;
       // ---- down projection + residual
-      prof_start(a, tok, ph + 4);
+      if (prof0) a.prof[2 * (pb + 4)] = gtime();
       {
-        XSrc xd = {};
-        xd.mode = X_PLAIN;
-        xd.x = a.tmp;
-        Epi ep = {};
-        ep.mode = EPI_ADD;
-        ep.y = a.hidden;
-        ep.N = H;
-        ep.split1 = ep.split2 = H;
-        gemv4_phase<6, false>(a, geo(a, l, P_DOWN), P_DOWN, cur, ring, full, empty, xd, xs, sred, red, ep);
+        const Run r = run_of(a, l, PH_DOWN);
+        const int gpr = a.I / kGroup;
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        float* xmul = reinterpret_cast<float*>(xcor + 2 * gpr);
+        XSrc x = {};
+        x.mode = X_PLAIN;
+        x.x = a.tmp;
+        if (r.t_lo < r.t_hi) {
+          stage_xd<3, false, NT>(x, a.I, xb, xcor, xmul, sred, 0);
+          consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+                            xb, xcor, xmul, red1, tile_full, tile_free, rp, tj, dead, a.err);
+        }
       }
-      prof_end(a, tok, ph + 4);
-      if (!grid_barrier(a.bar, a.err, epoch)) return;
+      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 4 : -1)) return;
     }
-    // ---- LM head (int8 rows) + argmax + token advance
-    if (!lm_runs(a, tok)) continue;
-    prof_start(a, tok, 5 * L);
-    float bv = -1e30f;
-    uint32_t bi = 0xffffffffu;
-    lm_phase(a, geo(a, a.layers[0], P_LM), cur, ring, full, empty, reinterpret_cast<uint2*>(scratch),
-             sred, red[0], bv, bi);
-    if (a.greedy) {
-      // per-CTA best, then the last CTA to arrive reduces (ARGMAX, kernels.js:771-784)
-      block_best(bv, bi, best_v, best_i);
-      if (threadIdx.x == 0) {
-        a.cand_v[blockIdx.x] = bv;
-        a.cand_i[blockIdx.x] = bi;
-        __threadfence();
-        last_cta = atomicAdd(a.lm_counter, 1u) == gridDim.x - 1;
+    // ---- LM head (int8) + argmax + token advance
+    if (!lm_runs(a, tok)) {
+      have_id = false;  // the next input is ids[pos + 1] (prefill)
+      continue;
+    }
+    const int pl = 5 * L;
+    if (a.prof && tok == 0 && blockIdx.x == 0 && threadIdx.x == 0) a.prof[2 * pl] = gtime();
+    {
+      const Run r = run_lm(a);
+      uint32_t* xb8 = reinterpret_cast<uint32_t*>(xreg);
+      float* xm8 = reinterpret_cast<float*>(xb8 + (size_t)r.gpr * 128);
+      XSrc x = {};
+      x.mode = X_RMS;
+      x.x = a.hidden;
+      x.norm_g = a.final_norm;
+      x.eps = a.eps;
+      x.f16 = a.f16;
+      if (r.t_lo < r.t_hi) {
+        stage_xd8<1, true, NT>(x, a.H, r.gpr * kGroup, xb8, xm8, sred, 0);
+        consume_q8_run(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr, xb8,
+                       xm8, red1, tile_full, tile_free, rp, tj, dead, a.err);
       }
-      cta_sync();
-      if (last_cta) {
-        __threadfence();
+    }
+    if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pl : -1)) return;
+    if (a.greedy) {
+      // every CTA merges the candidates (ARGMAX, kernels.js:771-784); ties
+      // to the lower index
+      if (warp == 0) {
         float v = -1e30f;
         uint32_t id = 0xffffffffu;
-        for (int b = threadIdx.x; b < (int)gridDim.x; b += kCtaThreads) {
+        for (int b = lane; b < (int)gridDim.x; b += 32) {
           const float cv = __ldcg(a.cand_v + b);
           const uint32_t ci = __ldcg(a.cand_i + b);
           if (beats(cv, ci, v, id)) {
@@ -781,44 +412,77 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(FusedArg
             id = ci;
           }
         }
-        block_best(v, id, best_v, best_i);
-        if (threadIdx.x == 0) {
-          *a.amax = id;
-          a.ids[pos + 1] = id;
-          a.out_ids[tok] = id;
-          *a.lm_counter = 0u;
-          __threadfence();
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+          const uint32_t oi = __shfl_xor_sync(0xffffffffu, id, o);
+          if (beats(ov, oi, v, id)) {
+            v = ov;
+            id = oi;
+          }
+        }
+        if (lane == 0) {
+          s_id = id;
+          if (blockIdx.x == 0) {
+            *a.amax = id;
+            a.ids[pos + 1] = id;
+            a.out_ids[tok] = id;
+          }
         }
       }
+      bar_sync_n<NT>();
+      next_id = s_id;
+      have_id = true;
+      // the candidates are rewritten by the next LM head only after many more
+      // grid barriers, so every CTA has read them by then
+    } else {
+      have_id = false;
     }
-    prof_end(a, tok, 5 * L);
-    if (tok + 1 < a.n_tokens && !grid_barrier(a.bar, a.err, epoch)) return;
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) a.state_pos[0] = a.start_pos + a.n_tokens;
 }
 
-cudaError_t fused_set_marks(unsigned long long* buf) {
-  return cudaMemcpyToSymbol(g_marks, &buf, sizeof(buf));
+// Activation region: the largest staged vector (int4 digit planes of H, QD
+// or I; int8 digit planes of H).
+static int fused_stages() {
+  const char* v = getenv("EG_FUSED_STAGES");  // tuning only
+  const int n = v ? atoi(v) : 4;
+  return std::max(2, std::min(kFMaxStages, n));
 }
 
-int fused_smem_bytes() {
-  const int attn = kAttnMaxChunk * (kKsStride + kHeadDim) * (int)sizeof(float);
-  const int frag = (2 * (12288 / 8) + 8) * (int)sizeof(uint4);
-  return kStages * kStageBytes + std::max(attn, frag);
+static int fused_xbytes(const FusedArgs& a) {
+  const int q4 = std::max(std::max(a.H, a.QD), a.I) / kGroup * (512 + 16);
+  const int q8 = (a.H + kGroup - 1) / kGroup * (512 + 8);
+  return (std::max(q4, q8) + 127) & ~127;
+}
+
+int fused_smem_bytes(const FusedArgs& a) {
+  return kFBarBytes + fused_xbytes(a) + fused_stages() * kFStageBytes;
 }
 
 cudaError_t fused_decode(const FusedArgs& a, cudaStream_t st) {
-  const int smem = fused_smem_bytes();
-  void (*k)(FusedArgs) = a.f16 ? fused_decode_kernel<__half> : fused_decode_kernel<float>;
+  const int smem = fused_smem_bytes(a);
+  const int xbytes = fused_xbytes(a);
+  const int stages = fused_stages();
+  void (*k)(FusedArgs, int, int) = a.f16 ? fused_decode_kernel<__half> : fused_decode_kernel<float>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kFusedThreads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kG4Threads, smem);
   if (e != cudaSuccess) return e;
-  if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+  if (per_sm < 1) {
+    cudaFuncAttributes fa = {};
+    cudaFuncGetAttributes(&fa, k);
+    fprintf(stderr,
+            "fused_decode: no CTA fits an SM: %d regs/thread x %d threads, %zu B static + %d B "
+            "dynamic shared (max dynamic %d), %zu B local\n",
+            fa.numRegs, kG4Threads, fa.sharedSizeBytes, smem, fa.maxDynamicSharedSizeBytes,
+            fa.localSizeBytes);
+    return cudaErrorCooperativeLaunchTooLarge;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sm_count());
-  cfg.blockDim = dim3(kFusedThreads);
+  cfg.blockDim = dim3(kG4Threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -826,7 +490,7 @@ cudaError_t fused_decode(const FusedArgs& a, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k, a);
+  return cudaLaunchKernelEx(&cfg, k, a, xbytes, stages);
 }
 
 }  // namespace eg

@@ -26,6 +26,7 @@
 #include "eg_common.cuh"
 #include "eg_device.cuh"
 #include "eg_kernels.h"
+#include "eg_stream.cuh"
 
 namespace eg {
 
@@ -56,21 +57,15 @@ static void launch(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, 
   cudaLaunchKernelEx(&cfg, k, args...);
 }
 
-// ----------------------------------------------------------------------
-// Streaming int4 GEMV over the "stream" layout (q4_to_stream): the matrix
-// as blocks (tile, group) -- 16 rows x 128 k of packed nibbles (for
-// [gate;up] a tile is the gate tile plus its up tile), stored in MMA
-// fragment order and followed by the block's 16 (32) group scales -- laid
-// out tile-major, group-minor.  The tiles are split into gridDim.x
-// contiguous ranges, one per CTA, and any contiguous run of blocks is one
-// contiguous byte range: warp 8 moves each ring stage (<= 16 KB of nibbles)
-// with a single cp.async.bulk.  The weights do not depend on the previous
-// kernel, so those copies start before griddepcontrol.wait.  Warps 0-7 build
-// the activation fragments (stage_xg), then turn each stage into m16n8k16
-// MMAs; each warp's 16-byte fragment loads cover 512 contiguous bytes (no
-// bank conflicts).  Every tile is finished inside one CTA, so the epilogue
-// needs no cross-CTA combine (a memory fence under a saturated memory
-// system costs microseconds).
+// ======================================================================
+// Streaming int4 GEMV (GEMV4 / GEMV4_ADD / QKV / GATE_UP_SILU_GEMV4,
+// kernels.js:884-1072) over the stream layout (q4_to_stream)
+// ======================================================================
+// One CTA per SM: warps 0-15 consume, warp 16 produces, warp 17 runs the
+// epilogues (eg_stream.cuh).  The tiles are split into contiguous ranges,
+// one per CTA; every tile is finished inside one CTA, so the epilogue needs
+// no cross-CTA combine (a memory fence under a saturated memory system costs
+// microseconds).  Shared memory: barriers | activation digit planes | ring.
 struct G4Args {
   const unsigned char* ws;  // stream layout
   int N, K;
@@ -81,254 +76,84 @@ struct G4Args {
   int pdl;
 };
 
-// Block of the stream layout: R * (1024 bytes of nibbles + 64 bytes of scales).
-__host__ __device__ constexpr int q4_block_bytes(int R) { return R * 1088; }
+// Barrier block at the start of the dynamic shared memory: 2 * stages ring
+// mbarriers + 2 tile_full + 2 tile_free (stages <= 8).
+constexpr int kBarBytes = 256;
 
-
-#ifdef EG_G4_TRACE  // timeline probe (clock64 per CTA), never in library builds
-__device__ long long g4_trace[512][64];
-#define G4T(slot)                                                     \
-  do {                                                                \
-    if (lane == 0 && (slot) < 64) g4_trace[blockIdx.x][(slot)] = clock64(); \
-  } while (0)
-#else
-#define G4T(slot) \
-  do {            \
-  } while (0)
-#endif
-
-constexpr int kG4Warps = 16;                   // consumer warps per CTA (one CTA per SM)
-constexpr int kG4Threads = kG4Warps * 32 + 64;  // + producer warp + epilogue warp
-
-// Producer warp of a streaming GEMV: copy `nitems` blocks of `blk` bytes
-// from src0 into the ring, `cap` blocks (one cp.async.bulk) per stage, each
-// stage reused once all consumer warps released it.
-__device__ __forceinline__ void ring_produce(unsigned char* ring, uint64_t* full, uint64_t* empty,
-                                             int stages, int stage_bytes,
-                                             const unsigned char* src0, int nitems, int cap,
-                                             int blk, int* err, int lane) {
-  const int nchunks = (nitems + cap - 1) / cap;
-  int st = 0, ph = 0, n = 0;
-  for (; n < nchunks; n++) {
-    if (!mbar_wait(&empty[st], ph ^ 1, err)) break;
-    if (lane == 0) {
-      const uint32_t bytes = (uint32_t)(min(cap, nitems - n * cap) * blk);
-      mbar_expect_tx(&full[st], bytes);
-      bulk_g2s(ring + (size_t)st * stage_bytes, src0 + (size_t)n * cap * blk, bytes, &full[st]);
+__device__ __forceinline__ void init_ring_barriers(uint64_t* full, uint64_t* empty,
+                                                   uint64_t* tile_full, uint64_t* tile_free,
+                                                   int stages) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kG4Warps);
     }
-    __syncwarp();
-    if (++st == stages) {
-      st = 0;
-      ph ^= 1;
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&tile_full[i], kG4Warps);
+      mbar_init(&tile_free[i], 1);
     }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // every issued copy has landed before the CTA may exit (bounded even after
-  // an error elsewhere)
-  for (int k = n > stages ? n - stages : 0; k < n; k++)
-    if (!mbar_wait_bounded(&full[k % stages], (k / stages) & 1)) break;
+  __syncthreads();
 }
 
-// One CTA per SM.  Warps 0-15 consume, warp 16 produces, warp 17 runs the
-// epilogues.  The CTA's tiles form a contiguous run of blocks (items) in the
-// stream layout; the producer copies it in stages of p.cap items (one
-// cp.async.bulk each) into a ring.  Consumer warp w takes items w, w + 16,
-// w + 32, ... (so for K = 2048 every warp holds one group of every tile),
-// keeps one running sum per row pair across stages, and at the end of each
-// tile leaves its partial row sums in red[buf] for the epilogue warp.  Every
-// consumer waits on every stage and releases it, items or not, so the ring
-// protocol needs no per-warp bookkeeping.
 template <int R, int MAXU, bool NORM>
 __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
-  constexpr int CW = kG4Warps, NT = CW * 32;
+  constexpr int NT = kG4Warps * 32;
   extern __shared__ __align__(128) unsigned char g4_smem[];
   __shared__ float sred[32];
-  __shared__ float red[2][CW][R][16];  // double buffered tile hand-off
+  __shared__ TileRed<R> red;
   uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
   uint64_t* empty = full + p.stages;
-  uint64_t* tile_full = empty + p.stages;  // [2]
-  uint64_t* tile_free = tile_full + 2;     // [2]
+  uint64_t* tile_full = empty + p.stages;
+  uint64_t* tile_free = tile_full + 2;
   const int gpr = p.K / kGroup;
   uint2* xb = reinterpret_cast<uint2*>(g4_smem + p.xs_off);  // [gpr][4][4][4]
   int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);  // [gpr][2]
   float* xmul = reinterpret_cast<float*>(xcor + 2 * gpr);     // [gpr][2]
   unsigned char* ring = g4_smem + p.ring_off;
   const int tiles = (p.N + 15) / 16;
-  const int P = gridDim.x, c = blockIdx.x;
-  const int t_lo = (int)((long long)tiles * c / P), t_hi = (int)((long long)tiles * (c + 1) / P);
-  const int nitems = (t_hi - t_lo) * gpr;
-  const int cap = p.cap;
-  const int nchunks = (nitems + cap - 1) / cap;
-  const int blk = q4_block_bytes(R);
-  const unsigned char* src0 = p.ws + (size_t)t_lo * gpr * blk;
+  const int t_lo = (int)((long long)tiles * blockIdx.x / gridDim.x);
+  const int t_hi = (int)((long long)tiles * (blockIdx.x + 1) / gridDim.x);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < p.stages; i++) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CW);
-    }
-    for (int i = 0; i < 2; i++) {
-      mbar_init(&tile_full[i], CW);
-      mbar_init(&tile_free[i], 1);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (warp == 0) G4T(0);
-
-  if (warp == CW) {  // --------------------------------------------- producer
-    ring_produce(ring, full, empty, p.stages, p.stage_bytes, src0, nitems, cap, blk, p.err, lane);
+  init_ring_barriers(full, empty, tile_full, tile_free, p.stages);
+  RingPos rp = {0, 0};
+  int tj = 0;
+  if (warp == kG4Warps) {  // producer: the weights need no wait
+    int issued = 0;
+    ring_produce(ring, full, empty, p.stages, p.stage_bytes,
+                 p.ws + (size_t)t_lo * gpr * q4_block_bytes(R), (t_hi - t_lo) * gpr, p.cap,
+                 q4_block_bytes(R), rp, issued, p.err, lane);
+    ring_drain(full, p.stages, rp, issued);
     return;
   }
-
-  if (warp == CW + 1) {  // ------------------------------------------- epilogue
-    if (p.pdl) pdl_wait();  // residuals are written by earlier kernels
-    const bool lora = p.e.mods != nullptr;
-    float pre = 0.f;
-    if (lane < 16 && !lora) pre = epi_pre(p.e, t_lo * 16 + lane);
-    for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
-      const int b = j & 1;
-      if (!mbar_wait(&tile_full[b], (j >> 1) & 1, p.err)) break;
-      float v = 0.f;
-      if (lane < 16 * R)
-        for (int ww = 0; ww < CW; ww++) v += red[b][ww][lane >> 4][lane & 15];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tile_free[b]);
-      const float up = __shfl_down_sync(0xffffffffu, v, 16);
-      if (lane < 16) {
-        const int row = tile * 16 + lane;
-        if (lora)
-          epilogue_row(p.e, row, v, R == 2 ? up : 0.f);
-        else
-          epilogue_row_pre(p.e, row, v, R == 2 ? up : 0.f, pre);
-        if (!lora && tile + 1 < t_hi) pre = epi_pre(p.e, row + 16);
-      }
-    }
+  if (warp == kG4Warps + 1) {  // epilogue: residuals come from earlier kernels
+    if (p.pdl) pdl_wait();
+    epilogue_q4_run<R>(p.e, t_lo, t_hi, red, tile_full, tile_free, tj, true, p.err);
     return;
   }
-
-  // ------------------------------------------------------------- consumers
   stage_xd<MAXU, NORM, NT>(p.x, p.K, xb, xcor, xmul, sred, p.pdl);
-  // the next kernel may start once this one's predecessors are complete
-  // (the attention kernel relies on that to read the position early)
+  // the next kernel may start once this one's predecessors are complete (the
+  // attention kernel relies on that to read the position early)
   if (p.pdl) pdl_launch_dependents();
-  if (warp == 0) G4T(1);
-  const int gq = lane >> 2, t = lane & 3;
-  const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
-  float acc[R][2];
-#pragma unroll
-  for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
-  // after a failed wait the CTA runs on without waiting and its results are
-  // void; the host sees the error word
   bool dead = false;
-  int st = 0, ph = 0, chunk = 0, chunk_lo = 0;
-  if (nchunks > 0 && !mbar_wait(&full[0], 0, p.err)) dead = true;
-  const unsigned char* stage = ring;
-  int i = warp;  // item index within the CTA's run
-  for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
-    const int tile_end = (j + 1) * gpr;
-    for (; i < tile_end; i += 16) {
-      while (i >= chunk_lo + cap) {  // next stage
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-        if (++st == p.stages) {
-          st = 0;
-          ph ^= 1;
-        }
-        chunk++;
-        chunk_lo += cap;
-        stage = ring + (size_t)st * p.stage_bytes;
-        if (!dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
-        if (warp == 0) G4T(2 + chunk);
-      }
-      const int g = i - j * gpr;
-      const unsigned char* bp = stage + (size_t)(i - chunk_lo) * blk;
-      // B: digit plane gq of this group's 4 k32 blocks (zero for gq >= 4)
-      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
-      if (bl) {
-        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 4);
-        X0 = xp[0];
-        X1 = xp[1];
-      }
-      uint4 A[R], B[R];
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        // words t, 4+t, 8+t, 12+t of rows gq (A) and gq+8 (B)
-        A[r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + lane * 16);
-        B[r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + 512 + lane * 16);
-      }
-      int cc[R][4];
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        cc[r][0] = cc[r][1] = cc[r][2] = cc[r][3] = 0;
-        imma16832(cc[r], nib_lo_u8(A[r].x), nib_lo_u8(B[r].x), nib_hi_u8(A[r].x), nib_hi_u8(B[r].x), X0.x, X0.y);
-        imma16832(cc[r], nib_lo_u8(A[r].y), nib_lo_u8(B[r].y), nib_hi_u8(A[r].y), nib_hi_u8(B[r].y), X0.z, X0.w);
-        imma16832(cc[r], nib_lo_u8(A[r].z), nib_lo_u8(B[r].z), nib_hi_u8(A[r].z), nib_hi_u8(B[r].z), X1.x, X1.y);
-        imma16832(cc[r], nib_lo_u8(A[r].w), nib_lo_u8(B[r].w), nib_hi_u8(A[r].w), nib_hi_u8(B[r].w), X1.z, X1.w);
-      }
-      if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
-        const int cor = xcor[2 * g + t];
-        const float mul = xmul[2 * g + t];
-        const float* sc = reinterpret_cast<const float*>(bp + R * 1024);
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-          const float sa = sc[16 * r + gq] * mul, sb = sc[16 * r + gq + 8] * mul;
-          acc[r][0] = fmaf(sa, (float)(cc[r][0] + 256 * cc[r][1] - cor), acc[r][0]);
-          acc[r][1] = fmaf(sb, (float)(cc[r][2] + 256 * cc[r][3] - cor), acc[r][1]);
-        }
-      }
-    }
-    // ---- tile complete for this warp: hand its partial rows to the epilogue
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-      acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], 1);
-      acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], 1);
-    }
-    const int b = j & 1;
-    if (!dead && !mbar_wait(&tile_free[b], ((j >> 1) & 1) ^ 1, p.err)) dead = true;
-    if (t == 0) {
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        red[b][warp][r][gq] = acc[r][0];
-        red[b][warp][r][gq + 8] = acc[r][1];
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&tile_full[b]);
-    if (warp == 0) G4T(48 + min(j, 13));
-  }
-  // release the current stage and wait/release any later ones this warp had
-  // no items in, so every stage sees all CW arrivals
-  for (; chunk < nchunks; chunk++) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (++st == p.stages) {
-      st = 0;
-      ph ^= 1;
-    }
-    if (chunk + 1 < nchunks && !dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
-  }
-  if (warp == 0) G4T(63);
+  consume_q4_run<R>(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xcor,
+                    xmul, red, tile_full, tile_free, rp, tj, dead, p.err);
 }
 
-
-// Shared-memory plan of one launch (bytes): barriers, x fragments + group
-// multipliers, then the ring of stages of `cap` items.
+// Shared-memory plan of one launch (bytes): barriers, x digit planes + group
+// words, then the ring; ~150 KB so an attention CTA fits beside it under PDL.
 struct G4Plan {
   int stages, stage_bytes, cap, xs_off, ring_off, smem;
 };
 static G4Plan g4_plan(int R, int K) {
   G4Plan q;
   const int gpr = K / kGroup;
-  q.cap = (getenv("EG_G4_CAP") ? atoi(getenv("EG_G4_CAP")) : 32) / R;  // items per stage: 35 KB
+  q.cap = 32 / R;  // blocks per stage: 34 KB
   q.stage_bytes = q.cap * q4_block_bytes(R);
-  q.xs_off = 256;  // barriers: 2 * stages + 4 mbarriers (stages <= 8)
-  const int xbytes = gpr * (512 + 16);
-  q.ring_off = (q.xs_off + xbytes + 127) & ~127;
-  // leave room for the attention kernel's CTA (67 KB) beside this one under PDL
-  const int budget = (getenv("EG_G4_SMEM") ? atoi(getenv("EG_G4_SMEM")) : 150) * 1024;
+  q.xs_off = kBarBytes;
+  q.ring_off = (q.xs_off + gpr * (512 + 16) + 127) & ~127;
+  const int budget = 150 * 1024;
   q.stages = std::max(2, std::min(8, (budget - q.ring_off) / q.stage_bytes));
   q.smem = q.ring_off + q.stages * q.stage_bytes;
   return q;
@@ -385,7 +210,7 @@ size_t q4_stream_bytes(int N, int K, int R) {
 }
 
 // One thread per 16-byte fragment word of the stream layout; rows past N
-// are zero.  Threads with u >= the fragment count copy the scales instead.
+// are zero.  Threads past the fragment words copy the scales instead.
 __global__ void q4_to_stream_kernel(const uint32_t* __restrict__ w, const float* __restrict__ s,
                                     int N, int K, int R, unsigned char* __restrict__ out) {
   const int gpr = K / kGroup, tiles = (N + 15) / 16;
@@ -435,8 +260,6 @@ void q4_to_stream(const uint32_t* w, const float* s, int N, int K, int R, unsign
 // the group, i.e. the m16n8k32 s8 A fragments of MMAs 2 k2 and 2 k2 + 1 with
 // no unpacking.  The row scales stay a plain f32 array (applied after the
 // row sum, as the reference does).
-constexpr int kQ8Block = 2048;
-
 size_t q8_stream_bytes(int N, int K) {
   return (size_t)((N + 15) / 16) * ((K + kGroup - 1) / kGroup) * kQ8Block;
 }
@@ -479,21 +302,20 @@ struct Q8Args {
   int pdl;
 };
 
-// Same warp roles as gemv_q4_kernel.  The epilogue warp writes
-// y[n] = (row sum) * s[n] and keeps the best (value, index); with a tail, the
-// CTAs' candidates are merged by the last CTA to finish, which also advances
-// the decode position (ARGMAX kernels.js:771-784, then decodeBatch's copy of
+// Same warp roles as gemv_q4_kernel.  With a tail, the CTAs' argmax
+// candidates are merged by the last CTA to finish, which also advances the
+// decode position (ARGMAX kernels.js:771-784, then decodeBatch's copy of
 // s.amax into the id buffer, runtime.js:1783-1785).
 template <int MAXU, bool NORM>
 __global__ void __launch_bounds__(kG4Threads, 1) gemv_q8_kernel(Q8Args p) {
-  constexpr int CW = kG4Warps, NT = CW * 32;
+  constexpr int NT = kG4Warps * 32;
   extern __shared__ __align__(128) unsigned char g4_smem[];
   __shared__ float sred[32];
-  __shared__ float red[2][CW][16];
+  __shared__ TileRed<1> red;
   uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
   uint64_t* empty = full + p.stages;
-  uint64_t* tile_full = empty + p.stages;  // [2]
-  uint64_t* tile_free = tile_full + 2;     // [2]
+  uint64_t* tile_full = empty + p.stages;
+  uint64_t* tile_free = tile_full + 2;
   const int gpr = (p.K + kGroup - 1) / kGroup;
   uint32_t* xb = reinterpret_cast<uint32_t*>(g4_smem + p.xs_off);  // [gpr][4][4][4][2]
   float* xmul = reinterpret_cast<float*>(xb + (size_t)gpr * 128);  // [gpr][2]
@@ -501,63 +323,23 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q8_kernel(Q8Args p) {
   const int tiles = (p.N + 15) / 16;
   const int P = gridDim.x, c = blockIdx.x;
   const int t_lo = (int)((long long)tiles * c / P), t_hi = (int)((long long)tiles * (c + 1) / P);
-  const int nitems = (t_hi - t_lo) * gpr;
-  const int cap = p.cap;
-  const int nchunks = (nitems + cap - 1) / cap;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < p.stages; i++) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], CW);
-    }
-    for (int i = 0; i < 2; i++) {
-      mbar_init(&tile_full[i], CW);
-      mbar_init(&tile_free[i], 1);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-
-  if (warp == CW) {  // --------------------------------------------- producer
+  init_ring_barriers(full, empty, tile_full, tile_free, p.stages);
+  RingPos rp = {0, 0};
+  int tj = 0;
+  if (warp == kG4Warps) {  // producer
+    int issued = 0;
     ring_produce(ring, full, empty, p.stages, p.stage_bytes, p.ws + (size_t)t_lo * gpr * kQ8Block,
-                 nitems, cap, kQ8Block, p.err, lane);
+                 (t_hi - t_lo) * gpr, p.cap, kQ8Block, rp, issued, p.err, lane);
+    ring_drain(full, p.stages, rp, issued);
     return;
   }
-
-  if (warp == CW + 1) {  // ------------------------------------------- epilogue
-    float sc = lane < 16 && t_lo * 16 + lane < p.N ? __ldg(p.s + t_lo * 16 + lane) : 0.f;
+  if (warp == kG4Warps + 1) {  // epilogue
     float bv = -1e30f;
     uint32_t bi = 0xffffffffu;
-    for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
-      const int b = j & 1;
-      if (!mbar_wait(&tile_full[b], (j >> 1) & 1, p.err)) break;
-      float v = 0.f;
-      if (lane < 16)
-        for (int ww = 0; ww < CW; ww++) v += red[b][ww][lane];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tile_free[b]);
-      const int n = tile * 16 + lane;
-      if (lane < 16 && n < p.N) {
-        const float o = __fmul_rn(v, sc);  // sum first, scale last
-        p.y[n] = o;
-        if (beats(o, (uint32_t)n, bv, bi)) {
-          bv = o;
-          bi = (uint32_t)n;
-        }
-        sc = n + 16 < p.N && tile + 1 < t_hi ? __ldg(p.s + n + 16) : 0.f;
-      }
-    }
+    if (!epilogue_q8_run(p.s, p.y, p.N, t_lo, t_hi, red, tile_full, tile_free, tj, bv, bi, p.err))
+      return;
     if (!p.has_tail) return;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (beats(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
     const StepTail& tl = p.tail;
     unsigned prev = 0;
     if (lane == 0) {
@@ -602,78 +384,11 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q8_kernel(Q8Args p) {
     }
     return;
   }
-
-  // ------------------------------------------------------------- consumers
   stage_xd8<MAXU, NORM, NT>(p.x, p.K, gpr * kGroup, xb, xmul, sred, p.pdl);
   if (p.pdl) pdl_launch_dependents();
-  const int gq = lane >> 2, t = lane & 3;
-  const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
-  float acc0 = 0.f, acc1 = 0.f;
   bool dead = false;
-  int st = 0, ph = 0, chunk = 0, chunk_lo = 0;
-  if (nchunks > 0 && !mbar_wait(&full[0], 0, p.err)) dead = true;
-  const unsigned char* stage = ring;
-  int i = warp;
-  for (int tile = t_lo, j = 0; tile < t_hi; tile++, j++) {
-    const int tile_end = (j + 1) * gpr;
-    for (; i < tile_end; i += 16) {
-      while (i >= chunk_lo + cap) {  // next stage
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
-        if (++st == p.stages) {
-          st = 0;
-          ph ^= 1;
-        }
-        chunk++;
-        chunk_lo += cap;
-        stage = ring + (size_t)st * p.stage_bytes;
-        if (!dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
-      }
-      const int g = i - j * gpr;
-      const unsigned char* bp = stage + (size_t)(i - chunk_lo) * kQ8Block;
-      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
-      if (bl) {
-        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 8);
-        X0 = xp[0];
-        X1 = xp[1];
-      }
-      const uint4 A0 = *reinterpret_cast<const uint4*>(bp + lane * 16);
-      const uint4 A1 = *reinterpret_cast<const uint4*>(bp + 512 + lane * 16);
-      const uint4 B0 = *reinterpret_cast<const uint4*>(bp + 1024 + lane * 16);
-      const uint4 B1 = *reinterpret_cast<const uint4*>(bp + 1536 + lane * 16);
-      int cc[4] = {0, 0, 0, 0};
-      imma16832_ss(cc, A0.x, B0.x, A0.y, B0.y, X0.x, X0.y);
-      imma16832_ss(cc, A0.z, B0.z, A0.w, B0.w, X0.z, X0.w);
-      imma16832_ss(cc, A1.x, B1.x, A1.y, B1.y, X1.x, X1.y);
-      imma16832_ss(cc, A1.z, B1.z, A1.w, B1.w, X1.z, X1.w);
-      if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
-        const float mul = xmul[2 * g + t];
-        acc0 = fmaf(mul, (float)(cc[0] + 256 * cc[1]), acc0);
-        acc1 = fmaf(mul, (float)(cc[2] + 256 * cc[3]), acc1);
-      }
-    }
-    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-    const int b = j & 1;
-    if (!dead && !mbar_wait(&tile_free[b], ((j >> 1) & 1) ^ 1, p.err)) dead = true;
-    if (t == 0) {
-      red[b][warp][gq] = acc0;
-      red[b][warp][gq + 8] = acc1;
-    }
-    acc0 = acc1 = 0.f;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&tile_full[b]);
-  }
-  // release the current stage and wait/release the later ones (see gemv_q4_kernel)
-  for (; chunk < nchunks; chunk++) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (++st == p.stages) {
-      st = 0;
-      ph ^= 1;
-    }
-    if (chunk + 1 < nchunks && !dead && !mbar_wait(&full[st], ph, p.err)) dead = true;
-  }
+  consume_q8_run(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xmul, red,
+                 tile_full, tile_free, rp, tj, dead, p.err);
 }
 
 template <int MAXU, bool NORM>
@@ -682,7 +397,7 @@ static void gemv_q8_go(const Q8Args& a0, cudaStream_t st, bool pdl) {
   const int gpr = (a.K + kGroup - 1) / kGroup;
   a.cap = 16;  // 32 KB stages
   a.stage_bytes = a.cap * kQ8Block;
-  a.xs_off = 256;
+  a.xs_off = kBarBytes;
   a.ring_off = (a.xs_off + gpr * (512 + 8) + 127) & ~127;
   const int budget = 150 * 1024;
   a.stages = std::max(2, std::min(8, (budget - a.ring_off) / a.stage_bytes));
@@ -716,7 +431,6 @@ void gemv_q8(const unsigned char* ws, const float* s, int N, int K, const XSrc& 
   }
 }
 
-
 // ======================================================================
 // LoRA A: d[m][r] = A_m[r] . x  (LORA_A, kernels.js:60-78)
 // ======================================================================
@@ -744,254 +458,15 @@ void lora_a(const XSrc& x, int K, const LoraMod* mods, int nmods, int max_rank, 
 }
 
 // ======================================================================
-// Attention: RoPE + KV append + split-K partials, then combine
+// Decode attention (attn_head_item, eg_stream.cuh): grid (splits, heads)
 // ======================================================================
 int attn_max_splits(int max_ctx) { return std::max(64, (max_ctx + 15) / 16); }
 
-// ----------------------------------------------------------------------
-// Decode attention, one CTA per (query head, split of <= kAttnKeys keys).
-// Each of the 16 warps takes keys t0 + w, t0 + w + 16, ...; a lane holds 4
-// of the 128 dims.  All K and V rows of the warp are requested before
-// griddepcontrol.wait (the cache rows t != pos were written by earlier
-// steps), so the kernel pays one memory latency for them.  Each warp forms a
-// partial (m, z, sum e^(s-m) v) over its keys (ATTN_PARTIAL, kernels.js:
-// 258-345), the 16 warp partials are merged in shared memory with the
-// ATTN_COMBINE formula (kernels.js:346-388, f16 rounding of the partial
-// outputs in the f16 variant), and for contexts longer than one split the
-// CTA partials are merged once more by the last CTA of the head.  The new
-// k (RoPE) / v row of position pos is formed in registers; the first query
-// head of each KV group appends it to the cache (runtime.js:1509-1514).
-constexpr int kAttnWarps = 16;
-constexpr int kAttnKeys = 256;                   // keys per split (16 per warp)
-constexpr int kAttnKpw = kAttnKeys / kAttnWarps;
-
-// A value as the cache stores it (rounded to the cache type).
-template <typename KVT>
-__device__ __forceinline__ float kv_round(float v);
-template <>
-__device__ __forceinline__ float kv_round<float>(float v) { return v; }
-template <>
-__device__ __forceinline__ float kv_round<__half>(float v) { return round_h(v); }
-
-template <typename KVT>
-struct KvRow;  // 4 consecutive cache values of one lane
-template <>
-struct KvRow<__half> {
-  uint2 u;
-  __device__ __forceinline__ void load(const __half* p) { u = __ldcg(reinterpret_cast<const uint2*>(p)); }
-  __device__ __forceinline__ float4 get() const {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-    return make_float4(a.x, a.y, b.x, b.y);
-  }
-  __device__ __forceinline__ void set(float4 v) {  // values already f16-exact
-    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
-    u.x = *reinterpret_cast<const uint32_t*>(&a);
-    u.y = *reinterpret_cast<const uint32_t*>(&b);
-  }
-};
-template <>
-struct KvRow<float> {
-  float4 f;
-  __device__ __forceinline__ void load(const float* p) { f = __ldcg(reinterpret_cast<const float4*>(p)); }
-  __device__ __forceinline__ float4 get() const { return f; }
-  __device__ __forceinline__ void set(float4 v) { f = v; }
-};
-
 template <typename KVT>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_head_kernel(AttnArgs a, int pdl) {
-  __shared__ float wm[kAttnWarps], wz[kAttnWarps];
-  __shared__ __align__(16) float wo[kAttnWarps][kHeadDim];
-  __shared__ bool last;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y, split = blockIdx.x;
-  const int G = a.nh / a.nkv, kvh = h / G, hd = kHeadDim, half = hd / 2;
-  const int kvd = a.nkv * hd;
-  const int f16 = a.kv_f16;
-  // The position and the cached rows t != pos were written before the
-  // producing GEMV started (it triggers this launch only after its own
-  // griddepcontrol.wait).
-  const int pos = a.pos ? __ldcg(a.pos) : a.fixed_pos;
-  const int ctx = pos + 1;
-  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
-  const int nsplit = (ctx + keys - 1) / keys;
-  if (split >= nsplit) return;
-  const int t0 = split * keys, t1 = min(t0 + keys, ctx);
-  const KVT* kc = reinterpret_cast<const KVT*>(a.kc) + kvh * hd + 4 * lane;
-  const KVT* vc = reinterpret_cast<const KVT*>(a.vc) + kvh * hd + 4 * lane;
-  KvRow<KVT> K[kAttnKpw], V[kAttnKpw];
-#pragma unroll
-  for (int i = 0; i < kAttnKpw; i++) {
-    const int t = t0 + warp + kAttnWarps * i;
-    if (t < t1 && t != pos) {
-      K[i].load(kc + (size_t)t * kvd);
-      V[i].load(vc + (size_t)t * kvd);
-    }
-  }
-  if (pdl) {
-    pdl_wait();
-    pdl_launch_dependents();
-  }
-  // q (ROPE_QK, f16 round in the f16 variant): lane holds dims 4l..4l+3; the
-  // RoPE partner of dim j < 64 is j + 64, held by lane l ^ 16
-  const float* cs = a.cosT + (size_t)pos * hd;
-  const float* sn = a.sinT + (size_t)pos * hd;
-  auto rope4 = [&](float4 x) {
-    float4 o = x;
-    float* e = reinterpret_cast<float*>(&o);
-    const float* xi = reinterpret_cast<const float*>(&x);
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-      const float other = __shfl_xor_sync(0xffffffffu, xi[c], 16);
-      const int d = 4 * lane + c, j = d & (half - 1);
-      float lo = lane < 16 ? xi[c] : other, hi = lane < 16 ? other : xi[c];
-      rope_pair(lo, hi, cs[j], sn[j], f16);
-      if (f16) round_h2(lo, hi);
-      e[c] = lane < 16 ? lo : hi;
-    }
-    return o;
-  };
-  const float4 q4 = rope4(__ldcg(reinterpret_cast<const float4*>(a.qkv + h * hd + 4 * lane)));
-  if (pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v (f16-rounded in the f16 cache)
-    const float* kn = a.qkv + a.nh * hd + kvh * hd;
-    const float* vn = a.qkv + a.nh * hd + kvd + kvh * hd;
-    float4 kr = __ldcg(reinterpret_cast<const float4*>(kn + 4 * lane));
-    float4 vr = __ldcg(reinterpret_cast<const float4*>(vn + 4 * lane));
-    // the cache keeps RoPE(k) rounded once to its type; scores use that value
-    float4 kx;
-    {
-      float* e = reinterpret_cast<float*>(&kx);
-      const float* xi = reinterpret_cast<const float*>(&kr);
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const float other = __shfl_xor_sync(0xffffffffu, xi[c], 16);
-        const int d = 4 * lane + c, j = d & (half - 1);
-        float lo = lane < 16 ? xi[c] : other, hi = lane < 16 ? other : xi[c];
-        rope_pair(lo, hi, cs[j], sn[j], f16);
-        e[c] = lane < 16 ? lo : hi;
-      }
-    }
-    KvRow<KVT> kn4, vn4;
-    kn4.set(make_float4(kv_round<KVT>(kx.x), kv_round<KVT>(kx.y), kv_round<KVT>(kx.z), kv_round<KVT>(kx.w)));
-    vn4.set(make_float4(kv_round<KVT>(vr.x), kv_round<KVT>(vr.y), kv_round<KVT>(vr.z), kv_round<KVT>(vr.w)));
-    const int i = (pos - t0) / kAttnWarps, w = (pos - t0) % kAttnWarps;
-    if (warp == w) {
-#pragma unroll
-      for (int ii = 0; ii < kAttnKpw; ii++)
-        if (ii == i) {
-          K[ii] = kn4;
-          V[ii] = vn4;
-        }
-    }
-    if (h % G == 0 && warp == 0) {  // one query head per KV group appends
-      KVT* kw = reinterpret_cast<KVT*>(a.kc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
-      KVT* vw = reinterpret_cast<KVT*>(a.vc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
-      kw[0] = kv_cvt<KVT>(kx.x); kw[1] = kv_cvt<KVT>(kx.y); kw[2] = kv_cvt<KVT>(kx.z); kw[3] = kv_cvt<KVT>(kx.w);
-      vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
-    }
-  }
-  // scores of this warp's keys: key i's score ends up in lane i
-  const float scale = 1.0f / sqrtf((float)hd);
-  float s_mine = -1e30f;
-  float m = -1e30f;
-#pragma unroll
-  for (int i = 0; i < kAttnKpw; i++) {
-    const int t = t0 + warp + kAttnWarps * i;
-    if (t >= t1) break;
-    const float4 k4 = K[i].get();
-    float p = __fmul_rn(q4.x, k4.x);
-    p = __fadd_rn(p, __fmul_rn(q4.y, k4.y));
-    p = __fadd_rn(p, __fmul_rn(q4.z, k4.z));
-    p = __fadd_rn(p, __fmul_rn(q4.w, k4.w));
-    const float sv = __fmul_rn(warp_sum(p), scale);
-    if (lane == i) s_mine = sv;
-    m = fmaxf(m, sv);
-  }
-  const int nk = t1 - t0 > warp ? (t1 - t0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
-  const float ev_mine = lane < nk ? expf(s_mine - m) : 0.f;
-  const float z = warp_sum(ev_mine);
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int i = 0; i < kAttnKpw; i++) {
-    if (i >= nk) break;
-    const float ev = __shfl_sync(0xffffffffu, ev_mine, i);
-    const float4 v4 = V[i].get();
-    acc.x = __fadd_rn(acc.x, __fmul_rn(ev, v4.x));
-    acc.y = __fadd_rn(acc.y, __fmul_rn(ev, v4.y));
-    acc.z = __fadd_rn(acc.z, __fmul_rn(ev, v4.z));
-    acc.w = __fadd_rn(acc.w, __fmul_rn(ev, v4.w));
-  }
-  if (f16) {  // ATTN_COMBINE_F16 reads the partial outputs through f16
-    round_h2(acc.x, acc.y);
-    round_h2(acc.z, acc.w);
-  }
-  if (lane == 0) {
-    wm[warp] = nk ? m : -1e30f;
-    wz[warp] = z;
-  }
-  *reinterpret_cast<float4*>(&wo[warp][4 * lane]) = acc;
-  __syncthreads();
-  // ---- merge the warp partials: warp 0, lane l holds dims 4l..4l+3
-  if (warp == 0) {
-    float M = -1e30f;
-    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wm[w]);
-    float Z = 0.f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int w = 0; w < kAttnWarps; w++) {
-      if (wz[w] == 0.f) continue;
-      const float wgt = expf(wm[w] - M);
-      Z = __fadd_rn(Z, __fmul_rn(wz[w], wgt));
-      const float4 p = *reinterpret_cast<const float4*>(&wo[w][4 * lane]);
-      o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
-      o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
-      o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
-      o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
-    }
-    if (nsplit == 1) {
-      const float invZ = 1.0f / Z;
-      *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
-          make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ), __fmul_rn(o.w, invZ));
-    } else {
-      if (f16) {
-        round_h2(o.x, o.y);
-        round_h2(o.z, o.w);
-      }
-      *reinterpret_cast<float4*>(a.po + ((size_t)h * a.max_splits + split) * hd + 4 * lane) = o;
-      if (lane == 0) {
-        a.pm[h * a.max_splits + split] = M;
-        a.pz[h * a.max_splits + split] = Z;
-      }
-    }
-  }
-  if (nsplit == 1) return;
-  // ---- several splits: the last CTA of the head merges them
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(a.counters + h, 1u) == (unsigned)nsplit - 1;
-  __syncthreads();
-  if (!last || warp != 0) return;
-  __threadfence();
-  const float* pm = a.pm + h * a.max_splits;
-  const float* pz = a.pz + h * a.max_splits;
-  float M = -1e30f;
-  for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(pm + s2));
-  float Z = 0.f;
-  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int s2 = 0; s2 < nsplit; s2++) {
-    const float wgt = expf(__ldcg(pm + s2) - M);
-    Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), wgt));
-    const float4 p = __ldcg(reinterpret_cast<const float4*>(a.po + ((size_t)h * a.max_splits + s2) * hd + 4 * lane));
-    o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
-    o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
-    o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
-    o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
-  }
-  const float invZ = 1.0f / Z;
-  *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
-      make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ), __fmul_rn(o.w, invZ));
-  if (lane == 0) a.counters[h] = 0u;  // ready for the next launch
+  __shared__ AttnSmem sm;
+  attn_head_item<KVT>(a, blockIdx.y, blockIdx.x, pdl, sm);
 }
-
 
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
   // splits of kAttnKeys keys (a fixed chunk, when given, for tests of the

@@ -33,6 +33,8 @@ struct XSrc {
   const uint32_t* ids;
   float* hidden_out;
   int fixed_pos;
+  int use_fixed_id;   // X_EMBED_RMS: 1 = embed fixed_id instead of ids[pos]
+  uint32_t fixed_id;
 };
 
 enum EpiMode { EPI_STORE = 0, EPI_ADD = 1, EPI_SILU = 2 };

@@ -99,8 +99,6 @@ struct eg_rt {
   cudaGraphExec_t graph[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [greedy][lora]
   int graph_rank[2] = {0, 0};
   int launches_per_step = 0;
-  int diag = 0;
-  int l2_ahead = 16;  // fused path: units of L2 prefetch ahead of the smem ring
   std::atomic<bool> busy{false};
   int64_t weight_bytes = 0, kv_bytes = 0, scratch_bytes = 0;
 };
@@ -579,8 +577,8 @@ static eg_status sync(eg_rt* rt) {
 
 static bool fused_ok(eg_rt* rt) {
   const eg_config& c = rt->c;
-  return rt->o.use_fused && !rt->active && c.hidden_size <= 2048 &&
-         c.num_heads * c.head_dim <= 2048 && c.intermediate_size <= 12288;
+  return rt->o.use_fused && !rt->active && c.hidden_size <= 4096 &&
+         c.num_heads * c.head_dim <= 4096 && c.intermediate_size <= 12288;
 }
 
 // n decode steps from start_pos in one cooperative launch (ids[start_pos..]
@@ -603,6 +601,7 @@ static eg_status run_fused(eg_rt* rt, int start_pos, int n, bool greedy, bool lm
   a.f16 = rt->o.kv_f16;
   a.emb_w = rt->emb_w;
   a.emb_s = rt->emb_s;
+  a.lm = rt->emb_t;
   a.final_norm = rt->final_norm;
   a.cosT = rt->cosT;
   a.sinT = rt->sinT;
@@ -623,7 +622,6 @@ static eg_status run_fused(eg_rt* rt, int start_pos, int n, bool greedy, bool lm
   a.state_pos = &rt->state->pos;
   a.cand_v = rt->cand_v;
   a.cand_i = rt->cand_i;
-  a.lm_counter = rt->lm_counter;
   a.bar = rt->fused_sync;
   a.err = reinterpret_cast<int*>(rt->fused_sync + 1);
   a.start_pos = start_pos;
@@ -631,8 +629,6 @@ static eg_status run_fused(eg_rt* rt, int start_pos, int n, bool greedy, bool lm
   a.greedy = greedy ? 1 : 0;
   a.lm_every = lm_every ? 1 : 0;
   a.prof = prof;
-  a.l2_ahead = rt->l2_ahead;
-  a.diag = rt->diag;
   CK(fused_decode(a, rt->st));
   rt->launches_per_step = 1;
   return EG_OK;
@@ -760,8 +756,6 @@ EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** 
   eg_rt* rt = new eg_rt();
   rt->c = c;
   rt->o = o;
-  if (const char* v = getenv("EG_L2_AHEAD")) rt->l2_ahead = atoi(v);
-  if (const char* v = getenv("EG_FUSED_DIAG")) rt->diag = atoi(v);
   if (cudaStreamCreateWithFlags(&rt->st, cudaStreamNonBlocking) != cudaSuccess) {
     delete rt;
     return fail(EG_ERR_CUDA, "stream create failed");
@@ -883,8 +877,7 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
   DALLOC(rt->sinT, sn.size() * 4, sb);
   CK(cudaMemcpy(rt->cosT, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(rt->sinT, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
-  {  // stream layouts of the int4 matrices; the reference-layout copies stay
-     // only for the fused kernel, which reads them directly
+  {  // stream layouts of the int4 matrices and of the LM head
     const int I = c.intermediate_size, NQKV = QD + 2 * KVD;
     int64_t* wb = &rt->weight_bytes;
     for (auto& l : rt->L) {
@@ -901,7 +894,7 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
     DALLOC(rt->emb_t, q8_stream_bytes(c.vocab_size, H), wb);
     q8_to_stream(rt->emb_w, c.vocab_size, H, rt->emb_t, rt->st);
     CK(cudaGetLastError());
-    if (!rt->o.use_fused) {
+    {  // the stream layouts replace the reference-layout copies
       CK(cudaStreamSynchronize(rt->st));
       for (auto& l : rt->L) {
         dfree(rt, (void**)&l.qkv_w, (int64_t)NQKV * H / 2, wb);
@@ -961,8 +954,8 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
     std::vector<FusedLayer> fl(c.num_layers);
     for (int i = 0; i < c.num_layers; i++) {
       const Layer& l = rt->L[i];
-      fl[i] = FusedLayer{l.qkv_w, l.o_w, l.gu_w, l.d_w, l.qkv_s, l.o_s, l.gu_s, l.d_s,
-                         c.attention_bias ? l.qkv_b : nullptr, l.in_norm, l.post_norm, l.kc, l.vc};
+      fl[i] = FusedLayer{l.qkv_t, l.o_t, l.gu_t, l.d_t, c.attention_bias ? l.qkv_b : nullptr,
+                         l.in_norm, l.post_norm, l.kc, l.vc};
     }
     DALLOC(rt->d_layers, fl.size() * sizeof(FusedLayer), sb);
     CK(cudaMemcpy(rt->d_layers, fl.data(), fl.size() * sizeof(FusedLayer), cudaMemcpyHostToDevice));
@@ -1314,20 +1307,17 @@ EG_API eg_status eg_profile_fused(eg_rt* rt, int start_pos, uint64_t* out_ns, in
   if (start_pos < 0 || start_pos >= rt->o.max_ctx) return fail(EG_ERR_ARG, "bad start_pos");
   const int nph = 2 * (rt->c.num_layers * 5 + 1);
   if (!out_ns || n_max < nph) return fail(EG_ERR_ARG, "need room for %d timestamps", nph);
-  const bool marks = n_max >= nph + 160;
   CK(cudaSetDevice(rt->o.device));
   unsigned long long* d = nullptr;
-  CK(cudaMalloc(&d, (nph + 160) * 8));
-  CK(cudaMemsetAsync(d, 0, (nph + 160) * 8, rt->st));
-  if (marks) CK(fused_set_marks(d + nph));
+  CK(cudaMalloc(&d, nph * 8));
+  CK(cudaMemsetAsync(d, 0, nph * 8, rt->st));
   if ((s = set_state(rt, start_pos, 1, 0, rt->amax))) { cudaFree(d); return s; }
   s = run_fused(rt, start_pos, 1, true, true, d);
   if (!s) s = sync(rt);
-  if (!s && cudaMemcpy(out_ns, d, (marks ? nph + 160 : nph) * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+  if (!s && cudaMemcpy(out_ns, d, nph * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
     s = fail(EG_ERR_CUDA, "profile readback failed");
-  if (marks) fused_set_marks(nullptr);
   cudaFree(d);
-  if (n_out) *n_out = marks ? nph + 160 : nph;
+  if (n_out) *n_out = nph;
   return s;
 }
 

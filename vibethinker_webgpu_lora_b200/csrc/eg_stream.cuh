@@ -1,0 +1,586 @@
+// eg_stream.cuh -- streaming GEMV building blocks (ring producer, integer-MMA
+// consumers, epilogue warp) and the decode-attention item, shared by the
+// per-op kernels (eg_kernels.cu) and the persistent decode kernel
+// (eg_fused.cu).
+//
+// A "run" is a contiguous range of tiles [t_lo, t_hi) of one stream-layout
+// matrix (gpr 128-wide groups per tile, one block per (tile, group)); in the
+// stream layout it is one contiguous byte range.  The producer warp copies a
+// run into the shared-memory ring, `cap` blocks per stage (one
+// cp.async.bulk); consumer warp w (of 16) takes the run's blocks w, w + 16,
+// w + 32, ... and keeps one running sum per row pair; at the end of each tile
+// every consumer warp leaves its partial row sums in red[tj & 1] and the
+// epilogue warp sums them and writes the outputs.  Ring positions (stage,
+// phase) and the tile hand-off counter tj carry over from one run to the
+// next, so a persistent kernel can chain runs of different matrices through
+// one ring; every warp walks the same run sequence.
+#pragma once
+#include "eg_device.cuh"
+
+namespace eg {
+
+constexpr int kG4Warps = 16;                    // consumer warps
+constexpr int kG4Threads = kG4Warps * 32 + 64;  // + producer warp + epilogue warp
+
+// int4 block: R row sets x (1024 bytes of nibbles in fragment order + 16 f32
+// group scales); int8 block: 16 rows x 128 bytes in fragment order.
+__host__ __device__ constexpr int q4_block_bytes(int R) { return R * 1088; }
+constexpr int kQ8Block = 2048;
+
+struct RingPos {
+  int st, ph;
+};
+
+__device__ __forceinline__ void ring_advance(RingPos& rp, int stages) {
+  if (++rp.st == stages) {
+    rp.st = 0;
+    rp.ph ^= 1;
+  }
+}
+
+// Producer (one warp): one run of nitems blocks of blk bytes from src0.
+// Returns false when a wait gave up (error recorded).
+__device__ __forceinline__ bool ring_produce(unsigned char* ring, uint64_t* full, uint64_t* empty,
+                                             int stages, int stage_bytes,
+                                             const unsigned char* src0, int nitems, int cap,
+                                             int blk, RingPos& rp, int& issued, int* err,
+                                             int lane) {
+  const int nchunks = (nitems + cap - 1) / cap;
+  for (int n = 0; n < nchunks; n++) {
+    if (!mbar_wait(&empty[rp.st], rp.ph ^ 1, err)) return false;
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)(min(cap, nitems - n * cap) * blk);
+      mbar_expect_tx(&full[rp.st], bytes);
+      bulk_g2s(ring + (size_t)rp.st * stage_bytes, src0 + (size_t)n * cap * blk, bytes,
+               &full[rp.st]);
+    }
+    __syncwarp();
+    issued++;
+    ring_advance(rp, stages);
+  }
+  return true;
+}
+
+// Producer exit: the last (up to `stages`) copies issued have landed, so the
+// CTA never exits with a bulk copy in flight (bounded even after an error).
+__device__ __forceinline__ void ring_drain(uint64_t* full, int stages, RingPos rp, int issued) {
+  for (int k = 0; k < stages && k < issued; k++) {
+    // step back one stage
+    if (rp.st == 0) {
+      rp.st = stages - 1;
+      rp.ph ^= 1;
+    } else {
+      rp.st--;
+    }
+    if (!mbar_wait_bounded(&full[rp.st], rp.ph)) break;
+  }
+}
+
+// Tile hand-off area of the consumers and the epilogue warp.
+template <int R>
+struct TileRed {
+  float v[2][kG4Warps][R][16];
+};
+
+// Consumer side of one hand-off: sum the lanes t = 0, 1, publish the warp's
+// partial rows in red[tj & 1] once the epilogue warp released that buffer.
+template <int R>
+__device__ __forceinline__ void tile_handoff(TileRed<R>& red, uint64_t* tile_full,
+                                             uint64_t* tile_free, int tj, float (&acc)[R][2],
+                                             bool& dead, int* err) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gq = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], 1);
+    acc[r][1] += __shfl_xor_sync(0xffffffffu, acc[r][1], 1);
+  }
+  const int b = tj & 1;
+  if (!dead && !mbar_wait(&tile_free[b], ((tj >> 1) & 1) ^ 1, err)) dead = true;
+  if (t == 0) {
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+      red.v[b][warp][r][gq] = acc[r][0];
+      red.v[b][warp][r][gq + 8] = acc[r][1];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&tile_full[b]);
+}
+
+// Consumers (warps 0-15) of one int4 run.  xb / xcor / xmul: the staged
+// activation (stage_xd).  After a failed wait a warp goes on without waiting
+// (its results are void; the host sees the error word).
+template <int R>
+__device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64_t* empty,
+                               int stages, int stage_bytes, int cap, int t_lo, int t_hi, int gpr,
+                               const uint2* xb, const int* xcor, const float* xmul,
+                               TileRed<R>& red, uint64_t* tile_full, uint64_t* tile_free,
+                               RingPos& rp, int& tj, bool& dead, int* err) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gq = lane >> 2, t = lane & 3;
+  const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
+  const int blk = q4_block_bytes(R);
+  const int nitems = (t_hi - t_lo) * gpr;
+  const int nchunks = (nitems + cap - 1) / cap;
+  if (nchunks == 0) return;
+  float acc[R][2];
+#pragma unroll
+  for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
+  int chunk = 0, chunk_lo = 0;
+  if (!dead && !mbar_wait(&full[rp.st], rp.ph, err)) dead = true;
+  const unsigned char* stage = ring + (size_t)rp.st * stage_bytes;
+  int i = warp;  // block index within the run
+  for (int j = 0; j < t_hi - t_lo; j++) {
+    const int tile_end = (j + 1) * gpr;
+    for (; i < tile_end; i += kG4Warps) {
+      while (i >= chunk_lo + cap) {  // next stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[rp.st]);
+        ring_advance(rp, stages);
+        chunk++;
+        chunk_lo += cap;
+        stage = ring + (size_t)rp.st * stage_bytes;
+        if (!dead && !mbar_wait(&full[rp.st], rp.ph, err)) dead = true;
+      }
+      const int g = i - j * gpr;
+      const unsigned char* bp = stage + (size_t)(i - chunk_lo) * blk;
+      // B: digit plane gq of this group's 4 k32 blocks (zero for gq >= 4)
+      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
+      if (bl) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 4);
+        X0 = xp[0];
+        X1 = xp[1];
+      }
+      uint4 A[R], B[R];
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        // words t, 4+t, 8+t, 12+t of rows gq (A) and gq+8 (B)
+        A[r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + lane * 16);
+        B[r] = *reinterpret_cast<const uint4*>(bp + r * 1024 + 512 + lane * 16);
+      }
+      int cc[R][4];
+#pragma unroll
+      for (int r = 0; r < R; r++) {
+        cc[r][0] = cc[r][1] = cc[r][2] = cc[r][3] = 0;
+        imma16832(cc[r], nib_lo_u8(A[r].x), nib_lo_u8(B[r].x), nib_hi_u8(A[r].x), nib_hi_u8(B[r].x), X0.x, X0.y);
+        imma16832(cc[r], nib_lo_u8(A[r].y), nib_lo_u8(B[r].y), nib_hi_u8(A[r].y), nib_hi_u8(B[r].y), X0.z, X0.w);
+        imma16832(cc[r], nib_lo_u8(A[r].z), nib_lo_u8(B[r].z), nib_hi_u8(A[r].z), nib_hi_u8(B[r].z), X1.x, X1.y);
+        imma16832(cc[r], nib_lo_u8(A[r].w), nib_lo_u8(B[r].w), nib_hi_u8(A[r].w), nib_hi_u8(B[r].w), X1.z, X1.w);
+      }
+      if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
+        const int cor = xcor[2 * g + t];
+        const float mul = xmul[2 * g + t];
+        const float* sc = reinterpret_cast<const float*>(bp + R * 1024);
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+          const float sa = sc[16 * r + gq] * mul, sb = sc[16 * r + gq + 8] * mul;
+          acc[r][0] = fmaf(sa, (float)(cc[r][0] + 256 * cc[r][1] - cor), acc[r][0]);
+          acc[r][1] = fmaf(sb, (float)(cc[r][2] + 256 * cc[r][3] - cor), acc[r][1]);
+        }
+      }
+    }
+    tile_handoff<R>(red, tile_full, tile_free, tj, acc, dead, err);
+    tj++;
+  }
+  // release the current stage and wait/release the later ones this warp had
+  // no blocks in, so every stage sees all kG4Warps arrivals
+  for (; chunk < nchunks; chunk++) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[rp.st]);
+    ring_advance(rp, stages);
+    if (chunk + 1 < nchunks && !dead && !mbar_wait(&full[rp.st], rp.ph, err)) dead = true;
+  }
+}
+
+// Consumers of one int8 run (m16n8k32 s8.s8; xb as uint32 [G][p][t][m][2]
+// from stage_xd8; no offset correction).
+static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full, uint64_t* empty,
+                               int stages, int stage_bytes, int cap, int t_lo, int t_hi, int gpr,
+                               const uint32_t* xb, const float* xmul, TileRed<1>& red,
+                               uint64_t* tile_full, uint64_t* tile_free, RingPos& rp, int& tj,
+                               bool& dead, int* err) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gq = lane >> 2, t = lane & 3;
+  const bool bl = gq < 4;
+  const int nitems = (t_hi - t_lo) * gpr;
+  const int nchunks = (nitems + cap - 1) / cap;
+  if (nchunks == 0) return;
+  float acc[1][2] = {{0.f, 0.f}};
+  int chunk = 0, chunk_lo = 0;
+  if (!dead && !mbar_wait(&full[rp.st], rp.ph, err)) dead = true;
+  const unsigned char* stage = ring + (size_t)rp.st * stage_bytes;
+  int i = warp;
+  for (int j = 0; j < t_hi - t_lo; j++) {
+    const int tile_end = (j + 1) * gpr;
+    for (; i < tile_end; i += kG4Warps) {
+      while (i >= chunk_lo + cap) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[rp.st]);
+        ring_advance(rp, stages);
+        chunk++;
+        chunk_lo += cap;
+        stage = ring + (size_t)rp.st * stage_bytes;
+        if (!dead && !mbar_wait(&full[rp.st], rp.ph, err)) dead = true;
+      }
+      const int g = i - j * gpr;
+      const unsigned char* bp = stage + (size_t)(i - chunk_lo) * kQ8Block;
+      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
+      if (bl) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 8);
+        X0 = xp[0];
+        X1 = xp[1];
+      }
+      const uint4 A0 = *reinterpret_cast<const uint4*>(bp + lane * 16);
+      const uint4 A1 = *reinterpret_cast<const uint4*>(bp + 512 + lane * 16);
+      const uint4 B0 = *reinterpret_cast<const uint4*>(bp + 1024 + lane * 16);
+      const uint4 B1 = *reinterpret_cast<const uint4*>(bp + 1536 + lane * 16);
+      int cc[4] = {0, 0, 0, 0};
+      imma16832_ss(cc, A0.x, B0.x, A0.y, B0.y, X0.x, X0.y);
+      imma16832_ss(cc, A0.z, B0.z, A0.w, B0.w, X0.z, X0.w);
+      imma16832_ss(cc, A1.x, B1.x, A1.y, B1.y, X1.x, X1.y);
+      imma16832_ss(cc, A1.z, B1.z, A1.w, B1.w, X1.z, X1.w);
+      if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
+        const float mul = xmul[2 * g + t];
+        acc[0][0] = fmaf(mul, (float)(cc[0] + 256 * cc[1]), acc[0][0]);
+        acc[0][1] = fmaf(mul, (float)(cc[2] + 256 * cc[3]), acc[0][1]);
+      }
+    }
+    tile_handoff<1>(red, tile_full, tile_free, tj, acc, dead, err);
+    tj++;
+  }
+  for (; chunk < nchunks; chunk++) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[rp.st]);
+    ring_advance(rp, stages);
+    if (chunk + 1 < nchunks && !dead && !mbar_wait(&full[rp.st], rp.ph, err)) dead = true;
+  }
+}
+
+// Epilogue warp of one int4 run: per tile, sum the consumer partials and run
+// the epilogue (scale already applied; bias / residual / SiLU / LoRA here).
+// pre_ok: the first tile's residual / bias may be read before its hand-off
+// (false when the inputs of this run are only ordered by that hand-off).
+template <int R>
+__device__ bool epilogue_q4_run(const Epi& e, int t_lo, int t_hi, TileRed<R>& red,
+                                uint64_t* tile_full, uint64_t* tile_free, int& tj, bool pre_ok,
+                                int* err) {
+  const int lane = threadIdx.x & 31;
+  const bool lora = e.mods != nullptr;
+  float pre = 0.f;
+  if (pre_ok && lane < 16 && !lora && t_lo < t_hi) pre = epi_pre(e, t_lo * 16 + lane);
+  for (int tile = t_lo; tile < t_hi; tile++, tj++) {
+    const int b = tj & 1;
+    if (!mbar_wait(&tile_full[b], (tj >> 1) & 1, err)) return false;
+    if (!pre_ok && tile == t_lo && lane < 16 && !lora) pre = epi_pre(e, tile * 16 + lane);
+    float v = 0.f;
+    if (lane < 16 * R)
+      for (int ww = 0; ww < kG4Warps; ww++) v += red.v[b][ww][lane >> 4][lane & 15];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tile_free[b]);
+    const float up = __shfl_down_sync(0xffffffffu, v, 16);
+    if (lane < 16) {
+      const int row = tile * 16 + lane;
+      if (lora)
+        epilogue_row(e, row, v, R == 2 ? up : 0.f);
+      else
+        epilogue_row_pre(e, row, v, R == 2 ? up : 0.f, pre);
+      if (!lora && tile + 1 < t_hi) pre = epi_pre(e, row + 16);
+    }
+  }
+  return true;
+}
+
+// Epilogue warp of one int8 run: y[n] = row sum * s[n] (sum first, scale
+// last) and the warp's best (value, index) in the reference's order.
+static __device__ bool epilogue_q8_run(const float* s, float* y, int N, int t_lo, int t_hi,
+                                TileRed<1>& red, uint64_t* tile_full, uint64_t* tile_free,
+                                int& tj, float& bv, uint32_t& bi, int* err) {
+  const int lane = threadIdx.x & 31;
+  float sc = lane < 16 && t_lo < t_hi && t_lo * 16 + lane < N ? __ldg(s + t_lo * 16 + lane) : 0.f;
+  for (int tile = t_lo; tile < t_hi; tile++, tj++) {
+    const int b = tj & 1;
+    if (!mbar_wait(&tile_full[b], (tj >> 1) & 1, err)) return false;
+    float v = 0.f;
+    if (lane < 16)
+      for (int ww = 0; ww < kG4Warps; ww++) v += red.v[b][ww][0][lane];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tile_free[b]);
+    const int n = tile * 16 + lane;
+    if (lane < 16 && n < N) {
+      const float o = __fmul_rn(v, sc);
+      y[n] = o;
+      if (beats(o, (uint32_t)n, bv, bi)) {
+        bv = o;
+        bi = (uint32_t)n;
+      }
+      sc = n + 16 < N && tile + 1 < t_hi ? __ldg(s + n + 16) : 0.f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (beats(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  return true;
+}
+
+// ======================================================================
+// Decode attention item
+// ======================================================================
+// One (query head, split of <= kAttnKeys keys) on 512 threads (warps 0-15;
+// named barrier 1).  Each warp takes keys t0 + w, t0 + w + 16, ...; a lane
+// holds 4 of the 128 dims.  All K and V rows of the warp are requested
+// before griddepcontrol.wait (pdl; the cache rows t != pos were written by
+// earlier steps), so the item pays one memory latency for them.  Each warp
+// forms a partial (m, z, sum e^(s-m) v) over its keys (ATTN_PARTIAL,
+// kernels.js:258-345), the 16 warp partials are merged in shared memory with
+// the ATTN_COMBINE formula (kernels.js:346-388, f16 rounding of the partial
+// outputs in the f16 variant), and for contexts longer than one split the
+// split partials are merged once more by the last item of the head.  The
+// new k (RoPE) / v row of position pos is formed in registers; the first
+// query head of each KV group appends it to the cache (runtime.js:1509-1514).
+constexpr int kAttnWarps = 16;
+constexpr int kAttnKeys = 256;  // keys per split (16 per warp)
+constexpr int kAttnKpw = kAttnKeys / kAttnWarps;
+
+// A value as the cache stores it (rounded to the cache type).
+template <typename KVT>
+__device__ __forceinline__ float kv_round(float v);
+template <>
+__device__ __forceinline__ float kv_round<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float kv_round<__half>(float v) { return round_h(v); }
+
+template <typename KVT>
+struct KvRow;  // 4 consecutive cache values of one lane
+template <>
+struct KvRow<__half> {
+  uint2 u;
+  __device__ __forceinline__ void load(const __half* p) { u = __ldcg(reinterpret_cast<const uint2*>(p)); }
+  __device__ __forceinline__ float4 get() const {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  __device__ __forceinline__ void set(float4 v) {  // values already f16-exact
+    const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+  }
+};
+template <>
+struct KvRow<float> {
+  float4 f;
+  __device__ __forceinline__ void load(const float* p) { f = __ldcg(reinterpret_cast<const float4*>(p)); }
+  __device__ __forceinline__ float4 get() const { return f; }
+  __device__ __forceinline__ void set(float4 v) { f = v; }
+};
+
+// Shared memory of one attention item (8.3 KB).
+struct AttnSmem {
+  float wm[kAttnWarps], wz[kAttnWarps];
+  __align__(16) float wo[kAttnWarps][kHeadDim];
+  int last;
+};
+
+// RoPE (ROPE_QK) of the 4 dims a lane holds; the partner of dim j < 64 is
+// j + 64, held by lane ^ 16.  rnd: round the result to f16 (q in the f16
+// variant).
+__device__ __forceinline__ float4 rope_lane4(float4 x, const float* cs, const float* sn, int f16,
+                                             bool rnd) {
+  const int lane = threadIdx.x & 31, half = kHeadDim / 2;
+  float4 o;
+  float* e = reinterpret_cast<float*>(&o);
+  const float* xi = reinterpret_cast<const float*>(&x);
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const float other = __shfl_xor_sync(0xffffffffu, xi[c], 16);
+    const int j = (4 * lane + c) & (half - 1);
+    float lo = lane < 16 ? xi[c] : other, hi = lane < 16 ? other : xi[c];
+    rope_pair(lo, hi, cs[j], sn[j], f16);
+    if (rnd) round_h2(lo, hi);
+    e[c] = lane < 16 ? lo : hi;
+  }
+  return o;
+}
+
+template <typename KVT>
+__device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, AttnSmem& sm) {
+  float* wm = sm.wm;
+  float* wz = sm.wz;
+  float (*wo)[kHeadDim] = sm.wo;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.nh / a.nkv, kvh = h / G, hd = kHeadDim;
+  const int kvd = a.nkv * hd;
+  const int f16 = a.kv_f16;
+  // The position and the cached rows t != pos were written before the
+  // producing GEMV started (it triggers this launch only after its own
+  // griddepcontrol.wait).
+  const int pos = a.pos ? __ldcg(a.pos) : a.fixed_pos;
+  const int ctx = pos + 1;
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  const int nsplit = (ctx + keys - 1) / keys;
+  if (split >= nsplit) return;
+  const int t0 = split * keys, t1 = min(t0 + keys, ctx);
+  const KVT* kc = reinterpret_cast<const KVT*>(a.kc) + kvh * hd + 4 * lane;
+  const KVT* vc = reinterpret_cast<const KVT*>(a.vc) + kvh * hd + 4 * lane;
+  KvRow<KVT> K[kAttnKpw], V[kAttnKpw];
+#pragma unroll
+  for (int i = 0; i < kAttnKpw; i++) {
+    const int t = t0 + warp + kAttnWarps * i;
+    if (t < t1 && t != pos) {
+      K[i].load(kc + (size_t)t * kvd);
+      V[i].load(vc + (size_t)t * kvd);
+    }
+  }
+  if (pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+  const float* cs = a.cosT + (size_t)pos * hd;
+  const float* sn = a.sinT + (size_t)pos * hd;
+  // q: ROPE_QK, read through f16 in the f16 variant (ATTN_PARTIAL_F16)
+  const float4 q4 = rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + h * hd + 4 * lane)),
+                               cs, sn, f16, f16 != 0);
+  if (pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v, as the cache stores them
+    const float* kn = a.qkv + a.nh * hd + kvh * hd;
+    const float* vn = a.qkv + a.nh * hd + kvd + kvh * hd;
+    const float4 kx = rope_lane4(__ldcg(reinterpret_cast<const float4*>(kn + 4 * lane)), cs, sn,
+                                 f16, false);
+    const float4 vr = __ldcg(reinterpret_cast<const float4*>(vn + 4 * lane));
+    KvRow<KVT> kn4, vn4;
+    kn4.set(make_float4(kv_round<KVT>(kx.x), kv_round<KVT>(kx.y), kv_round<KVT>(kx.z), kv_round<KVT>(kx.w)));
+    vn4.set(make_float4(kv_round<KVT>(vr.x), kv_round<KVT>(vr.y), kv_round<KVT>(vr.z), kv_round<KVT>(vr.w)));
+    const int i = (pos - t0) / kAttnWarps, w = (pos - t0) % kAttnWarps;
+    if (warp == w) {
+#pragma unroll
+      for (int ii = 0; ii < kAttnKpw; ii++)
+        if (ii == i) {
+          K[ii] = kn4;
+          V[ii] = vn4;
+        }
+    }
+    if (h % G == 0 && warp == 0) {  // one query head per KV group appends
+      KVT* kw = reinterpret_cast<KVT*>(a.kc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
+      KVT* vw = reinterpret_cast<KVT*>(a.vc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
+      kw[0] = kv_cvt<KVT>(kx.x); kw[1] = kv_cvt<KVT>(kx.y); kw[2] = kv_cvt<KVT>(kx.z); kw[3] = kv_cvt<KVT>(kx.w);
+      vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
+    }
+  }
+  // scores of this warp's keys: key i's score ends up in lane i
+  const float scale = 1.0f / sqrtf((float)hd);
+  float s_mine = -1e30f;
+  float m = -1e30f;
+#pragma unroll
+  for (int i = 0; i < kAttnKpw; i++) {
+    const int t = t0 + warp + kAttnWarps * i;
+    if (t >= t1) break;
+    const float4 k4 = K[i].get();
+    float p = __fmul_rn(q4.x, k4.x);
+    p = __fadd_rn(p, __fmul_rn(q4.y, k4.y));
+    p = __fadd_rn(p, __fmul_rn(q4.z, k4.z));
+    p = __fadd_rn(p, __fmul_rn(q4.w, k4.w));
+    const float sv = __fmul_rn(warp_sum(p), scale);
+    if (lane == i) s_mine = sv;
+    m = fmaxf(m, sv);
+  }
+  const int nk = t1 - t0 > warp ? (t1 - t0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
+  const float ev_mine = lane < nk ? expf(s_mine - m) : 0.f;
+  const float z = warp_sum(ev_mine);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kAttnKpw; i++) {
+    if (i >= nk) break;
+    const float ev = __shfl_sync(0xffffffffu, ev_mine, i);
+    const float4 v4 = V[i].get();
+    acc.x = __fadd_rn(acc.x, __fmul_rn(ev, v4.x));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(ev, v4.y));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(ev, v4.z));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(ev, v4.w));
+  }
+  if (f16) {  // ATTN_COMBINE_F16 reads the partial outputs through f16
+    round_h2(acc.x, acc.y);
+    round_h2(acc.z, acc.w);
+  }
+  if (lane == 0) {
+    wm[warp] = nk ? m : -1e30f;
+    wz[warp] = z;
+  }
+  *reinterpret_cast<float4*>(&wo[warp][4 * lane]) = acc;
+  bar_sync_n<kAttnWarps * 32>();
+  // ---- merge the warp partials: warp 0, lane l holds dims 4l..4l+3
+  if (warp == 0) {
+    float M = -1e30f;
+    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wm[w]);
+    float Z = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int w = 0; w < kAttnWarps; w++) {
+      if (wz[w] == 0.f) continue;
+      const float wgt = expf(wm[w] - M);
+      Z = __fadd_rn(Z, __fmul_rn(wz[w], wgt));
+      const float4 p = *reinterpret_cast<const float4*>(&wo[w][4 * lane]);
+      o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
+      o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
+      o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
+      o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
+    }
+    if (nsplit == 1) {
+      const float invZ = 1.0f / Z;
+      *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
+          make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ), __fmul_rn(o.w, invZ));
+    } else {
+      if (f16) {
+        round_h2(o.x, o.y);
+        round_h2(o.z, o.w);
+      }
+      *reinterpret_cast<float4*>(a.po + ((size_t)h * a.max_splits + split) * hd + 4 * lane) = o;
+      if (lane == 0) {
+        a.pm[h * a.max_splits + split] = M;
+        a.pz[h * a.max_splits + split] = Z;
+      }
+    }
+  }
+  if (nsplit == 1) {
+    bar_sync_n<kAttnWarps * 32>();  // the shared area may be reused by the caller
+    return;
+  }
+  // ---- several splits: the last item of the head merges them
+  __threadfence();
+  bar_sync_n<kAttnWarps * 32>();
+  if (threadIdx.x == 0) sm.last = atomicAdd(a.counters + h, 1u) == (unsigned)nsplit - 1;
+  bar_sync_n<kAttnWarps * 32>();
+  const bool last = sm.last != 0;
+  bar_sync_n<kAttnWarps * 32>();
+  if (last && warp == 0) {
+    __threadfence();
+    const float* pm = a.pm + h * a.max_splits;
+    const float* pz = a.pz + h * a.max_splits;
+    float M = -1e30f;
+    for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(pm + s2));
+    float Z = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s2 = 0; s2 < nsplit; s2++) {
+      const float wgt = expf(__ldcg(pm + s2) - M);
+      Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), wgt));
+      const float4 p = __ldcg(reinterpret_cast<const float4*>(a.po + ((size_t)h * a.max_splits + s2) * hd + 4 * lane));
+      o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
+      o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
+      o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
+      o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
+    }
+    const float invZ = 1.0f / Z;
+    *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
+        make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ),
+                    __fmul_rn(o.w, invZ));
+    if (lane == 0) a.counters[h] = 0u;  // ready for the next launch
+  }
+}
+
+}  // namespace eg
