@@ -113,16 +113,6 @@ __device__ __forceinline__ float block_sum_n(float v, float* sbuf) {
   for (int i = 0; i < NT / 32; i++) r += sbuf[i];  // fixed order: deterministic
   return r;
 }
-__device__ __forceinline__ float block_max(float v, float* sbuf) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kCtaThreads >> 5;
-  v = warp_max(v);
-  cta_sync();
-  if (lane == 0) sbuf[warp] = v;
-  cta_sync();
-  float r = sbuf[0];
-  for (int i = 1; i < nw; i++) r = fmaxf(r, sbuf[i]);
-  return r;
-}
 
 // ======================================================================
 // GEMV prologue: resolve the input vector (plain / RMSNorm / embed+RMSNorm)
@@ -179,139 +169,6 @@ __device__ __forceinline__ void setup_x(const XSrc& s, int K, XCtx& c, float* sr
   }
 }
 
-// Power-of-two shift keeping |x| * 2^-e inside the f16 range.
-__device__ __forceinline__ int shift_for(float amax) {
-  if (!(amax > 16384.f)) return 0;
-  int e;
-  frexpf(amax / 16384.f, &e);
-  return e;
-}
-
-// Register-staged prologue.  Thread i owns the 8-element units
-// u = i, i + blockDim, ... (k = 8u..8u+7); every global load of the input
-// (and of the norm weight) is issued before any is consumed, so the whole
-// prologue costs one memory latency.  The values are then transformed
-// (RMSNorm), range-checked and written once as MMA B fragments:
-//   fmt 4: int4 layout (see write_int4_word), fmt 8: int8 layout.
-// NORM = false compiles the plain-vector case only (fewer live registers).
-// [u0, u1): the 8-wide units staged (default all); only a plain input may be
-// staged partially (RMSNorm needs the whole vector).
-template <int MAXU, bool NORM = true>
-__device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred, int u0 = 0,
-                       int u1 = -1) {
-  const int K8 = K / 8;
-  if (u1 < 0) u1 = K8;
-  float v[MAXU][8];
-  float gw[NORM ? MAXU : 1][8];
-  const int8_t* erow = nullptr;
-  float escale = 0.f;
-  if ((NORM && s.mode == X_EMBED_RMS)) {
-    const uint32_t id =
-        s.use_fixed_id ? s.fixed_id : __ldcg(s.ids + (s.pos ? __ldcg(s.pos) : s.fixed_pos));
-    erow = reinterpret_cast<const int8_t*>(s.emb_w + (size_t)id * (K / 4));
-    escale = s.emb_s[id];
-  }
-#pragma unroll
-  for (int i = 0; i < MAXU; i++) {
-    const int u = u0 + threadIdx.x + i * kCtaThreads;
-    const bool ok = u < u1;
-    if ((NORM && s.mode == X_EMBED_RMS)) {
-      const uint2 b = ok ? *reinterpret_cast<const uint2*>(erow + 8 * u) : make_uint2(0, 0);
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const int8_t q = (int8_t)(((j < 4 ? b.x : b.y) >> (8 * (j & 3))) & 0xFF);
-        v[i][j] = __fmul_rn((float)q, escale);  // EMBED_BUF: f32(q8) * scale[id]
-      }
-    } else {
-      const float4 a = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u)) : make_float4(0, 0, 0, 0);
-      const float4 b = ok ? __ldcg(reinterpret_cast<const float4*>(s.x + 8 * u + 4)) : make_float4(0, 0, 0, 0);
-      v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
-      v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
-    }
-    if ((NORM && s.mode != X_PLAIN)) {
-      const float4 a = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u)) : make_float4(0, 0, 0, 0);
-      const float4 b = ok ? __ldg(reinterpret_cast<const float4*>(s.norm_g + 8 * u + 4)) : make_float4(0, 0, 0, 0);
-      gw[NORM ? i : 0][0] = a.x; gw[NORM ? i : 0][1] = a.y; gw[NORM ? i : 0][2] = a.z; gw[NORM ? i : 0][3] = a.w;
-      gw[NORM ? i : 0][4] = b.x; gw[NORM ? i : 0][5] = b.y; gw[NORM ? i : 0][6] = b.z; gw[NORM ? i : 0][7] = b.w;
-    }
-  }
-  if ((NORM && s.mode == X_EMBED_RMS) && blockIdx.x == 0 && s.hidden_out) {
-#pragma unroll
-    for (int i = 0; i < MAXU; i++) {
-      const int u = u0 + threadIdx.x + i * kCtaThreads;
-      if (u < u1) {
-        *reinterpret_cast<float4*>(s.hidden_out + 8 * u) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
-        *reinterpret_cast<float4*>(s.hidden_out + 8 * u + 4) = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
-      }
-    }
-  }
-  if ((NORM && s.mode != X_PLAIN)) {
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < MAXU; i++)
-#pragma unroll
-      for (int j = 0; j < 8; j++) ss = __fadd_rn(ss, __fmul_rn(v[i][j], v[i][j]));
-    ss = block_sum(ss, sred);
-    // RMSNORM: inverseSqrt(sum/K + eps) (kernels.js:142), IEEE sqrt + divide
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), s.eps)));
-    const __half inv16 = __float2half_rn(inv);
-#pragma unroll
-    for (int i = 0; i < MAXU; i++)
-#pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        if (!s.f16) {
-          v[i][j] = __fmul_rn(__fmul_rn(v[i][j], inv), gw[NORM ? i : 0][j]);
-          v[i][j + 1] = __fmul_rn(__fmul_rn(v[i][j + 1], inv), gw[NORM ? i : 0][j + 1]);
-        } else {  // RMSNORM_F16: f16(f16(x) * inv) * f16(g), two lanes at a time
-          __half2 t = __hmul2_rn(__floats2half2_rn(v[i][j], v[i][j + 1]), __half2half2(inv16));
-          t = __hmul2_rn(t, __floats2half2_rn(gw[NORM ? i : 0][j], gw[NORM ? i : 0][j + 1]));
-          const float2 r = __half22float2(t);
-          v[i][j] = r.x;
-          v[i][j + 1] = r.y;
-        }
-      }
-  }
-  float am = 0.f;
-#pragma unroll
-  for (int i = 0; i < MAXU; i++)
-#pragma unroll
-    for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
-  const int e = shift_for(block_max(am, sred));
-#pragma unroll
-  for (int i = 0; i < MAXU; i++) {
-    const int u = u0 + threadIdx.x + i * kCtaThreads;
-    if (u >= u1) continue;
-    float x[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) x[j] = e ? ldexpf(v[i][j], -e) : v[i][j];
-    if (fmt == 4) {
-      uint4* xs = reinterpret_cast<uint4*>(smem);
-      uint4* lo = xs + K8 + 4;
-      uint4 h, l;
-      split_h2(x[0], x[4], h.x, l.x);
-      split_h2(x[1] * 0.0625f, x[5] * 0.0625f, h.y, l.y);
-      split_h2(x[2], x[6], h.z, l.z);
-      split_h2(x[3] * 0.0625f, x[7] * 0.0625f, h.w, l.w);
-      const int slot = (u & ~15) + 4 * (u & 3) + ((u >> 2) & 3);
-      xs[slot] = h;
-      lo[slot] = l;
-    } else {
-      uint2* xs2 = reinterpret_cast<uint2*>(smem);
-      uint2* lo = xs2 + K / 4 + 2;
-      uint2 h, l;
-      split_h2(x[0], x[2], h.x, l.x);
-      split_h2(x[1], x[3], h.y, l.y);
-      xs2[2 * u] = h;
-      lo[2 * u] = l;
-      split_h2(x[4], x[6], h.x, l.x);
-      split_h2(x[5], x[7], h.y, l.y);
-      xs2[2 * u + 1] = h;
-      lo[2 * u + 1] = l;
-    }
-  }
-  cta_sync();
-  return e;
-}
 
 // Activation prologue of the integer-MMA int4 GEMV.  Each 128-wide group G
 // is put in fixed point, X = round(x * 2^f_G) with |X| < 2^30, and X is
@@ -320,14 +177,13 @@ __device__ int stage_x(const XSrc& s, int K, int fmt, void* smem, float* sred, i
 // plane per MMA column.  Per group it stores
 //   xb:   the m16n8k32 B fragments, uint2 [G][p][t][m] (lane (p, t) of MMA m
 //         holds plane p of elements 8(4m+t) + {0,2,4,6} and + {1,3,5,7}),
-//   xcor: 8 (S_{2i} + 256 S_{2i+1}), S_p = sum of plane p over the group
-//         (removes the +8 offset of the u8 weights), i = 0, 1,
-//   xmul: 2^-f_G * 65536^i (weight of the column pair (2i, 2i+1)).
+//   xcm:  per column pair (2i, 2i+1), i = 0, 1: .x = 8 (S_{2i} + 256 S_{2i+1}),
+//         S_p = sum of plane p over the group (removes the +8 offset of the u8
+//         weights); .y = the f32 bits of 2^-f_G * 65536^i (the pair's weight).
 // pdl: the norm weights are read first, then griddepcontrol.wait, then the
 // input (which the previous kernel writes).
 template <int MAXU, bool NORM, int NT = kCtaThreads>
-__device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul, float* sred,
-                         int pdl) {
+__device__ void stage_xd(const XSrc& s, int K, uint2* xb, int2* xcm, float* sred, int pdl) {
   const int K8 = K / 8;
   float v[MAXU][8];
   float gw[NORM ? MAXU : 1][8];
@@ -444,10 +300,8 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, float* xmul
 #pragma unroll
     for (int p = 0; p < 4; p++) xb[((G * 4 + p) * 4 + t) * 4 + m] = pl[p];
     if (q == 0) {
-      xcor[2 * G] = 8 * (S[0] + 256 * S[1]);
-      xcor[2 * G + 1] = 8 * (S[2] + 256 * S[3]);
-      xmul[2 * G] = __int_as_float((127 - f) << 23);      // 2^-f
-      xmul[2 * G + 1] = __int_as_float((143 - f) << 23);  // 2^(16-f)
+      xcm[2 * G] = make_int2(8 * (S[0] + 256 * S[1]), (127 - f) << 23);      // 2^-f
+      xcm[2 * G + 1] = make_int2(8 * (S[2] + 256 * S[3]), (143 - f) << 23);  // 2^(16-f)
     }
   }
   bar_sync_n<NT>();
@@ -618,22 +472,6 @@ __device__ __forceinline__ void rope_pair(float& lo, float& hi, float c, float s
   }
 }
 
-__host__ __device__ __forceinline__ int attn_chunk(int ctx, int fixed) {
-  if (fixed > 0) return fixed;
-  int c = (ctx + 63) / 64;          // aim for ~64 splits per KV head
-  c = (c + 15) & ~15;
-  return c < 16 ? 16 : (c > 64 ? 64 : c);
-}
-
-constexpr int kAttnMaxChunk = 64;
-constexpr int kAttnMaxGroup = 8;
-
-template <typename KVT>
-__device__ __forceinline__ float kv_load(const KVT* p);
-template <>
-__device__ __forceinline__ float kv_load<float>(const float* p) { return *p; }
-template <>
-__device__ __forceinline__ float kv_load<__half>(const __half* p) { return __half2float(*p); }
 template <typename KVT>
 __device__ __forceinline__ KVT kv_cvt(float v);
 template <>
@@ -641,21 +479,6 @@ __device__ __forceinline__ float kv_cvt<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ __half kv_cvt<__half>(float v) { return __float2half_rn(v); }
 
-template <typename KVT>
-__device__ __forceinline__ void kv_row4(const KVT* p, float* dst);  // 4 consecutive values
-template <>
-__device__ __forceinline__ void kv_row4<float>(const float* p, float* dst) {
-  *reinterpret_cast<float4*>(dst) = __ldcg(reinterpret_cast<const float4*>(p));
-}
-template <>
-__device__ __forceinline__ void kv_row4<__half>(const __half* p, float* dst) {
-  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-  *reinterpret_cast<float4*>(dst) = make_float4(a.x, a.y, b.x, b.y);
-}
-
-constexpr int kKsStride = kHeadDim + 4;  // padded K rows (keeps float4 alignment)
 
 __device__ __forceinline__ void block_best(float& v, uint32_t& id, float* sv, uint32_t* si) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = kCtaThreads >> 5;
@@ -681,174 +504,6 @@ __device__ __forceinline__ void block_best(float& v, uint32_t& id, float* sv, ui
       v = sv[i];
       id = si[i];
     }
-}
-
-// One block per (split, kv head): RoPE on the group's q heads, RoPE + append
-// of the new k/v row when this split holds position pos, split-K partials for
-// the group's q heads (one warp per head), then the last block of the KV head
-// to finish merges all splits (ATTN_COMBINE) and writes the output.
-template <typename KVT>
-__device__ void attn_item(const AttnArgs& a, int split, int kvh, float* attn_smem, int pdl) {
-  __shared__ __align__(16) float qs[kAttnMaxGroup][kHeadDim];
-  __shared__ float sc[kAttnMaxGroup][kAttnMaxChunk];
-  __shared__ bool last;
-  float* ks = attn_smem;                              // [chunk][kKsStride]
-  float* vs = attn_smem + kAttnMaxChunk * kKsStride;  // [chunk][128]
-  // The position and the cached K/V rows (t != pos) were written before the
-  // producing GEMV started (it triggers this launch only after its own
-  // griddepcontrol.wait), so they are read before this kernel's wait; only
-  // this step's q/k/v rows need it.
-  const int pos = a.pos ? __ldcg(a.pos) : a.fixed_pos;
-  const int ctx = pos + 1;
-  const int chunk = attn_chunk(ctx, a.chunk);
-  const int nsplit = (ctx + chunk - 1) / chunk;
-  if (split >= nsplit) return;
-  const int G = a.nh / a.nkv, hd = kHeadDim, half = hd / 2;
-  const int kvd = a.nkv * hd;
-  const int f16 = a.kv_f16;
-  const float* cs = a.cosT + (size_t)pos * hd;
-  const float* sn = a.sinT + (size_t)pos * hd;
-  const int t0 = split * chunk;
-  const int t1 = min(t0 + chunk, ctx);
-  const int len = t1 - t0;
-  KVT* kc = reinterpret_cast<KVT*>(a.kc);
-  KVT* vc = reinterpret_cast<KVT*>(a.vc);
-  // the cached K/V rows first: they do not depend on this step's q/k/v
-  for (int idx = threadIdx.x; idx < len * (hd / 4); idx += kCtaThreads) {
-    const int tt = idx / (hd / 4), d = 4 * (idx % (hd / 4)), t = t0 + tt;
-    if (t == pos) continue;
-    kv_row4<KVT>(kc + (size_t)t * kvd + kvh * hd + d, ks + tt * kKsStride + d);
-    kv_row4<KVT>(vc + (size_t)t * kvd + kvh * hd + d, vs + tt * hd + d);
-  }
-  if (pdl) {
-    pdl_wait();
-    pdl_launch_dependents();
-  }
-  for (int idx = threadIdx.x; idx < G * half; idx += kCtaThreads) {
-    const int hh = idx / half, j = idx % half;
-    const float* q = a.qkv + (kvh * G + hh) * hd;
-    float lo = __ldcg(q + j), hi = __ldcg(q + j + half);
-    rope_pair(lo, hi, cs[j], sn[j], f16);
-    if (f16) round_h2(lo, hi);  // ATTN_PARTIAL_F16 reads q through f16
-    qs[hh][j] = lo;
-    qs[hh][j + half] = hi;
-  }
-  if (pos >= t0 && pos < t1) {  // ROPE_QK on k, then the KV append (runtime.js:1509-1514)
-    const int tn = pos - t0;
-    const float* k = a.qkv + a.nh * hd + kvh * hd;
-    const float* v = a.qkv + a.nh * hd + kvd + kvh * hd;
-    for (int j = threadIdx.x; j < half; j += kCtaThreads) {
-      float lo = __ldcg(k + j), hi = __ldcg(k + j + half);
-      rope_pair(lo, hi, cs[j], sn[j], f16);
-      float rl = lo, rh = hi;
-      if (f16) round_h2(rl, rh);
-      ks[tn * kKsStride + j] = rl;
-      ks[tn * kKsStride + j + half] = rh;
-      kc[(size_t)pos * kvd + kvh * hd + j] = kv_cvt<KVT>(lo);
-      kc[(size_t)pos * kvd + kvh * hd + j + half] = kv_cvt<KVT>(hi);
-    }
-    for (int j = threadIdx.x; j < hd; j += kCtaThreads) {
-      const float vj = __ldcg(v + j);
-      vs[tn * hd + j] = f16 ? round_h(vj) : vj;
-      vc[(size_t)pos * kvd + kvh * hd + j] = kv_cvt<KVT>(vj);
-    }
-  }
-  cta_sync();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float scale = 1.0f / sqrtf((float)hd);
-  for (int hh = warp; hh < G; hh += kCtaThreads / 32) {
-    const float4 q4 = *reinterpret_cast<const float4*>(&qs[hh][4 * lane]);
-    float m = -1e30f;
-    for (int tt = 0; tt < len; tt++) {
-      const float4 k4 = *reinterpret_cast<const float4*>(ks + tt * kKsStride + 4 * lane);
-      float p = __fmul_rn(q4.x, k4.x);
-      p = __fadd_rn(p, __fmul_rn(q4.y, k4.y));
-      p = __fadd_rn(p, __fmul_rn(q4.z, k4.z));
-      p = __fadd_rn(p, __fmul_rn(q4.w, k4.w));
-      const float sv = __fmul_rn(warp_sum(p), scale);
-      if (lane == 0) sc[hh][tt] = sv;
-      m = fmaxf(m, sv);
-    }
-    __syncwarp();
-    float z = 0.f;
-    for (int tt = lane; tt < len; tt += 32) {
-      const float ev = expf(sc[hh][tt] - m);
-      sc[hh][tt] = ev;
-      z += ev;
-    }
-    z = warp_sum(z);
-    __syncwarp();
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int tt = 0; tt < len; tt++) {
-      const float ev = sc[hh][tt];
-      const float4 v4 = *reinterpret_cast<const float4*>(vs + tt * hd + 4 * lane);
-      acc.x = __fadd_rn(acc.x, __fmul_rn(ev, v4.x));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(ev, v4.y));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(ev, v4.z));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(ev, v4.w));
-    }
-    const int h = kvh * G + hh;
-    if (nsplit == 1) {  // one split: the combine is a plain 1/Z scaling (ATTN_COMBINE with nsplit 1)
-      float4 p = acc;
-      if (f16) {
-        round_h2(p.x, p.y);
-        round_h2(p.z, p.w);
-      }
-      // M = m, Z = z * e^0, o = (e^0 * po) / Z
-      const float invZ = 1.0f / z;
-      *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
-          make_float4(__fmul_rn(p.x, invZ), __fmul_rn(p.y, invZ), __fmul_rn(p.z, invZ), __fmul_rn(p.w, invZ));
-      continue;
-    }
-    *reinterpret_cast<float4*>(a.po + ((size_t)h * a.max_splits + split) * hd + 4 * lane) = acc;
-    if (lane == 0) {
-      a.pm[h * a.max_splits + split] = m;
-      a.pz[h * a.max_splits + split] = z;
-    }
-  }
-  if (nsplit == 1) {
-    cta_sync();
-    return;
-  }
-  // ---- last block of this KV head merges the splits (ATTN_COMBINE[_F16],
-  // kernels.js:346-388)
-  __threadfence();
-  cta_sync();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(a.counters + kvh, 1u);
-    last = prev == (unsigned)nsplit - 1;
-  }
-  cta_sync();
-  if (!last) return;
-  __threadfence();
-  for (int hh = warp; hh < G; hh += kCtaThreads / 32) {
-    const int h = kvh * G + hh;
-    const float* pm = a.pm + h * a.max_splits;
-    const float* pz = a.pz + h * a.max_splits;
-    float M = -1e30f;
-    for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(pm + s2));
-    float Z = 0.f;
-    for (int s2 = 0; s2 < nsplit; s2++) Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), expf(__ldcg(pm + s2) - M)));
-    const float invZ = 1.0f / Z;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s2 = 0; s2 < nsplit; s2++) {
-      const float wgt = expf(__ldcg(pm + s2) - M);
-      float4 p = __ldcg(reinterpret_cast<const float4*>(a.po + ((size_t)h * a.max_splits + s2) * hd + 4 * lane));
-      if (f16) {
-        round_h2(p.x, p.y);
-        round_h2(p.z, p.w);
-      }
-      acc.x = __fadd_rn(acc.x, __fmul_rn(wgt, p.x));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(wgt, p.y));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(wgt, p.z));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(wgt, p.w));
-    }
-    *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
-        make_float4(__fmul_rn(acc.x, invZ), __fmul_rn(acc.y, invZ), __fmul_rn(acc.z, invZ),
-                    __fmul_rn(acc.w, invZ));
-  }
-  if (threadIdx.x == 0) a.counters[kvh] = 0u;  // ready for the next launch
-  cta_sync();
 }
 
 }  // namespace eg

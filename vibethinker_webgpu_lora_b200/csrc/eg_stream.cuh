@@ -22,8 +22,9 @@ namespace eg {
 constexpr int kG4Warps = 16;                    // consumer warps
 constexpr int kG4Threads = kG4Warps * 32 + 64;  // + producer warp + epilogue warp
 
-// int4 block: R row sets x (1024 bytes of nibbles in fragment order + 16 f32
-// group scales); int8 block: 16 rows x 128 bytes in fragment order.
+// int4 block: R row sets x (1024 bytes of nibbles in fragment order), then
+// the 16 R f32 group scales as (row i, row i + 8) pairs; int8 block: 16 rows x
+// 128 bytes in fragment order.
 __host__ __device__ constexpr int q4_block_bytes(int R) { return R * 1088; }
 constexpr int kQ8Block = 2048;
 
@@ -110,18 +111,18 @@ __device__ __forceinline__ void tile_handoff(TileRed<R>& red, uint64_t* tile_ful
   if (lane == 0) mbar_arrive(&tile_full[b]);
 }
 
-// Consumers (warps 0-15) of one int4 run.  xb / xcor / xmul: the staged
-// activation (stage_xd).  After a failed wait a warp goes on without waiting
+// Consumers (warps 0-15) of one int4 run.  xb / xcm: the staged activation
+// (stage_xd).  Lanes gq >= 4 feed B columns 4-7, whose results are never
+// used: they load a copy of plane gq & 3 instead of a zero (no predication).  After a failed wait a warp goes on without waiting
 // (its results are void; the host sees the error word).
 template <int R>
 __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64_t* empty,
                                int stages, int stage_bytes, int cap, int t_lo, int t_hi, int gpr,
-                               const uint2* xb, const int* xcor, const float* xmul,
-                               TileRed<R>& red, uint64_t* tile_full, uint64_t* tile_free,
+                               const uint2* xb, const int2* xcm, TileRed<R>& red,
+                               uint64_t* tile_full, uint64_t* tile_free,
                                RingPos& rp, int& tj, bool& dead, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gq = lane >> 2, t = lane & 3;
-  const bool bl = gq < 4;  // lanes holding a digit plane (B columns 0-3)
   const int blk = q4_block_bytes(R);
   const int nitems = (t_hi - t_lo) * gpr;
   const int nchunks = (nitems + cap - 1) / cap;
@@ -147,13 +148,9 @@ __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64
       }
       const int g = i - j * gpr;
       const unsigned char* bp = stage + (size_t)(i - chunk_lo) * blk;
-      // B: digit plane gq of this group's 4 k32 blocks (zero for gq >= 4)
-      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
-      if (bl) {
-        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 4);
-        X0 = xp[0];
-        X1 = xp[1];
-      }
+      // B: digit plane gq & 3 of this group's 4 k32 blocks
+      const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + (gq & 3)) * 4 + t) * 4);
+      const uint4 X0 = xp[0], X1 = xp[1];
       uint4 A[R], B[R];
 #pragma unroll
       for (int r = 0; r < R; r++) {
@@ -171,12 +168,14 @@ __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64
         imma16832(cc[r], nib_lo_u8(A[r].w), nib_lo_u8(B[r].w), nib_hi_u8(A[r].w), nib_hi_u8(B[r].w), X1.z, X1.w);
       }
       if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
-        const int cor = xcor[2 * g + t];
-        const float mul = xmul[2 * g + t];
-        const float* sc = reinterpret_cast<const float*>(bp + R * 1024);
+        const int2 cm = xcm[2 * g + t];
+        const int cor = cm.x;
+        const float mul = __int_as_float(cm.y);
+        const float2* sc = reinterpret_cast<const float2*>(bp + R * 1024);  // (row gq, row gq+8)
 #pragma unroll
         for (int r = 0; r < R; r++) {
-          const float sa = sc[16 * r + gq] * mul, sb = sc[16 * r + gq + 8] * mul;
+          const float2 s2 = sc[8 * r + gq];
+          const float sa = s2.x * mul, sb = s2.y * mul;
           acc[r][0] = fmaf(sa, (float)(cc[r][0] + 256 * cc[r][1] - cor), acc[r][0]);
           acc[r][1] = fmaf(sb, (float)(cc[r][2] + 256 * cc[r][3] - cor), acc[r][1]);
         }
@@ -204,7 +203,6 @@ static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full,
                                bool& dead, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gq = lane >> 2, t = lane & 3;
-  const bool bl = gq < 4;
   const int nitems = (t_hi - t_lo) * gpr;
   const int nchunks = (nitems + cap - 1) / cap;
   if (nchunks == 0) return;
@@ -227,12 +225,9 @@ static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full,
       }
       const int g = i - j * gpr;
       const unsigned char* bp = stage + (size_t)(i - chunk_lo) * kQ8Block;
-      uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
-      if (bl) {
-        const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + gq) * 4 + t) * 8);
-        X0 = xp[0];
-        X1 = xp[1];
-      }
+      // B: plane gq & 3 (columns 4-7 unused, as in consume_q4_run)
+      const uint4* xp = reinterpret_cast<const uint4*>(xb + ((g * 4 + (gq & 3)) * 4 + t) * 8);
+      const uint4 X0 = xp[0], X1 = xp[1];
       const uint4 A0 = *reinterpret_cast<const uint4*>(bp + lane * 16);
       const uint4 A1 = *reinterpret_cast<const uint4*>(bp + 512 + lane * 16);
       const uint4 B0 = *reinterpret_cast<const uint4*>(bp + 1024 + lane * 16);
