@@ -116,7 +116,9 @@ EG_API eg_status eg_upload_quantized(eg_rt* rt, const char* name, int kind,
  * (q,k,v,o,gate,up,down) t=16i+1+p, bias b t=16i+8+b), norms = 1. */
 EG_API eg_status eg_build_synthetic(eg_rt* rt, uint64_t seed, double std_w);
 /* uploader.finalize + schema.assertComplete (model_schema.js:117-124):
- * "missing N required tensor(s): ..." ; then RoPE tables and KV cache. */
+ * "missing N required tensor(s): ..." ; then RoPE tables and KV cache, and
+ * the conversion of every int4 matrix and of the LM head into the library's
+ * streaming layout (the reference-layout int4 copies are freed). */
 EG_API eg_status eg_finalize(eg_rt* rt);
 
 /* ---------------- decode (runtime.js:1466-1793) --------------------------- */
