@@ -128,6 +128,24 @@ def dist_setup():
     return ws, rank, local
 
 
+def max_over_ranks(ms, ws, device):
+    """The job's time is the slowest rank's device time (weak scaling: every
+    rank decodes its own sequences on its own replica)."""
+    if ws <= 1:
+        return ms
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    return float(t.item())
+
+
+def job_throughput(ws, steps, ms):
+    """Whole-job tok/s: every rank decoded `steps` tokens within `ms`."""
+    return ws * steps / (ms / 1000.0)
+
+
 def positions(start, period, n, cap):
     """Chunked start positions cycling in [start, start+period)."""
     out, done, pos = [], 0, start
@@ -184,13 +202,7 @@ def run_ours(args, ws, rank, local):
         e1.record(st)
         rt.sync()
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if ws > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1), ws, dev)
     clocks = ck.summary()
     launches = rt.lastDispatchCount * args.steps
 
@@ -218,7 +230,7 @@ def run_ours(args, ws, rank, local):
     mean_ctx = n_prompt + period / 2
     step_bytes = weights + kv_per_pos * mean_ctx
     hbm, peak_kind = peaks()
-    value = ws * args.steps / (ms / 1000.0)
+    value = job_throughput(ws, args.steps, ms)
     ms_per_step = ms / args.steps
     achieved = GATE_UP_BYTES / (gu_us * 1e-6) / 1e9
     result = {
