@@ -14,15 +14,21 @@ namespace eg {
 constexpr int kGroup = 128;   // int4 group size (quantize.js:81, kernels.js:901 `bk >> 7`)
 constexpr int kHeadDim = 128;  // attention kernels are specialised for head_dim 128
 
-// Nibbles 0,2,4,6 (lo) or 1,3,5,7 (hi) of a packed int4 word (8
-// two's-complement nibbles, nibble j = k 8c+j, quantize.js:107) as four bytes
-// q + 8 in [0, 15] (offset binary): one LOP3 (+ one shift).
+// Nibbles 0,2,4,6 of a packed int4 word (8 two's-complement nibbles, nibble
+// j = k 8c+j, quantize.js:107) as four bytes q + 8 in [0, 15] (offset
+// binary): one LOP3.
 EG_DEV uint32_t nib_lo_u8(uint32_t w) {
   uint32_t d;
   asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(w), "r"(0x0F0F0F0Fu), "r"(0x08080808u));
   return d;
 }
-EG_DEV uint32_t nib_hi_u8(uint32_t w) { return nib_lo_u8(w >> 4); }
+// Nibbles 1,3,5,7 in place: four bytes 16 (q + 8) in [0, 240], one LOP3 (the
+// factor 16 is taken out of the matching activation elements).
+EG_DEV uint32_t nib_hi16_u8(uint32_t w) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(w), "r"(0xF0F0F0F0u), "r"(0x80808080u));
+  return d;
+}
 
 // D = A(16x32 u8, row) * B(32x8 s8, col) + C, s32 accumulate (exact).
 EG_DEV void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,

@@ -103,6 +103,17 @@ __device__ __forceinline__ void bar_sync_n() {
   asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
 }
 template <int NT>
+__device__ __forceinline__ float block_max_n(float v, float* sbuf) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  bar_sync_n<NT>();
+  if (lane == 0) sbuf[warp] = v;
+  bar_sync_n<NT>();
+  float r = sbuf[0];
+  for (int i = 1; i < NT / 32; i++) r = fmaxf(r, sbuf[i]);
+  return r;
+}
+template <int NT>
 __device__ __forceinline__ float block_sum_n(float v, float* sbuf) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   v = warp_sum(v);
@@ -170,20 +181,26 @@ __device__ __forceinline__ void setup_x(const XSrc& s, int K, XCtx& c, float* sr
 }
 
 
-// Activation prologue of the integer-MMA int4 GEMV.  Each 128-wide group G
-// is put in fixed point, X = round(x * 2^f_G) with |X| < 2^30, and X is
-// written as four balanced base-256 digits d_p in [-128, 127]
-// (X = sum_p d_p 256^p; bytes of (X + 0x80808080) ^ 0x80808080), one s8
-// plane per MMA column.  Per group it stores
+// Activation prologue of the integer-MMA int4 GEMV.  The vector is put in
+// fixed point with one exponent f (from its largest |x|): even elements
+// (they meet the low nibbles of the weights) as X = round(x * 2^f), |X| <
+// 2^30, odd elements (they meet the high nibbles, which the consumers use in
+// place as 16 (q + 8) bytes, without a shift) as X = round(x * 2^(f-4)), so
+// both halves carry the same scale into one accumulator.  X is written as
+// four balanced base-256 digits d_p in [-128, 127] (X = sum_p d_p 256^p;
+// bytes of (X + 0x80808080) ^ 0x80808080), one s8 plane per MMA column:
 //   xb:   the m16n8k32 B fragments, uint2 [G][p][t][m] (lane (p, t) of MMA m
 //         holds plane p of elements 8(4m+t) + {0,2,4,6} and + {1,3,5,7}),
-//   xcm:  per column pair (2i, 2i+1), i = 0, 1: .x = 8 (S_{2i} + 256 S_{2i+1}),
-//         S_p = sum of plane p over the group (removes the +8 offset of the u8
-//         weights); .y = the f32 bits of 2^-f_G * 65536^i (the pair's weight).
+//   xcor: per group and column pair (2i, 2i+1): the weight-offset correction
+//         8 (W_{2i} + 256 W_{2i+1}), W_p = sum over the group of plane p of the
+//         even elements + 16 x that of the odd elements,
+//   *xf:  f; a row's dot product is 2^-f (C_0 + 65536 C_1), C_i the sum over
+//         groups of scale * (column pair i value - xcor).
 // pdl: the norm weights are read first, then griddepcontrol.wait, then the
 // input (which the previous kernel writes).
 template <int MAXU, bool NORM, int NT = kCtaThreads>
-__device__ void stage_xd(const XSrc& s, int K, uint2* xb, int2* xcm, float* sred, int pdl) {
+__device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, int* xf, float* sred,
+                         int pdl) {
   const int K8 = K / 8;
   float v[MAXU][8];
   float gw[NORM ? MAXU : 1][8];
@@ -261,26 +278,28 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int2* xcm, float* sred
         }
       }
   }
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXU; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
+  am = block_max_n<NT>(am, sred);
+  // am < 2^ex, ex from the exponent field (0 and subnormals: f = 126)
+  const int ex = ((__float_as_int(am) >> 23) & 0xFF) - 126;
+  const int f = min(30 - ex, 126);
+  const float se = __int_as_float((127 + f) << 23);  // 2^f (even elements)
+  const float so = __int_as_float((123 + f) << 23);  // 2^(f-4) (odd elements)
+  if (threadIdx.x == 0) *xf = f;
 #pragma unroll
   for (int i = 0; i < MAXU; i++) {
     const int u = threadIdx.x + i * NT;
-    float am = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
-    // the 16 units of a group sit in 16 consecutive lanes (K8 % 16 == 0)
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    // am < 2^ex, ex from the exponent field (0 and subnormals: f = 126)
-    const int ex = ((__float_as_int(am) >> 23) & 0xFF) - 126;
-    const int f = min(30 - ex, 126);
-    const float sf = __int_as_float((127 + f) << 23);  // 2^f
     uint32_t D[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      const int X = __float2int_rn(v[i][j] * sf);  // exact scaling, |X| < 2^30
-      D[j] = ((uint32_t)X + 0x80808080u) ^ 0x80808080u;   // balanced base-256 digits
+      const int X = __float2int_rn(v[i][j] * ((j & 1) ? so : se));  // exact scaling
+      D[j] = ((uint32_t)X + 0x80808080u) ^ 0x80808080u;            // balanced base-256 digits
     }
-    int S[4];
+    int W[4];
     uint2 pl[4];
 #pragma unroll
     for (int p = 0; p < 4; p++) {
@@ -289,19 +308,20 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int2* xcm, float* sred
       const uint32_t o0 = __byte_perm(D[1], D[3], sel), o1 = __byte_perm(D[5], D[7], sel);
       pl[p].x = __byte_perm(e0, e1, 0x5410);
       pl[p].y = __byte_perm(o0, o1, 0x5410);
-      S[p] = __dp4a((int)pl[p].x, 0x01010101, __dp4a((int)pl[p].y, 0x01010101, 0));
+      W[p] = __dp4a((int)pl[p].x, 0x01010101, 16 * __dp4a((int)pl[p].y, 0x01010101, 0));
     }
+    // the 16 units of a group sit in 16 consecutive lanes (K8 % 16 == 0)
 #pragma unroll
     for (int p = 0; p < 4; p++)
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) S[p] += __shfl_xor_sync(0xffffffffu, S[p], o);
+      for (int o = 8; o > 0; o >>= 1) W[p] += __shfl_xor_sync(0xffffffffu, W[p], o);
     if (u >= K8) continue;
     const int G = u >> 4, q = u & 15, m = q >> 2, t = q & 3;
 #pragma unroll
     for (int p = 0; p < 4; p++) xb[((G * 4 + p) * 4 + t) * 4 + m] = pl[p];
     if (q == 0) {
-      xcm[2 * G] = make_int2(8 * (S[0] + 256 * S[1]), (127 - f) << 23);      // 2^-f
-      xcm[2 * G + 1] = make_int2(8 * (S[2] + 256 * S[3]), (143 - f) << 23);  // 2^(16-f)
+      xcor[2 * G] = 8 * (W[0] + 256 * W[1]);
+      xcor[2 * G + 1] = 8 * (W[2] + 256 * W[3]);
     }
   }
   bar_sync_n<NT>();

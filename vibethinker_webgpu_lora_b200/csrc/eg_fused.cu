@@ -269,7 +269,8 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
       {
         const Run r = run_of(a, l, PH_QKV);
         const int gpr = a.H / kGroup;
-        int2* xcm = reinterpret_cast<int2*>(xb + (size_t)gpr * 64);
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        int* xf = xcor + 2 * gpr;
         XSrc x = {};
         x.mode = li == 0 ? X_EMBED_RMS : X_RMS;
         x.x = a.hidden;
@@ -284,9 +285,9 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         x.fixed_id = next_id;
         x.hidden_out = a.hidden;
         if (r.t_lo < r.t_hi) {
-          stage_xd<1, true, NT>(x, a.H, xb, xcm, sred, 0);
+          stage_xd<1, true, NT>(x, a.H, xb, xcor, xf, sred, 0);
           consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
-                            xb, xcm, red1, tile_full, tile_free, rp, tj, dead, a.err);
+                            xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
       if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb : -1)) return;
@@ -323,14 +324,15 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
       {
         const Run r = run_of(a, l, PH_O);
         const int gpr = a.QD / kGroup;
-        int2* xcm = reinterpret_cast<int2*>(xb + (size_t)gpr * 64);
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        int* xf = xcor + 2 * gpr;
         XSrc x = {};
         x.mode = X_PLAIN;
         x.x = a.attn;
         if (r.t_lo < r.t_hi) {
-          stage_xd<1, false, NT>(x, a.QD, xb, xcm, sred, 0);
+          stage_xd<1, false, NT>(x, a.QD, xb, xcor, xf, sred, 0);
           consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
-                            xb, xcm, red1, tile_full, tile_free, rp, tj, dead, a.err);
+                            xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
       if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 2 : -1)) return;
@@ -339,7 +341,8 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
       {
         const Run r = run_of(a, l, PH_GU);
         const int gpr = a.H / kGroup;
-        int2* xcm = reinterpret_cast<int2*>(xb + (size_t)gpr * 64);
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        int* xf = xcor + 2 * gpr;
         XSrc x = {};
         x.mode = X_RMS;
         x.x = a.hidden;
@@ -347,9 +350,9 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         x.eps = a.eps;
         x.f16 = a.f16;
         if (r.t_lo < r.t_hi) {
-          stage_xd<1, true, NT>(x, a.H, xb, xcm, sred, 0);
+          stage_xd<1, true, NT>(x, a.H, xb, xcor, xf, sred, 0);
           consume_q4_run<2>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
-                            xb, xcm, red2, tile_full, tile_free, rp, tj, dead, a.err);
+                            xb, xcor, xf, red2, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
       if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 3 : -1)) return;
@@ -358,14 +361,15 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
       {
         const Run r = run_of(a, l, PH_DOWN);
         const int gpr = a.I / kGroup;
-        int2* xcm = reinterpret_cast<int2*>(xb + (size_t)gpr * 64);
+        int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);
+        int* xf = xcor + 2 * gpr;
         XSrc x = {};
         x.mode = X_PLAIN;
         x.x = a.tmp;
         if (r.t_lo < r.t_hi) {
-          stage_xd<3, false, NT>(x, a.I, xb, xcm, sred, 0);
+          stage_xd<3, false, NT>(x, a.I, xb, xcor, xf, sred, 0);
           consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
-                            xb, xcm, red1, tile_full, tile_free, rp, tj, dead, a.err);
+                            xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
       if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 4 : -1)) return;

@@ -109,7 +109,8 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
   uint64_t* tile_free = tile_full + 2;
   const int gpr = p.K / kGroup;
   uint2* xb = reinterpret_cast<uint2*>(g4_smem + p.xs_off);  // [gpr][4][4][4]
-  int2* xcm = reinterpret_cast<int2*>(xb + (size_t)gpr * 64);  // [gpr][2]
+  int* xcor = reinterpret_cast<int*>(xb + (size_t)gpr * 64);   // [gpr][2]
+  int* xf = xcor + 2 * gpr;
   unsigned char* ring = g4_smem + p.ring_off;
   const int tiles = (p.N + 15) / 16;
   const int t_lo = (int)((long long)tiles * blockIdx.x / gridDim.x);
@@ -131,13 +132,13 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
     epilogue_q4_run<R>(p.e, t_lo, t_hi, red, tile_full, tile_free, tj, true, p.err);
     return;
   }
-  stage_xd<MAXU, NORM, NT>(p.x, p.K, xb, xcm, sred, p.pdl);
+  stage_xd<MAXU, NORM, NT>(p.x, p.K, xb, xcor, xf, sred, p.pdl);
   // the next kernel may start once this one's predecessors are complete (the
   // attention kernel relies on that to read the position early)
   if (p.pdl) pdl_launch_dependents();
   bool dead = false;
-  consume_q4_run<R>(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xcm,
-                    red, tile_full, tile_free, rp, tj, dead, p.err);
+  consume_q4_run<R>(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xcor,
+                    xf, red, tile_full, tile_free, rp, tj, dead, p.err);
 }
 
 // Shared-memory plan of one launch (bytes): barriers, x digit planes + group

@@ -85,12 +85,19 @@ struct TileRed {
 
 // Consumer side of one hand-off: sum the lanes t = 0, 1, publish the warp's
 // partial rows in red[tj & 1] once the epilogue warp released that buffer.
+// sc0 / sc1: the final factor of lanes t = 0 / t = 1 (column pairs 0 / 1).
 template <int R>
 __device__ __forceinline__ void tile_handoff(TileRed<R>& red, uint64_t* tile_full,
                                              uint64_t* tile_free, int tj, float (&acc)[R][2],
-                                             bool& dead, int* err) {
+                                             float sc0, float sc1, bool& dead, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gq = lane >> 2, t = lane & 3;
+  const float sc = t ? sc1 : sc0;
+#pragma unroll
+  for (int r = 0; r < R; r++) {
+    acc[r][0] *= sc;
+    acc[r][1] *= sc;
+  }
 #pragma unroll
   for (int r = 0; r < R; r++) {
     acc[r][0] += __shfl_xor_sync(0xffffffffu, acc[r][0], 1);
@@ -111,15 +118,15 @@ __device__ __forceinline__ void tile_handoff(TileRed<R>& red, uint64_t* tile_ful
   if (lane == 0) mbar_arrive(&tile_full[b]);
 }
 
-// Consumers (warps 0-15) of one int4 run.  xb / xcm: the staged activation
-// (stage_xd).  Lanes gq >= 4 feed B columns 4-7, whose results are never
+// Consumers (warps 0-15) of one int4 run.  xb / xcor / xf: the staged
+// activation (stage_xd).  Lanes gq >= 4 feed B columns 4-7, whose results are never
 // used: they load a copy of plane gq & 3 instead of a zero (no predication).  After a failed wait a warp goes on without waiting
 // (its results are void; the host sees the error word).
 template <int R>
 __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64_t* empty,
                                int stages, int stage_bytes, int cap, int t_lo, int t_hi, int gpr,
-                               const uint2* xb, const int2* xcm, TileRed<R>& red,
-                               uint64_t* tile_full, uint64_t* tile_free,
+                               const uint2* xb, const int* xcor, const int* xf,
+                               TileRed<R>& red, uint64_t* tile_full, uint64_t* tile_free,
                                RingPos& rp, int& tj, bool& dead, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gq = lane >> 2, t = lane & 3;
@@ -130,6 +137,8 @@ __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64
   float acc[R][2];
 #pragma unroll
   for (int r = 0; r < R; r++) acc[r][0] = acc[r][1] = 0.f;
+  const int f = *xf;
+  const float sc0 = __int_as_float((127 - f) << 23), sc1 = __int_as_float((143 - f) << 23);
   int chunk = 0, chunk_lo = 0;
   if (!dead && !mbar_wait(&full[rp.st], rp.ph, err)) dead = true;
   const unsigned char* stage = ring + (size_t)rp.st * stage_bytes;
@@ -162,26 +171,23 @@ __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64
 #pragma unroll
       for (int r = 0; r < R; r++) {
         cc[r][0] = cc[r][1] = cc[r][2] = cc[r][3] = 0;
-        imma16832(cc[r], nib_lo_u8(A[r].x), nib_lo_u8(B[r].x), nib_hi_u8(A[r].x), nib_hi_u8(B[r].x), X0.x, X0.y);
-        imma16832(cc[r], nib_lo_u8(A[r].y), nib_lo_u8(B[r].y), nib_hi_u8(A[r].y), nib_hi_u8(B[r].y), X0.z, X0.w);
-        imma16832(cc[r], nib_lo_u8(A[r].z), nib_lo_u8(B[r].z), nib_hi_u8(A[r].z), nib_hi_u8(B[r].z), X1.x, X1.y);
-        imma16832(cc[r], nib_lo_u8(A[r].w), nib_lo_u8(B[r].w), nib_hi_u8(A[r].w), nib_hi_u8(B[r].w), X1.z, X1.w);
+        imma16832(cc[r], nib_lo_u8(A[r].x), nib_lo_u8(B[r].x), nib_hi16_u8(A[r].x), nib_hi16_u8(B[r].x), X0.x, X0.y);
+        imma16832(cc[r], nib_lo_u8(A[r].y), nib_lo_u8(B[r].y), nib_hi16_u8(A[r].y), nib_hi16_u8(B[r].y), X0.z, X0.w);
+        imma16832(cc[r], nib_lo_u8(A[r].z), nib_lo_u8(B[r].z), nib_hi16_u8(A[r].z), nib_hi16_u8(B[r].z), X1.x, X1.y);
+        imma16832(cc[r], nib_lo_u8(A[r].w), nib_lo_u8(B[r].w), nib_hi16_u8(A[r].w), nib_hi16_u8(B[r].w), X1.z, X1.w);
       }
       if (t < 2) {  // columns 2t, 2t+1 = digit planes 2t, 2t+1
-        const int2 cm = xcm[2 * g + t];
-        const int cor = cm.x;
-        const float mul = __int_as_float(cm.y);
+        const int cor = xcor[2 * g + t];
         const float2* sc = reinterpret_cast<const float2*>(bp + R * 1024);  // (row gq, row gq+8)
 #pragma unroll
         for (int r = 0; r < R; r++) {
           const float2 s2 = sc[8 * r + gq];
-          const float sa = s2.x * mul, sb = s2.y * mul;
-          acc[r][0] = fmaf(sa, (float)(cc[r][0] + 256 * cc[r][1] - cor), acc[r][0]);
-          acc[r][1] = fmaf(sb, (float)(cc[r][2] + 256 * cc[r][3] - cor), acc[r][1]);
+          acc[r][0] = fmaf(s2.x, (float)(cc[r][0] + 256 * cc[r][1] - cor), acc[r][0]);
+          acc[r][1] = fmaf(s2.y, (float)(cc[r][2] + 256 * cc[r][3] - cor), acc[r][1]);
         }
       }
     }
-    tile_handoff<R>(red, tile_full, tile_free, tj, acc, dead, err);
+    tile_handoff<R>(red, tile_full, tile_free, tj, acc, sc0, sc1, dead, err);
     tj++;
   }
   // release the current stage and wait/release the later ones this warp had
@@ -243,7 +249,7 @@ static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full,
         acc[0][1] = fmaf(mul, (float)(cc[2] + 256 * cc[3]), acc[0][1]);
       }
     }
-    tile_handoff<1>(red, tile_full, tile_free, tj, acc, dead, err);
+    tile_handoff<1>(red, tile_full, tile_free, tj, acc, 1.f, 1.f, dead, err);
     tj++;
   }
   for (; chunk < nchunks; chunk++) {
