@@ -31,6 +31,8 @@
 
 namespace eg {
 
+constexpr int kFusedWarps = 16;  // consumer warps (attention items need 512 threads)
+constexpr int kFusedThreads = kFusedWarps * 32 + 64;
 constexpr int kFStageBytes = 34816;  // 32 int4 blocks, 16 gate/up blocks, 17 int8 blocks
 constexpr int kFMaxStages = 6;
 constexpr int kFBarBytes = 256;      // ring + tile mbarriers
@@ -97,7 +99,7 @@ __device__ __forceinline__ Run run_lm(const FusedArgs& a) {
 // false, uniformly, when the launch is being abandoned.
 __device__ bool phase_barrier(const FusedArgs& a, unsigned& epoch, const int* epi_done,
                               int& pdone, bool epi, int* s_ok, int prof_ph) {
-  constexpr int NT = kG4Warps * 32;
+  constexpr int NT = kFusedWarps * 32;
   bar_sync_n<NT>();
   if (threadIdx.x == 0) {
     int ok = 1;
@@ -142,11 +144,11 @@ __device__ bool phase_barrier(const FusedArgs& a, unsigned& epoch, const int* ep
 // warps' worth), so a thread gets at most 96 registers.
 template <typename KVT>
 __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int kFStages) {
-  constexpr int NT = kG4Warps * 32;
+  constexpr int NT = kFusedWarps * 32;
   extern __shared__ __align__(128) unsigned char dsm[];
   __shared__ float sred[32];
-  __shared__ TileRed<1> red1;
-  __shared__ TileRed<2> red2;
+  __shared__ TileRed<kFusedWarps, 1> red1;
+  __shared__ TileRed<kFusedWarps, 2> red2;
   __shared__ AttnSmem asm_;
   __shared__ int epi_done;  // phases the epilogue warp has finished
   __shared__ int s_ok;
@@ -162,10 +164,10 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
   if (threadIdx.x == 0) {
     for (int i = 0; i < kFStages; i++) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kG4Warps);
+      mbar_init(&empty[i], kFusedWarps);
     }
     for (int i = 0; i < 2; i++) {
-      mbar_init(&tile_full[i], kG4Warps);
+      mbar_init(&tile_full[i], kFusedWarps);
       mbar_init(&tile_free[i], 1);
     }
     epi_done = 0;
@@ -176,7 +178,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
   int tj = 0;
   const int phs[4] = {PH_QKV, PH_O, PH_GU, PH_DOWN};
 
-  if (warp == kG4Warps) {  // ---------------------------------------- producer
+  if (warp == kFusedWarps) {  // ---------------------------------------- producer
     int issued = 0;
     bool ok = true;
     for (int tok = 0; tok < a.n_tokens && ok; tok++) {
@@ -196,7 +198,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
     return;
   }
 
-  if (warp == kG4Warps + 1) {  // ------------------------------------ epilogue
+  if (warp == kFusedWarps + 1) {  // ------------------------------------ epilogue
     for (int tok = 0; tok < a.n_tokens; tok++) {
       for (int li = 0; li < L; li++) {
         const FusedLayer& l = a.layers[li];
@@ -209,7 +211,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
             e.mode = EPI_SILU;
             e.y = a.tmp;
             e.N = a.I;
-            ok = epilogue_q4_run<2>(e, r.t_lo, r.t_hi, red2, tile_full, tile_free, tj, false, a.err);
+            ok = epilogue_q4_run<kFusedWarps, 2>(e, r.t_lo, r.t_hi, red2, tile_full, tile_free, tj, false, a.err);
           } else {
             if (ph == PH_QKV) {  // q/k/v rows + bias
               e.mode = EPI_STORE;
@@ -222,7 +224,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
               e.N = a.H;
             }
             e.split1 = e.split2 = e.N;
-            ok = epilogue_q4_run<1>(e, r.t_lo, r.t_hi, red1, tile_full, tile_free, tj, false, a.err);
+            ok = epilogue_q4_run<kFusedWarps, 1>(e, r.t_lo, r.t_hi, red1, tile_full, tile_free, tj, false, a.err);
           }
           if (!ok) return;
           __threadfence();  // the phase's outputs are visible GPU-wide ...
@@ -234,7 +236,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         const Run r = run_lm(a);
         float bv = -1e30f;
         uint32_t bi = 0xffffffffu;
-        if (!epilogue_q8_run(a.emb_s, a.logits, a.V, r.t_lo, r.t_hi, red1, tile_full, tile_free, tj,
+        if (!epilogue_q8_run<kFusedWarps>(a.emb_s, a.logits, a.V, r.t_lo, r.t_hi, red1, tile_full, tile_free, tj,
                              bv, bi, a.err))
           return;
         if (lane == 0) {
@@ -286,7 +288,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         x.hidden_out = a.hidden;
         if (r.t_lo < r.t_hi) {
           stage_xd<1, true, NT>(x, a.H, xb, xcor, xf, sred, 0);
-          consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+          consume_q4_run<kFusedWarps, 1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
                             xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
@@ -331,7 +333,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         x.x = a.attn;
         if (r.t_lo < r.t_hi) {
           stage_xd<1, false, NT>(x, a.QD, xb, xcor, xf, sred, 0);
-          consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+          consume_q4_run<kFusedWarps, 1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
                             xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
@@ -351,7 +353,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         x.f16 = a.f16;
         if (r.t_lo < r.t_hi) {
           stage_xd<1, true, NT>(x, a.H, xb, xcor, xf, sred, 0);
-          consume_q4_run<2>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+          consume_q4_run<kFusedWarps, 2>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
                             xb, xcor, xf, red2, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
@@ -368,7 +370,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         x.x = a.tmp;
         if (r.t_lo < r.t_hi) {
           stage_xd<3, false, NT>(x, a.I, xb, xcor, xf, sred, 0);
-          consume_q4_run<1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
+          consume_q4_run<kFusedWarps, 1>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr,
                             xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
@@ -393,7 +395,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
       x.f16 = a.f16;
       if (r.t_lo < r.t_hi) {
         stage_xd8<1, true, NT>(x, a.H, r.gpr * kGroup, xb8, xm8, sred, 0);
-        consume_q8_run(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr, xb8,
+        consume_q8_run<kFusedWarps>(ring, full, empty, kFStages, kFStageBytes, r.cap, r.t_lo, r.t_hi, r.gpr, xb8,
                        xm8, red1, tile_full, tile_free, rp, tj, dead, a.err);
       }
     }
@@ -468,7 +470,7 @@ cudaError_t fused_decode(const FusedArgs& a, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kG4Threads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kFusedThreads, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) {
     cudaFuncAttributes fa = {};
@@ -476,13 +478,13 @@ cudaError_t fused_decode(const FusedArgs& a, cudaStream_t st) {
     fprintf(stderr,
             "fused_decode: no CTA fits an SM: %d regs/thread x %d threads, %zu B static + %d B "
             "dynamic shared (max dynamic %d), %zu B local\n",
-            fa.numRegs, kG4Threads, fa.sharedSizeBytes, smem, fa.maxDynamicSharedSizeBytes,
+            fa.numRegs, kFusedThreads, fa.sharedSizeBytes, smem, fa.maxDynamicSharedSizeBytes,
             fa.localSizeBytes);
     return cudaErrorCooperativeLaunchTooLarge;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sm_count());
-  cfg.blockDim = dim3(kG4Threads);
+  cfg.blockDim = dim3(kFusedThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -80,16 +80,22 @@ struct G4Args {
 // mbarriers + 2 tile_full + 2 tile_free (stages <= 8).
 constexpr int kBarBytes = 256;
 
+// 16 consumer warps + producer + epilogue.  (8 consumer warps in ~105 KB, so
+// that the next kernel's CTA fits beside this one under PDL, measured slower:
+// the overlap gained less than the halved consumer group lost.)
+constexpr int kOpWarps = 16;
+constexpr int kOpThreads = kOpWarps * 32 + 64;
+
 __device__ __forceinline__ void init_ring_barriers(uint64_t* full, uint64_t* empty,
                                                    uint64_t* tile_full, uint64_t* tile_free,
                                                    int stages) {
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; i++) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kG4Warps);
+      mbar_init(&empty[i], kOpWarps);
     }
     for (int i = 0; i < 2; i++) {
-      mbar_init(&tile_full[i], kG4Warps);
+      mbar_init(&tile_full[i], kOpWarps);
       mbar_init(&tile_free[i], 1);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -98,11 +104,11 @@ __device__ __forceinline__ void init_ring_barriers(uint64_t* full, uint64_t* emp
 }
 
 template <int R, int MAXU, bool NORM>
-__global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
-  constexpr int NT = kG4Warps * 32;
+__global__ void __launch_bounds__(kOpThreads, 1) gemv_q4_kernel(G4Args p) {
+  constexpr int NT = kOpWarps * 32;
   extern __shared__ __align__(128) unsigned char g4_smem[];
   __shared__ float sred[32];
-  __shared__ TileRed<R> red;
+  __shared__ TileRed<kOpWarps, R> red;
   uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
   uint64_t* empty = full + p.stages;
   uint64_t* tile_full = empty + p.stages;
@@ -119,7 +125,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
   init_ring_barriers(full, empty, tile_full, tile_free, p.stages);
   RingPos rp = {0, 0};
   int tj = 0;
-  if (warp == kG4Warps) {  // producer: the weights need no wait
+  if (warp == kOpWarps) {  // producer: the weights need no wait
     int issued = 0;
     ring_produce(ring, full, empty, p.stages, p.stage_bytes,
                  p.ws + (size_t)t_lo * gpr * q4_block_bytes(R), (t_hi - t_lo) * gpr, p.cap,
@@ -127,9 +133,9 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
     ring_drain(full, p.stages, rp, issued);
     return;
   }
-  if (warp == kG4Warps + 1) {  // epilogue: residuals come from earlier kernels
+  if (warp == kOpWarps + 1) {  // epilogue: residuals come from earlier kernels
     if (p.pdl) pdl_wait();
-    epilogue_q4_run<R>(p.e, t_lo, t_hi, red, tile_full, tile_free, tj, true, p.err);
+    epilogue_q4_run<kOpWarps, R>(p.e, t_lo, t_hi, red, tile_full, tile_free, tj, true, p.err);
     return;
   }
   stage_xd<MAXU, NORM, NT>(p.x, p.K, xb, xcor, xf, sred, p.pdl);
@@ -137,7 +143,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q4_kernel(G4Args p) {
   // attention kernel relies on that to read the position early)
   if (p.pdl) pdl_launch_dependents();
   bool dead = false;
-  consume_q4_run<R>(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xcor,
+  consume_q4_run<kOpWarps, R>(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xcor,
                     xf, red, tile_full, tile_free, rp, tj, dead, p.err);
 }
 
@@ -173,20 +179,24 @@ static void gemv_q4_go(const G4Args& a0, const G4Plan& q, cudaStream_t st, bool 
   const int P = std::min(gemv_q4_ctas(), (a.N + 15) / 16);
   auto k = gemv_q4_kernel<R, MAXU, NORM>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q.smem);
-  launch(k, dim3(P), dim3(kG4Threads), (size_t)q.smem, st, pdl, a);
+  launch(k, dim3(P), dim3(kOpThreads), (size_t)q.smem, st, pdl, a);
 }
 
 template <int R>
 static void gemv_q4_r(const G4Args& a, cudaStream_t st, bool pdl) {
   const G4Plan q = g4_plan(R, a.K);
-  const int u = (a.K / 8 + kG4Warps * 32 - 1) / (kG4Warps * 32);  // units per thread
+  const int u = (a.K / 8 + kOpWarps * 32 - 1) / (kOpWarps * 32);  // units per thread
+  // MAXU >= u: every unit of the vector is staged (K <= 12288)
   if (a.x.mode != X_PLAIN) {  // RMSNorm holds the whole vector in registers
     if (u <= 1) gemv_q4_go<R, 1, true>(a, q, st, pdl);
-    else gemv_q4_go<R, 3, true>(a, q, st, pdl);
+    else if (u <= 3) gemv_q4_go<R, 3, true>(a, q, st, pdl);
+    else gemv_q4_go<R, 6, true>(a, q, st, pdl);
   } else if (u <= 1) {
     gemv_q4_go<R, 1, false>(a, q, st, pdl);
+  } else if (u <= 3) {
+    gemv_q4_go<R, 3, false>(a, q, st, pdl);
   } else {
-    gemv_q4_go<R, 3, false>(a, q, st, pdl);  // K <= 12288
+    gemv_q4_go<R, 6, false>(a, q, st, pdl);
   }
 }
 
@@ -308,11 +318,11 @@ struct Q8Args {
 // decode position (ARGMAX kernels.js:771-784, then decodeBatch's copy of
 // s.amax into the id buffer, runtime.js:1783-1785).
 template <int MAXU, bool NORM>
-__global__ void __launch_bounds__(kG4Threads, 1) gemv_q8_kernel(Q8Args p) {
-  constexpr int NT = kG4Warps * 32;
+__global__ void __launch_bounds__(kOpThreads, 1) gemv_q8_kernel(Q8Args p) {
+  constexpr int NT = kOpWarps * 32;
   extern __shared__ __align__(128) unsigned char g4_smem[];
   __shared__ float sred[32];
-  __shared__ TileRed<1> red;
+  __shared__ TileRed<kOpWarps, 1> red;
   uint64_t* full = reinterpret_cast<uint64_t*>(g4_smem);
   uint64_t* empty = full + p.stages;
   uint64_t* tile_full = empty + p.stages;
@@ -328,17 +338,17 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q8_kernel(Q8Args p) {
   init_ring_barriers(full, empty, tile_full, tile_free, p.stages);
   RingPos rp = {0, 0};
   int tj = 0;
-  if (warp == kG4Warps) {  // producer
+  if (warp == kOpWarps) {  // producer
     int issued = 0;
     ring_produce(ring, full, empty, p.stages, p.stage_bytes, p.ws + (size_t)t_lo * gpr * kQ8Block,
                  (t_hi - t_lo) * gpr, p.cap, kQ8Block, rp, issued, p.err, lane);
     ring_drain(full, p.stages, rp, issued);
     return;
   }
-  if (warp == kG4Warps + 1) {  // epilogue
+  if (warp == kOpWarps + 1) {  // epilogue
     float bv = -1e30f;
     uint32_t bi = 0xffffffffu;
-    if (!epilogue_q8_run(p.s, p.y, p.N, t_lo, t_hi, red, tile_full, tile_free, tj, bv, bi, p.err))
+    if (!epilogue_q8_run<kOpWarps>(p.s, p.y, p.N, t_lo, t_hi, red, tile_full, tile_free, tj, bv, bi, p.err))
       return;
     if (!p.has_tail) return;
     const StepTail& tl = p.tail;
@@ -388,7 +398,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_q8_kernel(Q8Args p) {
   stage_xd8<MAXU, NORM, NT>(p.x, p.K, gpr * kGroup, xb, xmul, sred, p.pdl);
   if (p.pdl) pdl_launch_dependents();
   bool dead = false;
-  consume_q8_run(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xmul, red,
+  consume_q8_run<kOpWarps>(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_lo, t_hi, gpr, xb, xmul, red,
                  tile_full, tile_free, rp, tj, dead, p.err);
 }
 
@@ -407,7 +417,7 @@ static void gemv_q8_go(const Q8Args& a0, cudaStream_t st, bool pdl) {
   const int P = std::min(sm_count(), (a.N + 15) / 16);
   auto k = gemv_q8_kernel<MAXU, NORM>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  launch(k, dim3(P), dim3(kG4Threads), (size_t)smem, st, pdl, a);
+  launch(k, dim3(P), dim3(kOpThreads), (size_t)smem, st, pdl, a);
 }
 
 void gemv_q8(const unsigned char* ws, const float* s, int N, int K, const XSrc& x, float* y,
@@ -422,7 +432,7 @@ void gemv_q8(const unsigned char* ws, const float* s, int N, int K, const XSrc& 
   if (tail) a.tail = *tail;
   a.has_tail = tail ? 1 : 0;
   a.err = wk.err;
-  const int u = (K / 4 + kG4Warps * 32 - 1) / (kG4Warps * 32);  // units of 4 per thread
+  const int u = (K / 4 + kOpWarps * 32 - 1) / (kOpWarps * 32);  // units of 4 per thread
   if (x.mode != X_PLAIN) {
     if (u <= 1) gemv_q8_go<1, true>(a, st, pdl);
     else gemv_q8_go<6, true>(a, st, pdl);

@@ -7,8 +7,8 @@
 // matrix (gpr 128-wide groups per tile, one block per (tile, group)); in the
 // stream layout it is one contiguous byte range.  The producer warp copies a
 // run into the shared-memory ring, `cap` blocks per stage (one
-// cp.async.bulk); consumer warp w (of 16) takes the run's blocks w, w + 16,
-// w + 32, ... and keeps one running sum per row pair; at the end of each tile
+// cp.async.bulk); consumer warp w (of CW) takes the run's blocks w, w + CW,
+// w + 2 CW, ... and keeps one running sum per row pair; at the end of each tile
 // every consumer warp leaves its partial row sums in red[tj & 1] and the
 // epilogue warp sums them and writes the outputs.  Ring positions (stage,
 // phase) and the tile hand-off counter tj carry over from one run to the
@@ -19,8 +19,8 @@
 
 namespace eg {
 
-constexpr int kG4Warps = 16;                    // consumer warps
-constexpr int kG4Threads = kG4Warps * 32 + 64;  // + producer warp + epilogue warp
+// A streaming GEMV CTA: CW consumer warps (a template parameter), then one
+// producer warp and one epilogue warp.
 
 // int4 block: R row sets x (1024 bytes of nibbles in fragment order), then
 // the 16 R f32 group scales as (row i, row i + 8) pairs; int8 block: 16 rows x
@@ -78,16 +78,16 @@ __device__ __forceinline__ void ring_drain(uint64_t* full, int stages, RingPos r
 }
 
 // Tile hand-off area of the consumers and the epilogue warp.
-template <int R>
+template <int CW, int R>
 struct TileRed {
-  float v[2][kG4Warps][R][16];
+  float v[2][CW][R][16];
 };
 
 // Consumer side of one hand-off: sum the lanes t = 0, 1, publish the warp's
 // partial rows in red[tj & 1] once the epilogue warp released that buffer.
 // sc0 / sc1: the final factor of lanes t = 0 / t = 1 (column pairs 0 / 1).
-template <int R>
-__device__ __forceinline__ void tile_handoff(TileRed<R>& red, uint64_t* tile_full,
+template <int CW, int R>
+__device__ __forceinline__ void tile_handoff(TileRed<CW, R>& red, uint64_t* tile_full,
                                              uint64_t* tile_free, int tj, float (&acc)[R][2],
                                              float sc0, float sc1, bool& dead, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -118,15 +118,15 @@ __device__ __forceinline__ void tile_handoff(TileRed<R>& red, uint64_t* tile_ful
   if (lane == 0) mbar_arrive(&tile_full[b]);
 }
 
-// Consumers (warps 0-15) of one int4 run.  xb / xcor / xf: the staged
+// Consumers (warps 0 .. CW-1) of one int4 run.  xb / xcor / xf: the staged
 // activation (stage_xd).  Lanes gq >= 4 feed B columns 4-7, whose results are never
 // used: they load a copy of plane gq & 3 instead of a zero (no predication).  After a failed wait a warp goes on without waiting
 // (its results are void; the host sees the error word).
-template <int R>
+template <int CW, int R>
 __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64_t* empty,
                                int stages, int stage_bytes, int cap, int t_lo, int t_hi, int gpr,
                                const uint2* xb, const int* xcor, const int* xf,
-                               TileRed<R>& red, uint64_t* tile_full, uint64_t* tile_free,
+                               TileRed<CW, R>& red, uint64_t* tile_full, uint64_t* tile_free,
                                RingPos& rp, int& tj, bool& dead, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gq = lane >> 2, t = lane & 3;
@@ -145,7 +145,7 @@ __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64
   int i = warp;  // block index within the run
   for (int j = 0; j < t_hi - t_lo; j++) {
     const int tile_end = (j + 1) * gpr;
-    for (; i < tile_end; i += kG4Warps) {
+    for (; i < tile_end; i += CW) {
       while (i >= chunk_lo + cap) {  // next stage
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[rp.st]);
@@ -187,11 +187,11 @@ __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64
         }
       }
     }
-    tile_handoff<R>(red, tile_full, tile_free, tj, acc, sc0, sc1, dead, err);
+    tile_handoff<CW, R>(red, tile_full, tile_free, tj, acc, sc0, sc1, dead, err);
     tj++;
   }
   // release the current stage and wait/release the later ones this warp had
-  // no blocks in, so every stage sees all kG4Warps arrivals
+  // no blocks in, so every stage sees all CW arrivals
   for (; chunk < nchunks; chunk++) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[rp.st]);
@@ -202,9 +202,10 @@ __device__ void consume_q4_run(const unsigned char* ring, uint64_t* full, uint64
 
 // Consumers of one int8 run (m16n8k32 s8.s8; xb as uint32 [G][p][t][m][2]
 // from stage_xd8; no offset correction).
-static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full, uint64_t* empty,
+template <int CW>
+__device__ void consume_q8_run(const unsigned char* ring, uint64_t* full, uint64_t* empty,
                                int stages, int stage_bytes, int cap, int t_lo, int t_hi, int gpr,
-                               const uint32_t* xb, const float* xmul, TileRed<1>& red,
+                               const uint32_t* xb, const float* xmul, TileRed<CW, 1>& red,
                                uint64_t* tile_full, uint64_t* tile_free, RingPos& rp, int& tj,
                                bool& dead, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -219,7 +220,7 @@ static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full,
   int i = warp;
   for (int j = 0; j < t_hi - t_lo; j++) {
     const int tile_end = (j + 1) * gpr;
-    for (; i < tile_end; i += kG4Warps) {
+    for (; i < tile_end; i += CW) {
       while (i >= chunk_lo + cap) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[rp.st]);
@@ -249,7 +250,7 @@ static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full,
         acc[0][1] = fmaf(mul, (float)(cc[2] + 256 * cc[3]), acc[0][1]);
       }
     }
-    tile_handoff<1>(red, tile_full, tile_free, tj, acc, 1.f, 1.f, dead, err);
+    tile_handoff<CW, 1>(red, tile_full, tile_free, tj, acc, 1.f, 1.f, dead, err);
     tj++;
   }
   for (; chunk < nchunks; chunk++) {
@@ -264,8 +265,8 @@ static __device__ void consume_q8_run(const unsigned char* ring, uint64_t* full,
 // the epilogue (scale already applied; bias / residual / SiLU / LoRA here).
 // pre_ok: the first tile's residual / bias may be read before its hand-off
 // (false when the inputs of this run are only ordered by that hand-off).
-template <int R>
-__device__ bool epilogue_q4_run(const Epi& e, int t_lo, int t_hi, TileRed<R>& red,
+template <int CW, int R>
+__device__ bool epilogue_q4_run(const Epi& e, int t_lo, int t_hi, TileRed<CW, R>& red,
                                 uint64_t* tile_full, uint64_t* tile_free, int& tj, bool pre_ok,
                                 int* err) {
   const int lane = threadIdx.x & 31;
@@ -278,7 +279,7 @@ __device__ bool epilogue_q4_run(const Epi& e, int t_lo, int t_hi, TileRed<R>& re
     if (!pre_ok && tile == t_lo && lane < 16 && !lora) pre = epi_pre(e, tile * 16 + lane);
     float v = 0.f;
     if (lane < 16 * R)
-      for (int ww = 0; ww < kG4Warps; ww++) v += red.v[b][ww][lane >> 4][lane & 15];
+      for (int ww = 0; ww < CW; ww++) v += red.v[b][ww][lane >> 4][lane & 15];
     __syncwarp();
     if (lane == 0) mbar_arrive(&tile_free[b]);
     const float up = __shfl_down_sync(0xffffffffu, v, 16);
@@ -296,8 +297,9 @@ __device__ bool epilogue_q4_run(const Epi& e, int t_lo, int t_hi, TileRed<R>& re
 
 // Epilogue warp of one int8 run: y[n] = row sum * s[n] (sum first, scale
 // last) and the warp's best (value, index) in the reference's order.
-static __device__ bool epilogue_q8_run(const float* s, float* y, int N, int t_lo, int t_hi,
-                                TileRed<1>& red, uint64_t* tile_full, uint64_t* tile_free,
+template <int CW>
+__device__ bool epilogue_q8_run(const float* s, float* y, int N, int t_lo, int t_hi,
+                                TileRed<CW, 1>& red, uint64_t* tile_full, uint64_t* tile_free,
                                 int& tj, float& bv, uint32_t& bi, int* err) {
   const int lane = threadIdx.x & 31;
   float sc = lane < 16 && t_lo < t_hi && t_lo * 16 + lane < N ? __ldg(s + t_lo * 16 + lane) : 0.f;
@@ -306,7 +308,7 @@ static __device__ bool epilogue_q8_run(const float* s, float* y, int N, int t_lo
     if (!mbar_wait(&tile_full[b], (tj >> 1) & 1, err)) return false;
     float v = 0.f;
     if (lane < 16)
-      for (int ww = 0; ww < kG4Warps; ww++) v += red.v[b][ww][0][lane];
+      for (int ww = 0; ww < CW; ww++) v += red.v[b][ww][0][lane];
     __syncwarp();
     if (lane == 0) mbar_arrive(&tile_free[b]);
     const int n = tile * 16 + lane;
