@@ -20,25 +20,23 @@ def _free_port():
     return port
 
 
-def _rank(rank, ws, port, out):
+def _rank(rank, ws, port, outdir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=ws)
     try:
         local_ms = [120.0, 150.0][rank]  # rank 1 is the slow one
         ms = bench.max_over_ranks(local_ms, ws, torch.device("cpu"))
-        out[rank] = (ms, bench.job_throughput(ws, 1000, ms))
+        with open(os.path.join(outdir, f"rank{rank}"), "w") as f:
+            f.write(f"{ms} {bench.job_throughput(ws, 1000, ms)}")
     finally:
         dist.destroy_process_group()
 
 
-def test_max_over_ranks_and_job_throughput_gloo():
+def test_max_over_ranks_and_job_throughput_gloo(tmp_path):
     ws = 2
-    with mp.Manager() as m:
-        out = m.dict()
-        mp.spawn(_rank, args=(ws, _free_port(), out), nprocs=ws, join=True)
-        got = dict(out)
+    mp.spawn(_rank, args=(ws, _free_port(), str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
-        ms, tput = got[r]
+        ms, tput = map(float, (tmp_path / f"rank{r}").read_text().split())
         assert ms == 150.0                   # every rank sees the max
         assert tput == pytest.approx(2 * 1000 / 0.150)
 

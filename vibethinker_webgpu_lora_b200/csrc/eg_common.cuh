@@ -71,9 +71,10 @@ EG_DEV float warp_max(float v) {
   return v;
 }
 
-// The building blocks in eg_device.cuh run on a 256-thread group: the whole
-// CTA of a per-op kernel, or the 8 consumer warps of the fused kernel (whose
-// producer warp never joins).  Named barrier 1 over those 256 threads.
+// The small standalone ops (RMSNorm, LoRA-A) run on a 256-thread CTA and
+// synchronise with named barrier 1 over those 256 threads; the streaming
+// kernels pass their consumer thread count to the *_n helpers of
+// eg_device.cuh instead (their producer and epilogue warps never join).
 constexpr int kCtaThreads = 256;
 EG_DEV void cta_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
