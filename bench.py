@@ -257,7 +257,7 @@ def run_ours(args, ws, rank, local):
                      "bytes_per_launch": GATE_UP_BYTES, "launch_us": round(gu_us, 3),
                      # dram__bytes_read + dram__bytes_write of one gate_up launch, ncu
                      # --set full of `python bench.py --ncu-probe 4` (same kernel and shape)
-                     "traffic": 24012544, "traffic_source": "ncu, bench.py --ncu-probe 4"},
+                     "traffic": 24009984, "traffic_source": "ncu, bench.py --ncu-probe 4"},
         "step_roofline": {"bytes_per_step": int(step_bytes),
                           "achieved_gbs": round(step_bytes * value / ws / 1e9, 1),
                           "frac": round(step_bytes * value / ws / 1e9 / hbm, 4),
