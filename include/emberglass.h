@@ -194,6 +194,18 @@ EG_API eg_status eg_profile_token(eg_rt* rt, uint32_t id, int pos, double* us, i
  * *n_out = 2 * (5 * num_layers + 1). */
 EG_API eg_status eg_profile_fused(eg_rt* rt, int start_pos, uint64_t* out_ns, int n_max,
                                   int* n_out);
+/* Vocab-split LM head (multi-GPU single-stream decode; each rank holds the
+ * full model and owns a slice of the vocabulary): final RMSNorm of `hidden`
+ * (device f32 [hidden_size], e.g. broadcast from the rank that ran the
+ * layers), the int8 LM head over rows [row0, row0 + rows) (row0 % 16 == 0)
+ * and their argmax: *best_val / *best_id (device; global id, ties to the
+ * lower id, as ARGMAX kernels.js:771-784).  logits: device f32 [rows] or
+ * NULL (then the runtime's logits buffer at row0 is used).  Asynchronous on
+ * `stream` like the single ops; it shares the runtime's argmax scratch, so
+ * the caller orders it after the runtime's own stream.  The ranks' (value, id) pairs merge
+ * to the single-GPU argmax (vibethinker_webgpu_lora_b200/parallel.py). */
+EG_API eg_status eg_lm_head_shard(eg_rt* rt, const float* hidden, int row0, int rows,
+                                  float* logits, float* best_val, uint32_t* best_id, void* stream);
 /* memoryFootprintBytes (runtime.js:661-681). */
 EG_API eg_status eg_memory_footprint(eg_rt* rt, int64_t* kv_bytes, int64_t* weight_bytes,
                                      int64_t* scratch_bytes);

@@ -381,7 +381,11 @@ __global__ void __launch_bounds__(kOpThreads, 1) gemv_q8_kernel(Q8Args p) {
         id = oi;
       }
     }
-    if (lane == 0) {
+    if (lane == 0 && !tl.advance) {  // shard mode: the best of this row range
+      *tl.amax = id + tl.id0;
+      *tl.best_v = v;
+      *tl.counter = 0u;
+    } else if (lane == 0) {
       const int ps = *tl.pos;
       if (tl.greedy) {
         *tl.amax = id;

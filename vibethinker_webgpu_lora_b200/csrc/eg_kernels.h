@@ -64,6 +64,11 @@ struct StepTail {
   float* cand_v;       // [grid] per-block best value
   uint32_t* cand_i;    // [grid] per-block best index
   unsigned* counter;   // last-block-done counter (self-resetting)
+  // Shard mode (advance = 0): only the best (value, id + id0) is written to
+  // (*best_v, *amax); the decode state is untouched.
+  int advance;
+  uint32_t id0;
+  float* best_v;
 };
 
 int sm_count();

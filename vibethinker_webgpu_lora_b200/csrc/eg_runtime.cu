@@ -509,6 +509,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
   tail.cand_v = rt->cand_v;
   tail.cand_i = rt->cand_i;
   tail.counter = rt->counter;
+  tail.advance = 1;
   gemv_q8(rt->emb_t, rt->emb_s, c.vocab_size, H, xf, rt->logits, &tail, st, pdl, wk);
   launches++;
   mark(rt, so, 5, cats);
@@ -1114,6 +1115,40 @@ EG_API eg_status eg_read_hidden(eg_rt* rt, float* out) {
   CK(cudaSetDevice(rt->o.device));
   CK(cudaMemcpyAsync(out, rt->hidden, (size_t)rt->c.hidden_size * 4, cudaMemcpyDeviceToHost, rt->st));
   return sync(rt);
+}
+
+EG_API eg_status eg_lm_head_shard(eg_rt* rt, const float* hidden, int row0, int rows,
+                                  float* logits, float* best_val, uint32_t* best_id, void* stream) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  const eg_config& c = rt->c;
+  if (!hidden || !best_val || !best_id) return fail(EG_ERR_ARG, "lm_head_shard: null argument");
+  if (row0 < 0 || rows <= 0 || row0 % 16 || row0 + rows > c.vocab_size)
+    return fail(EG_ERR_ARG, "lm_head_shard: rows [%d, %d) must lie in the vocab, row0 %% 16 == 0",
+                row0, row0 + rows);
+  CK(cudaSetDevice(rt->o.device));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  XSrc xf = {};
+  xf.mode = X_RMS;  // final RMSNorm of the (broadcast) hidden state
+  xf.x = hidden;
+  xf.norm_g = rt->final_norm;
+  xf.eps = c.rms_norm_eps;
+  xf.f16 = rt->o.kv_f16;
+  StepTail tail = {};
+  tail.cand_v = rt->cand_v;
+  tail.cand_i = rt->cand_i;
+  tail.counter = rt->counter;
+  tail.amax = best_id;
+  tail.best_v = best_val;
+  tail.id0 = (uint32_t)row0;
+  tail.advance = 0;
+  const int H = c.hidden_size, gpr = (H + 127) / 128;
+  const GemvWork wk{reinterpret_cast<int*>(rt->fused_sync + 1)};
+  // the shard's rows are a contiguous run of the stream layout (16-row tiles)
+  gemv_q8(rt->emb_t + (size_t)(row0 / 16) * gpr * 2048, rt->emb_s + row0, rows, H, xf,
+          logits ? logits : rt->logits + row0, &tail, st, false, wk);
+  CK(cudaGetLastError());
+  return EG_OK;
 }
 
 EG_API eg_status eg_generate(eg_rt* rt, const uint32_t* prompt, int n_prompt, int max_new,

@@ -396,18 +396,18 @@ struct AttnSmem {
 // RoPE (ROPE_QK) of the 4 dims a lane holds; the partner of dim j < 64 is
 // j + 64, held by lane ^ 16.  rnd: round the result to f16 (q in the f16
 // variant).
-__device__ __forceinline__ float4 rope_lane4(float4 x, const float* cs, const float* sn, int f16,
-                                             bool rnd) {
-  const int lane = threadIdx.x & 31, half = kHeadDim / 2;
+// cj / sj: cos / sin of the lane's 4 pair indices (dim & 63).
+__device__ __forceinline__ float4 rope_lane4(float4 x, const float (&cj)[4], const float (&sj)[4],
+                                             int f16, bool rnd) {
+  const int lane = threadIdx.x & 31;
   float4 o;
   float* e = reinterpret_cast<float*>(&o);
   const float* xi = reinterpret_cast<const float*>(&x);
 #pragma unroll
   for (int c = 0; c < 4; c++) {
     const float other = __shfl_xor_sync(0xffffffffu, xi[c], 16);
-    const int j = (4 * lane + c) & (half - 1);
     float lo = lane < 16 ? xi[c] : other, hi = lane < 16 ? other : xi[c];
-    rope_pair(lo, hi, cs[j], sn[j], f16);
+    rope_pair(lo, hi, cj[c], sj[c], f16);
     if (rnd) round_h2(lo, hi);
     e[c] = lane < 16 ? lo : hi;
   }
@@ -443,19 +443,27 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
       V[i].load(vc + (size_t)t * kvd);
     }
   }
+  // the RoPE rows of pos (constant tables) also come before the wait
+  const float* cs = a.cosT + (size_t)pos * hd;
+  const float* sn = a.sinT + (size_t)pos * hd;
+  float cj[4], sj[4];
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const int j = (4 * lane + c) & (hd / 2 - 1);
+    cj[c] = __ldg(cs + j);
+    sj[c] = __ldg(sn + j);
+  }
   if (pdl) {
     pdl_wait();
     pdl_launch_dependents();
   }
-  const float* cs = a.cosT + (size_t)pos * hd;
-  const float* sn = a.sinT + (size_t)pos * hd;
   // q: ROPE_QK, read through f16 in the f16 variant (ATTN_PARTIAL_F16)
   const float4 q4 = rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + h * hd + 4 * lane)),
-                               cs, sn, f16, f16 != 0);
+                               cj, sj, f16, f16 != 0);
   if (pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v, as the cache stores them
     const float* kn = a.qkv + a.nh * hd + kvh * hd;
     const float* vn = a.qkv + a.nh * hd + kvd + kvh * hd;
-    const float4 kx = rope_lane4(__ldcg(reinterpret_cast<const float4*>(kn + 4 * lane)), cs, sn,
+    const float4 kx = rope_lane4(__ldcg(reinterpret_cast<const float4*>(kn + 4 * lane)), cj, sj,
                                  f16, false);
     const float4 vr = __ldcg(reinterpret_cast<const float4*>(vn + 4 * lane));
     KvRow<KVT> kn4, vn4;
