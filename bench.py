@@ -276,6 +276,88 @@ def run_ours(args, ws, rank, local):
     return result
 
 
+BATCH_METRIC = "batched LoRA decode tok/s summed over 16 sequences (configs[4])"
+
+
+def run_batch16(args, local):
+    """16 sequences, each prefilled to 512 ids, then 64 sampled
+    steps (top-k 40, T 0.7) with a rank-8 adapter (alpha 16) on all 252
+    projections, hot-swapped for a second adapter at step 32.  Timed through
+    the public API (eg_batch_sample: r uniforms in, ids out) with CUDA events
+    on the runtime's stream; the prefill (511 batched steps) is the warm-up."""
+    import numpy as np
+    import torch
+
+    import vibethinker_webgpu_lora_b200 as E
+    from oracle import oracle as O  # prompt ids and r uniforms (SplitMix64)
+
+    cfg = E.QWEN25_3B
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n, n_prompt, steps, k, temp = 16, 512, 64, 40, 0.7
+    rt = E.QwenB200(cfg, {"maxCtx": n_prompt + steps + 8, "useF16": True,
+                          "device": local}).build("synthetic", seed=SEED)
+    a1 = E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16)
+    a2 = E.synthetic_adapter(rt, 0xA2, rank=8, alpha=16)
+    rt.setLora(a1)
+    rt.seqInit(n, n_prompt + steps + 2)
+    slots = list(range(n))
+    for sl in slots:
+        rt.seqSetPrompt(sl, O.token_ids(n_prompt, 0xE6B00100 + sl, cfg["vocabSize"]))
+    r = np.array([[O.uniform(1, 0xE6B00200 ^ sl ^ t)[0] for sl in slots] for t in range(steps)],
+                 np.float32)
+    st = torch.cuda.ExternalStream(rt.stream, device=dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    rt.batchDecode(slots, n_prompt - 1)  # prefill: warm-up, untimed
+    prefill_s = time.perf_counter() - t0
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as ck:
+        t0 = time.perf_counter()
+        e0.record(st)
+        out1 = rt.batchSample(slots, steps // 2, k, temp, r[: steps // 2])
+        rt.setLora(a2)  # hot swap at step 32
+        out2 = rt.batchSample(slots, steps - steps // 2, k, temp, r[steps // 2:])
+        e1.record(st)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    launches = rt.lastDispatchCount * steps
+    weights, kv_per_pos = cfg_bytes(cfg)
+    lora_bytes = 1662976 * cfg["numLayers"]
+    step_bytes = weights + n * kv_per_pos * (n_prompt + steps / 2) + lora_bytes
+    hbm, peak_kind = peaks()
+    value = n * steps / (ms / 1000.0)
+    achieved = step_bytes * steps / (ms / 1000.0) / 1e9
+    assert out1.shape == (steps // 2, n) and out2.shape == (steps - steps // 2, n)
+    a1.destroy()
+    a2.destroy()
+    return {
+        "metric": BATCH_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1,
+        "steps": steps, "warmup": n_prompt - 1, "ms_per_step": round(ms / steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xf32",
+        "data": "synthetic",
+        "config": {"workload": "configs[4]: 16 sequences x (prefill 512 + 64 sampled steps), "
+                               "rank-8 LoRA on 252 projections, hot swap at step 32, top-k 40, T 0.7",
+                   "kv": "f16", "lm_head": "int8 rows",
+                   "l2": "inputs larger than L2 (1.79 GB of weights streamed per step)",
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "hbm", "kernel": "whole batched step (weights once + 16 KV caches "
+                                               "+ LoRA A/B)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                     "bytes_per_launch": int(step_bytes), "traffic": None},
+        "prefill": {"steps": n_prompt - 1, "s": round(prefill_s, 3),
+                    "tok_s": round(n * (n_prompt - 1) / prefill_s, 1)},
+        "e2e": {"value": round(n * steps / wall, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": n * 4,
+                "what": "batchSample x2 (r uniforms H2D, ids D2H) + setLora, wall clock"},
+        "gpu_launches": launches,
+        "clocks": ck.summary(),
+    }
+
+
 def cpu_baseline(cfg, n_prompt, steps):
     """The reference's decode path restated in C (oracle/), all host cores:
     bounded sample of `steps` decode tokens after a short prompt."""
@@ -341,6 +423,20 @@ def ncu_probe(ctx):
     print(json.dumps({"ncu_probe": ctx, "launches_per_step": rt.lastDispatchCount}))
 
 
+def ncu_probe_batch(steps):
+    """Profiling target of the batched path: 16 slots with 8-token prompts,
+    `steps` batched greedy steps (launches_per_step launches each), exit."""
+    import vibethinker_webgpu_lora_b200 as E
+    from oracle import oracle as O
+    cfg = E.QWEN25_3B
+    rt = E.QwenB200(cfg, {"maxCtx": 128}).build("synthetic", seed=SEED)
+    rt.seqInit(16, 64)
+    for sl in range(16):
+        rt.seqSetPrompt(sl, O.token_ids(8, 0xE6B00100 + sl, cfg["vocabSize"]))
+    rt.batchDecode(list(range(16)), steps)
+    print(json.dumps({"ncu_probe_batch": steps, "launches_per_step": rt.lastDispatchCount}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -352,12 +448,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "graph"],
                     help="decode path: persistent fused kernel or per-op CUDA graph")
+    ap.add_argument("--workload", default="decode", choices=["decode", "batch16"],
+                    help="decode: configs[1]/[2] (the headline); batch16: configs[4]")
     ap.add_argument("--ncu-probe", type=int, default=0, metavar="CTX",
                     help="profiling target: build, prefill CTX tokens, decode 2 tokens, exit "
                          "(CTX * launches/step launches precede the 2 profiled steps)")
     args = ap.parse_args()
     if args.ncu_probe:
-        ncu_probe(args.ncu_probe)
+        if args.workload == "batch16":
+            ncu_probe_batch(args.ncu_probe)
+        else:
+            ncu_probe(args.ncu_probe)
         return
     assert args.warmup >= 3, "at least 3 warm-up steps"
     ws, rank, local = dist_setup() if args.impl == "ours" else (
@@ -366,6 +467,10 @@ def main():
         if rank != 0:
             return
         print(json.dumps(run_reference(args, ws, rank)), flush=True)
+        return
+    if args.workload == "batch16":
+        if rank == 0:
+            print(json.dumps(run_batch16(args, local)), flush=True)
         return
     res = run_ours(args, ws, rank, local)
     if rank == 0:

@@ -206,6 +206,33 @@ EG_API eg_status eg_profile_fused(eg_rt* rt, int start_pos, uint64_t* out_ns, in
  * to the single-GPU argmax (vibethinker_webgpu_lora_b200/parallel.py). */
 EG_API eg_status eg_lm_head_shard(eg_rt* rt, const float* hidden, int row0, int rows,
                                   float* logits, float* best_val, uint32_t* best_id, void* stream);
+/* ---------------- multi-sequence batched decode ---------------------------
+ * The reference decodes one sequence per runtime (step(), runtime.js:
+ * 1466-1571); these calls run that step for up to 16 sequences at once, each
+ * lane with its own KV cache, position and token ids, every weight tile read
+ * once per step for all lanes.
+ * eg_seq_init: n_slots sequence slots of slot_ctx positions each (KV caches
+ * allocated here; 0 frees them); every slot starts empty. */
+EG_API eg_status eg_seq_init(eg_rt* rt, int n_slots, int slot_ctx);
+/* The slot's prompt: ids[0..T) become its known tokens, its position 0. */
+EG_API eg_status eg_seq_set_prompt(eg_rt* rt, int slot, const uint32_t* ids, int T);
+/* Position (the token the next step consumes) and count of known ids. */
+EG_API eg_status eg_seq_state(eg_rt* rt, int slot, int* pos, int* len);
+/* `steps` batched steps over the slots seq_ids[0..nseq) (1 <= nseq <= 16,
+ * distinct).  A step consumes each slot's token at its position and moves it
+ * one on; a slot still inside its prompt keeps the prompt's next token
+ * (prefill), a slot past it appends the greedy token (argmax, ties to the
+ * lower id).  out[step * nseq + j] = slot j's token at its new position.
+ * Requires pos + steps <= slot_ctx - 1 for every slot. */
+EG_API eg_status eg_batch_decode(eg_rt* rt, int nseq, const int* seq_ids, int steps,
+                                 uint32_t* out);
+/* As eg_batch_decode, choosing tokens by topKLogits(k) + sampleToken(temp,
+ * r) (runtime.js:1648-1732) with r[step * nseq + j] for slot j. */
+EG_API eg_status eg_batch_sample(eg_rt* rt, int nseq, const int* seq_ids, int steps, int k,
+                                 float temp, const float* r, uint32_t* out);
+/* Logits of lane j (the j-th slot of the last batch call) after its last
+ * step: vocab floats. */
+EG_API eg_status eg_batch_read_logits(eg_rt* rt, int lane, float* out);
 /* memoryFootprintBytes (runtime.js:661-681). */
 EG_API eg_status eg_memory_footprint(eg_rt* rt, int64_t* kv_bytes, int64_t* weight_bytes,
                                      int64_t* scratch_bytes);

@@ -84,6 +84,12 @@ _SIGS = {
     "eg_profile_fused": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
     "eg_memory_footprint": (i32, [vp, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
     "eg_lm_head_shard": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
+    "eg_seq_init": (i32, [vp, i32, i32]),
+    "eg_seq_set_prompt": (i32, [vp, i32, vp, i32]),
+    "eg_seq_state": (i32, [vp, i32, vp, vp]),
+    "eg_batch_decode": (i32, [vp, i32, vp, i32, vp]),
+    "eg_batch_sample": (i32, [vp, i32, vp, i32, i32, f32, vp, vp]),
+    "eg_batch_read_logits": (i32, [vp, i32, vp]),
     "eg_launches_per_step": (i32, [vp]),
     "eg_op_gemv_q4": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, i32, vp]),
     "eg_op_gate_up_silu": (i32, [vp, vp, vp, i32, i32, vp, vp]),

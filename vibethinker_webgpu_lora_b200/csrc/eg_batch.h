@@ -1,0 +1,110 @@
+// eg_batch.h -- launch API of the multi-sequence batched decode kernels.
+//
+// Up to kBatchMax "lanes" (one per sequence) step together: every weight
+// tile is streamed from HBM once per step and multiplied against all lanes'
+// activations.  The reference decodes one sequence at a time (runtime.js:
+// 1466-1571); a batch step computes, for every lane, exactly that step's
+// math on the lane's own KV cache and position.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "eg_kernels.h"
+
+namespace eg {
+
+constexpr int kBatchMax = 16;
+
+// Per-sequence state on the device.  Slot s holds its token ids
+// ids[s * slot_ctx + t], its position pos[s] (the token consumed by the next
+// step) and len[s] (ids known so far: the prompt, then generated tokens).
+struct SeqTable {
+  const int* lane_slot;  // [kBatchMax] slot of each lane
+  int* pos;              // [slots]
+  int* len;              // [slots]
+  uint32_t* ids;         // [slots][slot_ctx]
+  int slot_ctx;
+  uint32_t vocab;        // ids >= vocab (argmax of all-NaN logits) are stored as 0
+};
+
+// Where each lane's GEMV input comes from: XSrc of lane 0 with x (and
+// hidden_out) advanced by `stride` floats per lane; X_EMBED_RMS takes the
+// lane's token id at its position from the sequence table.
+struct BatchSrc {
+  XSrc x;
+  int stride;
+  SeqTable seq;
+};
+
+// Staged activations of all lanes (global memory): the int4 GEMV's digit
+// planes (stage_xd: xb 512 B per 128-group, xcor 2 words per group, xf one
+// exponent) or the int8 GEMV's (stage_xd8: xb 512 B per group, xmul 2 per
+// group); lane v's planes start at v * gpr_max groups.
+struct BatchPlanes {
+  void* xb;
+  int* xcor;     // int4 only
+  float* xmul;   // int8 only
+  int* xf;       // int4 only
+  int gpr_max;
+};
+
+// Epilogue of a batched int4 GEMV: the single-lane epilogue (bias /
+// residual / SiLU) with y advanced by ystride per lane.  LoRA enters as
+// lora_pre[lane * lstride + row] (gate rows then up rows for SiLU), each
+// value the single-lane epilogue's lora_dot, computed ahead by lora_b_batch;
+// e.mods is not used by the batched GEMV.
+struct BatchEpi {
+  Epi e;
+  int ystride, dstride;
+  const float* lora_pre;
+  int lstride;
+};
+
+// pdl: launched as programmatic dependents of the previous kernel (each
+// kernel waits with griddepcontrol.wait before reading earlier outputs).
+void batch_stage_q4(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, cudaStream_t st,
+                    bool pdl);
+void batch_stage_q8(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, cudaStream_t st,
+                    bool pdl);
+void gemv_q4_batch(const unsigned char* ws, int N, int K, int lanes, const BatchPlanes& xp,
+                   const BatchEpi& be, int* err, cudaStream_t st, bool pdl);
+void gemv_q8_batch(const unsigned char* ws, const float* s, int N, int K, int lanes,
+                   const BatchPlanes& xp, float* y, int ystride, int* err, cudaStream_t st,
+                   bool pdl);
+
+// Attention of every lane: AttnArgs of lane 0 (kc/vc = the layer's slot-0
+// cache) with qkv/out/partials advanced per lane, the cache by the lane's
+// slot, the position from the sequence table.
+struct AttnBatch {
+  SeqTable seq;
+  int qkv_stride, out_stride, part_stride;  // floats per lane (part: pm/pz; po = 128x)
+  size_t kv_slot_bytes;                     // one slot's cache of one layer
+};
+void attn_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st, bool pdl);
+
+// LoRA B side of every lane: out[v * be.lstride + row] = the single-lane
+// epilogue's lora_dot for that row (e.mods, e.lora_d + v * dstride); rows =
+// N, or 2N for SiLU (gate rows, then up rows).
+void lora_b_batch(const BatchEpi& be, int rows, int lanes, float* out, cudaStream_t st, bool pdl);
+
+// LORA_A of every lane: d + v * dstride.
+void lora_a_batch(const BatchSrc& s, int K, const LoraMod* mods, int nmods, int max_rank, float* d,
+                  int dstride, int lanes, cudaStream_t st, bool pdl);
+
+// Per-lane argmax / top-k / sample over logits [lanes][n].
+void argmax_batch(const float* logits, int n, int lanes, uint32_t* out, float* cand_v,
+                  uint32_t* cand_i, cudaStream_t st);
+void topk_batch(const float* logits, int n, int k, int lanes, uint32_t* ids, float* vals,
+                float* cand_v, uint32_t* cand_i, cudaStream_t st);
+int topk_batch_cand(int n, int k);  // candidate slots per lane
+// r[step * kBatchMax + lane], step = *step_ctr (advanced by batch_advance).
+void sample_batch(const uint32_t* ids, const float* vals, int k, float temp, const float* r,
+                  const int* step_ctr, int lanes, uint32_t* out, cudaStream_t st);
+
+// End of a batch step: lane v's choice[v] becomes the slot's next token
+// when the slot is past its known ids; out[*step_ctr * lanes + v] = the
+// token at the new position; positions advance; *step_ctr += 1.
+void batch_advance(SeqTable seq, const uint32_t* choice, int lanes, uint32_t* out, int* step_ctr,
+                   cudaStream_t st);
+
+}  // namespace eg

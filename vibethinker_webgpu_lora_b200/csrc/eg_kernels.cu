@@ -25,6 +25,7 @@
 
 #include "eg_common.cuh"
 #include "eg_device.cuh"
+#include "eg_batch.h"
 #include "eg_kernels.h"
 #include "eg_stream.cuh"
 
@@ -553,9 +554,13 @@ void copy_u32(const uint32_t* src, uint32_t* dst, cudaStream_t st) {
 int topk_cand_blocks(int n) { return std::max(1, std::min(kCandMax, (n + 1023) / 1024)); }
 
 // Stage 1: per-block argmax candidates.  Stage 2 (one block) merges them.
+// Lanes of a batch: stage 1 blockIdx.y, stage 2 blockIdx.x (logits [lane][n]).
 __global__ void argmax_stage1(const float* logits, int n, float* cv, uint32_t* ci) {
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
+  logits += (size_t)blockIdx.y * n;
+  cv += (size_t)blockIdx.y * gridDim.x;
+  ci += (size_t)blockIdx.y * gridDim.x;
   const int per = (n + gridDim.x - 1) / gridDim.x;
   const int b0 = blockIdx.x * per, b1 = min(n, b0 + per);
   float v = -1e30f;
@@ -574,6 +579,9 @@ __global__ void argmax_stage1(const float* logits, int n, float* cv, uint32_t* c
 __global__ void argmax_stage2(const float* cv, const uint32_t* ci, int nc, uint32_t* out) {
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
+  cv += (size_t)blockIdx.x * nc;
+  ci += (size_t)blockIdx.x * nc;
+  out += blockIdx.x;
   float v = -1e30f;
   uint32_t id = 0xffffffffu;
   for (int i = threadIdx.x; i < nc; i += blockDim.x)
@@ -599,6 +607,9 @@ constexpr int kTopkPer = 8;  // elements per thread in stage 1 (256 threads)
 __global__ void topk_stage1(const float* logits, int n, int k, float* cv, uint32_t* ci) {
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
+  logits += (size_t)blockIdx.y * n;
+  cv += (size_t)blockIdx.y * gridDim.x * k;
+  ci += (size_t)blockIdx.y * gridDim.x * k;
   const int per = (n + gridDim.x - 1) / gridDim.x;
   const int b0 = blockIdx.x * per, b1 = min(n, b0 + per);
   float val[kTopkPer];
@@ -635,6 +646,10 @@ __global__ void topk_stage2(const float* cv_in, const uint32_t* ci_in, int nc, i
   extern __shared__ float cand[];
   float* cvs = cand;
   uint32_t* cis = reinterpret_cast<uint32_t*>(cand + nc);
+  cv_in += (size_t)blockIdx.x * nc;
+  ci_in += (size_t)blockIdx.x * nc;
+  ids += (size_t)blockIdx.x * k;
+  vals += (size_t)blockIdx.x * k;
   for (int i = threadIdx.x; i < nc; i += blockDim.x) {
     cvs[i] = cv_in[i];
     cis[i] = ci_in[i];
@@ -660,23 +675,45 @@ __global__ void topk_stage2(const float* cv_in, const uint32_t* ci_in, int nc, i
     __syncthreads();
   }
 }
-void topk(const float* logits, int n, int k, uint32_t* ids, float* vals, float* cand_v,
-          uint32_t* cand_i, cudaStream_t st) {
+static int topk_blocks(int n) {
   int nb = topk_cand_blocks(n);
   while ((long long)nb * 256 * kTopkPer < n) nb++;
-  nb = std::min(nb, kCandMax);
-  topk_stage1<<<nb, 256, 0, st>>>(logits, n, k, cand_v, cand_i);
+  return std::min(nb, kCandMax);
+}
+void topk(const float* logits, int n, int k, uint32_t* ids, float* vals, float* cand_v,
+          uint32_t* cand_i, cudaStream_t st) {
+  topk_batch(logits, n, k, 1, ids, vals, cand_v, cand_i, st);
+}
+int topk_batch_cand(int n, int k) { return topk_blocks(n) * k; }
+void topk_batch(const float* logits, int n, int k, int lanes, uint32_t* ids, float* vals,
+                float* cand_v, uint32_t* cand_i, cudaStream_t st) {
+  const int nb = topk_blocks(n);
+  topk_stage1<<<dim3(nb, lanes), 256, 0, st>>>(logits, n, k, cand_v, cand_i);
   const int nc = nb * k;
   cudaFuncSetAttribute(topk_stage2, cudaFuncAttributeMaxDynamicSharedMemorySize, nc * 8);
-  topk_stage2<<<1, 256, (size_t)nc * 8, st>>>(cand_v, cand_i, nc, k, ids, vals);
+  topk_stage2<<<lanes, 256, (size_t)nc * 8, st>>>(cand_v, cand_i, nc, k, ids, vals);
+}
+void argmax_batch(const float* logits, int n, int lanes, uint32_t* out, float* cand_v,
+                  uint32_t* cand_i, cudaStream_t st) {
+  const int nb = topk_cand_blocks(n);
+  argmax_stage1<<<dim3(nb, lanes), 256, 0, st>>>(logits, n, cand_v, cand_i);
+  argmax_stage2<<<lanes, 256, 0, st>>>(cand_v, cand_i, nb, out);
 }
 
 // SAMPLE_TOPK restated literally: 64 slots, exp without max subtraction,
 // pairwise tree sum, Hillis-Steele inclusive prefix, first j with r <= P_j.
+// Batch lanes: blockIdx.x, with r = r_all[*step_ctr * kBatchMax + lane].
 __global__ void sample_topk_kernel(const uint32_t* ids, const float* vals, int k, float temp, float r,
-                                   uint32_t* out, uint32_t* out2) {
+                                   uint32_t* out, uint32_t* out2, const float* r_all,
+                                   const int* step_ctr) {
   __shared__ float s[64], red[64];
   const int tid = threadIdx.x;
+  if (r_all) {
+    r = r_all[(size_t)*step_ctr * kBatchMax + blockIdx.x];
+    ids += (size_t)blockIdx.x * k;
+    vals += (size_t)blockIdx.x * k;
+    out += blockIdx.x;
+  }
   const float t = temp <= 0.f ? 1.f : temp;
   float v = -1e30f;
   if (tid < k) {
@@ -717,7 +754,11 @@ __global__ void sample_topk_kernel(const uint32_t* ids, const float* vals, int k
 }
 void sample_topk(const uint32_t* ids, const float* vals, int k, float temp, float r, uint32_t* out,
                  uint32_t* out2, cudaStream_t st) {
-  sample_topk_kernel<<<1, 64, 0, st>>>(ids, vals, k, temp, r, out, out2);
+  sample_topk_kernel<<<1, 64, 0, st>>>(ids, vals, k, temp, r, out, out2, nullptr, nullptr);
+}
+void sample_batch(const uint32_t* ids, const float* vals, int k, float temp, const float* r,
+                  const int* step_ctr, int lanes, uint32_t* out, cudaStream_t st) {
+  sample_topk_kernel<<<lanes, 64, 0, st>>>(ids, vals, k, temp, 0.f, out, nullptr, r, step_ctr);
 }
 
 }  // namespace eg

@@ -20,6 +20,7 @@
 #include <string>
 #include <vector>
 
+#include "eg_batch.h"
 #include "eg_fused.h"
 #include "eg_host.h"
 #include "eg_kernels.h"
@@ -101,6 +102,21 @@ struct eg_rt {
   int launches_per_step = 0;
   std::atomic<bool> busy{false};
   int64_t weight_bytes = 0, kv_bytes = 0, scratch_bytes = 0;
+  // multi-sequence slots and the batched step's scratch (eg_seq_init)
+  int seq_slots = 0, seq_ctx = 0, b_max_splits = 0, b_gpr = 0, b_out_cap = 0, b_r_cap = 0;
+  std::vector<void*> seq_kc, seq_vc;        // per layer: [slots][seq_ctx][kv dim]
+  std::vector<int> h_seq_pos, h_seq_len;    // host mirror of the slots' pos / len
+  int *seq_pos = nullptr, *seq_len = nullptr, *lane_slot = nullptr, *b_step = nullptr;
+  uint32_t* seq_ids = nullptr;
+  float *b_hidden = nullptr, *b_qkv = nullptr, *b_attn = nullptr, *b_tmp = nullptr,
+        *b_logits = nullptr, *b_pm = nullptr, *b_pz = nullptr, *b_po = nullptr,
+        *b_lora_d = nullptr, *b_lora_y = nullptr, *b_xmul = nullptr, *b_cand_v = nullptr, *b_topk_vals = nullptr,
+        *b_r = nullptr;
+  void* b_xb = nullptr;
+  int *b_xcor = nullptr, *b_xf = nullptr;
+  unsigned* b_attn_counters = nullptr;
+  uint32_t *b_choice = nullptr, *b_cand_i = nullptr, *b_topk_ids = nullptr, *b_out = nullptr;
+  int seq_lanes_last = 0;
 };
 
 namespace eg {
@@ -1149,6 +1165,389 @@ EG_API eg_status eg_lm_head_shard(eg_rt* rt, const float* hidden, int row0, int 
           logits ? logits : rt->logits + row0, &tail, st, false, wk);
   CK(cudaGetLastError());
   return EG_OK;
+}
+
+// ------------------------------------------------------------------ multi-sequence
+// Sequence slots and the batched step.  The reference decodes one sequence
+// per runtime (runtime.js:1466-1571); here up to kBatchMax slots step
+// together, each with its own KV cache, position and token ids, and each
+// lane's math is the single-sequence step's.
+static eg_status seq_free(eg_rt* rt) {
+  if (!rt->seq_slots) return EG_OK;
+  CK(cudaStreamSynchronize(rt->st));
+  const eg_config& c = rt->c;
+  const size_t kvb = (size_t)rt->seq_slots * rt->seq_ctx * c.num_kv_heads * c.head_dim *
+                     (rt->o.kv_f16 ? 2 : 4);
+  for (size_t i = 0; i < rt->seq_kc.size(); i++) {
+    dfree(rt, &rt->seq_kc[i], (int64_t)kvb, &rt->kv_bytes);
+    dfree(rt, &rt->seq_vc[i], (int64_t)kvb, &rt->kv_bytes);
+  }
+  rt->seq_kc.clear();
+  rt->seq_vc.clear();
+  void** sp[] = {(void**)&rt->seq_pos, (void**)&rt->seq_len, (void**)&rt->lane_slot,
+                 (void**)&rt->b_step, (void**)&rt->seq_ids, (void**)&rt->b_hidden,
+                 (void**)&rt->b_qkv, (void**)&rt->b_attn, (void**)&rt->b_tmp,
+                 (void**)&rt->b_logits, (void**)&rt->b_pm, (void**)&rt->b_pz, (void**)&rt->b_po,
+                 (void**)&rt->b_lora_d, (void**)&rt->b_lora_y, (void**)&rt->b_xmul, (void**)&rt->b_cand_v,
+                 (void**)&rt->b_topk_vals, (void**)&rt->b_r, (void**)&rt->b_xb,
+                 (void**)&rt->b_xcor, (void**)&rt->b_xf, (void**)&rt->b_attn_counters,
+                 (void**)&rt->b_choice, (void**)&rt->b_cand_i, (void**)&rt->b_topk_ids,
+                 (void**)&rt->b_out};
+  for (void** q : sp) dfree(rt, q, 0, nullptr);
+  rt->seq_slots = rt->seq_ctx = rt->b_out_cap = rt->b_r_cap = 0;
+  rt->h_seq_pos.clear();
+  rt->h_seq_len.clear();
+  return EG_OK;
+}
+
+EG_API eg_status eg_seq_init(eg_rt* rt, int n_slots, int slot_ctx) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (n_slots < 0 || n_slots > 4096 || (n_slots && (slot_ctx < 2 || slot_ctx > rt->o.max_ctx)))
+    return fail(EG_ERR_ARG, "seq_init: %d slots of %d positions (2 <= ctx <= maxCtx %d)", n_slots,
+                slot_ctx, rt->o.max_ctx);
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = seq_free(rt))) return s;
+  if (!n_slots) return EG_OK;
+  const eg_config& c = rt->c;
+  const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
+  const int I = c.intermediate_size, NQKV = QD + 2 * KVD, V = c.vocab_size, B = kBatchMax;
+  const size_t kvb = (size_t)n_slots * slot_ctx * KVD * (rt->o.kv_f16 ? 2 : 4);
+  rt->seq_kc.assign(c.num_layers, nullptr);
+  rt->seq_vc.assign(c.num_layers, nullptr);
+  for (int i = 0; i < c.num_layers; i++) {
+    DALLOC(rt->seq_kc[i], kvb, &rt->kv_bytes);
+    DALLOC(rt->seq_vc[i], kvb, &rt->kv_bytes);
+    CK(cudaMemsetAsync(rt->seq_kc[i], 0, kvb, rt->st));
+    CK(cudaMemsetAsync(rt->seq_vc[i], 0, kvb, rt->st));
+  }
+  int64_t* sb = &rt->scratch_bytes;
+  rt->seq_slots = n_slots;
+  rt->seq_ctx = slot_ctx;
+  rt->b_max_splits = attn_max_splits(slot_ctx);
+  rt->b_gpr = (std::max(std::max(H, QD), I) + 127) / 128;
+  DALLOC(rt->seq_pos, (size_t)n_slots * 4, sb);
+  DALLOC(rt->seq_len, (size_t)n_slots * 4, sb);
+  DALLOC(rt->seq_ids, (size_t)n_slots * slot_ctx * 4, sb);
+  DALLOC(rt->lane_slot, B * 4, sb);
+  DALLOC(rt->b_step, 4, sb);
+  DALLOC(rt->b_hidden, (size_t)B * H * 4, sb);
+  DALLOC(rt->b_qkv, (size_t)B * NQKV * 4, sb);
+  DALLOC(rt->b_attn, (size_t)B * QD * 4, sb);
+  DALLOC(rt->b_tmp, (size_t)B * I * 4, sb);
+  DALLOC(rt->b_logits, (size_t)B * V * 4, sb);
+  const size_t part = (size_t)c.num_heads * rt->b_max_splits;
+  DALLOC(rt->b_pm, B * part * 4, sb);
+  DALLOC(rt->b_pz, B * part * 4, sb);
+  DALLOC(rt->b_po, B * part * hd * 4, sb);
+  DALLOC(rt->b_lora_d, (size_t)B * 3 * kMaxRank * 4, sb);
+  DALLOC(rt->b_lora_y, (size_t)B * std::max(std::max(NQKV, 2 * I), H) * 4, sb);
+  DALLOC(rt->b_xb, (size_t)B * rt->b_gpr * 512, sb);
+  DALLOC(rt->b_xcor, (size_t)B * rt->b_gpr * 2 * 4, sb);
+  DALLOC(rt->b_xmul, (size_t)B * rt->b_gpr * 2 * 4, sb);
+  DALLOC(rt->b_xf, B * 4, sb);
+  DALLOC(rt->b_attn_counters, B * 64 * 4, sb);
+  DALLOC(rt->b_choice, B * 4, sb);
+  const size_t ncand = (size_t)B * std::max(topk_batch_cand(V, 64), kCandMax);
+  DALLOC(rt->b_cand_v, ncand * 4, sb);
+  DALLOC(rt->b_cand_i, ncand * 4, sb);
+  DALLOC(rt->b_topk_ids, B * 64 * 4, sb);
+  DALLOC(rt->b_topk_vals, B * 64 * 4, sb);
+  CK(cudaMemsetAsync(rt->seq_pos, 0, (size_t)n_slots * 4, rt->st));
+  CK(cudaMemsetAsync(rt->seq_len, 0, (size_t)n_slots * 4, rt->st));
+  CK(cudaMemsetAsync(rt->seq_ids, 0, (size_t)n_slots * slot_ctx * 4, rt->st));
+  CK(cudaMemsetAsync(rt->lane_slot, 0, B * 4, rt->st));
+  CK(cudaMemsetAsync(rt->b_xb, 0, (size_t)B * rt->b_gpr * 512, rt->st));
+  CK(cudaMemsetAsync(rt->b_xcor, 0, (size_t)B * rt->b_gpr * 8, rt->st));
+  CK(cudaMemsetAsync(rt->b_xmul, 0, (size_t)B * rt->b_gpr * 8, rt->st));
+  CK(cudaMemsetAsync(rt->b_xf, 0, B * 4, rt->st));
+  CK(cudaMemsetAsync(rt->b_attn_counters, 0, B * 64 * 4, rt->st));
+  rt->h_seq_pos.assign(n_slots, 0);
+  rt->h_seq_len.assign(n_slots, 0);
+  CK(cudaStreamSynchronize(rt->st));
+  return EG_OK;
+}
+
+EG_API eg_status eg_seq_set_prompt(eg_rt* rt, int slot, const uint32_t* ids, int T) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (slot < 0 || slot >= rt->seq_slots)
+    return fail(EG_ERR_ARG, "slot %d out of range (%d slots)", slot, rt->seq_slots);
+  if (T < 1 || !ids) return fail(EG_ERR_ARG, "prompt of %d ids", T);
+  if (T > rt->seq_ctx) return fail(EG_ERR_ARG, "prompt %d > slot ctx %d", T, rt->seq_ctx);
+  for (int i = 0; i < T; i++)
+    if (ids[i] >= (uint32_t)rt->c.vocab_size)
+      return fail(EG_ERR_ARG, "token id %u >= vocab %d", ids[i], rt->c.vocab_size);
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
+  CK(cudaSetDevice(rt->o.device));
+  CK(cudaMemcpy(rt->seq_ids + (size_t)slot * rt->seq_ctx, ids, (size_t)T * 4,
+                cudaMemcpyHostToDevice));
+  const int pl[2] = {0, T};
+  CK(cudaMemcpy(rt->seq_pos + slot, &pl[0], 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(rt->seq_len + slot, &pl[1], 4, cudaMemcpyHostToDevice));
+  rt->h_seq_pos[slot] = 0;
+  rt->h_seq_len[slot] = T;
+  return EG_OK;
+}
+
+EG_API eg_status eg_seq_state(eg_rt* rt, int slot, int* pos, int* len) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (slot < 0 || slot >= rt->seq_slots) return fail(EG_ERR_ARG, "slot %d out of range", slot);
+  if (pos) *pos = rt->h_seq_pos[slot];
+  if (len) *len = rt->h_seq_len[slot];
+  return EG_OK;
+}
+
+// One batched step over lanes 0..n-1 (lane v = slot lane_slot[v]).
+static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) {
+  const eg_config& c = rt->c;
+  const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
+  const int I = c.intermediate_size, NQKV = QD + 2 * KVD, V = c.vocab_size;
+  cudaStream_t st = rt->st;
+  int* err = reinterpret_cast<int*>(rt->fused_sync + 1);
+  const bool lora = rt->active != nullptr;
+  const int rank = lora ? rt->active->max_rank : 0;
+  const LoraMod* lt = rt->lora_table;
+  const int dstride = 3 * kMaxRank;
+  const SeqTable sq{rt->lane_slot, rt->seq_pos, rt->seq_len, rt->seq_ids, rt->seq_ctx,
+                   (uint32_t)c.vocab_size};
+  BatchPlanes xp;
+  xp.xb = rt->b_xb;
+  xp.xcor = rt->b_xcor;
+  xp.xmul = rt->b_xmul;
+  xp.xf = rt->b_xf;
+  xp.gpr_max = rt->b_gpr;
+  int launches = 0;
+  const bool pdl = rt->o.use_pdl != 0;
+  auto src = [&](int mode, const float* x, const float* g, int stride) {
+    BatchSrc b = {};
+    b.x.mode = mode;
+    b.x.x = x;
+    b.x.norm_g = g;
+    b.x.eps = c.rms_norm_eps;
+    b.x.f16 = rt->o.kv_f16;
+    b.x.emb_w = rt->emb_w;
+    b.x.emb_s = rt->emb_s;
+    b.stride = stride;
+    b.seq = sq;
+    return b;
+  };
+  auto epi = [&](int mode, float* y, int N, int ystride, const float* bias, int m, int s1, int s2) {
+    BatchEpi e = {};
+    e.e.mode = mode;
+    e.e.y = y;
+    e.e.N = N;
+    e.e.bias = bias;
+    e.e.mods = lora ? lt + m : nullptr;
+    e.e.lora_d = rt->b_lora_d;
+    e.e.split1 = s1;
+    e.e.split2 = s2;
+    e.ystride = ystride;
+    e.dstride = dstride;
+    if (lora) {  // the LoRA B terms of every lane and row, ahead of the GEMV
+      const int rows = mode == EPI_SILU ? 2 * N : N;
+      e.lora_pre = rt->b_lora_y;
+      e.lstride = rows;
+      lora_b_batch(e, rows, n, rt->b_lora_y, st, pdl);
+      launches++;
+    }
+    return e;
+  };
+  for (int i = 0; i < c.num_layers; i++) {
+    const Layer& l = rt->L[i];
+    BatchSrc xa = src(i == 0 ? X_EMBED_RMS : X_RMS, rt->b_hidden, l.in_norm, H);
+    if (i == 0) xa.x.hidden_out = rt->b_hidden;
+    if (lora) {
+      BatchSrc xl = xa;
+      xl.x.hidden_out = nullptr;
+      lora_a_batch(xl, H, lt + i * 7 + 0, 3, rank, rt->b_lora_d, dstride, n, st, pdl);
+      launches++;
+    }
+    batch_stage_q4(xa, H, n, xp, st, pdl);
+    gemv_q4_batch(l.qkv_t, NQKV, H, n, xp,
+                  epi(EPI_STORE, rt->b_qkv, NQKV, NQKV, c.attention_bias ? l.qkv_b : nullptr,
+                      i * 7 + 0, QD, QD + KVD),
+                  err, st, pdl);
+    launches += 2;
+    AttnArgs a = {};
+    a.qkv = rt->b_qkv;
+    a.kc = rt->seq_kc[i];
+    a.vc = rt->seq_vc[i];
+    a.cosT = rt->cosT;
+    a.sinT = rt->sinT;
+    a.nh = c.num_heads;
+    a.nkv = c.num_kv_heads;
+    a.max_splits = rt->b_max_splits;
+    a.ctx_bound = rt->seq_ctx;
+    a.kv_f16 = rt->o.kv_f16;
+    a.chunk = rt->o.attn_chunk;
+    a.pm = rt->b_pm;
+    a.pz = rt->b_pz;
+    a.po = rt->b_po;
+    a.out = rt->b_attn;
+    a.counters = rt->b_attn_counters;
+    AttnBatch ab;
+    ab.seq = sq;
+    ab.qkv_stride = NQKV;
+    ab.out_stride = QD;
+    ab.part_stride = c.num_heads * rt->b_max_splits;
+    ab.kv_slot_bytes = (size_t)rt->seq_ctx * KVD * (rt->o.kv_f16 ? 2 : 4);
+    attn_batch(a, ab, n, st, pdl);
+    launches++;
+    BatchSrc xo = src(X_PLAIN, rt->b_attn, nullptr, QD);
+    if (lora) {
+      lora_a_batch(xo, QD, lt + i * 7 + 3, 1, rank, rt->b_lora_d, dstride, n, st, pdl);
+      launches++;
+    }
+    batch_stage_q4(xo, QD, n, xp, st, pdl);
+    gemv_q4_batch(l.o_t, H, QD, n, xp, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 3, H, H),
+                  err, st, pdl);
+    launches += 2;
+    BatchSrc xb = src(X_RMS, rt->b_hidden, l.post_norm, H);
+    if (lora) {
+      lora_a_batch(xb, H, lt + i * 7 + 4, 2, rank, rt->b_lora_d, dstride, n, st, pdl);
+      launches++;
+    }
+    batch_stage_q4(xb, H, n, xp, st, pdl);
+    gemv_q4_batch(l.gu_t, I, H, n, xp, epi(EPI_SILU, rt->b_tmp, I, I, nullptr, i * 7 + 4, I, I),
+                  err, st, pdl);
+    launches += 2;
+    BatchSrc xd = src(X_PLAIN, rt->b_tmp, nullptr, I);
+    if (lora) {
+      lora_a_batch(xd, I, lt + i * 7 + 6, 1, rank, rt->b_lora_d, dstride, n, st, pdl);
+      launches++;
+    }
+    batch_stage_q4(xd, I, n, xp, st, pdl);
+    gemv_q4_batch(l.d_t, H, I, n, xp, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 6, H, H),
+                  err, st, pdl);
+    launches += 2;
+  }
+  BatchSrc xf = src(X_RMS, rt->b_hidden, rt->final_norm, H);
+  batch_stage_q8(xf, H, n, xp, st, pdl);
+  gemv_q8_batch(rt->emb_t, rt->emb_s, V, H, n, xp, rt->b_logits, V, err, st, pdl);
+  launches += 2;
+  if (!sample) {
+    argmax_batch(rt->b_logits, V, n, rt->b_choice, rt->b_cand_v, rt->b_cand_i, st);
+    launches += 2;
+  } else {
+    topk_batch(rt->b_logits, V, k, n, rt->b_topk_ids, rt->b_topk_vals, rt->b_cand_v,
+               rt->b_cand_i, st);
+    sample_batch(rt->b_topk_ids, rt->b_topk_vals, k, temp, rt->b_r, rt->b_step, n, rt->b_choice,
+                 st);
+    launches += 3;
+  }
+  batch_advance(sq, rt->b_choice, n, rt->b_out, rt->b_step, st);
+  return launches + 1;
+}
+
+static eg_status batch_run(eg_rt* rt, int nseq, const int* seq_ids, int steps, bool sample, int k,
+                           float temp, const float* r, uint32_t* out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (!rt->seq_slots) return fail(EG_ERR_STATE, "no sequence slots: call eg_seq_init first");
+  if (nseq < 1 || nseq > kBatchMax || !seq_ids)
+    return fail(EG_ERR_ARG, "batch of %d sequences (1..%d)", nseq, kBatchMax);
+  if (steps < 0 || (steps && !out)) return fail(EG_ERR_ARG, "steps %d", steps);
+  if (sample && steps && !r) return fail(EG_ERR_ARG, "sampling needs r[steps][nseq]");
+  std::vector<int> seen(rt->seq_slots, 0);
+  for (int j = 0; j < nseq; j++) {
+    const int sl = seq_ids[j];
+    if (sl < 0 || sl >= rt->seq_slots) return fail(EG_ERR_ARG, "slot %d out of range", sl);
+    if (seen[sl]++) return fail(EG_ERR_ARG, "slot %d listed twice", sl);
+    if (rt->h_seq_len[sl] < 1) return fail(EG_ERR_STATE, "slot %d has no prompt", sl);
+    if (rt->h_seq_pos[sl] + steps > rt->seq_ctx - 1)
+      return fail(EG_ERR_ARG, "slot %d: position %d + %d steps exceeds its ctx %d", sl,
+                  rt->h_seq_pos[sl], steps, rt->seq_ctx);
+  }
+  if (!steps) return EG_OK;
+  if (sample) {
+    k = std::max(1, std::min(k, std::min(rt->o.max_sampling_top_k, rt->c.vocab_size)));
+    for (int i = 0; i < steps * nseq; i++)
+      if (!(r[i] >= 0.f)) return fail(EG_ERR_ARG, "r[%d] is negative or NaN", i);
+  }
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
+  CK(cudaSetDevice(rt->o.device));
+  int64_t* sb = &rt->scratch_bytes;
+  if (rt->b_out_cap < steps * nseq) {
+    dfree(rt, (void**)&rt->b_out, 0, nullptr);
+    DALLOC(rt->b_out, (size_t)steps * nseq * 4, sb);
+    rt->b_out_cap = steps * nseq;
+  }
+  if (sample) {
+    if (rt->b_r_cap < steps) {
+      dfree(rt, (void**)&rt->b_r, 0, nullptr);
+      DALLOC(rt->b_r, (size_t)steps * kBatchMax * 4, sb);
+      rt->b_r_cap = steps;
+    }
+    std::vector<float> rp((size_t)steps * kBatchMax, 0.f);
+    for (int t = 0; t < steps; t++)
+      for (int j = 0; j < nseq; j++) rp[(size_t)t * kBatchMax + j] = std::min(r[t * nseq + j], 1.f);
+    CK(cudaMemcpyAsync(rt->b_r, rp.data(), rp.size() * 4, cudaMemcpyHostToDevice, rt->st));
+    CK(cudaStreamSynchronize(rt->st));
+  }
+  int lanes[kBatchMax] = {0};
+  for (int j = 0; j < nseq; j++) lanes[j] = seq_ids[j];
+  CK(cudaMemcpyAsync(rt->lane_slot, lanes, sizeof lanes, cudaMemcpyHostToDevice, rt->st));
+  CK(cudaMemsetAsync(rt->b_step, 0, 4, rt->st));
+  if (rt->o.use_graphs) {
+    cudaGraph_t g;
+    cudaGraphExec_t ge = nullptr;
+    CK(cudaStreamBeginCapture(rt->st, cudaStreamCaptureModeThreadLocal));
+    rt->launches_per_step = enqueue_batch_step(rt, nseq, sample, k, temp);
+    cudaError_t e1 = cudaGetLastError();
+    cudaError_t e2 = cudaStreamEndCapture(rt->st, &g);
+    if (e1 != cudaSuccess) return fail(EG_ERR_CUDA, "batch step capture: %s", cudaGetErrorString(e1));
+    if (e2 != cudaSuccess) return fail(EG_ERR_CUDA, "end capture: %s", cudaGetErrorString(e2));
+    cudaError_t e3 = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e3 != cudaSuccess) return fail(EG_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e3));
+    cudaError_t e4 = cudaSuccess;
+    for (int t = 0; t < steps && e4 == cudaSuccess; t++) e4 = cudaGraphLaunch(ge, rt->st);
+    cudaError_t e5 = cudaStreamSynchronize(rt->st);
+    cudaGraphExecDestroy(ge);
+    if (e4 != cudaSuccess) return fail(EG_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e4));
+    if (e5 != cudaSuccess) return fail(EG_ERR_CUDA, "batch steps: %s", cudaGetErrorString(e5));
+  } else {
+    for (int t = 0; t < steps; t++) rt->launches_per_step = enqueue_batch_step(rt, nseq, sample, k, temp);
+    CK(cudaGetLastError());
+  }
+  rt->seq_lanes_last = nseq;
+  std::vector<uint32_t> h((size_t)steps * nseq);
+  CK(cudaMemcpyAsync(h.data(), rt->b_out, h.size() * 4, cudaMemcpyDeviceToHost, rt->st));
+  if ((s = sync(rt))) return s;
+  memcpy(out, h.data(), h.size() * 4);
+  for (int j = 0; j < nseq; j++) {
+    const int sl = seq_ids[j];
+    rt->h_seq_pos[sl] += steps;
+    rt->h_seq_len[sl] = std::max(rt->h_seq_len[sl], rt->h_seq_pos[sl] + 1);
+  }
+  return EG_OK;
+}
+
+EG_API eg_status eg_batch_decode(eg_rt* rt, int nseq, const int* seq_ids, int steps,
+                                 uint32_t* out) {
+  return batch_run(rt, nseq, seq_ids, steps, false, 1, 1.f, nullptr, out);
+}
+
+EG_API eg_status eg_batch_sample(eg_rt* rt, int nseq, const int* seq_ids, int steps, int k,
+                                 float temp, const float* r, uint32_t* out) {
+  return batch_run(rt, nseq, seq_ids, steps, true, k, temp, r, out);
+}
+
+EG_API eg_status eg_batch_read_logits(eg_rt* rt, int lane, float* out) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (lane < 0 || lane >= rt->seq_lanes_last || !out)
+    return fail(EG_ERR_ARG, "lane %d of the last batch (%d lanes)", lane, rt->seq_lanes_last);
+  CK(cudaSetDevice(rt->o.device));
+  CK(cudaMemcpyAsync(out, rt->b_logits + (size_t)lane * rt->c.vocab_size,
+                     (size_t)rt->c.vocab_size * 4, cudaMemcpyDeviceToHost, rt->st));
+  return sync(rt);
 }
 
 EG_API eg_status eg_generate(eg_rt* rt, const uint32_t* prompt, int n_prompt, int max_new,

@@ -193,6 +193,46 @@ class QwenB200:
                 cb(t)
         return ids
 
+    # ------------------------------------------------------------ multi-sequence
+    def seqInit(self, nSlots: int, slotCtx: int):
+        """Allocate nSlots independent sequences of slotCtx positions each."""
+        L.check(L.lib().eg_seq_init(self._h, int(nSlots), int(slotCtx)))
+
+    def seqSetPrompt(self, slot: int, ids):
+        """Load a slot's prompt; its position returns to 0."""
+        p = np.ascontiguousarray(ids, np.uint32)
+        L.check(L.lib().eg_seq_set_prompt(self._h, int(slot), p.ctypes.data, int(p.size)))
+
+    def seqState(self, slot: int) -> tuple[int, int]:
+        """(position, known ids) of a slot."""
+        pos, n = C.c_int(0), C.c_int(0)
+        L.check(L.lib().eg_seq_state(self._h, int(slot), C.byref(pos), C.byref(n)))
+        return pos.value, n.value
+
+    def batchDecode(self, slots, steps: int) -> np.ndarray:
+        """`steps` batched greedy steps over `slots` (<= 16): [steps][len(slots)]
+        tokens at each slot's new position (prompt tokens while prefilling)."""
+        sl = np.ascontiguousarray(slots, np.int32)
+        out = np.zeros((max(int(steps), 1), sl.size), np.uint32)
+        L.check(L.lib().eg_batch_decode(self._h, int(sl.size), sl.ctypes.data, int(steps),
+                                        out.ctypes.data))
+        return out[:int(steps)]
+
+    def batchSample(self, slots, steps: int, k: int, temp: float, r) -> np.ndarray:
+        """As batchDecode with top-k sampling; r[steps][len(slots)] uniforms."""
+        sl = np.ascontiguousarray(slots, np.int32)
+        rr = np.ascontiguousarray(r, np.float32).reshape(int(steps), sl.size)
+        out = np.zeros((max(int(steps), 1), sl.size), np.uint32)
+        L.check(L.lib().eg_batch_sample(self._h, int(sl.size), sl.ctypes.data, int(steps), int(k),
+                                        float(temp), rr.ctypes.data, out.ctypes.data))
+        return out[:int(steps)]
+
+    def batchLogits(self, lane: int) -> np.ndarray:
+        """Logits of lane `lane` of the last batch call after its last step."""
+        out = np.empty(self.cfg["vocabSize"], np.float32)
+        L.check(L.lib().eg_batch_read_logits(self._h, int(lane), out.ctypes.data))
+        return out
+
     # ------------------------------------------------------------ LoRA
     def setLora(self, adapter):
         """setLora(adapter) (runtime.js:717-721)."""
