@@ -110,6 +110,18 @@ EG_API eg_status eg_upload_tensor(eg_rt* rt, const char* name, const float* data
 EG_API eg_status eg_upload_quantized(eg_rt* rt, const char* name, int kind,
                                      const uint32_t* packed, const float* scale,
                                      const int64_t* shape, int ndim);
+/* Streaming safetensors model load (safetensors_loader.js:83-126 +
+ * ModelUploader.visit, model_uploader.js:39-63): `path` is a .safetensors
+ * file or a directory with model.safetensors.index.json (sharded) or
+ * model.safetensors.  Each tensor is decoded from BF16 / F16 / F32 to f32
+ * and passed to eg_upload_tensor (schema check, quantisation, upload;
+ * unknown names skipped, a repeated name is an error).  *n_visited = the
+ * tensors read.  Call eg_finalize afterwards. */
+EG_API eg_status eg_load_safetensors(eg_rt* rt, const char* path, int* n_visited);
+/* Host-only: decode one tensor of a safetensors file / model directory to
+ * f32 (out == NULL: shape query only).  shape receives up to 8 dims. */
+EG_API eg_status eg_safetensors_tensor(const char* path, const char* name, float* out,
+                                       int64_t capacity, int64_t* shape, int* ndim);
 /* build('mock') equivalent with seeded weights instead of zeros: every
  * matrix and q/k/v bias ~ N(0, std) from the SplitMix64/Box-Muller stream
  * of tensor id t (seed_t = stream(seed)[t]; embed t=0, layer i projection p

@@ -84,6 +84,8 @@ _SIGS = {
     "eg_profile_fused": (i32, [vp, i32, vp, i32, C.POINTER(i32)]),
     "eg_memory_footprint": (i32, [vp, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
     "eg_lm_head_shard": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
+    "eg_load_safetensors": (i32, [vp, C.c_char_p, C.POINTER(i32)]),
+    "eg_safetensors_tensor": (i32, [C.c_char_p, C.c_char_p, vp, i64, vp, C.POINTER(i32)]),
     "eg_seq_init": (i32, [vp, i32, i32]),
     "eg_seq_set_prompt": (i32, [vp, i32, vp, i32]),
     "eg_seq_state": (i32, [vp, i32, vp, vp]),

@@ -28,7 +28,7 @@ CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-fopenmp", "-ffp-contract=off", "-mar
             "-I", INCLUDE, "-I", CSRC, "-I", "/usr/local/cuda/include"]
 
 CU = ["eg_kernels.cu", "eg_batch.cu", "eg_fused.cu", "eg_runtime.cu", "eg_noalloc.cu"]
-CPP = ["eg_host.cpp"]
+CPP = ["eg_host.cpp", "eg_safetensors.cpp"]
 HEADERS = ["eg_common.cuh", "eg_device.cuh", "eg_stream.cuh", "eg_kernels.h", "eg_batch.h", "eg_fused.h",
            "eg_host.h"]
 

@@ -800,6 +800,7 @@ EG_API eg_status eg_upload_tensor(eg_rt* rt, const char* name, const float* data
   CK(cudaSetDevice(rt->o.device));
   Desc d = describe(rt->c, name);
   if (d.role == R_UNKNOWN) return EG_OK;  // schema.validateTensor: unknown names are skipped
+  if (rt->seen.count(name)) return fail(EG_ERR_ARG, "duplicate tensor %s", name);  // visit()
   eg_status s = check_shape(name, d, shape, ndim);
   if (s) return s;
   if ((s = alloc_weights(rt))) return s;
@@ -814,6 +815,7 @@ EG_API eg_status eg_upload_quantized(eg_rt* rt, const char* name, int kind, cons
   Desc d = describe(rt->c, name);
   if (d.role != R_PROJ && d.role != R_EMBED)
     return fail(EG_ERR_ARG, "%s is not a quantised tensor", name);
+  if (rt->seen.count(name)) return fail(EG_ERR_ARG, "duplicate tensor %s", name);
   eg_status s = check_shape(name, d, shape, ndim);
   if (s) return s;
   if ((s = alloc_weights(rt))) return s;

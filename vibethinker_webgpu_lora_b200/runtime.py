@@ -8,6 +8,7 @@ happens in the CUDA library.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -78,10 +79,17 @@ class QwenB200:
     # ------------------------------------------------------------ weights
     def build(self, source="synthetic", seed: int = 0xE6B00000, std: float = 0.02):
         """build(source) (runtime.js:326): 'synthetic' = seeded N(0, std)
-        weights, or a mapping / iterable of (HF name, f32 array)."""
+        weights; a path = a safetensors model (file, or a directory with
+        model.safetensors.index.json / model.safetensors), streamed tensor by
+        tensor by the library's loader; or a mapping / iterable of (HF name,
+        f32 array)."""
         lib = L.lib()
         if source == "synthetic":
             L.check(lib.eg_build_synthetic(self._h, seed, std))
+        elif isinstance(source, (str, os.PathLike)):
+            n = C.c_int(0)
+            L.check(lib.eg_load_safetensors(self._h, os.fsencode(source), C.byref(n)))
+            self.tensorsVisited = n.value
         else:
             items = source.items() if hasattr(source, "items") else source
             for name, arr in items:
@@ -286,3 +294,16 @@ class QwenB200:
     @property
     def lastDispatchCount(self) -> int:
         return L.lib().eg_launches_per_step(self._h)
+
+
+def readSafetensorsTensor(path, name: str) -> np.ndarray:
+    """One tensor of a safetensors file / model directory decoded to f32 by
+    the library's loader (BF16 / F16 / F32, safetensors_loader.js:20-54)."""
+    shape = (C.c_int64 * 8)()
+    nd = C.c_int(0)
+    p, n = os.fsencode(path), name.encode()
+    L.check(L.lib().eg_safetensors_tensor(p, n, None, 0, shape, C.byref(nd)))
+    dims = tuple(shape[i] for i in range(nd.value))
+    out = np.empty(dims, np.float32)
+    L.check(L.lib().eg_safetensors_tensor(p, n, out.ctypes.data, out.size, shape, C.byref(nd)))
+    return out
