@@ -226,6 +226,18 @@ EG_API eg_status eg_lm_head_shard(eg_rt* rt, const float* hidden, int row0, int 
  * eg_seq_init: n_slots sequence slots of slot_ctx positions each (KV caches
  * allocated here; 0 frees them); every slot starts empty. */
 EG_API eg_status eg_seq_init(eg_rt* rt, int n_slots, int slot_ctx);
+/* Paged variant (PagedAttentionManager, runtime.js:2573-2616, with
+ * WRITE_KV_PAGE / ATTN_PARTIAL_PAGED, kernels.js:1657-1911): the slots share
+ * a pool of n_pages pages of 16 positions per layer; a slot takes pages as
+ * its positions are reached (ensureBlocks) and returns them when it gets a
+ * new prompt or is released (freeSeq).  A batch call that would need more
+ * pages than are free fails with EG_ERR_OOM before launching anything (the
+ * reference instead invents block ids past its pool). */
+EG_API eg_status eg_seq_init_paged(eg_rt* rt, int n_slots, int slot_ctx, int n_pages);
+/* freeSeq: the slot becomes empty and its pages return to the pool. */
+EG_API eg_status eg_seq_release(eg_rt* rt, int slot);
+/* Free and total pages of the pool (0 / 0 for dense slots). */
+EG_API eg_status eg_seq_pages(eg_rt* rt, int* free_pages, int* total_pages);
 /* The slot's prompt: ids[0..T) become its known tokens, its position 0. */
 EG_API eg_status eg_seq_set_prompt(eg_rt* rt, int slot, const uint32_t* ids, int T);
 /* Position (the token the next step consumes) and count of known ids. */

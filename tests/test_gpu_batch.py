@@ -195,3 +195,45 @@ def test_batch_argument_errors(cuda):
     rt.seqInit(0, 0)  # frees the slots
     with pytest.raises(E.EmberglassError):
         rt.batchDecode([0], 1)
+
+
+def test_paged_slots_equal_dense_slots(cuda):
+    """Slots on a shared pool of 16-position pages (PagedAttentionManager,
+    runtime.js:2573-2616) give the dense slots' tokens and logits bit for
+    bit, with pages handed out interleaved across slots, returned on a new
+    prompt, and exhaustion reported before anything runs."""
+    cfg = small_config(layers=2, vocab=3000)
+    dense = E.QwenB200(cfg, dict(maxCtx=64)).build("synthetic", seed=SEED)
+    paged = E.QwenB200(cfg, dict(maxCtx=64)).build("synthetic", seed=SEED)
+    ps = prompts(4, cfg["vocabSize"], [3, 18, 1, 7])
+    dense.seqInit(4, 48)
+    paged.seqInitPaged(4, 48, 9)
+    assert paged.seqPages() == (9, 9) and dense.seqPages() == (0, 0)
+    for sl, p in enumerate(ps):
+        dense.seqSetPrompt(sl, p)
+        paged.seqSetPrompt(sl, p)
+    plan = [([0, 1, 2, 3], 5), ([2, 0], 12), ([1, 3, 2], 6), ([3], 9), ([0, 1, 2, 3], 3)]
+    for slots, steps in plan:
+        a = dense.batchDecode(slots, steps)
+        b = paged.batchDecode(slots, steps)
+        assert np.array_equal(a, b)
+        for j in range(len(slots)):
+            assert np.array_equal(dense.batchLogits(j), paged.batchLogits(j))
+    # positions 20, 14, 26, 23: ceil(pos / 16) = 2 + 1 + 2 + 2 pages held
+    held = sum((dense.seqState(s)[0] + 15) // 16 for s in range(4))
+    assert held == 7 and paged.seqPages() == (2, 9)
+    paged.seqSetPrompt(2, ps[2])  # a new sequence in slot 2 returns its pages
+    dense.seqSetPrompt(2, ps[2])
+    assert paged.seqPages()[0] == 4
+    a = dense.batchDecode([2, 1], 8)
+    b = paged.batchDecode([2, 1], 8)
+    assert np.array_equal(a, b)
+    assert paged.seqPages()[0] == 2
+    with pytest.raises(E.EmberglassError, match="out of KV pages"):
+        paged.batchDecode([0, 3, 2], 24)  # needs 3 more pages, 2 are free
+    assert paged.seqPages()[0] == 2  # nothing was taken
+    assert paged.seqState(0)[0] == 20
+    paged.seqRelease(0)
+    assert paged.seqState(0) == (0, 0)
+    with pytest.raises(E.EmberglassError):
+        paged.batchDecode([0], 1)  # released: no prompt

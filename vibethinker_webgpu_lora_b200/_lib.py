@@ -87,6 +87,9 @@ _SIGS = {
     "eg_load_safetensors": (i32, [vp, C.c_char_p, C.POINTER(i32)]),
     "eg_safetensors_tensor": (i32, [C.c_char_p, C.c_char_p, vp, i64, vp, C.POINTER(i32)]),
     "eg_seq_init": (i32, [vp, i32, i32]),
+    "eg_seq_init_paged": (i32, [vp, i32, i32, i32]),
+    "eg_seq_release": (i32, [vp, i32]),
+    "eg_seq_pages": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
     "eg_seq_set_prompt": (i32, [vp, i32, vp, i32]),
     "eg_seq_state": (i32, [vp, i32, vp, vp]),
     "eg_batch_decode": (i32, [vp, i32, vp, i32, vp]),

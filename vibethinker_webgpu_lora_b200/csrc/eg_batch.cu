@@ -509,8 +509,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_batch_kernel(AttnArgs a0
   const int slot = b.seq.lane_slot[v];
   AttnArgs a = a0;
   a.qkv = a0.qkv + (size_t)v * b.qkv_stride;
-  a.kc = reinterpret_cast<char*>(a0.kc) + (size_t)slot * b.kv_slot_bytes;
-  a.vc = reinterpret_cast<char*>(a0.vc) + (size_t)slot * b.kv_slot_bytes;
+  if (b.page_table) {
+    a.pages = b.page_table + (size_t)slot * b.max_pages;
+  } else {
+    a.kc = reinterpret_cast<char*>(a0.kc) + (size_t)slot * b.kv_slot_bytes;
+    a.vc = reinterpret_cast<char*>(a0.vc) + (size_t)slot * b.kv_slot_bytes;
+  }
   a.pos = b.seq.pos + slot;
   a.pm = a0.pm + (size_t)v * b.part_stride;
   a.pz = a0.pz + (size_t)v * b.part_stride;

@@ -78,7 +78,11 @@ void gemv_q8_batch(const unsigned char* ws, const float* s, int N, int K, int la
 struct AttnBatch {
   SeqTable seq;
   int qkv_stride, out_stride, part_stride;  // floats per lane (part: pm/pz; po = 128x)
-  size_t kv_slot_bytes;                     // one slot's cache of one layer
+  size_t kv_slot_bytes;                     // one slot's cache of one layer (dense)
+  // Paged slots: kc / vc are the layer's page pool and slot s's page table
+  // is page_table[s * max_pages ..]; null = dense slots.
+  const uint32_t* page_table;
+  int max_pages;
 };
 void attn_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st, bool pdl);
 

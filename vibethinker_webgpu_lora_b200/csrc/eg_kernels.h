@@ -116,6 +116,10 @@ struct AttnArgs {
   float *pm, *pz, *po;  // partials [nh][max_splits], po [nh][max_splits][128]
   float* out;        // attention output [nh*128]
   unsigned* counters;  // [nkv] split-arrival counters, zero between launches
+  // Paged cache (WRITE_KV_PAGE / ATTN_PARTIAL_PAGED, kernels.js:1657-1911):
+  // row t lives at physical row pages[t / 16] * 16 + t % 16 of kc / vc;
+  // null = contiguous rows.
+  const uint32_t* pages;
 };
 int attn_max_splits(int max_ctx);
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);

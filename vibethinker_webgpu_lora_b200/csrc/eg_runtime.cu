@@ -117,6 +117,12 @@ struct eg_rt {
   unsigned* b_attn_counters = nullptr;
   uint32_t *b_choice = nullptr, *b_cand_i = nullptr, *b_topk_ids = nullptr, *b_out = nullptr;
   int seq_lanes_last = 0;
+  // paged slots (eg_seq_init_paged): pool of seq_pool_pages 16-row pages per
+  // layer, slot s's table at seq_page_table[s * seq_max_pages]
+  int seq_pool_pages = 0, seq_max_pages = 0;
+  uint32_t* seq_page_table = nullptr;
+  std::vector<std::vector<uint32_t>> h_pages;  // pages held by each slot
+  std::vector<uint32_t> free_pages;
 };
 
 namespace eg {
@@ -1178,8 +1184,9 @@ static eg_status seq_free(eg_rt* rt) {
   if (!rt->seq_slots) return EG_OK;
   CK(cudaStreamSynchronize(rt->st));
   const eg_config& c = rt->c;
-  const size_t kvb = (size_t)rt->seq_slots * rt->seq_ctx * c.num_kv_heads * c.head_dim *
-                     (rt->o.kv_f16 ? 2 : 4);
+  const size_t rows = rt->seq_pool_pages ? (size_t)rt->seq_pool_pages * 16
+                                          : (size_t)rt->seq_slots * rt->seq_ctx;
+  const size_t kvb = rows * c.num_kv_heads * c.head_dim * (rt->o.kv_f16 ? 2 : 4);
   for (size_t i = 0; i < rt->seq_kc.size(); i++) {
     dfree(rt, &rt->seq_kc[i], (int64_t)kvb, &rt->kv_bytes);
     dfree(rt, &rt->seq_vc[i], (int64_t)kvb, &rt->kv_bytes);
@@ -1194,20 +1201,27 @@ static eg_status seq_free(eg_rt* rt) {
                  (void**)&rt->b_topk_vals, (void**)&rt->b_r, (void**)&rt->b_xb,
                  (void**)&rt->b_xcor, (void**)&rt->b_xf, (void**)&rt->b_attn_counters,
                  (void**)&rt->b_choice, (void**)&rt->b_cand_i, (void**)&rt->b_topk_ids,
-                 (void**)&rt->b_out};
+                 (void**)&rt->b_out, (void**)&rt->seq_page_table};
   for (void** q : sp) dfree(rt, q, 0, nullptr);
+  rt->seq_pool_pages = rt->seq_max_pages = 0;
+  rt->h_pages.clear();
+  rt->free_pages.clear();
   rt->seq_slots = rt->seq_ctx = rt->b_out_cap = rt->b_r_cap = 0;
   rt->h_seq_pos.clear();
   rt->h_seq_len.clear();
   return EG_OK;
 }
 
-EG_API eg_status eg_seq_init(eg_rt* rt, int n_slots, int slot_ctx) {
+// n_pages == 0: every slot owns slot_ctx contiguous rows; n_pages > 0: the
+// slots share a pool of n_pages 16-row pages per layer (PagedAttentionManager,
+// runtime.js:2573-2616), allocated as positions are reached.
+static eg_status seq_setup(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
   eg_status s = need_ready(rt);
   if (s) return s;
   if (n_slots < 0 || n_slots > 4096 || (n_slots && (slot_ctx < 2 || slot_ctx > rt->o.max_ctx)))
     return fail(EG_ERR_ARG, "seq_init: %d slots of %d positions (2 <= ctx <= maxCtx %d)", n_slots,
                 slot_ctx, rt->o.max_ctx);
+  if (n_pages < 0 || n_pages > (1 << 24)) return fail(EG_ERR_ARG, "seq_init: %d pages", n_pages);
   Busy b(rt);
   if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
   CK(cudaSetDevice(rt->o.device));
@@ -1216,7 +1230,8 @@ EG_API eg_status eg_seq_init(eg_rt* rt, int n_slots, int slot_ctx) {
   const eg_config& c = rt->c;
   const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
   const int I = c.intermediate_size, NQKV = QD + 2 * KVD, V = c.vocab_size, B = kBatchMax;
-  const size_t kvb = (size_t)n_slots * slot_ctx * KVD * (rt->o.kv_f16 ? 2 : 4);
+  const size_t rows = n_pages ? (size_t)n_pages * 16 : (size_t)n_slots * slot_ctx;
+  const size_t kvb = rows * KVD * (rt->o.kv_f16 ? 2 : 4);
   rt->seq_kc.assign(c.num_layers, nullptr);
   rt->seq_vc.assign(c.num_layers, nullptr);
   for (int i = 0; i < c.num_layers; i++) {
@@ -1268,7 +1283,75 @@ EG_API eg_status eg_seq_init(eg_rt* rt, int n_slots, int slot_ctx) {
   CK(cudaMemsetAsync(rt->b_attn_counters, 0, B * 64 * 4, rt->st));
   rt->h_seq_pos.assign(n_slots, 0);
   rt->h_seq_len.assign(n_slots, 0);
+  if (n_pages) {
+    rt->seq_pool_pages = n_pages;
+    rt->seq_max_pages = (slot_ctx + 15) / 16;
+    DALLOC(rt->seq_page_table, (size_t)n_slots * rt->seq_max_pages * 4, sb);
+    CK(cudaMemsetAsync(rt->seq_page_table, 0, (size_t)n_slots * rt->seq_max_pages * 4, rt->st));
+    rt->h_pages.assign(n_slots, {});
+    rt->free_pages.resize(n_pages);
+    for (int i = 0; i < n_pages; i++) rt->free_pages[i] = (uint32_t)(n_pages - 1 - i);  // pop() = 0, 1, ...
+  }
   CK(cudaStreamSynchronize(rt->st));
+  return EG_OK;
+}
+
+EG_API eg_status eg_seq_init(eg_rt* rt, int n_slots, int slot_ctx) {
+  return seq_setup(rt, n_slots, slot_ctx, 0);
+}
+
+EG_API eg_status eg_seq_init_paged(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
+  if (n_slots && n_pages < 1) return fail(EG_ERR_ARG, "seq_init_paged: need at least one page");
+  return seq_setup(rt, n_slots, slot_ctx, n_pages);
+}
+
+// freeSeq: the slot's pages go back to the pool (most recent first).
+static void release_pages(eg_rt* rt, int slot) {
+  if (!rt->seq_pool_pages) return;
+  auto& hp = rt->h_pages[slot];
+  rt->free_pages.insert(rt->free_pages.end(), hp.begin(), hp.end());
+  hp.clear();
+}
+
+// ensureBlocks: pages for positions [0, n_pos) of the slot; the table row is
+// uploaded when it grew.  Fails (nothing launched) when the pool is empty.
+static eg_status ensure_pages(eg_rt* rt, int slot, int n_pos) {
+  if (!rt->seq_pool_pages) return EG_OK;
+  auto& hp = rt->h_pages[slot];
+  const size_t need = (size_t)(n_pos + 15) / 16, had = hp.size();
+  while (hp.size() < need) {
+    if (rt->free_pages.empty())
+      return fail(EG_ERR_OOM, "out of KV pages (%d in the pool): slot %d needs %zu", rt->seq_pool_pages,
+                  slot, need);
+    hp.push_back(rt->free_pages.back());
+    rt->free_pages.pop_back();
+  }
+  if (hp.size() != had)
+    CK(cudaMemcpy(rt->seq_page_table + (size_t)slot * rt->seq_max_pages + had, hp.data() + had,
+                  (hp.size() - had) * 4, cudaMemcpyHostToDevice));
+  return EG_OK;
+}
+
+EG_API eg_status eg_seq_release(eg_rt* rt, int slot) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (slot < 0 || slot >= rt->seq_slots) return fail(EG_ERR_ARG, "slot %d out of range", slot);
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
+  CK(cudaSetDevice(rt->o.device));
+  CK(cudaStreamSynchronize(rt->st));
+  release_pages(rt, slot);
+  const int z = 0;
+  CK(cudaMemcpy(rt->seq_len + slot, &z, 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(rt->seq_pos + slot, &z, 4, cudaMemcpyHostToDevice));
+  rt->h_seq_pos[slot] = rt->h_seq_len[slot] = 0;
+  return EG_OK;
+}
+
+EG_API eg_status eg_seq_pages(eg_rt* rt, int* free_pages, int* total_pages) {
+  if (!rt) return fail(EG_ERR_ARG, "null runtime");
+  if (free_pages) *free_pages = (int)rt->free_pages.size();
+  if (total_pages) *total_pages = rt->seq_pool_pages;
   return EG_OK;
 }
 
@@ -1285,6 +1368,8 @@ EG_API eg_status eg_seq_set_prompt(eg_rt* rt, int slot, const uint32_t* ids, int
   Busy b(rt);
   if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
   CK(cudaSetDevice(rt->o.device));
+  CK(cudaStreamSynchronize(rt->st));
+  release_pages(rt, slot);  // a new sequence in this slot
   CK(cudaMemcpy(rt->seq_ids + (size_t)slot * rt->seq_ctx, ids, (size_t)T * 4,
                 cudaMemcpyHostToDevice));
   const int pl[2] = {0, T};
@@ -1398,6 +1483,8 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) 
     ab.out_stride = QD;
     ab.part_stride = c.num_heads * rt->b_max_splits;
     ab.kv_slot_bytes = (size_t)rt->seq_ctx * KVD * (rt->o.kv_f16 ? 2 : 4);
+    ab.page_table = rt->seq_page_table;
+    ab.max_pages = rt->seq_max_pages;
     attn_batch(a, ab, n, st, pdl);
     launches++;
     BatchSrc xo = src(X_PLAIN, rt->b_attn, nullptr, QD);
@@ -1491,6 +1578,22 @@ static eg_status batch_run(eg_rt* rt, int nseq, const int* seq_ids, int steps, b
       for (int j = 0; j < nseq; j++) rp[(size_t)t * kBatchMax + j] = std::min(r[t * nseq + j], 1.f);
     CK(cudaMemcpyAsync(rt->b_r, rp.data(), rp.size() * 4, cudaMemcpyHostToDevice, rt->st));
     CK(cudaStreamSynchronize(rt->st));
+  }
+  if (rt->seq_pool_pages) {  // pages for every position these steps write, all or none
+    std::vector<size_t> had(nseq);
+    for (int j = 0; j < nseq; j++) had[j] = rt->h_pages[seq_ids[j]].size();
+    for (int j = 0; j < nseq; j++) {
+      if ((s = ensure_pages(rt, seq_ids[j], rt->h_seq_pos[seq_ids[j]] + steps))) {
+        for (int q = 0; q < nseq; q++) {
+          auto& hp = rt->h_pages[seq_ids[q]];
+          while (hp.size() > had[q]) {
+            rt->free_pages.push_back(hp.back());
+            hp.pop_back();
+          }
+        }
+        return s;
+      }
+    }
   }
   int lanes[kBatchMax] = {0};
   for (int j = 0; j < nseq; j++) lanes[j] = seq_ids[j];

@@ -414,6 +414,13 @@ __device__ __forceinline__ float4 rope_lane4(float4 x, const float (&cj)[4], con
   return o;
 }
 
+// Cache row of position t: contiguous, or through a page table of 16-row
+// pages (physical row = pages[t / 16] * 16 + t % 16, WRITE_KV_PAGE).
+constexpr int kKvPage = 16;
+__device__ __forceinline__ size_t kv_row(const uint32_t* pages, int t) {
+  return pages ? (size_t)__ldg(pages + t / kKvPage) * kKvPage + (t % kKvPage) : (size_t)t;
+}
+
 template <typename KVT>
 __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, AttnSmem& sm) {
   float* wm = sm.wm;
@@ -439,8 +446,9 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
   for (int i = 0; i < kAttnKpw; i++) {
     const int t = t0 + warp + kAttnWarps * i;
     if (t < t1 && t != pos) {
-      K[i].load(kc + (size_t)t * kvd);
-      V[i].load(vc + (size_t)t * kvd);
+      const size_t r = kv_row(a.pages, t);
+      K[i].load(kc + r * kvd);
+      V[i].load(vc + r * kvd);
     }
   }
   // the RoPE rows of pos (constant tables) also come before the wait
@@ -479,8 +487,8 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
         }
     }
     if (h % G == 0 && warp == 0) {  // one query head per KV group appends
-      KVT* kw = reinterpret_cast<KVT*>(a.kc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
-      KVT* vw = reinterpret_cast<KVT*>(a.vc) + (size_t)pos * kvd + kvh * hd + 4 * lane;
+      KVT* kw = reinterpret_cast<KVT*>(a.kc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane;
+      KVT* vw = reinterpret_cast<KVT*>(a.vc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane;
       kw[0] = kv_cvt<KVT>(kx.x); kw[1] = kv_cvt<KVT>(kx.y); kw[2] = kv_cvt<KVT>(kx.z); kw[3] = kv_cvt<KVT>(kx.w);
       vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
     }

@@ -206,6 +206,21 @@ class QwenB200:
         """Allocate nSlots independent sequences of slotCtx positions each."""
         L.check(L.lib().eg_seq_init(self._h, int(nSlots), int(slotCtx)))
 
+    def seqInitPaged(self, nSlots: int, slotCtx: int, nPages: int):
+        """Slots sharing a pool of nPages 16-position KV pages per layer
+        (PagedAttentionManager, runtime.js:2573-2616)."""
+        L.check(L.lib().eg_seq_init_paged(self._h, int(nSlots), int(slotCtx), int(nPages)))
+
+    def seqRelease(self, slot: int):
+        """freeSeq: empty the slot, its pages back to the pool."""
+        L.check(L.lib().eg_seq_release(self._h, int(slot)))
+
+    def seqPages(self) -> tuple[int, int]:
+        """(free pages, pool pages)."""
+        f, t = C.c_int(0), C.c_int(0)
+        L.check(L.lib().eg_seq_pages(self._h, C.byref(f), C.byref(t)))
+        return f.value, t.value
+
     def seqSetPrompt(self, slot: int, ids):
         """Load a slot's prompt; its position returns to 0."""
         p = np.ascontiguousarray(ids, np.uint32)
