@@ -358,6 +358,69 @@ def run_batch16(args, local):
     }
 
 
+PREFILL_METRIC = "prefill ms per prompt (configs[3], T=1024 and 4096)"
+
+
+def run_prefill(args, local):
+    """prefill of a T-token prompt (uniform ids) through the
+    public API (prefillBatch: host ids in, last logits on the device), timed
+    with CUDA events on the runtime's stream; T = 1024 and 4096, `--steps`
+    prompts each after `--warmup` untimed ones.  Positions 0..T-2 run in
+    batched chunks of 16 (one weight pass per chunk), the last position
+    through the decode step."""
+    import torch
+
+    import vibethinker_webgpu_lora_b200 as E
+    from oracle import oracle as O  # prompt ids only
+
+    cfg = E.QWEN25_3B
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    rt = E.QwenB200(cfg, {"maxCtx": 4096 + 64, "useF16": True, "device": local}).build(
+        "synthetic", seed=SEED)
+    st = torch.cuda.ExternalStream(rt.stream, device=dev)
+    steps = max(1, min(args.steps, 8))
+    res = {}
+    with Clocks(local) as ck:
+        for T in (1024, 4096):
+            p = O.token_ids(T, PROMPT_SEED, cfg["vocabSize"])
+            for _ in range(min(args.warmup, 3)):
+                rt.prefillBatch(p)
+            rt.sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(steps):
+                rt.prefillBatch(p)
+            e1.record(st)
+            rt.sync()
+            torch.cuda.synchronize()
+            res[T] = e0.elapsed_time(e1) / steps
+    weights, _ = cfg_bytes(cfg)
+    chunks = (4096 - 1 + 15) // 16 + 1  # weight passes of the T=4096 prefill
+    hbm, peak_kind = peaks()
+    achieved = weights * chunks / (res[4096] / 1000.0) / 1e9
+    return {
+        "metric": PREFILL_METRIC, "value": round(res[4096], 2), "unit": "ms",
+        "per_T_ms": {str(T): round(v, 2) for T, v in res.items()},
+        "tok_s": {str(T): round(T / (v / 1000.0), 1) for T, v in res.items()},
+        "n_gpus": 1, "steps": steps, "warmup": min(args.warmup, 3),
+        "ms_per_step": round(res[4096], 2), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4xf32", "data": "synthetic",
+        "config": {"workload": "configs[3]: Qwen2.5-3B-shape prefill of a uniform-id prompt, "
+                               "T = 1024 and 4096 (value: T = 4096)", "kv": "f16",
+                   "l2": "inputs larger than L2 (1.79 GB of weights per chunk pass)",
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "tensor (batched integer MMA)", "kernel": "whole prefill: one "
+                     "weight pass per 16-position chunk", "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s (weight bytes streamed)",
+                     "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": None},
+        "e2e": {"value": round(res[4096], 2), "unit": "ms", "h2d_bytes_per_step": 4 * 4096,
+                "d2h_bytes_per_step": 0, "what": "prefillBatch from host ids"},
+        "gpu_launches": None,
+        "clocks": ck.summary(),
+    }
+
+
 def cpu_baseline(cfg, n_prompt, steps):
     """The reference's decode path restated in C (oracle/), all host cores:
     bounded sample of `steps` decode tokens after a short prompt."""
@@ -448,8 +511,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "graph"],
                     help="decode path: persistent fused kernel or per-op CUDA graph")
-    ap.add_argument("--workload", default="decode", choices=["decode", "batch16"],
-                    help="decode: configs[1]/[2] (the headline); batch16: configs[4]")
+    ap.add_argument("--workload", default="decode", choices=["decode", "batch16", "prefill"],
+                    help="decode: configs[1]/[2] (the headline); batch16: configs[4]; "
+                         "prefill: configs[3]")
     ap.add_argument("--ncu-probe", type=int, default=0, metavar="CTX",
                     help="profiling target: build, prefill CTX tokens, decode 2 tokens, exit "
                          "(CTX * launches/step launches precede the 2 profiled steps)")
@@ -468,9 +532,10 @@ def main():
             return
         print(json.dumps(run_reference(args, ws, rank)), flush=True)
         return
-    if args.workload == "batch16":
+    if args.workload in ("batch16", "prefill"):
         if rank == 0:
-            print(json.dumps(run_batch16(args, local)), flush=True)
+            run = run_batch16 if args.workload == "batch16" else run_prefill
+            print(json.dumps(run(args, local)), flush=True)
         return
     res = run_ours(args, ws, rank, local)
     if rank == 0:

@@ -77,6 +77,9 @@ typedef struct {
   int use_fused;           /* 1: persistent fused decode kernel (one cooperative
                               launch per token batch) when no LoRA is active;
                               0 (default): per-op kernels in a CUDA graph */
+  int prefill_chunk;       /* prompt positions per batched prefill step (2..16,
+                              default 16): every weight tile is read once per
+                              chunk; 0 = one decode step per prompt token */
 } eg_options;
 
 EG_API const char* eg_last_error(void);
@@ -155,7 +158,9 @@ EG_API void* eg_stream(eg_rt* rt);
 EG_API eg_status eg_sync(eg_rt* rt);
 /* prefillBatch(ids), runtime.js:1936-1945: positions 0..T-1; throws
  * "prompt T > maxPrefillT M" / "prompt T > maxCtx M".  Logits of the last
- * position are left on the device. */
+ * position are left on the device.  Positions 0..T-2 run in batched chunks
+ * of prefill_chunk positions (K/V rows only), the last through the decode
+ * step. */
 EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T);
 /* argmaxLogits(), runtime.js:1602-1629: writes s.amax and returns it. */
 EG_API eg_status eg_argmax(eg_rt* rt, uint32_t* out_id);
@@ -240,6 +245,10 @@ EG_API eg_status eg_seq_release(eg_rt* rt, int slot);
 EG_API eg_status eg_seq_pages(eg_rt* rt, int* free_pages, int* total_pages);
 /* The slot's prompt: ids[0..T) become its known tokens, its position 0. */
 EG_API eg_status eg_seq_set_prompt(eg_rt* rt, int slot, const uint32_t* ids, int T);
+/* Prefill the slot's prompt up to its last token in batched chunks of 16
+ * positions (each chunk one pass over the weights; K/V rows only, no
+ * logits); the next batch step consumes the last prompt token. */
+EG_API eg_status eg_seq_prefill(eg_rt* rt, int slot);
 /* Position (the token the next step consumes) and count of known ids. */
 EG_API eg_status eg_seq_state(eg_rt* rt, int slot, int* pos, int* len);
 /* `steps` batched steps over the slots seq_ids[0..nseq) (1 <= nseq <= 16,

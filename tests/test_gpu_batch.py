@@ -237,3 +237,80 @@ def test_paged_slots_equal_dense_slots(cuda):
     assert paged.seqState(0) == (0, 0)
     with pytest.raises(E.EmberglassError):
         paged.batchDecode([0], 1)  # released: no prompt
+
+
+@pytest.mark.parametrize("f16", [True, False])
+def test_chunked_prefill_single_stream(cuda, f16):
+    """prefillBatch runs positions 0..T-2 as batched chunks of 16 (K/V rows
+    only) and the last position through the decode step: the logits after
+    the prompt and the greedy continuation match the oracle, and the KV
+    cache it leaves serves decoding like the per-token prefill's."""
+    cfg = small_config(layers=2, vocab=4096)
+    prompt = O.token_ids(40, 0xE6B00010, cfg["vocabSize"])  # 2 full chunks + a tail of 7
+    rt = E.QwenB200(cfg, dict(maxCtx=96, useF16=f16)).build("synthetic", seed=SEED)
+    ref = E.QwenB200(cfg, dict(maxCtx=96, useF16=f16, prefillChunk=0)).build("synthetic", seed=SEED)
+    orc = O.OracleModel(cfg, 96, f16, SEED)
+    for t, tok in enumerate(prompt):
+        want = orc.step(int(tok), t)
+    bars = Bars(f16)
+    rt.prefillBatch(prompt)
+    ref.prefillBatch(prompt)
+    bars.check(rt.readLogits(), want)
+    bars.check(ref.readLogits(), want)
+    first = rt.argmaxLogits()
+    assert first == ref.argmaxLogits()
+    got = rt.decodeBatch(len(prompt), 12)
+    exp = ref.decodeBatch(len(prompt), 12)
+    ids, margins = O.OracleModel(cfg, 96, f16, SEED).generate(prompt, 13)
+    assert first == ids[0] or margins[0] < TIE_BOUND
+    for i, (x, y) in enumerate(zip(got, ids[1:])):
+        if x != y:
+            assert margins[i + 1] < TIE_BOUND
+            break
+    # the two prefills' caches lead to the same continuation except at near-ties
+    for i, (x, y) in enumerate(zip(got, exp)):
+        if x != y:
+            assert margins[i + 1] < TIE_BOUND
+            break
+
+
+def test_chunked_prefill_slots_and_lora(cuda):
+    """seqPrefill runs each slot's prompt (but its last token) in chunks;
+    the next batched step then matches the oracle, with a LoRA adapter
+    active, on dense and paged slots."""
+    cfg = small_config(layers=2, vocab=3000)
+    rt = E.QwenB200(cfg, dict(maxCtx=96, useF16=True)).build("synthetic", seed=SEED)
+    a = E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16)
+    rt.setLora(a)
+    ps = prompts(3, cfg["vocabSize"], [33, 2, 17])
+    for paged in (False, True):
+        if paged:
+            rt.seqInitPaged(3, 64, 12)
+        else:
+            rt.seqInit(3, 64)
+        orcs = []
+        for sl, p in enumerate(ps):
+            rt.seqSetPrompt(sl, p)
+            rt.seqPrefill(sl)
+            assert rt.seqState(sl) == (len(p) - 1, len(p))
+            o = O.OracleModel(cfg, 96, True, SEED)
+            o.lora_synth(0xA1, 8, 2.0)
+            for t, tok in enumerate(p[:-1]):
+                o.step(int(tok), t)
+            orcs.append(o)
+        bars = Bars(True)
+        toks = [list(p) for p in ps]
+        for s in range(6):
+            out = rt.batchDecode([0, 1, 2], 1)[0]
+            for j in range(3):
+                pos = len(ps[j]) - 1 + s
+                ref = orcs[j].step(int(toks[j][pos]), pos)
+                bars.check(rt.batchLogits(j), ref)
+                if out[j] != O.argmax(ref):
+                    assert margin(ref) < TIE_BOUND
+                toks[j].append(int(out[j]) if out[j] == O.argmax(ref) else O.argmax(ref))
+            if any(out[j] != toks[j][-1] for j in range(3)):
+                break  # a near-tie parted the streams
+        bars.done()
+    rt.clearLora()
+    a.destroy()

@@ -63,14 +63,24 @@ def test_small_model_logits_and_greedy(cuda, f16, path):
 
 @pytest.mark.parametrize("fused", [True, False])
 def test_prefill_matches_token_loop(cuda, fused):
+    """Per-token prefill (prefillChunk=0) is the token loop, bit for bit;
+    the default chunked prefill (positions 0..T-2 through the batched GEMVs,
+    another f32 summation order) is held to the oracle bars."""
     cfg = small_config(layers=2, vocab=3000)
-    rt = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused)).build("synthetic", seed=SEED)
     prompt = O.token_ids(20, 5, cfg["vocabSize"])
+    rt = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused, prefillChunk=0)).build("synthetic", seed=SEED)
     rt.prefillBatch(prompt)
     a = rt.readLogits()
     for t, tok in enumerate(prompt):
         rt.token(int(tok), t)
     assert np.array_equal(a, rt.readLogits())  # deterministic, bitwise
+    orc = O.OracleModel(cfg, 128, True, SEED)
+    for t, tok in enumerate(prompt):
+        ref = orc.step(int(tok), t)
+    ch = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused)).build("synthetic", seed=SEED)
+    ch.prefillBatch(prompt)
+    close(ch.readLogits(), ref)
+    close(a, ref)
 
 
 def test_fused_equals_graph_path(cuda):

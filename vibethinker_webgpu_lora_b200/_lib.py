@@ -35,7 +35,7 @@ class EgOptions(C.Structure):
         ("device", C.c_int), ("max_ctx", C.c_int), ("max_prefill_t", C.c_int), ("kv_f16", C.c_int),
         ("decode_batch_capacity", C.c_int), ("sampling_top_k", C.c_int),
         ("max_sampling_top_k", C.c_int), ("attn_chunk", C.c_int), ("use_graphs", C.c_int),
-        ("use_pdl", C.c_int), ("use_fused", C.c_int),
+        ("use_pdl", C.c_int), ("use_fused", C.c_int), ("prefill_chunk", C.c_int),
     ]
 
 
@@ -89,6 +89,7 @@ _SIGS = {
     "eg_seq_init": (i32, [vp, i32, i32]),
     "eg_seq_init_paged": (i32, [vp, i32, i32, i32]),
     "eg_seq_release": (i32, [vp, i32]),
+    "eg_seq_prefill": (i32, [vp, i32]),
     "eg_seq_pages": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
     "eg_seq_set_prompt": (i32, [vp, i32, vp, i32]),
     "eg_seq_state": (i32, [vp, i32, vp, vp]),

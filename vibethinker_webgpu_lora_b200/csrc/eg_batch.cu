@@ -58,7 +58,8 @@ __device__ __forceinline__ XSrc lane_src(const BatchSrc& b, int v) {
   if (s.mode == X_EMBED_RMS) {
     const int slot = b.seq.lane_slot[v];
     s.pos = b.seq.pos + slot;
-    s.ids = b.seq.ids + (size_t)slot * b.seq.slot_ctx;
+    // chunked prefill: lane v embeds the token of position pos + v
+    s.ids = b.seq.ids + (size_t)slot * b.seq.slot_ctx + (b.seq.chunk ? v : 0);
     s.use_fixed_id = 0;
   }
   return s;
@@ -521,7 +522,51 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_batch_kernel(AttnArgs a0
   a.po = a0.po + (size_t)v * b.part_stride * kHeadDim;
   a.out = a0.out + (size_t)v * b.out_stride;
   a.counters = a0.counters + (size_t)v * 64;
+  if (b.seq.chunk) {
+    a.pos_off = v;
+    a.appended = 1;
+  }
   attn_head_item<KVT>(a, blockIdx.y, blockIdx.x, pdl, sm);
+}
+
+// One warp per (lane, KV head): RoPE(k) and v of position pos + lane into
+// the cache (rope_lane4 / kv_cvt, as the attention item appends them).
+template <typename KVT>
+__global__ void kv_append_batch_kernel(AttnArgs a0, AttnBatch b) {
+  const int v = blockIdx.x, lane = threadIdx.x & 31;
+  const int slot = b.seq.lane_slot[v];
+  const int pos = b.seq.pos[slot] + v;
+  const int hd = kHeadDim, kvd = a0.nkv * hd;
+  const uint32_t* pages = b.page_table ? b.page_table + (size_t)slot * b.max_pages : nullptr;
+  char* kb = reinterpret_cast<char*>(a0.kc) + (b.page_table ? 0 : (size_t)slot * b.kv_slot_bytes);
+  char* vb = reinterpret_cast<char*>(a0.vc) + (b.page_table ? 0 : (size_t)slot * b.kv_slot_bytes);
+  const float* qkv = a0.qkv + (size_t)v * b.qkv_stride;
+  const size_t row = kv_row(pages, pos);
+  float cj[4], sj[4];
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const int j = (4 * lane + c) & (hd / 2 - 1);
+    cj[c] = __ldg(a0.cosT + (size_t)pos * hd + j);
+    sj[c] = __ldg(a0.sinT + (size_t)pos * hd + j);
+  }
+  for (int kvh = threadIdx.x >> 5; kvh < a0.nkv; kvh += blockDim.x >> 5) {
+    const float4 kx = rope_lane4(
+        __ldcg(reinterpret_cast<const float4*>(qkv + a0.nh * hd + kvh * hd + 4 * lane)), cj, sj,
+        a0.kv_f16, false);
+    const float4 vr =
+        __ldcg(reinterpret_cast<const float4*>(qkv + a0.nh * hd + kvd + kvh * hd + 4 * lane));
+    KVT* kw = reinterpret_cast<KVT*>(kb) + row * kvd + kvh * hd + 4 * lane;
+    KVT* vw = reinterpret_cast<KVT*>(vb) + row * kvd + kvh * hd + 4 * lane;
+    kw[0] = kv_cvt<KVT>(kx.x); kw[1] = kv_cvt<KVT>(kx.y); kw[2] = kv_cvt<KVT>(kx.z); kw[3] = kv_cvt<KVT>(kx.w);
+    vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
+  }
+}
+
+void kv_append_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st) {
+  if (a.kv_f16)
+    kv_append_batch_kernel<__half><<<lanes, 32 * std::min(a.nkv, 32), 0, st>>>(a, b);
+  else
+    kv_append_batch_kernel<float><<<lanes, 32 * std::min(a.nkv, 32), 0, st>>>(a, b);
 }
 
 void attn_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st, bool pdl) {
@@ -595,6 +640,10 @@ __global__ void batch_advance_kernel(SeqTable seq, const uint32_t* choice, int l
                                      uint32_t* out, int* step_ctr) {
   const int v = threadIdx.x;
   const int step = *step_ctr;
+  if (seq.chunk) {  // chunked prefill: the slot moves on by the chunk
+    if (v == 0) seq.pos[seq.lane_slot[0]] += lanes;
+    return;
+  }
   if (v < lanes) {
     const int s = seq.lane_slot[v];
     const int p = seq.pos[s];

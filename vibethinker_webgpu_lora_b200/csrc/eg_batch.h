@@ -25,6 +25,10 @@ struct SeqTable {
   uint32_t* ids;         // [slots][slot_ctx]
   int slot_ctx;
   uint32_t vocab;        // ids >= vocab (argmax of all-NaN logits) are stored as 0
+  // Chunked prefill: every lane is the same slot and lane v is position
+  // pos[slot] + v (its token ids[pos + v]); a step moves pos on by the lane
+  // count.
+  int chunk;
 };
 
 // Where each lane's GEMV input comes from: XSrc of lane 0 with x (and
@@ -85,6 +89,12 @@ struct AttnBatch {
   int max_pages;
 };
 void attn_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st, bool pdl);
+
+// Chunked prefill, before the attention: lane v's k row (RoPE at its
+// position) and v row of qkv + v * qkv_stride go into the cache rows of
+// positions pos + v, rounded as the cache stores them (the attention
+// item's append, runtime.js:1509-1514).
+void kv_append_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st);
 
 // LoRA B side of every lane: out[v * be.lstride + row] = the single-lane
 // epilogue's lora_dot for that row (e.mods, e.lora_d + v * dstride); rows =

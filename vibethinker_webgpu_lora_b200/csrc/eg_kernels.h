@@ -120,6 +120,11 @@ struct AttnArgs {
   // row t lives at physical row pages[t / 16] * 16 + t % 16 of kc / vc;
   // null = contiguous rows.
   const uint32_t* pages;
+  // Chunked prefill: the query position is *pos + pos_off, and with
+  // `appended` the cache already holds every row up to it (written by
+  // kv_append_batch), so all rows are read from the cache and none is
+  // appended here.
+  int pos_off, appended;
 };
 int attn_max_splits(int max_ctx);
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);

@@ -742,7 +742,7 @@ EG_API void eg_default_config(eg_config* c) {
 }
 EG_API void eg_default_options(eg_options* o) {
   if (!o) return;
-  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0};
+  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0, 16};
 }
 
 EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** out) {
@@ -767,6 +767,7 @@ EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** 
   if (o.max_ctx <= 0) o.max_ctx = 8192;
   if (o.max_prefill_t <= 0 || o.max_prefill_t > o.max_ctx) o.max_prefill_t = o.max_ctx;
   if (o.decode_batch_capacity <= 0) o.decode_batch_capacity = 32;
+  o.prefill_chunk = o.prefill_chunk < 2 ? 0 : std::min(o.prefill_chunk, (int)kBatchMax);
   if (o.max_sampling_top_k <= 0 || o.max_sampling_top_k > 64) o.max_sampling_top_k = 64;
   if (o.sampling_top_k <= 0) o.sampling_top_k = 40;
   o.max_sampling_top_k = std::max(o.max_sampling_top_k, std::min(o.sampling_top_k, 64));
@@ -1054,6 +1055,8 @@ EG_API eg_status eg_sync(eg_rt* rt) {
   return sync(rt);
 }
 
+static eg_status prefill_main_chunks(eg_rt* rt, int npos, int chunk);
+
 EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T) {
   eg_status s = need_ready(rt);
   if (s) return s;
@@ -1065,6 +1068,13 @@ EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T) {
   CK(cudaSetDevice(rt->o.device));
   CK(cudaMemcpyAsync(rt->ids, ids, (size_t)T * 4, cudaMemcpyHostToDevice, rt->st));
   if ((s = set_state(rt, 0, 0, 0, nullptr))) return s;
+  // positions 0..T-2 in batched chunks (their K/V rows only), then the last
+  // position through the decode step, which leaves its logits
+  const int chunk = rt->o.prefill_chunk, pre = chunk ? T - 1 : 0;
+  if (pre >= 2) {
+    if ((s = prefill_main_chunks(rt, pre, chunk))) return s;
+    return run_tokens(rt, pre, T - pre, false, false);
+  }
   if ((s = run_tokens(rt, 0, T, false, false))) return s;  // logits of the last position only
   return EG_OK;
 }
@@ -1212,42 +1222,16 @@ static eg_status seq_free(eg_rt* rt) {
   return EG_OK;
 }
 
-// n_pages == 0: every slot owns slot_ctx contiguous rows; n_pages > 0: the
-// slots share a pool of n_pages 16-row pages per layer (PagedAttentionManager,
-// runtime.js:2573-2616), allocated as positions are reached.
-static eg_status seq_setup(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
-  eg_status s = need_ready(rt);
-  if (s) return s;
-  if (n_slots < 0 || n_slots > 4096 || (n_slots && (slot_ctx < 2 || slot_ctx > rt->o.max_ctx)))
-    return fail(EG_ERR_ARG, "seq_init: %d slots of %d positions (2 <= ctx <= maxCtx %d)", n_slots,
-                slot_ctx, rt->o.max_ctx);
-  if (n_pages < 0 || n_pages > (1 << 24)) return fail(EG_ERR_ARG, "seq_init: %d pages", n_pages);
-  Busy b(rt);
-  if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
-  CK(cudaSetDevice(rt->o.device));
-  if ((s = seq_free(rt))) return s;
-  if (!n_slots) return EG_OK;
+// Scratch of the batched step (16 lanes), shared by the sequence slots and
+// the chunked prefill of the single stream; sized for max_ctx.
+static eg_status batch_scratch(eg_rt* rt) {
+  if (rt->b_hidden) return EG_OK;
   const eg_config& c = rt->c;
   const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
   const int I = c.intermediate_size, NQKV = QD + 2 * KVD, V = c.vocab_size, B = kBatchMax;
-  const size_t rows = n_pages ? (size_t)n_pages * 16 : (size_t)n_slots * slot_ctx;
-  const size_t kvb = rows * KVD * (rt->o.kv_f16 ? 2 : 4);
-  rt->seq_kc.assign(c.num_layers, nullptr);
-  rt->seq_vc.assign(c.num_layers, nullptr);
-  for (int i = 0; i < c.num_layers; i++) {
-    DALLOC(rt->seq_kc[i], kvb, &rt->kv_bytes);
-    DALLOC(rt->seq_vc[i], kvb, &rt->kv_bytes);
-    CK(cudaMemsetAsync(rt->seq_kc[i], 0, kvb, rt->st));
-    CK(cudaMemsetAsync(rt->seq_vc[i], 0, kvb, rt->st));
-  }
   int64_t* sb = &rt->scratch_bytes;
-  rt->seq_slots = n_slots;
-  rt->seq_ctx = slot_ctx;
-  rt->b_max_splits = attn_max_splits(slot_ctx);
+  rt->b_max_splits = rt->max_splits;
   rt->b_gpr = (std::max(std::max(H, QD), I) + 127) / 128;
-  DALLOC(rt->seq_pos, (size_t)n_slots * 4, sb);
-  DALLOC(rt->seq_len, (size_t)n_slots * 4, sb);
-  DALLOC(rt->seq_ids, (size_t)n_slots * slot_ctx * 4, sb);
   DALLOC(rt->lane_slot, B * 4, sb);
   DALLOC(rt->b_step, 4, sb);
   DALLOC(rt->b_hidden, (size_t)B * H * 4, sb);
@@ -1272,15 +1256,52 @@ static eg_status seq_setup(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
   DALLOC(rt->b_cand_i, ncand * 4, sb);
   DALLOC(rt->b_topk_ids, B * 64 * 4, sb);
   DALLOC(rt->b_topk_vals, B * 64 * 4, sb);
-  CK(cudaMemsetAsync(rt->seq_pos, 0, (size_t)n_slots * 4, rt->st));
-  CK(cudaMemsetAsync(rt->seq_len, 0, (size_t)n_slots * 4, rt->st));
-  CK(cudaMemsetAsync(rt->seq_ids, 0, (size_t)n_slots * slot_ctx * 4, rt->st));
   CK(cudaMemsetAsync(rt->lane_slot, 0, B * 4, rt->st));
   CK(cudaMemsetAsync(rt->b_xb, 0, (size_t)B * rt->b_gpr * 512, rt->st));
   CK(cudaMemsetAsync(rt->b_xcor, 0, (size_t)B * rt->b_gpr * 8, rt->st));
   CK(cudaMemsetAsync(rt->b_xmul, 0, (size_t)B * rt->b_gpr * 8, rt->st));
   CK(cudaMemsetAsync(rt->b_xf, 0, B * 4, rt->st));
   CK(cudaMemsetAsync(rt->b_attn_counters, 0, B * 64 * 4, rt->st));
+  return EG_OK;
+}
+
+// n_pages == 0: every slot owns slot_ctx contiguous rows; n_pages > 0: the
+// slots share a pool of n_pages 16-row pages per layer (PagedAttentionManager,
+// runtime.js:2573-2616), allocated as positions are reached.
+static eg_status seq_setup(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (n_slots < 0 || n_slots > 4096 || (n_slots && (slot_ctx < 2 || slot_ctx > rt->o.max_ctx)))
+    return fail(EG_ERR_ARG, "seq_init: %d slots of %d positions (2 <= ctx <= maxCtx %d)", n_slots,
+                slot_ctx, rt->o.max_ctx);
+  if (n_pages < 0 || n_pages > (1 << 24)) return fail(EG_ERR_ARG, "seq_init: %d pages", n_pages);
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = seq_free(rt))) return s;
+  if (!n_slots) return EG_OK;
+  const eg_config& c = rt->c;
+  const int KVD = c.num_kv_heads * c.head_dim;
+  const size_t rows = n_pages ? (size_t)n_pages * 16 : (size_t)n_slots * slot_ctx;
+  const size_t kvb = rows * KVD * (rt->o.kv_f16 ? 2 : 4);
+  rt->seq_kc.assign(c.num_layers, nullptr);
+  rt->seq_vc.assign(c.num_layers, nullptr);
+  for (int i = 0; i < c.num_layers; i++) {
+    DALLOC(rt->seq_kc[i], kvb, &rt->kv_bytes);
+    DALLOC(rt->seq_vc[i], kvb, &rt->kv_bytes);
+    CK(cudaMemsetAsync(rt->seq_kc[i], 0, kvb, rt->st));
+    CK(cudaMemsetAsync(rt->seq_vc[i], 0, kvb, rt->st));
+  }
+  if ((s = batch_scratch(rt))) return s;
+  int64_t* sb = &rt->scratch_bytes;
+  rt->seq_slots = n_slots;
+  rt->seq_ctx = slot_ctx;
+  DALLOC(rt->seq_pos, (size_t)n_slots * 4, sb);
+  DALLOC(rt->seq_len, (size_t)n_slots * 4, sb);
+  DALLOC(rt->seq_ids, (size_t)n_slots * slot_ctx * 4, sb);
+  CK(cudaMemsetAsync(rt->seq_pos, 0, (size_t)n_slots * 4, rt->st));
+  CK(cudaMemsetAsync(rt->seq_len, 0, (size_t)n_slots * 4, rt->st));
+  CK(cudaMemsetAsync(rt->seq_ids, 0, (size_t)n_slots * slot_ctx * 4, rt->st));
   rt->h_seq_pos.assign(n_slots, 0);
   rt->h_seq_len.assign(n_slots, 0);
   if (n_pages) {
@@ -1389,8 +1410,51 @@ EG_API eg_status eg_seq_state(eg_rt* rt, int slot, int* pos, int* len) {
   return EG_OK;
 }
 
-// One batched step over lanes 0..n-1 (lane v = slot lane_slot[v]).
-static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) {
+// Where a batched step's lanes live: the sequence table and, per layer, the
+// K/V cache base (dense: slot s at s * kv_slot_bytes; paged: the pool).
+struct BatchTarget {
+  SeqTable sq;
+  std::vector<void*> kc, vc;
+  size_t kv_slot_bytes;
+  const uint32_t* page_table;
+  int max_pages;
+};
+
+static BatchTarget slots_target(eg_rt* rt, bool chunk) {
+  const eg_config& c = rt->c;
+  BatchTarget t;
+  t.sq = SeqTable{rt->lane_slot, rt->seq_pos, rt->seq_len, rt->seq_ids, rt->seq_ctx,
+                  (uint32_t)c.vocab_size, chunk ? 1 : 0};
+  t.kc = rt->seq_kc;
+  t.vc = rt->seq_vc;
+  t.kv_slot_bytes = (size_t)rt->seq_ctx * c.num_kv_heads * c.head_dim * (rt->o.kv_f16 ? 2 : 4);
+  t.page_table = rt->seq_page_table;
+  t.max_pages = rt->seq_max_pages;
+  return t;
+}
+
+// The single stream as slot 0 of a one-slot table (its cache is the dense
+// [max_ctx][kv dim] layout, its position the decode state's).
+static BatchTarget main_target(eg_rt* rt) {
+  const eg_config& c = rt->c;
+  BatchTarget t;
+  t.sq = SeqTable{rt->lane_slot, &rt->state->pos, nullptr, rt->ids, rt->o.max_ctx,
+                  (uint32_t)c.vocab_size, 1};
+  for (auto& l : rt->L) {
+    t.kc.push_back(l.kc);
+    t.vc.push_back(l.vc);
+  }
+  t.kv_slot_bytes = 0;
+  t.page_table = nullptr;
+  t.max_pages = 0;
+  return t;
+}
+
+// One batched step over lanes 0..n-1 (lane v = slot lane_slot[v]).  Chunk
+// mode (chunked prefill): the lanes are consecutive positions of one slot;
+// the K/V rows are appended before the attention and there is no LM head.
+static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
+                              const BatchTarget& tg) {
   const eg_config& c = rt->c;
   const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
   const int I = c.intermediate_size, NQKV = QD + 2 * KVD, V = c.vocab_size;
@@ -1400,8 +1464,8 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) 
   const int rank = lora ? rt->active->max_rank : 0;
   const LoraMod* lt = rt->lora_table;
   const int dstride = 3 * kMaxRank;
-  const SeqTable sq{rt->lane_slot, rt->seq_pos, rt->seq_len, rt->seq_ids, rt->seq_ctx,
-                   (uint32_t)c.vocab_size};
+  const SeqTable& sq = tg.sq;
+  const bool chunk = sq.chunk != 0;
   BatchPlanes xp;
   xp.xb = rt->b_xb;
   xp.xcor = rt->b_xcor;
@@ -1462,14 +1526,14 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) 
     launches += 2;
     AttnArgs a = {};
     a.qkv = rt->b_qkv;
-    a.kc = rt->seq_kc[i];
-    a.vc = rt->seq_vc[i];
+    a.kc = tg.kc[i];
+    a.vc = tg.vc[i];
     a.cosT = rt->cosT;
     a.sinT = rt->sinT;
     a.nh = c.num_heads;
     a.nkv = c.num_kv_heads;
     a.max_splits = rt->b_max_splits;
-    a.ctx_bound = rt->seq_ctx;
+    a.ctx_bound = tg.sq.slot_ctx;
     a.kv_f16 = rt->o.kv_f16;
     a.chunk = rt->o.attn_chunk;
     a.pm = rt->b_pm;
@@ -1482,11 +1546,17 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) 
     ab.qkv_stride = NQKV;
     ab.out_stride = QD;
     ab.part_stride = c.num_heads * rt->b_max_splits;
-    ab.kv_slot_bytes = (size_t)rt->seq_ctx * KVD * (rt->o.kv_f16 ? 2 : 4);
-    ab.page_table = rt->seq_page_table;
-    ab.max_pages = rt->seq_max_pages;
-    attn_batch(a, ab, n, st, pdl);
-    launches++;
+    ab.kv_slot_bytes = tg.kv_slot_bytes;
+    ab.page_table = tg.page_table;
+    ab.max_pages = tg.max_pages;
+    if (chunk) {  // every lane's row first, then attention reads them all (no early start)
+      kv_append_batch(a, ab, n, st);
+      attn_batch(a, ab, n, st, false);
+      launches += 2;
+    } else {
+      attn_batch(a, ab, n, st, pdl);
+      launches++;
+    }
     BatchSrc xo = src(X_PLAIN, rt->b_attn, nullptr, QD);
     if (lora) {
       lora_a_batch(xo, QD, lt + i * 7 + 3, 1, rank, rt->b_lora_d, dstride, n, st, pdl);
@@ -1515,6 +1585,10 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) 
                   err, st, pdl);
     launches += 2;
   }
+  if (chunk) {  // chunked prefill: no logits for these positions
+    batch_advance(sq, rt->b_choice, n, rt->b_out, rt->b_step, st);
+    return launches + 1;
+  }
   BatchSrc xf = src(X_RMS, rt->b_hidden, rt->final_norm, H);
   batch_stage_q8(xf, H, n, xp, st, pdl);
   gemv_q8_batch(rt->emb_t, rt->emb_s, V, H, n, xp, rt->b_logits, V, err, st, pdl);
@@ -1531,6 +1605,70 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp) 
   }
   batch_advance(sq, rt->b_choice, n, rt->b_out, rt->b_step, st);
   return launches + 1;
+}
+
+// Chunked prefill of `npos` positions of slot `slot` of the target, from
+// its current position: steps of `chunk` consecutive positions (one weight
+// pass each; the full-chunk step captured once as a graph), then the tail.
+// The batch scratch must exist before `tg` was built (its sequence table
+// points into it).
+static eg_status run_chunks(eg_rt* rt, const BatchTarget& tg, int slot, int npos, int chunk) {
+  if (npos <= 0) return EG_OK;
+  if (!rt->b_hidden || tg.sq.lane_slot != rt->lane_slot)
+    return fail(EG_ERR_STATE, "batched prefill: scratch not allocated");
+  int lanes[kBatchMax];
+  for (int& l : lanes) l = slot;
+  CK(cudaMemcpyAsync(rt->lane_slot, lanes, sizeof lanes, cudaMemcpyHostToDevice, rt->st));
+  const int full = npos / chunk, tail = npos % chunk;
+  if (full >= 2 && rt->o.use_graphs) {
+    cudaGraph_t g;
+    cudaGraphExec_t ge = nullptr;
+    CK(cudaStreamBeginCapture(rt->st, cudaStreamCaptureModeThreadLocal));
+    enqueue_batch_step(rt, chunk, false, 1, 1.f, tg);
+    cudaError_t e1 = cudaGetLastError();
+    cudaError_t e2 = cudaStreamEndCapture(rt->st, &g);
+    if (e1 != cudaSuccess) return fail(EG_ERR_CUDA, "prefill capture: %s", cudaGetErrorString(e1));
+    if (e2 != cudaSuccess) return fail(EG_ERR_CUDA, "end capture: %s", cudaGetErrorString(e2));
+    cudaError_t e3 = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e3 != cudaSuccess) return fail(EG_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e3));
+    cudaError_t e4 = cudaSuccess;
+    for (int t = 0; t < full && e4 == cudaSuccess; t++) e4 = cudaGraphLaunch(ge, rt->st);
+    cudaError_t e5 = cudaStreamSynchronize(rt->st);
+    cudaGraphExecDestroy(ge);
+    if (e4 != cudaSuccess) return fail(EG_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e4));
+    if (e5 != cudaSuccess) return fail(EG_ERR_CUDA, "prefill chunks: %s", cudaGetErrorString(e5));
+  } else {
+    for (int t = 0; t < full; t++) enqueue_batch_step(rt, chunk, false, 1, 1.f, tg);
+  }
+  if (tail) enqueue_batch_step(rt, tail, false, 1, 1.f, tg);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+// The single stream's positions 0..npos-1 (its decode-state position is 0).
+static eg_status prefill_main_chunks(eg_rt* rt, int npos, int chunk) {
+  eg_status s = batch_scratch(rt);  // before the target captures its pointers
+  if (s) return s;
+  return run_chunks(rt, main_target(rt), 0, npos, chunk);
+}
+
+EG_API eg_status eg_seq_prefill(eg_rt* rt, int slot) {
+  eg_status s = need_ready(rt);
+  if (s) return s;
+  if (slot < 0 || slot >= rt->seq_slots) return fail(EG_ERR_ARG, "slot %d out of range", slot);
+  const int pos = rt->h_seq_pos[slot], len = rt->h_seq_len[slot];
+  if (len < 1) return fail(EG_ERR_STATE, "slot %d has no prompt", slot);
+  const int npos = len - 1 - pos;  // the last prompt token is left to the next batch step
+  if (npos <= 0) return EG_OK;
+  Busy b(rt);
+  if (!b.ok) return fail(EG_ERR_BUSY, "a decode call is in flight");
+  CK(cudaSetDevice(rt->o.device));
+  if ((s = ensure_pages(rt, slot, len - 1))) return s;
+  if ((s = run_chunks(rt, slots_target(rt, true), slot, npos, kBatchMax))) return s;
+  if ((s = sync(rt))) return s;
+  rt->h_seq_pos[slot] = len - 1;
+  return EG_OK;
 }
 
 static eg_status batch_run(eg_rt* rt, int nseq, const int* seq_ids, int steps, bool sample, int k,
@@ -1603,7 +1741,7 @@ static eg_status batch_run(eg_rt* rt, int nseq, const int* seq_ids, int steps, b
     cudaGraph_t g;
     cudaGraphExec_t ge = nullptr;
     CK(cudaStreamBeginCapture(rt->st, cudaStreamCaptureModeThreadLocal));
-    rt->launches_per_step = enqueue_batch_step(rt, nseq, sample, k, temp);
+    rt->launches_per_step = enqueue_batch_step(rt, nseq, sample, k, temp, slots_target(rt, false));
     cudaError_t e1 = cudaGetLastError();
     cudaError_t e2 = cudaStreamEndCapture(rt->st, &g);
     if (e1 != cudaSuccess) return fail(EG_ERR_CUDA, "batch step capture: %s", cudaGetErrorString(e1));
@@ -1618,7 +1756,8 @@ static eg_status batch_run(eg_rt* rt, int nseq, const int* seq_ids, int steps, b
     if (e4 != cudaSuccess) return fail(EG_ERR_CUDA, "graph launch: %s", cudaGetErrorString(e4));
     if (e5 != cudaSuccess) return fail(EG_ERR_CUDA, "batch steps: %s", cudaGetErrorString(e5));
   } else {
-    for (int t = 0; t < steps; t++) rt->launches_per_step = enqueue_batch_step(rt, nseq, sample, k, temp);
+    for (int t = 0; t < steps; t++)
+      rt->launches_per_step = enqueue_batch_step(rt, nseq, sample, k, temp, slots_target(rt, false));
     CK(cudaGetLastError());
   }
   rt->seq_lanes_last = nseq;

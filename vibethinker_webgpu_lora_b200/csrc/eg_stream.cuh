@@ -433,7 +433,7 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
   // The position and the cached rows t != pos were written before the
   // producing GEMV started (it triggers this launch only after its own
   // griddepcontrol.wait).
-  const int pos = a.pos ? __ldcg(a.pos) : a.fixed_pos;
+  const int pos = (a.pos ? __ldcg(a.pos) : a.fixed_pos) + a.pos_off;
   const int ctx = pos + 1;
   const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
   const int nsplit = (ctx + keys - 1) / keys;
@@ -445,7 +445,7 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
 #pragma unroll
   for (int i = 0; i < kAttnKpw; i++) {
     const int t = t0 + warp + kAttnWarps * i;
-    if (t < t1 && t != pos) {
+    if (t < t1 && (t != pos || a.appended)) {
       const size_t r = kv_row(a.pages, t);
       K[i].load(kc + r * kvd);
       V[i].load(vc + r * kvd);
@@ -468,7 +468,7 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
   // q: ROPE_QK, read through f16 in the f16 variant (ATTN_PARTIAL_F16)
   const float4 q4 = rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + h * hd + 4 * lane)),
                                cj, sj, f16, f16 != 0);
-  if (pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v, as the cache stores them
+  if (!a.appended && pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v, as cached
     const float* kn = a.qkv + a.nh * hd + kvh * hd;
     const float* vn = a.qkv + a.nh * hd + kvd + kvh * hd;
     const float4 kx = rope_lane4(__ldcg(reinterpret_cast<const float4*>(kn + 4 * lane)), cj, sj,

@@ -50,6 +50,7 @@ class QwenB200:
         o.use_graphs = int(bool(opts.get("useGraphs", True)))
         o.use_pdl = int(bool(opts.get("usePdl", True)))
         o.use_fused = int(bool(opts.get("useFused", False)))
+        o.prefill_chunk = int(opts.get("prefillChunk", 16))
         self.opts = o
         h = C.c_void_p()
         L.check(L.lib().eg_create(C.byref(_cfg_struct(self.cfg)), C.byref(o), C.byref(h)))
@@ -225,6 +226,10 @@ class QwenB200:
         """Load a slot's prompt; its position returns to 0."""
         p = np.ascontiguousarray(ids, np.uint32)
         L.check(L.lib().eg_seq_set_prompt(self._h, int(slot), p.ctypes.data, int(p.size)))
+
+    def seqPrefill(self, slot: int):
+        """Run the slot's prompt up to its last token in batched chunks."""
+        L.check(L.lib().eg_seq_prefill(self._h, int(slot)))
 
     def seqState(self, slot: int) -> tuple[int, int]:
         """(position, known ids) of a slot."""
