@@ -121,6 +121,7 @@ struct eg_rt {
   // layer, slot s's table at seq_page_table[s * seq_max_pages]
   int seq_pool_pages = 0, seq_max_pages = 0;
   uint32_t* seq_page_table = nullptr;
+  int64_t batch_mark = -1;  // scratch_bytes before the batch scratch was allocated
   std::vector<std::vector<uint32_t>> h_pages;  // pages held by each slot
   std::vector<uint32_t> free_pages;
 };
@@ -1213,6 +1214,8 @@ static eg_status seq_free(eg_rt* rt) {
                  (void**)&rt->b_choice, (void**)&rt->b_cand_i, (void**)&rt->b_topk_ids,
                  (void**)&rt->b_out, (void**)&rt->seq_page_table};
   for (void** q : sp) dfree(rt, q, 0, nullptr);
+  if (rt->batch_mark >= 0) rt->scratch_bytes = rt->batch_mark;  // everything since is freed
+  rt->batch_mark = -1;
   rt->seq_pool_pages = rt->seq_max_pages = 0;
   rt->h_pages.clear();
   rt->free_pages.clear();
@@ -1226,6 +1229,7 @@ static eg_status seq_free(eg_rt* rt) {
 // the chunked prefill of the single stream; sized for max_ctx.
 static eg_status batch_scratch(eg_rt* rt) {
   if (rt->b_hidden) return EG_OK;
+  rt->batch_mark = rt->scratch_bytes;
   const eg_config& c = rt->c;
   const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
   const int I = c.intermediate_size, NQKV = QD + 2 * KVD, V = c.vocab_size, B = kBatchMax;
