@@ -314,3 +314,35 @@ def test_chunked_prefill_slots_and_lora(cuda):
         bars.done()
     rt.clearLora()
     a.destroy()
+
+
+@pytest.mark.parametrize("L,lora", [(16, False), (17, False), (256, False), (257, True), (512, False)])
+def test_prefill_lengths_chunked_vs_sequential(cuda, L, lora):
+    """test/prefill_diff.js:90-115 (batched vs sequential prefill at L in
+    {16, 17, 256, 257, 512}) and test/lora_validate.js:148-244 (the same
+    with LoRA): the chunked and the per-token prefill both meet the oracle's
+    bars at the last position and agree on its argmax unless near a tie."""
+    cfg = small_config(layers=2, vocab=3000)
+    prompt = O.token_ids(L, 0xE6B00010 + L, cfg["vocabSize"])
+    orc = O.OracleModel(cfg, 520, True, SEED)
+    if lora:
+        orc.lora_synth(0xA1, 8, 2.0)
+    for t, tok in enumerate(prompt):
+        ref = orc.step(int(tok), t)
+    out = []
+    for chunk in (16, 0):
+        rt = E.QwenB200(cfg, dict(maxCtx=520, prefillChunk=chunk)).build("synthetic", seed=SEED)
+        a = None
+        if lora:
+            a = E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16)
+            rt.setLora(a)
+        rt.prefillBatch(prompt)
+        got = rt.readLogits()
+        bars = Bars(True)
+        bars.check(got, ref)
+        out.append(got)
+        if a is not None:
+            rt.clearLora()
+            a.destroy()
+    if int(np.argmax(out[0])) != int(np.argmax(out[1])):
+        assert margin(ref) < TIE_BOUND
