@@ -93,7 +93,8 @@ def _raw(path, header_bytes, data=b"", hlen=None):
         f.write(data)
 
 
-@pytest.mark.parametrize("case", ["dtype", "hlen", "json", "offsets", "bytes", "missing", "nofile"])
+@pytest.mark.parametrize("case", ["dtype", "hlen", "json", "offsets", "bytes", "dims", "missing",
+                                  "nofile"])
 def test_broken_files_raise(tmp_path, case):
     p = str(tmp_path / "x.safetensors")
     ok = json.dumps({"t": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]}}).encode()
@@ -109,6 +110,9 @@ def test_broken_files_raise(tmp_path, case):
     elif case == "bytes":
         _raw(p, json.dumps({"t": {"dtype": "F32", "shape": [3], "data_offsets": [0, 8]}}).encode(),
              b"\0" * 8)
+    elif case == "dims":
+        _raw(p, json.dumps({"t": {"dtype": "F32", "shape": [1] * 9, "data_offsets": [0, 4]}}).encode(),
+             b"\0" * 4)
     elif case == "missing":
         _raw(p, ok, b"\0" * 8)
         with pytest.raises(E.EmberglassError, match="not found"):

@@ -1269,6 +1269,8 @@ static eg_status batch_scratch(eg_rt* rt) {
   return EG_OK;
 }
 
+static eg_status seq_alloc(eg_rt* rt, int n_slots, int slot_ctx, int n_pages);
+
 // n_pages == 0: every slot owns slot_ctx contiguous rows; n_pages > 0: the
 // slots share a pool of n_pages 16-row pages per layer (PagedAttentionManager,
 // runtime.js:2573-2616), allocated as positions are reached.
@@ -1284,8 +1286,18 @@ static eg_status seq_setup(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
   CK(cudaSetDevice(rt->o.device));
   if ((s = seq_free(rt))) return s;
   if (!n_slots) return EG_OK;
+  if ((s = seq_alloc(rt, n_slots, slot_ctx, n_pages))) seq_free(rt);  // no partial state
+  return s;
+}
+
+static eg_status seq_alloc(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
+  eg_status s;
   const eg_config& c = rt->c;
   const int KVD = c.num_kv_heads * c.head_dim;
+  // set first, so that seq_free releases whatever was allocated if this fails
+  rt->seq_slots = n_slots;
+  rt->seq_ctx = slot_ctx;
+  rt->seq_pool_pages = n_pages;
   const size_t rows = n_pages ? (size_t)n_pages * 16 : (size_t)n_slots * slot_ctx;
   const size_t kvb = rows * KVD * (rt->o.kv_f16 ? 2 : 4);
   rt->seq_kc.assign(c.num_layers, nullptr);
@@ -1298,8 +1310,6 @@ static eg_status seq_setup(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
   }
   if ((s = batch_scratch(rt))) return s;
   int64_t* sb = &rt->scratch_bytes;
-  rt->seq_slots = n_slots;
-  rt->seq_ctx = slot_ctx;
   DALLOC(rt->seq_pos, (size_t)n_slots * 4, sb);
   DALLOC(rt->seq_len, (size_t)n_slots * 4, sb);
   DALLOC(rt->seq_ids, (size_t)n_slots * slot_ctx * 4, sb);
@@ -1309,7 +1319,6 @@ static eg_status seq_setup(eg_rt* rt, int n_slots, int slot_ctx, int n_pages) {
   rt->h_seq_pos.assign(n_slots, 0);
   rt->h_seq_len.assign(n_slots, 0);
   if (n_pages) {
-    rt->seq_pool_pages = n_pages;
     rt->seq_max_pages = (slot_ctx + 15) / 16;
     DALLOC(rt->seq_page_table, (size_t)n_slots * rt->seq_max_pages * 4, sb);
     CK(cudaMemsetAsync(rt->seq_page_table, 0, (size_t)n_slots * rt->seq_max_pages * 4, rt->st));

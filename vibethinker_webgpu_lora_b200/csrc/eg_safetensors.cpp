@@ -269,10 +269,14 @@ eg_status open_shard(const std::string& path, Shard& sh) {
     r.name = kv.first;
     r.dtype = dt->str;
     for (auto& c : r.dtype) c = (char)toupper((unsigned char)c);
+    if (shp->arr.size() > 8) return fail(EG_ERR_ARG, "%s: %s has more than 8 dims", path.c_str(), kv.first.c_str());
     for (auto& d : shp->arr) {
-      if (d.kind != JVal::NUM || d.num < 0) return fail(EG_ERR_ARG, "%s: bad shape of %s", path.c_str(), kv.first.c_str());
+      if (d.kind != JVal::NUM || d.num < 0 || d.num > 1e15)
+        return fail(EG_ERR_ARG, "%s: bad shape of %s", path.c_str(), kv.first.c_str());
       r.shape.push_back((int64_t)d.num);
-      r.numel *= (int64_t)d.num;
+      if (r.shape.back() && r.numel > ((int64_t)1 << 50) / r.shape.back())
+        return fail(EG_ERR_ARG, "%s: %s is too large", path.c_str(), kv.first.c_str());
+      r.numel *= r.shape.back();
     }
     if (off->arr[0].kind != JVal::NUM || off->arr[1].kind != JVal::NUM)
       return fail(EG_ERR_ARG, "%s: bad data_offsets of %s", path.c_str(), kv.first.c_str());
