@@ -106,3 +106,21 @@ def test_safetensors_reader(tmp_path):
     t = _read_safetensors(str(p))
     assert np.array_equal(t["x.lora_A.weight"], a)
     assert np.array_equal(t["x.lora_B.weight"], np.arange(4, dtype=np.float32))
+
+
+def test_default_options_match_the_header_and_python_struct():
+    """eg_default_options fills every field of the Python mirror of
+    eg_options (the struct sizes agree: the last field is written), with the
+    defaults the header documents."""
+    o = L.EgOptions()
+    for name, _ in L.EgOptions._fields_:
+        setattr(o, name, -7)
+    L.lib().eg_default_options(C.byref(o))
+    got = {name: getattr(o, name) for name, _ in L.EgOptions._fields_}
+    assert -7 not in got.values()
+    assert got["max_ctx"] == 8192 and got["kv_f16"] == 1 and got["use_graphs"] == 1
+    assert got["use_pdl"] == 1 and got["use_fused"] == 0 and got["prefill_chunk"] == 16
+    hdr = open(HEADER).read()
+    fields = hdr[:hdr.index("} eg_options;")].rsplit("typedef struct {", 1)[1]
+    names = re.findall(r"\bint\s+(\w+);", fields)
+    assert names == [n for n, _ in L.EgOptions._fields_]
