@@ -5,16 +5,12 @@ upper half of an f32, F16 converts exactly), unsupported dtypes and broken
 files raise.  CPU tests use the host-only decode entry; the GPU test builds a
 model from a sharded directory and compares it with direct uploads."""
 import json
-import os
 import struct
 
 import numpy as np
 import pytest
 
 import vibethinker_webgpu_lora_b200 as E
-
-DT = {"F32": np.float32, "F16": np.float16, "BF16": np.uint16}
-
 
 def bf16_bits(a):
     """Truncate f32 to bf16 (the upper 16 bits)."""
