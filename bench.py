@@ -66,27 +66,62 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """SM clock and throttle reasons sampled DURING the timed region (read-only
+    NVML queries from a thread every 2 ms, so a 20 ms region still holds ~10
+    samples); nvidia-smi -lms 20 where NVML cannot be loaded."""
 
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
-        self.idx = gpu_index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.p = None
+    def __init__(self, gpu_index, period_s=0.002):
+        self.idx, self.period = gpu_index, period_s
+        self.sms, self.mx, self.reasons = [], None, set()
+        self.stop = None
+        self.p = self.f = None
+
+    def _poll(self, nv, h):
+        bits = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+                "sw_power_cap": 0x4}
+        reasons_fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            try:
+                self.sms.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                r = reasons_fn(h)
+                for n, b in bits.items():
+                    if r & b:
+                        self.reasons.add(n)
+            except Exception:
+                pass
+            time.sleep(self.period)
 
     def __enter__(self):
+        import threading
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
-                                      stdout=self.f, stderr=subprocess.DEVNULL)
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            self.mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.stop = threading.Event()
+            self.t = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self.t.start()
         except Exception:
-            self.p = None
+            self.stop = None
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            try:
+                self.p = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                           "--format=csv,noheader,nounits", "-lms", "20"],
+                                          stdout=self.f, stderr=subprocess.DEVNULL)
+            except Exception:
+                self.p = None
         return self
 
     def __exit__(self, *a):
+        if self.stop is not None:
+            self.stop.set()
+            self.t.join(timeout=2)
         if self.p:
             self.p.terminate()
             try:
@@ -95,25 +130,26 @@ class Clocks:
                 self.p.kill()
 
     def summary(self):
-        self.f.flush()
-        self.f.seek(0)
-        sms, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.f.read().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sms.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        os.unlink(self.f.name)
-        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sms)}
+        if self.f is not None:
+            self.f.flush()
+            self.f.seek(0)
+            for line in self.f.read().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    self.sms.append(float(parts[1]))
+                    self.mx = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(self.NAMES, parts[5:9]):
+                    if v.lower() == "active":
+                        self.reasons.add(n)
+            os.unlink(self.f.name)
+            self.f = None
+        return {"sm_mhz": statistics.median(self.sms) if self.sms else None, "sm_max_mhz": self.mx,
+                "reasons": sorted(self.reasons), "samples": len(self.sms),
+                "source": "nvml 2 ms" if self.stop is not None else "nvidia-smi 20 ms"}
 
 
 def dist_setup():
@@ -159,12 +195,112 @@ def positions(start, period, n, cap):
     return out
 
 
-def run_ours(args, ws, rank, local):
+def _decode_timed(rt, st, start, period, steps, warmup, cap):
+    """warmup untimed + `steps` timed greedy tokens at positions cycling in
+    [start, start + period) (decodeBatchAsync chains, ids stay on the
+    device); returns the CUDA-event milliseconds on the runtime's stream."""
+    import torch
+
+    def decode(n):
+        for pos, k in positions(start, period, n, cap):
+            rt.decodeBatchAsync(pos, k)
+
+    decode(warmup)
+    rt.sync()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    decode(steps)
+    e1.record(st)
+    rt.sync()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def long_context(rt, st, cfg, ctx, steps, hbm):
+    """f16 KV prefilled from a uniform-id prompt of `ctx` tokens,
+    then `steps` greedy tokens at ctx..ctx+steps-1."""
+    from vibethinker_webgpu_lora_b200.quantize import synth_ids
+    prompt = synth_ids(ctx, PROMPT_SEED, cfg["vocabSize"])
+    rt.prefillBatch(prompt)
+    rt.argmaxLogits()
+    ms = _decode_timed(rt, st, ctx, steps, steps, 3, 32)
+    prof = [rt.profToken(int(prompt[-1]), ctx + 1) for _ in range(3)]
+    attn_us = statistics.median(p["attn"] for p in prof) / cfg["numLayers"]
+    weights, kv_per_pos = cfg_bytes(cfg)
+    step_bytes = weights + kv_per_pos * (ctx + steps / 2)
+    tok_s = steps / (ms / 1000.0)
+    kv_layer = kv_per_pos // cfg["numLayers"] * (ctx + 1)
+    return {"ctx": f"{ctx}..{ctx + steps}", "steps": steps, "value": round(tok_s, 2), "unit": "tok/s",
+            "ms_per_step": round(ms / steps, 5),
+            "step_roofline": {"bytes_per_step": int(step_bytes),
+                              "frac": round(step_bytes * tok_s / 1e9 / hbm, 4),
+                              "roofline_tok_s": round(hbm * 1e9 / step_bytes, 1)},
+            "attention": {"us_per_layer": round(attn_us, 3), "kv_bytes_per_layer": int(kv_layer),
+                          "achieved_gbs": round(kv_layer / (attn_us * 1e-6) / 1e9, 1),
+                          "note": "profToken: eager launches, an event between categories"}}
+
+
+def gemv_2048(hbm):
+    """one int4 GEMV y = W x, W 2048 x 2048 ~ N(0, 0.02) quantised
+    by the reference quantiser, x ~ N(0, 1), weights converted to the device
+    layout once (as the model upload does).  72 launches captured in one CUDA
+    graph with programmatic dependent launch: "cold" rotates over 72 distinct
+    weight copies (161 MB > the 126 MB L2), "hot" reuses one copy."""
     import numpy as np
     import torch
 
+    from vibethinker_webgpu_lora_b200 import kernels as K
+    from vibethinker_webgpu_lora_b200.quantize import quantizeInt4Group, synth_normal
+    N = Kd = 2048
+    copies = 72
+    W = synth_normal(N * Kd, 0xE6B00001, 0.02).reshape(N, Kd)
+    x = torch.from_numpy(synth_normal(Kd, 0xE6B00002, 1.0)).cuda()
+    p, s, _ = quantizeInt4Group(W)
+    nb = K.q4_stream_bytes(N, Kd)
+    nb_al = (nb + 255) // 256 * 256
+    pool = torch.zeros(copies * nb_al, dtype=torch.uint8, device="cuda")
+    tp, ts = torch.from_numpy(p).cuda(), torch.from_numpy(s).cuda()
+    for c in range(copies):
+        K.q4_to_stream(tp, ts, N, Kd, pool[c * nb_al:])
+    y = torch.zeros(N, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    out = {}
+    for mode in ("cold", "hot"):
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        with torch.cuda.stream(side):
+            for c in range(copies):  # warm the launch path outside the capture
+                K.gemv_q4_stream(x, pool[(c if mode == "cold" else 0) * nb_al:], N, Kd, y, err, pdl=True)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for c in range(copies):
+                K.gemv_q4_stream(x, pool[(c if mode == "cold" else 0) * nb_al:], N, Kd, y, err, pdl=True)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = 20
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / (reps * copies)
+        out[mode] = {"us_per_gemv": round(us, 3), "achieved_gbs": round(2244608 / (us * 1e-6) / 1e9, 1),
+                     "frac": round(2244608 / (us * 1e-6) / 1e9 / hbm, 4)}
+    assert int(err.item()) == 0
+    out.update({"bytes_per_gemv": 2244608, "launches": f"{copies} per graph, PDL chained",
+                "note": "2 MiB nibbles + 128 KiB f32 scales + 8 KiB x + 8 KiB y per call"})
+    return out
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+
     import vibethinker_webgpu_lora_b200 as E
-    from oracle import oracle as O  # prompt ids generator and cpu_baseline only
+    from vibethinker_webgpu_lora_b200.quantize import synth_ids
 
     cfg = E.QWEN25_3B
     dev = torch.device("cuda", local)
@@ -172,37 +308,26 @@ def run_ours(args, ws, rank, local):
     if ws > 1:
         os.environ.setdefault("OMP_NUM_THREADS", str(max(1, (os.cpu_count() or 8) // ws)))
     long = args.ctx >= 1024
-    n_prompt = args.ctx if long else N_PROMPT
-    period = 64 if long else 128
-    max_ctx = n_prompt + period + 8
+    # ctx ~128: prefill 96 ids, timed tokens cycle over 96..159
+    n_prompt = args.ctx if long else 96
+    period = 64
+    extras = ws == 1 and not long and not args.no_extras
+    max_ctx = max(n_prompt + period, 7800 + period if extras else 0) + 8
     cap = 32
     opts = {"maxCtx": max_ctx, "useF16": True, "device": local, "decodeBatchSize": cap}
     if args.path != "auto":
         opts["useFused"] = args.path == "fused"
     rt = E.QwenB200(cfg, opts).build("synthetic", seed=SEED)
-    prompt = O.token_ids(n_prompt, PROMPT_SEED ^ rank, cfg["vocabSize"])
+    prompt = synth_ids(n_prompt, PROMPT_SEED ^ rank, cfg["vocabSize"])
     rt.prefillBatch(prompt)
     rt.argmaxLogits()
     st = torch.cuda.ExternalStream(rt.stream, device=dev)
-
-    def decode(n):
-        for pos, k in positions(n_prompt, period, n, cap):
-            rt.decodeBatchAsync(pos, k)
-
-    decode(args.warmup)
-    rt.sync()
     if ws > 1:
         import torch.distributed as dist
         dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as ck:
-        e0.record(st)
-        decode(args.steps)
-        e1.record(st)
-        rt.sync()
-        torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1), ws, dev)
+        ms = _decode_timed(rt, st, n_prompt, period, args.steps, args.warmup, cap)
+    ms = max_over_ranks(ms, ws, dev)
     clocks = ck.summary()
     launches = rt.lastDispatchCount * args.steps
 
@@ -212,14 +337,16 @@ def run_ours(args, ws, rank, local):
     gu_us = statistics.median(p["gate_up"] for p in prof) / cfg["numLayers"]
     step_us = statistics.median(sum(p.values()) for p in prof)
 
-    # end to end through the public API with host buffers: prompt ids H2D,
-    # prefill, greedy decode with ids D2H per decodeBatch call
-    e2e_tokens = min(args.steps, 128) if not long else min(args.steps, 64)
+    # end to end through the public API with host buffers, configs[1] as
+    # stated: prefillBatch(32 host ids) + argmaxLogits + 128 greedy tokens,
+    # ids read back to the host after every decodeBatch call
+    e2e_tokens = 128
+    p32 = synth_ids(N_PROMPT, PROMPT_SEED ^ rank, cfg["vocabSize"])
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    rt.prefillBatch(prompt)
+    rt.prefillBatch(p32)
     rt.argmaxLogits()
-    done, pos = 0, n_prompt
+    done, pos = 0, N_PROMPT
     while done < e2e_tokens:
         got = rt.decodeBatch(pos, min(cap, e2e_tokens - done))
         done += len(got)
@@ -247,7 +374,8 @@ def run_ours(args, ws, rank, local):
         "dtype": "int4xf32",
         "data": "synthetic",
         "config": {"workload": f"configs[{2 if long else 1}]: Qwen2.5-3B-shape int4 greedy decode, "
-                               f"batch 1, prompt {n_prompt}, decode ctx {n_prompt}..{n_prompt + period}",
+                               f"batch 1, prefill {n_prompt} ids, timed tokens at ctx "
+                               f"{n_prompt}..{n_prompt + period} (cycling)",
                    "kv": "f16", "scales": "f32 (stream layout: 16x128 blocks, interleaved f32 scales)", "lm_head": "int8 rows",
                    "l2": "inputs larger than L2 (1.79 GB of weights streamed per step)",
                    "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU"},
@@ -264,13 +392,17 @@ def run_ours(args, ws, rank, local):
                           "roofline_tok_s": round(hbm * 1e9 / step_bytes, 1),
                           "profiled_step_us": round(step_us, 1)},
         "e2e": {"value": round(e2e_tokens / e2e_s, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": round(4 * n_prompt / e2e_tokens, 3),
+                "h2d_bytes_per_step": round(4 * N_PROMPT / e2e_tokens, 3),
                 "d2h_bytes_per_step": 4,
-                "what": f"prefillBatch({n_prompt} host ids) + argmaxLogits + decodeBatch x "
-                        f"{e2e_tokens} tokens to host, wall clock"},
+                "what": f"prefillBatch({N_PROMPT} host ids) + argmaxLogits + decodeBatch to host, "
+                        f"{e2e_tokens} tokens (ctx {N_PROMPT}..{N_PROMPT + e2e_tokens}), wall clock"},
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if extras:
+        result["ctx4096"] = long_context(rt, st, cfg, 4096, 64, hbm)
+        result["ctx7800"] = long_context(rt, st, cfg, 7800, 64, hbm)
+        result["gemv_2048"] = gemv_2048(hbm)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(cfg, n_prompt, args.cpu_steps)
     return result
@@ -289,7 +421,7 @@ def run_batch16(args, local):
     import torch
 
     import vibethinker_webgpu_lora_b200 as E
-    from oracle import oracle as O  # prompt ids and r uniforms (SplitMix64)
+    from vibethinker_webgpu_lora_b200.quantize import synth_ids, synth_uniform
 
     cfg = E.QWEN25_3B
     dev = torch.device("cuda", local)
@@ -303,8 +435,8 @@ def run_batch16(args, local):
     rt.seqInit(n, n_prompt + steps + 2)
     slots = list(range(n))
     for sl in slots:
-        rt.seqSetPrompt(sl, O.token_ids(n_prompt, 0xE6B00100 + sl, cfg["vocabSize"]))
-    r = np.array([[O.uniform(1, 0xE6B00200 ^ sl ^ t)[0] for sl in slots] for t in range(steps)],
+        rt.seqSetPrompt(sl, synth_ids(n_prompt, 0xE6B00100 + sl, cfg["vocabSize"]))
+    r = np.array([[synth_uniform(1, 0xE6B00200 ^ sl ^ t)[0] for sl in slots] for t in range(steps)],
                  np.float32)
     st = torch.cuda.ExternalStream(rt.stream, device=dev)
     torch.cuda.synchronize()
@@ -371,7 +503,7 @@ def run_prefill(args, local):
     import torch
 
     import vibethinker_webgpu_lora_b200 as E
-    from oracle import oracle as O  # prompt ids only
+    from vibethinker_webgpu_lora_b200.quantize import synth_ids
 
     cfg = E.QWEN25_3B
     dev = torch.device("cuda", local)
@@ -383,7 +515,7 @@ def run_prefill(args, local):
     res = {}
     with Clocks(local) as ck:
         for T in (1024, 4096):
-            p = O.token_ids(T, PROMPT_SEED, cfg["vocabSize"])
+            p = synth_ids(T, PROMPT_SEED, cfg["vocabSize"])
             for _ in range(min(args.warmup, 3)):
                 rt.prefillBatch(p)
             rt.sync()
@@ -421,54 +553,55 @@ def run_prefill(args, local):
     }
 
 
-def cpu_baseline(cfg, n_prompt, steps):
-    """The reference's decode path restated in C (oracle/), all host cores:
-    bounded sample of `steps` decode tokens after a short prompt."""
+def _oracle_decode(cfg, n_prompt, warmup, steps):
+    """The reference's decode path restated in C (oracle/, f32 mimic of the
+    WGSL kernels, OpenMP over rows on all host cores): prefill n_prompt
+    uniform ids one position at a time (untimed), `warmup` untimed greedy
+    tokens, then `steps` timed greedy tokens -- the same positions as the GPU
+    arm's timed tokens.  Returns (tok/s, seconds, ctx range, cores)."""
     from oracle import oracle as O
-    m = O.OracleModel(cfg, n_prompt + steps + 8, True, SEED)
-    prompt = O.token_ids(min(n_prompt, 4), PROMPT_SEED, cfg["vocabSize"])
+    m = O.OracleModel(cfg, n_prompt + warmup + steps + 8, True, SEED)
+    prompt = O.token_ids(n_prompt, PROMPT_SEED, cfg["vocabSize"])
+    logits = None
     for t, tok in enumerate(prompt):
-        m.step(int(tok), t)
+        logits = m.step(int(tok), t)
+    tok, pos = O.argmax(logits), n_prompt
+    for _ in range(warmup):
+        tok = O.argmax(m.step(tok, pos))
+        pos += 1
+    p0 = pos
     t0 = time.perf_counter()
-    tok, pos = int(prompt[-1]), len(prompt)
     for _ in range(steps):
-        logits = m.step(tok, pos)
-        tok = O.argmax(logits)
+        tok = O.argmax(m.step(tok, pos))
         pos += 1
     s = time.perf_counter() - t0
     m.close()
-    return {"value": round(steps / s, 3), "unit": "tok/s", "cores": O.threads(), "kind": "port",
-            "sample": f"{steps} greedy decode tokens of the full model at ctx ~{len(prompt)} "
-                      f"(f32 mimic of the reference kernels, OpenMP over rows)"}
+    return steps / s, s, f"{p0}..{pos}", O.threads()
+
+
+def cpu_baseline(cfg, n_prompt, steps):
+    v, _, ctx, cores = _oracle_decode(cfg, n_prompt, 0, steps)
+    return {"value": round(v, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{steps} greedy decode tokens of the full model at ctx {ctx} after an "
+                      f"untimed {n_prompt}-token prefill (f32 mimic of the reference kernels, "
+                      f"OpenMP over rows)"}
 
 
 def run_reference(args, ws, rank):
     cfg = __import__("vibethinker_webgpu_lora_b200").QWEN25_3B
-    n_prompt = args.ctx if args.ctx >= 1024 else N_PROMPT
+    n_prompt = args.ctx if args.ctx >= 1024 else 96
     steps = max(1, min(args.steps, args.cpu_steps))
-    from oracle import oracle as O
-    m = O.OracleModel(cfg, 4 + args.warmup + steps + 8, True, SEED)
-    prompt = O.token_ids(4, PROMPT_SEED, cfg["vocabSize"])
-    for t, tok in enumerate(prompt):
-        m.step(int(tok), t)
-    tok, pos = int(prompt[-1]), len(prompt)
-    for _ in range(min(args.warmup, 2)):
-        tok = O.argmax(m.step(tok, pos))
-        pos += 1
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        tok = O.argmax(m.step(tok, pos))
-        pos += 1
-    s = time.perf_counter() - t0
-    v = steps / s
-    sample = (f"{steps} greedy decode tokens of the full model at ctx ~{pos} (the bench arm runs ctx "
-              f"{n_prompt}+; the CPU path's per-token cost is dominated by the 1.79 GB weight stream)")
+    warm = min(args.warmup, 2)
+    v, s, ctx, cores = _oracle_decode(cfg, n_prompt, warm, steps)
+    sample = (f"{steps} greedy decode tokens of the full model at ctx {ctx} (prefill {n_prompt} "
+              f"+ {warm} warm-up tokens untimed), the GPU arm's context")
     return {"metric": METRIC, "value": round(v, 3), "unit": "tok/s", "impl": "reference", "n_gpus": ws,
-            "steps": steps, "warmup": args.warmup, "ms_per_step": round(1000 * s / steps, 3),
+            "steps": steps, "warmup": warm, "ms_per_step": round(1000 * s / steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xf32",
             "data": "synthetic",
-            "config": {"workload": f"configs[{2 if args.ctx >= 1024 else 1}] on the host CPU"},
-            "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "config": {"workload": f"configs[{2 if args.ctx >= 1024 else 1}] on the host CPU: "
+                                   f"batch-1 greedy decode at ctx {ctx}"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -477,9 +610,9 @@ def ncu_probe(ctx):
     """Smallest run that contains full decode steps, for ncu launch lists and
     single-kernel captures (the weights are 1.8 GB; nothing else is held)."""
     import vibethinker_webgpu_lora_b200 as E
-    from oracle import oracle as O
+    from vibethinker_webgpu_lora_b200.quantize import synth_ids
     rt = E.QwenB200(E.QWEN25_3B, {"maxCtx": ctx + 40}).build("synthetic", seed=SEED)
-    rt.prefillBatch(O.token_ids(ctx, PROMPT_SEED, E.QWEN25_3B["vocabSize"]))
+    rt.prefillBatch(synth_ids(ctx, PROMPT_SEED, E.QWEN25_3B["vocabSize"]))
     rt.argmaxLogits()
     rt.decodeBatchAsync(ctx, 2)
     rt.sync()
@@ -490,12 +623,12 @@ def ncu_probe_batch(steps):
     """Profiling target of the batched path: 16 slots with 8-token prompts,
     `steps` batched greedy steps (launches_per_step launches each), exit."""
     import vibethinker_webgpu_lora_b200 as E
-    from oracle import oracle as O
+    from vibethinker_webgpu_lora_b200.quantize import synth_ids
     cfg = E.QWEN25_3B
     rt = E.QwenB200(cfg, {"maxCtx": 128}).build("synthetic", seed=SEED)
     rt.seqInit(16, 64)
     for sl in range(16):
-        rt.seqSetPrompt(sl, O.token_ids(8, 0xE6B00100 + sl, cfg["vocabSize"]))
+        rt.seqSetPrompt(sl, synth_ids(8, 0xE6B00100 + sl, cfg["vocabSize"]))
     rt.batchDecode(list(range(16)), steps)
     print(json.dumps({"ncu_probe_batch": steps, "launches_per_step": rt.lastDispatchCount}))
 
@@ -509,6 +642,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=128, choices=[128, 4096, 7800])
     ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the ctx 4096/7800 and configs[0] GEMV sub-objects")
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "graph"],
                     help="decode path: persistent fused kernel or per-op CUDA graph")
     ap.add_argument("--workload", default="decode", choices=["decode", "batch16", "prefill"],

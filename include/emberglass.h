@@ -71,7 +71,8 @@ typedef struct {
   int decode_batch_capacity; /* tokens per eg_decode_greedy call, default 32 */
   int sampling_top_k;      /* default 40 */
   int max_sampling_top_k;  /* default 64 (max 64) */
-  int attn_chunk;          /* keys per attention split; 0 = adaptive */
+  int attn_chunk;          /* keys per attention split: 0 = 128 (the reference's
+                              CHUNK, runtime.js:330), else 16..128 step 16 */
   int use_graphs;          /* capture the decode step in a CUDA graph (default 1) */
   int use_pdl;             /* programmatic dependent launch (default 1) */
   int use_fused;           /* 1: persistent fused decode kernel (one cooperative
@@ -278,6 +279,21 @@ EG_API int eg_launches_per_step(eg_rt* rt);
 EG_API eg_status eg_op_gemv_q4(const float* x, const uint32_t* w, const float* scale,
                                const float* bias, int N, int K, int group, float* y,
                                int accumulate, void* stream);
+/* The upload-once form of GEMV4 (the reference converts nothing per call:
+ * ModelUploader writes the packed weights once, model_uploader.js:39-63, and
+ * every gemv4() dispatch reads them, runtime.js:944-964).  eg_op_q4_stream_bytes
+ * gives the size of the device layout the library streams (16-row x 128-k
+ * blocks with their group scales); eg_op_q4_to_stream writes it from the
+ * reference layout (packed u32 [R*N][K/8], f32 scales [R*N][K/128]);
+ * eg_op_gemv_q4_stream then runs y = W4 x (+bias) over it with no
+ * conversion and no allocation.  err: one device int, zero before the call,
+ * set nonzero if a bounded wait inside the kernel gave up.  pdl = 1 lets the
+ * launch overlap the tail of the previous kernel on the stream. */
+EG_API eg_status eg_op_q4_stream_bytes(int N, int K, int R, uint64_t* bytes);
+EG_API eg_status eg_op_q4_to_stream(const uint32_t* w, const float* scale, int N, int K, int R,
+                                    void* out, void* stream);
+EG_API eg_status eg_op_gemv_q4_stream(const float* x, const void* ws, const float* bias, int N,
+                                      int K, float* y, int* err, int pdl, void* stream);
 /* GATE_UP_SILU_GEMV4, kernels.js:1021-1072: w/scale hold 2N rows [gate;up]. */
 EG_API eg_status eg_op_gate_up_silu(const float* x, const uint32_t* w, const float* scale,
                                     int N, int K, float* y, void* stream);
@@ -293,7 +309,8 @@ EG_API eg_status eg_op_rope_qk(float* q, float* k, int nq, int nkv, int pos, con
 /* ROPE_QK + KV append (runtime.js:1509-1514) + ATTN_PARTIAL/ATTN_COMBINE
  * (kernels.js:258-388; _F16 variants when kv_f16): qkv = raw [q | k | v],
  * caches [max_ctx][nkv][128] (f16 when kv_f16 else f32); attends over
- * positions 0..pos.  chunk = keys per split, 0 = adaptive.  Uses library
+ * positions 0..pos.  chunk = keys per split: 0 = 128, the reference's fixed
+ * CHUNK (runtime.js:330), else a multiple of 16 up to 128.  Uses library
  * scratch memory for the split partials. */
 EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cache,
                                    const float* cos_t, const float* sin_t, int nh, int nkv,
@@ -305,7 +322,8 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
  * cannot take cudaMalloc's implicit synchronisation): same arguments and
  * results, with the split partials in a 2 MB static device array loaded with
  * the library instead of library-allocated scratch.  Rejects calls needing
- * nh * ceil((pos+1) / max(chunk, 16)) > 4096 slots (EG_ERR_ARG).  All calls
+ * nh * ceil((pos+1) / keys) > 4096 slots (EG_ERR_ARG), keys = chunk, or 128
+ * when chunk = 0 (e.g. 32 heads at pos 4095 fit with chunk 0).  All calls
  * share the array: calls that overlap on the GPU race.  The first call on a
  * device looks up the array's device address; make it before any stream
  * capture. */

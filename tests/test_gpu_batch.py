@@ -239,6 +239,35 @@ def test_paged_slots_equal_dense_slots(cuda):
         paged.batchDecode([0], 1)  # released: no prompt
 
 
+def test_paged_prefill_oom_then_retry(cuda):
+    """seqPrefill into an exhausted page pool fails without taking any page;
+    once another slot returns its pages the retry runs, and the slot's
+    tokens and logits equal a dense slot's bit for bit (the slot's page list
+    and its device page table stayed in step)."""
+    cfg = small_config(layers=2, vocab=3000)
+    dense = E.QwenB200(cfg, dict(maxCtx=64)).build("synthetic", seed=SEED)
+    paged = E.QwenB200(cfg, dict(maxCtx=64)).build("synthetic", seed=SEED)
+    ps = prompts(2, cfg["vocabSize"], [40, 30])
+    dense.seqInit(2, 64)
+    paged.seqInitPaged(2, 64, 4)
+    for sl, p in enumerate(ps):
+        dense.seqSetPrompt(sl, p)
+        paged.seqSetPrompt(sl, p)
+    paged.seqPrefill(1)  # 29 positions: 2 pages
+    dense.seqPrefill(1)
+    assert paged.seqPages() == (2, 4)
+    with pytest.raises(E.EmberglassError, match="out of KV pages"):
+        paged.seqPrefill(0)  # 39 positions need 3 pages, 2 are free
+    assert paged.seqPages() == (2, 4) and paged.seqState(0)[0] == 0
+    paged.seqRelease(1)
+    paged.seqPrefill(0)
+    dense.seqPrefill(0)
+    a = dense.batchDecode([0], 6)
+    b = paged.batchDecode([0], 6)
+    assert np.array_equal(a, b)
+    assert np.array_equal(dense.batchLogits(0), paged.batchLogits(0))
+
+
 @pytest.mark.parametrize("f16", [True, False])
 def test_chunked_prefill_single_stream(cuda, f16):
     """prefillBatch runs positions 0..T-2 as batched chunks of 16 (K/V rows

@@ -98,6 +98,9 @@ _SIGS = {
     "eg_batch_read_logits": (i32, [vp, i32, vp]),
     "eg_launches_per_step": (i32, [vp]),
     "eg_op_gemv_q4": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, i32, vp]),
+    "eg_op_q4_stream_bytes": (i32, [i32, i32, i32, C.POINTER(u64)]),
+    "eg_op_q4_to_stream": (i32, [vp, vp, i32, i32, i32, vp, vp]),
+    "eg_op_gemv_q4_stream": (i32, [vp, vp, vp, i32, i32, vp, vp, i32, vp]),
     "eg_op_gate_up_silu": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "eg_op_gemv_q8": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "eg_op_rmsnorm": (i32, [vp, vp, i32, f32, i32, vp, vp]),

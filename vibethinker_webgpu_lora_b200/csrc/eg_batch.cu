@@ -571,7 +571,8 @@ void kv_append_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStrea
 
 void attn_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st, bool pdl) {
   const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
-  const dim3 grid(std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys), a.nh, lanes);
+  const dim3 grid(std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys),
+                  attn_items_per_chunk(a.nh, a.nkv), lanes);
   if (a.kv_f16)
     blaunch(attn_batch_kernel<__half>, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, b, (int)pdl);
   else

@@ -474,8 +474,9 @@ void lora_a(const XSrc& x, int K, const LoraMod* mods, int nmods, int max_rank, 
 }
 
 // ======================================================================
-// Decode attention (attn_head_item, eg_stream.cuh): grid (splits, heads)
+// Decode attention (attn_head_item, eg_stream.cuh): grid (chunks, KV head x head subset)
 // ======================================================================
+static_assert(kAttnDefaultChunk == kAttnKeys, "one default chunk");
 int attn_max_splits(int max_ctx) { return std::max(64, (max_ctx + 15) / 16); }
 
 template <typename KVT>
@@ -485,10 +486,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_head_kernel(AttnArgs a, 
 }
 
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  // splits of kAttnKeys keys (a fixed chunk, when given, for tests of the
-  // multi-split merge); the partial slots (max_splits per head) cover them
+  // chunks of kAttnKeys keys (a smaller fixed chunk, when given, for tests
+  // of the multi-chunk merge) x items per chunk; the partial slots
+  // (max_splits per head) cover the chunks
   const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
-  dim3 grid(std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys), a.nh);
+  dim3 grid(std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys), attn_items_per_chunk(a.nh, a.nkv));
   if (a.kv_f16)
     launch(attn_head_kernel<__half>, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, (int)pdl);
   else

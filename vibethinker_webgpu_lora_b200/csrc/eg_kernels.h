@@ -112,10 +112,10 @@ struct AttnArgs {
   int nh, nkv, max_splits;
   int ctx_bound;     // upper bound of pos + 1 for this launch (sizes the grid)
   int kv_f16;        // 1: f16 cache + ATTN_*_F16 / ROPE_QK_F16 numerics
-  int chunk;         // 0: adaptive; >0 fixed keys per split
+  int chunk;         // keys per split: 0 = 128 (the reference's CHUNK); else 16..128, % 16 == 0
   float *pm, *pz, *po;  // partials [nh][max_splits], po [nh][max_splits][128]
   float* out;        // attention output [nh*128]
-  unsigned* counters;  // [nkv] split-arrival counters, zero between launches
+  unsigned* counters;  // [nh] split-arrival counters (one per item's first head), zero between launches
   // Paged cache (WRITE_KV_PAGE / ATTN_PARTIAL_PAGED, kernels.js:1657-1911):
   // row t lives at physical row pages[t / 16] * 16 + t % 16 of kc / vc;
   // null = contiguous rows.
@@ -126,6 +126,8 @@ struct AttnArgs {
   // appended here.
   int pos_off, appended;
 };
+// Keys per split when AttnArgs::chunk is 0 (the reference's CHUNK).
+constexpr int kAttnDefaultChunk = 128;
 int attn_max_splits(int max_ctx);
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
 

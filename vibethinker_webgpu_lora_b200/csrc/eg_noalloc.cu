@@ -56,8 +56,9 @@ eg_status scratch_for_current_device(void** out) {
 extern "C" {
 
 // Same inputs, outputs and results as eg_op_attn_decode; scratch comes from
-// the static array above.  Limits: nh * ceil((pos+1) / max(chunk, 16)) must
-// not exceed 4096 (the adaptive chunk is never below 16 keys), nh <= 64.
+// the static array above.  Limits: nh * ceil((pos+1) / keys) must not exceed
+// 4096, where keys = chunk, or 128 (the fixed default chunk) when chunk = 0;
+// nh <= 64.
 // Every call shares the one array: calls that overlap on the GPU (concurrent
 // streams, or several host threads on one device) race on it.  The first
 // call on a device resolves the array's device address; make that first call
@@ -70,11 +71,11 @@ EG_API eg_status eg_op_attn_decode_noalloc(const float* qkv, void* k_cache, void
     return eg::fail(EG_ERR_ARG, "attn_decode_noalloc: null argument");
   if (nh <= 0 || nh > 64 || nkv <= 0 || nh % nkv || nh / nkv > 8 || pos < 0 || pos >= max_ctx)
     return eg::fail(EG_ERR_ARG, "attn_decode_noalloc: bad heads/pos");
-  if (chunk < 0 || chunk > 64 || chunk % 16)
-    return eg::fail(EG_ERR_ARG, "attn_decode_noalloc: chunk must be 0 or 16/32/48/64");
+  if (chunk < 0 || chunk > eg::kAttnDefaultChunk || chunk % 16)
+    return eg::fail(EG_ERR_ARG, "attn_decode_noalloc: chunk must be 0 or a multiple of 16 up to 128");
   const int ctx = pos + 1;
-  const int min_chunk = chunk > 0 ? chunk : 16;
-  const int splits = (ctx + min_chunk - 1) / min_chunk;
+  const int keys = chunk > 0 ? chunk : eg::kAttnDefaultChunk;
+  const int splits = (ctx + keys - 1) / keys;
   if ((long long)nh * splits > kSlots)
     return eg::fail(EG_ERR_ARG,
                     "attn_decode_noalloc: %d heads x %d splits (pos %d, chunk %d) exceed the "

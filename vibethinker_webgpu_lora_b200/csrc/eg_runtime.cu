@@ -772,8 +772,8 @@ EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** 
   if (o.max_sampling_top_k <= 0 || o.max_sampling_top_k > 64) o.max_sampling_top_k = 64;
   if (o.sampling_top_k <= 0) o.sampling_top_k = 40;
   o.max_sampling_top_k = std::max(o.max_sampling_top_k, std::min(o.sampling_top_k, 64));
-  if (o.attn_chunk < 0 || o.attn_chunk > 64 || o.attn_chunk % 16)
-    return fail(EG_ERR_ARG, "attn_chunk must be 0 or a multiple of 16 up to 64");
+  if (o.attn_chunk < 0 || o.attn_chunk > 128 || o.attn_chunk % 16)
+    return fail(EG_ERR_ARG, "attn_chunk must be 0 or a multiple of 16 up to 128");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || o.device < 0 || o.device >= ndev)
     return fail(EG_ERR_CUDA, "no CUDA device %d", o.device);
@@ -1348,15 +1348,18 @@ static void release_pages(eg_rt* rt, int slot) {
 }
 
 // ensureBlocks: pages for positions [0, n_pos) of the slot; the table row is
-// uploaded when it grew.  Fails (nothing launched) when the pool is empty.
+// uploaded when it grew.  All or none: when the pool cannot cover the whole
+// request, the pages taken by this call go back to the pool, so the slot's
+// page list and its device table row always agree.  Fails (nothing
+// launched) when the pool is short.
 static eg_status ensure_pages(eg_rt* rt, int slot, int n_pos) {
   if (!rt->seq_pool_pages) return EG_OK;
   auto& hp = rt->h_pages[slot];
   const size_t need = (size_t)(n_pos + 15) / 16, had = hp.size();
+  if (need > had && need - had > rt->free_pages.size())
+    return fail(EG_ERR_OOM, "out of KV pages (%d in the pool, %zu free): slot %d needs %zu more",
+                rt->seq_pool_pages, rt->free_pages.size(), slot, need - had);
   while (hp.size() < need) {
-    if (rt->free_pages.empty())
-      return fail(EG_ERR_OOM, "out of KV pages (%d in the pool): slot %d needs %zu", rt->seq_pool_pages,
-                  slot, need);
     hp.push_back(rt->free_pages.back());
     rt->free_pages.pop_back();
   }
@@ -2050,6 +2053,44 @@ EG_API eg_status eg_op_gemv_q4(const float* x, const uint32_t* w, const float* s
   return EG_OK;
 }
 
+EG_API eg_status eg_op_q4_stream_bytes(int N, int K, int R, uint64_t* bytes) {
+  if (!bytes || N <= 0 || K <= 0 || K % 128 || K > 12288 || (R != 1 && R != 2))
+    return fail(EG_ERR_ARG, "q4_stream_bytes: need K %% 128 == 0, K <= 12288, R = 1 or 2");
+  *bytes = q4_stream_bytes(N, K, R);
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_q4_to_stream(const uint32_t* w, const float* scale, int N, int K, int R, void* out,
+                                    void* stream) {
+  if (!w || !scale || !out || N <= 0 || K <= 0 || K % 128 || K > 12288 || (R != 1 && R != 2))
+    return fail(EG_ERR_ARG, "q4_to_stream: bad argument");
+  if (reinterpret_cast<uintptr_t>(out) & 15) return fail(EG_ERR_ARG, "q4_to_stream: out must be 16-byte aligned");
+  q4_to_stream(w, scale, N, K, R, static_cast<unsigned char*>(out), OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_gemv_q4_stream(const float* x, const void* ws, const float* bias, int N, int K,
+                                      float* y, int* err, int pdl, void* stream) {
+  if (!x || !ws || !y || !err || N <= 0 || K <= 0 || K % 128 || K > 12288)
+    return fail(EG_ERR_ARG, "gemv_q4_stream: bad argument");
+  if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(EG_ERR_ARG, "gemv_q4_stream: ws must be 16-byte aligned");
+  XSrc xs = {};
+  xs.mode = X_PLAIN;
+  xs.x = x;
+  Epi e = {};
+  e.mode = EPI_STORE;
+  e.y = y;
+  e.bias = bias;
+  e.N = N;
+  e.split1 = e.split2 = N;
+  GemvWork wk;
+  wk.err = err;
+  gemv_q4(static_cast<const unsigned char*>(ws), N, K, xs, e, OPSTREAM, pdl != 0, wk);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
 EG_API eg_status eg_op_gate_up_silu(const float* x, const uint32_t* w, const float* scale, int N, int K,
                                     float* y, void* stream) {
   if (!x || !w || !scale || !y || N <= 0 || K <= 0 || K % 128 || K > 12288)
@@ -2112,7 +2153,8 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
   if (!qkv || !k_cache || !v_cache || !cos_t || !sin_t || !out) return fail(EG_ERR_ARG, "attn_decode: null argument");
   if (nh <= 0 || nh > 64 || nkv <= 0 || nh % nkv || nh / nkv > 8 || pos < 0 || pos >= max_ctx)
     return fail(EG_ERR_ARG, "attn_decode: bad heads/pos");
-  if (chunk < 0 || chunk > 64 || chunk % 16) return fail(EG_ERR_ARG, "attn_decode: chunk must be 0 or 16/32/48/64");
+  if (chunk < 0 || chunk > 128 || chunk % 16)
+    return fail(EG_ERR_ARG, "attn_decode: chunk must be 0 or a multiple of 16 up to 128");
   const int ms = attn_max_splits(max_ctx);
   void* scr = nullptr;
   const size_t part = (size_t)nh * ms * (128 + 2) * 4;

@@ -337,21 +337,39 @@ __device__ bool epilogue_q8_run(const float* s, float* y, int N, int t_lo, int t
 // ======================================================================
 // Decode attention item
 // ======================================================================
-// One (query head, split of <= kAttnKeys keys) on 512 threads (warps 0-15;
-// named barrier 1).  Each warp takes keys t0 + w, t0 + w + 16, ...; a lane
-// holds 4 of the 128 dims.  All K and V rows of the warp are requested
-// before griddepcontrol.wait (pdl; the cache rows t != pos were written by
-// earlier steps), so the item pays one memory latency for them.  Each warp
-// forms a partial (m, z, sum e^(s-m) v) over its keys (ATTN_PARTIAL,
-// kernels.js:258-345), the 16 warp partials are merged in shared memory with
-// the ATTN_COMBINE formula (kernels.js:346-388, f16 rounding of the partial
-// outputs in the f16 variant), and for contexts longer than one split the
-// split partials are merged once more by the last item of the head.  The
-// new k (RoPE) / v row of position pos is formed in registers; the first
-// query head of each KV group appends it to the cache (runtime.js:1509-1514).
+// One item = one KV head's chunk of <= kAttnKeys keys (the reference's
+// CHUNK = 128, runtime.js:330) for up to kAttnHq of the query heads that
+// share that KV head (GQA), on 512 threads (warps 0-15; named barrier 1).
+// Each K/V row is fetched once per item and used by all its query heads.
+// Each warp takes keys t0 + w, t0 + w + 16, ...; a lane holds 4 of the 128
+// dims.  All K and V rows of the warp are requested before
+// griddepcontrol.wait (pdl; the cache rows t != pos were written by earlier
+// steps), so the item pays one memory latency for them.
+//
+// The arithmetic is ATTN_PARTIAL(_F16) (kernels.js:258-345) over the whole
+// chunk: M = the chunk's max score, ev = exp(s - M), Z = sum ev,
+// po = sum ev * v, all f32; then ATTN_COMBINE(_F16) (kernels.js:346-388)
+// over the chunks: o = sum_s exp(pm_s - M) * po_s / sum_s pz_s exp(pm_s - M),
+// with po rounded through f16 once per chunk in the f16 variant -- the
+// rounding points of the reference, so the two differ only by f32
+// summation order.  A single-chunk context is combined in place; longer
+// contexts write (pm, pz, po) per chunk and the last item of the head set
+// merges them (__threadfence + arrival counter).  The new k (RoPE) / v row
+// of position pos is formed in registers; the first item of each KV group
+// appends it to the cache (runtime.js:1509-1514).
 constexpr int kAttnWarps = 16;
-constexpr int kAttnKeys = 256;  // keys per split (16 per warp)
+constexpr int kAttnKeys = 128;  // keys per chunk (runtime.js:330 CHUNK)
 constexpr int kAttnKpw = kAttnKeys / kAttnWarps;
+constexpr int kAttnHq = 4;      // query heads per item
+static_assert(kAttnHq * kHeadDim == kAttnWarps * 32, "one thread per (head, dim) in the merge");
+
+// Items per chunk: KV heads x ceil(G / kAttnHq) query-head subsets.
+__host__ __device__ __forceinline__ int attn_subsets(int nh, int nkv) {
+  return (nh / nkv + kAttnHq - 1) / kAttnHq;
+}
+__host__ __device__ __forceinline__ int attn_items_per_chunk(int nh, int nkv) {
+  return nkv * attn_subsets(nh, nkv);
+}
 
 // A value as the cache stores it (rounded to the cache type).
 template <typename KVT>
@@ -386,10 +404,10 @@ struct KvRow<float> {
   __device__ __forceinline__ void set(float4 v) { f = v; }
 };
 
-// Shared memory of one attention item (8.3 KB).
+// Shared memory of one attention item (33 KB).
 struct AttnSmem {
-  float wm[kAttnWarps], wz[kAttnWarps];
-  __align__(16) float wo[kAttnWarps][kHeadDim];
+  float wm[kAttnWarps][kAttnHq], wz[kAttnWarps][kAttnHq];
+  __align__(16) float wo[kAttnWarps][kAttnHq][kHeadDim];
   int last;
 };
 
@@ -421,14 +439,28 @@ __device__ __forceinline__ size_t kv_row(const uint32_t* pages, int t) {
   return pages ? (size_t)__ldg(pages + t / kKvPage) * kKvPage + (t % kKvPage) : (size_t)t;
 }
 
+__device__ __forceinline__ float dot4(float4 a, float4 b) {
+  float p = __fmul_rn(a.x, b.x);
+  p = __fadd_rn(p, __fmul_rn(a.y, b.y));
+  p = __fadd_rn(p, __fmul_rn(a.z, b.z));
+  return __fadd_rn(p, __fmul_rn(a.w, b.w));
+}
+__device__ __forceinline__ void axpy4(float4& acc, float w, float4 v) {
+  acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+  acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+  acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+  acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+}
+
+// item: KV head * attn_subsets + subset; split: the chunk index.
 template <typename KVT>
-__device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, AttnSmem& sm) {
-  float* wm = sm.wm;
-  float* wz = sm.wz;
-  float (*wo)[kHeadDim] = sm.wo;
+__device__ void attn_head_item(const AttnArgs& a, int item, int split, int pdl, AttnSmem& sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = a.nh / a.nkv, kvh = h / G, hd = kHeadDim;
-  const int kvd = a.nkv * hd;
+  const int G = a.nh / a.nkv, subs = attn_subsets(a.nh, a.nkv);
+  const int kvh = item / subs, sub = item % subs;
+  const int h0 = kvh * G + sub * kAttnHq;            // first query head of the item
+  const int nhq = min(kAttnHq, G - sub * kAttnHq);   // query heads of the item
+  const int hd = kHeadDim, kvd = a.nkv * hd;
   const int f16 = a.kv_f16;
   // The position and the cached rows t != pos were written before the
   // producing GEMV started (it triggers this launch only after its own
@@ -465,9 +497,13 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
     pdl_wait();
     pdl_launch_dependents();
   }
-  // q: ROPE_QK, read through f16 in the f16 variant (ATTN_PARTIAL_F16)
-  const float4 q4 = rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + h * hd + 4 * lane)),
-                               cj, sj, f16, f16 != 0);
+  // q of each head: ROPE_QK, read through f16 in the f16 variant (ATTN_PARTIAL_F16)
+  float4 q4[kAttnHq];
+#pragma unroll
+  for (int j = 0; j < kAttnHq; j++)
+    q4[j] = j < nhq ? rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + (h0 + j) * hd + 4 * lane)),
+                                 cj, sj, f16, f16 != 0)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
   if (!a.appended && pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v, as cached
     const float* kn = a.qkv + a.nh * hd + kvh * hd;
     const float* vn = a.qkv + a.nh * hd + kvd + kvh * hd;
@@ -486,120 +522,105 @@ __device__ void attn_head_item(const AttnArgs& a, int h, int split, int pdl, Att
           V[ii] = vn4;
         }
     }
-    if (h % G == 0 && warp == 0) {  // one query head per KV group appends
+    if (sub == 0 && warp == 0) {  // one item per KV group appends
       KVT* kw = reinterpret_cast<KVT*>(a.kc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane;
       KVT* vw = reinterpret_cast<KVT*>(a.vc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane;
       kw[0] = kv_cvt<KVT>(kx.x); kw[1] = kv_cvt<KVT>(kx.y); kw[2] = kv_cvt<KVT>(kx.z); kw[3] = kv_cvt<KVT>(kx.w);
       vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
     }
   }
-  // scores of this warp's keys: key i's score ends up in lane i
+  // ---- scores of this warp's keys: key i's score (per head) ends up in lane i
   const float scale = 1.0f / sqrtf((float)hd);
-  float s_mine = -1e30f;
-  float m = -1e30f;
-#pragma unroll
-  for (int i = 0; i < kAttnKpw; i++) {
-    const int t = t0 + warp + kAttnWarps * i;
-    if (t >= t1) break;
-    const float4 k4 = K[i].get();
-    float p = __fmul_rn(q4.x, k4.x);
-    p = __fadd_rn(p, __fmul_rn(q4.y, k4.y));
-    p = __fadd_rn(p, __fmul_rn(q4.z, k4.z));
-    p = __fadd_rn(p, __fmul_rn(q4.w, k4.w));
-    const float sv = __fmul_rn(warp_sum(p), scale);
-    if (lane == i) s_mine = sv;
-    m = fmaxf(m, sv);
-  }
   const int nk = t1 - t0 > warp ? (t1 - t0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
-  const float ev_mine = lane < nk ? expf(s_mine - m) : 0.f;
-  const float z = warp_sum(ev_mine);
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float s_mine[kAttnHq], m[kAttnHq];
+#pragma unroll
+  for (int j = 0; j < kAttnHq; j++) {
+    s_mine[j] = -1e30f;
+    m[j] = -1e30f;
+  }
 #pragma unroll
   for (int i = 0; i < kAttnKpw; i++) {
     if (i >= nk) break;
-    const float ev = __shfl_sync(0xffffffffu, ev_mine, i);
-    const float4 v4 = V[i].get();
-    acc.x = __fadd_rn(acc.x, __fmul_rn(ev, v4.x));
-    acc.y = __fadd_rn(acc.y, __fmul_rn(ev, v4.y));
-    acc.z = __fadd_rn(acc.z, __fmul_rn(ev, v4.z));
-    acc.w = __fadd_rn(acc.w, __fmul_rn(ev, v4.w));
-  }
-  if (f16) {  // ATTN_COMBINE_F16 reads the partial outputs through f16
-    round_h2(acc.x, acc.y);
-    round_h2(acc.z, acc.w);
+    const float4 k4 = K[i].get();
+#pragma unroll
+    for (int j = 0; j < kAttnHq; j++) {
+      const float sv = __fmul_rn(warp_sum(dot4(q4[j], k4)), scale);
+      if (lane == i) s_mine[j] = sv;
+      m[j] = fmaxf(m[j], sv);
+    }
   }
   if (lane == 0) {
-    wm[warp] = nk ? m : -1e30f;
-    wz[warp] = z;
+#pragma unroll
+    for (int j = 0; j < kAttnHq; j++) sm.wm[warp][j] = m[j];
   }
-  *reinterpret_cast<float4*>(&wo[warp][4 * lane]) = acc;
   bar_sync_n<kAttnWarps * 32>();
-  // ---- merge the warp partials: warp 0, lane l holds dims 4l..4l+3
-  if (warp == 0) {
+  // ---- the chunk's max per head, then ev = exp(s - M), Z and sum ev * v
+  float4 acc[kAttnHq];
+#pragma unroll
+  for (int j = 0; j < kAttnHq; j++) {
     float M = -1e30f;
-    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, wm[w]);
-    float Z = 0.f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int w = 0; w < kAttnWarps; w++) {
-      if (wz[w] == 0.f) continue;
-      const float wgt = expf(wm[w] - M);
-      Z = __fadd_rn(Z, __fmul_rn(wz[w], wgt));
-      const float4 p = *reinterpret_cast<const float4*>(&wo[w][4 * lane]);
-      o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
-      o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
-      o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
-      o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm.wm[w][j]);
+    const float ev_mine = lane < nk ? expf(s_mine[j] - M) : 0.f;
+    const float z = warp_sum(ev_mine);
+    if (lane == 0) sm.wz[warp][j] = z;
+    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kAttnKpw; i++) {
+      if (i >= nk) break;
+      axpy4(acc[j], __shfl_sync(0xffffffffu, ev_mine, i), V[i].get());
     }
-    if (nsplit == 1) {
-      const float invZ = 1.0f / Z;
-      *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
-          make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ), __fmul_rn(o.w, invZ));
-    } else {
-      if (f16) {
-        round_h2(o.x, o.y);
-        round_h2(o.z, o.w);
-      }
-      *reinterpret_cast<float4*>(a.po + ((size_t)h * a.max_splits + split) * hd + 4 * lane) = o;
-      if (lane == 0) {
-        a.pm[h * a.max_splits + split] = M;
-        a.pz[h * a.max_splits + split] = Z;
-      }
-    }
+    *reinterpret_cast<float4*>(&sm.wo[warp][j][4 * lane]) = acc[j];
   }
+  bar_sync_n<kAttnWarps * 32>();
+  // ---- one thread per (head j, dim d): the chunk's partial (pm, pz, po)
+  const int j = threadIdx.x / kHeadDim, d = threadIdx.x % kHeadDim;
+  float M = -1e30f, Z = 0.f, po = 0.f;
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; w++) {
+    M = fmaxf(M, sm.wm[w][j]);
+    Z = __fadd_rn(Z, sm.wz[w][j]);
+    po = __fadd_rn(po, sm.wo[w][j][d]);
+  }
+  if (f16) po = round_h(po);  // ATTN_COMBINE_F16 reads po through f16
+  const int h = h0 + j;
   if (nsplit == 1) {
+    // ATTN_COMBINE over one chunk: M' = pm, Z' = pz * exp(0), o = 1 * po / Z'
+    if (j < nhq) a.out[h * hd + d] = __fmul_rn(po, 1.0f / Z);
     bar_sync_n<kAttnWarps * 32>();  // the shared area may be reused by the caller
     return;
   }
-  // ---- several splits: the last item of the head merges them
+  if (j < nhq) {
+    a.po[((size_t)h * a.max_splits + split) * hd + d] = po;
+    if (d == 0) {
+      a.pm[h * a.max_splits + split] = M;
+      a.pz[h * a.max_splits + split] = Z;
+    }
+  }
+  // ---- several chunks: the last item of the head set merges them
   __threadfence();
   bar_sync_n<kAttnWarps * 32>();
-  if (threadIdx.x == 0) sm.last = atomicAdd(a.counters + h, 1u) == (unsigned)nsplit - 1;
+  if (threadIdx.x == 0) sm.last = atomicAdd(a.counters + h0, 1u) == (unsigned)nsplit - 1;
   bar_sync_n<kAttnWarps * 32>();
   const bool last = sm.last != 0;
   bar_sync_n<kAttnWarps * 32>();
-  if (last && warp == 0) {
-    __threadfence();
+  if (!last) return;
+  __threadfence();
+  if (j < nhq) {
     const float* pm = a.pm + h * a.max_splits;
     const float* pz = a.pz + h * a.max_splits;
-    float M = -1e30f;
-    for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(pm + s2));
-    float Z = 0.f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* pp = a.po + (size_t)h * a.max_splits * hd + d;
+    float Mg = -1e30f;
+    for (int s2 = 0; s2 < nsplit; s2++) Mg = fmaxf(Mg, __ldcg(pm + s2));
+    float Zg = 0.f, o = 0.f;
     for (int s2 = 0; s2 < nsplit; s2++) {
-      const float wgt = expf(__ldcg(pm + s2) - M);
-      Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), wgt));
-      const float4 p = __ldcg(reinterpret_cast<const float4*>(a.po + ((size_t)h * a.max_splits + s2) * hd + 4 * lane));
-      o.x = __fadd_rn(o.x, __fmul_rn(wgt, p.x));
-      o.y = __fadd_rn(o.y, __fmul_rn(wgt, p.y));
-      o.z = __fadd_rn(o.z, __fmul_rn(wgt, p.z));
-      o.w = __fadd_rn(o.w, __fmul_rn(wgt, p.w));
+      const float wgt = expf(__ldcg(pm + s2) - Mg);
+      Zg = __fadd_rn(Zg, __fmul_rn(__ldcg(pz + s2), wgt));
+      o = __fadd_rn(o, __fmul_rn(wgt, __ldcg(pp + (size_t)s2 * hd)));
     }
-    const float invZ = 1.0f / Z;
-    *reinterpret_cast<float4*>(a.out + h * hd + 4 * lane) =
-        make_float4(__fmul_rn(o.x, invZ), __fmul_rn(o.y, invZ), __fmul_rn(o.z, invZ),
-                    __fmul_rn(o.w, invZ));
-    if (lane == 0) a.counters[h] = 0u;  // ready for the next launch
+    a.out[h * hd + d] = __fmul_rn(o, 1.0f / Zg);
   }
+  if (threadIdx.x == 0) a.counters[h0] = 0u;  // ready for the next launch
 }
 
 }  // namespace eg

@@ -22,6 +22,27 @@ def gemv_q4(x, w, scale, N, K, y, bias=None, accumulate=False, group=128, stream
                                   L.ptr(y), int(accumulate), _st(stream)))
 
 
+def q4_stream_bytes(N, K, R=1):
+    """Bytes of the device stream layout of an int4 matrix (R = 2: [gate;up])."""
+    import ctypes as C
+    n = C.c_uint64(0)
+    L.check(L.lib().eg_op_q4_stream_bytes(N, K, R, C.byref(n)))
+    return int(n.value)
+
+
+def q4_to_stream(w, scale, N, K, out, R=1, stream=None):
+    """Write the stream layout of a reference-layout int4 matrix into `out`
+    (a uint8 device buffer of q4_stream_bytes(N, K, R) bytes), once."""
+    L.check(L.lib().eg_op_q4_to_stream(L.ptr(w), L.ptr(scale), N, K, R, L.ptr(out), _st(stream)))
+
+
+def gemv_q4_stream(x, ws, N, K, y, err, bias=None, pdl=False, stream=None):
+    """GEMV4 over a matrix already in the stream layout: no conversion, no
+    allocation.  err: int32 device word, zero before the call."""
+    L.check(L.lib().eg_op_gemv_q4_stream(L.ptr(x), L.ptr(ws), L.ptr(bias), N, K, L.ptr(y), L.ptr(err),
+                                         int(pdl), _st(stream)))
+
+
 def gate_up_silu(x, w, scale, N, K, y, stream=None):
     L.check(L.lib().eg_op_gate_up_silu(L.ptr(x), L.ptr(w), L.ptr(scale), N, K, L.ptr(y), _st(stream)))
 

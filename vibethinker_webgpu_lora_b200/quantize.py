@@ -34,3 +34,23 @@ def synth_normal(n: int, seed: int, std: float = 1.0, start: int = 0) -> np.ndar
     out = np.empty(n, np.float32)
     L.lib().eg_synth_normal(out.ctypes.data, n, seed, std, start)
     return out
+
+
+def _splitmix_at(seed: int, n: int) -> np.ndarray:
+    """Outputs 0..n-1 of the counter-form SplitMix64 stream starting at
+    `seed` (the synthetic-input generator of the model build)."""
+    with np.errstate(over="ignore"):
+        z = np.uint64(seed) + (np.arange(1, n + 1, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15))
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def synth_ids(n: int, seed: int, vocab: int) -> np.ndarray:
+    """n uniform token ids (SplitMix64 output mod vocab)."""
+    return (_splitmix_at(seed, n) % np.uint64(vocab)).astype(np.uint32)
+
+
+def synth_uniform(n: int, seed: int) -> np.ndarray:
+    """n uniforms in [0, 1) from the top 53 bits, rounded to f32."""
+    return ((_splitmix_at(seed, n) >> np.uint64(11)).astype(np.float64) * 2.0 ** -53).astype(np.float32)
