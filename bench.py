@@ -390,7 +390,9 @@ def run_ours(args, ws, rank, local):
                           "achieved_gbs": round(step_bytes * value / ws / 1e9, 1),
                           "frac": round(step_bytes * value / ws / 1e9 / hbm, 4),
                           "roofline_tok_s": round(hbm * 1e9 / step_bytes, 1),
-                          "profiled_step_us": round(step_us, 1)},
+                          "profiled_step_us": round(step_us, 1),
+                          "profiled_us_by_kernel": {k: round(statistics.median(p[k] for p in prof), 1)
+                                                    for k in prof[0]}},
         "e2e": {"value": round(e2e_tokens / e2e_s, 2), "unit": "tok/s",
                 "h2d_bytes_per_step": round(4 * N_PROMPT / e2e_tokens, 3),
                 "d2h_bytes_per_step": 4,

@@ -189,6 +189,15 @@ typedef struct {
   float scale;            /* MLX scale | alpha/r | 2.0 (lora_gpu.js:73-80,108) */
 } eg_lora_module;
 
+/* The orientation step of loadLoraAdapterGPU (lora_gpu.js:100-107), on the
+ * host: rank = the smallest of A's and B's dimensions; A is transposed to
+ * [rank][in_dim] unless it already has rank rows (PEFT lora_A [r][in] stays,
+ * MLX lora_a [in][r] turns), B likewise to [rank][out_dim] (PEFT lora_B
+ * [out][r] turns, MLX lora_b [r][out] stays).  A_out holds rank*in_dim
+ * floats, B_out rank*out_dim.  EG_ERR_ARG when the shapes do not fit. */
+EG_API eg_status eg_lora_orient(const float* A, int64_t a_rows, int64_t a_cols, const float* B,
+                               int64_t b_rows, int64_t b_cols, int64_t in_dim, int64_t out_dim,
+                               float* A_out, float* B_out, int* rank);
 /* loadLoraAdapterGPU: rank = smallest dim, A -> [r][in], B -> [r][out]
  * (lora_gpu.js:100-107); device copies owned by the adapter. */
 EG_API eg_status eg_lora_create(eg_rt* rt, int n, const eg_lora_module* mods, eg_lora** out);

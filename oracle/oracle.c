@@ -163,13 +163,23 @@ static inline float nib_at(uint32_t word, int j) { return (float)((int32_t)(word
 /* ------------------------------------------------------------------------ */
 /* GEMV4 / GEMV4_ADD, src/qwgpu/kernels.js:884-971.  Per word the eight
  * products are summed first, then scaled by the group scale (bk>>7). */
+/* Summation order of the reductions (GEMV row words, RMSNorm sum of
+ * squares, attention q.k dot and weighted-V sum): 0 = ascending (the order
+ * one WGSL thread walks them), 1 = descending.  Both are f32 restatements
+ * of the same sums; the second exists to measure how far two valid
+ * reduction orders of the reference part -- the numerical noise floor an
+ * independent implementation is held to. */
+static int g_sum_order = 0;
+ORC_API void orc_set_sum_order(int order) { g_sum_order = order; }
+
 static float gemv4_row(const float* x, const uint32_t* w, const float* scale, int n, int K,
                        int gpr) {
   const int K8 = K / 8;
   const uint32_t* rw = w + (int64_t)n * K8;
   const float* rs = scale + (int64_t)n * gpr;
   float acc = 0.0f;
-  for (int c = 0; c < K8; c++) {
+  for (int cc = 0; cc < K8; cc++) {
+    const int c = g_sum_order ? K8 - 1 - cc : cc;
     uint32_t word = rw[c];
     int bk = c * 8;
     float sc = rs[bk >> 7];
@@ -257,7 +267,10 @@ ORC_API void orc_lora_a(const float* x, const float* A, int K, int rank, float* 
 /* RMSNORM (kernels.js:128-144) and RMSNORM_F16 (kernels.js:145-166). */
 ORC_API void orc_rmsnorm(const float* x, const float* g, int K, float eps, int f16, float* y) {
   float s = 0.0f;
-  for (int k = 0; k < K; k++) s = s + x[k] * x[k];
+  for (int kk = 0; kk < K; kk++) {
+    const int k = g_sum_order ? K - 1 - kk : kk;
+    s = s + x[k] * x[k];
+  }
   /* inverseSqrt: WGSL leaves its rounding to the device; restated as an
    * IEEE f32 sqrt followed by an IEEE f32 divide. */
   float inv = 1.0f / sqrtf(s / (float)K + eps);
@@ -341,10 +354,10 @@ ORC_API void orc_attention(const float* q, const float* kc, const float* vc, int
       for (int t = t0; t < t1; t++) {
         const float* kr = kc + (int64_t)t * stride + kvh * hd;
         float dot = 0.0f;
-        if (!f16)
-          for (int d = 0; d < hd; d++) dot = dot + qh[d] * kr[d];
-        else
-          for (int d = 0; d < hd; d++) dot = dot + h16(qh[d]) * h16(kr[d]);
+        for (int dd = 0; dd < hd; dd++) {
+          const int d = g_sum_order ? hd - 1 - dd : dd;
+          dot = dot + (f16 ? h16(qh[d]) * h16(kr[d]) : qh[d] * kr[d]);
+        }
         sc[t - t0] = dot * scale;
         if (sc[t - t0] > M) M = sc[t - t0];
       }
@@ -356,7 +369,8 @@ ORC_API void orc_attention(const float* q, const float* kc, const float* vc, int
       }
       for (int d = 0; d < hd; d++) {
         float acc = 0.0f;
-        for (int t = t0; t < t1; t++) {
+        for (int tt = t0; tt < t1; tt++) {
+          const int t = g_sum_order ? t0 + t1 - 1 - tt : tt;
           float v = vc[(int64_t)t * stride + kvh * hd + d];
           acc = acc + sc[t - t0] * (f16 ? h16(v) : v);
         }

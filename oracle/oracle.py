@@ -70,6 +70,7 @@ def _declare(L):
         "orc_tensor_seed": (u64, [u64, i]),
         "orc_model_create": (vp, [C.POINTER(OrcCfg), i, i, u64, d]),
         "orc_model_set_chunk": (None, [vp, i]),
+        "orc_set_sum_order": (None, [i]),
         "orc_model_tensor": (vp, [vp, i, i]),
         "orc_model_lora_synth": (None, [vp, u64, i, f, d, d]),
         "orc_model_lora_clear": (None, [vp]),

@@ -75,6 +75,7 @@ _SIGS = {
     "eg_read_hidden": (i32, [vp, vp]),
     "eg_generate": (i32, [vp, vp, i32, i32, i32, f32, vp, vp]),
     "eg_lora_create": (i32, [vp, i32, vp, C.POINTER(vp)]),
+    "eg_lora_orient": (i32, [vp, i64, i64, vp, i64, i64, i64, i64, vp, vp, C.POINTER(i32)]),
     "eg_lora_destroy": (i32, [vp, vp]),
     "eg_lora_update": (i32, [vp, vp, C.c_char_p, vp, vp]),
     "eg_set_lora": (i32, [vp, vp]),

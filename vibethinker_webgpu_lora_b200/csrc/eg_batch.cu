@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_batch_kernel(AttnArgs a0
     a.pos_off = v;
     a.appended = 1;
   }
-  attn_head_item<KVT>(a, blockIdx.y, blockIdx.x, pdl, sm);
+  attn_run<KVT>(a, blockIdx.x, gridDim.x, pdl, sm);
 }
 
 // One warp per (lane, KV head): RoPE(k) and v of position pos + lane into
@@ -570,9 +570,7 @@ void kv_append_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStrea
 }
 
 void attn_batch(const AttnArgs& a, const AttnBatch& b, int lanes, cudaStream_t st, bool pdl) {
-  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
-  const dim3 grid(std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys),
-                  attn_items_per_chunk(a.nh, a.nkv), lanes);
+  const dim3 grid(attn_ctas(a, lanes), 1, lanes);
   if (a.kv_f16)
     blaunch(attn_batch_kernel<__half>, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, b, (int)pdl);
   else

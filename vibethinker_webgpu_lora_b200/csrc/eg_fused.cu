@@ -315,11 +315,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         at.po = a.po;
         at.out = a.attn;
         at.counters = a.attn_counters;
-        const int keys = a.attn_chunk > 0 ? a.attn_chunk : kAttnKeys;
-        const int ipc = attn_items_per_chunk(a.nh, a.nkv);
-        const int items = (pos + keys) / keys * ipc;
-        for (int it = blockIdx.x; it < items; it += gridDim.x)
-          attn_head_item<KVT>(at, it % ipc, it / ipc, 0, asm_);
+        attn_run<KVT>(at, blockIdx.x, gridDim.x, 0, asm_);
       }
       if (!phase_barrier(a, epoch, &epi_done, pdone, false, &s_ok, tok == 0 ? pb + 1 : -1)) return;
       // ---- O projection + residual

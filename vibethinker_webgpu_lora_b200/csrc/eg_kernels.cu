@@ -474,23 +474,29 @@ void lora_a(const XSrc& x, int K, const LoraMod* mods, int nmods, int max_rank, 
 }
 
 // ======================================================================
-// Decode attention (attn_head_item, eg_stream.cuh): grid (chunks, KV head x head subset)
+// Decode attention (attn_run, eg_stream.cuh): a 1-D grid of CTAs that take
+// the (KV head, head subset, chunk) items of the current context
 // ======================================================================
 static_assert(kAttnDefaultChunk == kAttnKeys, "one default chunk");
 int attn_max_splits(int max_ctx) { return std::max(64, (max_ctx + 15) / 16); }
 
+// CTAs of one attention launch: enough for one item per query head and
+// chunk at ctx_bound, at most one per SM (512 threads x 111-128 registers).
+int attn_ctas(const AttnArgs& a, int lanes) {
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  const int chunks = std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys);
+  const int cap = std::max(1, sm_count() / std::max(1, lanes));
+  return std::max(1, std::min(cap, a.nh * chunks));
+}
+
 template <typename KVT>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_head_kernel(AttnArgs a, int pdl) {
   __shared__ AttnSmem sm;
-  attn_head_item<KVT>(a, blockIdx.y, blockIdx.x, pdl, sm);
+  attn_run<KVT>(a, blockIdx.x, gridDim.x, pdl, sm);
 }
 
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  // chunks of kAttnKeys keys (a smaller fixed chunk, when given, for tests
-  // of the multi-chunk merge) x items per chunk; the partial slots
-  // (max_splits per head) cover the chunks
-  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
-  dim3 grid(std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys), attn_items_per_chunk(a.nh, a.nkv));
+  const dim3 grid(attn_ctas(a, 1));
   if (a.kv_f16)
     launch(attn_head_kernel<__half>, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, (int)pdl);
   else

@@ -129,6 +129,7 @@ struct AttnArgs {
 // Keys per split when AttnArgs::chunk is 0 (the reference's CHUNK).
 constexpr int kAttnDefaultChunk = 128;
 int attn_max_splits(int max_ctx);
+int attn_ctas(const AttnArgs& a, int lanes);
 void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
 
 // y[r] += A[r] . x for up to 3 modules (LORA_A, kernels.js:60-78); x from src.

@@ -1853,6 +1853,28 @@ EG_API eg_status eg_generate(eg_rt* rt, const uint32_t* prompt, int n_prompt, in
 }
 
 // ---------------------------------------------------------------- LoRA
+EG_API eg_status eg_lora_orient(const float* A, int64_t a_rows, int64_t a_cols, const float* B,
+                               int64_t b_rows, int64_t b_cols, int64_t in_dim, int64_t out_dim,
+                               float* A_out, float* B_out, int* rank) {
+  if (!A || !B || !A_out || !B_out || !rank) return fail(EG_ERR_ARG, "lora_orient: null argument");
+  // rank = the smallest dimension (lora_gpu.js:101); A -> [r][in] unless it
+  // already has r rows, B -> [r][out] likewise (lora_gpu.js:102-107)
+  const int64_t r = std::min(std::min(a_rows, a_cols), std::min(b_rows, b_cols));
+  if (r <= 0) return fail(EG_ERR_ARG, "lora_orient: empty A or B");
+  const bool a_t = a_rows != r, b_t = b_rows != r;
+  const int64_t a_in = a_t ? a_rows : a_cols, b_out = b_t ? b_rows : b_cols;
+  if (a_in != in_dim || b_out != out_dim)
+    return fail(EG_ERR_ARG, "lora_orient: A %lldx%lld / B %lldx%lld do not give [%lld][%lld] / [%lld][%lld]",
+                (long long)a_rows, (long long)a_cols, (long long)b_rows, (long long)b_cols, (long long)r,
+                (long long)in_dim, (long long)r, (long long)out_dim);
+  for (int64_t i = 0; i < r; i++)
+    for (int64_t k = 0; k < in_dim; k++) A_out[i * in_dim + k] = a_t ? A[k * r + i] : A[i * in_dim + k];
+  for (int64_t i = 0; i < r; i++)
+    for (int64_t j = 0; j < out_dim; j++) B_out[i * out_dim + j] = b_t ? B[j * r + i] : B[i * out_dim + j];
+  *rank = (int)r;
+  return EG_OK;
+}
+
 EG_API eg_status eg_lora_create(eg_rt* rt, int n, const eg_lora_module* mods, eg_lora** out) {
   if (!rt || !out || (n > 0 && !mods)) return fail(EG_ERR_ARG, "eg_lora_create: null argument");
   *out = nullptr;
@@ -1877,17 +1899,12 @@ EG_API eg_status eg_lora_create(eg_rt* rt, int n, const eg_lora_module* mods, eg
     const int64_t r = std::min(std::min(md.a_rows, md.a_cols), std::min(md.b_rows, md.b_cols));
     if (r <= 0 || r > kMaxRank)
       return bail(fail(EG_ERR_ARG, "%s: rank %lld outside [1, %d]", md.key, (long long)r, kMaxRank));
-    // A -> [r][in], B -> [r][out] (lora_gpu.js:100-107)
-    const bool a_t = md.a_rows != r, b_t = md.b_rows != r;
-    const int64_t a_in = a_t ? md.a_rows : md.a_cols, b_out = b_t ? md.b_rows : md.b_cols;
-    if (a_in != K || b_out != N)
+    std::vector<float> A((size_t)r * K), B((size_t)r * N);
+    int rr = 0;
+    if (eg_lora_orient(md.A, md.a_rows, md.a_cols, md.B, md.b_rows, md.b_cols, K, N, A.data(), B.data(),
+                       &rr) != EG_OK)
       return bail(fail(EG_ERR_ARG, "%s: A/B shapes do not match the %lldx%lld projection", md.key,
                        (long long)N, (long long)K));
-    std::vector<float> A((size_t)r * K), B((size_t)r * N);
-    for (int64_t i = 0; i < r; i++)
-      for (int64_t k = 0; k < K; k++) A[i * K + k] = a_t ? md.A[k * r + i] : md.A[i * K + k];
-    for (int64_t i = 0; i < r; i++)
-      for (int64_t j = 0; j < N; j++) B[i * N + j] = b_t ? md.B[j * r + i] : md.B[i * N + j];
     float *dA = nullptr, *dB = nullptr;
     if (cudaMalloc(&dA, A.size() * 4) != cudaSuccess || cudaMalloc(&dB, B.size() * 4) != cudaSuccess) {
       if (dA) cudaFree(dA);

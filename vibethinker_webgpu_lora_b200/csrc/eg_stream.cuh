@@ -335,16 +335,20 @@ __device__ bool epilogue_q8_run(const float* s, float* y, int N, int t_lo, int t
 }
 
 // ======================================================================
-// Decode attention item
+// Decode attention
 // ======================================================================
-// One item = one KV head's chunk of <= kAttnKeys keys (the reference's
-// CHUNK = 128, runtime.js:330) for up to kAttnHq of the query heads that
-// share that KV head (GQA), on 512 threads (warps 0-15; named barrier 1).
-// Each K/V row is fetched once per item and used by all its query heads.
+// Work item = one KV head's chunk of <= kAttnKeys keys (the reference's
+// CHUNK = 128, runtime.js:330) for `hq` of the query heads that share that
+// KV head (GQA), on 512 threads (warps 0-15; named barrier 1).  Each K/V row
+// is fetched once per item and used by all its query heads.  hq (1, 2 or 4)
+// is chosen on the device from the current context: the fewest heads per
+// item such that all items fit the launched CTAs (short contexts spread the
+// heads over many CTAs, long contexts share each K/V row among 4 heads);
+// CTAs loop over the items when even hq = 4 leaves more items than CTAs.
 // Each warp takes keys t0 + w, t0 + w + 16, ...; a lane holds 4 of the 128
 // dims.  All K and V rows of the warp are requested before
 // griddepcontrol.wait (pdl; the cache rows t != pos were written by earlier
-// steps), so the item pays one memory latency for them.
+// steps), so an item pays one memory latency for them.
 //
 // The arithmetic is ATTN_PARTIAL(_F16) (kernels.js:258-345) over the whole
 // chunk: M = the chunk's max score, ev = exp(s - M), Z = sum ev,
@@ -354,21 +358,23 @@ __device__ bool epilogue_q8_run(const float* s, float* y, int N, int t_lo, int t
 // rounding points of the reference, so the two differ only by f32
 // summation order.  A single-chunk context is combined in place; longer
 // contexts write (pm, pz, po) per chunk and the last item of the head set
-// merges them (__threadfence + arrival counter).  The new k (RoPE) / v row
-// of position pos is formed in registers; the first item of each KV group
-// appends it to the cache (runtime.js:1509-1514).
+// merges them with all 512 threads (__threadfence + arrival counter).  The
+// new k (RoPE) / v row of position pos is formed in registers; the first
+// item of each KV group appends it to the cache (runtime.js:1509-1514).
 constexpr int kAttnWarps = 16;
 constexpr int kAttnKeys = 128;  // keys per chunk (runtime.js:330 CHUNK)
 constexpr int kAttnKpw = kAttnKeys / kAttnWarps;
-constexpr int kAttnHq = 4;      // query heads per item
+constexpr int kAttnHq = 4;      // most query heads per item
 static_assert(kAttnHq * kHeadDim == kAttnWarps * 32, "one thread per (head, dim) in the merge");
 
-// Items per chunk: KV heads x ceil(G / kAttnHq) query-head subsets.
-__host__ __device__ __forceinline__ int attn_subsets(int nh, int nkv) {
-  return (nh / nkv + kAttnHq - 1) / kAttnHq;
-}
-__host__ __device__ __forceinline__ int attn_items_per_chunk(int nh, int nkv) {
-  return nkv * attn_subsets(nh, nkv);
+// Heads per item for a context of nsplit chunks on ncta CTAs, and the item
+// count.  Every item of a launch uses the same hq (the arrival counters are
+// per item's first head).
+__host__ __device__ __forceinline__ int attn_hq(int nh, int nkv, int nsplit, int ncta) {
+  const int G = nh / nkv;
+  for (int hq = 1; hq < kAttnHq; hq *= 2)
+    if (nkv * ((G + hq - 1) / hq) * nsplit <= ncta) return hq;
+  return kAttnHq;
 }
 
 // A value as the cache stores it (rounded to the cache type).
@@ -404,10 +410,11 @@ struct KvRow<float> {
   __device__ __forceinline__ void set(float4 v) { f = v; }
 };
 
-// Shared memory of one attention item (33 KB).
+// Shared memory of the attention (33 KB).
 struct AttnSmem {
   float wm[kAttnWarps][kAttnHq], wz[kAttnWarps][kAttnHq];
   __align__(16) float wo[kAttnWarps][kAttnHq][kHeadDim];
+  float mz[kAttnHq][2];  // merge: global max and sum per head
   int last;
 };
 
@@ -439,12 +446,6 @@ __device__ __forceinline__ size_t kv_row(const uint32_t* pages, int t) {
   return pages ? (size_t)__ldg(pages + t / kKvPage) * kKvPage + (t % kKvPage) : (size_t)t;
 }
 
-__device__ __forceinline__ float dot4(float4 a, float4 b) {
-  float p = __fmul_rn(a.x, b.x);
-  p = __fadd_rn(p, __fmul_rn(a.y, b.y));
-  p = __fadd_rn(p, __fmul_rn(a.z, b.z));
-  return __fadd_rn(p, __fmul_rn(a.w, b.w));
-}
 __device__ __forceinline__ void axpy4(float4& acc, float w, float4 v) {
   acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
   acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
@@ -452,24 +453,63 @@ __device__ __forceinline__ void axpy4(float4& acc, float w, float4 v) {
   acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
 }
 
-// item: KV head * attn_subsets + subset; split: the chunk index.
-template <typename KVT>
-__device__ void attn_head_item(const AttnArgs& a, int item, int split, int pdl, AttnSmem& sm) {
+// The merge of nsplit chunk partials of the head set [h0, h0 + hq) by one
+// CTA (ATTN_COMBINE(_F16), kernels.js:346-388): per head the global max and
+// the weighted sum of the split sums (one warp per head), then the weighted
+// po sums with thread (head, dim quad, split phase) summing every P-th split
+// as float4s and the phases added in shared memory.
+__device__ __forceinline__ void attn_merge(const AttnArgs& a, int h0, int hq, int nsplit, AttnSmem& sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = a.nh / a.nkv, subs = attn_subsets(a.nh, a.nkv);
-  const int kvh = item / subs, sub = item % subs;
-  const int h0 = kvh * G + sub * kAttnHq;            // first query head of the item
-  const int nhq = min(kAttnHq, G - sub * kAttnHq);   // query heads of the item
+  const int hd = kHeadDim;
+  if (warp < hq) {
+    const float* pm = a.pm + (h0 + warp) * a.max_splits;
+    const float* pz = a.pz + (h0 + warp) * a.max_splits;
+    float M = -1e30f;
+    for (int s2 = lane; s2 < nsplit; s2 += 32) M = fmaxf(M, __ldcg(pm + s2));
+    M = warp_max(M);
+    float Z = 0.f;
+    for (int s2 = lane; s2 < nsplit; s2 += 32)
+      Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), expf(__ldcg(pm + s2) - M)));
+    Z = warp_sum(Z);
+    if (lane == 0) {
+      sm.mz[warp][0] = M;
+      sm.mz[warp][1] = Z;
+    }
+  }
+  bar_sync_n<kAttnWarps * 32>();
+  // thread = (phase p, head j, dim quad q): P = 16 / hq phases
+  const int P = kAttnHq * kAttnWarps / (4 * hq);  // 16 / hq
+  const int q = threadIdx.x & 31, j = (threadIdx.x >> 5) % hq, p = (threadIdx.x >> 5) / hq;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (p < P) {
+    const int h = h0 + j;
+    const float M = sm.mz[j][0];
+    const float* pm = a.pm + h * a.max_splits;
+    const float4* pp = reinterpret_cast<const float4*>(a.po + (size_t)h * a.max_splits * hd) + q;
+#pragma unroll 4
+    for (int s2 = p; s2 < nsplit; s2 += P) axpy4(o, expf(__ldcg(pm + s2) - M), __ldcg(pp + (size_t)s2 * (hd / 4)));
+  }
+  // phases -> shared memory (wo reused: [phase][head][dim] as 16 x 4 x 128)
+  float* red = &sm.wo[0][0][0];
+  if (p < P) *reinterpret_cast<float4*>(red + ((size_t)p * hq + j) * hd + 4 * q) = o;
+  bar_sync_n<kAttnWarps * 32>();
+  const int jj = threadIdx.x / hd, d = threadIdx.x % hd;
+  if (jj < hq) {
+    float v = 0.f;
+    for (int pp2 = 0; pp2 < P; pp2++) v = __fadd_rn(v, red[((size_t)pp2 * hq + jj) * hd + d]);
+    a.out[(h0 + jj) * hd + d] = __fmul_rn(v, 1.0f / sm.mz[jj][1]);
+  }
+}
+
+// One item: KV head kvh, heads [h0, h0 + nhq), chunk `split` of nsplit.
+template <typename KVT>
+__device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split, int nsplit,
+                          int pos, bool append, int pdl, AttnSmem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hd = kHeadDim, kvd = a.nkv * hd;
   const int f16 = a.kv_f16;
-  // The position and the cached rows t != pos were written before the
-  // producing GEMV started (it triggers this launch only after its own
-  // griddepcontrol.wait).
-  const int pos = (a.pos ? __ldcg(a.pos) : a.fixed_pos) + a.pos_off;
   const int ctx = pos + 1;
   const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
-  const int nsplit = (ctx + keys - 1) / keys;
-  if (split >= nsplit) return;
   const int t0 = split * keys, t1 = min(t0 + keys, ctx);
   const KVT* kc = reinterpret_cast<const KVT*>(a.kc) + kvh * hd + 4 * lane;
   const KVT* vc = reinterpret_cast<const KVT*>(a.vc) + kvh * hd + 4 * lane;
@@ -522,78 +562,103 @@ __device__ void attn_head_item(const AttnArgs& a, int item, int split, int pdl, 
           V[ii] = vn4;
         }
     }
-    if (sub == 0 && warp == 0) {  // one item per KV group appends
+    if (append && warp == 0) {  // one item per KV group appends
       KVT* kw = reinterpret_cast<KVT*>(a.kc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane;
       KVT* vw = reinterpret_cast<KVT*>(a.vc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane;
       kw[0] = kv_cvt<KVT>(kx.x); kw[1] = kv_cvt<KVT>(kx.y); kw[2] = kv_cvt<KVT>(kx.z); kw[3] = kv_cvt<KVT>(kx.w);
       vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
     }
   }
-  // ---- scores of this warp's keys: key i's score (per head) ends up in lane i
+  // ---- scores: lane L holds the 4 dims 4L..4L+3 of q (4 heads) and of the
+  // warp's 8 keys; the 32 partial dots (key i, head j) at slot v = 4i + j are
+  // summed over the warp by a transposing butterfly (each round halves the
+  // slots a lane keeps), after which lane L holds the whole dot of slot L.
   const float scale = 1.0f / sqrtf((float)hd);
   const int nk = t1 - t0 > warp ? (t1 - t0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
-  float s_mine[kAttnHq], m[kAttnHq];
-#pragma unroll
-  for (int j = 0; j < kAttnHq; j++) {
-    s_mine[j] = -1e30f;
-    m[j] = -1e30f;
-  }
+  float pd[kAttnKpw * kAttnHq];
 #pragma unroll
   for (int i = 0; i < kAttnKpw; i++) {
-    if (i >= nk) break;
     const float4 k4 = K[i].get();
 #pragma unroll
     for (int j = 0; j < kAttnHq; j++) {
-      const float sv = __fmul_rn(warp_sum(dot4(q4[j], k4)), scale);
-      if (lane == i) s_mine[j] = sv;
-      m[j] = fmaxf(m[j], sv);
+      float p = __fmul_rn(q4[j].x, k4.x);
+      p = fmaf(q4[j].y, k4.y, p);
+      p = fmaf(q4[j].z, k4.z, p);
+      pd[4 * i + j] = fmaf(q4[j].w, k4.w, p);
     }
   }
-  if (lane == 0) {
 #pragma unroll
-    for (int j = 0; j < kAttnHq; j++) sm.wm[warp][j] = m[j];
+  for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int k = 0; k < n / 2; k++) {
+      const float send = up ? pd[k] : pd[k + n / 2];
+      const float keep = up ? pd[k + n / 2] : pd[k];
+      pd[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
   }
+  const int ki = lane >> 2, hj = lane & 3;  // this lane's (key, head) slot
+  const bool valid = ki < nk && hj < nhq;
+  const float sv = valid ? __fmul_rn(pd[0], scale) : -1e30f;
+  float m = sv;  // the warp's max per head: lanes with the same hj
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+  if (lane < kAttnHq) sm.wm[warp][lane] = m;
   bar_sync_n<kAttnWarps * 32>();
   // ---- the chunk's max per head, then ev = exp(s - M), Z and sum ev * v
+  float M = -1e30f;
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm.wm[w][hj]);
+  const float ev = valid ? expf(sv - M) : 0.f;
+  float z = ev + __shfl_xor_sync(0xffffffffu, ev, 4);
+  z += __shfl_xor_sync(0xffffffffu, z, 8);
+  z += __shfl_xor_sync(0xffffffffu, z, 16);
+  if (lane < kAttnHq) sm.wz[warp][lane] = z;
   float4 acc[kAttnHq];
 #pragma unroll
-  for (int j = 0; j < kAttnHq; j++) {
-    float M = -1e30f;
+  for (int jj = 0; jj < kAttnHq; jj++) acc[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm.wm[w][j]);
-    const float ev_mine = lane < nk ? expf(s_mine[j] - M) : 0.f;
-    const float z = warp_sum(ev_mine);
-    if (lane == 0) sm.wz[warp][j] = z;
-    acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < kAttnKpw; i++) {
+    if (i >= nk) break;
+    const float4 v4 = V[i].get();
 #pragma unroll
-    for (int i = 0; i < kAttnKpw; i++) {
-      if (i >= nk) break;
-      axpy4(acc[j], __shfl_sync(0xffffffffu, ev_mine, i), V[i].get());
+    for (int jj = 0; jj < kAttnHq; jj++) {
+      if (jj >= nhq) break;
+      const float e = __shfl_sync(0xffffffffu, ev, 4 * i + jj);
+      acc[jj].x = fmaf(e, v4.x, acc[jj].x);
+      acc[jj].y = fmaf(e, v4.y, acc[jj].y);
+      acc[jj].z = fmaf(e, v4.z, acc[jj].z);
+      acc[jj].w = fmaf(e, v4.w, acc[jj].w);
     }
-    *reinterpret_cast<float4*>(&sm.wo[warp][j][4 * lane]) = acc[j];
   }
+#pragma unroll
+  for (int jj = 0; jj < kAttnHq; jj++)
+    if (jj < nhq) *reinterpret_cast<float4*>(&sm.wo[warp][jj][4 * lane]) = acc[jj];
   bar_sync_n<kAttnWarps * 32>();
   // ---- one thread per (head j, dim d): the chunk's partial (pm, pz, po)
   const int j = threadIdx.x / kHeadDim, d = threadIdx.x % kHeadDim;
-  float M = -1e30f, Z = 0.f, po = 0.f;
+  float Mc = -1e30f, Z = 0.f, po = 0.f;
+  if (j < nhq) {
 #pragma unroll
-  for (int w = 0; w < kAttnWarps; w++) {
-    M = fmaxf(M, sm.wm[w][j]);
-    Z = __fadd_rn(Z, sm.wz[w][j]);
-    po = __fadd_rn(po, sm.wo[w][j][d]);
+    for (int w = 0; w < kAttnWarps; w++) {
+      Mc = fmaxf(Mc, sm.wm[w][j]);
+      Z = __fadd_rn(Z, sm.wz[w][j]);
+      po = __fadd_rn(po, sm.wo[w][j][d]);
+    }
+    if (f16) po = round_h(po);  // ATTN_COMBINE_F16 reads po through f16
   }
-  if (f16) po = round_h(po);  // ATTN_COMBINE_F16 reads po through f16
   const int h = h0 + j;
   if (nsplit == 1) {
     // ATTN_COMBINE over one chunk: M' = pm, Z' = pz * exp(0), o = 1 * po / Z'
     if (j < nhq) a.out[h * hd + d] = __fmul_rn(po, 1.0f / Z);
-    bar_sync_n<kAttnWarps * 32>();  // the shared area may be reused by the caller
+    bar_sync_n<kAttnWarps * 32>();  // the shared area is reused by the next item
     return;
   }
   if (j < nhq) {
     a.po[((size_t)h * a.max_splits + split) * hd + d] = po;
     if (d == 0) {
-      a.pm[h * a.max_splits + split] = M;
+      a.pm[h * a.max_splits + split] = Mc;
       a.pz[h * a.max_splits + split] = Z;
     }
   }
@@ -603,24 +668,39 @@ __device__ void attn_head_item(const AttnArgs& a, int item, int split, int pdl, 
   if (threadIdx.x == 0) sm.last = atomicAdd(a.counters + h0, 1u) == (unsigned)nsplit - 1;
   bar_sync_n<kAttnWarps * 32>();
   const bool last = sm.last != 0;
-  bar_sync_n<kAttnWarps * 32>();
-  if (!last) return;
-  __threadfence();
-  if (j < nhq) {
-    const float* pm = a.pm + h * a.max_splits;
-    const float* pz = a.pz + h * a.max_splits;
-    const float* pp = a.po + (size_t)h * a.max_splits * hd + d;
-    float Mg = -1e30f;
-    for (int s2 = 0; s2 < nsplit; s2++) Mg = fmaxf(Mg, __ldcg(pm + s2));
-    float Zg = 0.f, o = 0.f;
-    for (int s2 = 0; s2 < nsplit; s2++) {
-      const float wgt = expf(__ldcg(pm + s2) - Mg);
-      Zg = __fadd_rn(Zg, __fmul_rn(__ldcg(pz + s2), wgt));
-      o = __fadd_rn(o, __fmul_rn(wgt, __ldcg(pp + (size_t)s2 * hd)));
-    }
-    a.out[h * hd + d] = __fmul_rn(o, 1.0f / Zg);
+  if (last) {
+    __threadfence();
+    attn_merge(a, h0, nhq, nsplit, sm);
+    if (threadIdx.x == 0) a.counters[h0] = 0u;  // ready for the next launch
   }
-  if (threadIdx.x == 0) a.counters[h0] = 0u;  // ready for the next launch
+  bar_sync_n<kAttnWarps * 32>();  // the shared area is reused by the next item
+}
+
+// All items of one attention launch, taken by CTA `cta` of `ncta`.
+template <typename KVT>
+__device__ void attn_run(const AttnArgs& a, int cta, int ncta, int pdl, AttnSmem& sm) {
+  // The position and the cached rows t != pos were written before the
+  // producing GEMV started (it triggers this launch only after its own
+  // griddepcontrol.wait).
+  const int pos = (a.pos ? __ldcg(a.pos) : a.fixed_pos) + a.pos_off;
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  const int nsplit = (pos + keys) / keys;
+  const int G = a.nh / a.nkv;
+  const int hq = attn_hq(a.nh, a.nkv, nsplit, ncta);
+  const int subs = (G + hq - 1) / hq;
+  const int items = a.nkv * subs * nsplit;
+  bool waited = !pdl;
+  for (int it = cta; it < items; it += ncta) {
+    const int split = it / (a.nkv * subs), r = it % (a.nkv * subs);
+    const int kvh = r / subs, sub = r % subs;
+    attn_item<KVT>(a, kvh, kvh * G + sub * hq, min(hq, G - sub * hq), split, nsplit, pos, sub == 0,
+                   waited ? 0 : 1, sm);
+    waited = true;
+  }
+  if (!waited) {  // no item for this CTA: still order the launch chain
+    pdl_wait();
+    pdl_launch_dependents();
+  }
 }
 
 }  // namespace eg

@@ -94,8 +94,12 @@ def _read_safetensors(path: str) -> dict:
     return out
 
 
-def loadLoraAdapter(rt, files: list[str], cfg: dict | None = None) -> LoraAdapter:
-    """loadLoraAdapterGPU(dev, files, cfg) (lora_gpu.js:65-113)."""
+def parseLoraAdapter(files: list[str]) -> tuple[str, dict]:
+    """The host half of loadLoraAdapterGPU (lora_gpu.js:65-113): the adapter
+    name and {module key: {A, B, scale}} with A / B as the file holds them.
+    Scale: lora_parameters.scale (MLX), else lora_alpha / rank (PEFT), else
+    alpha / rank, else 2.0; rank from r / rank / lora_rank /
+    lora_parameters.rank, 16 when absent (lora_gpu.js:68-80)."""
     st = [f for f in files if f.endswith(".safetensors")]
     if not st:
         raise ValueError("no .safetensors in adapter files")
@@ -110,7 +114,8 @@ def loadLoraAdapter(rt, files: list[str], cfg: dict | None = None) -> LoraAdapte
                 rank_cfg = c[k]
                 break
         else:
-            rank_cfg = lp.get("rank", rank_cfg)
+            if lp.get("rank") is not None:
+                rank_cfg = lp["rank"]
         if lp.get("scale") is not None:
             scale_cfg = lp["scale"]
         elif c.get("lora_alpha") is not None:
@@ -131,7 +136,26 @@ def loadLoraAdapter(rt, files: list[str], cfg: dict | None = None) -> LoraAdapte
                if "A" in g and "B" in g}
     if not modules:
         raise ValueError("no LoRA modules matched layers.*.{self_attn,mlp}.*_proj")
-    name = os.path.basename(st[0]).rsplit(".safetensors", 1)[0]
+    return os.path.basename(st[0]).rsplit(".safetensors", 1)[0], modules
+
+
+def orientLora(A: np.ndarray, B: np.ndarray, in_dim: int, out_dim: int):
+    """(A [r][in], B [r][out], r) as the library stores them (eg_lora_orient,
+    lora_gpu.js:100-107)."""
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    r = int(min(*A.shape, *B.shape))
+    a = np.empty((r, in_dim), np.float32)
+    b = np.empty((r, out_dim), np.float32)
+    rr = C.c_int(0)
+    L.check(L.lib().eg_lora_orient(A.ctypes.data, A.shape[0], A.shape[1], B.ctypes.data, B.shape[0],
+                                   B.shape[1], in_dim, out_dim, a.ctypes.data, b.ctypes.data, C.byref(rr)))
+    return a, b, rr.value
+
+
+def loadLoraAdapter(rt, files: list[str], cfg: dict | None = None) -> LoraAdapter:
+    """loadLoraAdapterGPU(dev, files, cfg) (lora_gpu.js:65-113)."""
+    name, modules = parseLoraAdapter(files)
     return LoraAdapter(rt, name, modules)
 
 
