@@ -81,6 +81,11 @@ typedef struct {
   int prefill_chunk;       /* prompt positions per batched prefill step (2..16,
                               default 16): every weight tile is read once per
                               chunk; 0 = one decode step per prompt token */
+  int use_tc_batch;        /* 1: the int4 GEMVs of batched steps of 4 or more
+                              lanes (batched decode, chunked prefill) run on
+                              the tcgen05 tensor cores (keeps a second,
+                              octet-major copy of the int4 weights); 0
+                              (default): the integer mma.sync path */
 } eg_options;
 
 EG_API const char* eg_last_error(void);
@@ -303,6 +308,20 @@ EG_API eg_status eg_op_q4_to_stream(const uint32_t* w, const float* scale, int N
                                     void* out, void* stream);
 EG_API eg_status eg_op_gemv_q4_stream(const float* x, const void* ws, const float* bias, int N,
                                       int K, float* y, int* err, int pdl, void* stream);
+/* The tensor-core weight layout: the stream-layout blocks regrouped
+ * octet-major (128-row octets, group, tile), so that the tcgen05 GEMM
+ * streams each pipeline stage as one contiguous copy.  Built once, like the
+ * stream layout. */
+EG_API eg_status eg_op_q4_tc_bytes(int N, int K, int R, uint64_t* bytes);
+EG_API eg_status eg_op_q4_stream_to_tc(const void* ws, int N, int K, int R, void* out, void* stream);
+/* GEMM4 / GEMM4_ADD_T, kernels.js:389-473: Y[t][n] = W4 x_t (+bias) for
+ * T token vectors x [T][K]; accumulate = 1 gives Y += W4 x_t.  use_tc = 1:
+ * the tcgen05 tensor-core path (T <= 32) over the tc layout
+ * (eg_op_q4_stream_to_tc); 0: the integer mma.sync path (T <= 16) over the
+ * stream layout (eg_op_q4_to_stream).  Uses library scratch memory for the
+ * staged activations. */
+EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, const float* bias, int N,
+                                      int K, float* y, int accumulate, int use_tc, void* stream);
 /* GATE_UP_SILU_GEMV4, kernels.js:1021-1072: w/scale hold 2N rows [gate;up]. */
 EG_API eg_status eg_op_gate_up_silu(const float* x, const uint32_t* w, const float* scale,
                                     int N, int K, float* y, void* stream);

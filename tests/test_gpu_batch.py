@@ -108,6 +108,31 @@ def test_batch_greedy_lanes_match_single_sequence_oracle(cuda, f16):
         assert rt.seqState(sl)[0] == 16
 
 
+@pytest.mark.parametrize("lanes", [4, 7, 16])
+def test_tc_gemv_matches_legacy_integer_mma(cuda, lanes):
+    """The tcgen05 batched GEMVs (useTcBatch, 4+ lanes) compute the same
+    exact integer group dots as the legacy mma.sync path and differ only in
+    the f32 order of the group fold: f32 KV, logits of every lane after each
+    of 6 steps agree to f32 noise and the greedy tokens are identical; one
+    full octet, split octets and a partial last octet all occur (QKV 2560
+    rows, O / down 2048, gate_up 2 x 1024 over 148 CTAs)."""
+    cfg = small_config(layers=2, vocab=3000, inter=1024)
+    rts = [E.QwenB200(cfg, dict(maxCtx=64, useF16=False, useTcBatch=tc)).build("synthetic", seed=SEED)
+           for tc in (True, False)]
+    ps = prompts(lanes, cfg["vocabSize"], [3 + (i % 5) for i in range(lanes)])
+    for rt in rts:
+        rt.seqInit(lanes, 40)
+        for sl, p in enumerate(ps):
+            rt.seqSetPrompt(sl, p)
+    for step in range(6):
+        a, b = (rt.batchDecode(list(range(lanes)), 1) for rt in rts)
+        assert np.array_equal(a, b), step
+        for j in range(lanes):
+            la, lb = rts[0].batchLogits(j), rts[1].batchLogits(j)
+            d = np.abs(la.astype(np.float64) - lb)
+            assert d.max() <= 2e-4 and d.mean() / np.abs(lb).mean() <= 2e-5, (step, j, d.max())
+
+
 def test_batch_multi_step_call_equals_single_steps(cuda):
     """One call of K steps (one captured graph replayed K times) gives the
     same tokens as K calls of one step, and matches the single-sequence

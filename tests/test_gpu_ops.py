@@ -131,6 +131,33 @@ def test_gemv_q4_stream_upload_once(cuda):
     close(host(y0), ref, 2e-4, 1e-4)
 
 
+@pytest.mark.parametrize("N,Kd,T", [(2560, 2048, 16), (517, 2048, 5), (2048, 11008, 32), (128, 128, 4)])
+def test_gemm4_tc_and_mma_vs_oracle(cuda, N, Kd, T):
+    """GEMM4 / GEMM4_ADD_T (kernels.js:389-473): T token vectors through one
+    weight pass, on the tcgen05 path (tc layout) and, for T <= 16, the
+    integer mma.sync path (stream layout), each row against the oracle's
+    GEMV of that token; full octets, a partial last octet (N = 517) and
+    split-K octets all occur."""
+    W = O.normal(N * Kd, 0xE6B00101 + N, 0.02).reshape(N, Kd)
+    X = O.normal(T * Kd, 0xE6B00102 + T, 1.0).reshape(T, Kd)
+    bias = O.normal(N, 0xE6B00103, 0.02)
+    p, s = O.quantize_int4_group(W)
+    ref = np.stack([O.gemv_q4(X[t], p, s, N, Kd, bias=bias) for t in range(T)])
+    ws = torch.zeros(K.q4_stream_bytes(N, Kd), dtype=torch.uint8, device=cuda)
+    K.q4_to_stream(dev(p), dev(s), N, Kd, ws)
+    wc = torch.zeros(K.q4_tc_bytes(N, Kd), dtype=torch.uint8, device=cuda)
+    K.q4_stream_to_tc(ws, N, Kd, wc)
+    paths = [True] + ([False] if T <= 16 else [])
+    for tc in paths:
+        y = torch.full((T, N), float("nan"), device=cuda)
+        K.gemm_q4_stream(dev(X), T, wc if tc else ws, N, Kd, y, bias=dev(bias), use_tc=tc)
+        close(host(y), ref, 2e-4, 1e-4)
+        y0 = O.normal(T * N, 7, 1.0).reshape(T, N)
+        ya = dev(y0)
+        K.gemm_q4_stream(dev(X), T, wc if tc else ws, N, Kd, ya, accumulate=True, use_tc=tc)
+        close(host(ya), y0 + (ref - bias), 2e-4, 1e-4)
+
+
 @pytest.mark.parametrize("f16", [0, 1])
 @pytest.mark.parametrize("pos,chunk", [(0, 0), (16, 0), (127, 0), (128, 0), (300, 0), (1000, 16),
                                        (4095, 0), (4095, 64), (7799, 0)])

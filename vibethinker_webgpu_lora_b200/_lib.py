@@ -36,6 +36,7 @@ class EgOptions(C.Structure):
         ("decode_batch_capacity", C.c_int), ("sampling_top_k", C.c_int),
         ("max_sampling_top_k", C.c_int), ("attn_chunk", C.c_int), ("use_graphs", C.c_int),
         ("use_pdl", C.c_int), ("use_fused", C.c_int), ("prefill_chunk", C.c_int),
+        ("use_tc_batch", C.c_int),
     ]
 
 
@@ -102,6 +103,9 @@ _SIGS = {
     "eg_op_q4_stream_bytes": (i32, [i32, i32, i32, C.POINTER(u64)]),
     "eg_op_q4_to_stream": (i32, [vp, vp, i32, i32, i32, vp, vp]),
     "eg_op_gemv_q4_stream": (i32, [vp, vp, vp, i32, i32, vp, vp, i32, vp]),
+    "eg_op_gemm_q4_stream": (i32, [vp, i32, vp, vp, i32, i32, vp, i32, i32, vp]),
+    "eg_op_q4_tc_bytes": (i32, [i32, i32, i32, C.POINTER(u64)]),
+    "eg_op_q4_stream_to_tc": (i32, [vp, i32, i32, i32, vp, vp]),
     "eg_op_gate_up_silu": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "eg_op_gemv_q8": (i32, [vp, vp, vp, i32, i32, vp, vp]),
     "eg_op_rmsnorm": (i32, [vp, vp, i32, f32, i32, vp, vp]),

@@ -50,6 +50,12 @@ struct BatchPlanes {
   float* xmul;   // int8 only
   int* xf;       // int4 only
   int gpr_max;
+  // int4 only, optional: the same digit planes as the B operand of the
+  // tcgen05 GEMV (gemv_q4_tc): per group, N = 4 tc_tpad columns (lane v,
+  // plane p at column 4v + p) x 128 bytes, K-major 8 x 16-byte core
+  // matrices, the 8 k-chunks N / 8 core matrices apart.
+  void* xtc;
+  int tc_tpad;
 };
 
 // Epilogue of a batched int4 GEMV: the single-lane epilogue (bias /
@@ -63,6 +69,20 @@ struct BatchEpi {
   const float* lora_pre;
   int lstride;
 };
+
+// Batched int4 GEMV on the tcgen05 tensor cores (eg_tc.cu): the epilogue
+// of gemv_q4_batch for lanes <= 32 (xp.xtc staged by batch_stage_q4), R = 2
+// for GATE_UP_SILU; ws in the tc layout (q4_stream_to_tc).  part / counters: split-octet scratch
+// (gemv_q4_tc_part_bytes, counters zero between launches).
+void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const BatchPlanes& xp,
+                const BatchEpi& be, float* part, unsigned* counters, int* err, cudaStream_t st,
+                bool pdl);
+size_t gemv_q4_tc_part_bytes();
+// The weight layout gemv_q4_tc streams (from the stream layout): octet-major,
+// so that every pipeline stage is one contiguous copy.
+size_t q4_tc_bytes(int N, int K, int R);
+void q4_stream_to_tc(const unsigned char* ws, int N, int K, int R, unsigned char* out, cudaStream_t st);
+int gemv_q4_tc_max_octets();
 
 // pdl: launched as programmatic dependents of the previous kernel (each
 // kernel waits with griddepcontrol.wait before reading earlier outputs).

@@ -198,9 +198,13 @@ __device__ __forceinline__ void setup_x(const XSrc& s, int K, XCtx& c, float* sr
 //         groups of scale * (column pair i value - xcor).
 // pdl: the norm weights are read first, then griddepcontrol.wait, then the
 // input (which the previous kernel writes).
+// xtc (optional): the same planes also as the tcgen05 B operand (see
+// BatchPlanes::xtc), this vector at columns tc_col0 .. tc_col0 + 3 of
+// tc_ncol.
 template <int MAXU, bool NORM, int NT = kCtaThreads>
 __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, int* xf, float* sred,
-                         int pdl) {
+                         int pdl, unsigned char* xtc = nullptr, int tc_ncol = 0,
+                         int tc_col0 = 0) {
   const int K8 = K / 8;
   float v[MAXU][8];
   float gw[NORM ? MAXU : 1][8];
@@ -319,6 +323,14 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, int* xf, fl
     const int G = u >> 4, q = u & 15, m = q >> 2, t = q & 3;
 #pragma unroll
     for (int p = 0; p < 4; p++) xb[((G * 4 + p) * 4 + t) * 4 + m] = pl[p];
+    if (xtc) {  // unit q = k bytes 8q .. 8q + 7: k-chunk q / 2, half q & 1
+      unsigned char* gb = xtc + (size_t)G * tc_ncol * 128 + (size_t)(q >> 1) * (tc_ncol / 8) * 128 + (q & 1) * 8;
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        const int n = tc_col0 + p;
+        *reinterpret_cast<uint2*>(gb + (n >> 3) * 128 + (n & 7) * 16) = pl[p];
+      }
+    }
     if (q == 0) {
       xcor[2 * G] = 8 * (W[0] + 256 * W[1]);
       xcor[2 * G + 1] = 8 * (W[2] + 256 * W[3]);

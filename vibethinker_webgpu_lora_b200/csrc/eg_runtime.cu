@@ -51,6 +51,8 @@ struct Layer {
   void *kc = nullptr, *vc = nullptr;
   // stream-layout copies of the int4 matrices (q4_to_stream), built at finalize
   unsigned char *qkv_t = nullptr, *o_t = nullptr, *gu_t = nullptr, *d_t = nullptr;
+  // the same blocks octet-major for the tcgen05 batched GEMV (q4_stream_to_tc)
+  unsigned char *qkv_c = nullptr, *o_c = nullptr, *gu_c = nullptr, *d_c = nullptr;
 };
 
 struct DevState {
@@ -113,6 +115,9 @@ struct eg_rt {
         *b_lora_d = nullptr, *b_lora_y = nullptr, *b_xmul = nullptr, *b_cand_v = nullptr, *b_topk_vals = nullptr,
         *b_r = nullptr;
   void* b_xb = nullptr;
+  void* b_xtc = nullptr;      // tcgen05 B planes (gpr x 64 columns x 128 B)
+  float* b_tc_part = nullptr; // tcgen05 GEMV split-octet partials
+  unsigned* b_tc_cnt = nullptr;
   int *b_xcor = nullptr, *b_xf = nullptr;
   unsigned* b_attn_counters = nullptr;
   uint32_t *b_choice = nullptr, *b_cand_i = nullptr, *b_topk_ids = nullptr, *b_out = nullptr;
@@ -743,7 +748,7 @@ EG_API void eg_default_config(eg_config* c) {
 }
 EG_API void eg_default_options(eg_options* o) {
   if (!o) return;
-  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0, 16};
+  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0, 16, 0};
 }
 
 EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** out) {
@@ -917,6 +922,17 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
       q4_to_stream(l.gu_w, l.gu_s, I, H, 2, l.gu_t, rt->st);
       q4_to_stream(l.d_w, l.d_s, H, I, 1, l.d_t, rt->st);
       CK(cudaGetLastError());
+      if (rt->o.use_tc_batch) {
+        DALLOC(l.qkv_c, q4_tc_bytes(NQKV, H, 1), wb);
+        DALLOC(l.o_c, q4_tc_bytes(H, QD, 1), wb);
+        DALLOC(l.gu_c, q4_tc_bytes(I, H, 2), wb);
+        DALLOC(l.d_c, q4_tc_bytes(H, I, 1), wb);
+        q4_stream_to_tc(l.qkv_t, NQKV, H, 1, l.qkv_c, rt->st);
+        q4_stream_to_tc(l.o_t, H, QD, 1, l.o_c, rt->st);
+        q4_stream_to_tc(l.gu_t, I, H, 2, l.gu_c, rt->st);
+        q4_stream_to_tc(l.d_t, H, I, 1, l.d_c, rt->st);
+        CK(cudaGetLastError());
+      }
     }
     DALLOC(rt->emb_t, q8_stream_bytes(c.vocab_size, H), wb);
     q8_to_stream(rt->emb_w, c.vocab_size, H, rt->emb_t, rt->st);
@@ -1212,7 +1228,8 @@ static eg_status seq_free(eg_rt* rt) {
                  (void**)&rt->b_topk_vals, (void**)&rt->b_r, (void**)&rt->b_xb,
                  (void**)&rt->b_xcor, (void**)&rt->b_xf, (void**)&rt->b_attn_counters,
                  (void**)&rt->b_choice, (void**)&rt->b_cand_i, (void**)&rt->b_topk_ids,
-                 (void**)&rt->b_out, (void**)&rt->seq_page_table};
+                 (void**)&rt->b_out, (void**)&rt->seq_page_table, (void**)&rt->b_xtc,
+                 (void**)&rt->b_tc_part, (void**)&rt->b_tc_cnt};
   for (void** q : sp) dfree(rt, q, 0, nullptr);
   if (rt->batch_mark >= 0) rt->scratch_bytes = rt->batch_mark;  // everything since is freed
   rt->batch_mark = -1;
@@ -1250,6 +1267,9 @@ static eg_status batch_scratch(eg_rt* rt) {
   DALLOC(rt->b_lora_d, (size_t)B * 3 * kMaxRank * 4, sb);
   DALLOC(rt->b_lora_y, (size_t)B * std::max(std::max(NQKV, 2 * I), H) * 4, sb);
   DALLOC(rt->b_xb, (size_t)B * rt->b_gpr * 512, sb);
+  DALLOC(rt->b_xtc, (size_t)rt->b_gpr * 4 * kBatchMax * 128, sb);
+  DALLOC(rt->b_tc_part, gemv_q4_tc_part_bytes(), sb);
+  DALLOC(rt->b_tc_cnt, (size_t)gemv_q4_tc_max_octets() * 4, sb);
   DALLOC(rt->b_xcor, (size_t)B * rt->b_gpr * 2 * 4, sb);
   DALLOC(rt->b_xmul, (size_t)B * rt->b_gpr * 2 * 4, sb);
   DALLOC(rt->b_xf, B * 4, sb);
@@ -1262,6 +1282,8 @@ static eg_status batch_scratch(eg_rt* rt) {
   DALLOC(rt->b_topk_vals, B * 64 * 4, sb);
   CK(cudaMemsetAsync(rt->lane_slot, 0, B * 4, rt->st));
   CK(cudaMemsetAsync(rt->b_xb, 0, (size_t)B * rt->b_gpr * 512, rt->st));
+  CK(cudaMemsetAsync(rt->b_xtc, 0, (size_t)rt->b_gpr * 4 * kBatchMax * 128, rt->st));
+  CK(cudaMemsetAsync(rt->b_tc_cnt, 0, (size_t)gemv_q4_tc_max_octets() * 4, rt->st));
   CK(cudaMemsetAsync(rt->b_xcor, 0, (size_t)B * rt->b_gpr * 8, rt->st));
   CK(cudaMemsetAsync(rt->b_xmul, 0, (size_t)B * rt->b_gpr * 8, rt->st));
   CK(cudaMemsetAsync(rt->b_xf, 0, B * 4, rt->st));
@@ -1488,8 +1510,19 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
   xp.xmul = rt->b_xmul;
   xp.xf = rt->b_xf;
   xp.gpr_max = rt->b_gpr;
+  // 4 or more lanes: the int4 GEMVs on the tcgen05 tensor cores
+  const bool tc = rt->o.use_tc_batch && n >= 4 && rt->L[0].qkv_c;
+  xp.xtc = tc ? rt->b_xtc : nullptr;
+  xp.tc_tpad = (n + 3) / 4 * 4;
   int launches = 0;
   const bool pdl = rt->o.use_pdl != 0;
+  auto gemv4 = [&](const unsigned char* w, const unsigned char* wc, int N, int K, const BatchEpi& e) {
+    if (tc)
+      gemv_q4_tc(wc, N, K, e.e.mode == EPI_SILU ? 2 : 1, n, xp, e, rt->b_tc_part, rt->b_tc_cnt, err, st,
+                 pdl);
+    else
+      gemv_q4_batch(w, N, K, n, xp, e, err, st, pdl);
+  };
   auto src = [&](int mode, const float* x, const float* g, int stride) {
     BatchSrc b = {};
     b.x.mode = mode;
@@ -1535,10 +1568,9 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
       launches++;
     }
     batch_stage_q4(xa, H, n, xp, st, pdl);
-    gemv_q4_batch(l.qkv_t, NQKV, H, n, xp,
-                  epi(EPI_STORE, rt->b_qkv, NQKV, NQKV, c.attention_bias ? l.qkv_b : nullptr,
-                      i * 7 + 0, QD, QD + KVD),
-                  err, st, pdl);
+    gemv4(l.qkv_t, l.qkv_c, NQKV, H,
+          epi(EPI_STORE, rt->b_qkv, NQKV, NQKV, c.attention_bias ? l.qkv_b : nullptr, i * 7 + 0, QD,
+              QD + KVD));
     launches += 2;
     AttnArgs a = {};
     a.qkv = rt->b_qkv;
@@ -1579,8 +1611,7 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
       launches++;
     }
     batch_stage_q4(xo, QD, n, xp, st, pdl);
-    gemv_q4_batch(l.o_t, H, QD, n, xp, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 3, H, H),
-                  err, st, pdl);
+    gemv4(l.o_t, l.o_c, H, QD, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 3, H, H));
     launches += 2;
     BatchSrc xb = src(X_RMS, rt->b_hidden, l.post_norm, H);
     if (lora) {
@@ -1588,8 +1619,7 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
       launches++;
     }
     batch_stage_q4(xb, H, n, xp, st, pdl);
-    gemv_q4_batch(l.gu_t, I, H, n, xp, epi(EPI_SILU, rt->b_tmp, I, I, nullptr, i * 7 + 4, I, I),
-                  err, st, pdl);
+    gemv4(l.gu_t, l.gu_c, I, H, epi(EPI_SILU, rt->b_tmp, I, I, nullptr, i * 7 + 4, I, I));
     launches += 2;
     BatchSrc xd = src(X_PLAIN, rt->b_tmp, nullptr, I);
     if (lora) {
@@ -1597,8 +1627,7 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
       launches++;
     }
     batch_stage_q4(xd, I, n, xp, st, pdl);
-    gemv_q4_batch(l.d_t, H, I, n, xp, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 6, H, H),
-                  err, st, pdl);
+    gemv4(l.d_t, l.d_c, H, I, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 6, H, H));
     launches += 2;
   }
   if (chunk) {  // chunked prefill: no logits for these positions
@@ -2104,6 +2133,70 @@ EG_API eg_status eg_op_gemv_q4_stream(const float* x, const void* ws, const floa
   GemvWork wk;
   wk.err = err;
   gemv_q4(static_cast<const unsigned char*>(ws), N, K, xs, e, OPSTREAM, pdl != 0, wk);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_q4_tc_bytes(int N, int K, int R, uint64_t* bytes) {
+  if (!bytes || N <= 0 || K <= 0 || K % 128 || K > 12288 || (R != 1 && R != 2))
+    return fail(EG_ERR_ARG, "q4_tc_bytes: need K %% 128 == 0, K <= 12288, R = 1 or 2");
+  *bytes = q4_tc_bytes(N, K, R);
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_q4_stream_to_tc(const void* ws, int N, int K, int R, void* out, void* stream) {
+  if (!ws || !out || N <= 0 || K <= 0 || K % 128 || K > 12288 || (R != 1 && R != 2))
+    return fail(EG_ERR_ARG, "q4_stream_to_tc: bad argument");
+  if ((reinterpret_cast<uintptr_t>(ws) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(EG_ERR_ARG, "q4_stream_to_tc: 16-byte aligned buffers required");
+  q4_stream_to_tc(static_cast<const unsigned char*>(ws), N, K, R, static_cast<unsigned char*>(out), OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, const float* bias, int N,
+                                      int K, float* y, int accumulate, int use_tc, void* stream) {
+  if (!x || !ws || !y || T < 1 || N <= 0 || K <= 0 || K % 128 || K > 12288)
+    return fail(EG_ERR_ARG, "gemm_q4_stream: bad argument");
+  if (T > (use_tc ? 32 : kBatchMax))
+    return fail(EG_ERR_ARG, "gemm_q4_stream: at most %d tokens per call", use_tc ? 32 : kBatchMax);
+  if (accumulate && bias) return fail(EG_ERR_ARG, "gemm_q4_stream: bias with accumulate is not supported");
+  if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(EG_ERR_ARG, "gemm_q4_stream: ws must be 16-byte aligned");
+  const int gpr = K / 128, tpad = (T + 3) / 4 * 4;
+  const size_t xb = (size_t)T * gpr * 512, xc = (size_t)T * gpr * 8, xtc = (size_t)gpr * 4 * tpad * 128;
+  const size_t cnt = (size_t)gemv_q4_tc_max_octets() * 4, part = gemv_q4_tc_part_bytes();
+  void* scr = nullptr;
+  eg_status s = op_scratch(256 + xb + xc + 256 + xtc + cnt + part, &scr);
+  if (s) return s;
+  char* b = static_cast<char*>(scr);
+  int* err = reinterpret_cast<int*>(b);
+  BatchPlanes xp = {};
+  xp.xb = b + 256;
+  xp.xcor = reinterpret_cast<int*>(b + 256 + xb);
+  xp.xf = reinterpret_cast<int*>(b + 256 + xb + xc);
+  xp.gpr_max = gpr;
+  xp.xtc = use_tc ? b + 512 + xb + xc : nullptr;
+  xp.tc_tpad = tpad;
+  unsigned* counters = reinterpret_cast<unsigned*>(b + 512 + xb + xc + xtc);
+  float* prt = reinterpret_cast<float*>(b + 512 + xb + xc + xtc + cnt);
+  CK(cudaMemsetAsync(err, 0, 4, OPSTREAM));
+  if (use_tc) CK(cudaMemsetAsync(counters, 0, cnt, OPSTREAM));
+  BatchSrc src = {};
+  src.x.mode = X_PLAIN;
+  src.x.x = x;
+  src.stride = K;
+  batch_stage_q4(src, K, T, xp, OPSTREAM, false);
+  BatchEpi be = {};
+  be.e.mode = accumulate ? EPI_ADD : EPI_STORE;
+  be.e.y = y;
+  be.e.N = N;
+  be.e.bias = bias;
+  be.e.split1 = be.e.split2 = N;
+  be.ystride = N;
+  if (use_tc)
+    gemv_q4_tc(static_cast<const unsigned char*>(ws), N, K, 1, T, xp, be, prt, counters, err, OPSTREAM, false);
+  else
+    gemv_q4_batch(static_cast<const unsigned char*>(ws), N, K, T, xp, be, err, OPSTREAM, false);
   CK(cudaGetLastError());
   return EG_OK;
 }

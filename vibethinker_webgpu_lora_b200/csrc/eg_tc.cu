@@ -1,0 +1,555 @@
+// eg_tc.cu -- batched int4 GEMV on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, accumulators in tensor memory), sm_100a.
+//
+// Y[t][n] = sum_g s[n][g] * dot_g(W4 row n, x_t) for up to 32 token vectors
+// x_t (the lanes of a batched decode step, or the positions of a prefill
+// chunk) over the same stream-layout int4 matrices as the batch-1 GEMV
+// (GEMV4 / GEMV4_ADD / GATE_UP_SILU_GEMV4, kernels.js:884-1072, and the
+// prefill GEMM4 / GEMM4_ADD_T, kernels.js:389-473).  The arithmetic is the
+// batch-1 one: each 128-wide group's dot product is exact in integers,
+// sum_k (q + 8) * D_p[k] per base-256 digit plane p of the token's
+// fixed-point activation, and is folded into f32 with the group scale.
+//
+// MMA shape: A = 128 weight rows (one "octet" of 8 row tiles, or 4 tiles of
+// gate + up rows) x 128 k as signed bytes q (odd k as 16 q, the batch-1
+// nibble trick, matched by the activation digits); B = the digit planes,
+// N = 4 x tokens columns (token t, plane p at column 4t + p); D = 128 TMEM
+// lanes x N s32 columns, one fresh accumulator per group (4 instructions of
+// K = 32).  The epilogue warps fold every group into f32 registers: per row
+// and token, acc01 += s * (P0 + 256 P1) and acc23 += s * (P2 + 256 P3);
+// y = 2^-f acc01 + 2^(16-f) acc23 -- the same integers as the batch-1
+// path's (P - offset correction) with unsigned q + 8.
+//
+// Work split: the (octet, group) items of the matrix, octet-major, are
+// divided evenly among the CTAs (split-K where a CTA boundary falls inside
+// an octet).  An octet a single CTA covers is finished by it; a split octet
+// is finished by the last of its CTAs to arrive, which sums the partial
+// outputs in CTA order (deterministic) before the epilogue.
+//
+// Warp roles (19 warps): 0-7 convert the int4 stage into the A operand
+// (nibbles to bytes, canonical K-major layout); 8-15 epilogue (two
+// warpgroups, one per half of the tokens; warp w reads TMEM lanes
+// 32 (w % 4) ..); 16 streams the weight stages (cp.async.bulk); 17 issues
+// the MMAs (one elected thread) and owns the TMEM allocation; 18 copies the
+// B planes.  Pipelines: weight stages (3) -> A slots (3, freed when the MMAs
+// that read them complete) ; B slots (4, likewise) ; TMEM accumulators (up
+// to 4, freed by the epilogue).
+#include <algorithm>
+
+#include "eg_batch.h"
+#include "eg_common.cuh"
+#include "eg_device.cuh"
+#include "eg_stream.cuh"
+#include "eg_tc.cuh"
+
+namespace eg {
+
+namespace {
+
+constexpr int kTcThreads = 19 * 32;
+constexpr int kTcConvWarps = 8;
+constexpr int kTcEpiWarp0 = 8, kTcEpiWarps = 8;
+constexpr int kTcProdWarp = 16, kTcMmaWarp = 17, kTcBWarp = 18;
+constexpr int kTcRaw = 3;          // weight stages (int4, as streamed)
+constexpr int kTcA = 3;            // A operand slots (bytes)
+constexpr int kTcB = 4;            // B operand slots (digit planes)
+constexpr int kTcSc = 8;           // group-scale slots (converter -> epilogue)
+constexpr int kTcGroupsPerStage = 4;
+constexpr int kTcStageBytes = 8 * kTcGroupsPerStage * 1088;  // = 4 * 4 * 2176
+constexpr int kTcABytes = 128 * 128;                          // 128 rows x 128 bytes
+constexpr int kTcMaxTok = 32;
+constexpr int kTcBBytes = 4 * kTcMaxTok * 128;                // N x 128 bytes
+constexpr uint32_t kTcTmemCols = 256;
+
+struct TcArgs {
+  const unsigned char* ws;   // tc layout (q4_stream_to_tc)
+  int N, K, R, lanes, tpad;
+  const unsigned char* xtc;  // B planes, per group N x 128 bytes (BatchPlanes::xtc)
+  const int* xf;             // [lane] fixed-point exponent
+  BatchEpi be;
+  float* part;               // [ncta][2][32][128]
+  unsigned* counters;        // [octets]
+  int* err;
+  int pdl;
+};
+
+struct TcSmem {
+  uint64_t raw_full[kTcRaw], raw_empty[kTcRaw];
+  uint64_t a_full[kTcA], a_empty[kTcA], b_full[kTcB], b_empty[kTcB];
+  uint64_t acc_full[4], acc_empty[4];
+  uint64_t sc_full[kTcSc], sc_empty[kTcSc];
+  uint32_t tmem_base;
+  int last;
+  float scale[kTcSc][128];  // group scale of every MMA row, per item
+};
+
+// items * ncta < 2^31 for every matrix here (at most 20,000 items x 296 CTAs).
+__host__ __device__ __forceinline__ int item_lo(int items, int ncta, int c) {
+  return (int)((unsigned)(items * c) / (unsigned)ncta);
+}
+__device__ __forceinline__ int cta_of(int items, int ncta, int i) {
+  int c = (int)((unsigned)(i * ncta) / (unsigned)items);
+  while (c + 1 < ncta && item_lo(items, ncta, c + 1) <= i) c++;
+  while (c > 0 && item_lo(items, ncta, c) > i) c--;
+  return c;
+}
+
+// Stages of this CTA's item range: (octet, first group, group count) in order.
+struct StageIter {
+  int i, hi, gpr, o, g;  // next item i = (octet o, group g)
+  __device__ StageIter(int lo, int hi_, int gpr_) : i(lo), hi(hi_), gpr(gpr_), o(lo / gpr_), g(lo % gpr_) {}
+  __device__ bool next(int& oo, int& g0, int& ng) {
+    if (i >= hi) return false;
+    oo = o;
+    g0 = g;
+    ng = min(kTcGroupsPerStage, min(hi - i, gpr - g));
+    i += ng;
+    g += ng;
+    if (g == gpr) {
+      g = 0;
+      o++;
+    }
+    return true;
+  }
+};
+
+// Ring position (slot, phase parity) of a pipeline of n slots.
+struct Ring {
+  int slot, ph;
+  __device__ void adv(int n) {
+    if (++slot == n) {
+      slot = 0;
+      ph ^= 1;
+    }
+  }
+};
+
+// The final epilogue of one row and token (batch_epilogue's arithmetic).
+__device__ __forceinline__ void tc_store(const TcArgs& a, int t, int n, float v, float up) {
+  const Epi& E = a.be.e;
+  const float* lp = a.be.lora_pre;
+  if (a.R == 2) {
+    float g = v, u = up;
+    if (lp) {
+      g = __fadd_rn(g, lp[(size_t)t * a.be.lstride + n]);
+      u = __fadd_rn(u, lp[(size_t)t * a.be.lstride + E.N + n]);
+    }
+    E.y[(size_t)t * a.be.ystride + n] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+    return;
+  }
+  float o = v;
+  if (E.bias) o = __fadd_rn(o, E.bias[n]);
+  if (lp) o = __fadd_rn(o, lp[(size_t)t * a.be.lstride + n]);
+  float* yp = E.y + (size_t)t * a.be.ystride + n;
+  *yp = E.mode == EPI_ADD ? __fadd_rn(__ldcg(yp), o) : o;
+}
+
+}  // namespace
+
+// A operand bytes of one int4 word (8 nibbles, k = 8w .. 8w + 7): the even
+// nibbles as signed bytes q, the odd ones in place as 16 q (the activation
+// digits of odd k carry the matching 1/16).  Signed A makes the integer dot
+// exactly sum q * D with no offset correction.
+__device__ __forceinline__ uint2 a_bytes(uint32_t w) {
+  // even: u = nibble, (u ^ 8) + 120 = v + 128 in [120, 135] (no carry
+  // between bytes), ^ 0x80 = v as a two's-complement byte
+  return make_uint2((((w & 0x0F0F0F0Fu) ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u, w & 0xF0F0F0F0u);
+}
+
+template <int TH>  // tokens per epilogue warpgroup (tpad / 2 <= TH)
+__global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
+  extern __shared__ __align__(1024) unsigned char tc_dsm[];
+  __shared__ TcSmem S;
+  unsigned char* raw = tc_dsm;                                // kTcRaw stages
+  unsigned char* abuf = raw + (size_t)kTcRaw * kTcStageBytes; // kTcA x 16 KB
+  unsigned char* bbuf = abuf + (size_t)kTcA * kTcABytes;      // kTcB x N x 128
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = a.R, blk = q4_block_bytes(R), TPO = 8 / R;
+  const int gpr = a.K / kGroup, tiles = (a.N + 15) / 16, octets = (tiles + TPO - 1) / TPO;
+  const int items = octets * gpr;
+  const int ncta = gridDim.x, c = blockIdx.x;
+  const int i0 = item_lo(items, ncta, c), i1 = item_lo(items, ncta, c + 1);
+  const int ncol = 4 * a.tpad;
+  const int NT = min(4, (int)kTcTmemCols / ncol);  // TMEM accumulator slots
+  const uint32_t bbytes = (uint32_t)ncol * 128;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTcRaw; i++) {
+      mbar_init(&S.raw_full[i], 1);
+      mbar_init(&S.raw_empty[i], kTcConvWarps);
+    }
+    for (int i = 0; i < kTcA; i++) {
+      mbar_init(&S.a_full[i], kTcConvWarps);
+      mbar_init(&S.a_empty[i], 1);
+    }
+    for (int i = 0; i < kTcB; i++) {
+      mbar_init(&S.b_full[i], 1);
+      mbar_init(&S.b_empty[i], 1);
+    }
+    for (int i = 0; i < 4; i++) {
+      mbar_init(&S.acc_full[i], 1);
+      mbar_init(&S.acc_empty[i], kTcEpiWarps);
+    }
+    for (int i = 0; i < kTcSc; i++) {
+      mbar_init(&S.sc_full[i], kTcConvWarps);
+      mbar_init(&S.sc_empty[i], kTcEpiWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kTcMmaWarp) tmem_alloc(&S.tmem_base, kTcTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+  bool dead = false;
+
+  if (warp == kTcProdWarp) {
+    // ---------------------------------------------------- weight stages
+    // the weights depend on no earlier kernel: no griddepcontrol.wait here
+    if (a.pdl && lane == 0) pdl_launch_dependents();
+    StageIter it(i0, i1, gpr);
+    int o, g0, ng, s = 0, ph = 0, issued = 0;
+    while (it.next(o, g0, ng)) {
+      if (!dead && !tc_wait(&S.raw_empty[s], ph ^ 1, a.err)) dead = true;
+      if (lane == 0) {  // the tc layout: one contiguous run per stage
+        const uint32_t bytes = (uint32_t)(ng * TPO * blk);
+        mbar_expect_tx(&S.raw_full[s], bytes);
+        bulk_g2s(raw + (size_t)s * kTcStageBytes, a.ws + ((size_t)o * gpr + g0) * TPO * blk, bytes,
+                 &S.raw_full[s]);
+      }
+      __syncwarp();
+      issued++;
+      if (++s == kTcRaw) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+    // never leave with a copy in flight
+    for (int k = 0; k < kTcRaw && k < issued; k++) {
+      if (s == 0) {
+        s = kTcRaw - 1;
+        ph ^= 1;
+      } else {
+        s--;
+      }
+      if (!tc_wait_bounded(&S.raw_full[s], ph)) break;
+    }
+  } else if (warp == kTcBWarp) {
+    // ---------------------------------------------------- B planes
+    if (a.pdl) pdl_wait();
+    Ring rb{0, 0};
+    int g = i0 % gpr;
+    for (int i = i0; i < i1; i++) {
+      if (!dead && !tc_wait(&S.b_empty[rb.slot], rb.ph ^ 1, a.err)) dead = true;
+      if (lane == 0) {
+        mbar_expect_tx(&S.b_full[rb.slot], bbytes);
+        bulk_g2s(bbuf + (size_t)rb.slot * kTcBBytes, a.xtc + (size_t)g * bbytes, bbytes, &S.b_full[rb.slot]);
+      }
+      __syncwarp();
+      rb.adv(kTcB);
+      if (++g == gpr) g = 0;
+    }
+    for (int j = 0; j < kTcB && j < i1 - i0; j++) {  // copies in flight have landed
+      if (rb.slot == 0) {
+        rb.slot = kTcB - 1;
+        rb.ph ^= 1;
+      } else {
+        rb.slot--;
+      }
+      tc_wait_bounded(&S.b_full[rb.slot], rb.ph);
+    }
+  } else if (warp == kTcMmaWarp) {
+    // ---------------------------------------------------- MMA issue
+    const uint32_t idesc = idesc_i8(128, ncol) | (1u << 7);  // A signed
+    Ring ra{0, 0}, rb{0, 0}, rt{0, 0};
+    for (int i = i0; i < i1; i++) {
+      if (!dead && !tc_wait(&S.a_full[ra.slot], ra.ph, a.err)) dead = true;
+      if (!dead && !tc_wait(&S.b_full[rb.slot], rb.ph, a.err)) dead = true;
+      if (!dead && !tc_wait(&S.acc_empty[rt.slot], rt.ph ^ 1, a.err)) dead = true;
+      tc_fence_after();
+      if (lane == 0) {
+        const unsigned char* A = abuf + (size_t)ra.slot * kTcABytes;
+        const unsigned char* B = bbuf + (size_t)rb.slot * kTcBBytes;
+        const uint32_t d = tmem + (uint32_t)(rt.slot * ncol);
+#pragma unroll
+        for (int j = 0; j < 4; j++)  // K = 32 bytes = 2 core matrices per instruction
+          mma_i8(d, smem_desc(A + j * 2 * 2048, 2048, 128),
+                 smem_desc(B + (size_t)j * 2 * (ncol / 8) * 128, (ncol / 8) * 128, 128), idesc,
+                 j > 0);
+        mma_commit(&S.acc_full[rt.slot]);
+        mma_commit(&S.a_empty[ra.slot]);
+        mma_commit(&S.b_empty[rb.slot]);
+      }
+      __syncwarp();
+      ra.adv(kTcA);
+      rb.adv(kTcB);
+      rt.adv(NT);
+    }
+    // the MMAs this warp issued have finished before TMEM is freed
+    for (int j = 0; j < NT && j < i1 - i0; j++) {
+      if (rt.slot == 0) {
+        rt.slot = NT - 1;
+        rt.ph ^= 1;
+      } else {
+        rt.slot--;
+      }
+      tc_wait_bounded(&S.acc_full[rt.slot], rt.ph);
+    }
+  } else if (warp < kTcConvWarps) {
+    // ---------------------------------------------------- convert to A
+    const int ct = threadIdx.x;  // 0..255
+    StageIter it(i0, i1, gpr);
+    int o, g0, ng, s = 0, ph = 0;
+    Ring ra{0, 0}, rs{0, 0};
+    const int sm_ = ct & 127;  // threads 0..127 copy the scale of MMA row sm_
+    const int sti = R == 1 ? sm_ >> 4 : sm_ >> 5, sr = R == 1 ? 0 : (sm_ >> 4) & 1, srow = sm_ & 15;
+    const int sc_off = R * 1024 + 4 * (sr * 16 + 2 * (srow & 7) + (srow >> 3));
+    while (it.next(o, g0, ng)) {
+      if (!dead && !tc_wait(&S.raw_full[s], ph, a.err)) dead = true;
+      const unsigned char* st = raw + (size_t)s * kTcStageBytes;
+      for (int gj = 0; gj < ng; gj++) {
+        if (!dead && !tc_wait(&S.a_empty[ra.slot], ra.ph ^ 1, a.err)) dead = true;
+        unsigned char* A = abuf + (size_t)ra.slot * kTcABytes;
+        // 512 pieces of 16 B (block, part, row half, lane): words t, 4+t,
+        // 8+t, 12+t of MMA row m; word w goes to k chunk w / 2, half w & 1
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+          const int pc = ct + 256 * j;
+          const int pl = pc & 31, h = (pc >> 5) & 1, rest = pc >> 6;
+          const int ti = R == 1 ? rest : rest >> 1, r = R == 1 ? 0 : rest & 1;
+          const int m = R == 1 ? 16 * ti + 8 * h + (pl >> 2) : 32 * ti + 16 * r + 8 * h + (pl >> 2);
+          const int t = pl & 3;
+          const uint4 v = *reinterpret_cast<const uint4*>(
+              st + (gj * TPO + ti) * blk + r * 1024 + h * 512 + pl * 16);
+          unsigned char* rowp = A + (m >> 3) * 128 + (m & 7) * 16 + (t & 1) * 8;
+          const int kc = t >> 1;
+          *reinterpret_cast<uint2*>(rowp + (kc + 0) * 2048) = a_bytes(v.x);
+          *reinterpret_cast<uint2*>(rowp + (kc + 2) * 2048) = a_bytes(v.y);
+          *reinterpret_cast<uint2*>(rowp + (kc + 4) * 2048) = a_bytes(v.z);
+          *reinterpret_cast<uint2*>(rowp + (kc + 6) * 2048) = a_bytes(v.w);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.a_full[ra.slot]);
+        // the group scale of MMA row ct, for the epilogue
+        if (!dead && !tc_wait(&S.sc_empty[rs.slot], rs.ph ^ 1, a.err)) dead = true;
+        if (ct < 128)
+          S.scale[rs.slot][ct] = *reinterpret_cast<const float*>(st + (gj * TPO + sti) * blk + sc_off);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.sc_full[rs.slot]);
+        rs.adv(kTcSc);
+        ra.adv(kTcA);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.raw_empty[s]);
+      if (++s == kTcRaw) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+  } else if (warp >= kTcEpiWarp0 && warp < kTcEpiWarp0 + kTcEpiWarps) {
+    // ---------------------------------------------------- epilogue
+    if (a.pdl) pdl_wait();
+    const int sub = warp & 3, wg = (warp - kTcEpiWarp0) >> 2;
+    const int m = 32 * sub + lane;  // MMA row = TMEM lane
+    const int th = a.tpad / 2, tb = wg * th;  // this warpgroup's tokens [tb, tb + th)
+    const int ti = R == 1 ? m >> 4 : m >> 5, r = R == 1 ? 0 : (m >> 4) & 1, row = m & 15;
+    // (octet, group) of the next item
+    int o = i0 / gpr, g = i0 % gpr;
+    float acc01[TH], acc23[TH];
+    int fx[TH];  // the tokens' fixed-point exponents
+#pragma unroll
+    for (int j = 0; j < TH; j++) {
+      acc01[j] = acc23[j] = 0.f;
+      fx[j] = (j < th && tb + j < a.lanes) ? __ldcg(a.xf + tb + j) : 0;
+    }
+    const int first_o = i0 / gpr;
+    Ring rt{0, 0}, rs{0, 0};
+    for (int i = i0; i < i1; i++) {
+      const int qt = rt.slot;
+      if (!dead && !tc_wait(&S.sc_full[rs.slot], rs.ph, a.err)) dead = true;
+      const float s_m = S.scale[rs.slot][m];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.sc_empty[rs.slot]);
+      rs.adv(kTcSc);
+      if (!dead && !tc_wait(&S.acc_full[qt], rt.ph, a.err)) dead = true;
+      rt.adv(NT);
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(qt * ncol + 4 * tb);
+      // 8 tokens (32 columns) per TMEM load
+#pragma unroll
+      for (int h8 = 0; h8 < (TH + 7) / 8; h8++) {
+        if (8 * h8 >= th) break;
+        uint32_t v[32];
+        tmem_ld32(taddr + 32 * h8, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+          const int j = 8 * h8 + jj;
+          if (j >= th) break;
+          const int p01 = (int)v[4 * jj] + 256 * (int)v[4 * jj + 1];
+          const int p23 = (int)v[4 * jj + 2] + 256 * (int)v[4 * jj + 3];
+          acc01[j] = fmaf(s_m, (float)p01, acc01[j]);
+          acc23[j] = fmaf(s_m, (float)p23, acc23[j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.acc_empty[qt]);
+      const int oc = o;  // this item's octet
+      const bool oct_end = g + 1 == gpr;
+      if (++g == gpr) {
+        g = 0;
+        o++;
+      }
+      if (i + 1 != i1 && !oct_end) continue;  // octet not finished here
+      const int o_ = oc;
+      // ---- octet o done in this CTA: final or partial output
+      const int c_lo = cta_of(items, ncta, o_ * gpr);
+      const int c_hi = cta_of(items, ncta, o_ * gpr + gpr - 1);
+      float y[TH];
+#pragma unroll
+      for (int j = 0; j < TH; j++) {
+        y[j] = __fadd_rn(__fmul_rn(acc01[j], __int_as_float((127 - fx[j]) << 23)),
+                         __fmul_rn(acc23[j], __int_as_float((143 - fx[j]) << 23)));
+        acc01[j] = acc23[j] = 0.f;
+      }
+      bool fin = c_lo == c_hi;
+      if (!fin) {
+        // partial: every thread stores, the warpgroups meet, ONE thread
+        // fences and counts the arrival (a fence per thread serialises)
+        float* pp = a.part + ((size_t)c * 2 + (o_ == first_o ? 0 : 1)) * kTcMaxTok * 128;
+#pragma unroll
+        for (int j = 0; j < TH; j++)
+          if (j < th) pp[(size_t)(tb + j) * 128 + m] = y[j];
+        __syncwarp();
+        asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
+        __syncwarp();
+        if (warp == kTcEpiWarp0 && lane == 0) {
+          __threadfence();
+          const bool last = atomicAdd(a.counters + o_, 1u) == (unsigned)(c_hi - c_lo);
+          if (last) {
+            __threadfence();
+            a.counters[o_] = 0u;  // for the next launch
+          }
+          S.last = last;
+        }
+        __syncwarp();
+        asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
+        fin = S.last != 0;
+        if (fin) {  // sum the partials in CTA order, four CTAs' loads in flight at a time
+#pragma unroll
+          for (int j = 0; j < TH; j++) y[j] = 0.f;
+          for (int cc = c_lo; cc <= c_hi; cc += 4) {
+            float pv[4][TH];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+              const int c2 = cc + u;
+              const float* qp = nullptr;
+              if (c2 <= c_hi) {
+                const int cfirst = item_lo(items, ncta, c2) / gpr;
+                qp = a.part + ((size_t)c2 * 2 + (o_ == cfirst ? 0 : 1)) * kTcMaxTok * 128;
+              }
+#pragma unroll
+              for (int j = 0; j < TH; j++)
+                pv[u][j] = (qp && j < th) ? __ldcg(qp + (size_t)(tb + j) * 128 + m) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+              for (int j = 0; j < TH; j++)
+                if (cc + u <= c_hi) y[j] = __fadd_rn(y[j], pv[u][j]);
+          }
+        }
+        asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");  // S.last reuse
+      }
+      if (!fin) continue;
+      const int n = 16 * (o_ * TPO + ti) + row;
+#pragma unroll
+      for (int j = 0; j < TH; j++) {
+        const float up = __shfl_down_sync(0xffffffffu, y[j], 16);  // R = 2: the up row
+        const int t = tb + j;
+        if (j >= th || t >= a.lanes || n >= a.N) continue;
+        if (R == 2 && r == 1) continue;
+        tc_store(a, t, n, y[j], up);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kTcMmaWarp) tmem_free(tmem, kTcTmemCols);
+}
+
+// The tc layout: the stream-layout blocks regrouped octet-major, group-next,
+// tile-minor ([octet][group][tile of the octet][block]), so that a stage
+// (an octet's run of groups) is one contiguous range; tiles past the matrix
+// in the last octet are zero blocks.
+size_t q4_tc_bytes(int N, int K, int R) {
+  const int tiles = (N + 15) / 16, TPO = 8 / R, octets = (tiles + TPO - 1) / TPO;
+  return (size_t)octets * TPO * (K / kGroup) * q4_block_bytes(R);
+}
+
+__global__ void q4_stream_to_tc_kernel(const uint4* __restrict__ ws, int tiles, int gpr, int TPO,
+                                       int blk16, uint4* __restrict__ out, long long n16) {
+  for (long long u = (long long)blockIdx.x * blockDim.x + threadIdx.x; u < n16;
+       u += (long long)gridDim.x * blockDim.x) {
+    const long long b = u / blk16;  // output block: (octet, group, tile in octet)
+    const int w = (int)(u % blk16);
+    const int i = (int)(b % TPO);
+    const long long og = b / TPO;
+    const int g = (int)(og % gpr);
+    const int tile = (int)(og / gpr) * TPO + i;
+    out[u] = tile < tiles ? ws[((long long)tile * gpr + g) * blk16 + w] : make_uint4(0, 0, 0, 0);
+  }
+}
+
+void q4_stream_to_tc(const unsigned char* ws, int N, int K, int R, unsigned char* out, cudaStream_t st) {
+  const int tiles = (N + 15) / 16, TPO = 8 / R, blk16 = q4_block_bytes(R) / 16;
+  const long long n16 = (long long)q4_tc_bytes(N, K, R) / 16;
+  q4_stream_to_tc_kernel<<<(unsigned)std::min<long long>((n16 + 255) / 256, 148 * 16), 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(ws), tiles, K / kGroup, TPO, blk16, reinterpret_cast<uint4*>(out), n16);
+}
+
+size_t gemv_q4_tc_part_bytes() { return (size_t)2 * 148 * 2 * kTcMaxTok * 128 * sizeof(float); }
+int gemv_q4_tc_max_octets() { return 4096; }
+
+void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const BatchPlanes& xp,
+                const BatchEpi& be, float* part, unsigned* counters, int* err, cudaStream_t st,
+                bool pdl) {
+  TcArgs a = {};
+  a.ws = ws;
+  a.N = N;
+  a.K = K;
+  a.R = R;
+  a.lanes = lanes;
+  a.tpad = xp.tc_tpad;
+  a.xtc = static_cast<const unsigned char*>(xp.xtc);
+  a.xf = xp.xf;
+  a.be = be;
+  a.part = part;
+  a.counters = counters;
+  a.err = err;
+  a.pdl = pdl;
+  const int gpr = K / kGroup, tiles = (N + 15) / 16, octets = (tiles + 8 / R - 1) / (8 / R);
+  const int items = octets * gpr;
+  // at most two CTAs per octet: a split octet costs a fence, an atomic and
+  // the partial-sum reads of its last CTA
+  const int ncta = std::min(std::min(sm_count(), 2 * octets), items);
+  const size_t smem = (size_t)kTcRaw * kTcStageBytes + (size_t)kTcA * kTcABytes + (size_t)kTcB * kTcBBytes;
+  void (*kern)(TcArgs) = a.tpad <= 16 ? gemv_q4_tc_kernel<8> : gemv_q4_tc_kernel<16>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ncta);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+}  // namespace eg

@@ -43,6 +43,25 @@ def gemv_q4_stream(x, ws, N, K, y, err, bias=None, pdl=False, stream=None):
                                          int(pdl), _st(stream)))
 
 
+def q4_tc_bytes(N, K, R=1):
+    """Bytes of the tensor-core (octet-major) layout of an int4 matrix."""
+    import ctypes as C
+    n = C.c_uint64(0)
+    L.check(L.lib().eg_op_q4_tc_bytes(N, K, R, C.byref(n)))
+    return int(n.value)
+
+
+def q4_stream_to_tc(ws, N, K, out, R=1, stream=None):
+    """Regroup a stream-layout matrix into the tensor-core layout, once."""
+    L.check(L.lib().eg_op_q4_stream_to_tc(L.ptr(ws), N, K, R, L.ptr(out), _st(stream)))
+
+
+def gemm_q4_stream(x, T, ws, N, K, y, bias=None, accumulate=False, use_tc=True, stream=None):
+    """GEMM4 / GEMM4_ADD_T over a stream-layout matrix: y[t] (+)= W x[t]."""
+    L.check(L.lib().eg_op_gemm_q4_stream(L.ptr(x), T, L.ptr(ws), L.ptr(bias), N, K, L.ptr(y),
+                                         int(accumulate), int(use_tc), _st(stream)))
+
+
 def gate_up_silu(x, w, scale, N, K, y, stream=None):
     L.check(L.lib().eg_op_gate_up_silu(L.ptr(x), L.ptr(w), L.ptr(scale), N, K, L.ptr(y), _st(stream)))
 
