@@ -413,12 +413,21 @@ def run_ours(args, ws, rank, local):
 BATCH_METRIC = "batched LoRA decode tok/s summed over 16 sequences (configs[4])"
 
 
-def run_batch16(args, local):
+def shard_sequences(total: int, rank: int, ws: int) -> list[int]:
+    """The sequences rank `rank` of `ws` decodes: contiguous, every sequence
+    on exactly one rank, sizes differing by at most one."""
+    return list(range(total * rank // ws, total * (rank + 1) // ws))
+
+
+def run_batch16(args, ws, rank, local):
     """16 sequences, each prefilled to 512 ids, then 64 sampled
     steps (top-k 40, T 0.7) with a rank-8 adapter (alpha 16) on all 252
-    projections, hot-swapped for a second adapter at step 32.  Timed through
-    the public API (eg_batch_sample: r uniforms in, ids out) with CUDA events
-    on the runtime's stream; the prefill (511 batched steps) is the warm-up."""
+    projections, hot-swapped for a second adapter at step 32.  Under
+    torchrun the 16 sequences shard over the ranks (16 / N each, weights
+    replicated, no collective): strong scaling, value = 16 x 64 tokens /
+    the slowest rank's time.  Timed through the public API (eg_batch_sample:
+    r uniforms in, ids out) with CUDA events on the runtime's stream; the
+    prefill (511 batched steps) is the warm-up."""
     import numpy as np
     import torch
 
@@ -428,7 +437,9 @@ def run_batch16(args, local):
     cfg = E.QWEN25_3B
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    n, n_prompt, steps, k, temp = 16, 512, 64, 40, 0.7
+    total, n_prompt, steps, k, temp = 16, 512, 64, 40, 0.7
+    mine = shard_sequences(total, rank, ws)
+    n = len(mine)
     rt = E.QwenB200(cfg, {"maxCtx": n_prompt + steps + 8, "useF16": True,
                           "device": local}).build("synthetic", seed=SEED)
     a1 = E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16)
@@ -436,9 +447,9 @@ def run_batch16(args, local):
     rt.setLora(a1)
     rt.seqInit(n, n_prompt + steps + 2)
     slots = list(range(n))
-    for sl in slots:
-        rt.seqSetPrompt(sl, synth_ids(n_prompt, 0xE6B00100 + sl, cfg["vocabSize"]))
-    r = np.array([[synth_uniform(1, 0xE6B00200 ^ sl ^ t)[0] for sl in slots] for t in range(steps)],
+    for sl, g in zip(slots, mine):
+        rt.seqSetPrompt(sl, synth_ids(n_prompt, 0xE6B00100 + g, cfg["vocabSize"]))
+    r = np.array([[synth_uniform(1, 0xE6B00200 ^ g ^ t)[0] for g in mine] for t in range(steps)],
                  np.float32)
     st = torch.cuda.ExternalStream(rt.stream, device=dev)
     torch.cuda.synchronize()
@@ -446,6 +457,9 @@ def run_batch16(args, local):
     rt.batchDecode(slots, n_prompt - 1)  # prefill: warm-up, untimed
     prefill_s = time.perf_counter() - t0
     torch.cuda.synchronize()
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as ck:
         t0 = time.perf_counter()
@@ -456,37 +470,38 @@ def run_batch16(args, local):
         e1.record(st)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
-    ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(e0.elapsed_time(e1), ws, dev)
+    wall = max_over_ranks(wall * 1000.0, ws, dev) / 1000.0
     launches = rt.lastDispatchCount * steps
     weights, kv_per_pos = cfg_bytes(cfg)
     lora_bytes = 1662976 * cfg["numLayers"]
     step_bytes = weights + n * kv_per_pos * (n_prompt + steps / 2) + lora_bytes
     hbm, peak_kind = peaks()
-    value = n * steps / (ms / 1000.0)
+    value = total * steps / (ms / 1000.0)
     achieved = step_bytes * steps / (ms / 1000.0) / 1e9
     assert out1.shape == (steps // 2, n) and out2.shape == (steps - steps // 2, n)
     a1.destroy()
     a2.destroy()
     return {
-        "metric": BATCH_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": 1,
+        "metric": BATCH_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": ws,
         "steps": steps, "warmup": n_prompt - 1, "ms_per_step": round(ms / steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4xf32",
-        "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None,
+        "dtype": "int4xf32", "data": "synthetic",
         "config": {"workload": "configs[4]: 16 sequences x (prefill 512 + 64 sampled steps), "
                                "rank-8 LoRA on 252 projections, hot swap at step 32, top-k 40, T 0.7",
                    "kv": "f16", "lm_head": "int8 rows",
                    "l2": "inputs larger than L2 (1.79 GB of weights streamed per step)",
-                   "parallelism": "single GPU"},
-        "roofline": {"bound": "hbm", "kernel": "whole batched step (weights once + 16 KV caches "
-                                               "+ LoRA A/B)",
+                   "parallelism": f"{n} sequences per GPU x {ws} GPUs (replicated weights)"},
+        "roofline": {"bound": "hbm", "kernel": "whole batched step per GPU (weights once + its "
+                                               "KV caches + LoRA A/B)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                      "bytes_per_launch": int(step_bytes), "traffic": None},
         "prefill": {"steps": n_prompt - 1, "s": round(prefill_s, 3),
                     "tok_s": round(n * (n_prompt - 1) / prefill_s, 1)},
-        "e2e": {"value": round(n * steps / wall, 2), "unit": "tok/s",
-                "h2d_bytes_per_step": n * 4, "d2h_bytes_per_step": n * 4,
-                "what": "batchSample x2 (r uniforms H2D, ids D2H) + setLora, wall clock"},
+        "e2e": {"value": round(total * steps / wall, 2), "unit": "tok/s",
+                "h2d_bytes_per_step": total * 4, "d2h_bytes_per_step": total * 4,
+                "what": "batchSample x2 (r uniforms H2D, ids D2H) + setLora, wall clock, max over ranks"},
         "gpu_launches": launches,
         "clocks": ck.summary(),
     }
@@ -669,10 +684,17 @@ def main():
             return
         print(json.dumps(run_reference(args, ws, rank)), flush=True)
         return
-    if args.workload in ("batch16", "prefill"):
+    if args.workload == "batch16":
+        res = run_batch16(args, ws, rank, local)
         if rank == 0:
-            run = run_batch16 if args.workload == "batch16" else run_prefill
-            print(json.dumps(run(args, local)), flush=True)
+            print(json.dumps(res), flush=True)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    if args.workload == "prefill":
+        if rank == 0:
+            print(json.dumps(run_prefill(args, local)), flush=True)
         return
     res = run_ours(args, ws, rank, local)
     if rank == 0:

@@ -51,3 +51,10 @@ def test_positions_cycle_inside_the_window():
     assert sum(k for _, k in got) == 300
     for p, k in got:
         assert 32 <= p and p + k <= 32 + 128
+
+
+@pytest.mark.parametrize("ws", [1, 2, 4, 8, 3])
+def test_batch16_sequences_shard_once(ws):
+    got = [bench.shard_sequences(16, r, ws) for r in range(ws)]
+    assert sum(got, []) == list(range(16))
+    assert max(map(len, got)) - min(map(len, got)) <= 1

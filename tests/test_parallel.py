@@ -30,6 +30,21 @@ def test_merge_order_ties_and_nan():
     assert P.merge_argmax([-2.0, -1.0], [0, 100]) == (-1.0, 100)
 
 
+def test_merge_topk_is_the_global_topk_order():
+    rng = np.random.default_rng(3)
+    logits = rng.standard_normal(3000).astype(np.float32).round(1)  # many ties
+    world, k = 3, 40
+    vals, ids = [], []
+    for r in range(world):
+        r0, r1 = P.vocab_slice(len(logits), r, world)
+        order = sorted(range(r0, r1), key=lambda i: (-logits[i], i))[:k]
+        vals.append([logits[i] for i in order])
+        ids.append(order)
+    got_v, got_i = P.merge_topk(vals, ids, k)
+    want = sorted(range(len(logits)), key=lambda i: (-logits[i], i))[:k]
+    assert got_i == want and got_v == [logits[i] for i in want]
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -60,6 +75,82 @@ def test_gather_merge_gloo_matches_global_argmax(tmp_path):
     mp.spawn(_rank, args=(ws, _free_port(), logits, str(tmp_path)), nprocs=ws, join=True)
     for r in range(ws):
         assert int((tmp_path / f"rank{r}").read_text()) == 123
+
+
+def _rank_topk(rank, ws, port, logits, k, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        r0, r1 = P.vocab_slice(len(logits), rank, ws)
+        order = sorted(range(r0, r1), key=lambda i: (-logits[i], i))[:k]
+        v = torch.tensor([logits[i] for i in order], dtype=torch.float32)
+        i = torch.tensor(order, dtype=torch.int32)
+        gv = [torch.empty_like(v) for _ in range(ws)]
+        gi = [torch.empty_like(i) for _ in range(ws)]
+        dist.all_gather(gv, v)
+        dist.all_gather(gi, i)
+        _, mi = P.merge_topk([g.tolist() for g in gv], [g.tolist() for g in gi], k)
+        with open(os.path.join(outdir, f"rank{rank}"), "w") as f:
+            f.write(",".join(map(str, mi)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_topk_all_gather_merge_gloo(tmp_path):
+    """k = 40 candidates per rank, all-gathered over two gloo ranks, merge to
+    the global TOPK_SELECT order on every rank (ties across the slice
+    boundary go to the lower id)."""
+    rng = np.random.default_rng(11)
+    logits = rng.standard_normal(2000).astype(np.float32).round(1)
+    ws, k = 2, 40
+    mp.spawn(_rank_topk, args=(ws, _free_port(), logits, k, str(tmp_path)), nprocs=ws, join=True)
+    want = sorted(range(len(logits)), key=lambda i: (-logits[i], i))[:k]
+    for r in range(ws):
+        assert [int(x) for x in (tmp_path / f"rank{r}").read_text().split(",")] == want
+
+
+@pytest.mark.gpu
+def test_lm_head_shards_topk_sample_equal_single_gpu(cuda):
+    """Three shards of the LM head on one GPU (as three ranks would run them):
+    local TOPK_SELECT with global ids, concatenation in rank order, the
+    device merge and SAMPLE_TOPK give the single-GPU topKLogits(40) and
+    sampleToken for several r."""
+    import ctypes as C
+
+    import vibethinker_webgpu_lora_b200 as E
+    from vibethinker_webgpu_lora_b200 import _lib as L
+    from vibethinker_webgpu_lora_b200 import kernels as K
+    from vibethinker_webgpu_lora_b200.config import small_config
+    from oracle import oracle as O
+
+    cfg = small_config(layers=2, vocab=5000)
+    rt = E.QwenB200(cfg, {"maxCtx": 64}).build("synthetic", seed=0xE6B00000)
+    for t, tok in enumerate(O.token_ids(6, 5, cfg["vocabSize"])):
+        rt.token(int(tok), t)
+    want = rt.topKLogits(40)
+    hidden = torch.from_numpy(rt.readHidden()).to(cuda)
+    cv, ci = [], []
+    for rank in range(3):
+        r0, r1 = P.vocab_slice(cfg["vocabSize"], rank, 3)
+        lg = torch.empty(r1 - r0, device=cuda)
+        v = torch.empty(1, device=cuda)
+        i = torch.empty(1, dtype=torch.int32, device=cuda)
+        L.check(L.lib().eg_lm_head_shard(rt.handle, C.c_void_p(hidden.data_ptr()), r0, r1 - r0,
+                                         C.c_void_p(lg.data_ptr()), C.c_void_p(v.data_ptr()),
+                                         C.c_void_p(i.data_ptr()), None))
+        ids = torch.empty(40, dtype=torch.int32, device=cuda)
+        vals = torch.empty(40, device=cuda)
+        K.topk(lg, r1 - r0, 40, ids, vals)
+        cv.append(vals)
+        ci.append(ids + r0)
+    mids, mvals = P.topk_merge_device(torch.cat(cv), torch.cat(ci), 40)
+    torch.cuda.synchronize()
+    assert mids.cpu().tolist() == [w["id"] for w in want]
+    assert mvals.cpu().tolist() == [w["logit"] for w in want]
+    out = torch.empty(1, dtype=torch.int32, device=cuda)
+    for r in (0.0, 0.3, 0.77, 1.0):
+        K.sample_topk(mids, mvals, 40, 0.7, r, out)
+        assert int(out.item()) == rt.sampleToken(0.7, r)
 
 
 @pytest.mark.gpu

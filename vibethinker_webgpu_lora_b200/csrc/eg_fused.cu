@@ -13,9 +13,9 @@
 // it never waits for a grid barrier: HBM keeps streaming the next phases'
 // weights while the consumers wait at a barrier, stage activations or run
 // attention.  At the end of a GEMV phase the epilogue warp, once its last
-// tile's outputs are written and fenced, bumps a shared-memory phase count;
-// consumer thread 0 waits for it, then arrives at the grid barrier
-// (red.release.gpu) and polls it (ld.acquire.gpu).  Activations written before a barrier are read after it
+// tile's outputs are written, arrives at the grid barrier itself with one
+// release reduction (red.release.gpu, no separate fence); consumer thread 0
+// polls it (ld.acquire.gpu).  Activations written before a barrier are read after it
 // with ld.global.cg, so no stale L1 line is seen inside the launch.  After
 // the LM head every CTA reduces the CTAs' argmax candidates itself, so the
 // next token's embedding needs no further barrier.  Every wait is bounded:
@@ -91,33 +91,24 @@ __device__ __forceinline__ Run run_lm(const FusedArgs& a) {
 
 // ---------------------------------------------------------------- barrier
 // Monotonic arrival counter: the k-th barrier completes when the counter
-// reaches k * gridDim.x.  Called by all consumer threads; thread 0 first
-// waits until the epilogue warp has finished this phase (`epi`: its
-// monotonic count of finished phases reaches pdone + 1; a count, not an
-// mbarrier phase, because a CTA without tiles in a phase lets the epilogue
-// warp finish two phases back to back), then arrives and polls.  Returns
-// false, uniformly, when the launch is being abandoned.
-__device__ bool phase_barrier(const FusedArgs& a, unsigned& epoch, const int* epi_done,
-                              int& pdone, bool epi, int* s_ok, int prof_ph) {
+// reaches k * gridDim.x, one arrival per CTA and phase.  Called by all
+// consumer threads; in a GEMV phase (`epi`) the CTA's epilogue warp has
+// arrived (epi_arrive), otherwise thread 0 arrives; thread 0 polls, then
+// publishes the passed phase count for the epilogue warp.  Returns false,
+// uniformly, when the launch is being abandoned.
+__device__ bool phase_barrier(const FusedArgs& a, unsigned& epoch, volatile int* passed, bool epi,
+                              int* s_ok, int prof_ph) {
   constexpr int NT = kFusedWarps * 32;
   bar_sync_n<NT>();
   if (threadIdx.x == 0) {
     int ok = 1;
-    if (epi) {
-      pdone++;
-      const unsigned long long t0 = gtime();
-      for (long long spins = 0; *(volatile const int*)epi_done < pdone; spins++) {
-        if ((spins & 255) == 255 && (err_set(a.err) || gtime() - t0 > kBarrierTimeoutNs)) {
-          atomicExch(a.err, 1);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    if (a.prof && prof_ph >= 0) atomicMax(a.prof + 2 * prof_ph + 1, gtime());
+    if (a.prof && prof_ph >= 0 && !epi) atomicMax(a.prof + 2 * prof_ph + 1, gtime());
     epoch += 1;
     const unsigned target = epoch * gridDim.x;
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+    // GEMV phases: this CTA's epilogue warp arrived after writing its
+    // outputs; other phases (attention): thread 0 arrives for the consumers,
+    // whose writes the bar.sync above ordered before this release
+    if (!epi) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
     const unsigned long long t0 = gtime();
     for (long long spins = 0; ok; spins++) {
       unsigned v;
@@ -134,9 +125,33 @@ __device__ bool phase_barrier(const FusedArgs& a, unsigned& epoch, const int* ep
     }
     if (err_set(a.err)) ok = 0;
     *s_ok = ok;
+    *passed = (int)epoch;  // the epilogue warp may arrive for the next phase
   }
   bar_sync_n<NT>();
   return *s_ok != 0;
+}
+
+// The epilogue warp's grid-barrier arrival for launch phase q (0-based),
+// once its outputs of the phase are written: a release reduction by lane 0
+// after __syncwarp covers the whole warp's stores (no separate fence).  It
+// waits until the barrier of phase q - 1 has passed in this CTA, so a CTA
+// with no tiles in phase q cannot arrive before the others finished q - 1.
+__device__ __forceinline__ bool epi_arrive(const FusedArgs& a, volatile int* passed, int q,
+                                           int prof_ph) {
+  __syncwarp();
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    const unsigned long long t0 = gtime();
+    for (long long spins = 0; *passed < q; spins++)
+      if ((spins & 255) == 255 && (err_set(a.err) || gtime() - t0 > kBarrierTimeoutNs)) {
+        atomicExch(a.err, 1);
+        ok = false;
+        break;
+      }
+    if (a.prof && prof_ph >= 0) atomicMax(a.prof + 2 * prof_ph + 1, gtime());
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+  }
+  return __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -150,7 +165,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
   __shared__ TileRed<kFusedWarps, 1> red1;
   __shared__ TileRed<kFusedWarps, 2> red2;
   __shared__ AttnSmem asm_;
-  __shared__ int epi_done;  // phases the epilogue warp has finished
+  __shared__ int bar_passed;  // launch phases whose grid barrier this CTA passed
   __shared__ int s_ok;
   __shared__ uint32_t s_id;
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm);
@@ -170,7 +185,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
       mbar_init(&tile_full[i], kFusedWarps);
       mbar_init(&tile_free[i], 1);
     }
-    epi_done = 0;
+    bar_passed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -199,6 +214,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
   }
 
   if (warp == kFusedWarps + 1) {  // ------------------------------------ epilogue
+    int q0 = 0;  // launch phase index of this token's first phase
     for (int tok = 0; tok < a.n_tokens; tok++) {
       for (int li = 0; li < L; li++) {
         const FusedLayer& l = a.layers[li];
@@ -227,9 +243,8 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
             ok = epilogue_q4_run<kFusedWarps, 1>(e, r.t_lo, r.t_hi, red1, tile_full, tile_free, tj, false, a.err);
           }
           if (!ok) return;
-          __threadfence();  // the phase's outputs are visible GPU-wide ...
-          __syncwarp();
-          if (lane == 0) atomicAdd(&epi_done, 1);  // ... before the count moves
+          const int q = q0 + 5 * li + ph;
+          if (!epi_arrive(a, &bar_passed, q, tok == 0 ? 5 * li + ph : -1)) return;
         }
       }
       if (lm_runs(a, tok)) {
@@ -243,17 +258,15 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
           a.cand_v[blockIdx.x] = bv;
           a.cand_i[blockIdx.x] = bi;
         }
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) atomicAdd(&epi_done, 1);
+        if (!epi_arrive(a, &bar_passed, q0 + 5 * L, tok == 0 ? 5 * L : -1)) return;
       }
+      q0 += 5 * L + (lm_runs(a, tok) ? 1 : 0);
     }
     return;
   }
 
   // -------------------------------------------------------------- consumers
   unsigned epoch = 0;
-  int pdone = 0;
   bool dead = false;
   uint2* xb = reinterpret_cast<uint2*>(xreg);
   // the first input token is ids[start_pos]; later ones come from the
@@ -292,7 +305,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
                             xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
-      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb : -1)) return;
+      if (!phase_barrier(a, epoch, &bar_passed, true, &s_ok, tok == 0 ? pb : -1)) return;
       // ---- attention: RoPE, KV append, split partials, merge
       if (prof0) a.prof[2 * (pb + 1)] = gtime();
       {
@@ -317,7 +330,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         at.counters = a.attn_counters;
         attn_run<KVT>(at, blockIdx.x, gridDim.x, 0, asm_);
       }
-      if (!phase_barrier(a, epoch, &epi_done, pdone, false, &s_ok, tok == 0 ? pb + 1 : -1)) return;
+      if (!phase_barrier(a, epoch, &bar_passed, false, &s_ok, tok == 0 ? pb + 1 : -1)) return;
       // ---- O projection + residual
       if (prof0) a.prof[2 * (pb + 2)] = gtime();
       {
@@ -334,7 +347,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
                             xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
-      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 2 : -1)) return;
+      if (!phase_barrier(a, epoch, &bar_passed, true, &s_ok, tok == 0 ? pb + 2 : -1)) return;
       // ---- gate/up + SiLU
       if (prof0) a.prof[2 * (pb + 3)] = gtime();
       {
@@ -354,7 +367,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
                             xb, xcor, xf, red2, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
-      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 3 : -1)) return;
+      if (!phase_barrier(a, epoch, &bar_passed, true, &s_ok, tok == 0 ? pb + 3 : -1)) return;
       // ---- down projection + residual
       if (prof0) a.prof[2 * (pb + 4)] = gtime();
       {
@@ -371,7 +384,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
                             xb, xcor, xf, red1, tile_full, tile_free, rp, tj, dead, a.err);
         }
       }
-      if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pb + 4 : -1)) return;
+      if (!phase_barrier(a, epoch, &bar_passed, true, &s_ok, tok == 0 ? pb + 4 : -1)) return;
     }
     // ---- LM head (int8) + argmax + token advance
     if (!lm_runs(a, tok)) {
@@ -396,7 +409,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
                        xm8, red1, tile_full, tile_free, rp, tj, dead, a.err);
       }
     }
-    if (!phase_barrier(a, epoch, &epi_done, pdone, true, &s_ok, tok == 0 ? pl : -1)) return;
+    if (!phase_barrier(a, epoch, &bar_passed, true, &s_ok, tok == 0 ? pl : -1)) return;
     if (a.greedy) {
       // every CTA merges the candidates (ARGMAX, kernels.js:771-784); ties
       // to the lower index

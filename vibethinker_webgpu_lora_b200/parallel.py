@@ -8,7 +8,12 @@ slice of the int8 LM head and a local argmax with global ids
 (``eg_lm_head_shard``), the ranks all-gather their (value, id) pairs and each
 merges them with the reference's selection order -- larger value first, ties
 to the lower id (ARGMAX, kernels.js:771-784) -- which reproduces the
-single-GPU argmax exactly.
+single-GPU argmax exactly.  Sampling (top-k, temperature, r) splits the
+same way: each rank selects its slice's top k with global ids, the ranks
+all-gather the k (value, id) pairs, the concatenation (rank order) is
+reduced to the global top k by the TOPK_SELECT kernel itself -- rank slices
+are ordered by id, so "lower position" is "lower id" among equal values --
+and every rank runs SAMPLE_TOPK with the shared r (runtime.js:1648-1732).
 """
 from __future__ import annotations
 
@@ -52,6 +57,29 @@ def gather_merge(best_val: torch.Tensor, best_id: torch.Tensor, group=None) -> t
     return merge_argmax([o[0].item() for o in out], [o[1].item() for o in out])
 
 
+def merge_topk(vals_per_rank, ids_per_rank, k: int):
+    """The global top-k of the ranks' candidate lists in the reference's
+    TOPK_SELECT order (value descending, ties to the lower id, NaN and values
+    at or below -1e30 never taken), as (values, ids).  Host restatement of the
+    device merge, for tests."""
+    cand = [(float(v), int(i)) for vs, iz in zip(vals_per_rank, ids_per_rank)
+            for v, i in zip(vs, iz) if v == v and float(v) > -1e30]
+    cand.sort(key=lambda p: (-p[0], p[1]))
+    cand = cand[:k]
+    return [c[0] for c in cand], [c[1] for c in cand]
+
+
+def topk_merge_device(cat_vals: torch.Tensor, cat_ids: torch.Tensor, k: int, stream=None):
+    """Global top-k of the concatenated per-rank candidate lists (each list in
+    TOPK_SELECT order, lists in rank = vocabulary order) with the library's
+    TOPK_SELECT kernel: returns (ids, vals) device tensors of length k."""
+    from . import kernels as K
+    pos = torch.empty(k, dtype=torch.int32, device=cat_vals.device)
+    vals = torch.empty(k, dtype=torch.float32, device=cat_vals.device)
+    K.topk(cat_vals, int(cat_vals.numel()), k, pos, vals, stream=stream)
+    return cat_ids[pos.long()], vals
+
+
 class VocabSplitLmHead:
     """The vocab-split LM head of one stream over the ranks of `group`; `rt`
     is this rank's QwenB200 (the full model, built the same way everywhere)."""
@@ -82,6 +110,37 @@ class VocabSplitLmHead:
             None, C.c_void_p(self.val.data_ptr()), C.c_void_p(self.idx.data_ptr()),
             C.c_void_p(stream)))
         return gather_merge(self.val, self.idx, self.group)[1]
+
+    def sample(self, k: int, temp: float, r: float, hidden: torch.Tensor | None = None,
+               src: int = 0) -> int:
+        """sampleToken(temp, r) of the stream (topKLogits(k) + SAMPLE_TOPK,
+        runtime.js:1648-1732) over the vocab-split head: every rank returns
+        the same id."""
+        from . import kernels as K
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(self.rt_stream)
+        if self.rank == src and hidden is not None:
+            self.hidden.copy_(hidden)
+        dist.broadcast(self.hidden, src=src, group=self.group)
+        rows = self.r1 - self.r0
+        if not hasattr(self, "logits") or self.logits.numel() != rows:
+            self.logits = torch.empty(rows, dtype=torch.float32, device=self.hidden.device)
+        L.check(L.lib().eg_lm_head_shard(
+            self.rt.handle, C.c_void_p(self.hidden.data_ptr()), self.r0, rows,
+            C.c_void_p(self.logits.data_ptr()), C.c_void_p(self.val.data_ptr()),
+            C.c_void_p(self.idx.data_ptr()), C.c_void_p(cur.cuda_stream)))
+        ids = torch.empty(k, dtype=torch.int32, device=self.hidden.device)
+        vals = torch.empty(k, dtype=torch.float32, device=self.hidden.device)
+        K.topk(self.logits, rows, k, ids, vals)
+        ids += self.r0  # global ids
+        gv = [torch.empty_like(vals) for _ in range(self.world)]
+        gi = [torch.empty_like(ids) for _ in range(self.world)]
+        dist.all_gather(gv, vals, group=self.group)
+        dist.all_gather(gi, ids, group=self.group)
+        mids, mvals = topk_merge_device(torch.cat(gv), torch.cat(gi), k)
+        out = torch.empty(1, dtype=torch.int32, device=self.hidden.device)
+        K.sample_topk(mids, mvals, k, temp, r, out)
+        return int(out.item())
 
 
 def measure(steps: int = 200, warmup: int = 20) -> dict | None:
