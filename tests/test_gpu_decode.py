@@ -146,6 +146,18 @@ def test_topk_sample_api(cuda):
     assert t == O.sample_topk(rid, rv, 40, 0.7, 0.3)
 
 
+def test_topk_readback_small_max_ctx(cuda):
+    """topKLogits(64) reads 64 ids and 64 values back through the runtime's
+    pinned staging buffer, which must hold them however small maxCtx is."""
+    cfg = small_config(layers=1, vocab=1000)
+    rt, orc = make(cfg, True, max_ctx=8)
+    rt.token(5, 0)
+    ref = orc.step(5, 0)
+    top = rt.topKLogits(64)
+    rid, _ = O.topk(ref, 64)
+    assert len(top) == 64 and [d["id"] for d in top][:16] == rid[:16].tolist()
+
+
 def test_lora_apply_swap_clear(cuda):
     cfg = small_config(layers=2, vocab=3000)
     rt, orc = make(cfg, True)

@@ -1003,7 +1003,8 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
     DALLOC(rt->d_layers, fl.size() * sizeof(FusedLayer), sb);
     CK(cudaMemcpy(rt->d_layers, fl.data(), fl.size() * sizeof(FusedLayer), cudaMemcpyHostToDevice));
   }
-  CK(cudaMallocHost(&rt->h_small, (size_t)std::max(mc, rt->o.decode_batch_capacity) * 4 + 64));
+  // ids of a decode batch / a generate call, or topk's 64 ids + 64 values
+  CK(cudaMallocHost(&rt->h_small, (size_t)std::max(std::max(mc, rt->o.decode_batch_capacity), 128) * 4 + 64));
   CK(cudaDeviceSynchronize());
   rt->finalized = true;
   return EG_OK;
