@@ -131,13 +131,15 @@ def test_gemv_q4_stream_upload_once(cuda):
     close(host(y0), ref, 2e-4, 1e-4)
 
 
-@pytest.mark.parametrize("N,Kd,T", [(2560, 2048, 16), (517, 2048, 5), (2048, 11008, 32), (128, 128, 4)])
+@pytest.mark.parametrize("N,Kd,T", [(2560, 2048, 16), (517, 2048, 5), (2048, 11008, 32), (128, 128, 4),
+                                    (2560, 2048, 33), (517, 384, 100), (2048, 2048, 300)])
 def test_gemm4_tc_and_mma_vs_oracle(cuda, N, Kd, T):
     """GEMM4 / GEMM4_ADD_T (kernels.js:389-473): T token vectors through one
     weight pass, on the tcgen05 path (tc layout) and, for T <= 16, the
     integer mma.sync path (stream layout), each row against the oracle's
     GEMV of that token; full octets, a partial last octet (N = 517) and
-    split-K octets all occur."""
+    split-K octets all occur.  More than 32 tokens run the whole-prompt mode
+    (32-token tiles, every CTA on whole octets), ragged last tiles included."""
     W = O.normal(N * Kd, 0xE6B00101 + N, 0.02).reshape(N, Kd)
     X = O.normal(T * Kd, 0xE6B00102 + T, 1.0).reshape(T, Kd)
     bias = O.normal(N, 0xE6B00103, 0.02)

@@ -14,6 +14,8 @@
 namespace eg {
 
 constexpr int kBatchMax = 16;
+// Most tokens of one whole-prompt (tcgen05) GEMM call or prefill block.
+constexpr int kPrefillMaxT = 8192;
 
 // Per-sequence state on the device.  Slot s holds its token ids
 // ids[s * slot_ctx + t], its position pos[s] (the token consumed by the next
@@ -53,7 +55,9 @@ struct BatchPlanes {
   // int4 only, optional: the same digit planes as the B operand of the
   // tcgen05 GEMV (gemv_q4_tc): per group, N = 4 tc_tpad columns (lane v,
   // plane p at column 4v + p) x 128 bytes, K-major 8 x 16-byte core
-  // matrices, the 8 k-chunks N / 8 core matrices apart.
+  // matrices, the 8 k-chunks N / 8 core matrices apart.  More lanes than
+  // tc_tpad (whole-prompt mode, tc_tpad = 32): lane v sits in token tile
+  // v / 32 at column 4 (v % 32) + p, the tiles gpr x 16 KB apart.
   void* xtc;
   int tc_tpad;
 };
@@ -71,9 +75,12 @@ struct BatchEpi {
 };
 
 // Batched int4 GEMV on the tcgen05 tensor cores (eg_tc.cu): the epilogue
-// of gemv_q4_batch for lanes <= 32 (xp.xtc staged by batch_stage_q4), R = 2
-// for GATE_UP_SILU; ws in the tc layout (q4_stream_to_tc).  part / counters: split-octet scratch
-// (gemv_q4_tc_part_bytes, counters zero between launches).
+// of gemv_q4_batch (xp.xtc staged by batch_stage_q4), R = 2 for
+// GATE_UP_SILU; ws in the tc layout (q4_stream_to_tc).  lanes <= 32: the
+// CTAs split the K groups of every octet (split-K); part / counters are the
+// split-octet scratch (gemv_q4_tc_part_bytes, counters zero between
+// launches).  lanes > 32 (whole-prompt mode, tc_tpad = 32): every CTA
+// walks whole (token tile, octet) pairs, no split, part / counters unused.
 void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const BatchPlanes& xp,
                 const BatchEpi& be, float* part, unsigned* counters, int* err, cudaStream_t st,
                 bool pdl);

@@ -2159,27 +2159,32 @@ EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, con
                                       int K, float* y, int accumulate, int use_tc, void* stream) {
   if (!x || !ws || !y || T < 1 || N <= 0 || K <= 0 || K % 128 || K > 12288)
     return fail(EG_ERR_ARG, "gemm_q4_stream: bad argument");
-  if (T > (use_tc ? 32 : kBatchMax))
-    return fail(EG_ERR_ARG, "gemm_q4_stream: at most %d tokens per call", use_tc ? 32 : kBatchMax);
+  if (T > (use_tc ? kPrefillMaxT : kBatchMax))
+    return fail(EG_ERR_ARG, "gemm_q4_stream: at most %d tokens per call", use_tc ? kPrefillMaxT : kBatchMax);
   if (accumulate && bias) return fail(EG_ERR_ARG, "gemm_q4_stream: bias with accumulate is not supported");
   if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(EG_ERR_ARG, "gemm_q4_stream: ws must be 16-byte aligned");
-  const int gpr = K / 128, tpad = (T + 3) / 4 * 4;
-  const size_t xb = (size_t)T * gpr * 512, xc = (size_t)T * gpr * 8, xtc = (size_t)gpr * 4 * tpad * 128;
+  const int gpr = K / 128, tpad = T > 32 ? 32 : (T + 3) / 4 * 4;
+  const size_t xb = (size_t)T * gpr * 512, xc = ((size_t)T * gpr * 8 + 255) / 256 * 256,
+               xtc = (size_t)((T + tpad - 1) / tpad) * gpr * 4 * tpad * 128;
   const size_t cnt = (size_t)gemv_q4_tc_max_octets() * 4, part = gemv_q4_tc_part_bytes();
+  const size_t xfb = ((size_t)T * 4 + 255) / 256 * 256;  // one exponent per token
+  // [err | xb | xcor | xf | xtc | counters | partials], every piece 256-byte aligned
+  const size_t o_xb = 256, o_xc = o_xb + xb, o_xf = o_xc + xc, o_tc = o_xf + xfb, o_cnt = o_tc + xtc,
+               o_part = o_cnt + cnt;
   void* scr = nullptr;
-  eg_status s = op_scratch(256 + xb + xc + 256 + xtc + cnt + part, &scr);
+  eg_status s = op_scratch(o_part + part, &scr);
   if (s) return s;
   char* b = static_cast<char*>(scr);
   int* err = reinterpret_cast<int*>(b);
   BatchPlanes xp = {};
-  xp.xb = b + 256;
-  xp.xcor = reinterpret_cast<int*>(b + 256 + xb);
-  xp.xf = reinterpret_cast<int*>(b + 256 + xb + xc);
+  xp.xb = b + o_xb;
+  xp.xcor = reinterpret_cast<int*>(b + o_xc);
+  xp.xf = reinterpret_cast<int*>(b + o_xf);
   xp.gpr_max = gpr;
-  xp.xtc = use_tc ? b + 512 + xb + xc : nullptr;
+  xp.xtc = use_tc ? b + o_tc : nullptr;
   xp.tc_tpad = tpad;
-  unsigned* counters = reinterpret_cast<unsigned*>(b + 512 + xb + xc + xtc);
-  float* prt = reinterpret_cast<float*>(b + 512 + xb + xc + xtc + cnt);
+  unsigned* counters = reinterpret_cast<unsigned*>(b + o_cnt);
+  float* prt = reinterpret_cast<float*>(b + o_part);
   CK(cudaMemsetAsync(err, 0, 4, OPSTREAM));
   if (use_tc) CK(cudaMemsetAsync(counters, 0, cnt, OPSTREAM));
   BatchSrc src = {};

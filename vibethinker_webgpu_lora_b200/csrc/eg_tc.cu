@@ -63,8 +63,13 @@ constexpr uint32_t kTcTmemCols = 256;
 
 struct TcArgs {
   const unsigned char* ws;   // tc layout (q4_stream_to_tc)
-  int N, K, R, lanes, tpad;
-  const unsigned char* xtc;  // B planes, per group N x 128 bytes (BatchPlanes::xtc)
+  int N, K, R, lanes, tpad;  // lanes: token vectors; tpad: tokens per B tile (<= 32)
+  // 0: the CTAs split the (octet, group) items of one token tile evenly
+  // (split-K where a CTA boundary falls inside an octet); 1: whole prompt,
+  // ceil(lanes / 32) token tiles, each CTA takes whole (token tile, octet)
+  // pairs (every group), so no octet is split
+  int whole;
+  const unsigned char* xtc;  // B planes: per (token tile, group) 4 tpad x 128 bytes
   const int* xf;             // [lane] fixed-point exponent
   BatchEpi be;
   float* part;               // [ncta][2][32][128]
@@ -94,21 +99,41 @@ __device__ __forceinline__ int cta_of(int items, int ncta, int i) {
   return c;
 }
 
-// Stages of this CTA's item range: (octet, first group, group count) in order.
-struct StageIter {
-  int i, hi, gpr, o, g;  // next item i = (octet o, group g)
-  __device__ StageIter(int lo, int hi_, int gpr_) : i(lo), hi(hi_), gpr(gpr_), o(lo / gpr_), g(lo % gpr_) {}
-  __device__ bool next(int& oo, int& g0, int& ng) {
-    if (i >= hi) return false;
-    oo = o;
-    g0 = g;
-    ng = min(kTcGroupsPerStage, min(hi - i, gpr - g));
-    i += ng;
-    g += ng;
-    if (g == gpr) {
-      g = 0;
-      o++;
+// One run of a CTA: token tile tau, octet o, groups [g0, g1).
+struct Seg {
+  int tau, o, g0, g1;
+};
+
+// The CTA's runs in order, the same sequence for every warp role.
+struct SegIter {
+  int whole, gpr, octets;
+  int i, i1;             // split mode: next item, end
+  int pr, step, npairs;  // whole mode: next (token tile, octet) pair
+  __device__ SegIter(const TcArgs& a, int gpr_, int octets_) : whole(a.whole), gpr(gpr_), octets(octets_) {
+    const int items = octets * gpr;
+    i = item_lo(items, gridDim.x, blockIdx.x);
+    i1 = item_lo(items, gridDim.x, blockIdx.x + 1);
+    pr = blockIdx.x;
+    step = gridDim.x;
+    npairs = ((a.lanes + 31) / 32) * octets;
+  }
+  __device__ bool next(Seg& sg) {
+    if (whole) {  // octet-major: CTAs running at once share an octet's weights in L2
+      if (pr >= npairs) return false;
+      const int ntau = npairs / octets;
+      sg.o = pr / ntau;
+      sg.tau = pr % ntau;
+      sg.g0 = 0;
+      sg.g1 = gpr;
+      pr += step;
+      return true;
     }
+    if (i >= i1) return false;
+    sg.tau = 0;
+    sg.o = i / gpr;
+    sg.g0 = i % gpr;
+    sg.g1 = min(gpr, sg.g0 + (i1 - i));
+    i += sg.g1 - sg.g0;
     return true;
   }
 };
@@ -168,7 +193,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
   const int gpr = a.K / kGroup, tiles = (a.N + 15) / 16, octets = (tiles + TPO - 1) / TPO;
   const int items = octets * gpr;
   const int ncta = gridDim.x, c = blockIdx.x;
-  const int i0 = item_lo(items, ncta, c), i1 = item_lo(items, ncta, c + 1);
   const int ncol = 4 * a.tpad;
   const int NT = min(4, (int)kTcTmemCols / ncol);  // TMEM accumulator slots
   const uint32_t bbytes = (uint32_t)ncol * 128;
@@ -207,21 +231,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     // ---------------------------------------------------- weight stages
     // the weights depend on no earlier kernel: no griddepcontrol.wait here
     if (a.pdl && lane == 0) pdl_launch_dependents();
-    StageIter it(i0, i1, gpr);
-    int o, g0, ng, s = 0, ph = 0, issued = 0;
-    while (it.next(o, g0, ng)) {
-      if (!dead && !tc_wait(&S.raw_empty[s], ph ^ 1, a.err)) dead = true;
-      if (lane == 0) {  // the tc layout: one contiguous run per stage
-        const uint32_t bytes = (uint32_t)(ng * TPO * blk);
-        mbar_expect_tx(&S.raw_full[s], bytes);
-        bulk_g2s(raw + (size_t)s * kTcStageBytes, a.ws + ((size_t)o * gpr + g0) * TPO * blk, bytes,
-                 &S.raw_full[s]);
-      }
-      __syncwarp();
-      issued++;
-      if (++s == kTcRaw) {
-        s = 0;
-        ph ^= 1;
+    SegIter it(a, gpr, octets);
+    Seg sg;
+    int s = 0, ph = 0, issued = 0;
+    while (it.next(sg)) {
+      for (int g0 = sg.g0; g0 < sg.g1; g0 += kTcGroupsPerStage) {
+        const int ng = min(kTcGroupsPerStage, sg.g1 - g0);
+        if (!dead && !tc_wait(&S.raw_empty[s], ph ^ 1, a.err)) dead = true;
+        if (lane == 0) {  // the tc layout: one contiguous run per stage
+          const uint32_t bytes = (uint32_t)(ng * TPO * blk);
+          mbar_expect_tx(&S.raw_full[s], bytes);
+          bulk_g2s(raw + (size_t)s * kTcStageBytes, a.ws + ((size_t)sg.o * gpr + g0) * TPO * blk, bytes,
+                   &S.raw_full[s]);
+        }
+        __syncwarp();
+        issued++;
+        if (++s == kTcRaw) {
+          s = 0;
+          ph ^= 1;
+        }
       }
     }
     // never leave with a copy in flight
@@ -238,18 +266,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     // ---------------------------------------------------- B planes
     if (a.pdl) pdl_wait();
     Ring rb{0, 0};
-    int g = i0 % gpr;
-    for (int i = i0; i < i1; i++) {
-      if (!dead && !tc_wait(&S.b_empty[rb.slot], rb.ph ^ 1, a.err)) dead = true;
-      if (lane == 0) {
-        mbar_expect_tx(&S.b_full[rb.slot], bbytes);
-        bulk_g2s(bbuf + (size_t)rb.slot * kTcBBytes, a.xtc + (size_t)g * bbytes, bbytes, &S.b_full[rb.slot]);
+    int nb = 0;
+    SegIter it(a, gpr, octets);
+    Seg sg;
+    while (it.next(sg))
+      for (int g = sg.g0; g < sg.g1; g++, nb++) {
+        if (!dead && !tc_wait(&S.b_empty[rb.slot], rb.ph ^ 1, a.err)) dead = true;
+        if (lane == 0) {
+          mbar_expect_tx(&S.b_full[rb.slot], bbytes);
+          bulk_g2s(bbuf + (size_t)rb.slot * kTcBBytes, a.xtc + ((size_t)sg.tau * gpr + g) * bbytes, bbytes,
+                   &S.b_full[rb.slot]);
+        }
+        __syncwarp();
+        rb.adv(kTcB);
       }
-      __syncwarp();
-      rb.adv(kTcB);
-      if (++g == gpr) g = 0;
-    }
-    for (int j = 0; j < kTcB && j < i1 - i0; j++) {  // copies in flight have landed
+    for (int j = 0; j < kTcB && j < nb; j++) {  // copies in flight have landed
       if (rb.slot == 0) {
         rb.slot = kTcB - 1;
         rb.ph ^= 1;
@@ -262,7 +293,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     // ---------------------------------------------------- MMA issue
     const uint32_t idesc = idesc_i8(128, ncol) | (1u << 7);  // A signed
     Ring ra{0, 0}, rb{0, 0}, rt{0, 0};
-    for (int i = i0; i < i1; i++) {
+    int nm = 0;
+    SegIter it(a, gpr, octets);
+    Seg sg;
+    while (it.next(sg))
+      for (int g = sg.g0; g < sg.g1; g++, nm++) {
       if (!dead && !tc_wait(&S.a_full[ra.slot], ra.ph, a.err)) dead = true;
       if (!dead && !tc_wait(&S.b_full[rb.slot], rb.ph, a.err)) dead = true;
       if (!dead && !tc_wait(&S.acc_empty[rt.slot], rt.ph ^ 1, a.err)) dead = true;
@@ -286,7 +321,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
       rt.adv(NT);
     }
     // the MMAs this warp issued have finished before TMEM is freed
-    for (int j = 0; j < NT && j < i1 - i0; j++) {
+    for (int j = 0; j < NT && j < nm; j++) {
       if (rt.slot == 0) {
         rt.slot = NT - 1;
         rt.ph ^= 1;
@@ -298,53 +333,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
   } else if (warp < kTcConvWarps) {
     // ---------------------------------------------------- convert to A
     const int ct = threadIdx.x;  // 0..255
-    StageIter it(i0, i1, gpr);
-    int o, g0, ng, s = 0, ph = 0;
+    SegIter it(a, gpr, octets);
+    Seg sg;
+    int s = 0, ph = 0;
     Ring ra{0, 0}, rs{0, 0};
     const int sm_ = ct & 127;  // threads 0..127 copy the scale of MMA row sm_
     const int sti = R == 1 ? sm_ >> 4 : sm_ >> 5, sr = R == 1 ? 0 : (sm_ >> 4) & 1, srow = sm_ & 15;
     const int sc_off = R * 1024 + 4 * (sr * 16 + 2 * (srow & 7) + (srow >> 3));
-    while (it.next(o, g0, ng)) {
-      if (!dead && !tc_wait(&S.raw_full[s], ph, a.err)) dead = true;
-      const unsigned char* st = raw + (size_t)s * kTcStageBytes;
-      for (int gj = 0; gj < ng; gj++) {
-        if (!dead && !tc_wait(&S.a_empty[ra.slot], ra.ph ^ 1, a.err)) dead = true;
-        unsigned char* A = abuf + (size_t)ra.slot * kTcABytes;
-        // 512 pieces of 16 B (block, part, row half, lane): words t, 4+t,
-        // 8+t, 12+t of MMA row m; word w goes to k chunk w / 2, half w & 1
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-          const int pc = ct + 256 * j;
-          const int pl = pc & 31, h = (pc >> 5) & 1, rest = pc >> 6;
-          const int ti = R == 1 ? rest : rest >> 1, r = R == 1 ? 0 : rest & 1;
-          const int m = R == 1 ? 16 * ti + 8 * h + (pl >> 2) : 32 * ti + 16 * r + 8 * h + (pl >> 2);
-          const int t = pl & 3;
-          const uint4 v = *reinterpret_cast<const uint4*>(
-              st + (gj * TPO + ti) * blk + r * 1024 + h * 512 + pl * 16);
-          unsigned char* rowp = A + (m >> 3) * 128 + (m & 7) * 16 + (t & 1) * 8;
-          const int kc = t >> 1;
-          *reinterpret_cast<uint2*>(rowp + (kc + 0) * 2048) = a_bytes(v.x);
-          *reinterpret_cast<uint2*>(rowp + (kc + 2) * 2048) = a_bytes(v.y);
-          *reinterpret_cast<uint2*>(rowp + (kc + 4) * 2048) = a_bytes(v.z);
-          *reinterpret_cast<uint2*>(rowp + (kc + 6) * 2048) = a_bytes(v.w);
+    while (it.next(sg)) {
+      for (int g0 = sg.g0; g0 < sg.g1; g0 += kTcGroupsPerStage) {
+        const int ng = min(kTcGroupsPerStage, sg.g1 - g0);
+        if (!dead && !tc_wait(&S.raw_full[s], ph, a.err)) dead = true;
+        const unsigned char* st = raw + (size_t)s * kTcStageBytes;
+        for (int gj = 0; gj < ng; gj++) {
+          if (!dead && !tc_wait(&S.a_empty[ra.slot], ra.ph ^ 1, a.err)) dead = true;
+          unsigned char* A = abuf + (size_t)ra.slot * kTcABytes;
+          // 512 pieces of 16 B (block, part, row half, lane): words t, 4+t,
+          // 8+t, 12+t of MMA row m; word w goes to k chunk w / 2, half w & 1
+  #pragma unroll
+          for (int j = 0; j < 2; j++) {
+            const int pc = ct + 256 * j;
+            const int pl = pc & 31, h = (pc >> 5) & 1, rest = pc >> 6;
+            const int ti = R == 1 ? rest : rest >> 1, r = R == 1 ? 0 : rest & 1;
+            const int m = R == 1 ? 16 * ti + 8 * h + (pl >> 2) : 32 * ti + 16 * r + 8 * h + (pl >> 2);
+            const int t = pl & 3;
+            const uint4 v = *reinterpret_cast<const uint4*>(
+                st + (gj * TPO + ti) * blk + r * 1024 + h * 512 + pl * 16);
+            unsigned char* rowp = A + (m >> 3) * 128 + (m & 7) * 16 + (t & 1) * 8;
+            const int kc = t >> 1;
+            *reinterpret_cast<uint2*>(rowp + (kc + 0) * 2048) = a_bytes(v.x);
+            *reinterpret_cast<uint2*>(rowp + (kc + 2) * 2048) = a_bytes(v.y);
+            *reinterpret_cast<uint2*>(rowp + (kc + 4) * 2048) = a_bytes(v.z);
+            *reinterpret_cast<uint2*>(rowp + (kc + 6) * 2048) = a_bytes(v.w);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.a_full[ra.slot]);
+          // the group scale of MMA row ct, for the epilogue
+          if (!dead && !tc_wait(&S.sc_empty[rs.slot], rs.ph ^ 1, a.err)) dead = true;
+          if (ct < 128)
+            S.scale[rs.slot][ct] = *reinterpret_cast<const float*>(st + (gj * TPO + sti) * blk + sc_off);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.sc_full[rs.slot]);
+          rs.adv(kTcSc);
+          ra.adv(kTcA);
         }
-        fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.a_full[ra.slot]);
-        // the group scale of MMA row ct, for the epilogue
-        if (!dead && !tc_wait(&S.sc_empty[rs.slot], rs.ph ^ 1, a.err)) dead = true;
-        if (ct < 128)
-          S.scale[rs.slot][ct] = *reinterpret_cast<const float*>(st + (gj * TPO + sti) * blk + sc_off);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.sc_full[rs.slot]);
-        rs.adv(kTcSc);
-        ra.adv(kTcA);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.raw_empty[s]);
-      if (++s == kTcRaw) {
-        s = 0;
-        ph ^= 1;
+        if (lane == 0) mbar_arrive(&S.raw_empty[s]);
+        if (++s == kTcRaw) {
+          s = 0;
+          ph ^= 1;
+        }
       }
     }
   } else if (warp >= kTcEpiWarp0 && warp < kTcEpiWarp0 + kTcEpiWarps) {
@@ -352,123 +391,119 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     if (a.pdl) pdl_wait();
     const int sub = warp & 3, wg = (warp - kTcEpiWarp0) >> 2;
     const int m = 32 * sub + lane;  // MMA row = TMEM lane
-    const int th = a.tpad / 2, tb = wg * th;  // this warpgroup's tokens [tb, tb + th)
+    const int th = a.tpad / 2, tb = wg * th;  // this warpgroup's tokens of a tile [tb, tb + th)
     const int ti = R == 1 ? m >> 4 : m >> 5, r = R == 1 ? 0 : (m >> 4) & 1, row = m & 15;
-    // (octet, group) of the next item
-    int o = i0 / gpr, g = i0 % gpr;
     float acc01[TH], acc23[TH];
-    int fx[TH];  // the tokens' fixed-point exponents
 #pragma unroll
-    for (int j = 0; j < TH; j++) {
-      acc01[j] = acc23[j] = 0.f;
-      fx[j] = (j < th && tb + j < a.lanes) ? __ldcg(a.xf + tb + j) : 0;
-    }
-    const int first_o = i0 / gpr;
+    for (int j = 0; j < TH; j++) acc01[j] = acc23[j] = 0.f;
+    const int first_o = item_lo(items, ncta, c) / gpr;
     Ring rt{0, 0}, rs{0, 0};
-    for (int i = i0; i < i1; i++) {
-      const int qt = rt.slot;
-      if (!dead && !tc_wait(&S.sc_full[rs.slot], rs.ph, a.err)) dead = true;
-      const float s_m = S.scale[rs.slot][m];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.sc_empty[rs.slot]);
-      rs.adv(kTcSc);
-      if (!dead && !tc_wait(&S.acc_full[qt], rt.ph, a.err)) dead = true;
-      rt.adv(NT);
-      tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(qt * ncol + 4 * tb);
-      // 8 tokens (32 columns) per TMEM load
+    SegIter it(a, gpr, octets);
+    Seg sg;
+    while (it.next(sg)) {
+      for (int g = sg.g0; g < sg.g1; g++) {
+        const int qt = rt.slot;
+        if (!dead && !tc_wait(&S.sc_full[rs.slot], rs.ph, a.err)) dead = true;
+        const float s_m = S.scale[rs.slot][m];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.sc_empty[rs.slot]);
+        rs.adv(kTcSc);
+        if (!dead && !tc_wait(&S.acc_full[qt], rt.ph, a.err)) dead = true;
+        rt.adv(NT);
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(qt * ncol + 4 * tb);
+        // 8 tokens (32 columns) per TMEM load
 #pragma unroll
-      for (int h8 = 0; h8 < (TH + 7) / 8; h8++) {
-        if (8 * h8 >= th) break;
-        uint32_t v[32];
-        tmem_ld32(taddr + 32 * h8, v);
-        tmem_wait_ld();
+        for (int h8 = 0; h8 < (TH + 7) / 8; h8++) {
+          if (8 * h8 >= th) break;
+          uint32_t v[32];
+          tmem_ld32(taddr + 32 * h8, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int jj = 0; jj < 8; jj++) {
-          const int j = 8 * h8 + jj;
-          if (j >= th) break;
-          const int p01 = (int)v[4 * jj] + 256 * (int)v[4 * jj + 1];
-          const int p23 = (int)v[4 * jj + 2] + 256 * (int)v[4 * jj + 3];
-          acc01[j] = fmaf(s_m, (float)p01, acc01[j]);
-          acc23[j] = fmaf(s_m, (float)p23, acc23[j]);
+          for (int jj = 0; jj < 8; jj++) {
+            const int j = 8 * h8 + jj;
+            if (j >= th) break;
+            const int p01 = (int)v[4 * jj] + 256 * (int)v[4 * jj + 1];
+            const int p23 = (int)v[4 * jj + 2] + 256 * (int)v[4 * jj + 3];
+            acc01[j] = fmaf(s_m, (float)p01, acc01[j]);
+            acc23[j] = fmaf(s_m, (float)p23, acc23[j]);
+          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.acc_empty[qt]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.acc_empty[qt]);
-      const int oc = o;  // this item's octet
-      const bool oct_end = g + 1 == gpr;
-      if (++g == gpr) {
-        g = 0;
-        o++;
-      }
-      if (i + 1 != i1 && !oct_end) continue;  // octet not finished here
-      const int o_ = oc;
-      // ---- octet o done in this CTA: final or partial output
-      const int c_lo = cta_of(items, ncta, o_ * gpr);
-      const int c_hi = cta_of(items, ncta, o_ * gpr + gpr - 1);
+      // ---- run done: final or partial output of octet sg.o, token tile sg.tau
+      const int o_ = sg.o, t0 = 32 * sg.tau;  // the tile's first token
       float y[TH];
 #pragma unroll
       for (int j = 0; j < TH; j++) {
-        y[j] = __fadd_rn(__fmul_rn(acc01[j], __int_as_float((127 - fx[j]) << 23)),
-                         __fmul_rn(acc23[j], __int_as_float((143 - fx[j]) << 23)));
+        const int t = t0 + tb + j;
+        const int f = (j < th && t < a.lanes) ? __ldcg(a.xf + t) : 0;
+        y[j] = __fadd_rn(__fmul_rn(acc01[j], __int_as_float((127 - f) << 23)),
+                         __fmul_rn(acc23[j], __int_as_float((143 - f) << 23)));
         acc01[j] = acc23[j] = 0.f;
       }
-      bool fin = c_lo == c_hi;
-      if (!fin) {
-        // partial: every thread stores, the warpgroups meet, ONE thread
-        // fences and counts the arrival (a fence per thread serialises)
-        float* pp = a.part + ((size_t)c * 2 + (o_ == first_o ? 0 : 1)) * kTcMaxTok * 128;
+      bool fin = true;
+      if (!a.whole) {
+        const int c_lo = cta_of(items, ncta, o_ * gpr);
+        const int c_hi = cta_of(items, ncta, o_ * gpr + gpr - 1);
+        fin = c_lo == c_hi;
+        if (!fin) {
+          // partial: every thread stores, the warpgroups meet, ONE thread
+          // fences and counts the arrival (a fence per thread serialises)
+          float* pp = a.part + ((size_t)c * 2 + (o_ == first_o ? 0 : 1)) * kTcMaxTok * 128;
 #pragma unroll
-        for (int j = 0; j < TH; j++)
-          if (j < th) pp[(size_t)(tb + j) * 128 + m] = y[j];
-        __syncwarp();
-        asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
-        __syncwarp();
-        if (warp == kTcEpiWarp0 && lane == 0) {
-          __threadfence();
-          const bool last = atomicAdd(a.counters + o_, 1u) == (unsigned)(c_hi - c_lo);
-          if (last) {
+          for (int j = 0; j < TH; j++)
+            if (j < th) pp[(size_t)(tb + j) * 128 + m] = y[j];
+          __syncwarp();
+          asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
+          __syncwarp();
+          if (warp == kTcEpiWarp0 && lane == 0) {
             __threadfence();
-            a.counters[o_] = 0u;  // for the next launch
+            const bool last = atomicAdd(a.counters + o_, 1u) == (unsigned)(c_hi - c_lo);
+            if (last) {
+              __threadfence();
+              a.counters[o_] = 0u;  // for the next launch
+            }
+            S.last = last;
           }
-          S.last = last;
-        }
-        __syncwarp();
-        asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
-        fin = S.last != 0;
-        if (fin) {  // sum the partials in CTA order, four CTAs' loads in flight at a time
+          __syncwarp();
+          asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
+          fin = S.last != 0;
+          if (fin) {  // sum the partials in CTA order, four CTAs' loads in flight at a time
 #pragma unroll
-          for (int j = 0; j < TH; j++) y[j] = 0.f;
-          for (int cc = c_lo; cc <= c_hi; cc += 4) {
-            float pv[4][TH];
+            for (int j = 0; j < TH; j++) y[j] = 0.f;
+            for (int cc = c_lo; cc <= c_hi; cc += 4) {
+              float pv[4][TH];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-              const int c2 = cc + u;
-              const float* qp = nullptr;
-              if (c2 <= c_hi) {
-                const int cfirst = item_lo(items, ncta, c2) / gpr;
-                qp = a.part + ((size_t)c2 * 2 + (o_ == cfirst ? 0 : 1)) * kTcMaxTok * 128;
+              for (int u = 0; u < 4; u++) {
+                const int c2 = cc + u;
+                const float* qp = nullptr;
+                if (c2 <= c_hi) {
+                  const int cfirst = item_lo(items, ncta, c2) / gpr;
+                  qp = a.part + ((size_t)c2 * 2 + (o_ == cfirst ? 0 : 1)) * kTcMaxTok * 128;
+                }
+#pragma unroll
+                for (int j = 0; j < TH; j++)
+                  pv[u][j] = (qp && j < th) ? __ldcg(qp + (size_t)(tb + j) * 128 + m) : 0.f;
               }
 #pragma unroll
-              for (int j = 0; j < TH; j++)
-                pv[u][j] = (qp && j < th) ? __ldcg(qp + (size_t)(tb + j) * 128 + m) : 0.f;
+              for (int u = 0; u < 4; u++)
+#pragma unroll
+                for (int j = 0; j < TH; j++)
+                  if (cc + u <= c_hi) y[j] = __fadd_rn(y[j], pv[u][j]);
             }
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-#pragma unroll
-              for (int j = 0; j < TH; j++)
-                if (cc + u <= c_hi) y[j] = __fadd_rn(y[j], pv[u][j]);
           }
+          asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");  // S.last reuse
         }
-        asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");  // S.last reuse
       }
       if (!fin) continue;
       const int n = 16 * (o_ * TPO + ti) + row;
 #pragma unroll
       for (int j = 0; j < TH; j++) {
         const float up = __shfl_down_sync(0xffffffffu, y[j], 16);  // R = 2: the up row
-        const int t = tb + j;
+        const int t = t0 + tb + j;
         if (j >= th || t >= a.lanes || n >= a.N) continue;
         if (R == 2 && r == 1) continue;
         tc_store(a, t, n, y[j], up);
@@ -524,6 +559,7 @@ void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const B
   a.R = R;
   a.lanes = lanes;
   a.tpad = xp.tc_tpad;
+  a.whole = lanes > kTcMaxTok;
   a.xtc = static_cast<const unsigned char*>(xp.xtc);
   a.xf = xp.xf;
   a.be = be;
@@ -533,9 +569,11 @@ void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const B
   a.pdl = pdl;
   const int gpr = K / kGroup, tiles = (N + 15) / 16, octets = (tiles + 8 / R - 1) / (8 / R);
   const int items = octets * gpr;
-  // at most two CTAs per octet: a split octet costs a fence, an atomic and
-  // the partial-sum reads of its last CTA
-  const int ncta = std::min(std::min(sm_count(), 2 * octets), items);
+  // split mode: at most two CTAs per octet (a split octet costs a fence, an
+  // atomic and the partial-sum reads of its last CTA); whole mode: one
+  // (token tile, octet) pair per CTA at a time
+  const int ncta = a.whole ? std::min(sm_count(), octets * ((lanes + kTcMaxTok - 1) / kTcMaxTok))
+                           : std::min(std::min(sm_count(), 2 * octets), items);
   const size_t smem = (size_t)kTcRaw * kTcStageBytes + (size_t)kTcA * kTcABytes + (size_t)kTcB * kTcBBytes;
   void (*kern)(TcArgs) = a.tpad <= 16 ? gemv_q4_tc_kernel<8> : gemv_q4_tc_kernel<16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
