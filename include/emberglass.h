@@ -86,6 +86,19 @@ typedef struct {
                               the tcgen05 tensor cores (keeps a second,
                               octet-major copy of the int4 weights); 0
                               (default): the integer mma.sync path */
+  int prefill_tc;          /* 1 (default): eg_prefill runs prefillBatch's own
+                              arithmetic (runtime.js:1936-2087: GEMM4 over the
+                              prompt, ROPE_T, ATTN_PREFILL_BLOCK, SILUMUL) as
+                              whole-prompt tcgen05 GEMMs and a tensor-core
+                              prefill attention (keeps the octet-major weight
+                              copy, plus prefill scratch sized for
+                              max_prefill_t or prefill_chunk_size positions);
+                              0: positions through the decode step's
+                              arithmetic (prefill_chunk above) */
+  int prefill_chunk_size;  /* prefillChunkSize (runtime.js:118, :1940-1942),
+                              prefill_tc only: 0 (default) = the whole prompt
+                              in one pass (_prefillFull); n > 0 = passes of n
+                              positions (_prefillChunked) */
 } eg_options;
 
 EG_API const char* eg_last_error(void);
@@ -164,9 +177,12 @@ EG_API void* eg_stream(eg_rt* rt);
 EG_API eg_status eg_sync(eg_rt* rt);
 /* prefillBatch(ids), runtime.js:1936-1945: positions 0..T-1; throws
  * "prompt T > maxPrefillT M" / "prompt T > maxCtx M".  Logits of the last
- * position are left on the device.  Positions 0..T-2 run in batched chunks
- * of prefill_chunk positions (K/V rows only), the last through the decode
- * step. */
+ * position are left on the device and decoding continues at position T.
+ * prefill_tc (default): passes of the whole prompt (or prefill_chunk_size
+ * positions) through the tcgen05 GEMMs and the prefill attention, the
+ * reference's prefill arithmetic.  prefill_tc = 0: positions 0..T-2 in
+ * batched chunks of prefill_chunk positions (K/V rows only), the last
+ * through the decode step. */
 EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T);
 /* argmaxLogits(), runtime.js:1602-1629: writes s.amax and returns it. */
 EG_API eg_status eg_argmax(eg_rt* rt, uint32_t* out_id);
@@ -344,6 +360,17 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
                                    const float* cos_t, const float* sin_t, int nh, int nkv,
                                    int pos, int max_ctx, int kv_f16, int chunk, float* out,
                                    void* stream);
+/* ROPE_T (kernels.js:588-618) + the K/V rows + ATTN_PREFILL_BLOCK
+ * (kernels.js:684-770) of one prefill pass, on the tensor cores:
+ * qkv = T raw rows [q | k | v] (nh + 2 nkv heads of 128) for positions
+ * q_start .. q_start + T - 1; q is rotated in place, k rotated and v copied
+ * into cache rows q_start + t of the dense caches [max_ctx][nkv][128] (f16
+ * when kv_f16 else f32), then every row attends causally over cache rows
+ * 0 .. q_start + T - 1 in 128-key online-softmax blocks.  out [T][nh*128].
+ * Allocates nothing. */
+EG_API eg_status eg_op_attn_prefill(float* qkv, int T, void* k_cache, void* v_cache, const float* cos_t,
+                                    const float* sin_t, int nh, int nkv, int q_start, int max_ctx, int kv_f16,
+                                    float* out, void* stream);
 /* No counterpart in the reference.  eg_op_attn_decode for callers that must
  * not allocate device memory at call time (a framework whose caching
  * allocator already holds the device memory, or a latency-critical loop that

@@ -400,6 +400,147 @@ ORC_API void orc_attention(const float* q, const float* kc, const float* vc, int
 }
 
 /* ------------------------------------------------------------------------ */
+/* Whole-prompt prefill (prefillBatch)                                       */
+/* ------------------------------------------------------------------------ */
+/* GEMM4 / GEMM4_ADD_T, kernels.js:389-473: per word the eight weights are
+ * dequantised first (f32(nibble) * scale), the eight products summed left to
+ * right, the sum added to the running accumulator. */
+static float gemm4_row(const float* x, const uint32_t* w, const float* scale, int n, int K, int gpr) {
+  const int K8 = K / 8;
+  const uint32_t* rw = w + (int64_t)n * K8;
+  const float* rs = scale + (int64_t)n * gpr;
+  float acc = 0.0f;
+  for (int cc = 0; cc < K8; cc++) {
+    const int c = g_sum_order ? K8 - 1 - cc : cc;
+    const uint32_t word = rw[c];
+    const float sc = rs[(c * 8) >> 7];
+    const float* a = x + c * 8;
+    float p = a[0] * (nib_at(word, 0) * sc);
+    for (int j = 1; j < 8; j++) p = p + a[j] * (nib_at(word, j) * sc);
+    acc = acc + p;
+  }
+  return acc;
+}
+
+/* Y[t] = W4 X[t] + bias (GEMM4) or Y[t] = Y[t] + W4 X[t] + bias (GEMM4_ADD_T). */
+ORC_API void orc_gemm4(const float* X, int T, const uint32_t* w, const float* scale, const float* bias, int N,
+                       int K, int add, float* Y) {
+  const int gpr = K / 128;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int t = 0; t < T; t++)
+    for (int n = 0; n < N; n++) {
+      const float acc = gemm4_row(X + (int64_t)t * K, w, scale, n, K, gpr);
+      const float bv = bias ? bias[n] : 0.0f;
+      float* y = Y + (int64_t)t * N + n;
+      *y = add ? (*y + acc) + bv : acc + bv;
+    }
+}
+
+/* loraBatchDelta (runtime.js:1814-1843): LORA_A_BATCH (kernels.js:79-97)
+ * d[t][r] = sum_k X[t][k] A[r][k], then LORA_B_ADD_T (kernels.js:98-112)
+ * Y[t][n] += scale * sum_r d[t][r] B[r][n]. */
+ORC_API void orc_lora_batch_delta(const float* X, int T, const float* A, const float* B, int rank, float scale,
+                                  int K, int N, float* Y) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; t++) {
+    float d[256];
+    for (int r = 0; r < rank; r++) {
+      float acc = 0.0f;
+      for (int k = 0; k < K; k++) acc = acc + X[(int64_t)t * K + k] * A[(int64_t)r * K + k];
+      d[r] = acc;
+    }
+    for (int n = 0; n < N; n++) {
+      float acc = 0.0f;
+      for (int r = 0; r < rank; r++) acc = acc + d[r] * B[(int64_t)r * N + n];
+      Y[(int64_t)t * N + n] = Y[(int64_t)t * N + n] + scale * acc;
+    }
+  }
+}
+
+/* SILUMUL / SILUMUL_F16, kernels.js:499-523: silu in f32; the f16 variant
+ * rounds silu(g) and u to f16 and multiplies in f16. */
+ORC_API void orc_silu_mul(float* gate, const float* up, int64_t n, int f16) {
+  for (int64_t i = 0; i < n; i++) {
+    const float v = gate[i];
+    const float sg = v / (1.0f + expf(-v));
+    gate[i] = f16 ? h16((double)h16(sg) * (double)h16(up[i])) : sg * up[i];
+  }
+}
+
+/* ROPE_T / ROPE_T_F16, kernels.js:588-618: rows t of x (nh heads) at
+ * position pos0 + t, the decode pair rotation. */
+ORC_API void orc_rope_t(float* x, int T, int nh, int hd, int pos0, const float* cosT, const float* sinT,
+                        int f16) {
+  const int half = hd / 2;
+  for (int t = 0; t < T; t++)
+    for (int h = 0; h < nh; h++) {
+      float* r = x + ((int64_t)t * nh + h) * hd;
+      for (int j = 0; j < half; j++) {
+        const int64_t off = (int64_t)(pos0 + t) * hd + j;
+        rope_pair(&r[j], &r[j + half], cosT[off], sinT[off], f16);
+      }
+    }
+}
+
+/* ATTN_PREFILL_BLOCK, kernels.js:684-770: query row t (absolute position
+ * qStart + t) over keys 0..ctx-1 in blocks of 128 with an online softmax:
+ * per block the running max moves to max(m, block max), the running sum
+ * and the accumulator are rescaled by exp(m_old - m_new), then the block's
+ * exp(s - m_new) weights are added; keys past the query are masked.
+ * q [T][nh*hd], kc / vc [ctx][nkv*hd], out [T][nh*hd]. */
+ORC_API void orc_attn_prefill(const float* q, const float* kc, const float* vc, int nh, int nkv, int hd, int T,
+                              int qStart, int ctx, float* out) {
+  const int stride = nkv * hd, BK = 128;
+  const float scl = 1.0f / sqrtf((float)hd);
+#pragma omp parallel for collapse(2) schedule(dynamic)
+  for (int t = 0; t < T; t++)
+    for (int h = 0; h < nh; h++) {
+      const int kvh = h / (nh / nkv), absQ = qStart + t;
+      const float* qr = q + ((int64_t)t * nh + h) * hd;
+      float acc[256], p[128];
+      for (int d = 0; d < hd; d++) acc[d] = 0.0f;
+      float mrun = -1e30f, lrun = 0.0f;
+      for (int kb = 0; kb < ctx; kb += BK) {
+        float bm = -1e30f;
+        for (int j = 0; j < BK; j++) {
+          const int kk = kb + j;
+          p[j] = -1e30f;
+          if (kk < ctx && kk <= absQ) {
+            const float* kr = kc + (int64_t)kk * stride + kvh * hd;
+            float dot = 0.0f;
+            for (int dd = 0; dd < hd; dd++) {
+              const int d = g_sum_order ? hd - 1 - dd : dd;
+              dot = dot + qr[d] * kr[d];
+            }
+            p[j] = dot * scl;
+          }
+          bm = fmaxf(bm, p[j]);
+        }
+        const float mnew = fmaxf(mrun, bm), corr = expf(mrun - mnew);
+        float bs = 0.0f;
+        for (int j = 0; j < BK; j++) {
+          const int kk = kb + j;
+          p[j] = (kk < ctx && kk <= absQ) ? expf(p[j] - mnew) : 0.0f;
+          bs = bs + p[j];
+        }
+        lrun = lrun * corr + bs;
+        mrun = mnew;
+        const int bcount = ctx - kb < BK ? ctx - kb : BK;
+        for (int d = 0; d < hd; d++) {
+          float a = acc[d] * corr;
+          for (int jj = 0; jj < bcount; jj++) {
+            const int j = g_sum_order ? bcount - 1 - jj : jj;
+            a = a + p[j] * vc[(int64_t)(kb + j) * stride + kvh * hd + d];
+          }
+          acc[d] = a;
+        }
+      }
+      const float invL = 1.0f / lrun;
+      for (int d = 0; d < hd; d++) out[((int64_t)t * nh + h) * hd + d] = acc[d] * invL;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Sampling                                                                  */
 /* ------------------------------------------------------------------------ */
 static inline int beats(float x, uint32_t i, float v, uint32_t idx) {
@@ -713,6 +854,79 @@ ORC_API int orc_model_step(void* mp, uint32_t id, int pos, float* logits_out) {
   orc_rmsnorm(m->hidden, m->final_norm, H, c->eps, m->f16, m->normed);
   orc_gemv_q8(m->normed, m->emb_w, m->emb_s, NULL, c->vocab, H, m->logits);
   if (logits_out) memcpy(logits_out, m->logits, sizeof(float) * c->vocab);
+  return 0;
+}
+
+/* One projection of a prefill pass: GEMM4(_ADD_T) then the adapter's batch
+ * delta (gemm4 / gemm4AddT, runtime.js:1800-1813). */
+static void proj_t(orc_model* m, int i, int p, const float* X, int T, const float* bias, int add, float* Y) {
+  int N, K;
+  proj_dims(&m->c, p, &N, &K);
+  orc_gemm4(X, T, m->w[p][i], m->s[p][i], bias, N, K, add, Y);
+  orc_lora_mod* md = lmod(m, i, p);
+  if (md) orc_lora_batch_delta(X, T, md->A, md->B, md->rank, md->scale, K, N, Y);
+}
+
+/* prefillBatch(ids), runtime.js:1936-2087: chunk <= 0 or T <= chunk runs
+ * _prefillFull (one pass over the whole prompt), else _prefillChunked
+ * (passes of `chunk` positions, each attending to every earlier row).  Per
+ * pass and layer: RMSNORM_T, GEMM4 q/k/v (+bias, +LoRA), ROPE_T, the K/V rows
+ * into the cache, ATTN_PREFILL_BLOCK, GEMM4_ADD_T o, RMSNORM_T, GEMM4
+ * gate/up, SILUMUL, GEMM4_ADD_T down.  Then the last row's final norm and
+ * LM-head GEMV.  Leaves the cache filled to T - 1 and hidden = the last row. */
+ORC_API int orc_model_prefill(void* mp, const uint32_t* ids, int T, int chunk, float* logits_out) {
+  orc_model* m = (orc_model*)mp;
+  const orc_cfg* c = &m->c;
+  if (T <= 0 || T > m->max_ctx) return -1;
+  for (int t = 0; t < T; t++)
+    if (ids[t] >= (uint32_t)c->vocab) return -1;
+  const int H = c->hidden, hd = c->head_dim, QD = c->heads * hd, KVD = c->kv_heads * hd, I = c->inter;
+  const int CT = (chunk > 0 && T > chunk) ? chunk : T;
+  float* hid = (float*)xmalloc(sizeof(float) * (size_t)CT * H);
+  float* nrm = (float*)xmalloc(sizeof(float) * (size_t)CT * H);
+  float* q = (float*)xmalloc(sizeof(float) * (size_t)CT * QD);
+  float* k = (float*)xmalloc(sizeof(float) * (size_t)CT * KVD);
+  float* v = (float*)xmalloc(sizeof(float) * (size_t)CT * KVD);
+  float* at = (float*)xmalloc(sizeof(float) * (size_t)CT * QD);
+  float* g = (float*)xmalloc(sizeof(float) * (size_t)CT * I);
+  float* u = (float*)xmalloc(sizeof(float) * (size_t)CT * I);
+  for (int off = 0; off < T; off += CT) {
+    const int n = T - off < CT ? T - off : CT, end = off + n;
+    for (int t = 0; t < n; t++) orc_embed(m->emb_w, m->emb_s, ids[off + t], H, hid + (size_t)t * H);
+    for (int i = 0; i < c->layers; i++) {
+      for (int t = 0; t < n; t++)
+        orc_rmsnorm(hid + (size_t)t * H, m->in_norm[i], H, c->eps, m->f16, nrm + (size_t)t * H);
+      proj_t(m, i, 0, nrm, n, m->bias[0][i], 0, q);
+      proj_t(m, i, 1, nrm, n, m->bias[1][i], 0, k);
+      proj_t(m, i, 2, nrm, n, m->bias[2][i], 0, v);
+      orc_rope_t(q, n, c->heads, hd, off, m->cosT, m->sinT, m->f16);
+      orc_rope_t(k, n, c->kv_heads, hd, off, m->cosT, m->sinT, m->f16);
+      float* kc = m->kc + (size_t)i * m->max_ctx * KVD;
+      float* vc = m->vc + (size_t)i * m->max_ctx * KVD;
+      memcpy(kc + (size_t)off * KVD, k, sizeof(float) * (size_t)n * KVD);
+      memcpy(vc + (size_t)off * KVD, v, sizeof(float) * (size_t)n * KVD);
+      orc_attn_prefill(q, kc, vc, c->heads, c->kv_heads, hd, n, off, end, at);
+      proj_t(m, i, 3, at, n, NULL, 1, hid);
+      for (int t = 0; t < n; t++)
+        orc_rmsnorm(hid + (size_t)t * H, m->post_norm[i], H, c->eps, m->f16, nrm + (size_t)t * H);
+      proj_t(m, i, 4, nrm, n, NULL, 0, g);
+      proj_t(m, i, 5, nrm, n, NULL, 0, u);
+      orc_silu_mul(g, u, (int64_t)n * I, m->f16);
+      proj_t(m, i, 6, g, n, NULL, 1, hid);
+    }
+    if (end == T) memcpy(m->hidden, hid + (size_t)(n - 1) * H, sizeof(float) * H);
+  }
+  orc_rmsnorm(m->hidden, m->final_norm, H, c->eps, m->f16, m->normed);
+  orc_gemv_q8(m->normed, m->emb_w, m->emb_s, NULL, c->vocab, H, m->logits);
+  if (logits_out) memcpy(logits_out, m->logits, sizeof(float) * c->vocab);
+  free(hid);
+  free(nrm);
+  free(q);
+  free(k);
+  free(v);
+  free(at);
+  free(g);
+  free(u);
   return 0;
 }
 

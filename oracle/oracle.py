@@ -64,6 +64,12 @@ def _declare(L):
         "orc_rope_qk": (None, [f32p, f32p, i, i, i, i, f32p, f32p, i]),
         "orc_embed": (None, [u32p, f32p, u32, i, f32p]),
         "orc_attention": (None, [f32p, f32p, f32p, i, i, i, i, i, i, f32p]),
+        "orc_gemm4": (None, [f32p, i, u32p, f32p, vp, i, i, i, f32p]),
+        "orc_lora_batch_delta": (None, [f32p, i, f32p, f32p, i, f, i, i, f32p]),
+        "orc_silu_mul": (None, [f32p, f32p, i64, i]),
+        "orc_rope_t": (None, [f32p, i, i, i, i, f32p, f32p, i]),
+        "orc_attn_prefill": (None, [f32p, f32p, f32p, i, i, i, i, i, i, f32p]),
+        "orc_model_prefill": (i, [vp, u32p, i, i, vp]),
         "orc_argmax": (u32, [f32p, i]),
         "orc_topk": (None, [f32p, i, i, u32p, f32p]),
         "orc_sample_topk": (u32, [u32p, f32p, i, f, f]),
@@ -206,6 +212,29 @@ def attention(q, kc, vc, nh, nkv, ctx, hd, chunk=128, f16=False):
     return out
 
 
+def gemm4(X, packed, scale, N, K, bias=None, Y=None, add=False):
+    """GEMM4 / GEMM4_ADD_T over T rows of X (kernels.js:389-473)."""
+    X = np.ascontiguousarray(X, np.float32)
+    T = X.size // K
+    out = np.zeros((T, N), np.float32) if Y is None else Y
+    lib().orc_gemm4(X, T, packed, scale, _ptr(bias), N, K, int(add), out)
+    return out
+
+
+def rope_t(x, T, nh, hd, pos0, cosT, sinT, f16=False):
+    x = np.array(x, np.float32)
+    lib().orc_rope_t(x, T, nh, hd, pos0, cosT, sinT, int(f16))
+    return x
+
+
+def attn_prefill(q, kc, vc, nh, nkv, hd, T, q_start, ctx):
+    """ATTN_PREFILL_BLOCK (kernels.js:684-770): rows q_start .. q_start+T-1."""
+    out = np.empty(T * nh * hd, np.float32)
+    lib().orc_attn_prefill(np.ascontiguousarray(q, np.float32), np.ascontiguousarray(kc, np.float32),
+                           np.ascontiguousarray(vc, np.float32), nh, nkv, hd, T, q_start, ctx, out)
+    return out
+
+
 def argmax(logits) -> int:
     logits = np.ascontiguousarray(logits, np.float32)
     return int(lib().orc_argmax(logits, logits.size))
@@ -265,6 +294,14 @@ class OracleModel:
             raise ValueError("oracle step: bad token or position")
         return out
 
+    def prefill(self, ids, chunk: int = 0) -> np.ndarray:
+        """prefillBatch(ids) (runtime.js:1936-2087); returns the last row's logits."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        out = np.empty(self.vocab, np.float32)
+        if lib().orc_model_prefill(self._h, ids, ids.size, chunk, out.ctypes.data_as(C.c_void_p)) != 0:
+            raise ValueError("oracle prefill: bad token or length")
+        return out
+
     def logits(self) -> np.ndarray:
         p = lib().orc_model_logits(self._h)
         return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), (self.vocab,)).copy()
@@ -273,8 +310,21 @@ class OracleModel:
         p = lib().orc_model_hidden(self._h)
         return np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), (self.cfg["hiddenSize"],)).copy()
 
-    def generate(self, prompt, n_gen: int):
+    def generate(self, prompt, n_gen: int, prefill: bool = False, chunk: int = 0):
+        """Greedy continuation (decodeBatch, runtime.js:1776-1793); the prompt
+        through the token loop, or with prefill=True through prefillBatch."""
         prompt = np.ascontiguousarray(prompt, np.uint32)
+        if prefill:
+            logits = self.prefill(prompt, chunk)
+            ids = np.zeros(n_gen, np.uint32)
+            margins = np.zeros(n_gen, np.float32)
+            for g in range(n_gen):
+                top2 = np.partition(logits, -2)[-2:]
+                ids[g] = argmax(logits)
+                margins[g] = top2[1] - top2[0]
+                if g + 1 < n_gen:
+                    logits = self.step(int(ids[g]), prompt.size + g)
+            return ids, margins
         ids = np.zeros(n_gen, np.uint32)
         margins = np.zeros(n_gen, np.float32)
         rc = lib().orc_model_generate(self._h, prompt, prompt.size, n_gen, ids,

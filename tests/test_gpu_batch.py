@@ -295,14 +295,15 @@ def test_paged_prefill_oom_then_retry(cuda):
 
 @pytest.mark.parametrize("f16", [True, False])
 def test_chunked_prefill_single_stream(cuda, f16):
-    """prefillBatch runs positions 0..T-2 as batched chunks of 16 (K/V rows
+    """prefillTc off: prefillBatch runs positions 0..T-2 as batched chunks of 16 (K/V rows
     only) and the last position through the decode step: the logits after
     the prompt and the greedy continuation match the oracle, and the KV
     cache it leaves serves decoding like the per-token prefill's."""
     cfg = small_config(layers=2, vocab=4096)
     prompt = O.token_ids(40, 0xE6B00010, cfg["vocabSize"])  # 2 full chunks + a tail of 7
-    rt = E.QwenB200(cfg, dict(maxCtx=96, useF16=f16)).build("synthetic", seed=SEED)
-    ref = E.QwenB200(cfg, dict(maxCtx=96, useF16=f16, prefillChunk=0)).build("synthetic", seed=SEED)
+    rt = E.QwenB200(cfg, dict(maxCtx=96, useF16=f16, prefillTc=False)).build("synthetic", seed=SEED)
+    ref = E.QwenB200(cfg, dict(maxCtx=96, useF16=f16, prefillChunk=0, prefillTc=False)).build(
+        "synthetic", seed=SEED)
     orc = O.OracleModel(cfg, 96, f16, SEED)
     for t, tok in enumerate(prompt):
         want = orc.step(int(tok), t)
@@ -375,7 +376,8 @@ def test_prefill_lengths_chunked_vs_sequential(cuda, L, lora):
     """test/prefill_diff.js:90-115 (batched vs sequential prefill at L in
     {16, 17, 256, 257, 512}) and test/lora_validate.js:148-244 (the same
     with LoRA): the chunked and the per-token prefill both meet the oracle's
-    bars at the last position and agree on its argmax unless near a tie."""
+    bars at the last position and agree on its argmax unless near a tie; the
+    whole-prompt tcgen05 prefill meets them against the oracle's prefillBatch."""
     cfg = small_config(layers=2, vocab=3000)
     prompt = O.token_ids(L, 0xE6B00010 + L, cfg["vocabSize"])
     orc = O.OracleModel(cfg, 520, True, SEED)
@@ -383,9 +385,15 @@ def test_prefill_lengths_chunked_vs_sequential(cuda, L, lora):
         orc.lora_synth(0xA1, 8, 2.0)
     for t, tok in enumerate(prompt):
         ref = orc.step(int(tok), t)
+    orc_p = O.OracleModel(cfg, 520, True, SEED)
+    if lora:
+        orc_p.lora_synth(0xA1, 8, 2.0)
+    ref_p = orc_p.prefill(prompt)
     out = []
-    for chunk in (16, 0):
-        rt = E.QwenB200(cfg, dict(maxCtx=520, prefillChunk=chunk)).build("synthetic", seed=SEED)
+    for chunk in (16, 0, "tc"):
+        tc = chunk == "tc"
+        rt = E.QwenB200(cfg, dict(maxCtx=520, prefillChunk=16 if tc else chunk, prefillTc=tc)).build(
+            "synthetic", seed=SEED)
         a = None
         if lora:
             a = E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16)
@@ -393,10 +401,11 @@ def test_prefill_lengths_chunked_vs_sequential(cuda, L, lora):
         rt.prefillBatch(prompt)
         got = rt.readLogits()
         bars = Bars(True)
-        bars.check(got, ref)
+        bars.check(got, ref_p if tc else ref)
         out.append(got)
         if a is not None:
             rt.clearLora()
             a.destroy()
-    if int(np.argmax(out[0])) != int(np.argmax(out[1])):
-        assert margin(ref) < TIE_BOUND
+    for o in out[1:]:
+        if int(np.argmax(out[0])) != int(np.argmax(o)):
+            assert margin(ref) < TIE_BOUND

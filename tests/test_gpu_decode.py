@@ -68,7 +68,8 @@ def test_prefill_matches_token_loop(cuda, fused):
     another f32 summation order) is held to the oracle bars."""
     cfg = small_config(layers=2, vocab=3000)
     prompt = O.token_ids(20, 5, cfg["vocabSize"])
-    rt = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused, prefillChunk=0)).build("synthetic", seed=SEED)
+    rt = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused, prefillChunk=0, prefillTc=False)).build(
+        "synthetic", seed=SEED)
     rt.prefillBatch(prompt)
     a = rt.readLogits()
     for t, tok in enumerate(prompt):
@@ -77,7 +78,7 @@ def test_prefill_matches_token_loop(cuda, fused):
     orc = O.OracleModel(cfg, 128, True, SEED)
     for t, tok in enumerate(prompt):
         ref = orc.step(int(tok), t)
-    ch = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused)).build("synthetic", seed=SEED)
+    ch = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused, prefillTc=False)).build("synthetic", seed=SEED)
     ch.prefillBatch(prompt)
     close(ch.readLogits(), ref)
     close(a, ref)
@@ -89,7 +90,7 @@ def test_fused_equals_graph_path(cuda):
     cfg = small_config(layers=3, vocab=4000)
     prompt = O.token_ids(16, 9, cfg["vocabSize"])
     orc = O.OracleModel(cfg, 128, True, SEED)
-    ref, margins = orc.generate(prompt, 33)
+    ref, margins = orc.generate(prompt, 33, prefill=True)
     for fused in (True, False):
         rt = E.QwenB200(cfg, dict(maxCtx=128, useFused=fused)).build("synthetic", seed=SEED)
         rt.prefillBatch(prompt)
@@ -105,14 +106,13 @@ def test_generate_greedy_and_sampled(cuda):
     rt, orc = make(cfg, True)
     prompt = O.token_ids(10, 6, cfg["vocabSize"])
     g = rt.generate(prompt, 20)
-    ref, margins = orc.generate(prompt, 20)
+    ref, margins = orc.generate(prompt, 20, prefill=True)
     assert_stream(g, ref, margins)
     # sampled generate: oracle = step + topk(40) + SAMPLE_TOPK with the same r
     r = O.uniform(20, 0xE6B00200)
     s = rt.generate(prompt, 20, {"sample": True, "temp": 0.7, "rSeq": r})
     orc2 = O.OracleModel(cfg, 256, True, SEED)
-    for t, tok in enumerate(prompt):
-        logits = orc2.step(int(tok), t)
+    logits = orc2.prefill(prompt)
     pos = len(prompt)
     for i in range(20):
         ids, vals = O.topk(logits, 40)
@@ -132,8 +132,7 @@ def test_topk_sample_api(cuda):
     rt, orc = make(cfg, True)
     prompt = O.token_ids(8, 7, cfg["vocabSize"])
     rt.prefillBatch(prompt)
-    for t, tok in enumerate(prompt):
-        ref = orc.step(int(tok), t)
+    ref = orc.prefill(prompt)
     top = rt.topKLogits(40)
     rid, rv = O.topk(ref, 40)
     ids = [d["id"] for d in top]
@@ -170,8 +169,7 @@ def test_lora_apply_swap_clear(cuda):
     rt.prefillBatch(prompt)
     l1 = rt.readLogits()
     orc.lora_synth(0xA1, 8, 2.0)
-    for t, tok in enumerate(prompt):
-        ref1 = orc.step(int(tok), t)
+    ref1 = orc.prefill(prompt)
     close(l1, ref1)
     assert np.abs(l1 - base).max() > 1e-3
     rt.setLora(a2)  # hot swap
@@ -290,8 +288,8 @@ def gpu_teacher_forced(f16, prefill_chunk):
     key = (f16, prefill_chunk)
     if key not in _GPU:
         prompt, ids, _, _ = full_oracle(f16)
-        rt = E.QwenB200(E.QWEN25_3B, dict(maxCtx=256, useF16=f16, prefillChunk=prefill_chunk)).build(
-            "synthetic", seed=SEED)
+        rt = E.QwenB200(E.QWEN25_3B, dict(maxCtx=256, useF16=f16, prefillChunk=prefill_chunk,
+                                          prefillTc=False)).build("synthetic", seed=SEED)
         rt.prefillBatch(prompt)
         steps = []
         for g in range(129):
@@ -351,7 +349,7 @@ def test_full_model_greedy_128(cuda, f16):
     cfg = E.QWEN25_3B
     prompt, ref, margins, steps = full_oracle(f16)
     bound = max(TIE_BOUND, 2 * worst(curve_of(gpu_teacher_forced(f16, 16), steps))[0])
-    rt = E.QwenB200(cfg, dict(maxCtx=256, useF16=f16)).build("synthetic", seed=SEED)
+    rt = E.QwenB200(cfg, dict(maxCtx=256, useF16=f16, prefillTc=False)).build("synthetic", seed=SEED)
     ids = rt.generate(prompt, 128)
     n = assert_stream(ids, ref, margins, bound)
     print(f"full model f16={f16}: {n}/128 greedy tokens identical (tie bound {bound:.2e}); "

@@ -210,6 +210,46 @@ def _attn_case(cuda, f16, pos, chunk, nh, nkv, max_ctx):
     assert np.array_equal(vrow, v.astype(np.float16).astype(np.float32) if f16 else v)
 
 
+@pytest.mark.parametrize("f16,T,q_start,nh,nkv", [(1, 200, 0, 16, 2), (0, 200, 0, 16, 2), (1, 64, 300, 16, 2),
+                                                 (0, 33, 129, 16, 2), (1, 100, 0, 32, 8), (0, 50, 10, 12, 2),
+                                                 (1, 1, 0, 16, 16), (1, 517, 0, 16, 2)])
+def test_attn_prefill(cuda, f16, T, q_start, nh, nkv):
+    """ROPE_T + K/V rows + ATTN_PREFILL_BLOCK of one pass (kernels.js:588-618,
+    684-770) against the oracle: whole prompts and later chunks (q_start > 0
+    over earlier cache rows), ragged row tiles, GQA groups of 8, 4, 6 and 1.
+    The tensor-core products carry f16 hi/lo splits of every f32 operand, so
+    the bar is f32 noise."""
+    hd, max_ctx = 128, 1024
+    c, s = O.rope_tables(max_ctx, hd, 1e6)
+    W = nh + 2 * nkv
+    kc = O.normal(max_ctx * nkv * hd, 71, 1.0)
+    vc = O.normal(max_ctx * nkv * hd, 72, 1.0)
+    if f16:
+        kc = kc.astype(np.float16).astype(np.float32)
+        vc = vc.astype(np.float16).astype(np.float32)
+    qkv = O.normal(T * W * hd, 73 + T, 1.0).reshape(T, W * hd)
+    q = O.rope_t(qkv[:, : nh * hd].ravel(), T, nh, hd, q_start, c, s, bool(f16)).reshape(T, nh * hd)
+    k = O.rope_t(qkv[:, nh * hd: (nh + nkv) * hd].ravel(), T, nkv, hd, q_start, c, s, bool(f16))
+    v = qkv[:, (nh + nkv) * hd:]
+    rnd = (lambda a: a.astype(np.float16).astype(np.float32)) if f16 else (lambda a: a)
+    kref = kc.copy().reshape(max_ctx, nkv * hd)
+    vref = vc.copy().reshape(max_ctx, nkv * hd)
+    kref[q_start:q_start + T] = rnd(k.reshape(T, nkv * hd))
+    vref[q_start:q_start + T] = rnd(v)
+    ctx = q_start + T
+    ref = O.attn_prefill(q, kref[:ctx].ravel(), vref[:ctx].ravel(), nh, nkv, hd, T, q_start, ctx)
+    dt = torch.float16 if f16 else torch.float32
+    tk = torch.from_numpy(kc).to(dt).cuda()
+    tv = torch.from_numpy(vc).to(dt).cuda()
+    tq = dev(qkv)
+    out = torch.full((T, nh * hd), float("nan"), device=cuda)
+    K.attn_prefill(tq, T, tk, tv, dev(c), dev(s), nh, nkv, q_start, max_ctx, f16, out)
+    close(host(out).ravel(), ref, 3e-5, 3e-6)
+    assert np.array_equal(host(tq)[:, : nh * hd], q)  # q rotated in place
+    assert np.array_equal(host(tk.float()).reshape(max_ctx, -1), kref)
+    assert np.array_equal(host(tv.float()).reshape(max_ctx, -1), vref)
+
+
 def test_argmax_topk_ties_reference_case(cuda):
     logits = np.full(300, -5, np.float32)
     logits[1] = 7

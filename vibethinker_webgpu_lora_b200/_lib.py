@@ -36,7 +36,7 @@ class EgOptions(C.Structure):
         ("decode_batch_capacity", C.c_int), ("sampling_top_k", C.c_int),
         ("max_sampling_top_k", C.c_int), ("attn_chunk", C.c_int), ("use_graphs", C.c_int),
         ("use_pdl", C.c_int), ("use_fused", C.c_int), ("prefill_chunk", C.c_int),
-        ("use_tc_batch", C.c_int),
+        ("use_tc_batch", C.c_int), ("prefill_tc", C.c_int), ("prefill_chunk_size", C.c_int),
     ]
 
 
@@ -111,6 +111,7 @@ _SIGS = {
     "eg_op_rmsnorm": (i32, [vp, vp, i32, f32, i32, vp, vp]),
     "eg_op_rope_qk": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),
     "eg_op_attn_decode": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
+    "eg_op_attn_prefill": (i32, [vp, i32, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     "eg_op_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]),
     "eg_op_embed": (i32, [vp, vp, vp, i32, vp, vp]),
     "eg_op_lora_a": (i32, [vp, vp, i32, i32, vp, vp]),

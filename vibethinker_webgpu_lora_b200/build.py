@@ -27,9 +27,9 @@ NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xcomp
 CXXFLAGS = ["-O3", "-std=c++17", "-fPIC", "-fopenmp", "-ffp-contract=off", "-march=x86-64-v3",
             "-I", INCLUDE, "-I", CSRC, "-I", "/usr/local/cuda/include"]
 
-CU = ["eg_kernels.cu", "eg_batch.cu", "eg_tc.cu", "eg_fused.cu", "eg_runtime.cu", "eg_noalloc.cu"]
+CU = ["eg_kernels.cu", "eg_batch.cu", "eg_tc.cu", "eg_prefill.cu", "eg_fused.cu", "eg_runtime.cu", "eg_noalloc.cu"]
 CPP = ["eg_host.cpp", "eg_safetensors.cpp"]
-HEADERS = ["eg_common.cuh", "eg_device.cuh", "eg_stream.cuh", "eg_tc.cuh", "eg_kernels.h", "eg_batch.h", "eg_fused.h",
+HEADERS = ["eg_common.cuh", "eg_device.cuh", "eg_stream.cuh", "eg_tc.cuh", "eg_kernels.h", "eg_batch.h", "eg_prefill.h", "eg_fused.h",
            "eg_host.h"]
 
 

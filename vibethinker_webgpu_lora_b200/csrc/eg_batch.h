@@ -72,6 +72,11 @@ struct BatchEpi {
   int ystride, dstride;
   const float* lora_pre;
   int lstride;
+  // tcgen05 path only, the whole-prompt prefill's arithmetic
+  // (prefillBatch, runtime.js:1936-2087): add_first: EPI_ADD is
+  // (y + W x) + LoRA as GEMM4_ADD_T then LORA_B_ADD_T; silu_f16: SiLU(g) and
+  // u meet in f16 (SILUMUL_F16, kernels.js:499-512).
+  int add_first, silu_f16;
 };
 
 // Batched int4 GEMV on the tcgen05 tensor cores (eg_tc.cu): the epilogue

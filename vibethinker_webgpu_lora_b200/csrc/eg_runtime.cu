@@ -24,6 +24,7 @@
 #include "eg_fused.h"
 #include "eg_host.h"
 #include "eg_kernels.h"
+#include "eg_prefill.h"
 #include "emberglass.h"
 
 namespace eg {
@@ -129,6 +130,14 @@ struct eg_rt {
   int64_t batch_mark = -1;  // scratch_bytes before the batch scratch was allocated
   std::vector<std::vector<uint32_t>> h_pages;  // pages held by each slot
   std::vector<uint32_t> free_pages;
+  // whole-prompt prefill (prefill_tc): scratch for p_cap positions per pass,
+  // the LoRA part allocated on the first pass with an adapter active
+  int p_cap = 0, p_gpr = 0;
+  float *p_hidden = nullptr, *p_qkv = nullptr, *p_attn = nullptr, *p_tmp = nullptr;
+  float *p_lora_d = nullptr, *p_lora_y = nullptr, *p_part = nullptr;
+  void *p_xb = nullptr, *p_xtc = nullptr;
+  int *p_xcor = nullptr, *p_xf = nullptr;
+  unsigned* p_cnt = nullptr;
 };
 
 namespace eg {
@@ -748,7 +757,7 @@ EG_API void eg_default_config(eg_config* c) {
 }
 EG_API void eg_default_options(eg_options* o) {
   if (!o) return;
-  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0, 16, 0};
+  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0, 16, 0, 1, 0};
 }
 
 EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** out) {
@@ -774,6 +783,10 @@ EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** 
   if (o.max_prefill_t <= 0 || o.max_prefill_t > o.max_ctx) o.max_prefill_t = o.max_ctx;
   if (o.decode_batch_capacity <= 0) o.decode_batch_capacity = 32;
   o.prefill_chunk = o.prefill_chunk < 2 ? 0 : std::min(o.prefill_chunk, (int)kBatchMax);
+  if (o.prefill_chunk_size < 0) return fail(EG_ERR_ARG, "prefill_chunk_size must be >= 0");
+  if (o.max_prefill_t > kPrefillMaxT && o.prefill_tc &&
+      (o.prefill_chunk_size == 0 || o.prefill_chunk_size > kPrefillMaxT))
+    o.prefill_chunk_size = kPrefillMaxT;  // one pass holds at most kPrefillMaxT positions
   if (o.max_sampling_top_k <= 0 || o.max_sampling_top_k > 64) o.max_sampling_top_k = 64;
   if (o.sampling_top_k <= 0) o.sampling_top_k = 40;
   o.max_sampling_top_k = std::max(o.max_sampling_top_k, std::min(o.sampling_top_k, 64));
@@ -922,7 +935,7 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
       q4_to_stream(l.gu_w, l.gu_s, I, H, 2, l.gu_t, rt->st);
       q4_to_stream(l.d_w, l.d_s, H, I, 1, l.d_t, rt->st);
       CK(cudaGetLastError());
-      if (rt->o.use_tc_batch) {
+      if (rt->o.use_tc_batch || rt->o.prefill_tc) {
         DALLOC(l.qkv_c, q4_tc_bytes(NQKV, H, 1), wb);
         DALLOC(l.o_c, q4_tc_bytes(H, QD, 1), wb);
         DALLOC(l.gu_c, q4_tc_bytes(I, H, 2), wb);
@@ -1074,6 +1087,7 @@ EG_API eg_status eg_sync(eg_rt* rt) {
 }
 
 static eg_status prefill_main_chunks(eg_rt* rt, int npos, int chunk);
+static eg_status prefill_tc_run(eg_rt* rt, int T);
 
 EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T) {
   eg_status s = need_ready(rt);
@@ -1086,6 +1100,7 @@ EG_API eg_status eg_prefill(eg_rt* rt, const uint32_t* ids, int T) {
   CK(cudaSetDevice(rt->o.device));
   CK(cudaMemcpyAsync(rt->ids, ids, (size_t)T * 4, cudaMemcpyHostToDevice, rt->st));
   if ((s = set_state(rt, 0, 0, 0, nullptr))) return s;
+  if (rt->o.prefill_tc) return prefill_tc_run(rt, T);
   // positions 0..T-2 in batched chunks (their K/V rows only), then the last
   // position through the decode step, which leaves its logits
   const int chunk = rt->o.prefill_chunk, pre = chunk ? T - 1 : 0;
@@ -1699,6 +1714,165 @@ static eg_status prefill_main_chunks(eg_rt* rt, int npos, int chunk) {
   return run_chunks(rt, main_target(rt), 0, npos, chunk);
 }
 
+// Scratch of the whole-prompt prefill, for passes of up to `cap` positions.
+static eg_status prefill_scratch(eg_rt* rt, int cap, bool lora) {
+  const eg_config& c = rt->c;
+  const int H = c.hidden_size, QD = c.num_heads * c.head_dim, KVD = c.num_kv_heads * c.head_dim;
+  const int I = c.intermediate_size, NQKV = QD + 2 * KVD;
+  int64_t* sb = &rt->scratch_bytes;
+  if (!rt->p_hidden) {
+    rt->p_cap = cap;
+    rt->p_gpr = (std::max(std::max(H, QD), I) + 127) / 128;
+    const size_t T = (size_t)cap, gpr = (size_t)rt->p_gpr, tiles = (T + 31) / 32;
+    DALLOC(rt->p_hidden, T * H * 4, sb);
+    DALLOC(rt->p_qkv, T * NQKV * 4, sb);
+    DALLOC(rt->p_attn, T * QD * 4, sb);
+    DALLOC(rt->p_tmp, T * I * 4, sb);
+    DALLOC(rt->p_xb, T * gpr * 512, sb);
+    DALLOC(rt->p_xcor, T * gpr * 8, sb);
+    DALLOC(rt->p_xf, T * 4, sb);
+    DALLOC(rt->p_xtc, tiles * gpr * 32 * 4 * 128, sb);
+    DALLOC(rt->p_part, gemv_q4_tc_part_bytes(), sb);
+    DALLOC(rt->p_cnt, (size_t)gemv_q4_tc_max_octets() * 4, sb);
+    CK(cudaMemsetAsync(rt->p_xtc, 0, tiles * gpr * 32 * 4 * 128, rt->st));
+    CK(cudaMemsetAsync(rt->p_cnt, 0, (size_t)gemv_q4_tc_max_octets() * 4, rt->st));
+  }
+  if (lora && !rt->p_lora_y) {
+    DALLOC(rt->p_lora_d, (size_t)rt->p_cap * 3 * kMaxRank * 4, sb);
+    DALLOC(rt->p_lora_y, (size_t)rt->p_cap * std::max(std::max(NQKV, 2 * I), H) * 4, sb);
+  }
+  return EG_OK;
+}
+
+// One prefill pass over positions off .. off + n - 1 of the single stream
+// (ids already on the device), prefillBatch's per-layer sequence
+// (runtime.js:1967-2080): RMSNORM_T, GEMM4 q/k/v (+bias, LoRA), ROPE_T and the
+// K/V rows, ATTN_PREFILL_BLOCK over keys 0 .. off + n - 1, GEMM4_ADD_T o,
+// RMSNORM_T, GEMM4 gate/up + SILUMUL, GEMM4_ADD_T down.  Returns launches.
+static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
+  const eg_config& c = rt->c;
+  const int H = c.hidden_size, hd = c.head_dim, QD = c.num_heads * hd, KVD = c.num_kv_heads * hd;
+  const int I = c.intermediate_size, NQKV = QD + 2 * KVD;
+  cudaStream_t st = rt->st;
+  int* err = reinterpret_cast<int*>(rt->fused_sync + 1);
+  const bool lora = rt->active != nullptr;
+  const int rank = lora ? rt->active->max_rank : 0;
+  const LoraMod* lt = rt->lora_table;
+  const int dstride = 3 * kMaxRank;
+  const int f16 = rt->o.kv_f16;
+  BatchPlanes xp = {};
+  xp.xb = rt->p_xb;
+  xp.xcor = rt->p_xcor;
+  xp.xf = rt->p_xf;
+  xp.gpr_max = rt->p_gpr;
+  xp.xtc = rt->p_xtc;
+  xp.tc_tpad = n > 32 ? 32 : (n + 3) / 4 * 4;
+  int launches = 0;
+  auto src = [&](int mode, const float* x, const float* g, int stride) {
+    BatchSrc b = {};
+    b.x.mode = mode;
+    b.x.x = x;
+    b.x.norm_g = g;
+    b.x.eps = c.rms_norm_eps;
+    b.x.f16 = f16;
+    b.stride = stride;
+    return b;
+  };
+  auto gemm = [&](const unsigned char* wc, int N, int K, int R, const BatchSrc& x, int nmods, int mode, float* y,
+                  int ystride, const float* bias, int m, int s1, int s2) {
+    if (lora) {
+      lora_a_batch(x, K, lt + m, nmods, rank, rt->p_lora_d, dstride, n, st, false);
+      launches++;
+    }
+    batch_stage_q4(x, K, n, xp, st, false);
+    BatchEpi e = {};
+    e.e.mode = mode;
+    e.e.y = y;
+    e.e.N = N;
+    e.e.bias = bias;
+    e.e.mods = lora ? lt + m : nullptr;
+    e.e.lora_d = rt->p_lora_d;
+    e.e.split1 = s1;
+    e.e.split2 = s2;
+    e.ystride = ystride;
+    e.dstride = dstride;
+    e.add_first = 1;
+    e.silu_f16 = f16;
+    if (lora) {
+      const int rows = mode == EPI_SILU ? 2 * N : N;
+      e.lora_pre = rt->p_lora_y;
+      e.lstride = rows;
+      lora_b_batch(e, rows, n, rt->p_lora_y, st, false);
+      launches++;
+    }
+    gemv_q4_tc(wc, N, K, R, n, xp, e, rt->p_part, rt->p_cnt, err, st, false);
+    launches += 2;
+  };
+  prefill_embed(rt->ids + off, rt->emb_w, rt->emb_s, n, H, rt->p_hidden, st);
+  launches++;
+  for (int i = 0; i < c.num_layers; i++) {
+    const Layer& l = rt->L[i];
+    gemm(l.qkv_c, NQKV, H, 1, src(X_RMS, rt->p_hidden, l.in_norm, H), 3, EPI_STORE, rt->p_qkv, NQKV,
+         c.attention_bias ? l.qkv_b : nullptr, i * 7 + 0, QD, QD + KVD);
+    prefill_rope_append(rt->p_qkv, n, NQKV, c.num_heads, c.num_kv_heads, off, rt->cosT, rt->sinT, f16, l.kc, l.vc,
+                        st);
+    PrefillAttn pa = {};
+    pa.qkv = rt->p_qkv;
+    pa.qkv_stride = NQKV;
+    pa.kc = l.kc;
+    pa.vc = l.vc;
+    pa.nh = c.num_heads;
+    pa.nkv = c.num_kv_heads;
+    pa.kv_f16 = f16;
+    pa.T = n;
+    pa.q_start = off;
+    pa.ctx = off + n;
+    pa.out = rt->p_attn;
+    pa.out_stride = QD;
+    attn_prefill(pa, st);
+    launches += 2;
+    gemm(l.o_c, H, QD, 1, src(X_PLAIN, rt->p_attn, nullptr, QD), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 3,
+         H, H);
+    gemm(l.gu_c, I, H, 2, src(X_RMS, rt->p_hidden, l.post_norm, H), 2, EPI_SILU, rt->p_tmp, I, nullptr, i * 7 + 4,
+         I, I);
+    gemm(l.d_c, H, I, 1, src(X_PLAIN, rt->p_tmp, nullptr, I), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 6, H,
+         H);
+  }
+  return launches;
+}
+
+// prefillBatch through the tcgen05 passes: _prefillFull when the prompt fits
+// one pass, else _prefillChunked; then the last row's final norm and LM head
+// (runtime.js:2081-2084), and the decode state moves to position T.
+static eg_status prefill_tc_run(eg_rt* rt, int T) {
+  const eg_config& c = rt->c;
+  const int H = c.hidden_size;
+  const int cs = rt->o.prefill_chunk_size;
+  const int pass = (cs > 0 && T > cs) ? cs : T;
+  const int cap = cs > 0 ? std::min(cs, rt->o.max_prefill_t) : rt->o.max_prefill_t;
+  eg_status s = prefill_scratch(rt, std::max(cap, pass), rt->active != nullptr);
+  if (s) return s;
+  if (pass > rt->p_cap) return fail(EG_ERR_STATE, "prefill pass of %d positions > scratch %d", pass, rt->p_cap);
+  int last = 0;
+  for (int off = 0; off < T; off += pass) {
+    last = std::min(pass, T - off);
+    enqueue_prefill_pass(rt, off, last);
+  }
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(rt->hidden, rt->p_hidden + (size_t)(last - 1) * H, (size_t)H * 4, cudaMemcpyDeviceToDevice,
+                     rt->st));
+  XSrc xf = {};
+  xf.mode = X_RMS;
+  xf.x = rt->hidden;
+  xf.norm_g = rt->final_norm;
+  xf.eps = c.rms_norm_eps;
+  xf.f16 = rt->o.kv_f16;
+  gemv_q8(rt->emb_t, rt->emb_s, c.vocab_size, H, xf, rt->logits, nullptr, rt->st, false,
+          GemvWork{reinterpret_cast<int*>(rt->fused_sync + 1)});
+  CK(cudaGetLastError());
+  return set_state(rt, T, 0, 0, nullptr);
+}
+
 EG_API eg_status eg_seq_prefill(eg_rt* rt, int slot) {
   eg_status s = need_ready(rt);
   if (s) return s;
@@ -2259,6 +2433,35 @@ EG_API eg_status eg_op_rope_qk(float* q, float* k, int nq, int nkv, int pos, con
                                const float* sin_t, int f16, void* stream) {
   if (!q || !k || !cos_t || !sin_t || nq < 0 || nkv < 0 || pos < 0) return fail(EG_ERR_ARG, "rope_qk: bad argument");
   rope_qk(q, k, nq, nkv, pos, cos_t, sin_t, f16, OPSTREAM);
+  CK(cudaGetLastError());
+  return EG_OK;
+}
+
+EG_API eg_status eg_op_attn_prefill(float* qkv, int T, void* k_cache, void* v_cache, const float* cos_t,
+                                    const float* sin_t, int nh, int nkv, int q_start, int max_ctx, int kv_f16,
+                                    float* out, void* stream) {
+  if (!qkv || !k_cache || !v_cache || !cos_t || !sin_t || !out) return fail(EG_ERR_ARG, "attn_prefill: null argument");
+  if (nh <= 0 || nh > 64 || nkv <= 0 || nh % nkv || T < 1 || q_start < 0 || q_start + T > max_ctx)
+    return fail(EG_ERR_ARG, "attn_prefill: bad heads or rows");
+  if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(k_cache) |
+       reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(EG_ERR_ARG, "attn_prefill: 16-byte aligned buffers required");
+  const int stride = (nh + 2 * nkv) * 128;
+  prefill_rope_append(qkv, T, stride, nh, nkv, q_start, cos_t, sin_t, kv_f16, k_cache, v_cache, OPSTREAM);
+  PrefillAttn a = {};
+  a.qkv = qkv;
+  a.qkv_stride = stride;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.nh = nh;
+  a.nkv = nkv;
+  a.kv_f16 = kv_f16;
+  a.T = T;
+  a.q_start = q_start;
+  a.ctx = q_start + T;
+  a.out = out;
+  a.out_stride = nh * 128;
+  attn_prefill(a, OPSTREAM);
   CK(cudaGetLastError());
   return EG_OK;
 }

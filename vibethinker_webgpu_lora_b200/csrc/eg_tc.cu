@@ -159,7 +159,17 @@ __device__ __forceinline__ void tc_store(const TcArgs& a, int t, int n, float v,
       g = __fadd_rn(g, lp[(size_t)t * a.be.lstride + n]);
       u = __fadd_rn(u, lp[(size_t)t * a.be.lstride + E.N + n]);
     }
-    E.y[(size_t)t * a.be.ystride + n] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u);
+    const float sg = __fdiv_rn(g, __fadd_rn(1.f, expf(-g)));
+    E.y[(size_t)t * a.be.ystride + n] =
+        a.be.silu_f16 ? __half2float(__hmul(__float2half_rn(sg), __float2half_rn(u))) : __fmul_rn(sg, u);
+    return;
+  }
+  if (a.be.add_first && E.mode == EPI_ADD) {  // (y + W x) + LoRA
+    float* yp = E.y + (size_t)t * a.be.ystride + n;
+    float o = __fadd_rn(__ldcg(yp), v);
+    if (E.bias) o = __fadd_rn(o, E.bias[n]);
+    if (lp) o = __fadd_rn(o, lp[(size_t)t * a.be.lstride + n]);
+    *yp = o;
     return;
   }
   float o = v;

@@ -79,6 +79,13 @@ def rope_qk(q, k, nq, nkv, pos, cos_t, sin_t, f16, stream=None):
                                   int(f16), _st(stream)))
 
 
+def attn_prefill(qkv, T, k_cache, v_cache, cos_t, sin_t, nh, nkv, q_start, max_ctx, kv_f16, out, stream=None):
+    """ROPE_T + K/V rows + ATTN_PREFILL_BLOCK of one prefill pass (qkv rotated in place)."""
+    L.check(L.lib().eg_op_attn_prefill(L.ptr(qkv), T, L.ptr(k_cache), L.ptr(v_cache), L.ptr(cos_t),
+                                       L.ptr(sin_t), nh, nkv, q_start, max_ctx, int(kv_f16), L.ptr(out),
+                                       _st(stream)))
+
+
 def attn_decode(qkv, k_cache, v_cache, cos_t, sin_t, nh, nkv, pos, max_ctx, kv_f16, out, chunk=0,
                 stream=None):
     L.check(L.lib().eg_op_attn_decode(L.ptr(qkv), L.ptr(k_cache), L.ptr(v_cache), L.ptr(cos_t),

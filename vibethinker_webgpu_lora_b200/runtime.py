@@ -52,6 +52,8 @@ class QwenB200:
         o.use_fused = int(bool(opts.get("useFused", False)))
         o.prefill_chunk = int(opts.get("prefillChunk", 16))
         o.use_tc_batch = int(bool(opts.get("useTcBatch", False)))
+        o.prefill_tc = int(bool(opts.get("prefillTc", True)))
+        o.prefill_chunk_size = int(opts.get("prefillChunkSize", 0))
         self.opts = o
         h = C.c_void_p()
         L.check(L.lib().eg_create(C.byref(_cfg_struct(self.cfg)), C.byref(o), C.byref(h)))
