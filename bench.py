@@ -636,6 +636,66 @@ def ncu_probe(ctx):
     print(json.dumps({"ncu_probe": ctx, "launches_per_step": rt.lastDispatchCount}))
 
 
+def ncu_probe_prefill(T):
+    """Profiling target of the whole-prompt prefill: two prefillBatch calls
+    of a T-token prompt (the first allocates the prefill scratch), exit."""
+    import vibethinker_webgpu_lora_b200 as E
+    from vibethinker_webgpu_lora_b200.quantize import synth_ids
+    cfg = E.QWEN25_3B
+    rt = E.QwenB200(cfg, {"maxCtx": T + 8}).build("synthetic", seed=SEED)
+    p = synth_ids(T, PROMPT_SEED, cfg["vocabSize"])
+    rt.prefillBatch(p)
+    rt.prefillBatch(p)
+    rt.sync()
+    print(json.dumps({"ncu_probe_prefill": T}))
+
+
+def ncu_probe_gemm(T):
+    """Profiling target of one whole-prompt tcgen05 GEMM launch shape: the
+    down projection (2048 x 11008 int4, random words and scales) against T
+    token rows, three calls, exit (a few tens of MB on the device)."""
+    import numpy as np
+    import torch
+
+    from vibethinker_webgpu_lora_b200 import kernels as K
+    N, Kd = 2048, 11008
+    rng = np.random.default_rng(1)
+    w = torch.from_numpy(rng.integers(0, 2 ** 32, N * Kd // 8, dtype=np.uint32)).cuda()
+    sc = torch.from_numpy(rng.uniform(1e-3, 2e-3, N * (Kd // 128)).astype(np.float32)).cuda()
+    ws = torch.zeros(K.q4_stream_bytes(N, Kd), dtype=torch.uint8, device="cuda")
+    K.q4_to_stream(w, sc, N, Kd, ws)
+    wc = torch.zeros(K.q4_tc_bytes(N, Kd), dtype=torch.uint8, device="cuda")
+    K.q4_stream_to_tc(ws, N, Kd, wc)
+    x = torch.randn(T, Kd, device="cuda")
+    y = torch.empty(T, N, device="cuda")
+    for _ in range(3):
+        K.gemm_q4_stream(x, T, wc, N, Kd, y, use_tc=True)
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_probe_gemm": T}))
+
+
+def ncu_probe_attn(T):
+    """Profiling target of the prefill attention: one KV layer of the 3B
+    shape (16 query / 2 KV heads, f16 cache), a T-row pass from position 0,
+    three calls, exit (tens of MB on the device)."""
+    import torch
+
+    from vibethinker_webgpu_lora_b200 import kernels as K
+    nh, nkv, hd = 16, 2, 128
+    g = torch.Generator(device="cuda").manual_seed(1)
+    qkv0 = torch.randn(T, (nh + 2 * nkv) * hd, device="cuda", generator=g)
+    kc = torch.zeros(T, nkv * hd, dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    ang = torch.arange(T, device="cuda", dtype=torch.float32)[:, None] * torch.ones(hd, device="cuda")
+    cos_t, sin_t = torch.cos(ang * 1e-3).contiguous(), torch.sin(ang * 1e-3).contiguous()
+    out = torch.empty(T, nh * hd, device="cuda")
+    for _ in range(3):
+        qkv = qkv0.clone()
+        K.attn_prefill(qkv, T, kc, vc, cos_t, sin_t, nh, nkv, 0, T, 1, out)
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_probe_attn": T}))
+
+
 def ncu_probe_batch(steps):
     """Profiling target of the batched path: 16 slots with 8-token prompts,
     `steps` batched greedy steps (launches_per_step launches each), exit."""
@@ -663,7 +723,7 @@ def main():
                     help="skip the ctx 4096/7800 and configs[0] GEMV sub-objects")
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "graph"],
                     help="decode path: persistent fused kernel or per-op CUDA graph")
-    ap.add_argument("--workload", default="decode", choices=["decode", "batch16", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "batch16", "prefill", "gemm4", "attn"],
                     help="decode: configs[1]/[2] (the headline); batch16: configs[4]; "
                          "prefill: configs[3]")
     ap.add_argument("--ncu-probe", type=int, default=0, metavar="CTX",
@@ -673,9 +733,17 @@ def main():
     if args.ncu_probe:
         if args.workload == "batch16":
             ncu_probe_batch(args.ncu_probe)
+        elif args.workload == "prefill":
+            ncu_probe_prefill(args.ncu_probe)
+        elif args.workload == "gemm4":
+            ncu_probe_gemm(args.ncu_probe)
+        elif args.workload == "attn":
+            ncu_probe_attn(args.ncu_probe)
         else:
             ncu_probe(args.ncu_probe)
         return
+    if args.workload in ("gemm4", "attn"):
+        ap.error(f"--workload {args.workload} is a profiling target: give --ncu-probe T")
     assert args.warmup >= 3, "at least 3 warm-up steps"
     ws, rank, local = dist_setup() if args.impl == "ours" else (
         int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)

@@ -75,11 +75,10 @@ __global__ void __launch_bounds__(kStageThreads) batch_stage_q4_kernel(BatchSrc 
   const XSrc s = lane_src(b, v);
   uint2* xb = reinterpret_cast<uint2*>(xp.xb) + (size_t)v * xp.gpr_max * 64;
   stage_xd<MAXU, NORM, kStageThreads>(s, K, xb, xp.xcor + (size_t)v * 2 * xp.gpr_max, xp.xf + v,
-                                      sred, pdl,
-                                      xp.xtc ? static_cast<unsigned char*>(xp.xtc) +
-                                                   (size_t)(v / xp.tc_tpad) * (K / kGroup) * 4 * xp.tc_tpad * 128
-                                             : nullptr,
-                                      4 * xp.tc_tpad, 4 * (v % xp.tc_tpad));
+                                      sred, pdl, static_cast<unsigned char*>(xp.xtc), 4 * xp.tc_tpad, 4 * v,
+                                      xp.xh ? static_cast<unsigned char*>(xp.xh) + (size_t)(v / 128) * (K / kGroup) * 65536
+                                            : nullptr,
+                                      v % 128);
   if (pdl) pdl_launch_dependents();
 }
 

@@ -55,11 +55,13 @@ struct BatchPlanes {
   // int4 only, optional: the same digit planes as the B operand of the
   // tcgen05 GEMV (gemv_q4_tc): per group, N = 4 tc_tpad columns (lane v,
   // plane p at column 4v + p) x 128 bytes, K-major 8 x 16-byte core
-  // matrices, the 8 k-chunks N / 8 core matrices apart.  More lanes than
-  // tc_tpad (whole-prompt mode, tc_tpad = 32): lane v sits in token tile
-  // v / 32 at column 4 (v % 32) + p, the tiles gpr x 16 KB apart.
+  // matrices, the 8 k-chunks N / 8 core matrices apart.
   void* xtc;
   int tc_tpad;
+  // int4 only, optional, instead of the digit planes: the f16 hi/lo operand
+  // of the whole-prompt GEMM (stage_xd's xh), tiles of 128 lanes, each
+  // gpr_max groups x 64 KB
+  void* xh;
 };
 
 // Epilogue of a batched int4 GEMV: the single-lane epilogue (bias /
@@ -95,6 +97,17 @@ size_t gemv_q4_tc_part_bytes();
 size_t q4_tc_bytes(int N, int K, int R);
 void q4_stream_to_tc(const unsigned char* ws, int N, int K, int R, unsigned char* out, cudaStream_t st);
 int gemv_q4_tc_max_octets();
+
+// Whole-prompt GEMM on the tcgen05 tensor cores (eg_tc.cu), for more than 32
+// token rows, kind::f16: A images expanded once from the tc layout
+// (q4_tc_to_a16: per (octet, group) the 128 x 128 nibble values as f16, and
+// the 128 group scales), B = the rows' f16 hi/lo operand (xp.xh, staged by
+// batch_stage_q4), gemv_q4_tc's epilogue.
+size_t q4_a16_bytes(int N, int K, int R);
+size_t q4_a16_scale_bytes(int N, int K, int R);
+void q4_tc_to_a16(const unsigned char* wc, int N, int K, int R, unsigned char* a16, float* s16, cudaStream_t st);
+void gemm_q4_prefill(const unsigned char* a16, const float* s16, int N, int K, int R, int lanes,
+                     const BatchPlanes& xp, const BatchEpi& be, int* err, cudaStream_t st);
 
 // pdl: launched as programmatic dependents of the previous kernel (each
 // kernel waits with griddepcontrol.wait before reading earlier outputs).

@@ -201,10 +201,16 @@ __device__ __forceinline__ void setup_x(const XSrc& s, int K, XCtx& c, float* sr
 // xtc (optional): the same planes also as the tcgen05 B operand (see
 // BatchPlanes::xtc), this vector at columns tc_col0 .. tc_col0 + 3 of
 // tc_ncol.
+// xh (optional, instead of all of the above but *xf): the f16 operand of
+// the whole-prompt GEMM, this vector as column xh_col of a 128-column tile
+// (the tile's group G at xh + G * 64 KB): x' = x * 2^f with max |x'| < 2^15
+// split into f16 hi = f16(x') and lo = f16(x' - hi), stacked along k (hi
+// elements 0..127, lo 128..255), K-major 8 x 16-byte core matrices, the 32
+// eight-element k-chunks 2 KB apart; *xf = f.
 template <int MAXU, bool NORM, int NT = kCtaThreads>
 __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, int* xf, float* sred,
                          int pdl, unsigned char* xtc = nullptr, int tc_ncol = 0,
-                         int tc_col0 = 0) {
+                         int tc_col0 = 0, unsigned char* xh = nullptr, int xh_col = 0) {
   const int K8 = K / 8;
   float v[MAXU][8];
   float gw[NORM ? MAXU : 1][8];
@@ -288,6 +294,34 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, int* xf, fl
 #pragma unroll
     for (int j = 0; j < 8; j++) am = fmaxf(am, fabsf(v[i][j]));
   am = block_max_n<NT>(am, sred);
+  if (xh) {
+    // am < 2^ex; f = 15 - ex puts max |x'| below 2^15 (f = 0 for a zero vector)
+    const int ex = ((__float_as_int(am) >> 23) & 0xFF) - 126;
+    const int f = am > 0.f ? max(-126, min(126, 15 - ex)) : 0;
+    const float sc = __int_as_float((127 + f) << 23);
+    if (threadIdx.x == 0) *xf = f;
+#pragma unroll
+    for (int i = 0; i < MAXU; i++) {
+      const int u = threadIdx.x + i * NT;
+      if (u >= K8) continue;
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float a = __fmul_rn(v[i][j], sc), b = __fmul_rn(v[i][j + 1], sc);
+        const __half2 h = __floats2half2_rn(a, b);
+        const float2 hf = __half22float2(h);
+        const __half2 l = __floats2half2_rn(__fsub_rn(a, hf.x), __fsub_rn(b, hf.y));
+        hi[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[j / 2] = *reinterpret_cast<const uint32_t*>(&l);
+      }
+      const int G = u >> 4, q = u & 15;
+      unsigned char* gb = xh + (size_t)G * 65536 + (xh_col >> 3) * 128 + (xh_col & 7) * 16;
+      *reinterpret_cast<uint4*>(gb + q * 2048) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      *reinterpret_cast<uint4*>(gb + (16 + q) * 2048) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    bar_sync_n<NT>();
+    return;
+  }
   // am < 2^ex, ex from the exponent field (0 and subnormals: f = 126)
   const int ex = ((__float_as_int(am) >> 23) & 0xFF) - 126;
   const int f = min(30 - ex, 126);

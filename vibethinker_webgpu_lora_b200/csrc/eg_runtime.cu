@@ -54,6 +54,9 @@ struct Layer {
   unsigned char *qkv_t = nullptr, *o_t = nullptr, *gu_t = nullptr, *d_t = nullptr;
   // the same blocks octet-major for the tcgen05 batched GEMV (q4_stream_to_tc)
   unsigned char *qkv_c = nullptr, *o_c = nullptr, *gu_c = nullptr, *d_c = nullptr;
+  // f16 A images + row scales of the whole-prompt GEMM (q4_tc_to_a16), prefill_tc
+  unsigned char *qkv_a = nullptr, *o_a = nullptr, *gu_a = nullptr, *d_a = nullptr;
+  float *qkv_s16 = nullptr, *o_s16 = nullptr, *gu_s16 = nullptr, *d_s16 = nullptr;
 };
 
 struct DevState {
@@ -135,7 +138,7 @@ struct eg_rt {
   int p_cap = 0, p_gpr = 0;
   float *p_hidden = nullptr, *p_qkv = nullptr, *p_attn = nullptr, *p_tmp = nullptr;
   float *p_lora_d = nullptr, *p_lora_y = nullptr, *p_part = nullptr;
-  void *p_xb = nullptr, *p_xtc = nullptr;
+  void *p_xb = nullptr, *p_xtc = nullptr, *p_xh = nullptr;
   int *p_xcor = nullptr, *p_xf = nullptr;
   unsigned* p_cnt = nullptr;
 };
@@ -946,6 +949,21 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
         q4_stream_to_tc(l.d_t, H, I, 1, l.d_c, rt->st);
         CK(cudaGetLastError());
       }
+      if (rt->o.prefill_tc) {
+        DALLOC(l.qkv_a, q4_a16_bytes(NQKV, H, 1), wb);
+        DALLOC(l.o_a, q4_a16_bytes(H, QD, 1), wb);
+        DALLOC(l.gu_a, q4_a16_bytes(I, H, 2), wb);
+        DALLOC(l.d_a, q4_a16_bytes(H, I, 1), wb);
+        DALLOC(l.qkv_s16, q4_a16_scale_bytes(NQKV, H, 1), wb);
+        DALLOC(l.o_s16, q4_a16_scale_bytes(H, QD, 1), wb);
+        DALLOC(l.gu_s16, q4_a16_scale_bytes(I, H, 2), wb);
+        DALLOC(l.d_s16, q4_a16_scale_bytes(H, I, 1), wb);
+        q4_tc_to_a16(l.qkv_c, NQKV, H, 1, l.qkv_a, l.qkv_s16, rt->st);
+        q4_tc_to_a16(l.o_c, H, QD, 1, l.o_a, l.o_s16, rt->st);
+        q4_tc_to_a16(l.gu_c, I, H, 2, l.gu_a, l.gu_s16, rt->st);
+        q4_tc_to_a16(l.d_c, H, I, 1, l.d_a, l.d_s16, rt->st);
+        CK(cudaGetLastError());
+      }
     }
     DALLOC(rt->emb_t, q8_stream_bytes(c.vocab_size, H), wb);
     q8_to_stream(rt->emb_w, c.vocab_size, H, rt->emb_t, rt->st);
@@ -1520,7 +1538,7 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
   const int dstride = 3 * kMaxRank;
   const SeqTable& sq = tg.sq;
   const bool chunk = sq.chunk != 0;
-  BatchPlanes xp;
+  BatchPlanes xp = {};
   xp.xb = rt->b_xb;
   xp.xcor = rt->b_xcor;
   xp.xmul = rt->b_xmul;
@@ -1723,7 +1741,7 @@ static eg_status prefill_scratch(eg_rt* rt, int cap, bool lora) {
   if (!rt->p_hidden) {
     rt->p_cap = cap;
     rt->p_gpr = (std::max(std::max(H, QD), I) + 127) / 128;
-    const size_t T = (size_t)cap, gpr = (size_t)rt->p_gpr, tiles = (T + 31) / 32;
+    const size_t T = (size_t)cap, gpr = (size_t)rt->p_gpr, tiles = (T + 127) / 128;
     DALLOC(rt->p_hidden, T * H * 4, sb);
     DALLOC(rt->p_qkv, T * NQKV * 4, sb);
     DALLOC(rt->p_attn, T * QD * 4, sb);
@@ -1731,10 +1749,12 @@ static eg_status prefill_scratch(eg_rt* rt, int cap, bool lora) {
     DALLOC(rt->p_xb, T * gpr * 512, sb);
     DALLOC(rt->p_xcor, T * gpr * 8, sb);
     DALLOC(rt->p_xf, T * 4, sb);
-    DALLOC(rt->p_xtc, tiles * gpr * 32 * 4 * 128, sb);
+    DALLOC(rt->p_xtc, gpr * 32 * 4 * 128, sb);
+    DALLOC(rt->p_xh, tiles * gpr * 65536, sb);
     DALLOC(rt->p_part, gemv_q4_tc_part_bytes(), sb);
     DALLOC(rt->p_cnt, (size_t)gemv_q4_tc_max_octets() * 4, sb);
-    CK(cudaMemsetAsync(rt->p_xtc, 0, tiles * gpr * 32 * 4 * 128, rt->st));
+    CK(cudaMemsetAsync(rt->p_xtc, 0, gpr * 32 * 4 * 128, rt->st));
+    CK(cudaMemsetAsync(rt->p_xh, 0, tiles * gpr * 65536, rt->st));
     CK(cudaMemsetAsync(rt->p_cnt, 0, (size_t)gemv_q4_tc_max_octets() * 4, rt->st));
   }
   if (lora && !rt->p_lora_y) {
@@ -1765,8 +1785,10 @@ static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
   xp.xcor = rt->p_xcor;
   xp.xf = rt->p_xf;
   xp.gpr_max = rt->p_gpr;
-  xp.xtc = rt->p_xtc;
-  xp.tc_tpad = n > 32 ? 32 : (n + 3) / 4 * 4;
+  // up to 32 rows: split-K gemv_q4_tc over digit planes; more: the f16 GEMM
+  xp.xtc = n > 32 ? nullptr : rt->p_xtc;
+  xp.tc_tpad = (n + 3) / 4 * 4;
+  xp.xh = n > 32 ? rt->p_xh : nullptr;
   int launches = 0;
   auto src = [&](int mode, const float* x, const float* g, int stride) {
     BatchSrc b = {};
@@ -1778,8 +1800,9 @@ static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
     b.stride = stride;
     return b;
   };
-  auto gemm = [&](const unsigned char* wc, int N, int K, int R, const BatchSrc& x, int nmods, int mode, float* y,
-                  int ystride, const float* bias, int m, int s1, int s2) {
+  auto gemm = [&](const unsigned char* wc, const unsigned char* a16, const float* s16, int N, int K, int R,
+                  const BatchSrc& x, int nmods, int mode, float* y, int ystride, const float* bias, int m, int s1,
+                  int s2) {
     if (lora) {
       lora_a_batch(x, K, lt + m, nmods, rank, rt->p_lora_d, dstride, n, st, false);
       launches++;
@@ -1805,14 +1828,17 @@ static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
       lora_b_batch(e, rows, n, rt->p_lora_y, st, false);
       launches++;
     }
-    gemv_q4_tc(wc, N, K, R, n, xp, e, rt->p_part, rt->p_cnt, err, st, false);
+    if (n > 32)
+      gemm_q4_prefill(a16, s16, N, K, R, n, xp, e, err, st);
+    else
+      gemv_q4_tc(wc, N, K, R, n, xp, e, rt->p_part, rt->p_cnt, err, st, false);
     launches += 2;
   };
   prefill_embed(rt->ids + off, rt->emb_w, rt->emb_s, n, H, rt->p_hidden, st);
   launches++;
   for (int i = 0; i < c.num_layers; i++) {
     const Layer& l = rt->L[i];
-    gemm(l.qkv_c, NQKV, H, 1, src(X_RMS, rt->p_hidden, l.in_norm, H), 3, EPI_STORE, rt->p_qkv, NQKV,
+    gemm(l.qkv_c, l.qkv_a, l.qkv_s16, NQKV, H, 1, src(X_RMS, rt->p_hidden, l.in_norm, H), 3, EPI_STORE, rt->p_qkv, NQKV,
          c.attention_bias ? l.qkv_b : nullptr, i * 7 + 0, QD, QD + KVD);
     prefill_rope_append(rt->p_qkv, n, NQKV, c.num_heads, c.num_kv_heads, off, rt->cosT, rt->sinT, f16, l.kc, l.vc,
                         st);
@@ -1831,11 +1857,11 @@ static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
     pa.out_stride = QD;
     attn_prefill(pa, st);
     launches += 2;
-    gemm(l.o_c, H, QD, 1, src(X_PLAIN, rt->p_attn, nullptr, QD), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 3,
+    gemm(l.o_c, l.o_a, l.o_s16, H, QD, 1, src(X_PLAIN, rt->p_attn, nullptr, QD), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 3,
          H, H);
-    gemm(l.gu_c, I, H, 2, src(X_RMS, rt->p_hidden, l.post_norm, H), 2, EPI_SILU, rt->p_tmp, I, nullptr, i * 7 + 4,
+    gemm(l.gu_c, l.gu_a, l.gu_s16, I, H, 2, src(X_RMS, rt->p_hidden, l.post_norm, H), 2, EPI_SILU, rt->p_tmp, I, nullptr, i * 7 + 4,
          I, I);
-    gemm(l.d_c, H, I, 1, src(X_PLAIN, rt->p_tmp, nullptr, I), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 6, H,
+    gemm(l.d_c, l.d_a, l.d_s16, H, I, 1, src(X_PLAIN, rt->p_tmp, nullptr, I), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 6, H,
          H);
   }
   return launches;
@@ -2339,14 +2365,16 @@ EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, con
   if (reinterpret_cast<uintptr_t>(ws) & 15) return fail(EG_ERR_ARG, "gemm_q4_stream: ws must be 16-byte aligned");
   const int gpr = K / 128, tpad = T > 32 ? 32 : (T + 3) / 4 * 4;
   const size_t xb = (size_t)T * gpr * 512, xc = ((size_t)T * gpr * 8 + 255) / 256 * 256,
-               xtc = (size_t)((T + tpad - 1) / tpad) * gpr * 4 * tpad * 128;
+               xtc = T > 32 && use_tc ? (size_t)(T + 127) / 128 * gpr * 65536 : (size_t)gpr * 4 * tpad * 128;
   const size_t cnt = (size_t)gemv_q4_tc_max_octets() * 4, part = gemv_q4_tc_part_bytes();
   const size_t xfb = ((size_t)T * 4 + 255) / 256 * 256;  // one exponent per token
   // [err | xb | xcor | xf | xtc | counters | partials], every piece 256-byte aligned
+  // more than 32 rows: the whole-prompt GEMM over A images built here from ws
+  const size_t a8 = use_tc && T > 32 ? q4_a16_bytes(N, K, 1) : 0, s8 = use_tc && T > 32 ? q4_a16_scale_bytes(N, K, 1) : 0;
   const size_t o_xb = 256, o_xc = o_xb + xb, o_xf = o_xc + xc, o_tc = o_xf + xfb, o_cnt = o_tc + xtc,
-               o_part = o_cnt + cnt;
+               o_part = o_cnt + cnt, o_a8 = o_part + part, o_s8 = o_a8 + a8;
   void* scr = nullptr;
-  eg_status s = op_scratch(o_part + part, &scr);
+  eg_status s = op_scratch(o_s8 + s8, &scr);
   if (s) return s;
   char* b = static_cast<char*>(scr);
   int* err = reinterpret_cast<int*>(b);
@@ -2355,7 +2383,8 @@ EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, con
   xp.xcor = reinterpret_cast<int*>(b + o_xc);
   xp.xf = reinterpret_cast<int*>(b + o_xf);
   xp.gpr_max = gpr;
-  xp.xtc = use_tc ? b + o_tc : nullptr;
+  xp.xtc = use_tc && T <= 32 ? b + o_tc : nullptr;
+  xp.xh = use_tc && T > 32 ? b + o_tc : nullptr;  // the f16 operand of the whole-prompt GEMM
   xp.tc_tpad = tpad;
   unsigned* counters = reinterpret_cast<unsigned*>(b + o_cnt);
   float* prt = reinterpret_cast<float*>(b + o_part);
@@ -2373,7 +2402,12 @@ EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, con
   be.e.bias = bias;
   be.e.split1 = be.e.split2 = N;
   be.ystride = N;
-  if (use_tc)
+  if (use_tc && T > 32) {
+    unsigned char* ia = reinterpret_cast<unsigned char*>(b + o_a8);
+    float* is = reinterpret_cast<float*>(b + o_s8);
+    q4_tc_to_a16(static_cast<const unsigned char*>(ws), N, K, 1, ia, is, OPSTREAM);
+    gemm_q4_prefill(ia, is, N, K, 1, T, xp, be, err, OPSTREAM);
+  } else if (use_tc)
     gemv_q4_tc(static_cast<const unsigned char*>(ws), N, K, 1, T, xp, be, prt, counters, err, OPSTREAM, false);
   else
     gemv_q4_batch(static_cast<const unsigned char*>(ws), N, K, T, xp, be, err, OPSTREAM, false);

@@ -63,13 +63,8 @@ constexpr uint32_t kTcTmemCols = 256;
 
 struct TcArgs {
   const unsigned char* ws;   // tc layout (q4_stream_to_tc)
-  int N, K, R, lanes, tpad;  // lanes: token vectors; tpad: tokens per B tile (<= 32)
-  // 0: the CTAs split the (octet, group) items of one token tile evenly
-  // (split-K where a CTA boundary falls inside an octet); 1: whole prompt,
-  // ceil(lanes / 32) token tiles, each CTA takes whole (token tile, octet)
-  // pairs (every group), so no octet is split
-  int whole;
-  const unsigned char* xtc;  // B planes: per (token tile, group) 4 tpad x 128 bytes
+  int N, K, R, lanes, tpad;  // lanes: token vectors (<= 32); tpad: lanes rounded up to 4
+  const unsigned char* xtc;  // B planes: per group 4 tpad x 128 bytes
   const int* xf;             // [lane] fixed-point exponent
   BatchEpi be;
   float* part;               // [ncta][2][32][128]
@@ -99,37 +94,23 @@ __device__ __forceinline__ int cta_of(int items, int ncta, int i) {
   return c;
 }
 
-// One run of a CTA: token tile tau, octet o, groups [g0, g1).
+// One run of a CTA: octet o, groups [g0, g1).
 struct Seg {
-  int tau, o, g0, g1;
+  int o, g0, g1;
 };
 
-// The CTA's runs in order, the same sequence for every warp role.
+// The CTA's runs (its share of the (octet, group) items, octet-major) in
+// order, the same sequence for every warp role.
 struct SegIter {
-  int whole, gpr, octets;
-  int i, i1;             // split mode: next item, end
-  int pr, step, npairs;  // whole mode: next (token tile, octet) pair
-  __device__ SegIter(const TcArgs& a, int gpr_, int octets_) : whole(a.whole), gpr(gpr_), octets(octets_) {
+  int gpr;
+  int i, i1;  // next item, end
+  __device__ SegIter(int gpr_, int octets) : gpr(gpr_) {
     const int items = octets * gpr;
     i = item_lo(items, gridDim.x, blockIdx.x);
     i1 = item_lo(items, gridDim.x, blockIdx.x + 1);
-    pr = blockIdx.x;
-    step = gridDim.x;
-    npairs = ((a.lanes + 31) / 32) * octets;
   }
   __device__ bool next(Seg& sg) {
-    if (whole) {  // octet-major: CTAs running at once share an octet's weights in L2
-      if (pr >= npairs) return false;
-      const int ntau = npairs / octets;
-      sg.o = pr / ntau;
-      sg.tau = pr % ntau;
-      sg.g0 = 0;
-      sg.g1 = gpr;
-      pr += step;
-      return true;
-    }
     if (i >= i1) return false;
-    sg.tau = 0;
     sg.o = i / gpr;
     sg.g0 = i % gpr;
     sg.g1 = min(gpr, sg.g0 + (i1 - i));
@@ -150,7 +131,8 @@ struct Ring {
 };
 
 // The final epilogue of one row and token (batch_epilogue's arithmetic).
-__device__ __forceinline__ void tc_store(const TcArgs& a, int t, int n, float v, float up) {
+template <class Args>
+__device__ __forceinline__ void tc_store(const Args& a, int t, int n, float v, float up) {
   const Epi& E = a.be.e;
   const float* lp = a.be.lora_pre;
   if (a.R == 2) {
@@ -241,7 +223,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     // ---------------------------------------------------- weight stages
     // the weights depend on no earlier kernel: no griddepcontrol.wait here
     if (a.pdl && lane == 0) pdl_launch_dependents();
-    SegIter it(a, gpr, octets);
+    SegIter it(gpr, octets);
     Seg sg;
     int s = 0, ph = 0, issued = 0;
     while (it.next(sg)) {
@@ -277,14 +259,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     if (a.pdl) pdl_wait();
     Ring rb{0, 0};
     int nb = 0;
-    SegIter it(a, gpr, octets);
+    SegIter it(gpr, octets);
     Seg sg;
     while (it.next(sg))
       for (int g = sg.g0; g < sg.g1; g++, nb++) {
         if (!dead && !tc_wait(&S.b_empty[rb.slot], rb.ph ^ 1, a.err)) dead = true;
         if (lane == 0) {
           mbar_expect_tx(&S.b_full[rb.slot], bbytes);
-          bulk_g2s(bbuf + (size_t)rb.slot * kTcBBytes, a.xtc + ((size_t)sg.tau * gpr + g) * bbytes, bbytes,
+          bulk_g2s(bbuf + (size_t)rb.slot * kTcBBytes, a.xtc + (size_t)g * bbytes, bbytes,
                    &S.b_full[rb.slot]);
         }
         __syncwarp();
@@ -304,7 +286,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     const uint32_t idesc = idesc_i8(128, ncol) | (1u << 7);  // A signed
     Ring ra{0, 0}, rb{0, 0}, rt{0, 0};
     int nm = 0;
-    SegIter it(a, gpr, octets);
+    SegIter it(gpr, octets);
     Seg sg;
     while (it.next(sg))
       for (int g = sg.g0; g < sg.g1; g++, nm++) {
@@ -343,7 +325,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
   } else if (warp < kTcConvWarps) {
     // ---------------------------------------------------- convert to A
     const int ct = threadIdx.x;  // 0..255
-    SegIter it(a, gpr, octets);
+    SegIter it(gpr, octets);
     Seg sg;
     int s = 0, ph = 0;
     Ring ra{0, 0}, rs{0, 0};
@@ -408,7 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     for (int j = 0; j < TH; j++) acc01[j] = acc23[j] = 0.f;
     const int first_o = item_lo(items, ncta, c) / gpr;
     Ring rt{0, 0}, rs{0, 0};
-    SegIter it(a, gpr, octets);
+    SegIter it(gpr, octets);
     Seg sg;
     while (it.next(sg)) {
       for (int g = sg.g0; g < sg.g1; g++) {
@@ -443,19 +425,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.acc_empty[qt]);
       }
-      // ---- run done: final or partial output of octet sg.o, token tile sg.tau
-      const int o_ = sg.o, t0 = 32 * sg.tau;  // the tile's first token
+      // ---- run done: final or partial output of octet sg.o
+      const int o_ = sg.o;
       float y[TH];
 #pragma unroll
       for (int j = 0; j < TH; j++) {
-        const int t = t0 + tb + j;
+        const int t = tb + j;
         const int f = (j < th && t < a.lanes) ? __ldcg(a.xf + t) : 0;
         y[j] = __fadd_rn(__fmul_rn(acc01[j], __int_as_float((127 - f) << 23)),
                          __fmul_rn(acc23[j], __int_as_float((143 - f) << 23)));
         acc01[j] = acc23[j] = 0.f;
       }
-      bool fin = true;
-      if (!a.whole) {
+      bool fin;
+      {  // an octet split across CTAs is finished by the last to arrive
         const int c_lo = cta_of(items, ncta, o_ * gpr);
         const int c_hi = cta_of(items, ncta, o_ * gpr + gpr - 1);
         fin = c_lo == c_hi;
@@ -513,7 +495,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
 #pragma unroll
       for (int j = 0; j < TH; j++) {
         const float up = __shfl_down_sync(0xffffffffu, y[j], 16);  // R = 2: the up row
-        const int t = t0 + tb + j;
+        const int t = tb + j;
         if (j >= th || t >= a.lanes || n >= a.N) continue;
         if (R == 2 && r == 1) continue;
         tc_store(a, t, n, y[j], up);
@@ -569,7 +551,6 @@ void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const B
   a.R = R;
   a.lanes = lanes;
   a.tpad = xp.tc_tpad;
-  a.whole = lanes > kTcMaxTok;
   a.xtc = static_cast<const unsigned char*>(xp.xtc);
   a.xf = xp.xf;
   a.be = be;
@@ -579,11 +560,9 @@ void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const B
   a.pdl = pdl;
   const int gpr = K / kGroup, tiles = (N + 15) / 16, octets = (tiles + 8 / R - 1) / (8 / R);
   const int items = octets * gpr;
-  // split mode: at most two CTAs per octet (a split octet costs a fence, an
-  // atomic and the partial-sum reads of its last CTA); whole mode: one
-  // (token tile, octet) pair per CTA at a time
-  const int ncta = a.whole ? std::min(sm_count(), octets * ((lanes + kTcMaxTok - 1) / kTcMaxTok))
-                           : std::min(std::min(sm_count(), 2 * octets), items);
+  // at most two CTAs per octet: a split octet costs a fence, an atomic and
+  // the partial-sum reads of its last CTA
+  const int ncta = std::min(std::min(sm_count(), 2 * octets), items);
   const size_t smem = (size_t)kTcRaw * kTcStageBytes + (size_t)kTcA * kTcABytes + (size_t)kTcB * kTcBBytes;
   void (*kern)(TcArgs) = a.tpad <= 16 ? gemv_q4_tc_kernel<8> : gemv_q4_tc_kernel<16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -598,6 +577,312 @@ void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const B
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
   cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// ======================================================================
+// Whole-prompt GEMM (prefill passes of more than 32 positions)
+// ======================================================================
+// Many token rows make the MMA's N large, and then the per-group fold of the
+// integer path (four digit-plane columns per token, each converted and
+// scaled) costs more issue slots than the MMAs.  So the whole-prompt GEMM
+// runs kind::f16 with f32 accumulation: A = the 128 x 128 nibble values q of
+// an (octet, group) as f16 (exact), expanded once at load into 32 KB images
+// in the MMA's shared-memory layout; B = each token's x' = x * 2^f as f16
+// hi + lo, STACKED ALONG K (k 0..127 hi, 128..255 lo) against the same A
+// twice, so the tensor core adds the two halves and each token needs ONE
+// f32 accumulator column.  The products q * hi, q * lo are exact in f32; the
+// sum is the f32 accumulation of the tensor core (the reference's GEMM4
+// sums f32 products too).  Per group: 16 MMAs of M = 128, N = 128 tokens,
+// K = 16; the epilogue folds acc += s * D per token and group, and
+// y = 2^-f acc.
+//
+// Warp roles (19 warps): 0-15 epilogue (warp w reads TMEM lanes 32 (w % 4)
+// .. and tokens 32 (w / 4) .. of the tile, and its row's group scales from
+// global memory one group ahead); 16 copies A images; 17 issues the MMAs and
+// owns TMEM; 18 copies B tiles.  Each CTA walks whole (octet, token tile)
+// pairs, octet-major, so CTAs running at once share an octet's images in L2.
+namespace {
+
+constexpr int kPgTok = 128;                  // tokens per B tile (MMA N)
+constexpr int kPgThreads = 19 * 32;
+constexpr int kPgEpiWarps = 16;
+constexpr int kPgAWarp = 16, kPgMmaWarp = 17, kPgBWarp = 18;
+constexpr int kPgA = 2, kPgB = 2;            // ring slots
+constexpr int kPgABytes = 128 * 128 * 2;     // 32 KB: 128 rows x 128 k, f16
+constexpr int kPgBBytes = kPgTok * 256 * 2;  // 64 KB: 128 tokens x (128 hi + 128 lo), f16
+constexpr uint32_t kPgTmemCols = 2 * kPgTok;  // two accumulators
+
+struct PgArgs {
+  const unsigned char* a16;  // [octet][group][32 KB] A images (q4_tc_to_a16)
+  const float* s16;          // [octet][group][128] group scale of each MMA row
+  int N, K, R, lanes;
+  const unsigned char* xh;   // [token tile][group][64 KB] B tiles
+  const int* xf;
+  BatchEpi be;
+  int* err;
+};
+
+struct PgSmem {
+  uint64_t a_full[kPgA], a_empty[kPgA], b_full[kPgB], b_empty[kPgB];
+  uint64_t acc_full[2], acc_empty[2];
+  uint32_t tmem_base;
+};
+
+// Instruction descriptor of tcgen05.mma kind::f16: D f32, A and B f16,
+// both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t taddr, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(taddr),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kPgThreads, 1) gemm_q4_prefill_kernel(PgArgs a) {
+  extern __shared__ __align__(1024) unsigned char pg_dsm[];
+  __shared__ PgSmem S;
+  unsigned char* abuf = pg_dsm;                            // kPgA x 32 KB
+  unsigned char* bbuf = abuf + (size_t)kPgA * kPgABytes;   // kPgB x 64 KB
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = a.R, TPO = 8 / R;
+  const int gpr = a.K / kGroup, tiles = (a.N + 15) / 16, octets = (tiles + TPO - 1) / TPO;
+  const int ntau = (a.lanes + kPgTok - 1) / kPgTok, npairs = octets * ntau;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPgA; i++) {
+      mbar_init(&S.a_full[i], 1);
+      mbar_init(&S.a_empty[i], 1);
+    }
+    for (int i = 0; i < kPgB; i++) {
+      mbar_init(&S.b_full[i], 1);
+      mbar_init(&S.b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&S.acc_full[i], 1);
+      mbar_init(&S.acc_empty[i], kPgEpiWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kPgMmaWarp) tmem_alloc(&S.tmem_base, kPgTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+  bool dead = false;
+
+  if (warp == kPgAWarp) {
+    // ---------------------------------------------------- A images
+    Ring ra{0, 0};
+    int n = 0;
+    for (int pr = blockIdx.x; pr < npairs; pr += gridDim.x) {
+      const int o = pr / ntau;
+      for (int g = 0; g < gpr; g++, n++) {
+        if (!dead && !tc_wait(&S.a_empty[ra.slot], ra.ph ^ 1, a.err)) dead = true;
+        if (lane == 0) {
+          mbar_expect_tx(&S.a_full[ra.slot], kPgABytes);
+          bulk_g2s(abuf + (size_t)ra.slot * kPgABytes, a.a16 + ((size_t)o * gpr + g) * kPgABytes, kPgABytes,
+                   &S.a_full[ra.slot]);
+        }
+        __syncwarp();
+        ra.adv(kPgA);
+      }
+    }
+    for (int j = 0; j < kPgA && j < n; j++) {  // copies in flight have landed
+      if (ra.slot == 0) {
+        ra.slot = kPgA - 1;
+        ra.ph ^= 1;
+      } else {
+        ra.slot--;
+      }
+      tc_wait_bounded(&S.a_full[ra.slot], ra.ph);
+    }
+  } else if (warp == kPgBWarp) {
+    // ---------------------------------------------------- B tiles
+    Ring rb{0, 0};
+    int n = 0;
+    for (int pr = blockIdx.x; pr < npairs; pr += gridDim.x) {
+      const int tau = pr % ntau;
+      for (int g = 0; g < gpr; g++, n++) {
+        if (!dead && !tc_wait(&S.b_empty[rb.slot], rb.ph ^ 1, a.err)) dead = true;
+        if (lane == 0) {
+          mbar_expect_tx(&S.b_full[rb.slot], kPgBBytes);
+          bulk_g2s(bbuf + (size_t)rb.slot * kPgBBytes, a.xh + ((size_t)tau * gpr + g) * kPgBBytes, kPgBBytes,
+                   &S.b_full[rb.slot]);
+        }
+        __syncwarp();
+        rb.adv(kPgB);
+      }
+    }
+    for (int j = 0; j < kPgB && j < n; j++) {
+      if (rb.slot == 0) {
+        rb.slot = kPgB - 1;
+        rb.ph ^= 1;
+      } else {
+        rb.slot--;
+      }
+      tc_wait_bounded(&S.b_full[rb.slot], rb.ph);
+    }
+  } else if (warp == kPgMmaWarp) {
+    // ---------------------------------------------------- MMA issue
+    const uint32_t idesc = idesc_f16(128, kPgTok);
+    Ring ra{0, 0}, rb{0, 0}, rt{0, 0};
+    int n = 0;
+    for (int pr = blockIdx.x; pr < npairs; pr += gridDim.x)
+      for (int g = 0; g < gpr; g++, n++) {
+        if (!dead && !tc_wait(&S.a_full[ra.slot], ra.ph, a.err)) dead = true;
+        if (!dead && !tc_wait(&S.b_full[rb.slot], rb.ph, a.err)) dead = true;
+        if (!dead && !tc_wait(&S.acc_empty[rt.slot], rt.ph ^ 1, a.err)) dead = true;
+        tc_fence_after();
+        if (lane == 0) {
+          const unsigned char* A = abuf + (size_t)ra.slot * kPgABytes;
+          const unsigned char* B = bbuf + (size_t)rb.slot * kPgBBytes;
+          const uint32_t d = tmem + (uint32_t)(rt.slot * kPgTok);
+          // 8 k-steps of 16 over the hi half of B, then the same A against the lo half
+#pragma unroll
+          for (int j = 0; j < 16; j++)
+            mma_f16(d, smem_desc(A + (j & 7) * 2 * 2048, 2048, 128), smem_desc(B + j * 2 * 2048, 2048, 128),
+                    idesc, j > 0);
+          mma_commit(&S.acc_full[rt.slot]);
+          mma_commit(&S.a_empty[ra.slot]);
+          mma_commit(&S.b_empty[rb.slot]);
+        }
+        __syncwarp();
+        ra.adv(kPgA);
+        rb.adv(kPgB);
+        rt.adv(2);
+      }
+    for (int j = 0; j < 2 && j < n; j++) {  // the MMAs have finished before TMEM is freed
+      if (rt.slot == 0) {
+        rt.slot = 1;
+        rt.ph ^= 1;
+      } else {
+        rt.slot--;
+      }
+      tc_wait_bounded(&S.acc_full[rt.slot], rt.ph);
+    }
+  } else if (warp < kPgEpiWarps) {
+    // ---------------------------------------------------- epilogue
+    const int sub = warp & 3, tb = 32 * (warp >> 2);  // TMEM lanes 32 sub.., tokens tb .. tb + 31
+    const int m = 32 * sub + lane;
+    const int ti = R == 1 ? m >> 4 : m >> 5, r = R == 1 ? 0 : (m >> 4) & 1, row = m & 15;
+    Ring rt{0, 0};
+    for (int pr = blockIdx.x; pr < npairs; pr += gridDim.x) {
+      const int o = pr / ntau, t0 = kPgTok * (pr % ntau) + tb;
+      const float* srow = a.s16 + (size_t)o * gpr * 128 + m;  // this row's scale of group g at g * 128
+      float acc[32];
+#pragma unroll
+      for (int j = 0; j < 32; j++) acc[j] = 0.f;
+      float s_next = __ldg(srow);
+      for (int g = 0; g < gpr; g++) {
+        const float s_m = s_next;
+        if (g + 1 < gpr) s_next = __ldg(srow + (size_t)(g + 1) * 128);  // one group ahead
+        const int qt = rt.slot;
+        if (!dead && !tc_wait(&S.acc_full[qt], rt.ph, a.err)) dead = true;
+        rt.adv(2);
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * sub) << 16) + (uint32_t)(qt * kPgTok + tb), v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.acc_empty[qt]);
+#pragma unroll
+        for (int j = 0; j < 32; j++) acc[j] = fmaf(s_m, __uint_as_float(v[j]), acc[j]);
+      }
+      const int n = 16 * (o * TPO + ti) + row;
+#pragma unroll
+      for (int j = 0; j < 32; j++) {
+        const int t = t0 + j;
+        const int f = t < a.lanes ? __ldcg(a.xf + t) : 0;
+        const float y = __fmul_rn(acc[j], __int_as_float((127 - f) << 23));  // 2^-f, exact
+        const float up = __shfl_down_sync(0xffffffffu, y, 16);  // R = 2: the up row
+        if (t >= a.lanes || n >= a.N || (R == 2 && r == 1)) continue;
+        tc_store(a, t, n, y, up);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kPgMmaWarp) tmem_free(tmem, kPgTmemCols);
+}
+
+// A images from the tc layout: block og = (octet, group) of 128 rows x 128 k
+// as f16 nibble values, element (m, k) at (k / 8) * 2 KB + (m / 8) * 128 +
+// (m % 8) * 16 + (k % 8) * 2 (K-major 8 x 16-byte core matrices), and the
+// group scale of each MMA row.  Word w of MMA row m's fragment-order block
+// holds k = 8w .. 8w + 7 (the mapping gemv_q4_tc's converter warps use).
+__global__ void q4_tc_to_a16_kernel(const unsigned char* __restrict__ wc, int R, unsigned char* __restrict__ a16,
+                                    float* __restrict__ s16) {
+  const int blk = q4_block_bytes(R), TPO = 8 / R;
+  const size_t og = blockIdx.x;
+  const unsigned char* st = wc + og * TPO * blk;
+  unsigned char* A = a16 + og * kPgABytes;
+  const int ct = threadIdx.x;
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int pc = ct + 256 * j;
+    const int pl = pc & 31, h = (pc >> 5) & 1, rest = pc >> 6;
+    const int ti = R == 1 ? rest : rest >> 1, r = R == 1 ? 0 : rest & 1;
+    const int m = R == 1 ? 16 * ti + 8 * h + (pl >> 2) : 32 * ti + 16 * r + 8 * h + (pl >> 2);
+    const int t = pl & 3;
+    const uint4 v = *reinterpret_cast<const uint4*>(st + ti * blk + r * 1024 + h * 512 + pl * 16);
+    const uint32_t words[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int w = 4 * i + t;  // word index: k = 8w .. 8w + 7
+      uint32_t hv[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int q0 = (int)(words[i] << (28 - 8 * e)) >> 28, q1 = (int)(words[i] << (24 - 8 * e)) >> 28;
+        const __half2 hh = __floats2half2_rn((float)q0, (float)q1);
+        hv[e] = *reinterpret_cast<const uint32_t*>(&hh);
+      }
+      *reinterpret_cast<uint4*>(A + w * 2048 + (m >> 3) * 128 + (m & 7) * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    }
+  }
+  if (ct < 128) {
+    const int sti = R == 1 ? ct >> 4 : ct >> 5, sr = R == 1 ? 0 : (ct >> 4) & 1, srow = ct & 15;
+    s16[og * 128 + ct] =
+        *reinterpret_cast<const float*>(st + sti * blk + R * 1024 + 4 * (sr * 16 + 2 * (srow & 7) + (srow >> 3)));
+  }
+}
+
+}  // namespace
+
+size_t q4_a16_bytes(int N, int K, int R) {
+  const int tiles = (N + 15) / 16, TPO = 8 / R, octets = (tiles + TPO - 1) / TPO;
+  return (size_t)octets * (K / kGroup) * kPgABytes;
+}
+size_t q4_a16_scale_bytes(int N, int K, int R) { return q4_a16_bytes(N, K, R) / kPgABytes * 128 * sizeof(float); }
+
+void q4_tc_to_a16(const unsigned char* wc, int N, int K, int R, unsigned char* a16, float* s16, cudaStream_t st) {
+  const unsigned blocks = (unsigned)(q4_a16_bytes(N, K, R) / kPgABytes);
+  q4_tc_to_a16_kernel<<<blocks, 256, 0, st>>>(wc, R, a16, s16);
+}
+
+void gemm_q4_prefill(const unsigned char* a16, const float* s16, int N, int K, int R, int lanes,
+                     const BatchPlanes& xp, const BatchEpi& be, int* err, cudaStream_t st) {
+  PgArgs a = {};
+  a.a16 = a16;
+  a.s16 = s16;
+  a.N = N;
+  a.K = K;
+  a.R = R;
+  a.lanes = lanes;
+  a.xh = static_cast<const unsigned char*>(xp.xh);
+  a.xf = xp.xf;
+  a.be = be;
+  a.err = err;
+  const int tiles = (N + 15) / 16, octets = (tiles + 8 / R - 1) / (8 / R);
+  const int npairs = octets * ((lanes + kPgTok - 1) / kPgTok);
+  const int smem = kPgA * kPgABytes + kPgB * kPgBBytes;
+  cudaFuncSetAttribute(gemm_q4_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  gemm_q4_prefill_kernel<<<std::min(sm_count(), npairs), kPgThreads, smem, st>>>(a);
 }
 
 }  // namespace eg
