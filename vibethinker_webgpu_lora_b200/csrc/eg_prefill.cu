@@ -95,6 +95,16 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// 16-byte global -> shared copy; src_bytes 0 fills zeros
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 // (x, y) = hi + lo, each an f16 pair (low half = x)
 __device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
@@ -118,9 +128,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(PrefillAttn
   constexpr int NQ = F32 ? 2 : 1, NK = F32 ? 2 : 1;  // f16 parts of q and of K / V
   constexpr int TILE = 128 * kPfPitch;                // halfs per shared tile
   extern __shared__ __align__(16) unsigned char pf_sm[];
+  // f32 cache: q hi/lo, K hi/lo, V hi/lo.  f16 cache: q, then two buffers of
+  // (K, V): block b + 1 is copied (cp.async) while block b computes.
   __half* Qs = reinterpret_cast<__half*>(pf_sm);  // [NQ][128 rows][pitch]
-  __half* Ks = Qs + NQ * TILE;                     // [NK][128 keys][pitch]
-  __half* Vs = Ks + NK * TILE;                     // [NK][128 keys][pitch]
+  __half* Ks = Qs + NQ * TILE;                     // [NK][128 keys][pitch] (buffer 0)
+  __half* Vs = Ks + NK * TILE;                     // [NK][128 keys][pitch] (buffer 0)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gsz = a.nh / a.nkv, qt = 16 * nsub;
   const int tile = gridDim.x - 1 - blockIdx.x;  // the longest rows start first
@@ -155,10 +167,36 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(PrefillAttn
   const uint32_t kb_addr = smem_addr(Ks + ((lane & 7) + ((lane >> 4) << 3)) * kPfPitch + ((lane >> 3) & 1) * 8);
   const uint32_t vb_addr = smem_addr(Vs + ((lane & 7) + (((lane >> 3) & 1) << 3)) * kPfPitch + (lane >> 4) * 8);
 
+  // f16 cache: K / V rows of block b into buffer buf (rows past kend zero)
+  auto issue_f16 = [&](int b, int buf) {
+    const __half* kc = static_cast<const __half*>(a.kc);
+    const __half* vc = static_cast<const __half*>(a.vc);
+    __half* kd = Ks + buf * 2 * TILE;
+    __half* vd = kd + TILE;
+    for (int i = threadIdx.x; i < 128 * 16; i += kPfThreads) {
+      const int r = i >> 4, c8 = i & 15, key = b * 128 + r;
+      const bool ok = key < kend;
+      const size_t off = ok ? (size_t)key * kvd + kvh * kHeadDim + 8 * c8 : 0;
+      cp_async16(kd + r * kPfPitch + 8 * c8, kc + off, ok ? 16 : 0);
+      cp_async16(vd + r * kPfPitch + 8 * c8, vc + off, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  if (!F32) issue_f16(0, 0);
+
   for (int b = 0; b < nblk; b++) {
     const int kb = b * 128;
-    __syncthreads();  // the previous block's tiles are consumed
-    if (F32) {
+    const uint32_t boff = F32 ? 0u : (uint32_t)((b & 1) * 2 * TILE * 2);  // this block's buffer, bytes
+    if (!F32) {
+      if (b + 1 < nblk) {
+        issue_f16(b + 1, (b + 1) & 1);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+    } else {
+      __syncthreads();  // the previous block's tiles are consumed
       const float* kc = static_cast<const float*>(a.kc);
       const float* vc = static_cast<const float*>(a.vc);
       for (int i = threadIdx.x; i < 128 * 32; i += kPfThreads) {
@@ -173,120 +211,109 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_kernel(PrefillAttn
         put4(kd, kd + TILE, k4);
         put4(vd, vd + TILE, v4);
       }
-    } else {
-      const __half* kc = static_cast<const __half*>(a.kc);
-      const __half* vc = static_cast<const __half*>(a.vc);
-      for (int i = threadIdx.x; i < 128 * 16; i += kPfThreads) {
-        const int r = i >> 4, c8 = i & 15, key = kb + r;
-        uint4 k8 = make_uint4(0, 0, 0, 0), v8 = k8;
-        if (key < kend) {
-          k8 = __ldg(reinterpret_cast<const uint4*>(kc + (size_t)key * kvd + kvh * kHeadDim) + c8);
-          v8 = __ldg(reinterpret_cast<const uint4*>(vc + (size_t)key * kvd + kvh * kHeadDim) + c8);
-        }
-        *reinterpret_cast<uint4*>(Ks + r * kPfPitch + 8 * c8) = k8;
-        *reinterpret_cast<uint4*>(Vs + r * kPfPitch + 8 * c8) = v8;
-      }
+      __syncthreads();
     }
-    __syncthreads();
-    if (!active) continue;
+    if (active) {
 
-    // ---- S = q K^T over the block's 128 keys (16 n-tiles of 8 keys)
-    float S[16][4];
+      // ---- S = q K^T over the block's 128 keys (16 n-tiles of 8 keys)
+      float S[16][4];
 #pragma unroll
-    for (int j = 0; j < 16; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
+      for (int j = 0; j < 16; j++) S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
 #pragma unroll
-    for (int ks = 0; ks < 8; ks++) {
-      uint32_t qh[4], ql[4];
-      ldsm_x4(qa_addr + ks * 32, qh[0], qh[1], qh[2], qh[3]);
-      if (NQ == 2) ldsm_x4(qa_addr + TILE * 2 + ks * 32, ql[0], ql[1], ql[2], ql[3]);
+      for (int ks = 0; ks < 8; ks++) {
+        uint32_t qh[4], ql[4];
+        ldsm_x4(qa_addr + ks * 32, qh[0], qh[1], qh[2], qh[3]);
+        if (NQ == 2) ldsm_x4(qa_addr + TILE * 2 + ks * 32, ql[0], ql[1], ql[2], ql[3]);
 #pragma unroll
-      for (int np = 0; np < 8; np++) {
-        const uint32_t ka = kb_addr + (np * 16 * kPfPitch + ks * 16) * 2;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(ka, b0, b1, b2, b3);
-        mma16816(S[2 * np], qh, b0, b1);
-        mma16816(S[2 * np + 1], qh, b2, b3);
-        if (F32) {
-          mma16816(S[2 * np], ql, b0, b1);
-          mma16816(S[2 * np + 1], ql, b2, b3);
-          ldsm_x4(ka + TILE * 2, b0, b1, b2, b3);
+        for (int np = 0; np < 8; np++) {
+          const uint32_t ka = kb_addr + boff + (np * 16 * kPfPitch + ks * 16) * 2;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(ka, b0, b1, b2, b3);
           mma16816(S[2 * np], qh, b0, b1);
           mma16816(S[2 * np + 1], qh, b2, b3);
+          if (F32) {
+            mma16816(S[2 * np], ql, b0, b1);
+            mma16816(S[2 * np + 1], ql, b2, b3);
+            ldsm_x4(ka + TILE * 2, b0, b1, b2, b3);
+            mma16816(S[2 * np], qh, b0, b1);
+            mma16816(S[2 * np + 1], qh, b2, b3);
+          }
         }
       }
-    }
-    // ---- scale, causal mask, block max of each of the thread's two rows
-    float bm0 = -1e30f, bm1 = -1e30f;
+      // ---- scale, causal mask, block max of each of the thread's two rows
+      float bm0 = -1e30f, bm1 = -1e30f;
 #pragma unroll
-    for (int j = 0; j < 16; j++)
+      for (int j = 0; j < 16; j++)
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const int key = kb + 8 * j + 2 * tq + (c & 1);
-        const bool ok = key < kend && key <= (c < 2 ? abs0 : abs1);
-        const float s = ok ? __fmul_rn(S[j][c], scl) : -1e30f;
-        S[j][c] = s;
-        if (c < 2) bm0 = fmaxf(bm0, s);
-        else bm1 = fmaxf(bm1, s);
+        for (int c = 0; c < 4; c++) {
+          const int key = kb + 8 * j + 2 * tq + (c & 1);
+          const bool ok = key < kend && key <= (c < 2 ? abs0 : abs1);
+          const float s = ok ? __fmul_rn(S[j][c], scl) : -1e30f;
+          S[j][c] = s;
+          if (c < 2) bm0 = fmaxf(bm0, s);
+          else bm1 = fmaxf(bm1, s);
+        }
+#pragma unroll
+      for (int o = 1; o <= 2; o <<= 1) {
+        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, o));
+        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, o));
       }
+      const float n0 = fmaxf(m0, bm0), n1 = fmaxf(m1, bm1);
+      const float corr0 = expf(m0 - n0), corr1 = expf(m1 - n1);
+      float bs0 = 0.f, bs1 = 0.f;
 #pragma unroll
-    for (int o = 1; o <= 2; o <<= 1) {
-      bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, o));
-      bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, o));
-    }
-    const float n0 = fmaxf(m0, bm0), n1 = fmaxf(m1, bm1);
-    const float corr0 = expf(m0 - n0), corr1 = expf(m1 - n1);
-    float bs0 = 0.f, bs1 = 0.f;
+      for (int j = 0; j < 16; j++)
 #pragma unroll
-    for (int j = 0; j < 16; j++)
+        for (int c = 0; c < 4; c++) {
+          const int key = kb + 8 * j + 2 * tq + (c & 1);
+          const bool ok = key < kend && key <= (c < 2 ? abs0 : abs1);
+          const float p = ok ? expf(S[j][c] - (c < 2 ? n0 : n1)) : 0.f;
+          S[j][c] = p;
+          if (c < 2) bs0 = __fadd_rn(bs0, p);
+          else bs1 = __fadd_rn(bs1, p);
+        }
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const int key = kb + 8 * j + 2 * tq + (c & 1);
-        const bool ok = key < kend && key <= (c < 2 ? abs0 : abs1);
-        const float p = ok ? expf(S[j][c] - (c < 2 ? n0 : n1)) : 0.f;
-        S[j][c] = p;
-        if (c < 2) bs0 = __fadd_rn(bs0, p);
-        else bs1 = __fadd_rn(bs1, p);
+      for (int o = 1; o <= 2; o <<= 1) {
+        bs0 = __fadd_rn(bs0, __shfl_xor_sync(0xffffffffu, bs0, o));
+        bs1 = __fadd_rn(bs1, __shfl_xor_sync(0xffffffffu, bs1, o));
       }
+      l0 = __fadd_rn(__fmul_rn(l0, corr0), bs0);
+      l1 = __fadd_rn(__fmul_rn(l1, corr1), bs1);
+      m0 = n0;
+      m1 = n1;
 #pragma unroll
-    for (int o = 1; o <= 2; o <<= 1) {
-      bs0 = __fadd_rn(bs0, __shfl_xor_sync(0xffffffffu, bs0, o));
-      bs1 = __fadd_rn(bs1, __shfl_xor_sync(0xffffffffu, bs1, o));
-    }
-    l0 = __fadd_rn(__fmul_rn(l0, corr0), bs0);
-    l1 = __fadd_rn(__fmul_rn(l1, corr1), bs1);
-    m0 = n0;
-    m1 = n1;
+      for (int j = 0; j < 16; j++) {
+        O[j][0] = __fmul_rn(O[j][0], corr0);
+        O[j][1] = __fmul_rn(O[j][1], corr0);
+        O[j][2] = __fmul_rn(O[j][2], corr1);
+        O[j][3] = __fmul_rn(O[j][3], corr1);
+      }
+      // ---- O += P V: P from the S accumulators (A fragments of 16 keys)
 #pragma unroll
-    for (int j = 0; j < 16; j++) {
-      O[j][0] = __fmul_rn(O[j][0], corr0);
-      O[j][1] = __fmul_rn(O[j][1], corr0);
-      O[j][2] = __fmul_rn(O[j][2], corr1);
-      O[j][3] = __fmul_rn(O[j][3], corr1);
-    }
-    // ---- O += P V: P from the S accumulators (A fragments of 16 keys)
+      for (int kk = 0; kk < 8; kk++) {
+        uint32_t ph[4], pl[4];
+        split2(S[2 * kk][0], S[2 * kk][1], ph[0], pl[0]);
+        split2(S[2 * kk][2], S[2 * kk][3], ph[1], pl[1]);
+        split2(S[2 * kk + 1][0], S[2 * kk + 1][1], ph[2], pl[2]);
+        split2(S[2 * kk + 1][2], S[2 * kk + 1][3], ph[3], pl[3]);
 #pragma unroll
-    for (int kk = 0; kk < 8; kk++) {
-      uint32_t ph[4], pl[4];
-      split2(S[2 * kk][0], S[2 * kk][1], ph[0], pl[0]);
-      split2(S[2 * kk][2], S[2 * kk][3], ph[1], pl[1]);
-      split2(S[2 * kk + 1][0], S[2 * kk + 1][1], ph[2], pl[2]);
-      split2(S[2 * kk + 1][2], S[2 * kk + 1][3], ph[3], pl[3]);
-#pragma unroll
-      for (int dn = 0; dn < 8; dn++) {
-        const uint32_t va = vb_addr + (kk * 16 * kPfPitch + dn * 16) * 2;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(va, b0, b1, b2, b3);
-        mma16816(O[2 * dn], ph, b0, b1);
-        mma16816(O[2 * dn + 1], ph, b2, b3);
-        mma16816(O[2 * dn], pl, b0, b1);
-        mma16816(O[2 * dn + 1], pl, b2, b3);
-        if (F32) {
-          ldsm_x4_t(va + TILE * 2, b0, b1, b2, b3);
+        for (int dn = 0; dn < 8; dn++) {
+          const uint32_t va = vb_addr + boff + (kk * 16 * kPfPitch + dn * 16) * 2;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(va, b0, b1, b2, b3);
           mma16816(O[2 * dn], ph, b0, b1);
           mma16816(O[2 * dn + 1], ph, b2, b3);
+          mma16816(O[2 * dn], pl, b0, b1);
+          mma16816(O[2 * dn + 1], pl, b2, b3);
+          if (F32) {
+            ldsm_x4_t(va + TILE * 2, b0, b1, b2, b3);
+            mma16816(O[2 * dn], ph, b0, b1);
+            mma16816(O[2 * dn + 1], ph, b2, b3);
+          }
         }
       }
-    }
+    }  // active
+    if (!F32) __syncthreads();  // this buffer is refilled with block b + 2 next
   }
   if (!active) return;
   const float inv0 = __fdiv_rn(1.f, l0), inv1 = __fdiv_rn(1.f, l1);
@@ -326,7 +353,7 @@ void attn_prefill(const PrefillAttn& a, cudaStream_t st) {
   const int qt = 16 * nsub, tiles = (a.T + qt - 1) / qt;
   const dim3 grid(tiles, a.nkv * hc);
   if (a.kv_f16) {
-    const int smem = 3 * kPfTileBytes;
+    const int smem = 5 * kPfTileBytes;
     cudaFuncSetAttribute(attn_prefill_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attn_prefill_kernel<__half><<<grid, kPfThreads, smem, st>>>(a, hw, nsub, hc);
   } else {
