@@ -502,27 +502,41 @@ __device__ __forceinline__ void attn_merge(const AttnArgs& a, int h0, int hq, in
 }
 
 // One item: KV head kvh, heads [h0, h0 + nhq), chunk `split` of nsplit.
-template <typename KVT>
+// NCH = 2 (a two-chunk context): one head (nhq = 1) over BOTH chunks in one
+// pass, the chunks taking the place of the head slots (slot c = chunk c, the
+// same q), then the two partials merged in registers with the arithmetic and
+// order of attn_merge (bit-identical to the cross-CTA merge, without its
+// global partials, fence, arrival counter and second pass).
+template <typename KVT, int NCH = 1>
 __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split, int nsplit,
                           int pos, bool append, int pdl, AttnSmem& sm) {
+  static_assert(NCH == 1 || NCH == 2, "one chunk, or two chunks of one head");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hd = kHeadDim, kvd = a.nkv * hd;
   const int f16 = a.kv_f16;
   const int ctx = pos + 1;
   const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
-  const int t0 = split * keys, t1 = min(t0 + keys, ctx);
+  const int nslot = NCH == 1 ? nhq : NCH;  // head slots in use
+  int t0[NCH], t1[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; c++) {
+    t0[c] = (split + c) * keys;
+    t1[c] = min(t0[c] + keys, ctx);
+  }
   const KVT* kc = reinterpret_cast<const KVT*>(a.kc) + kvh * hd + 4 * lane;
   const KVT* vc = reinterpret_cast<const KVT*>(a.vc) + kvh * hd + 4 * lane;
-  KvRow<KVT> K[kAttnKpw], V[kAttnKpw];
+  KvRow<KVT> K[NCH][kAttnKpw], V[NCH][kAttnKpw];
 #pragma unroll
-  for (int i = 0; i < kAttnKpw; i++) {
-    const int t = t0 + warp + kAttnWarps * i;
-    if (t < t1 && (t != pos || a.appended)) {
-      const size_t r = kv_row(a.pages, t);
-      K[i].load(kc + r * kvd);
-      V[i].load(vc + r * kvd);
+  for (int c = 0; c < NCH; c++)
+#pragma unroll
+    for (int i = 0; i < kAttnKpw; i++) {
+      const int t = t0[c] + warp + kAttnWarps * i;
+      if (t < t1[c] && (t != pos || a.appended)) {
+        const size_t r = kv_row(a.pages, t);
+        K[c][i].load(kc + r * kvd);
+        V[c][i].load(vc + r * kvd);
+      }
     }
-  }
   // the RoPE rows of pos (constant tables) also come before the wait
   const float* cs = a.cosT + (size_t)pos * hd;
   const float* sn = a.sinT + (size_t)pos * hd;
@@ -539,12 +553,20 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
   }
   // q of each head: ROPE_QK, read through f16 in the f16 variant (ATTN_PARTIAL_F16)
   float4 q4[kAttnHq];
+  if (NCH == 1) {
 #pragma unroll
-  for (int j = 0; j < kAttnHq; j++)
-    q4[j] = j < nhq ? rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + (h0 + j) * hd + 4 * lane)),
-                                 cj, sj, f16, f16 != 0)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
-  if (!a.appended && pos >= t0 && pos < t1) {  // the new row: k = RoPE(k), v, as cached
+    for (int j = 0; j < kAttnHq; j++)
+      q4[j] = j < nhq ? rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + (h0 + j) * hd + 4 * lane)),
+                                   cj, sj, f16, f16 != 0)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+  } else {
+    const float4 q = rope_lane4(__ldcg(reinterpret_cast<const float4*>(a.qkv + h0 * hd + 4 * lane)), cj, sj, f16,
+                                f16 != 0);
+#pragma unroll
+    for (int j = 0; j < kAttnHq; j++) q4[j] = j < NCH ? q : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const int cp = NCH == 1 ? 0 : (pos - t0[0]) / keys;  // the chunk holding pos
+  if (!a.appended && pos >= t0[0] && pos < t1[NCH - 1]) {  // the new row: k = RoPE(k), v, as cached
     const float* kn = a.qkv + a.nh * hd + kvh * hd;
     const float* vn = a.qkv + a.nh * hd + kvd + kvh * hd;
     const float4 kx = rope_lane4(__ldcg(reinterpret_cast<const float4*>(kn + 4 * lane)), cj, sj,
@@ -553,14 +575,16 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
     KvRow<KVT> kn4, vn4;
     kn4.set(make_float4(kv_round<KVT>(kx.x), kv_round<KVT>(kx.y), kv_round<KVT>(kx.z), kv_round<KVT>(kx.w)));
     vn4.set(make_float4(kv_round<KVT>(vr.x), kv_round<KVT>(vr.y), kv_round<KVT>(vr.z), kv_round<KVT>(vr.w)));
-    const int i = (pos - t0) / kAttnWarps, w = (pos - t0) % kAttnWarps;
+    const int i = (pos - t0[cp]) / kAttnWarps, w = (pos - t0[cp]) % kAttnWarps;
     if (warp == w) {
 #pragma unroll
-      for (int ii = 0; ii < kAttnKpw; ii++)
-        if (ii == i) {
-          K[ii] = kn4;
-          V[ii] = vn4;
-        }
+      for (int c = 0; c < NCH; c++)
+#pragma unroll
+        for (int ii = 0; ii < kAttnKpw; ii++)
+          if (c == cp && ii == i) {
+            K[c][ii] = kn4;
+            V[c][ii] = vn4;
+          }
     }
     if (append && warp == 0) {  // one item per KV group appends
       KVT* kw = reinterpret_cast<KVT*>(a.kc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane;
@@ -569,18 +593,21 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
       vw[0] = kv_cvt<KVT>(vr.x); vw[1] = kv_cvt<KVT>(vr.y); vw[2] = kv_cvt<KVT>(vr.z); vw[3] = kv_cvt<KVT>(vr.w);
     }
   }
-  // ---- scores: lane L holds the 4 dims 4L..4L+3 of q (4 heads) and of the
-  // warp's 8 keys; the 32 partial dots (key i, head j) at slot v = 4i + j are
+  // ---- scores: lane L holds the 4 dims 4L..4L+3 of q (4 slots) and of the
+  // warp's 8 keys; the 32 partial dots (key i, slot j) at v = 4i + j are
   // summed over the warp by a transposing butterfly (each round halves the
   // slots a lane keeps), after which lane L holds the whole dot of slot L.
   const float scale = 1.0f / sqrtf((float)hd);
-  const int nk = t1 - t0 > warp ? (t1 - t0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
+  int nkc[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; c++)
+    nkc[c] = t1[c] - t0[c] > warp ? (t1[c] - t0[c] - warp + kAttnWarps - 1) / kAttnWarps : 0;
   float pd[kAttnKpw * kAttnHq];
 #pragma unroll
   for (int i = 0; i < kAttnKpw; i++) {
-    const float4 k4 = K[i].get();
 #pragma unroll
     for (int j = 0; j < kAttnHq; j++) {
+      const float4 k4 = K[NCH == 1 ? 0 : (j < NCH ? j : 0)][i].get();
       float p = __fmul_rn(q4[j].x, k4.x);
       p = fmaf(q4[j].y, k4.y, p);
       p = fmaf(q4[j].z, k4.z, p);
@@ -597,16 +624,17 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
       pd[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
     }
   }
-  const int ki = lane >> 2, hj = lane & 3;  // this lane's (key, head) slot
-  const bool valid = ki < nk && hj < nhq;
+  const int ki = lane >> 2, hj = lane & 3;  // this lane's (key, slot)
+  const int nk_hj = NCH == 1 ? nkc[0] : (hj == 1 ? nkc[NCH - 1] : nkc[0]);
+  const bool valid = ki < nk_hj && hj < nslot;
   const float sv = valid ? __fmul_rn(pd[0], scale) : -1e30f;
-  float m = sv;  // the warp's max per head: lanes with the same hj
+  float m = sv;  // the warp's max per slot: lanes with the same hj
   m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
   m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
   m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
   if (lane < kAttnHq) sm.wm[warp][lane] = m;
   bar_sync_n<kAttnWarps * 32>();
-  // ---- the chunk's max per head, then ev = exp(s - M), Z and sum ev * v
+  // ---- the chunk's max per slot, then ev = exp(s - M), Z and sum ev * v
   float M = -1e30f;
 #pragma unroll
   for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, sm.wm[w][hj]);
@@ -620,11 +648,14 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
   for (int jj = 0; jj < kAttnHq; jj++) acc[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < kAttnKpw; i++) {
-    if (i >= nk) break;
-    const float4 v4 = V[i].get();
+    if (NCH == 1 && i >= nkc[0]) break;
+    const float4 v40 = V[0][i].get();
 #pragma unroll
     for (int jj = 0; jj < kAttnHq; jj++) {
-      if (jj >= nhq) break;
+      if (jj >= nslot) break;
+      const int cc = NCH == 1 ? 0 : (jj < NCH ? jj : 0);
+      if (NCH == 2 && i >= nkc[cc]) continue;
+      const float4 v4 = NCH == 1 ? v40 : V[cc][i].get();
       const float e = __shfl_sync(0xffffffffu, ev, 4 * i + jj);
       acc[jj].x = fmaf(e, v4.x, acc[jj].x);
       acc[jj].y = fmaf(e, v4.y, acc[jj].y);
@@ -634,12 +665,12 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
   }
 #pragma unroll
   for (int jj = 0; jj < kAttnHq; jj++)
-    if (jj < nhq) *reinterpret_cast<float4*>(&sm.wo[warp][jj][4 * lane]) = acc[jj];
+    if (jj < nslot) *reinterpret_cast<float4*>(&sm.wo[warp][jj][4 * lane]) = acc[jj];
   bar_sync_n<kAttnWarps * 32>();
-  // ---- one thread per (head j, dim d): the chunk's partial (pm, pz, po)
+  // ---- one thread per (slot j, dim d): the chunk's partial (pm, pz, po)
   const int j = threadIdx.x / kHeadDim, d = threadIdx.x % kHeadDim;
   float Mc = -1e30f, Z = 0.f, po = 0.f;
-  if (j < nhq) {
+  if (j < nslot) {
 #pragma unroll
     for (int w = 0; w < kAttnWarps; w++) {
       Mc = fmaxf(Mc, sm.wm[w][j]);
@@ -647,6 +678,28 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
       po = __fadd_rn(po, sm.wo[w][j][d]);
     }
     if (f16) po = round_h(po);  // ATTN_COMBINE_F16 reads po through f16
+  }
+  if (NCH == 2) {
+    // ---- ATTN_COMBINE over the two chunks, as attn_merge computes it
+    bar_sync_n<kAttnWarps * 32>();  // wo / mz are rewritten below
+    if (j < NCH) {
+      sm.wo[0][j][d] = po;
+      if (d == 0) {
+        sm.mz[j][0] = Mc;
+        sm.mz[j][1] = Z;
+      }
+    }
+    bar_sync_n<kAttnWarps * 32>();
+    if (j == 0) {
+      const float m0 = sm.mz[0][0], m1 = sm.mz[1][0];
+      const float Mg = fmaxf(fmaxf(-1e30f, m0), m1);
+      const float e0 = expf(m0 - Mg), e1 = expf(m1 - Mg);
+      const float Zg = __fadd_rn(__fadd_rn(0.f, __fmul_rn(sm.mz[0][1], e0)), __fmul_rn(sm.mz[1][1], e1));
+      const float v = __fadd_rn(__fadd_rn(0.f, __fmul_rn(e0, sm.wo[0][0][d])), __fmul_rn(e1, sm.wo[0][1][d]));
+      a.out[h0 * hd + d] = __fmul_rn(v, 1.0f / Zg);
+    }
+    bar_sync_n<kAttnWarps * 32>();  // the shared area is reused by the next item
+    return;
   }
   const int h = h0 + j;
   if (nsplit == 1) {
@@ -686,10 +739,23 @@ __device__ void attn_run(const AttnArgs& a, int cta, int ncta, int pdl, AttnSmem
   const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
   const int nsplit = (pos + keys) / keys;
   const int G = a.nh / a.nkv;
+  bool waited = !pdl;
+  // f16 cache: one item per query head over both chunks, merged in place
+  // (the f32 cache's rows are twice as wide and would spill)
+  if (sizeof(KVT) == 2 && nsplit == 2) {
+    for (int h = cta; h < a.nh; h += ncta) {
+      attn_item<KVT, 2>(a, h / G, h, 1, 0, 2, pos, h % G == 0, waited ? 0 : 1, sm);
+      waited = true;
+    }
+    if (!waited) {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    return;
+  }
   const int hq = attn_hq(a.nh, a.nkv, nsplit, ncta);
   const int subs = (G + hq - 1) / hq;
   const int items = a.nkv * subs * nsplit;
-  bool waited = !pdl;
   for (int it = cta; it < items; it += ncta) {
     const int split = it / (a.nkv * subs), r = it % (a.nkv * subs);
     const int kvh = r / subs, sub = r % subs;
