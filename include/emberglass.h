@@ -99,6 +99,10 @@ typedef struct {
                               prefill_tc only: 0 (default) = the whole prompt
                               in one pass (_prefillFull); n > 0 = passes of n
                               positions (_prefillChunked) */
+  int use_l2_prefetch;     /* 1 (default): in the per-op decode step every int4
+                              GEMV also prefetches a later matrix of the step
+                              into L2 (cp.async.bulk.prefetch), so HBM streams
+                              ahead of the kernel chain; 0: off */
 } eg_options;
 
 EG_API const char* eg_last_error(void);

@@ -121,7 +121,7 @@ def test_default_options_match_the_header_and_python_struct():
     assert got["max_ctx"] == 8192 and got["kv_f16"] == 1 and got["use_graphs"] == 1
     assert got["use_pdl"] == 1 and got["use_fused"] == 0 and got["prefill_chunk"] == 16
     assert got["use_tc_batch"] == 0
-    assert got["prefill_tc"] == 1 and got["prefill_chunk_size"] == 0
+    assert got["prefill_tc"] == 1 and got["prefill_chunk_size"] == 0 and got["use_l2_prefetch"] == 1
     hdr = open(HEADER).read()
     fields = hdr[:hdr.index("} eg_options;")].rsplit("typedef struct {", 1)[1]
     names = re.findall(r"\bint\s+(\w+);", fields)

@@ -37,6 +37,7 @@ class EgOptions(C.Structure):
         ("max_sampling_top_k", C.c_int), ("attn_chunk", C.c_int), ("use_graphs", C.c_int),
         ("use_pdl", C.c_int), ("use_fused", C.c_int), ("prefill_chunk", C.c_int),
         ("use_tc_batch", C.c_int), ("prefill_tc", C.c_int), ("prefill_chunk_size", C.c_int),
+        ("use_l2_prefetch", C.c_int),
     ]
 
 

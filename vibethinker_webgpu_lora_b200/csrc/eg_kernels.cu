@@ -69,6 +69,8 @@ static void launch(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, 
 // microseconds).  Shared memory: barriers | activation digit planes | ring.
 struct G4Args {
   const unsigned char* ws;  // stream layout
+  const unsigned char* pf;  // optional L2 prefetch (GemvWork)
+  size_t pf_bytes;
   int N, K;
   XSrc x;
   Epi e;
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(kOpThreads, 1) gemv_q4_kernel(G4Args p) {
     int issued = 0;
     ring_produce(ring, full, empty, p.stages, p.stage_bytes,
                  p.ws + (size_t)t_lo * gpr * q4_block_bytes(R), (t_hi - t_lo) * gpr, p.cap,
-                 q4_block_bytes(R), rp, issued, p.err, lane);
+                 q4_block_bytes(R), rp, issued, p.err, lane, p.pf, p.pf_bytes);
     ring_drain(full, p.stages, rp, issued);
     return;
   }
@@ -210,6 +212,8 @@ void gemv_q4(const unsigned char* ws, int N, int K, const XSrc& x, const Epi& e,
   a.x = x;
   a.e = e;
   a.err = wk.err;
+  a.pf = wk.pf;
+  a.pf_bytes = wk.pf_bytes;
   if (e.mode == EPI_SILU)
     gemv_q4_r<2>(a, st, pdl);
   else

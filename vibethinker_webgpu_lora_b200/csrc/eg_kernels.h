@@ -76,6 +76,12 @@ int sm_count();
 // Error word of the streaming int4 GEMV, set when a bounded wait gives up.
 struct GemvWork {
   int* err;
+  // Optional L2 prefetch of a later kernel's weights (the next matrix of the
+  // step): each CTA's producer prefetches its 1/grid slice of
+  // [pf, pf + pf_bytes) once its own first ring stages are issued, so the
+  // HBM stream runs ahead of the dependency chain.  16-byte aligned.
+  const unsigned char* pf = nullptr;
+  size_t pf_bytes = 0;
 };
 int gemv_q4_ctas();
 

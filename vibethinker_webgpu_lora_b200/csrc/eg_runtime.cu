@@ -423,8 +423,19 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
   int launches = 0;
   const LoraMod* lt = rt->lora_table;
   const GemvWork wk{reinterpret_cast<int*>(rt->fused_sync + 1)};
+  // each GEMV prefetches a later matrix of the step into L2: QKV the layer's
+  // gate_up, O its down, gate_up the next QKV, down the next O
+  auto pf = [&](const unsigned char* p, size_t bytes) {
+    GemvWork w = wk;
+    if (rt->o.use_l2_prefetch) {
+      w.pf = p;
+      w.pf_bytes = bytes;
+    }
+    return w;
+  };
   for (int i = 0; i < c.num_layers; i++) {
     const Layer& l = rt->L[i];
+    const Layer* nl = i + 1 < c.num_layers ? &rt->L[i + 1] : nullptr;
     XSrc xa = {};
     xa.mode = i == 0 ? X_EMBED_RMS : X_RMS;
     xa.x = rt->hidden;
@@ -451,7 +462,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     e.lora_d = rt->lora_d;
     e.split1 = QD;
     e.split2 = QD + KVD;
-    gemv_q4(l.qkv_t, NQKV, H, xa, e, st, pdl, wk);
+    gemv_q4(l.qkv_t, NQKV, H, xa, e, st, pdl, pf(l.gu_t, q4_stream_bytes(I, H, 2)));
     launches++;
     mark(rt, so, 0, cats);
 
@@ -491,7 +502,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     eo.mods = so.lora ? lt + i * 7 + 3 : nullptr;
     eo.lora_d = rt->lora_d;
     eo.split1 = eo.split2 = H;
-    gemv_q4(l.o_t, H, QD, xo, eo, st, pdl, wk);
+    gemv_q4(l.o_t, H, QD, xo, eo, st, pdl, pf(l.d_t, q4_stream_bytes(H, I, 1)));
     launches++;
     mark(rt, so, 2, cats);
 
@@ -511,7 +522,8 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     eg.N = I;
     eg.mods = so.lora ? lt + i * 7 + 4 : nullptr;
     eg.lora_d = rt->lora_d;
-    gemv_q4(l.gu_t, I, H, xb, eg, st, pdl, wk);
+    gemv_q4(l.gu_t, I, H, xb, eg, st, pdl,
+            nl ? pf(nl->qkv_t, q4_stream_bytes(NQKV, H, 1)) : wk);
     launches++;
     mark(rt, so, 3, cats);
 
@@ -529,7 +541,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     ed.mods = so.lora ? lt + i * 7 + 6 : nullptr;
     ed.lora_d = rt->lora_d;
     ed.split1 = ed.split2 = H;
-    gemv_q4(l.d_t, H, I, xd, ed, st, pdl, wk);
+    gemv_q4(l.d_t, H, I, xd, ed, st, pdl, nl ? pf(nl->o_t, q4_stream_bytes(H, QD, 1)) : wk);
     launches++;
     mark(rt, so, 4, cats);
   }
@@ -760,7 +772,7 @@ EG_API void eg_default_config(eg_config* c) {
 }
 EG_API void eg_default_options(eg_options* o) {
   if (!o) return;
-  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0, 16, 0, 1, 0};
+  *o = eg_options{0, 8192, 0, 1, 32, 40, 64, 0, 1, 1, 0, 16, 0, 1, 0, 1};
 }
 
 EG_API eg_status eg_create(const eg_config* cfg, const eg_options* opt, eg_rt** out) {

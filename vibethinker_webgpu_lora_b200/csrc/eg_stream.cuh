@@ -39,14 +39,32 @@ __device__ __forceinline__ void ring_advance(RingPos& rp, int stages) {
   }
 }
 
+// This CTA's slice of an L2 prefetch of [pf, pf + bytes) (16-byte aligned
+// pieces of at most 64 KB), issued by one thread.
+__device__ __forceinline__ void l2_prefetch_slice(const unsigned char* pf, size_t bytes) {
+  if (!pf || !bytes) return;
+  const size_t P = gridDim.x, c = blockIdx.x;
+  const size_t lo = (bytes * c / P) & ~(size_t)15;
+  const size_t hi = c + 1 == P ? bytes & ~(size_t)15 : (bytes * (c + 1) / P) & ~(size_t)15;
+  for (size_t o = lo; o < hi; o += 65536) {
+    const uint32_t n = (uint32_t)min((size_t)65536, hi - o);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf + o), "r"(n) : "memory");
+  }
+}
+
 // Producer (one warp): one run of nitems blocks of blk bytes from src0.
+// pf / pf_bytes (optional): a later kernel's weights to prefetch into L2,
+// this CTA's slice issued right after the ring's first fill.
 // Returns false when a wait gave up (error recorded).
 __device__ __forceinline__ bool ring_produce(unsigned char* ring, uint64_t* full, uint64_t* empty,
                                              int stages, int stage_bytes,
                                              const unsigned char* src0, int nitems, int cap,
                                              int blk, RingPos& rp, int& issued, int* err,
-                                             int lane) {
+                                             int lane, const unsigned char* pf = nullptr,
+                                             size_t pf_bytes = 0) {
   const int nchunks = (nitems + cap - 1) / cap;
+  const int fill = min(stages, nchunks);
+  if (nchunks == 0 && lane == 0) l2_prefetch_slice(pf, pf_bytes);
   for (int n = 0; n < nchunks; n++) {
     if (!mbar_wait(&empty[rp.st], rp.ph ^ 1, err)) return false;
     if (lane == 0) {
@@ -54,6 +72,7 @@ __device__ __forceinline__ bool ring_produce(unsigned char* ring, uint64_t* full
       mbar_expect_tx(&full[rp.st], bytes);
       bulk_g2s(ring + (size_t)rp.st * stage_bytes, src0 + (size_t)n * cap * blk, bytes,
                &full[rp.st]);
+      if (n == fill - 1) l2_prefetch_slice(pf, pf_bytes);
     }
     __syncwarp();
     issued++;

@@ -54,6 +54,7 @@ class QwenB200:
         o.use_tc_batch = int(bool(opts.get("useTcBatch", False)))
         o.prefill_tc = int(bool(opts.get("prefillTc", True)))
         o.prefill_chunk_size = int(opts.get("prefillChunkSize", 0))
+        o.use_l2_prefetch = int(bool(opts.get("useL2Prefetch", True)))
         self.opts = o
         h = C.c_void_p()
         L.check(L.lib().eg_create(C.byref(_cfg_struct(self.cfg)), C.byref(o), C.byref(h)))
