@@ -440,7 +440,7 @@ def run_batch16(args, ws, rank, local):
     total, n_prompt, steps, k, temp = 16, 512, 64, 40, 0.7
     mine = shard_sequences(total, rank, ws)
     n = len(mine)
-    rt = E.QwenB200(cfg, {"maxCtx": n_prompt + steps + 8, "useF16": True,
+    rt = E.QwenB200(cfg, {"maxCtx": n_prompt + steps + 8, "useF16": True, "useTcBatch": args.tc_batch,
                           "device": local}).build("synthetic", seed=SEED)
     a1 = E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16)
     a2 = E.synthetic_adapter(rt, 0xA2, rank=8, alpha=16)
@@ -706,13 +706,16 @@ def ncu_probe_attn(T):
     print(json.dumps({"ncu_probe_attn": T}))
 
 
-def ncu_probe_batch(steps):
-    """Profiling target of the batched path: 16 slots with 8-token prompts,
-    `steps` batched greedy steps (launches_per_step launches each), exit."""
+def ncu_probe_batch(steps, tc=False):
+    """Profiling target of the batched path as configs[4] runs it: a rank-8
+    adapter on every projection, 16 slots with 8-token prompts, `steps`
+    batched greedy steps (launches_per_step launches each), exit.  tc: the
+    int4 GEMVs on the tcgen05 path."""
     import vibethinker_webgpu_lora_b200 as E
     from vibethinker_webgpu_lora_b200.quantize import synth_ids
     cfg = E.QWEN25_3B
-    rt = E.QwenB200(cfg, {"maxCtx": 128}).build("synthetic", seed=SEED)
+    rt = E.QwenB200(cfg, {"maxCtx": 128, "useTcBatch": tc}).build("synthetic", seed=SEED)
+    rt.setLora(E.synthetic_adapter(rt, 0xA1, rank=8, alpha=16))
     rt.seqInit(16, 64)
     for sl in range(16):
         rt.seqSetPrompt(sl, synth_ids(8, 0xE6B00100 + sl, cfg["vocabSize"]))
@@ -736,13 +739,15 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "batch16", "prefill", "gemm4", "attn"],
                     help="decode: configs[1]/[2] (the headline); batch16: configs[4]; "
                          "prefill: configs[3]")
+    ap.add_argument("--tc-batch", action="store_true",
+                    help="batch16: the batched int4 GEMVs on the tcgen05 path (useTcBatch)")
     ap.add_argument("--ncu-probe", type=int, default=0, metavar="CTX",
                     help="profiling target: build, prefill CTX tokens, decode 2 tokens, exit "
                          "(CTX * launches/step launches precede the 2 profiled steps)")
     args = ap.parse_args()
     if args.ncu_probe:
         if args.workload == "batch16":
-            ncu_probe_batch(args.ncu_probe)
+            ncu_probe_batch(args.ncu_probe, args.tc_batch)
         elif args.workload == "prefill":
             ncu_probe_prefill(args.ncu_probe)
         elif args.workload == "gemm4":

@@ -66,37 +66,50 @@ __device__ __forceinline__ XSrc lane_src(const BatchSrc& b, int v) {
 }
 
 // ----------------------------------------------------------- staging
+// LoRA A rows folded into the staging (lane v's d at d + v * dstride).
+struct LoraFold {
+  const LoraMod* mods;
+  int nmods;
+  float* d;
+  int dstride;
+};
+
 template <int MAXU, bool NORM>
 __global__ void __launch_bounds__(kStageThreads) batch_stage_q4_kernel(BatchSrc b, int K,
-                                                                        BatchPlanes xp, int pdl) {
+                                                                        BatchPlanes xp, LoraFold lf, int pdl) {
   __shared__ float sred[32];
+  __shared__ float lsm[kStageLoraRows * (kStageThreads / 32 + 1)];
   const int v = blockIdx.y;
   // the lane's slot (X_EMBED_RMS) was set before the step began
   const XSrc s = lane_src(b, v);
   uint2* xb = reinterpret_cast<uint2*>(xp.xb) + (size_t)v * xp.gpr_max * 64;
+  StageLora sl = {lf.mods, lf.nmods, lf.d + (size_t)v * lf.dstride, lsm};
   stage_xd<MAXU, NORM, kStageThreads>(s, K, xb, xp.xcor + (size_t)v * 2 * xp.gpr_max, xp.xf + v,
                                       sred, pdl, static_cast<unsigned char*>(xp.xtc), 4 * xp.tc_tpad, 4 * v,
                                       xp.xh ? static_cast<unsigned char*>(xp.xh) + (size_t)(v / 128) * (K / kGroup) * 65536
                                             : nullptr,
-                                      v % 128);
+                                      v % 128, lf.mods ? &sl : nullptr);
   if (pdl) pdl_launch_dependents();
 }
 
-void batch_stage_q4(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, cudaStream_t st,
-                    bool pdl) {
+bool batch_stage_q4(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, cudaStream_t st, bool pdl,
+                    const LoraMod* mods, int nmods, int max_rank, float* d, int dstride) {
   const int u = (K / 8 + kStageThreads - 1) / kStageThreads;
   const dim3 grid(1, lanes);
   const bool norm = s.x.mode != X_PLAIN;
+  const bool fold = mods && nmods * max_rank <= kStageLoraRows;
+  const LoraFold lf = {fold ? mods : nullptr, nmods, d, dstride};
   if (u <= 1) {
-    if (norm) blaunch(batch_stage_q4_kernel<1, true>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, (int)pdl);
-    else blaunch(batch_stage_q4_kernel<1, false>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, (int)pdl);
+    if (norm) blaunch(batch_stage_q4_kernel<1, true>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, lf, (int)pdl);
+    else blaunch(batch_stage_q4_kernel<1, false>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, lf, (int)pdl);
   } else if (u <= 3) {
-    if (norm) blaunch(batch_stage_q4_kernel<3, true>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, (int)pdl);
-    else blaunch(batch_stage_q4_kernel<3, false>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, (int)pdl);
+    if (norm) blaunch(batch_stage_q4_kernel<3, true>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, lf, (int)pdl);
+    else blaunch(batch_stage_q4_kernel<3, false>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, lf, (int)pdl);
   } else {
-    if (norm) blaunch(batch_stage_q4_kernel<6, true>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, (int)pdl);
-    else blaunch(batch_stage_q4_kernel<6, false>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, (int)pdl);
+    if (norm) blaunch(batch_stage_q4_kernel<6, true>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, lf, (int)pdl);
+    else blaunch(batch_stage_q4_kernel<6, false>, grid, dim3(kStageThreads), 0, st, pdl, s, K, xp, lf, (int)pdl);
   }
+  return fold;
 }
 
 template <int MAXU, bool NORM>

@@ -82,37 +82,44 @@ struct BatchEpi {
 };
 
 // Batched int4 GEMV on the tcgen05 tensor cores (eg_tc.cu): the epilogue
-// of gemv_q4_batch (xp.xtc staged by batch_stage_q4), R = 2 for
-// GATE_UP_SILU; ws in the tc layout (q4_stream_to_tc).  lanes <= 32: the
-// CTAs split the K groups of every octet (split-K); part / counters are the
-// split-octet scratch (gemv_q4_tc_part_bytes, counters zero between
-// launches).  lanes > 32 (whole-prompt mode, tc_tpad = 32): every CTA
-// walks whole (token tile, octet) pairs, no split, part / counters unused.
-void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const BatchPlanes& xp,
-                const BatchEpi& be, float* part, unsigned* counters, int* err, cudaStream_t st,
-                bool pdl);
+// of gemv_q4_batch for up to 32 lanes (xp.xtc staged by batch_stage_q4),
+// R = 2 for GATE_UP_SILU.  The weights come as int8 A images expanded once
+// at load (q4_tc_to_a8: per (octet, group) the 128 x 128 operand bytes in the
+// MMA's shared-memory layout, plus each MMA row's group scale); the CTAs split
+// the (octet, group) items (split-K); part / counters are the split-octet
+// scratch (gemv_q4_tc_part_bytes, counters zero between launches).
+void gemv_q4_tc(const unsigned char* a8, const float* sc, int N, int K, int R, int lanes, const BatchPlanes& xp,
+                const BatchEpi& be, float* part, unsigned* counters, int* err, cudaStream_t st, bool pdl);
 size_t gemv_q4_tc_part_bytes();
-// The weight layout gemv_q4_tc streams (from the stream layout): octet-major,
-// so that every pipeline stage is one contiguous copy.
+int gemv_q4_tc_max_octets();
+// The octet-major regrouping of the stream layout (q4_stream_to_tc), the
+// source of the A images.
 size_t q4_tc_bytes(int N, int K, int R);
 void q4_stream_to_tc(const unsigned char* ws, int N, int K, int R, unsigned char* out, cudaStream_t st);
-int gemv_q4_tc_max_octets();
+size_t q4_a8_bytes(int N, int K, int R);
+size_t q4_row_scale_bytes(int N, int K, int R);
+void q4_tc_to_a8(const unsigned char* wc, int N, int K, int R, unsigned char* a8, float* sc, cudaStream_t st);
 
 // Whole-prompt GEMM on the tcgen05 tensor cores (eg_tc.cu), for more than 32
 // token rows, kind::f16: A images expanded once from the tc layout
-// (q4_tc_to_a16: per (octet, group) the 128 x 128 nibble values as f16, and
-// the 128 group scales), B = the rows' f16 hi/lo operand (xp.xh, staged by
-// batch_stage_q4), gemv_q4_tc's epilogue.
+// (q4_tc_to_a16: per (octet, group) the 128 x 128 nibble values as f16), the
+// row scales of q4_tc_to_a8, B = the rows' f16 hi/lo operand (xp.xh, staged
+// by batch_stage_q4), gemv_q4_tc's epilogue.
 size_t q4_a16_bytes(int N, int K, int R);
-size_t q4_a16_scale_bytes(int N, int K, int R);
-void q4_tc_to_a16(const unsigned char* wc, int N, int K, int R, unsigned char* a16, float* s16, cudaStream_t st);
-void gemm_q4_prefill(const unsigned char* a16, const float* s16, int N, int K, int R, int lanes,
+void q4_tc_to_a16(const unsigned char* wc, int N, int K, int R, unsigned char* a16, cudaStream_t st);
+void gemm_q4_prefill(const unsigned char* a16, const float* sc, int N, int K, int R, int lanes,
                      const BatchPlanes& xp, const BatchEpi& be, int* err, cudaStream_t st);
 
 // pdl: launched as programmatic dependents of the previous kernel (each
 // kernel waits with griddepcontrol.wait before reading earlier outputs).
-void batch_stage_q4(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, cudaStream_t st,
-                    bool pdl);
+// mods / nmods / max_rank / d / dstride (optional): the LoRA A rows of the
+// nmods modules at mods over each lane's staged vector, d + v * dstride as
+// lora_a_batch writes them, folded into the staging when nmods * max_rank
+// <= kStageLoraRows (returns true); otherwise nothing is computed (false)
+// and the caller runs lora_a_batch.
+bool batch_stage_q4(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, cudaStream_t st, bool pdl,
+                    const LoraMod* mods = nullptr, int nmods = 0, int max_rank = 0, float* d = nullptr,
+                    int dstride = 0);
 void batch_stage_q8(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, cudaStream_t st,
                     bool pdl);
 void gemv_q4_batch(const unsigned char* ws, int N, int K, int lanes, const BatchPlanes& xp,

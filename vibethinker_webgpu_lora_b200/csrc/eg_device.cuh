@@ -207,10 +207,23 @@ __device__ __forceinline__ void setup_x(const XSrc& s, int K, XCtx& c, float* sr
 // split into f16 hi = f16(x') and lo = f16(x' - hi), stacked along k (hi
 // elements 0..127, lo 128..255), K-major 8 x 16-byte core matrices, the 32
 // eight-element k-chunks 2 KB apart; *xf = f.
+// Staged LoRA A side (optional): d[m * kMaxRank + r] = sum_k x[k] A_m[r][k]
+// (LORA_A over the normalised input, kernels.js:60-97) for the nlm modules
+// at mods, at most kStageLoraRows rows in all; lsm: kStageLoraRows x NT/32
+// floats + kStageLoraRows ints of shared memory.
+constexpr int kStageLoraRows = 96;
+struct StageLora {
+  const LoraMod* mods;
+  int nmods;
+  float* d;
+  float* lsm;
+};
+
 template <int MAXU, bool NORM, int NT = kCtaThreads>
 __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, int* xf, float* sred,
                          int pdl, unsigned char* xtc = nullptr, int tc_ncol = 0,
-                         int tc_col0 = 0, unsigned char* xh = nullptr, int xh_col = 0) {
+                         int tc_col0 = 0, unsigned char* xh = nullptr, int xh_col = 0,
+                         const StageLora* lora = nullptr) {
   const int K8 = K / 8;
   float v[MAXU][8];
   float gw[NORM ? MAXU : 1][8];
@@ -287,6 +300,59 @@ __device__ void stage_xd(const XSrc& s, int K, uint2* xb, int* xcor, int* xf, fl
           v[i][j + 1] = r.y;
         }
       }
+  }
+  if (lora) {  // the adapter's A rows against the vector this block holds
+    constexpr int NW = NT / 32;
+    float* part = lora->lsm;
+    int* slot = reinterpret_cast<int*>(part + kStageLoraRows * NW);
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    int row = 0;
+    for (int m = 0; m < lora->nmods; m++) {
+      const LoraMod md = lora->mods[m];
+      if (!md.A) continue;
+      const int rk = min(md.rank, kStageLoraRows - row);
+      // four rows at a time: their loads are in flight together
+      for (int r0 = 0; r0 < rk; r0 += 4) {
+        float p[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < MAXU; i++) {
+          const int u = threadIdx.x + i * NT;
+          if (u >= K8) continue;
+          float4 a0[4], a1[4];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float* Ar = md.A + (size_t)min(r0 + q, rk - 1) * K + 8 * u;
+            a0[q] = __ldg(reinterpret_cast<const float4*>(Ar));
+            a1[q] = __ldg(reinterpret_cast<const float4*>(Ar + 4));
+          }
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            p[q] = fmaf(v[i][0], a0[q].x, p[q]); p[q] = fmaf(v[i][1], a0[q].y, p[q]);
+            p[q] = fmaf(v[i][2], a0[q].z, p[q]); p[q] = fmaf(v[i][3], a0[q].w, p[q]);
+            p[q] = fmaf(v[i][4], a1[q].x, p[q]); p[q] = fmaf(v[i][5], a1[q].y, p[q]);
+            p[q] = fmaf(v[i][6], a1[q].z, p[q]); p[q] = fmaf(v[i][7], a1[q].w, p[q]);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int q = 0; q < 4; q++) p[q] += __shfl_xor_sync(0xffffffffu, p[q], o);
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          if (r0 + q < rk) {
+            if (ln == 0) part[(row + r0 + q) * NW + w] = p[q];
+            if (threadIdx.x == 0) slot[row + r0 + q] = m * kMaxRank + r0 + q;
+          }
+      }
+      row += rk;
+    }
+    bar_sync_n<NT>();
+    for (int q = threadIdx.x; q < row; q += NT) {
+      float t = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < NW; ww++) t = __fadd_rn(t, part[q * NW + ww]);
+      lora->d[slot[q]] = t;
+    }
   }
   float am = 0.f;
 #pragma unroll

@@ -52,11 +52,13 @@ struct Layer {
   void *kc = nullptr, *vc = nullptr;
   // stream-layout copies of the int4 matrices (q4_to_stream), built at finalize
   unsigned char *qkv_t = nullptr, *o_t = nullptr, *gu_t = nullptr, *d_t = nullptr;
-  // the same blocks octet-major for the tcgen05 batched GEMV (q4_stream_to_tc)
-  unsigned char *qkv_c = nullptr, *o_c = nullptr, *gu_c = nullptr, *d_c = nullptr;
-  // f16 A images + row scales of the whole-prompt GEMM (q4_tc_to_a16), prefill_tc
+  // tcgen05 paths (use_tc_batch or prefill_tc), built at finalize from the
+  // octet-major regrouping (q4_stream_to_tc, freed afterwards): int8 A images
+  // of the split-K GEMV, each MMA row's group scales, and (prefill_tc) the f16
+  // A images of the whole-prompt GEMM
+  unsigned char *qkv_a8 = nullptr, *o_a8 = nullptr, *gu_a8 = nullptr, *d_a8 = nullptr;
+  float *qkv_sc = nullptr, *o_sc = nullptr, *gu_sc = nullptr, *d_sc = nullptr;
   unsigned char *qkv_a = nullptr, *o_a = nullptr, *gu_a = nullptr, *d_a = nullptr;
-  float *qkv_s16 = nullptr, *o_s16 = nullptr, *gu_s16 = nullptr, *d_s16 = nullptr;
 };
 
 struct DevState {
@@ -951,30 +953,27 @@ EG_API eg_status eg_finalize(eg_rt* rt) {
       q4_to_stream(l.d_w, l.d_s, H, I, 1, l.d_t, rt->st);
       CK(cudaGetLastError());
       if (rt->o.use_tc_batch || rt->o.prefill_tc) {
-        DALLOC(l.qkv_c, q4_tc_bytes(NQKV, H, 1), wb);
-        DALLOC(l.o_c, q4_tc_bytes(H, QD, 1), wb);
-        DALLOC(l.gu_c, q4_tc_bytes(I, H, 2), wb);
-        DALLOC(l.d_c, q4_tc_bytes(H, I, 1), wb);
-        q4_stream_to_tc(l.qkv_t, NQKV, H, 1, l.qkv_c, rt->st);
-        q4_stream_to_tc(l.o_t, H, QD, 1, l.o_c, rt->st);
-        q4_stream_to_tc(l.gu_t, I, H, 2, l.gu_c, rt->st);
-        q4_stream_to_tc(l.d_t, H, I, 1, l.d_c, rt->st);
-        CK(cudaGetLastError());
-      }
-      if (rt->o.prefill_tc) {
-        DALLOC(l.qkv_a, q4_a16_bytes(NQKV, H, 1), wb);
-        DALLOC(l.o_a, q4_a16_bytes(H, QD, 1), wb);
-        DALLOC(l.gu_a, q4_a16_bytes(I, H, 2), wb);
-        DALLOC(l.d_a, q4_a16_bytes(H, I, 1), wb);
-        DALLOC(l.qkv_s16, q4_a16_scale_bytes(NQKV, H, 1), wb);
-        DALLOC(l.o_s16, q4_a16_scale_bytes(H, QD, 1), wb);
-        DALLOC(l.gu_s16, q4_a16_scale_bytes(I, H, 2), wb);
-        DALLOC(l.d_s16, q4_a16_scale_bytes(H, I, 1), wb);
-        q4_tc_to_a16(l.qkv_c, NQKV, H, 1, l.qkv_a, l.qkv_s16, rt->st);
-        q4_tc_to_a16(l.o_c, H, QD, 1, l.o_a, l.o_s16, rt->st);
-        q4_tc_to_a16(l.gu_c, I, H, 2, l.gu_a, l.gu_s16, rt->st);
-        q4_tc_to_a16(l.d_c, H, I, 1, l.d_a, l.d_s16, rt->st);
-        CK(cudaGetLastError());
+        const int Ns[4] = {NQKV, H, I, H}, Ks[4] = {H, QD, H, I}, Rs[4] = {1, 1, 2, 1};
+        const unsigned char* src[4] = {l.qkv_t, l.o_t, l.gu_t, l.d_t};
+        unsigned char** a8[4] = {&l.qkv_a8, &l.o_a8, &l.gu_a8, &l.d_a8};
+        float** sc[4] = {&l.qkv_sc, &l.o_sc, &l.gu_sc, &l.d_sc};
+        unsigned char** a16[4] = {&l.qkv_a, &l.o_a, &l.gu_a, &l.d_a};
+        for (int m = 0; m < 4; m++) {
+          const size_t tcb = q4_tc_bytes(Ns[m], Ks[m], Rs[m]);
+          unsigned char* wc = nullptr;
+          DALLOC(wc, tcb, nullptr);
+          q4_stream_to_tc(src[m], Ns[m], Ks[m], Rs[m], wc, rt->st);
+          DALLOC(*a8[m], q4_a8_bytes(Ns[m], Ks[m], Rs[m]), wb);
+          DALLOC(*sc[m], q4_row_scale_bytes(Ns[m], Ks[m], Rs[m]), wb);
+          q4_tc_to_a8(wc, Ns[m], Ks[m], Rs[m], *a8[m], *sc[m], rt->st);
+          if (rt->o.prefill_tc) {
+            DALLOC(*a16[m], q4_a16_bytes(Ns[m], Ks[m], Rs[m]), wb);
+            q4_tc_to_a16(wc, Ns[m], Ks[m], Rs[m], *a16[m], rt->st);
+          }
+          CK(cudaGetLastError());
+          CK(cudaStreamSynchronize(rt->st));
+          dfree(rt, (void**)&wc, 0, nullptr);
+        }
       }
     }
     DALLOC(rt->emb_t, q8_stream_bytes(c.vocab_size, H), wb);
@@ -1557,14 +1556,15 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
   xp.xf = rt->b_xf;
   xp.gpr_max = rt->b_gpr;
   // 4 or more lanes: the int4 GEMVs on the tcgen05 tensor cores
-  const bool tc = rt->o.use_tc_batch && n >= 4 && rt->L[0].qkv_c;
+  const bool tc = rt->o.use_tc_batch && n >= 4 && rt->L[0].qkv_a8;
   xp.xtc = tc ? rt->b_xtc : nullptr;
   xp.tc_tpad = (n + 3) / 4 * 4;
   int launches = 0;
   const bool pdl = rt->o.use_pdl != 0;
-  auto gemv4 = [&](const unsigned char* w, const unsigned char* wc, int N, int K, const BatchEpi& e) {
+  auto gemv4 = [&](const unsigned char* w, const unsigned char* a8, const float* sc, int N, int K,
+                   const BatchEpi& e) {
     if (tc)
-      gemv_q4_tc(wc, N, K, e.e.mode == EPI_SILU ? 2 : 1, n, xp, e, rt->b_tc_part, rt->b_tc_cnt, err, st,
+      gemv_q4_tc(a8, sc, N, K, e.e.mode == EPI_SILU ? 2 : 1, n, xp, e, rt->b_tc_part, rt->b_tc_cnt, err, st,
                  pdl);
     else
       gemv_q4_batch(w, N, K, n, xp, e, err, st, pdl);
@@ -1607,14 +1607,15 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
     const Layer& l = rt->L[i];
     BatchSrc xa = src(i == 0 ? X_EMBED_RMS : X_RMS, rt->b_hidden, l.in_norm, H);
     if (i == 0) xa.x.hidden_out = rt->b_hidden;
-    if (lora) {
+    // the LoRA A rows fold into the staging when the adapter is small
+    if (!batch_stage_q4(xa, H, n, xp, st, pdl, lora ? lt + i * 7 + 0 : nullptr, 3, rank, rt->b_lora_d, dstride) &&
+        lora) {
       BatchSrc xl = xa;
       xl.x.hidden_out = nullptr;
       lora_a_batch(xl, H, lt + i * 7 + 0, 3, rank, rt->b_lora_d, dstride, n, st, pdl);
       launches++;
     }
-    batch_stage_q4(xa, H, n, xp, st, pdl);
-    gemv4(l.qkv_t, l.qkv_c, NQKV, H,
+    gemv4(l.qkv_t, l.qkv_a8, l.qkv_sc, NQKV, H,
           epi(EPI_STORE, rt->b_qkv, NQKV, NQKV, c.attention_bias ? l.qkv_b : nullptr, i * 7 + 0, QD,
               QD + KVD));
     launches += 2;
@@ -1652,28 +1653,31 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
       launches++;
     }
     BatchSrc xo = src(X_PLAIN, rt->b_attn, nullptr, QD);
-    if (lora) {
+    if (!batch_stage_q4(xo, QD, n, xp, st, pdl, lora ? lt + i * 7 + 3 : nullptr, 1, rank, rt->b_lora_d,
+                        dstride) &&
+        lora) {
       lora_a_batch(xo, QD, lt + i * 7 + 3, 1, rank, rt->b_lora_d, dstride, n, st, pdl);
       launches++;
     }
-    batch_stage_q4(xo, QD, n, xp, st, pdl);
-    gemv4(l.o_t, l.o_c, H, QD, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 3, H, H));
+    gemv4(l.o_t, l.o_a8, l.o_sc, H, QD, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 3, H, H));
     launches += 2;
     BatchSrc xb = src(X_RMS, rt->b_hidden, l.post_norm, H);
-    if (lora) {
+    if (!batch_stage_q4(xb, H, n, xp, st, pdl, lora ? lt + i * 7 + 4 : nullptr, 2, rank, rt->b_lora_d,
+                        dstride) &&
+        lora) {
       lora_a_batch(xb, H, lt + i * 7 + 4, 2, rank, rt->b_lora_d, dstride, n, st, pdl);
       launches++;
     }
-    batch_stage_q4(xb, H, n, xp, st, pdl);
-    gemv4(l.gu_t, l.gu_c, I, H, epi(EPI_SILU, rt->b_tmp, I, I, nullptr, i * 7 + 4, I, I));
+    gemv4(l.gu_t, l.gu_a8, l.gu_sc, I, H, epi(EPI_SILU, rt->b_tmp, I, I, nullptr, i * 7 + 4, I, I));
     launches += 2;
     BatchSrc xd = src(X_PLAIN, rt->b_tmp, nullptr, I);
-    if (lora) {
+    if (!batch_stage_q4(xd, I, n, xp, st, pdl, lora ? lt + i * 7 + 6 : nullptr, 1, rank, rt->b_lora_d,
+                        dstride) &&
+        lora) {
       lora_a_batch(xd, I, lt + i * 7 + 6, 1, rank, rt->b_lora_d, dstride, n, st, pdl);
       launches++;
     }
-    batch_stage_q4(xd, I, n, xp, st, pdl);
-    gemv4(l.d_t, l.d_c, H, I, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 6, H, H));
+    gemv4(l.d_t, l.d_a8, l.d_sc, H, I, epi(EPI_ADD, rt->b_hidden, H, H, nullptr, i * 7 + 6, H, H));
     launches += 2;
   }
   if (chunk) {  // chunked prefill: no logits for these positions
@@ -1812,14 +1816,14 @@ static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
     b.stride = stride;
     return b;
   };
-  auto gemm = [&](const unsigned char* wc, const unsigned char* a16, const float* s16, int N, int K, int R,
+  auto gemm = [&](const unsigned char* a8, const unsigned char* a16, const float* sc, int N, int K, int R,
                   const BatchSrc& x, int nmods, int mode, float* y, int ystride, const float* bias, int m, int s1,
                   int s2) {
-    if (lora) {
+    if (!batch_stage_q4(x, K, n, xp, st, false, lora ? lt + m : nullptr, nmods, rank, rt->p_lora_d, dstride) &&
+        lora) {
       lora_a_batch(x, K, lt + m, nmods, rank, rt->p_lora_d, dstride, n, st, false);
       launches++;
     }
-    batch_stage_q4(x, K, n, xp, st, false);
     BatchEpi e = {};
     e.e.mode = mode;
     e.e.y = y;
@@ -1841,16 +1845,16 @@ static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
       launches++;
     }
     if (n > 32)
-      gemm_q4_prefill(a16, s16, N, K, R, n, xp, e, err, st);
+      gemm_q4_prefill(a16, sc, N, K, R, n, xp, e, err, st);
     else
-      gemv_q4_tc(wc, N, K, R, n, xp, e, rt->p_part, rt->p_cnt, err, st, false);
+      gemv_q4_tc(a8, sc, N, K, R, n, xp, e, rt->p_part, rt->p_cnt, err, st, false);
     launches += 2;
   };
   prefill_embed(rt->ids + off, rt->emb_w, rt->emb_s, n, H, rt->p_hidden, st);
   launches++;
   for (int i = 0; i < c.num_layers; i++) {
     const Layer& l = rt->L[i];
-    gemm(l.qkv_c, l.qkv_a, l.qkv_s16, NQKV, H, 1, src(X_RMS, rt->p_hidden, l.in_norm, H), 3, EPI_STORE, rt->p_qkv, NQKV,
+    gemm(l.qkv_a8, l.qkv_a, l.qkv_sc, NQKV, H, 1, src(X_RMS, rt->p_hidden, l.in_norm, H), 3, EPI_STORE, rt->p_qkv, NQKV,
          c.attention_bias ? l.qkv_b : nullptr, i * 7 + 0, QD, QD + KVD);
     prefill_rope_append(rt->p_qkv, n, NQKV, c.num_heads, c.num_kv_heads, off, rt->cosT, rt->sinT, f16, l.kc, l.vc,
                         st);
@@ -1869,11 +1873,11 @@ static int enqueue_prefill_pass(eg_rt* rt, int off, int n) {
     pa.out_stride = QD;
     attn_prefill(pa, st);
     launches += 2;
-    gemm(l.o_c, l.o_a, l.o_s16, H, QD, 1, src(X_PLAIN, rt->p_attn, nullptr, QD), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 3,
+    gemm(l.o_a8, l.o_a, l.o_sc, H, QD, 1, src(X_PLAIN, rt->p_attn, nullptr, QD), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 3,
          H, H);
-    gemm(l.gu_c, l.gu_a, l.gu_s16, I, H, 2, src(X_RMS, rt->p_hidden, l.post_norm, H), 2, EPI_SILU, rt->p_tmp, I, nullptr, i * 7 + 4,
+    gemm(l.gu_a8, l.gu_a, l.gu_sc, I, H, 2, src(X_RMS, rt->p_hidden, l.post_norm, H), 2, EPI_SILU, rt->p_tmp, I, nullptr, i * 7 + 4,
          I, I);
-    gemm(l.d_c, l.d_a, l.d_s16, H, I, 1, src(X_PLAIN, rt->p_tmp, nullptr, I), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 6, H,
+    gemm(l.d_a8, l.d_a, l.d_sc, H, I, 1, src(X_PLAIN, rt->p_tmp, nullptr, I), 1, EPI_ADD, rt->p_hidden, H, nullptr, i * 7 + 6, H,
          H);
   }
   return launches;
@@ -2382,7 +2386,10 @@ EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, con
   const size_t xfb = ((size_t)T * 4 + 255) / 256 * 256;  // one exponent per token
   // [err | xb | xcor | xf | xtc | counters | partials], every piece 256-byte aligned
   // more than 32 rows: the whole-prompt GEMM over A images built here from ws
-  const size_t a8 = use_tc && T > 32 ? q4_a16_bytes(N, K, 1) : 0, s8 = use_tc && T > 32 ? q4_a16_scale_bytes(N, K, 1) : 0;
+  // tcgen05: the int8 A images and row scales (and for more than 32 rows the
+  // f16 A images) built here from the tc-layout ws
+  const size_t a8 = use_tc ? q4_a8_bytes(N, K, 1) + q4_a16_bytes(N, K, 1) * (T > 32) : 0,
+               s8 = use_tc ? q4_row_scale_bytes(N, K, 1) : 0;
   const size_t o_xb = 256, o_xc = o_xb + xb, o_xf = o_xc + xc, o_tc = o_xf + xfb, o_cnt = o_tc + xtc,
                o_part = o_cnt + cnt, o_a8 = o_part + part, o_s8 = o_a8 + a8;
   void* scr = nullptr;
@@ -2414,14 +2421,19 @@ EG_API eg_status eg_op_gemm_q4_stream(const float* x, int T, const void* ws, con
   be.e.bias = bias;
   be.e.split1 = be.e.split2 = N;
   be.ystride = N;
-  if (use_tc && T > 32) {
-    unsigned char* ia = reinterpret_cast<unsigned char*>(b + o_a8);
-    float* is = reinterpret_cast<float*>(b + o_s8);
-    q4_tc_to_a16(static_cast<const unsigned char*>(ws), N, K, 1, ia, is, OPSTREAM);
-    gemm_q4_prefill(ia, is, N, K, 1, T, xp, be, err, OPSTREAM);
-  } else if (use_tc)
-    gemv_q4_tc(static_cast<const unsigned char*>(ws), N, K, 1, T, xp, be, prt, counters, err, OPSTREAM, false);
-  else
+  if (use_tc) {
+    const unsigned char* wc = static_cast<const unsigned char*>(ws);
+    unsigned char* ia8 = reinterpret_cast<unsigned char*>(b + o_a8);
+    unsigned char* ia16 = ia8 + q4_a8_bytes(N, K, 1);
+    float* isc = reinterpret_cast<float*>(b + o_s8);
+    q4_tc_to_a8(wc, N, K, 1, ia8, isc, OPSTREAM);
+    if (T > 32) {
+      q4_tc_to_a16(wc, N, K, 1, ia16, OPSTREAM);
+      gemm_q4_prefill(ia16, isc, N, K, 1, T, xp, be, err, OPSTREAM);
+    } else {
+      gemv_q4_tc(ia8, isc, N, K, 1, T, xp, be, prt, counters, err, OPSTREAM, false);
+    }
+  } else
     gemv_q4_batch(static_cast<const unsigned char*>(ws), N, K, T, xp, be, err, OPSTREAM, false);
   CK(cudaGetLastError());
   return EG_OK;

@@ -46,23 +46,19 @@ namespace eg {
 
 namespace {
 
-constexpr int kTcThreads = 19 * 32;
-constexpr int kTcConvWarps = 8;
-constexpr int kTcEpiWarp0 = 8, kTcEpiWarps = 8;
-constexpr int kTcProdWarp = 16, kTcMmaWarp = 17, kTcBWarp = 18;
-constexpr int kTcRaw = 3;          // weight stages (int4, as streamed)
-constexpr int kTcA = 3;            // A operand slots (bytes)
-constexpr int kTcB = 4;            // B operand slots (digit planes)
-constexpr int kTcSc = 8;           // group-scale slots (converter -> epilogue)
-constexpr int kTcGroupsPerStage = 4;
-constexpr int kTcStageBytes = 8 * kTcGroupsPerStage * 1088;  // = 4 * 4 * 2176
-constexpr int kTcABytes = 128 * 128;                          // 128 rows x 128 bytes
+constexpr int kTcThreads = 11 * 32;
+constexpr int kTcEpiWarps = 8;                 // warps 0-7
+constexpr int kTcProdWarp = 8, kTcMmaWarp = 9, kTcBWarp = 10;
+constexpr int kTcA = 8;                        // A image slots (one group each)
+constexpr int kTcB = 4;                        // B operand slots (digit planes)
+constexpr int kTcABytes = 128 * 128;           // 128 rows x 128 bytes
 constexpr int kTcMaxTok = 32;
-constexpr int kTcBBytes = 4 * kTcMaxTok * 128;                // N x 128 bytes
+constexpr int kTcBBytes = 4 * kTcMaxTok * 128; // N x 128 bytes
 constexpr uint32_t kTcTmemCols = 256;
 
 struct TcArgs {
-  const unsigned char* ws;   // tc layout (q4_stream_to_tc)
+  const unsigned char* a8;   // [octet][group][16 KB] int8 A images (q4_tc_to_a8)
+  const float* sc;           // [octet][group][128] group scale of each MMA row
   int N, K, R, lanes, tpad;  // lanes: token vectors (<= 32); tpad: lanes rounded up to 4
   const unsigned char* xtc;  // B planes: per group 4 tpad x 128 bytes
   const int* xf;             // [lane] fixed-point exponent
@@ -74,13 +70,10 @@ struct TcArgs {
 };
 
 struct TcSmem {
-  uint64_t raw_full[kTcRaw], raw_empty[kTcRaw];
   uint64_t a_full[kTcA], a_empty[kTcA], b_full[kTcB], b_empty[kTcB];
   uint64_t acc_full[4], acc_empty[4];
-  uint64_t sc_full[kTcSc], sc_empty[kTcSc];
   uint32_t tmem_base;
   int last;
-  float scale[kTcSc][128];  // group scale of every MMA row, per item
 };
 
 // items * ncta < 2^31 for every matrix here (at most 20,000 items x 296 CTAs).
@@ -177,11 +170,10 @@ template <int TH>  // tokens per epilogue warpgroup (tpad / 2 <= TH)
 __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
   extern __shared__ __align__(1024) unsigned char tc_dsm[];
   __shared__ TcSmem S;
-  unsigned char* raw = tc_dsm;                                // kTcRaw stages
-  unsigned char* abuf = raw + (size_t)kTcRaw * kTcStageBytes; // kTcA x 16 KB
+  unsigned char* abuf = tc_dsm;                               // kTcA x 16 KB
   unsigned char* bbuf = abuf + (size_t)kTcA * kTcABytes;      // kTcB x N x 128
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int R = a.R, blk = q4_block_bytes(R), TPO = 8 / R;
+  const int R = a.R, TPO = 8 / R;
   const int gpr = a.K / kGroup, tiles = (a.N + 15) / 16, octets = (tiles + TPO - 1) / TPO;
   const int items = octets * gpr;
   const int ncta = gridDim.x, c = blockIdx.x;
@@ -190,12 +182,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
   const uint32_t bbytes = (uint32_t)ncol * 128;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcRaw; i++) {
-      mbar_init(&S.raw_full[i], 1);
-      mbar_init(&S.raw_empty[i], kTcConvWarps);
-    }
     for (int i = 0; i < kTcA; i++) {
-      mbar_init(&S.a_full[i], kTcConvWarps);
+      mbar_init(&S.a_full[i], 1);
       mbar_init(&S.a_empty[i], 1);
     }
     for (int i = 0; i < kTcB; i++) {
@@ -205,10 +193,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     for (int i = 0; i < 4; i++) {
       mbar_init(&S.acc_full[i], 1);
       mbar_init(&S.acc_empty[i], kTcEpiWarps);
-    }
-    for (int i = 0; i < kTcSc; i++) {
-      mbar_init(&S.sc_full[i], kTcConvWarps);
-      mbar_init(&S.sc_empty[i], kTcEpiWarps);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -220,39 +204,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
   bool dead = false;
 
   if (warp == kTcProdWarp) {
-    // ---------------------------------------------------- weight stages
+    // ---------------------------------------------------- A images
     // the weights depend on no earlier kernel: no griddepcontrol.wait here
     if (a.pdl && lane == 0) pdl_launch_dependents();
     SegIter it(gpr, octets);
     Seg sg;
-    int s = 0, ph = 0, issued = 0;
-    while (it.next(sg)) {
-      for (int g0 = sg.g0; g0 < sg.g1; g0 += kTcGroupsPerStage) {
-        const int ng = min(kTcGroupsPerStage, sg.g1 - g0);
-        if (!dead && !tc_wait(&S.raw_empty[s], ph ^ 1, a.err)) dead = true;
-        if (lane == 0) {  // the tc layout: one contiguous run per stage
-          const uint32_t bytes = (uint32_t)(ng * TPO * blk);
-          mbar_expect_tx(&S.raw_full[s], bytes);
-          bulk_g2s(raw + (size_t)s * kTcStageBytes, a.ws + ((size_t)sg.o * gpr + g0) * TPO * blk, bytes,
-                   &S.raw_full[s]);
+    Ring ra{0, 0};
+    int n = 0;
+    while (it.next(sg))
+      for (int g = sg.g0; g < sg.g1; g++, n++) {
+        if (!dead && !tc_wait(&S.a_empty[ra.slot], ra.ph ^ 1, a.err)) dead = true;
+        if (lane == 0) {
+          mbar_expect_tx(&S.a_full[ra.slot], kTcABytes);
+          bulk_g2s(abuf + (size_t)ra.slot * kTcABytes, a.a8 + ((size_t)sg.o * gpr + g) * kTcABytes, kTcABytes,
+                   &S.a_full[ra.slot]);
         }
         __syncwarp();
-        issued++;
-        if (++s == kTcRaw) {
-          s = 0;
-          ph ^= 1;
-        }
+        ra.adv(kTcA);
       }
-    }
-    // never leave with a copy in flight
-    for (int k = 0; k < kTcRaw && k < issued; k++) {
-      if (s == 0) {
-        s = kTcRaw - 1;
-        ph ^= 1;
+    for (int j = 0; j < kTcA && j < n; j++) {  // never leave with a copy in flight
+      if (ra.slot == 0) {
+        ra.slot = kTcA - 1;
+        ra.ph ^= 1;
       } else {
-        s--;
+        ra.slot--;
       }
-      if (!tc_wait_bounded(&S.raw_full[s], ph)) break;
+      if (!tc_wait_bounded(&S.a_full[ra.slot], ra.ph)) break;
     }
   } else if (warp == kTcBWarp) {
     // ---------------------------------------------------- B planes
@@ -266,8 +243,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
         if (!dead && !tc_wait(&S.b_empty[rb.slot], rb.ph ^ 1, a.err)) dead = true;
         if (lane == 0) {
           mbar_expect_tx(&S.b_full[rb.slot], bbytes);
-          bulk_g2s(bbuf + (size_t)rb.slot * kTcBBytes, a.xtc + (size_t)g * bbytes, bbytes,
-                   &S.b_full[rb.slot]);
+          bulk_g2s(bbuf + (size_t)rb.slot * kTcBBytes, a.xtc + (size_t)g * bbytes, bbytes, &S.b_full[rb.slot]);
         }
         __syncwarp();
         rb.adv(kTcB);
@@ -290,28 +266,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
     Seg sg;
     while (it.next(sg))
       for (int g = sg.g0; g < sg.g1; g++, nm++) {
-      if (!dead && !tc_wait(&S.a_full[ra.slot], ra.ph, a.err)) dead = true;
-      if (!dead && !tc_wait(&S.b_full[rb.slot], rb.ph, a.err)) dead = true;
-      if (!dead && !tc_wait(&S.acc_empty[rt.slot], rt.ph ^ 1, a.err)) dead = true;
-      tc_fence_after();
-      if (lane == 0) {
-        const unsigned char* A = abuf + (size_t)ra.slot * kTcABytes;
-        const unsigned char* B = bbuf + (size_t)rb.slot * kTcBBytes;
-        const uint32_t d = tmem + (uint32_t)(rt.slot * ncol);
+        if (!dead && !tc_wait(&S.a_full[ra.slot], ra.ph, a.err)) dead = true;
+        if (!dead && !tc_wait(&S.b_full[rb.slot], rb.ph, a.err)) dead = true;
+        if (!dead && !tc_wait(&S.acc_empty[rt.slot], rt.ph ^ 1, a.err)) dead = true;
+        tc_fence_after();
+        if (lane == 0) {
+          const unsigned char* A = abuf + (size_t)ra.slot * kTcABytes;
+          const unsigned char* B = bbuf + (size_t)rb.slot * kTcBBytes;
+          const uint32_t d = tmem + (uint32_t)(rt.slot * ncol);
 #pragma unroll
-        for (int j = 0; j < 4; j++)  // K = 32 bytes = 2 core matrices per instruction
-          mma_i8(d, smem_desc(A + j * 2 * 2048, 2048, 128),
-                 smem_desc(B + (size_t)j * 2 * (ncol / 8) * 128, (ncol / 8) * 128, 128), idesc,
-                 j > 0);
-        mma_commit(&S.acc_full[rt.slot]);
-        mma_commit(&S.a_empty[ra.slot]);
-        mma_commit(&S.b_empty[rb.slot]);
+          for (int j = 0; j < 4; j++)  // K = 32 bytes = 2 core matrices per instruction
+            mma_i8(d, smem_desc(A + j * 2 * 2048, 2048, 128),
+                   smem_desc(B + (size_t)j * 2 * (ncol / 8) * 128, (ncol / 8) * 128, 128), idesc,
+                   j > 0);
+          mma_commit(&S.acc_full[rt.slot]);
+          mma_commit(&S.a_empty[ra.slot]);
+          mma_commit(&S.b_empty[rb.slot]);
+        }
+        __syncwarp();
+        ra.adv(kTcA);
+        rb.adv(kTcB);
+        rt.adv(NT);
       }
-      __syncwarp();
-      ra.adv(kTcA);
-      rb.adv(kTcB);
-      rt.adv(NT);
-    }
     // the MMAs this warp issued have finished before TMEM is freed
     for (int j = 0; j < NT && j < nm; j++) {
       if (rt.slot == 0) {
@@ -322,84 +298,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
       }
       tc_wait_bounded(&S.acc_full[rt.slot], rt.ph);
     }
-  } else if (warp < kTcConvWarps) {
-    // ---------------------------------------------------- convert to A
-    const int ct = threadIdx.x;  // 0..255
-    SegIter it(gpr, octets);
-    Seg sg;
-    int s = 0, ph = 0;
-    Ring ra{0, 0}, rs{0, 0};
-    const int sm_ = ct & 127;  // threads 0..127 copy the scale of MMA row sm_
-    const int sti = R == 1 ? sm_ >> 4 : sm_ >> 5, sr = R == 1 ? 0 : (sm_ >> 4) & 1, srow = sm_ & 15;
-    const int sc_off = R * 1024 + 4 * (sr * 16 + 2 * (srow & 7) + (srow >> 3));
-    while (it.next(sg)) {
-      for (int g0 = sg.g0; g0 < sg.g1; g0 += kTcGroupsPerStage) {
-        const int ng = min(kTcGroupsPerStage, sg.g1 - g0);
-        if (!dead && !tc_wait(&S.raw_full[s], ph, a.err)) dead = true;
-        const unsigned char* st = raw + (size_t)s * kTcStageBytes;
-        for (int gj = 0; gj < ng; gj++) {
-          if (!dead && !tc_wait(&S.a_empty[ra.slot], ra.ph ^ 1, a.err)) dead = true;
-          unsigned char* A = abuf + (size_t)ra.slot * kTcABytes;
-          // 512 pieces of 16 B (block, part, row half, lane): words t, 4+t,
-          // 8+t, 12+t of MMA row m; word w goes to k chunk w / 2, half w & 1
-  #pragma unroll
-          for (int j = 0; j < 2; j++) {
-            const int pc = ct + 256 * j;
-            const int pl = pc & 31, h = (pc >> 5) & 1, rest = pc >> 6;
-            const int ti = R == 1 ? rest : rest >> 1, r = R == 1 ? 0 : rest & 1;
-            const int m = R == 1 ? 16 * ti + 8 * h + (pl >> 2) : 32 * ti + 16 * r + 8 * h + (pl >> 2);
-            const int t = pl & 3;
-            const uint4 v = *reinterpret_cast<const uint4*>(
-                st + (gj * TPO + ti) * blk + r * 1024 + h * 512 + pl * 16);
-            unsigned char* rowp = A + (m >> 3) * 128 + (m & 7) * 16 + (t & 1) * 8;
-            const int kc = t >> 1;
-            *reinterpret_cast<uint2*>(rowp + (kc + 0) * 2048) = a_bytes(v.x);
-            *reinterpret_cast<uint2*>(rowp + (kc + 2) * 2048) = a_bytes(v.y);
-            *reinterpret_cast<uint2*>(rowp + (kc + 4) * 2048) = a_bytes(v.z);
-            *reinterpret_cast<uint2*>(rowp + (kc + 6) * 2048) = a_bytes(v.w);
-          }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&S.a_full[ra.slot]);
-          // the group scale of MMA row ct, for the epilogue
-          if (!dead && !tc_wait(&S.sc_empty[rs.slot], rs.ph ^ 1, a.err)) dead = true;
-          if (ct < 128)
-            S.scale[rs.slot][ct] = *reinterpret_cast<const float*>(st + (gj * TPO + sti) * blk + sc_off);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&S.sc_full[rs.slot]);
-          rs.adv(kTcSc);
-          ra.adv(kTcA);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.raw_empty[s]);
-        if (++s == kTcRaw) {
-          s = 0;
-          ph ^= 1;
-        }
-      }
-    }
-  } else if (warp >= kTcEpiWarp0 && warp < kTcEpiWarp0 + kTcEpiWarps) {
+  } else if (warp < kTcEpiWarps) {
     // ---------------------------------------------------- epilogue
     if (a.pdl) pdl_wait();
-    const int sub = warp & 3, wg = (warp - kTcEpiWarp0) >> 2;
+    const int sub = warp & 3, wg = warp >> 2;
     const int m = 32 * sub + lane;  // MMA row = TMEM lane
-    const int th = a.tpad / 2, tb = wg * th;  // this warpgroup's tokens of a tile [tb, tb + th)
+    const int th = a.tpad / 2, tb = wg * th;  // this warpgroup's tokens [tb, tb + th)
     const int ti = R == 1 ? m >> 4 : m >> 5, r = R == 1 ? 0 : (m >> 4) & 1, row = m & 15;
     float acc01[TH], acc23[TH];
 #pragma unroll
     for (int j = 0; j < TH; j++) acc01[j] = acc23[j] = 0.f;
     const int first_o = item_lo(items, ncta, c) / gpr;
-    Ring rt{0, 0}, rs{0, 0};
+    Ring rt{0, 0};
     SegIter it(gpr, octets);
     Seg sg;
     while (it.next(sg)) {
+      const float* srow = a.sc + (size_t)sg.o * gpr * 128 + m;  // this row's scale of group g at g * 128
+      float s_next = __ldg(srow + (size_t)sg.g0 * 128);
       for (int g = sg.g0; g < sg.g1; g++) {
+        const float s_m = s_next;
+        if (g + 1 < sg.g1) s_next = __ldg(srow + (size_t)(g + 1) * 128);  // one group ahead
         const int qt = rt.slot;
-        if (!dead && !tc_wait(&S.sc_full[rs.slot], rs.ph, a.err)) dead = true;
-        const float s_m = S.scale[rs.slot][m];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.sc_empty[rs.slot]);
-        rs.adv(kTcSc);
         if (!dead && !tc_wait(&S.acc_full[qt], rt.ph, a.err)) dead = true;
         rt.adv(NT);
         tc_fence_after();
@@ -451,7 +370,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
           __syncwarp();
           asm volatile("bar.sync 2, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
           __syncwarp();
-          if (warp == kTcEpiWarp0 && lane == 0) {
+          if (warp == 0 && lane == 0) {
             __threadfence();
             const bool last = atomicAdd(a.counters + o_, 1u) == (unsigned)(c_hi - c_lo);
             if (last) {
@@ -508,6 +427,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemv_q4_tc_kernel(TcArgs a) {
   if (warp == kTcMmaWarp) tmem_free(tmem, kTcTmemCols);
 }
 
+// int8 A images from the tc layout: block og = (octet, group) of 128 rows x
+// 128 k as signed bytes (even nibbles q, odd nibbles in place as 16 q) in the
+// MMA's canonical K-major layout.  Word w of MMA row m's fragment-order
+// block holds k = 8w .. 8w + 7: k-chunk w / 2, half w & 1.
+__global__ void q4_tc_to_a8_kernel(const unsigned char* __restrict__ wc, int R, unsigned char* __restrict__ a8,
+                                   float* __restrict__ sc) {
+  const int blk = q4_block_bytes(R), TPO = 8 / R;
+  const size_t og = blockIdx.x;
+  const unsigned char* st = wc + og * TPO * blk;
+  unsigned char* A = a8 + og * kTcABytes;
+  const int ct = threadIdx.x;
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int pc = ct + 256 * j;
+    const int pl = pc & 31, h = (pc >> 5) & 1, rest = pc >> 6;
+    const int ti = R == 1 ? rest : rest >> 1, r = R == 1 ? 0 : rest & 1;
+    const int m = R == 1 ? 16 * ti + 8 * h + (pl >> 2) : 32 * ti + 16 * r + 8 * h + (pl >> 2);
+    const int t = pl & 3;
+    const uint4 v = *reinterpret_cast<const uint4*>(st + ti * blk + r * 1024 + h * 512 + pl * 16);
+    unsigned char* rowp = A + (m >> 3) * 128 + (m & 7) * 16 + (t & 1) * 8;
+    const int kc = t >> 1;
+    *reinterpret_cast<uint2*>(rowp + (kc + 0) * 2048) = a_bytes(v.x);
+    *reinterpret_cast<uint2*>(rowp + (kc + 2) * 2048) = a_bytes(v.y);
+    *reinterpret_cast<uint2*>(rowp + (kc + 4) * 2048) = a_bytes(v.z);
+    *reinterpret_cast<uint2*>(rowp + (kc + 6) * 2048) = a_bytes(v.w);
+  }
+  if (ct < 128) {  // the group scale of each MMA row
+    const int sti = R == 1 ? ct >> 4 : ct >> 5, sr = R == 1 ? 0 : (ct >> 4) & 1, srow = ct & 15;
+    sc[og * 128 + ct] =
+        *reinterpret_cast<const float*>(st + sti * blk + R * 1024 + 4 * (sr * 16 + 2 * (srow & 7) + (srow >> 3)));
+  }
+}
+
 // The tc layout: the stream-layout blocks regrouped octet-major, group-next,
 // tile-minor ([octet][group][tile of the octet][block]), so that a stage
 // (an octet's run of groups) is one contiguous range; tiles past the matrix
@@ -541,11 +493,22 @@ void q4_stream_to_tc(const unsigned char* ws, int N, int K, int R, unsigned char
 size_t gemv_q4_tc_part_bytes() { return (size_t)2 * 148 * 2 * kTcMaxTok * 128 * sizeof(float); }
 int gemv_q4_tc_max_octets() { return 4096; }
 
-void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const BatchPlanes& xp,
-                const BatchEpi& be, float* part, unsigned* counters, int* err, cudaStream_t st,
-                bool pdl) {
+size_t q4_a8_bytes(int N, int K, int R) {
+  const int tiles = (N + 15) / 16, TPO = 8 / R, octets = (tiles + TPO - 1) / TPO;
+  return (size_t)octets * (K / kGroup) * kTcABytes;
+}
+
+size_t q4_row_scale_bytes(int N, int K, int R) { return q4_a8_bytes(N, K, R) / kTcABytes * 128 * sizeof(float); }
+
+void q4_tc_to_a8(const unsigned char* wc, int N, int K, int R, unsigned char* a8, float* sc, cudaStream_t st) {
+  q4_tc_to_a8_kernel<<<(unsigned)(q4_a8_bytes(N, K, R) / kTcABytes), 256, 0, st>>>(wc, R, a8, sc);
+}
+
+void gemv_q4_tc(const unsigned char* a8, const float* sc, int N, int K, int R, int lanes, const BatchPlanes& xp,
+                const BatchEpi& be, float* part, unsigned* counters, int* err, cudaStream_t st, bool pdl) {
   TcArgs a = {};
-  a.ws = ws;
+  a.a8 = a8;
+  a.sc = sc;
   a.N = N;
   a.K = K;
   a.R = R;
@@ -560,10 +523,11 @@ void gemv_q4_tc(const unsigned char* ws, int N, int K, int R, int lanes, const B
   a.pdl = pdl;
   const int gpr = K / kGroup, tiles = (N + 15) / 16, octets = (tiles + 8 / R - 1) / (8 / R);
   const int items = octets * gpr;
-  // at most two CTAs per octet: a split octet costs a fence, an atomic and
-  // the partial-sum reads of its last CTA
-  const int ncta = std::min(std::min(sm_count(), 2 * octets), items);
-  const size_t smem = (size_t)kTcRaw * kTcStageBytes + (size_t)kTcA * kTcABytes + (size_t)kTcB * kTcBBytes;
+  // every SM takes a share of at least 4 groups: a narrow matrix (16 octets
+  // for N = 2048) splits each octet over many CTAs, whose partials the last
+  // to arrive sums (a fence, an atomic and its partial reads per split octet)
+  const int ncta = std::max(1, std::min(sm_count(), items / 4));
+  const size_t smem = (size_t)kTcA * kTcABytes + (size_t)kTcB * kTcBBytes;
   void (*kern)(TcArgs) = a.tpad <= 16 ? gemv_q4_tc_kernel<8> : gemv_q4_tc_kernel<16>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaLaunchConfig_t cfg = {};
@@ -813,11 +777,9 @@ __global__ void __launch_bounds__(kPgThreads, 1) gemm_q4_prefill_kernel(PgArgs a
 
 // A images from the tc layout: block og = (octet, group) of 128 rows x 128 k
 // as f16 nibble values, element (m, k) at (k / 8) * 2 KB + (m / 8) * 128 +
-// (m % 8) * 16 + (k % 8) * 2 (K-major 8 x 16-byte core matrices), and the
-// group scale of each MMA row.  Word w of MMA row m's fragment-order block
+// (m % 8) * 16 + (k % 8) * 2 (K-major 8 x 16-byte core matrices).  Word w of MMA row m's fragment-order block
 // holds k = 8w .. 8w + 7 (the mapping gemv_q4_tc's converter warps use).
-__global__ void q4_tc_to_a16_kernel(const unsigned char* __restrict__ wc, int R, unsigned char* __restrict__ a16,
-                                    float* __restrict__ s16) {
+__global__ void q4_tc_to_a16_kernel(const unsigned char* __restrict__ wc, int R, unsigned char* __restrict__ a16) {
   const int blk = q4_block_bytes(R), TPO = 8 / R;
   const size_t og = blockIdx.x;
   const unsigned char* st = wc + og * TPO * blk;
@@ -845,11 +807,6 @@ __global__ void q4_tc_to_a16_kernel(const unsigned char* __restrict__ wc, int R,
       *reinterpret_cast<uint4*>(A + w * 2048 + (m >> 3) * 128 + (m & 7) * 16) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
     }
   }
-  if (ct < 128) {
-    const int sti = R == 1 ? ct >> 4 : ct >> 5, sr = R == 1 ? 0 : (ct >> 4) & 1, srow = ct & 15;
-    s16[og * 128 + ct] =
-        *reinterpret_cast<const float*>(st + sti * blk + R * 1024 + 4 * (sr * 16 + 2 * (srow & 7) + (srow >> 3)));
-  }
 }
 
 }  // namespace
@@ -858,11 +815,9 @@ size_t q4_a16_bytes(int N, int K, int R) {
   const int tiles = (N + 15) / 16, TPO = 8 / R, octets = (tiles + TPO - 1) / TPO;
   return (size_t)octets * (K / kGroup) * kPgABytes;
 }
-size_t q4_a16_scale_bytes(int N, int K, int R) { return q4_a16_bytes(N, K, R) / kPgABytes * 128 * sizeof(float); }
-
-void q4_tc_to_a16(const unsigned char* wc, int N, int K, int R, unsigned char* a16, float* s16, cudaStream_t st) {
+void q4_tc_to_a16(const unsigned char* wc, int N, int K, int R, unsigned char* a16, cudaStream_t st) {
   const unsigned blocks = (unsigned)(q4_a16_bytes(N, K, R) / kPgABytes);
-  q4_tc_to_a16_kernel<<<blocks, 256, 0, st>>>(wc, R, a16, s16);
+  q4_tc_to_a16_kernel<<<blocks, 256, 0, st>>>(wc, R, a16);
 }
 
 void gemm_q4_prefill(const unsigned char* a16, const float* s16, int N, int K, int R, int lanes,
