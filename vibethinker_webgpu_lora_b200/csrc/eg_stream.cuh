@@ -480,14 +480,41 @@ __device__ __forceinline__ void axpy4(float4& acc, float w, float4 v) {
 __device__ __forceinline__ void attn_merge(const AttnArgs& a, int h0, int hq, int nsplit, AttnSmem& sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hd = kHeadDim;
-  if (warp < hq) {
+  // thread = (phase p, head j, dim quad q): P = 16 / hq phases; its first
+  // kPre splits' po rows and maxima are loaded before anything waits
+  constexpr int kPre = 8;
+  const int P = kAttnHq * kAttnWarps / (4 * hq);  // 16 / hq
+  const int q = threadIdx.x & 31, j = (threadIdx.x >> 5) % hq, p = (threadIdx.x >> 5) / hq;
+  const float* pmj = a.pm + (h0 + j) * a.max_splits;
+  const float4* pp = reinterpret_cast<const float4*>(a.po + (size_t)(h0 + j) * a.max_splits * hd) + q;
+  float4 pv[kPre];
+  float pmv[kPre];
+#pragma unroll
+  for (int k = 0; k < kPre; k++) {
+    const int s2 = p + k * P;
+    const bool ok = p < P && s2 < nsplit;
+    pv[k] = ok ? __ldcg(pp + (size_t)s2 * (hd / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    pmv[k] = ok ? __ldcg(pmj + s2) : 0.f;
+  }
+  if (warp < hq) {  // per head the global max and the weighted sum of the split sums
     const float* pm = a.pm + (h0 + warp) * a.max_splits;
     const float* pz = a.pz + (h0 + warp) * a.max_splits;
+    float m2[2], z2[2];  // this lane's splits lane and lane + 32 (nsplit <= 64)
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      const int s2 = lane + 32 * k;
+      m2[k] = s2 < nsplit ? __ldcg(pm + s2) : -1e30f;
+      z2[k] = s2 < nsplit ? __ldcg(pz + s2) : 0.f;
+    }
     float M = -1e30f;
-    for (int s2 = lane; s2 < nsplit; s2 += 32) M = fmaxf(M, __ldcg(pm + s2));
+    for (int s2 = lane + 64; s2 < nsplit; s2 += 32) M = fmaxf(M, __ldcg(pm + s2));
+    M = fmaxf(M, fmaxf(m2[0], m2[1]));
     M = warp_max(M);
     float Z = 0.f;
-    for (int s2 = lane; s2 < nsplit; s2 += 32)
+#pragma unroll
+    for (int k = 0; k < 2; k++)
+      if (lane + 32 * k < nsplit) Z = __fadd_rn(Z, __fmul_rn(z2[k], expf(m2[k] - M)));
+    for (int s2 = lane + 64; s2 < nsplit; s2 += 32)
       Z = __fadd_rn(Z, __fmul_rn(__ldcg(pz + s2), expf(__ldcg(pm + s2) - M)));
     Z = warp_sum(Z);
     if (lane == 0) {
@@ -496,17 +523,14 @@ __device__ __forceinline__ void attn_merge(const AttnArgs& a, int h0, int hq, in
     }
   }
   bar_sync_n<kAttnWarps * 32>();
-  // thread = (phase p, head j, dim quad q): P = 16 / hq phases
-  const int P = kAttnHq * kAttnWarps / (4 * hq);  // 16 / hq
-  const int q = threadIdx.x & 31, j = (threadIdx.x >> 5) % hq, p = (threadIdx.x >> 5) / hq;
   float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
   if (p < P) {
-    const int h = h0 + j;
     const float M = sm.mz[j][0];
-    const float* pm = a.pm + h * a.max_splits;
-    const float4* pp = reinterpret_cast<const float4*>(a.po + (size_t)h * a.max_splits * hd) + q;
-#pragma unroll 4
-    for (int s2 = p; s2 < nsplit; s2 += P) axpy4(o, expf(__ldcg(pm + s2) - M), __ldcg(pp + (size_t)s2 * (hd / 4)));
+#pragma unroll
+    for (int k = 0; k < kPre; k++)
+      if (p + k * P < nsplit) axpy4(o, expf(pmv[k] - M), pv[k]);
+    for (int s2 = p + kPre * P; s2 < nsplit; s2 += P)
+      axpy4(o, expf(__ldcg(pmj + s2) - M), __ldcg(pp + (size_t)s2 * (hd / 4)));
   }
   // phases -> shared memory (wo reused: [phase][head][dim] as 16 x 4 x 128)
   float* red = &sm.wo[0][0][0];
