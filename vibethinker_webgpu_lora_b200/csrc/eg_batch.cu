@@ -144,6 +144,7 @@ void batch_stage_q8(const BatchSrc& s, int K, int lanes, const BatchPlanes& xp, 
 template <int R>
 struct BRed {
   float v[2][4][kBatchMax][R][16];  // [buffer][k-slice][lane][r][row]
+  float l[2][kBatchMax][R][16];     // LoRA B terms computed at hand-off (lora_pre null)
 };
 
 struct GBArgs {
@@ -176,6 +177,25 @@ __device__ __forceinline__ void batch_barriers(uint64_t* full, uint64_t* empty,
   __syncthreads();
 }
 
+// LoRA B term of row n of lane vector v (lora_b_batch's value: the module
+// split of epilogue_row, or gate (half 0) / up (half 1) for SiLU).
+__device__ __forceinline__ float batch_lora(const BatchEpi& be, int v, int n, int half) {
+  Epi e = be.e;
+  e.lora_d += (size_t)v * be.dstride;
+  if (e.mode == EPI_SILU) return lora_dot(e, half, n, e.N);
+  int m = 0, nm = n, Nm = e.split1;
+  if (n >= e.split2) {
+    m = 2;
+    nm = n - e.split2;
+    Nm = e.N - e.split2;
+  } else if (n >= e.split1) {
+    m = 1;
+    nm = n - e.split1;
+    Nm = e.split2 - e.split1;
+  }
+  return lora_dot(e, m, nm, Nm);
+}
+
 // Consumer hand-off of one tile: lane (gq, t) holds, per n-tile nt and
 // weight half r, rows gq and gq + 8 of lane vector 4vq + 2nt + (t >> 1),
 // column pair t & 1 (already scaled); the pair sum goes to red.
@@ -183,7 +203,8 @@ template <int R>
 __device__ __forceinline__ void batch_handoff(BRed<R>& red, uint64_t* tile_full,
                                               uint64_t* tile_free, int tj, float (&acc)[2][R][2],
                                               const float (&scl)[2], int ks, int vq, bool& dead,
-                                              int* err) {
+                                              int* err, const BatchEpi* lf = nullptr, int n0 = 0,
+                                              int lanes = 0) {
   const int lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int nt = 0; nt < 2; nt++)
@@ -196,6 +217,13 @@ __device__ __forceinline__ void batch_handoff(BRed<R>& red, uint64_t* tile_full,
     }
   const int b = tj & 1;
   if (!dead && !mbar_wait(&tile_free[b], ((tj >> 1) & 1) ^ 1, err)) dead = true;
+  if (lf) {  // LoRA B: the 4 warps of lane quad vq share its 4 x R x 16 terms
+    for (int w = lane + 32 * ks; w < 4 * R * 16; w += 128) {
+      const int vi = w / (R * 16), r = (w / 16) % R, row = w % 16;
+      const int v = vq * 4 + vi, n = n0 + row;
+      red.l[b][v][r][row] = (v < lanes && n < lf->e.N) ? batch_lora(*lf, v, n, r) : 0.f;
+    }
+  }
   if ((t & 1) == 0) {
 #pragma unroll
     for (int nt = 0; nt < 2; nt++) {
@@ -261,7 +289,9 @@ __device__ __forceinline__ void batch_walk(const unsigned char* ring, uint64_t* 
 // gate rows and 16-31 the up rows of every lane vector.
 template <int R>
 __device__ __forceinline__ void batch_epilogue(const BatchEpi& be, int lanes, int n, int hi,
-                                               const float (&val)[R == 2 ? kBatchMax : kBatchMax / 2]) {
+                                               const float (&val)[R == 2 ? kBatchMax : kBatchMax / 2],
+                                               const float* ls = nullptr) {
+  // ls (optional): this row's LoRA B terms from the hand-off, term (v, r) at ls[(v * R + r) * 16]
   const Epi& E = be.e;
   const bool ok_n = n < E.N;
   const float* lp = be.lora_pre;
@@ -271,14 +301,14 @@ __device__ __forceinline__ void batch_epilogue(const BatchEpi& be, int lanes, in
     for (int i = 0; i < kBatchMax; i++) {
       up[i] = __shfl_down_sync(0xffffffffu, val[i], 16);
       const bool ok = hi == 0 && ok_n && i < lanes && lp;
-      lg[i] = ok ? lp[(size_t)i * be.lstride + n] : 0.f;
-      lu[i] = ok ? lp[(size_t)i * be.lstride + E.N + n] : 0.f;
+      lg[i] = ok ? lp[(size_t)i * be.lstride + n] : ls ? ls[(i * 2) * 16] : 0.f;
+      lu[i] = ok ? lp[(size_t)i * be.lstride + E.N + n] : ls ? ls[(i * 2 + 1) * 16] : 0.f;
     }
 #pragma unroll
     for (int i = 0; i < kBatchMax; i++) {
       if (hi != 0 || !ok_n || i >= lanes) continue;
       float g = val[i], u = up[i];
-      if (lp) {
+      if (lp || ls) {
         g = __fadd_rn(g, lg[i]);
         u = __fadd_rn(u, lu[i]);
       }
@@ -294,7 +324,7 @@ __device__ __forceinline__ void batch_epilogue(const BatchEpi& be, int lanes, in
     const int v = hi + 2 * i;
     const bool ok = ok_n && v < lanes;
     res[i] = (ok && E.mode == EPI_ADD) ? __ldcg(E.y + (size_t)v * be.ystride + n) : 0.f;
-    lo[i] = (ok && lp) ? lp[(size_t)v * be.lstride + n] : 0.f;
+    lo[i] = (ok && lp) ? lp[(size_t)v * be.lstride + n] : (ok && ls) ? ls[v * 16] : 0.f;
   }
 #pragma unroll
   for (int i = 0; i < NV; i++) {
@@ -302,7 +332,7 @@ __device__ __forceinline__ void batch_epilogue(const BatchEpi& be, int lanes, in
     if (!ok_n || v >= lanes) continue;
     float o = val[i];
     if (E.bias) o = __fadd_rn(o, bn);
-    if (lp) o = __fadd_rn(o, lo[i]);
+    if (lp || ls) o = __fadd_rn(o, lo[i]);
     E.y[(size_t)v * be.ystride + n] = E.mode == EPI_ADD ? __fadd_rn(res[i], o) : o;
   }
 }
@@ -351,8 +381,11 @@ __global__ void __launch_bounds__(kBThreads, 1) gemv_batch_kernel(GBArgs p) {
         val[i] = ((red.v[b][0][v][r][row] + red.v[b][1][v][r][row]) + red.v[b][2][v][r][row]) +
                  red.v[b][3][v][r][row];
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tile_free[b]);
+      const bool lfold = !Q8 && p.be.e.mods && !p.be.lora_pre;  // LoRA B terms in red.l
+      if (!lfold) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tile_free[b]);
+      }
       const int n = tile * 16 + row;
       if (Q8) {
 #pragma unroll
@@ -362,7 +395,11 @@ __global__ void __launch_bounds__(kBThreads, 1) gemv_batch_kernel(GBArgs p) {
           if (v < p.lanes && n < p.N) p.y[(size_t)v * p.ystride + n] = __fmul_rn(val[i], p.s[n]);
         }
       } else {
-        batch_epilogue<R>(p.be, p.lanes, n, hi, val);
+        batch_epilogue<R>(p.be, p.lanes, n, hi, val, lfold ? &red.l[b][0][0][row] : nullptr);
+      }
+      if (lfold) {  // red.l[b] read: the buffer is free
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tile_free[b]);
       }
     }
     return;
@@ -456,8 +493,10 @@ __global__ void __launch_bounds__(kBThreads, 1) gemv_batch_kernel(GBArgs p) {
       }
     }
   };
-  auto hand = [&](int) {
-    batch_handoff<R>(red, tile_full, tile_free, tj, acc, scl, ks, vq, dead, p.err);
+  const bool lfold = !Q8 && p.be.e.mods && !p.be.lora_pre;
+  auto hand = [&](int j) {
+    batch_handoff<R>(red, tile_full, tile_free, tj, acc, scl, ks, vq, dead, p.err, lfold ? &p.be : nullptr,
+                     (t_lo + j) * 16, p.lanes);
     tj++;
   };
   batch_walk(ring, full, empty, p.stages, p.stage_bytes, p.cap, t_hi - t_lo, gpr, blk, ks, dead,

@@ -1594,13 +1594,13 @@ static int enqueue_batch_step(eg_rt* rt, int n, bool sample, int k, float temp,
     e.e.split2 = s2;
     e.ystride = ystride;
     e.dstride = dstride;
-    if (lora) {  // the LoRA B terms of every lane and row, ahead of the GEMV
+    if (lora && tc) {  // the tcgen05 epilogue reads the LoRA B terms ahead of the GEMV
       const int rows = mode == EPI_SILU ? 2 * N : N;
       e.lora_pre = rt->b_lora_y;
       e.lstride = rows;
       lora_b_batch(e, rows, n, rt->b_lora_y, st, pdl);
       launches++;
-    }
+    }  // the mma.sync GEMV computes them at each tile hand-off (lora_pre null, mods set)
     return e;
   };
   for (int i = 0; i < c.num_layers; i++) {
