@@ -12,13 +12,14 @@
 //
 // MMA shape: A = 128 weight rows (one "octet" of 8 row tiles, or 4 tiles of
 // gate + up rows) x 128 k as signed bytes q (odd k as 16 q, the batch-1
-// nibble trick, matched by the activation digits); B = the digit planes,
-// N = 4 x tokens columns (token t, plane p at column 4t + p); D = 128 TMEM
-// lanes x N s32 columns, one fresh accumulator per group (4 instructions of
-// K = 32).  The epilogue warps fold every group into f32 registers: per row
-// and token, acc01 += s * (P0 + 256 P1) and acc23 += s * (P2 + 256 P3);
-// y = 2^-f acc01 + 2^(16-f) acc23 -- the same integers as the batch-1
-// path's (P - offset correction) with unsigned q + 8.
+// nibble trick, matched by the activation digits), expanded once at load
+// into 16 KB int8 images in the MMA's shared-memory layout (q4_tc_to_a8);
+// B = the digit planes, N = 4 x tokens columns (token t, plane p at column
+// 4t + p); D = 128 TMEM lanes x N s32 columns, one fresh accumulator per
+// group (4 instructions of K = 32).  The epilogue warps fold every group
+// into f32 registers: per row and token, acc01 += s * (P0 + 256 P1) and
+// acc23 += s * (P2 + 256 P3); y = 2^-f acc01 + 2^(16-f) acc23 -- the same
+// integers as the batch-1 path's (P - offset correction) with unsigned q + 8.
 //
 // Work split: the (octet, group) items of the matrix, octet-major, are
 // divided evenly among the CTAs (split-K where a CTA boundary falls inside
@@ -26,14 +27,15 @@
 // is finished by the last of its CTAs to arrive, which sums the partial
 // outputs in CTA order (deterministic) before the epilogue.
 //
-// Warp roles (19 warps): 0-7 convert the int4 stage into the A operand
-// (nibbles to bytes, canonical K-major layout); 8-15 epilogue (two
-// warpgroups, one per half of the tokens; warp w reads TMEM lanes
-// 32 (w % 4) ..); 16 streams the weight stages (cp.async.bulk); 17 issues
-// the MMAs (one elected thread) and owns the TMEM allocation; 18 copies the
-// B planes.  Pipelines: weight stages (3) -> A slots (3, freed when the MMAs
-// that read them complete) ; B slots (4, likewise) ; TMEM accumulators (up
-// to 4, freed by the epilogue).
+// Warp roles (11 warps): 0-7 epilogue (two warpgroups, one per half of the
+// tokens; warp w reads TMEM lanes 32 (w % 4) .., and its row's group scale
+// from global memory one group ahead); 8 copies the A images (cp.async.bulk,
+// 8 slots, freed when the MMAs that read them complete); 9 issues the MMAs
+// (one elected thread) and owns the TMEM allocation; 10 copies the B planes
+// (4 slots).  TMEM accumulators: up to 4, freed by the epilogue.
+//
+// The second half of this file is the whole-prompt (prefill) GEMM for more
+// than 32 token rows: kind::f16 over f16 nibble images, described there.
 #include <algorithm>
 
 #include "eg_batch.h"
