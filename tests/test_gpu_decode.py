@@ -356,3 +356,19 @@ def test_full_model_greedy_128(cuda, f16):
           f"min oracle margin {margins.min():.3g}")
     if n == 128 and not f16:
         close(rt.readLogits(), steps[127])  # after feeding generated token 126
+
+
+def test_l2_prefetch_changes_no_result(cuda):
+    """useL2Prefetch only warms L2 with later weights: the decode stream and
+    its logits are bit-identical with it on and off."""
+    cfg = small_config(layers=2, vocab=3000)
+    prompt = O.token_ids(20, 0xE6B00041, cfg["vocabSize"])
+    out = []
+    for on in (True, False):
+        rt = E.QwenB200(cfg, dict(maxCtx=64, useL2Prefetch=on)).build("synthetic", seed=SEED)
+        rt.prefillBatch(prompt)
+        first = rt.argmaxLogits()
+        ids = rt.decodeBatch(len(prompt), 8)
+        out.append(([first] + ids, rt.readLogits()))
+    assert out[0][0] == out[1][0]
+    assert np.array_equal(out[0][1], out[1][1])
