@@ -328,7 +328,7 @@ __global__ void __maxnreg__(96) fused_decode_kernel(FusedArgs a, int xbytes, int
         at.po = a.po;
         at.out = a.attn;
         at.counters = a.attn_counters;
-        attn_run<KVT>(at, blockIdx.x, gridDim.x, 0, asm_);
+        attn_run<KVT, false>(at, blockIdx.x, gridDim.x, 0, asm_);
       }
       if (!phase_barrier(a, epoch, &bar_passed, false, &s_ok, tok == 0 ? pb + 1 : -1)) return;
       // ---- O projection + residual

@@ -429,12 +429,30 @@ struct KvRow<float> {
   __device__ __forceinline__ void set(float4 v) { f = v; }
 };
 
-// Shared memory of the attention (33 KB).
+// Long-context items on the tensor cores (attn_item_mma): one item serves
+// all query heads of a KV head (at most kAmHeads) over one chunk.
+constexpr int kAmHeads = 8;
+constexpr int kAmMinSplits = 3;         // contexts of >= 3 chunks take the tensor-core item
+constexpr int kAmQPitch = kHeadDim + 8; // halfs per staged q row (conflict-free 16-byte reads)
+struct AttnMmaSmem {
+  // the chunk's V rows (f16); 16-byte piece c of row r at piece c ^ (r & 7),
+  // so the 8 rows of an ldmatrix read fall on distinct banks
+  __align__(16) uint16_t v[kAttnKeys][kHeadDim];
+  __align__(16) uint32_t ph[kAmHeads][kAttnKeys / 2 + 4];    // P = exp(s - M): f16 hi pairs
+  __align__(16) uint32_t pl[kAmHeads][kAttnKeys / 2 + 4];    // and the f16 lo pairs
+  float wm[kAttnWarps][kAmHeads], wz[kAttnWarps][kAmHeads];  // per warp max / sum per head
+};
+
+// Shared memory of the attention (39 KB; the tensor-core item's staging
+// overlays the per-warp partial rows).
 struct AttnSmem {
   float wm[kAttnWarps][kAttnHq], wz[kAttnWarps][kAttnHq];
-  __align__(16) float wo[kAttnWarps][kAttnHq][kHeadDim];
-  float mz[kAttnHq][2];  // merge: global max and sum per head
+  float mz[kAmHeads][2];  // merge: global max and sum per head
   int last;
+  union {
+    __align__(16) float wo[kAttnWarps][kAttnHq][kHeadDim];
+    AttnMmaSmem m;
+  };
 };
 
 // RoPE (ROPE_QK) of the 4 dims a lane holds; the partner of dim j < 64 is
@@ -529,15 +547,26 @@ __device__ __forceinline__ void attn_merge(const AttnArgs& a, int h0, int hq, in
 #pragma unroll
     for (int k = 0; k < kPre; k++)
       if (p + k * P < nsplit) axpy4(o, expf(pmv[k] - M), pv[k]);
-    for (int s2 = p + kPre * P; s2 < nsplit; s2 += P)
-      axpy4(o, expf(__ldcg(pmj + s2) - M), __ldcg(pp + (size_t)s2 * (hd / 4)));
+    // later splits kPre at a time: all loads of a batch before its sums
+    for (int base = p + kPre * P; base < nsplit; base += kPre * P) {
+#pragma unroll
+      for (int k = 0; k < kPre; k++) {
+        const int s2 = base + k * P;
+        const bool ok = s2 < nsplit;
+        pv[k] = ok ? __ldcg(pp + (size_t)s2 * (hd / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        pmv[k] = ok ? __ldcg(pmj + s2) : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < kPre; k++)
+        if (base + k * P < nsplit) axpy4(o, expf(pmv[k] - M), pv[k]);
+    }
   }
   // phases -> shared memory (wo reused: [phase][head][dim] as 16 x 4 x 128)
   float* red = &sm.wo[0][0][0];
   if (p < P) *reinterpret_cast<float4*>(red + ((size_t)p * hq + j) * hd + 4 * q) = o;
   bar_sync_n<kAttnWarps * 32>();
-  const int jj = threadIdx.x / hd, d = threadIdx.x % hd;
-  if (jj < hq) {
+  const int d = threadIdx.x % hd;
+  for (int jj = threadIdx.x / hd; jj < hq; jj += kAttnWarps * 32 / hd) {
     float v = 0.f;
     for (int pp2 = 0; pp2 < P; pp2++) v = __fadd_rn(v, red[((size_t)pp2 * hq + jj) * hd + d]);
     a.out[(h0 + jj) * hd + d] = __fmul_rn(v, 1.0f / sm.mz[jj][1]);
@@ -772,8 +801,202 @@ __device__ void attn_item(const AttnArgs& a, int kvh, int h0, int nhq, int split
   bar_sync_n<kAttnWarps * 32>();  // the shared area is reused by the next item
 }
 
-// All items of one attention launch, taken by CTA `cta` of `ncta`.
+// Long-context item on the tensor cores (f16 cache, G = nh / nkv <= 8): KV
+// head kvh, all G query heads of its group, chunk `split` of nsplit.  The
+// arithmetic is ATTN_PARTIAL_F16 (kernels.js:258-345) with the products
+// taken by mma.sync m16n8k16 (f16 in, f32 accumulate): scores S = q K^T with
+// the heads as the 16 rows (8 used) and warp w's 8 keys as the columns, so
+// the K rows and each K row's slice a lane loads are read straight from the
+// cache into B fragments; then M = the chunk's max per head, ev = exp(s - M),
+// Z = sum ev, all f32 as in attn_item; then po = sum ev v with ev split into
+// f16 hi + lo (two MMAs, |ev - hi - lo| <= 2^-22 ev) against the chunk's V
+// rows staged in shared memory, warp w producing dims 8w..8w+7 of every head
+// over all the chunk's keys (no cross-warp sum of partial rows).  po is read
+// through f16 once per chunk as in the f16 variant, and the last item of the
+// KV head merges the chunks (attn_merge over its G heads).
+//
+// The dot over the 128 dims is summed in a permuted order: logical k index
+// 2 tq + e of k-step ks is dim 32 tq + 4 ks + e (and 2 tq + 8 + e is dim
+// 32 tq + 4 ks + 2 + e), the same map for q (A) and K (B), so lane (g, tq)
+// holds dims 32 tq .. 32 tq + 31 of key g and of head g contiguously.
 template <typename KVT>
+__device__ void attn_item_mma(const AttnArgs& a, int kvh, int split, int pos, int nsplit, int pdl,
+                              AttnSmem& sm) {
+  AttnMmaSmem& m = sm.m;
+  constexpr int NT = kAttnWarps * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int hd = kHeadDim, kvd = a.nkv * hd, G = a.nh / a.nkv, h0 = kvh * G;
+  const int ctx = pos + 1;
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  const int t0 = split * keys, t1 = min(t0 + keys, ctx);
+  const bool has_new = !a.appended && pos >= t0 && pos < t1;
+  const __half* kc = static_cast<const __half*>(a.kc) + kvh * hd;
+  const __half* vc = static_cast<const __half*>(a.vc) + kvh * hd;
+  // ---- before the wait: the chunk's cached V rows -> shared memory (rows
+  // past t1 zero-filled; the new row is written below), this lane's K slice,
+  // and the RoPE row of pos
+  for (int i = threadIdx.x; i < kAttnKeys * 16; i += NT) {
+    const int r = i >> 4, c8 = i & 15, t = t0 + r;
+    if (has_new && t == pos) continue;
+    const bool ok = t < t1;
+    cp_async16(&m.v[r][8 * (c8 ^ (r & 7))], ok ? vc + kv_row(a.pages, t) * kvd + 8 * c8 : vc, ok ? 16 : 0);
+  }
+  cp_async_commit();
+  const int tk = t0 + 8 * warp + g;  // this lane's key
+  uint32_t kw[16];
+  {
+    const bool ok = tk < t1 && !(has_new && tk == pos);
+    const uint4* src = reinterpret_cast<const uint4*>(kc + (ok ? kv_row(a.pages, tk) * kvd : 0) + 32 * tq);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const uint4 u = ok ? __ldcg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+      kw[4 * c] = u.x;
+      kw[4 * c + 1] = u.y;
+      kw[4 * c + 2] = u.z;
+      kw[4 * c + 3] = u.w;
+    }
+  }
+  // this thread's RoPE pair of the post-wait step: dim i and i + 64 of head
+  // h0 + (tid >> 6) of q (and of the new k for tid < 64)
+  const int pi = threadIdx.x & 63, pj = threadIdx.x >> 6;
+  const float rc = __ldg(a.cosT + (size_t)pos * hd + pi), rs = __ldg(a.sinT + (size_t)pos * hd + pi);
+  if (pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+  // ---- RoPE (ROPE_QK_F16) of q -> f16 rows qs[head] (heads >= G zero); the
+  // new row of pos: k likewise -> kn and the cache, v -> the staged V rows
+  // and the cache (runtime.js:1509-1514)
+  uint16_t* qs = reinterpret_cast<uint16_t*>(&m.ph[0][0]);  // [8][kAmQPitch], in P's space until P
+  uint16_t* kn = reinterpret_cast<uint16_t*>(&m.pl[0][0]);  // [128]
+  {
+    float lo = 0.f, hi = 0.f;
+    if (pj < G) {
+      const float* qh = a.qkv + (size_t)(h0 + pj) * hd;
+      lo = __ldcg(qh + pi);
+      hi = __ldcg(qh + pi + 64);
+      rope_pair(lo, hi, rc, rs, 1);
+    }
+    qs[pj * kAmQPitch + pi] = __half_as_ushort(__float2half_rn(lo));
+    qs[pj * kAmQPitch + pi + 64] = __half_as_ushort(__float2half_rn(hi));
+  }
+  const int r = pos - t0;  // the new row's place in the chunk (has_new)
+  if (has_new) {
+    if (threadIdx.x < 64) {
+      const float* kh = a.qkv + a.nh * hd + kvh * hd;
+      float lo = __ldcg(kh + pi), hi = __ldcg(kh + pi + 64);
+      rope_pair(lo, hi, rc, rs, 1);
+      const __half l16 = __float2half_rn(lo), h16 = __float2half_rn(hi);
+      kn[pi] = __half_as_ushort(l16);
+      kn[pi + 64] = __half_as_ushort(h16);
+      __half* kw0 = static_cast<__half*>(a.kc) + kv_row(a.pages, pos) * kvd + kvh * hd;
+      kw0[pi] = l16;
+      kw0[pi + 64] = h16;
+    }
+    if (warp == kAttnWarps - 1) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(a.qkv + a.nh * hd + kvd + kvh * hd) + lane);
+      const uint2 u = make_uint2(h2_bits(__floats2half2_rn(v.x, v.y)), h2_bits(__floats2half2_rn(v.z, v.w)));
+      *reinterpret_cast<uint2*>(&m.v[r][8 * ((lane >> 1) ^ (r & 7)) + 4 * (lane & 1)]) = u;
+      *reinterpret_cast<uint2*>(static_cast<__half*>(a.vc) + kv_row(a.pages, pos) * kvd + kvh * hd + 4 * lane) = u;
+    }
+  }
+  bar_sync_n<NT>();  // qs, kn
+  uint32_t qa[16];
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(qs + g * kAmQPitch + 32 * tq);
+#pragma unroll
+    for (int c2 = 0; c2 < 4; c2++) {
+      const uint4 u = src[c2];
+      qa[4 * c2] = u.x;
+      qa[4 * c2 + 1] = u.y;
+      qa[4 * c2 + 2] = u.z;
+      qa[4 * c2 + 3] = u.w;
+    }
+  }
+  if (has_new && warp == r >> 3 && g == (r & 7)) {
+    const uint4* src = reinterpret_cast<const uint4*>(kn + 32 * tq);
+#pragma unroll
+    for (int c2 = 0; c2 < 4; c2++) {
+      const uint4 u = src[c2];
+      kw[4 * c2] = u.x;
+      kw[4 * c2 + 1] = u.y;
+      kw[4 * c2 + 2] = u.z;
+      kw[4 * c2 + 3] = u.w;
+    }
+  }
+  // ---- scores of head g, keys 8 warp + 2 tq + {0, 1}
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int ks = 0; ks < 8; ks++) {
+    const uint32_t af[4] = {qa[2 * ks], 0u, qa[2 * ks + 1], 0u};
+    mma16816(c, af, kw[2 * ks], kw[2 * ks + 1]);
+  }
+  const float scale = 1.0f / sqrtf((float)hd);
+  const int kb = t0 + 8 * warp + 2 * tq;
+  const bool v0 = g < G && kb < t1, v1 = g < G && kb + 1 < t1;
+  const float s0 = v0 ? __fmul_rn(c[0], scale) : -1e30f, s1 = v1 ? __fmul_rn(c[1], scale) : -1e30f;
+  float mx = fmaxf(s0, s1);
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  if (tq == 0) m.wm[warp][g] = mx;
+  bar_sync_n<NT>();
+  float M = -1e30f;
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, m.wm[w][g]);
+  const float e0 = v0 ? expf(s0 - M) : 0.f, e1 = v1 ? expf(s1 - M) : 0.f;
+  float z = __fadd_rn(e0, e1);
+  z = __fadd_rn(z, __shfl_xor_sync(0xffffffffu, z, 1));
+  z = __fadd_rn(z, __shfl_xor_sync(0xffffffffu, z, 2));
+  if (tq == 0) m.wz[warp][g] = z;
+  split2(e0, e1, m.ph[g][4 * warp + tq], m.pl[g][4 * warp + tq]);
+  cp_async_wait<0>();
+  bar_sync_n<NT>();  // V rows, P, wz
+  // ---- po[head g][dims 8 warp + 2 tq + {0, 1}] over the chunk's keys
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  // row 16 s2 + lane (s2 even keeps lane & 7 = row & 7), piece `warp`
+  const uint32_t vaddr = smem_addr(&m.v[lane][8 * (warp ^ (lane & 7))]);
+#pragma unroll
+  for (int s2 = 0; s2 < 8; s2 += 2) {
+    uint32_t b[4];
+    ldsm_x4_t(vaddr + s2 * 16 * kHeadDim * 2, b[0], b[1], b[2], b[3]);
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int s = s2 + u;
+      const uint32_t ah[4] = {m.ph[g][8 * s + tq], 0u, m.ph[g][8 * s + 4 + tq], 0u};
+      const uint32_t al[4] = {m.pl[g][8 * s + tq], 0u, m.pl[g][8 * s + 4 + tq], 0u};
+      mma16816(o, ah, b[2 * u], b[2 * u + 1]);
+      mma16816(o, al, b[2 * u], b[2 * u + 1]);
+    }
+  }
+  float Z = 0.f;
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; w++) Z = __fadd_rn(Z, m.wz[w][g]);
+  if (g < G) {
+    const int h = h0 + g;
+    *reinterpret_cast<float2*>(a.po + ((size_t)h * a.max_splits + split) * hd + 8 * warp + 2 * tq) =
+        make_float2(round_h(o[0]), round_h(o[1]));  // ATTN_COMBINE_F16 reads po through f16
+    if (warp == 0 && tq == 0) {
+      a.pm[h * a.max_splits + split] = M;
+      a.pz[h * a.max_splits + split] = Z;
+    }
+  }
+  // ---- the last item of the KV head merges its chunks
+  __threadfence();
+  bar_sync_n<NT>();
+  if (threadIdx.x == 0) sm.last = atomicAdd(a.counters + h0, 1u) == (unsigned)nsplit - 1;
+  bar_sync_n<NT>();
+  if (sm.last != 0) {
+    __threadfence();
+    attn_merge(a, h0, G, nsplit, sm);
+    if (threadIdx.x == 0) a.counters[h0] = 0u;  // ready for the next launch
+  }
+  bar_sync_n<NT>();  // the shared area is reused by the next item
+}
+
+// All items of one attention launch, taken by CTA `cta` of `ncta`.
+// MMA: long contexts of an f16 cache take attn_item_mma.
+template <typename KVT, bool MMA = true>
 __device__ void attn_run(const AttnArgs& a, int cta, int ncta, int pdl, AttnSmem& sm) {
   // The position and the cached rows t != pos were written before the
   // producing GEMV started (it triggers this launch only after its own
@@ -783,6 +1006,18 @@ __device__ void attn_run(const AttnArgs& a, int cta, int ncta, int pdl, AttnSmem
   const int nsplit = (pos + keys) / keys;
   const int G = a.nh / a.nkv;
   bool waited = !pdl;
+  // f16 cache, >= 3 chunks: one tensor-core item per (KV head, chunk)
+  if (MMA && sizeof(KVT) == 2 && nsplit >= kAmMinSplits && G <= kAmHeads) {
+    for (int it = cta; it < a.nkv * nsplit; it += ncta) {
+      attn_item_mma<KVT>(a, it % a.nkv, it / a.nkv, pos, nsplit, waited ? 0 : 1, sm);
+      waited = true;
+    }
+    if (!waited) {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    return;
+  }
   // f16 cache: one item per query head over both chunks, merged in place
   // (the f32 cache's rows are twice as wide and would spill)
   if (sizeof(KVT) == 2 && nsplit == 2) {
