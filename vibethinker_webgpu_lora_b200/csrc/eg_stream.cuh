@@ -495,12 +495,12 @@ __device__ __forceinline__ void axpy4(float4& acc, float w, float4 v) {
 // the weighted sum of the split sums (one warp per head), then the weighted
 // po sums with thread (head, dim quad, split phase) summing every P-th split
 // as float4s and the phases added in shared memory.
+template <int kPre = 8>
 __device__ __forceinline__ void attn_merge(const AttnArgs& a, int h0, int hq, int nsplit, AttnSmem& sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hd = kHeadDim;
   // thread = (phase p, head j, dim quad q): P = 16 / hq phases; its first
   // kPre splits' po rows and maxima are loaded before anything waits
-  constexpr int kPre = 8;
   const int P = kAttnHq * kAttnWarps / (4 * hq);  // 16 / hq
   const int q = threadIdx.x & 31, j = (threadIdx.x >> 5) % hq, p = (threadIdx.x >> 5) / hq;
   const float* pmj = a.pm + (h0 + j) * a.max_splits;
@@ -988,7 +988,7 @@ __device__ void attn_item_mma(const AttnArgs& a, int kvh, int split, int pos, in
   bar_sync_n<NT>();
   if (sm.last != 0) {
     __threadfence();
-    attn_merge(a, h0, G, nsplit, sm);
+    attn_merge<16>(a, h0, G, nsplit, sm);  // 8 heads: 2 phases, 16 splits a thread
     if (threadIdx.x == 0) a.counters[h0] = 0u;  // ready for the next launch
   }
   bar_sync_n<NT>();  // the shared area is reused by the next item
