@@ -496,10 +496,28 @@ int attn_ctas(const AttnArgs& a, int lanes) {
 template <typename KVT>
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_head_kernel(AttnArgs a, int pdl) {
   __shared__ AttnSmem sm;
-  attn_run<KVT>(a, blockIdx.x, gridDim.x, pdl, sm);
+  attn_run<KVT, false>(a, blockIdx.x, gridDim.x, pdl, sm);
 }
 
-void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl) {
+// Long contexts: one tensor-core item per (KV head, chunk).
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_long_kernel(AttnArgs a, int pdl) {
+  __shared__ AttnSmem sm;
+  attn_run_mma<__half>(a, blockIdx.x, gridDim.x, pdl, sm);
+}
+
+bool attn_long(const AttnArgs& a, int pos) {
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  return a.kv_f16 && a.nh / a.nkv <= kAmHeads && (pos + keys) / keys >= kAmMinSplits;
+}
+
+void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl, bool long_ctx) {
+  if (long_ctx && a.kv_f16 && a.nh / a.nkv <= kAmHeads) {
+    const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+    const int chunks = std::min(a.max_splits, (a.ctx_bound + keys - 1) / keys);
+    const dim3 grid(std::max(1, std::min(sm_count(), a.nkv * chunks)));
+    launch(attn_long_kernel, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, (int)pdl);
+    return;
+  }
   const dim3 grid(attn_ctas(a, 1));
   if (a.kv_f16)
     launch(attn_head_kernel<__half>, grid, dim3(kAttnWarps * 32), 0, st, pdl, a, (int)pdl);

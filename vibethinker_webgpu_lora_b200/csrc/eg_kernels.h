@@ -136,7 +136,11 @@ struct AttnArgs {
 constexpr int kAttnDefaultChunk = 128;
 int attn_max_splits(int max_ctx);
 int attn_ctas(const AttnArgs& a, int lanes);
-void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl);
+// long_ctx: the launch runs at a position where attn_long holds (the
+// tensor-core items of attn_run_mma); either kernel is correct at any
+// position, the choice is only speed.
+bool attn_long(const AttnArgs& a, int pos);
+void attn_decode(const AttnArgs& a, cudaStream_t st, bool pdl, bool long_ctx);
 
 // y[r] += A[r] . x for up to 3 modules (LORA_A, kernels.js:60-78); x from src.
 void lora_a(const XSrc& x, int K, const LoraMod* mods, int nmods, int max_rank, float* d,

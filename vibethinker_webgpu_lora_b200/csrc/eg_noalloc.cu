@@ -109,7 +109,7 @@ EG_API eg_status eg_op_attn_decode_noalloc(const float* qkv, void* k_cache, void
   a.po = f + 2 * (size_t)nh * splits;
   a.out = out;
   a.counters = counters;
-  eg::attn_decode(a, st, false);
+  eg::attn_decode(a, st, false, eg::attn_long(a, pos));
   e = cudaGetLastError();
   if (e != cudaSuccess) return eg::fail(EG_ERR_CUDA, "attn_decode_noalloc: %s", cudaGetErrorString(e));
   return EG_OK;

@@ -105,8 +105,8 @@ struct eg_rt {
   std::set<std::string> seen;
   bool finalized = false;
   eg_lora* active = nullptr;
-  cudaGraphExec_t graph[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [greedy][lora]
-  int graph_rank[2] = {0, 0};
+  cudaGraphExec_t graph[2][2][2] = {};  // [greedy][lora][long-context attention]
+  int graph_rank[2][2] = {};
   int launches_per_step = 0;
   std::atomic<bool> busy{false};
   int64_t weight_bytes = 0, kv_bytes = 0, scratch_bytes = 0;
@@ -181,11 +181,12 @@ struct Busy {
 
 static void drop_graphs(eg_rt* rt) {
   for (auto& g : rt->graph)
-    for (auto& x : g)
-      if (x) {
-        cudaGraphExecDestroy(x);
-        x = nullptr;
-      }
+    for (auto& gl : g)
+      for (auto& x : gl)
+        if (x) {
+          cudaGraphExecDestroy(x);
+          x = nullptr;
+        }
 }
 
 // ------------------------------------------------------------------ schema
@@ -403,6 +404,7 @@ struct StepOpts {
   bool greedy, lora, pdl;
   int lora_rank;
   std::vector<cudaEvent_t>* marks;  // profiling: event after each category
+  bool long_ctx;                    // the step's position takes the long-context attention
 };
 
 static void mark(eg_rt* rt, const StepOpts& so, int cat, std::vector<int>* cats) {
@@ -486,7 +488,7 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
     a.po = rt->po;
     a.out = rt->attn;
     a.counters = rt->attn_counters;
-    attn_decode(a, st, pdl);
+    attn_decode(a, st, pdl, so.long_ctx);
     launches += 1;
     mark(rt, so, 1, cats);
 
@@ -570,17 +572,29 @@ static int enqueue_step(eg_rt* rt, const StepOpts& so, std::vector<int>* cats) {
   return launches;
 }
 
-static eg_status run_step(eg_rt* rt, bool greedy) {
+// Attention of a decode step at position pos: the long-context kernel?
+static bool step_long(eg_rt* rt, int pos) {
+  AttnArgs a = {};
+  a.nh = rt->c.num_heads;
+  a.nkv = rt->c.num_kv_heads;
+  a.kv_f16 = rt->o.kv_f16;
+  a.chunk = rt->o.attn_chunk;
+  return attn_long(a, pos);
+}
+
+// One decode step at position pos (the device state's position).
+static eg_status run_step(eg_rt* rt, bool greedy, int pos) {
   const bool lora = rt->active != nullptr;
   const int rank = lora ? rt->active->max_rank : 0;
-  StepOpts so{greedy, lora, rt->o.use_pdl != 0, rank, nullptr};
+  const bool lg = step_long(rt, pos);
+  StepOpts so{greedy, lora, rt->o.use_pdl != 0, rank, nullptr, lg};
   if (!rt->o.use_graphs) {
     rt->launches_per_step = enqueue_step(rt, so, nullptr);
     CK(cudaGetLastError());
     return EG_OK;
   }
-  cudaGraphExec_t& ge = rt->graph[greedy][lora];
-  if (ge && lora && rt->graph_rank[greedy] < rank) {
+  cudaGraphExec_t& ge = rt->graph[greedy][lora][lg];
+  if (ge && lora && rt->graph_rank[greedy][lg] < rank) {
     cudaGraphExecDestroy(ge);
     ge = nullptr;
   }
@@ -595,7 +609,7 @@ static eg_status run_step(eg_rt* rt, bool greedy) {
     cudaError_t e3 = cudaGraphInstantiate(&ge, g, 0);
     cudaGraphDestroy(g);
     if (e3 != cudaSuccess) return fail(EG_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e3));
-    if (lora) rt->graph_rank[greedy] = rank;
+    if (lora) rt->graph_rank[greedy][lg] = rank;
   }
   CK(cudaGraphLaunch(ge, rt->st));
   return EG_OK;
@@ -693,7 +707,7 @@ static eg_status run_fused(eg_rt* rt, int start_pos, int n, bool greedy, bool lm
 static eg_status run_tokens(eg_rt* rt, int start_pos, int n, bool greedy, bool lm_every) {
   if (fused_ok(rt)) return run_fused(rt, start_pos, n, greedy, lm_every);
   for (int k = 0; k < n; k++) {
-    eg_status s = run_step(rt, greedy);
+    eg_status s = run_step(rt, greedy, start_pos + k);
     if (s) return s;
   }
   return EG_OK;
@@ -2237,7 +2251,8 @@ EG_API eg_status eg_profile_token(eg_rt* rt, uint32_t id, int pos, double* us, i
   cudaEvent_t start;
   CK(cudaEventCreate(&start));
   CK(cudaEventRecord(start, rt->st));
-  StepOpts so{false, rt->active != nullptr, false, rt->active ? rt->active->max_rank : 0, &marks};
+  StepOpts so{false, rt->active != nullptr, false, rt->active ? rt->active->max_rank : 0, &marks,
+              step_long(rt, pos)};
   enqueue_step(rt, so, &cats);
   CK(cudaGetLastError());
   if ((s = sync(rt))) return s;
@@ -2558,7 +2573,7 @@ EG_API eg_status eg_op_attn_decode(const float* qkv, void* k_cache, void* v_cach
   a.po = a.pz + (size_t)nh * ms;
   a.out = out;
   a.counters = counters;
-  attn_decode(a, OPSTREAM, false);
+  attn_decode(a, OPSTREAM, false, attn_long(a, pos));
   CK(cudaGetLastError());
   return EG_OK;
 }

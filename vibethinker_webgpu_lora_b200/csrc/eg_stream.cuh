@@ -995,7 +995,28 @@ __device__ void attn_item_mma(const AttnArgs& a, int kvh, int split, int pos, in
 }
 
 // All items of one attention launch, taken by CTA `cta` of `ncta`.
-// MMA: long contexts of an f16 cache take attn_item_mma.
+// Every item of a launch as tensor-core items (any context; f16 cache,
+// G <= 8), taken by CTA `cta` of `ncta`.
+template <typename KVT>
+__device__ void attn_run_mma(const AttnArgs& a, int cta, int ncta, int pdl, AttnSmem& sm) {
+  const int pos = (a.pos ? __ldcg(a.pos) : a.fixed_pos) + a.pos_off;
+  const int keys = a.chunk > 0 ? a.chunk : kAttnKeys;
+  const int nsplit = (pos + keys) / keys;
+  bool waited = !pdl;
+  for (int it = cta; it < a.nkv * nsplit; it += ncta) {
+    attn_item_mma<KVT>(a, it % a.nkv, it / a.nkv, pos, nsplit, waited ? 0 : 1, sm);
+    waited = true;
+  }
+  if (!waited) {  // no item for this CTA: still order the launch chain
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+}
+
+// MMA: long contexts of an f16 cache take attn_item_mma (the batched
+// attention; the single-stream decode launches attn_run_mma's own kernel for
+// them instead, chosen on the host, so that its short-context kernel keeps
+// none of the tensor-core item's code).
 template <typename KVT, bool MMA = true>
 __device__ void attn_run(const AttnArgs& a, int cta, int ncta, int pdl, AttnSmem& sm) {
   // The position and the cached rows t != pos were written before the
@@ -1008,14 +1029,7 @@ __device__ void attn_run(const AttnArgs& a, int cta, int ncta, int pdl, AttnSmem
   bool waited = !pdl;
   // f16 cache, >= 3 chunks: one tensor-core item per (KV head, chunk)
   if (MMA && sizeof(KVT) == 2 && nsplit >= kAmMinSplits && G <= kAmHeads) {
-    for (int it = cta; it < a.nkv * nsplit; it += ncta) {
-      attn_item_mma<KVT>(a, it % a.nkv, it / a.nkv, pos, nsplit, waited ? 0 : 1, sm);
-      waited = true;
-    }
-    if (!waited) {
-      pdl_wait();
-      pdl_launch_dependents();
-    }
+    attn_run_mma<KVT>(a, cta, ncta, pdl, sm);
     return;
   }
   // f16 cache: one item per query head over both chunks, merged in place
