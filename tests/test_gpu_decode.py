@@ -372,3 +372,34 @@ def test_l2_prefetch_changes_no_result(cuda):
         out.append(([first] + ids, rt.readLogits()))
     assert out[0][0] == out[1][0]
     assert np.array_equal(out[0][1], out[1][1])
+
+
+def test_decode_across_long_context_switch(cuda):
+    """Greedy decode over positions 250..261 crosses from the short-context
+    attention kernel (<= 2 chunks of 128 keys) to the long-context
+    tensor-core kernel (>= 3 chunks, from position 256), each step's kernel
+    chosen on the host: the stream and the last logits meet the oracle, and
+    the graph replay equals eager launches bit for bit."""
+    cfg = small_config(layers=2, vocab=3000)
+    T, n = 250, 12
+    prompt = O.token_ids(T, 0xE6B00051, cfg["vocabSize"])
+    out = []
+    for graphs in (True, False):
+        rt = E.QwenB200(cfg, dict(maxCtx=320, useGraphs=graphs)).build("synthetic", seed=SEED)
+        rt.prefillBatch(prompt)
+        first = rt.argmaxLogits()
+        ids = rt.decodeBatch(T, n)
+        out.append(([first] + list(ids), rt.readLogits()))
+    assert out[0][0] == out[1][0]
+    assert np.array_equal(out[0][1], out[1][1])
+    orc = O.OracleModel(cfg, 320, True, SEED)
+    logits = orc.prefill(prompt)
+    want, margins = [], []
+    for g in range(n + 1):
+        s = np.sort(logits.astype(np.float64))
+        want.append(O.argmax(logits))
+        margins.append(s[-1] - s[-2])
+        if g < n:
+            logits = orc.step(want[-1], T + g)
+    if assert_stream(out[0][0], want, margins) == n + 1:
+        close(out[0][1], logits)
